@@ -1,0 +1,183 @@
+/*
+ * so3lr_b200.h -- C ABI of the B200-native SO3LR force evaluation.
+ *
+ * This is the boundary the LAMMPS pair styles `so3lr/native/mpi` and
+ * `so3lr/turbo` of CPradaL/so3lrxlammps cross on every MD step. Each entry point
+ * names the reference interface it replaces (paths relative to
+ * source/so3lr-lammps-native/ in the reference repository).
+ *
+ * Conventions
+ *   - Every function returns 0 on success and a nonzero status on failure; on
+ *     failure a NUL-terminated message is written to `err` (at most `errlen`
+ *     bytes, when `err` is not NULL). No C++ exception crosses this ABI. The
+ *     reference converts its C++ exceptions into LAMMPS `error->all`
+ *     (plugins/lammps/pair_so3lr_native_mpi.cpp:1133-1136, 1974-1977); a caller
+ *     of this ABI does the same with the returned message.
+ *   - Units are LAMMPS `metal`: positions in Angstrom, energies in eV, forces in
+ *     eV/Angstrom, virial in eV (LAMMPS order xx, yy, zz, xy, xz, yz).
+ *   - Host pointers are owned by the caller; all device memory is owned by the
+ *     handle and persists (grow-only) between calls.
+ *   - One handle per GPU; a handle is not thread-safe. Calls are ordered on the
+ *     handle's CUDA stream and synchronous at return unless stated otherwise.
+ *   - All arithmetic is IEEE float64. Every per-atom and global sum is computed
+ *     in a fixed order, so repeated calls on the same input return identical bits.
+ */
+#ifndef SO3LR_B200_H
+#define SO3LR_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SO3LR_B200_ABI_VERSION 1
+
+typedef struct so3lr_handle so3lr_handle;
+
+/* Architecture record (replaces So3lrArchitecture / ArchDims,
+ * include/so3lr/so3lr_architecture.hpp:62-185). The pair style reads the
+ * cutoffs from it for init_style/init_one (pair_so3lr_native_mpi.cpp:1162-1192). */
+typedef struct {
+  int abi_version;
+  int layers;           /* interaction blocks */
+  int features;         /* invariant width F */
+  int heads;            /* attention heads */
+  int head_width;
+  int degrees;          /* equivariant degrees l = 1..degrees */
+  int ev_width;         /* sum (2l+1) */
+  int rbf;              /* radial basis functions */
+  double sr_cutoff;     /* Angstrom */
+  double lr_cutoff;     /* Angstrom */
+  double attention_norm;
+  double embedding_scale;
+  long long parameter_count;
+  char summary[512];
+} so3lr_arch_info;
+
+/* One system (replaces the atom snapshot + neighbour lists the pair style
+ * hands the evaluator, pair_so3lr_native_mpi.cpp:1267-1280). Neighbour lists are
+ * built on the GPU from the positions; no LAMMPS list is needed. */
+typedef struct {
+  long long natoms;
+  const double *x;       /* natoms * 3 */
+  const int *z;          /* atomic number of every atom, 1..99 (so3lr_element_from_token maps pair_coeff tokens) */
+  int periodic;          /* 1: orthorhombic periodic box (boxlo, boxlen); 0: open boundaries */
+  double boxlo[3];
+  double boxlen[3];
+  double total_charge;   /* pair_style ... MODEL [charge [multiplicity]] (pair_so3lr_native_mpi.cpp:1097-1104) */
+  double multiplicity;
+} so3lr_frame;
+
+/* Outputs of so3lr_compute (replace the writes to atom->f, eatom, eng_vdwl and
+ * virial[6], pair_so3lr_native_mpi.cpp:1867-1878, and the per-atom debug terms,
+ * :1811-1865). Optional arrays may be NULL. */
+typedef struct {
+  double *f;             /* natoms * 3, overwritten with the total force */
+  double *eatom;         /* natoms: learned + ZBL + long-range energy per atom */
+  double *charges;       /* natoms: partial charges after charge conservation */
+  double *ratios;        /* natoms: Hirshfeld ratios */
+  double *e_learned;     /* natoms: network energy incl. per-element shift */
+  double *e_zbl;         /* natoms: repulsion */
+  double *e_lr;          /* natoms: electrostatics + dispersion */
+  double *e_elec;        /* natoms */
+  double *e_disp;        /* natoms */
+  double energy;         /* total potential energy */
+  double virial[6];      /* xx yy zz xy xz yz */
+} so3lr_result;
+
+/* Packed independent open-boundary images (replaces the turbo broker + packed
+ * evaluator, src/mpi_turbo_replica_broker.cpp:130-307,
+ * src/kokkos_turbo_replica_bridge.cpp:64-179,
+ * src/kokkos_packed_so3lr_evaluator.cpp:43-149). Atoms of image k are
+ * [image_offsets[k], image_offsets[k+1]). */
+typedef struct {
+  long long natoms;
+  int nimages;
+  const double *x;                    /* natoms * 3 */
+  const int *z;                       /* natoms */
+  const long long *image_offsets;     /* nimages + 1 */
+  const double *image_charge;         /* nimages */
+  const double *image_multiplicity;   /* nimages */
+} so3lr_batch;
+
+typedef struct {
+  double *f;             /* natoms * 3 */
+  double *eatom;         /* natoms, optional */
+  double *charges;       /* natoms, optional */
+  double *image_energy;  /* nimages, optional */
+} so3lr_batch_result;
+
+/* Load and verify a `.so3lr` v1 model (header, SHA-256 of manifest, payload and
+ * every tensor), negotiate capabilities and upload the weights to `cuda_device`.
+ * Replaces NativeModel::load (src/native_model.cpp:325-405),
+ * describe_architecture (src/so3lr_architecture.cpp:296) and
+ * negotiate_capabilities (src/so3lr_capabilities.cpp:276), as called from
+ * PairSO3LRNativeMPI::settings (pair_so3lr_native_mpi.cpp:1097-1137). */
+int so3lr_create(const char *model_path, int cuda_device, so3lr_handle **out, char *err, size_t errlen);
+
+/* Architecture record of a loaded model (src/so3lr_architecture.cpp:296-450). */
+int so3lr_describe(const so3lr_handle *h, so3lr_arch_info *out);
+
+/* Host-only model check: load, verify and capability-negotiate a `.so3lr` file
+ * without touching a GPU, filling `out` on success. Replaces the reference's
+ * capability probe (tests/so3lr_capability_probe.cpp driven by
+ * tests/test_capability_rejection.py): a model this build cannot execute is
+ * refused here with the list of unsupported features. */
+int so3lr_inspect_model(const char *model_path, so3lr_arch_info *out, char *err, size_t errlen);
+
+/* Validate a (charge, multiplicity) pair against a global element count, as
+ * PairSO3LRNativeMPI::setup_charge_spin does after its MPI_Allreduce of the
+ * counts (pair_so3lr_native_mpi.cpp:1196-1235; src/so3lr_charge_spin.cpp:116-141).
+ * element_counts[z] for z = 1..118 (index 0 unused). */
+int so3lr_validate_charge_spin(const long long element_counts[119], double total_charge, double multiplicity,
+                               char *err, size_t errlen);
+
+/* pair_coeff token -> atomic number: element symbol H..Es (case-insensitive) or a
+ * number 1..99; 0 when the token is not valid (plugins/lammps/so3lr_element_map.h:19-52). */
+int so3lr_element_from_token(const char *token);
+
+/* Energy, forces, per-atom energies and the global virial of one system
+ * (replaces PairSO3LRNativeMPI::compute, pair_so3lr_native_mpi.cpp:1246-1978,
+ * for a single rank that owns every atom). Host buffers; the call copies the
+ * positions to the GPU and the results back. */
+int so3lr_compute(so3lr_handle *h, const so3lr_frame *in, so3lr_result *out, char *err, size_t errlen);
+
+/* Same, with positions and forces in device memory of the handle's GPU
+ * (pointers from cudaMalloc on that device). Only `energy` and `virial` are
+ * returned on the host; d_eatom may be NULL. */
+int so3lr_compute_device(so3lr_handle *h, const so3lr_frame *in_device_x, double *d_f, double *d_eatom,
+                         double *energy, double virial[6], char *err, size_t errlen);
+
+/* Packed turbo evaluation: every image is an independent open-boundary system
+ * with its own charge and multiplicity (replaces MpiTurboReplicaBroker::evaluate,
+ * KokkosPackedSo3lrEvaluator::launch_device and the per-image charge constraint of
+ * src/kokkos_image_segments.cpp:49-141). */
+int so3lr_compute_batch(so3lr_handle *h, const so3lr_batch *in, so3lr_batch_result *out, char *err, size_t errlen);
+
+/* Device-resident NVE molecular dynamics (velocity Verlet, LAMMPS `fix nve`
+ * semantics, metal units). The reference leaves integration to LAMMPS; this
+ * harness keeps positions and velocities in HBM so a step costs no host
+ * transfer. mass in g/mol per atom. */
+int so3lr_md_init(so3lr_handle *h, const so3lr_frame *in, const double *v, const double *mass, char *err,
+                  size_t errlen);
+int so3lr_md_run(so3lr_handle *h, int nsteps, double dt_ps, char *err, size_t errlen);
+/* Copies the current state to host buffers (any may be NULL) and returns the
+ * potential energy of the last force evaluation. Synchronises the stream. */
+int so3lr_md_state(so3lr_handle *h, double *x, double *v, double *f, double *energy, char *err, size_t errlen);
+
+/* The handle's CUDA stream (cudaStream_t), for callers that time or order work. */
+void *so3lr_stream(so3lr_handle *h);
+
+/* Edge and pair counts of the last evaluation and the device memory held. */
+int so3lr_last_stats(const so3lr_handle *h, long long *sr_edges, long long *sr_pairs, long long *device_bytes);
+
+/* Release the handle and all of its device memory (the reference frees its
+ * PersistentCache before Kokkos::finalize, pair_so3lr_native_mpi.cpp:1070-1086). */
+void so3lr_destroy(so3lr_handle *h);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SO3LR_B200_H */

@@ -1,0 +1,71 @@
+// Cell-list helpers shared by the edge builder and the long-range kernel.
+#pragma once
+#include "kernels.cuh"
+
+namespace so3lr_b200 {
+
+__host__ __device__ inline int pack_image(int a, int b, int c) {
+  return ((a + 512) << 20) | ((b + 512) << 10) | (c + 512);
+}
+__device__ inline void unpack_image(int code, int &a, int &b, int &c) {
+  a = ((code >> 20) & 1023) - 512;
+  b = ((code >> 10) & 1023) - 512;
+  c = (code & 1023) - 512;
+}
+__device__ inline int negate_image(int code) {
+  int a, b, c;
+  unpack_image(code, a, b, c);
+  return pack_image(-a, -b, -c);
+}
+constexpr int kZeroImage = (512 << 20) | (512 << 10) | 512;
+
+// Visit every candidate (j, image) of atom i: periodic cell stencil or the
+// atom's own image range (open boundaries / turbo packs).
+template <class Visit>
+__device__ inline void for_each_candidate(int i, const double *__restrict__ xw, const CellGrid &g,
+                                          const int *__restrict__ cell, const int *__restrict__ cell_start,
+                                          const int *__restrict__ cell_count, const int *__restrict__ cell_atoms,
+                                          const int *__restrict__ image_of, const int *__restrict__ image_start,
+                                          int reach, Visit &&visit) {
+  const double xi = xw[3 * i], yi = xw[3 * i + 1], zi = xw[3 * i + 2];
+  if (!g.periodic) {
+    const int im = image_of[i];
+    const int s = image_start[im], e = image_start[im + 1];
+    for (int j = s; j < e; ++j) {
+      const double dx = xi - xw[3 * j], dy = yi - xw[3 * j + 1], dz = zi - xw[3 * j + 2];
+      visit(j, kZeroImage, dx, dy, dz);
+    }
+    return;
+  }
+  const int c = cell[i];
+  const int cx = c % g.ncell[0], cy = (c / g.ncell[0]) % g.ncell[1], cz = c / (g.ncell[0] * g.ncell[1]);
+  for (int oz = -reach; oz <= reach; ++oz) {
+    int wz = cz + oz, sz = 0;
+    while (wz < 0) { wz += g.ncell[2]; --sz; }
+    while (wz >= g.ncell[2]) { wz -= g.ncell[2]; ++sz; }
+    for (int oy = -reach; oy <= reach; ++oy) {
+      int wy = cy + oy, sy = 0;
+      while (wy < 0) { wy += g.ncell[1]; --sy; }
+      while (wy >= g.ncell[1]) { wy -= g.ncell[1]; ++sy; }
+      for (int ox = -reach; ox <= reach; ++ox) {
+        int wx = cx + ox, sx = 0;
+        while (wx < 0) { wx += g.ncell[0]; --sx; }
+        while (wx >= g.ncell[0]) { wx -= g.ncell[0]; ++sx; }
+        const int cc = (wz * g.ncell[1] + wy) * g.ncell[0] + wx;
+        const int code = pack_image(sx, sy, sz);
+        const double shx = sx * g.len[0], shy = sy * g.len[1], shz = sz * g.len[2];
+        const int *a = cell_atoms + cell_start[cc];
+        const int m = cell_count[cc];
+        for (int t = 0; t < m; ++t) {
+          const int j = a[t];
+          const double dx = xi - (xw[3 * j] + shx);
+          const double dy = yi - (xw[3 * j + 1] + shy);
+          const double dz = zi - (xw[3 * j + 2] + shz);
+          visit(j, code, dx, dy, dz);
+        }
+      }
+    }
+  }
+}
+
+}  // namespace so3lr_b200

@@ -1,0 +1,156 @@
+// SO3LR force evaluation on one GPU: owns the device copy of the model and the
+// per-system workspace, and runs neighbour build -> geometry -> interaction
+// blocks -> heads -> charge conservation -> long range -> reverse pass ->
+// forces, energies and virial. Stream-ordered; nothing here calls MPI or NCCL.
+//
+// Mirrors the per-step sequence of PairSO3LRNativeMPI::compute
+// (plugins/lammps/pair_so3lr_native_mpi.cpp:1595-1788) and of the packed turbo
+// evaluator (src/kokkos_packed_so3lr_evaluator.cpp:43-149).
+#pragma once
+
+#include <array>
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "kernels.cuh"
+#include "model_host.hpp"
+
+namespace so3lr_b200 {
+
+template <class T>
+class DeviceArray {
+ public:
+  DeviceArray() = default;
+  DeviceArray(const DeviceArray &) = delete;
+  DeviceArray &operator=(const DeviceArray &) = delete;
+  ~DeviceArray() { release(); }
+  void release() {
+    if (ptr_) cudaFree(ptr_);
+    ptr_ = nullptr;
+    cap_ = 0;
+  }
+  // grow-only; contents are not preserved
+  T *reserve(std::size_t n, double slack = 1.0) {
+    if (n > cap_) {
+      release();
+      const std::size_t want = std::max<std::size_t>(1, std::size_t(double(n) * slack));
+      SO3_CUDA(cudaMalloc(&ptr_, want * sizeof(T)));
+      cap_ = want;
+    }
+    return ptr_;
+  }
+  T *get() const { return ptr_; }
+  std::size_t capacity() const { return cap_; }
+  std::size_t bytes() const { return cap_ * sizeof(T); }
+
+ private:
+  T *ptr_ = nullptr;
+  std::size_t cap_ = 0;
+};
+
+// What the caller asks to be evaluated. Atoms of one image are contiguous.
+struct SystemSpec {
+  int n = 0;
+  bool periodic = false;
+  double lo[3] = {0, 0, 0};
+  double len[3] = {0, 0, 0};
+  std::vector<int> z;                 // atomic numbers, 1..99
+  std::vector<int> image_start;       // n_images + 1 (one image when not batched)
+  std::vector<double> image_charge;   // n_images
+  std::vector<double> image_mult;     // n_images
+};
+
+struct StepStats {
+  long long edges = 0, pairs = 0;
+};
+
+class Evaluator {
+ public:
+  Evaluator(const std::string &model_path, int device);
+  ~Evaluator();
+  const Model &model() const { return model_; }
+  cudaStream_t stream() const { return stream_; }
+  int device() const { return device_; }
+
+  // Validates Z, charges and multiplicities (so3lr_charge_spin.cpp:116-141),
+  // builds the charge/spin offset tables, uploads static per-atom data.
+  void prepare(const SystemSpec &spec);
+  const SystemSpec &spec() const { return spec_; }
+
+  // Device positions buffer for the prepared system (N x 3). Callers may write
+  // it directly (device-resident MD) or through upload_positions().
+  double *positions() { return x_.get(); }
+  void upload_positions(const double *host_x);
+  // Run the whole evaluation on stream(); outputs stay on the device.
+  void compute();
+  // Copy results to host (after compute(); synchronises the stream).
+  struct HostResult {
+    double energy = 0;
+    std::array<double, 6> virial{};
+  };
+  HostResult download(double *f, double *eatom, double *charges, double *ratios, double *e_learned, double *e_zbl,
+                      double *e_lr, double *e_elec, double *e_disp, double *image_energy);
+  const double *forces() const { return force_.get(); }
+  const double *energy_device() const { return totals_.get(); }  // [0] energy, [1..6] virial
+  StepStats stats() const { return stats_; }
+  std::size_t device_bytes() const;
+
+  // velocity-Verlet MD on the device (LAMMPS metal units); masses in g/mol
+  void md_setup(const double *host_v, const double *host_mass);
+  void md_steps(int nsteps, double dt_ps);
+  void md_download(double *x, double *v);
+
+ private:
+  Model model_;
+  int device_ = 0;
+  cudaStream_t stream_ = nullptr;
+  SystemSpec spec_;
+  StepStats stats_;
+
+  // weights
+  DeviceArray<double> wbuf_;
+  std::vector<BlockW> blocks_;
+  HeadsW heads_{};
+  RadialW rad_{};
+  ZblDev zbl_{};
+  LrDev lr_{};
+  const double *emb_w_ = nullptr, *alpha_ref_ = nullptr, *c6_ref_ = nullptr;
+  int ref_table_ = 0;
+  double inv_emb_scale_ = 1.0, norm_ = 1.0, sr_cut_ = 0, lr_cut_ = 0;
+  int layers_ = 0;
+
+  // static per-system data
+  DeviceArray<int> z_, image_of_, image_start_, table_of_atom_;
+  DeviceArray<double> cs_tables_, image_charge_;
+  bool any_charge_spin_ = false;
+
+  // neighbour state
+  NeighborState nb_{};
+  DeviceArray<double> xw_;
+  DeviceArray<int> cell_, cell_count_, cell_start_, cell_fill_, cell_atoms_;
+  DeviceArray<int> deg_, row_start_, nbr_, img_, primary_, rev_, pair_scan_, edge_pair_;
+  DeviceArray<int> pair_a_, pair_b_, pair_img_, pair_edge_, scan_scratch_, small_ints_;
+  int *host_small_ = nullptr;  // pinned
+  double *host_totals_ = nullptr;
+
+  // per-pair arrays
+  DeviceArray<double> geo_, sh_, gv_, gl0_, pair_sc_;
+  std::vector<std::unique_ptr<DeviceArray<double>>> f_inv_, f_ev_;
+
+  // per-atom arrays
+  DeviceArray<double> x_, v_, inv_mass_, force_;
+  std::vector<std::unique_ptr<DeviceArray<double>>> xb_, evb_, qkv_, xhat1_, rstd1_, n1_, A_, hp_, gate_, xhat2_, rstd2_;
+  DeviceArray<double> d_inv_, d_ev_, act_, cat_, t_, hpre_, hcat_, hk_, e_nn_, raw_q_, q_, ratio_;
+  DeviceArray<double> e_lr_, e_elec_, e_disp_, dq_, dh_, f_lr_, w_lr_, img_sums_, dq_mean_;
+  DeviceArray<double> g_hcat_, g_x_, g_x2_, g_ev_, g_ev2_, g_t_, g_cat_, g_hp_, g_n1_, g_a_, g_A_, g_qkv_;
+  DeviceArray<double> e_atom_, e_zbl_, w_atom_, totals_, image_energy_;
+
+  void upload_weights();
+  void alloc_atoms();
+  void build_neighbors();
+};
+
+}  // namespace so3lr_b200

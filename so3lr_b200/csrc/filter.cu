@@ -1,0 +1,390 @@
+// Radial/equivariant filter MLPs of the attention block, forward and reverse,
+// evaluated once per undirected short-range pair on FP64 tensor cores (DMMA).
+//
+// Reference: src/kokkos_integrated_block0.cpp:138-163 (cutoff + Bernstein basis),
+// :166-192 (edge L0 invariants), :194-255 (the two filter MLPs); reverse:
+// src/kokkos_block2_attention_input_reverse.cpp:186-336 (filter input gradients,
+// L0 reverse, radial/cutoff reverse) and src/kokkos_learned_energy_forces.cpp:241-306
+// (geometry VJP).
+//
+// Why pairs: the filter of directed edge s->r depends on |x_r - x_s| and on
+// sum (ev_s - ev_r)^2, both symmetric in (s, r), so both directions share one
+// value. The reference evaluates it for every directed edge; here each pair
+// evaluates it once and both directions read it. In reverse, the filter VJP is
+// linear in the incoming gradient, so the two directions' gradients are summed
+// first and pushed through the MLP once.
+//
+// Tile: 64 pairs per CTA, 8 warps, each warp owns a 32x32 block of the 64x128
+// output and issues m8n8k4 DMMA on fragments read from shared memory (pair
+// activations) and L2-resident weights.
+#include "kernels.cuh"
+#include "sh.cuh"
+
+namespace so3lr_b200 {
+namespace {
+
+constexpr int TP = 64;     // pairs per tile
+constexpr int LDU = 132;   // padded stride of 128-wide smem tiles (conflict-free fragment reads)
+constexpr int LDR = 36;    // padded stride of 32-wide smem tiles
+
+__device__ inline void compute_rbf(const double *rr, double *rbf, const RadialW &rad) {
+  const int pl = threadIdx.x >> 2;
+  const int k0 = (threadIdx.x & 3) * 8;
+  const double r = rr[pl];
+  double x = exp(-rad.gamma * r);
+  if (x < 1.0e-6) x = 1.0e-6;
+  if (x > 1.0 - 1.0e-6) x = 1.0 - 1.0e-6;
+  const double lx = log(x), l1x = log(1.0 - x);
+#pragma unroll
+  for (int k = k0; k < k0 + 8; ++k) rbf[pl * LDR + k] = exp(rad.b[k] + rad.k[k] * lx + rad.kr[k] * l1x);
+}
+
+__device__ inline void compute_l0(int P, int p0, const int *pa, const int *pb, const double *ev, const double *cg,
+                                  double *l0) {
+  const int pl = threadIdx.x >> 2, d = threadIdx.x & 3;
+  const int p = p0 + pl;
+  double v = 0.0;
+  if (ev != nullptr && p < P) {
+    const int a = pa[p], b = pb[p];
+    const int m0 = d == 0 ? 0 : (d == 1 ? 3 : (d == 2 ? 8 : 15));
+    const int m1 = d == 0 ? 3 : (d == 1 ? 8 : (d == 2 ? 15 : 24));
+    for (int m = m0; m < m1; ++m) {
+      const double diff = ev[(size_t)b * kEV + m] - ev[(size_t)a * kEV + m];
+      v += diff * diff * cg[m];
+    }
+  }
+  l0[pl * 4 + d] = v;
+}
+
+// acc[mi][ni][2] += A(64 x K, smem, row stride lda) * B(K x 128), B(k, n) = W[n * K + k]
+template <int K>
+__device__ inline void mma_rows_wT(double (&acc)[4][4][2], const double *A, int lda, const double *__restrict__ W,
+                                   int wm, int wn, int g, int t) {
+#pragma unroll 4
+  for (int k0 = 0; k0 < K; k0 += 4) {
+    double a[4], b[4];
+#pragma unroll
+    for (int mi = 0; mi < 4; ++mi) a[mi] = A[(wm * 32 + mi * 8 + g) * lda + k0 + t];
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni) b[ni] = __ldg(W + (wn * 32 + ni * 8 + g) * K + k0 + t);
+#pragma unroll
+    for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) dmma(acc[mi][ni][0], acc[mi][ni][1], a[mi], b[ni]);
+  }
+}
+
+// acc[mi][ni][2] += A(64 x 128, smem) * B(128 x 128), B(k, n) = W[k * 128 + n]
+__device__ inline void mma_rows_w(double (&acc)[4][4][2], const double *A, const double *__restrict__ W, int wm,
+                                  int wn, int g, int t) {
+#pragma unroll 4
+  for (int k0 = 0; k0 < 128; k0 += 4) {
+    double a[4], b[4];
+#pragma unroll
+    for (int mi = 0; mi < 4; ++mi) a[mi] = A[(wm * 32 + mi * 8 + g) * LDU + k0 + t];
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni) b[ni] = __ldg(W + (k0 + t) * 128 + wn * 32 + ni * 8 + g);
+#pragma unroll
+    for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) dmma(acc[mi][ni][0], acc[mi][ni][1], a[mi], b[ni]);
+  }
+}
+
+// acc[ni][2] (8 rows x 32 cols per warp) += A(8 rows at row0, K=128, smem LDU) * B(128 x 32), B(k, n) = W[k*32 + n]
+__device__ inline void mma_8x32_w(double (&acc)[4][2], const double *A, int row0, const double *__restrict__ W, int g,
+                                  int t) {
+#pragma unroll 4
+  for (int k0 = 0; k0 < 128; k0 += 4) {
+    const double a = A[(row0 + g) * LDU + k0 + t];
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni) {
+      const double b = __ldg(W + (k0 + t) * 32 + ni * 8 + g);
+      dmma(acc[ni][0], acc[ni][1], a, b);
+    }
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// forward: f_inv[p][128], f_ev[p][128]
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_filter_forward(int P, const double *__restrict__ geo,
+                                                        const int *__restrict__ pa, const int *__restrict__ pb,
+                                                        const double *__restrict__ ev, const double *__restrict__ cg,
+                                                        FilterW finv, FilterW fev, RadialW rad,
+                                                        double *__restrict__ f_inv, double *__restrict__ f_ev) {
+  extern __shared__ double sm[];
+  double *rbf = sm;               // TP x LDR
+  double *u = rbf + TP * LDR;     // TP x LDU
+  double *w = u + TP * LDU;       // TP x LDR
+  double *l0 = w + TP * LDR;      // TP x 4
+  double *rr = l0 + TP * 4;       // TP
+  const int p0 = blockIdx.x * TP;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int wm = warp >> 2, wn = warp & 3;
+  if (tid < TP) {
+    const int p = p0 + tid;
+    rr[tid] = p < P ? geo[(size_t)p * kGeo] : 1.0;
+  }
+  compute_l0(P, p0, pa, pb, ev, cg, l0);
+  __syncthreads();
+  compute_rbf(rr, rbf, rad);
+  __syncthreads();
+  for (int filt = 0; filt < 2; ++filt) {
+    const FilterW &W = filt ? fev : finv;
+    double *out = filt ? f_ev : f_inv;
+    {  // ev branch hidden layer: w = silu(L0 V0^T + c0), 64 x 32
+      const int pl = tid >> 2, j0 = (tid & 3) * 8;
+      const double l00 = l0[pl * 4], l01 = l0[pl * 4 + 1], l02 = l0[pl * 4 + 2], l03 = l0[pl * 4 + 3];
+#pragma unroll
+      for (int j = j0; j < j0 + 8; ++j) {
+        const double s = l00 * W.v0[j * 4] + l01 * W.v0[j * 4 + 1] + l02 * W.v0[j * 4 + 2] + l03 * W.v0[j * 4 + 3];
+        w[pl * LDR + j] = silu(s + W.c0[j]);
+      }
+    }
+    double acc[4][4][2];
+#pragma unroll
+    for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
+    mma_rows_wT<kR>(acc, rbf, LDR, W.w0, wm, wn, g, t);
+#pragma unroll
+    for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) {
+        const int row = wm * 32 + mi * 8 + g, col = wn * 32 + ni * 8 + 2 * t;
+        u[row * LDU + col] = silu(acc[mi][ni][0] + W.b0[col]);
+        u[row * LDU + col + 1] = silu(acc[mi][ni][1] + W.b0[col + 1]);
+        acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
+      }
+    __syncthreads();
+    mma_rows_wT<kF>(acc, u, LDU, W.w1, wm, wn, g, t);
+    mma_rows_wT<kEH>(acc, w, LDR, W.v1, wm, wn, g, t);
+#pragma unroll
+    for (int mi = 0; mi < 4; ++mi) {
+      const int row = wm * 32 + mi * 8 + g;
+      const int p = p0 + row;
+      if (p >= P) continue;
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) {
+        const int col = wn * 32 + ni * 8 + 2 * t;
+        double2 v;
+        v.x = (acc[mi][ni][0] + W.b1[col]) + W.c1[col];
+        v.y = (acc[mi][ni][1] + W.b1[col + 1]) + W.c1[col + 1];
+        *reinterpret_cast<double2 *>(out + (size_t)p * kF + col) = v;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+void launch_filter_forward(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
+                           const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,
+                           double *f_inv, double *f_ev, cudaStream_t s) {
+  if (P == 0) return;
+  const size_t smem = sizeof(double) * (TP * LDR * 2 + TP * LDU + TP * 4 + TP);
+  static bool configured = false;
+  if (!configured) {
+    SO3_CUDA(cudaFuncSetAttribute(k_filter_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    configured = true;
+  }
+  k_filter_forward<<<(P + TP - 1) / TP, 256, smem, s>>>(P, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad, f_inv,
+                                                         f_ev);
+  SO3_LAUNCH("filter_forward");
+}
+
+// ---------------------------------------------------------------------------
+// reverse: filter input gradients for both directions of every pair, then the
+// radial, cutoff and spherical-harmonic gradients accumulated into gv[p] (3)
+// and, when ev is live, the L0 gradient gl0[p][4].
+// pair_sc[p][32] = alpha_inv, alpha_ev, s_inv, s_ev for the direction into the
+// pair's primary receiver ("in", [0:16]) and out of it ("out", [16:32]).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_filter_reverse(
+    int P, const double *__restrict__ geo, const double *__restrict__ sh, const int *__restrict__ pa,
+    const int *__restrict__ pb, const double *__restrict__ ev, const double *__restrict__ cg, FilterW finv,
+    FilterW fev, RadialW rad, const double *__restrict__ qkv, const double *__restrict__ gA,
+    const double *__restrict__ pair_sc, double norm, int need_l0, double *__restrict__ gv,
+    double *__restrict__ gl0) {
+  extern __shared__ double sm[];
+  double *rbf = sm;             // TP x LDR
+  double *gF = rbf + TP * LDR;  // TP x LDU
+  double *gw = gF + TP * LDU;   // TP x LDR
+  double *l0 = gw + TP * LDR;   // TP x 4
+  double *gl = l0 + TP * 4;     // TP x 4 (L0 gradient accumulator)
+  double *rr = gl + TP * 4;     // TP
+  const int p0 = blockIdx.x * TP;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int wm = warp >> 2, wn = warp & 3;
+  if (tid < TP) {
+    const int p = p0 + tid;
+    rr[tid] = p < P ? geo[(size_t)p * kGeo] : 1.0;
+  }
+  gl[tid] = 0.0;
+  compute_l0(P, p0, pa, pb, need_l0 ? ev : nullptr, cg, l0);
+  __syncthreads();
+  compute_rbf(rr, rbf, rad);
+  double grbf_acc[4][2];
+#pragma unroll
+  for (int ni = 0; ni < 4; ++ni) grbf_acc[ni][0] = grbf_acc[ni][1] = 0.0;
+
+  for (int filt = 0; filt < 2; ++filt) {
+    const FilterW &W = filt ? fev : finv;
+    const int qproj = filt ? 3 : 0, kproj = filt ? 4 : 1;
+    const int sc_in = filt ? 12 : 8, sc_out = filt ? 28 : 24;
+    // gF[pl][c] = phi/norm * (s_in[h] q_a[c] k_b[c] + s_out[h] q_b[c] k_a[c]); warp per pair, lane owns 4 channels
+    for (int pl = warp; pl < TP; pl += 8) {
+      const int p = p0 + pl;
+      double v[4] = {0, 0, 0, 0};
+      if (p < P) {
+        const int a = pa[p], b = pb[p];
+        const int h = lane >> 3, o = (lane & 7) * 4;
+        const double phi = geo[(size_t)p * kGeo + 4];
+        const double s_in = pair_sc[(size_t)p * kPairScalars + sc_in + h];
+        const double s_out = pair_sc[(size_t)p * kPairScalars + sc_out + h];
+        const double ci = phi / norm * s_in, co = phi / norm * s_out;
+        const double *qa = qkv + (size_t)a * kQKV + h * 160 + qproj * 32 + o;
+        const double *ka = qkv + (size_t)a * kQKV + h * 160 + kproj * 32 + o;
+        const double *qb = qkv + (size_t)b * kQKV + h * 160 + qproj * 32 + o;
+        const double *kb = qkv + (size_t)b * kQKV + h * 160 + kproj * 32 + o;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = ci * (qa[j] * kb[j]) + co * (qb[j] * ka[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) gF[pl * LDU + lane * 4 + j] = v[j];
+    }
+    __syncthreads();
+    // recompute the hidden pre-activation of the rbf branch: sp = silu'(rbf W0^T + b0)
+    double sp[4][4][2];
+#pragma unroll
+    for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) sp[mi][ni][0] = sp[mi][ni][1] = 0.0;
+    mma_rows_wT<kR>(sp, rbf, LDR, W.w0, wm, wn, g, t);
+#pragma unroll
+    for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) {
+        const int col = wn * 32 + ni * 8 + 2 * t;
+        sp[mi][ni][0] = silu_prime(sp[mi][ni][0] + W.b0[col]);
+        sp[mi][ni][1] = silu_prime(sp[mi][ni][1] + W.b0[col + 1]);
+      }
+    // g_hidden = gF W1 (B(k=c, n=j) = W1[c][j]) then times silu'
+    double acc[4][4][2];
+#pragma unroll
+    for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
+    mma_rows_w(acc, gF, W.w1, wm, wn, g, t);
+    // ev branch: g_w = gF V1 (64 x 32), warp w owns rows 8w..8w+7
+    double gwa[4][2];
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni) gwa[ni][0] = gwa[ni][1] = 0.0;
+    mma_8x32_w(gwa, gF, warp * 8, W.v1, g, t);
+    __syncthreads();  // everyone is done reading gF
+#pragma unroll
+    for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) {
+        const int row = wm * 32 + mi * 8 + g, col = wn * 32 + ni * 8 + 2 * t;
+        gF[row * LDU + col] = acc[mi][ni][0] * sp[mi][ni][0];
+        gF[row * LDU + col + 1] = acc[mi][ni][1] * sp[mi][ni][1];
+      }
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni) {
+      const int row = warp * 8 + g, col = ni * 8 + 2 * t;
+      gw[row * LDR + col] = gwa[ni][0];
+      gw[row * LDR + col + 1] = gwa[ni][1];
+    }
+    __syncthreads();
+    // g_rbf += g_pre W0 (B(k=j, n=k') = W0[j][k'], W0 is [128][32])
+    mma_8x32_w(grbf_acc, gF, warp * 8, W.w0, g, t);
+    // L0 gradient: g_pe = g_w * silu'(L0 V0^T + c0); gl[d] += sum_j g_pe[j] V0[j][d]
+    if (need_l0) {
+      const int pl = tid >> 2, d = tid & 3;
+      const double l00 = l0[pl * 4], l01 = l0[pl * 4 + 1], l02 = l0[pl * 4 + 2], l03 = l0[pl * 4 + 3];
+      double s = 0.0;
+      for (int j = 0; j < kEH; ++j) {
+        const double pe = l00 * W.v0[j * 4] + l01 * W.v0[j * 4 + 1] + l02 * W.v0[j * 4 + 2] + l03 * W.v0[j * 4 + 3] + W.c0[j];
+        s += gw[pl * LDR + j] * silu_prime(pe) * W.v0[j * 4 + d];
+      }
+      gl[pl * 4 + d] += s;
+    }
+    __syncthreads();
+  }
+  // g_rbf -> smem (reuse gw)
+#pragma unroll
+  for (int ni = 0; ni < 4; ++ni) {
+    const int row = warp * 8 + g, col = ni * 8 + 2 * t;
+    gw[row * LDR + col] = grbf_acc[ni][0];
+    gw[row * LDR + col + 1] = grbf_acc[ni][1];
+  }
+  __syncthreads();
+  // per pair: radial + cutoff + SH gradients -> gv; warp per pair
+  for (int pl = warp; pl < TP; pl += 8) {
+    const int p = p0 + pl;
+    if (p >= P) continue;
+    const double *gp = geo + (size_t)p * kGeo;
+    const double r = gp[0], ux = gp[1], uy = gp[2], uz = gp[3], phi = gp[4], dphi = gp[5];
+    // Bernstein derivative (block2_attention_input_reverse.cpp:322-333)
+    const double raw_x = exp(-rad.gamma * r);
+    double gr = 0.0;
+    if (raw_x > 1.0e-6 && raw_x < 1.0 - 1.0e-6) {
+      const double dl = -rad.gamma * rad.k[lane] + rad.gamma * rad.kr[lane] * raw_x / (1.0 - raw_x);
+      gr = gw[pl * LDR + lane] * rbf[pl * LDR + lane] * dl;
+    }
+    // cutoff gradient: sum over heads of alpha*s for both directions
+    const double *sc = pair_sc + (size_t)p * kPairScalars;
+    const int h = lane & 3, which = lane >> 2;  // which: 0..7 -> (alpha, s) pairs below
+    double gphi_term = 0.0;
+    if (which < 4) {
+      // (alpha_in_inv, s_in_inv), (alpha_in_ev, s_in_ev), (alpha_out_inv, s_out_inv), (alpha_out_ev, s_out_ev)
+      const int ao = which == 0 ? 0 : (which == 1 ? 4 : (which == 2 ? 16 : 20));
+      gphi_term = sc[ao + h] * sc[ao + 8 + h];
+    }
+    gr += gphi_term * dphi;
+    // spherical-harmonic gradient (pair orientation)
+    double gy = 0.0;
+    if (lane < kEV) {
+      const int d = degree_of_channel(lane);
+      const double a_in = sc[4 + d], a_out = sc[20 + d];
+      const double gAa = gA[(size_t)pa[p] * kEV + lane], gAb = gA[(size_t)pb[p] * kEV + lane];
+      gy = phi * (a_in * gAa + parity_sign(d) * a_out * gAb);
+    }
+    __shared__ double ybuf[8][kEV];
+    if (lane < kEV) ybuf[warp][lane] = gy;
+    for (int off = 16; off > 0; off >>= 1) gr += __shfl_xor_sync(0xffffffffu, gr, off);
+    __syncwarp();
+    if (lane == 0) {
+      double gux, guy, guz;
+      real_sh_vjp(ux, uy, uz, ybuf[warp], gux, guy, guz);
+      const double rad_c = ux * gux + uy * guy + uz * guz;
+      const double ir = r > 1.0e-14 ? 1.0 / r : 0.0;
+      gv[3 * p] += gr * ux + (gux - ux * rad_c) * ir;
+      gv[3 * p + 1] += gr * uy + (guy - uy * rad_c) * ir;
+      gv[3 * p + 2] += gr * uz + (guz - uz * rad_c) * ir;
+    }
+    if (need_l0 && lane < 4) gl0[(size_t)p * 4 + lane] = gl[pl * 4 + lane];
+    __syncwarp();
+  }
+}
+
+void launch_filter_reverse(int P, const double *geo, const double *sh, const int *pair_a, const int *pair_b,
+                           const double *ev, const double *cg_att, const FilterW &finv, const FilterW &fev,
+                           const RadialW &rad, const double *qkv, const double *gA, const double *pair_sc,
+                           double norm, bool need_l0, double *gv, double *gl0, cudaStream_t s) {
+  if (P == 0) return;
+  const size_t smem = sizeof(double) * (TP * LDR * 2 + TP * LDU + TP * 8 + TP);
+  static bool configured = false;
+  if (!configured) {
+    SO3_CUDA(cudaFuncSetAttribute(k_filter_reverse, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    configured = true;
+  }
+  k_filter_reverse<<<(P + TP - 1) / TP, 256, smem, s>>>(P, geo, sh, pair_a, pair_b, ev, cg_att, finv, fev, rad, qkv,
+                                                         gA, pair_sc, norm, need_l0 ? 1 : 0, gv, gl0);
+  SO3_LAUNCH("filter_reverse");
+}
+
+}  // namespace so3lr_b200

@@ -1,0 +1,450 @@
+// Per-pair geometry (distance, real spherical harmonics, PhysNet cutoff, learned
+// ZBL), the long-range physics kernel, force/energy/virial assembly, the
+// deterministic segment sums and the velocity-Verlet integrator.
+//
+// Reference arithmetic restated here:
+//   real SH l=1..4 and their input VJP: src/kokkos_learned_energy_forces.cpp:14-139
+//   PhysNet cutoff: src/kokkos_integrated_block0.cpp:145-155 (derivative: block2_attention_input_reverse.cpp:314-321)
+//   learned ZBL: src/kokkos_physical_zbl.cpp:81-178
+//   long range (erf Coulomb, shifted force + switch; QDO dispersion): src/kokkos_physical_long_range.cpp:11-380
+//   virial: plugins/lammps/pair_so3lr_native_mpi.cpp:944-990
+// The reference accumulates atoms with float atomics; here every per-atom sum is
+// a gather over the atom's own CSR row or cell stencil in a fixed order.
+#include "cells.cuh"
+#include "sh.cuh"
+
+namespace so3lr_b200 {
+
+// ---------------------------------------------------------------------------
+// geometry of every undirected short-range pair
+// ---------------------------------------------------------------------------
+__global__ void k_pair_geometry(int P, const int *__restrict__ pa, const int *__restrict__ pb,
+                                const int *__restrict__ pimg, const double *__restrict__ xw, CellGrid g,
+                                const int *__restrict__ z, ZblDev zbl, double rc, double *__restrict__ geo,
+                                double *__restrict__ sh, double *__restrict__ gv) {
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= P) return;
+  const int a = pa[p], b = pb[p];
+  int sx, sy, sz;
+  unpack_image(pimg[p], sx, sy, sz);
+  const double vx = xw[3 * a] - (xw[3 * b] + sx * g.len[0]);
+  const double vy = xw[3 * a + 1] - (xw[3 * b + 1] + sy * g.len[1]);
+  const double vz = xw[3 * a + 2] - (xw[3 * b + 2] + sz * g.len[2]);
+  const double r = sqrt(vx * vx + vy * vy + vz * vz);
+  const double inv = r > 1.0e-14 ? 1.0 / r : 0.0;
+  const double ux = vx * inv, uy = vy * inv, uz = vz * inv;
+  double y[kEV];
+  real_sh(ux, uy, uz, y);
+  for (int m = 0; m < kEV; ++m) sh[(size_t)p * kEV + m] = y[m];
+  // PhysNet cutoff 1 - 10x^3 + 15x^4 - 6x^5 and its derivative
+  double phi = 0.0, dphi = 0.0;
+  if (r < rc) {
+    const double x = r / rc, x2 = x * x, x3 = x2 * x;
+    phi = 1.0 - 10.0 * x3 + 15.0 * x3 * x - 6.0 * x3 * x2;
+    const double om = 1.0 - x;
+    dphi = -30.0 * x * x * om * om / rc;
+  }
+  // learned ZBL, directed edge b -> a (identical value for a -> b)
+  double e_dir = 0.0, de_pair = 0.0;
+  if (r > 0.0 && !(r > zbl.cutoff * (1.0 + 1.0e-12))) {
+    const double zi = double(z[a]), zj = double(z[b]), zz = zi * zj;
+    const double xn = r / zbl.cutoff, x2 = xn * xn, x3 = x2 * xn;
+    const double cut = r < zbl.cutoff ? 1.0 - 10.0 * x3 + 15.0 * x3 * xn - 6.0 * x3 * x2 : 0.0;
+    const double dcut = r < zbl.cutoff ? (-30.0 * x2 + 60.0 * x3 - 30.0 * x3 * xn) / zbl.cutoff : 0.0;
+    const double c = r / zbl.switch_off;
+    const double left = 1.0 - c, right = c;
+    const double sl_ = left > 1.0e-12 ? left : 1.0e-12, sr_ = right > 1.0e-12 ? right : 1.0e-12;
+    const double sig_l = left > 0.0 ? exp(-1.0 / sl_) : 0.0;
+    const double sig_r = right > 0.0 ? exp(-1.0 / sr_) : 0.0;
+    const double den = sig_l + sig_r + 1.0e-12;
+    const double dl = left > 0.0 ? -sig_l / (sl_ * sl_) : 0.0;
+    const double dr = right > 0.0 ? sig_r / (sr_ * sr_) : 0.0;
+    const double sw = sig_l / den;
+    const double dsw = ((dl * den - sig_l * (dl + dr)) / (den * den)) / zbl.switch_off;
+    const double safe_r = r > 1.0e-6 ? r : 1.0e-6;
+    const double ir = 1.0 / safe_r;
+    const double dir = r > 1.0e-6 ? -1.0 / (r * r) : 0.0;
+    const double xx = zbl.ke * cut * zz * ir;
+    const double dxx = zbl.ke * zz * (dcut * ir + cut * dir);
+    const double rate = (pow(zi, zbl.p) + pow(zj, zbl.p)) * zbl.d;
+    const double rzd = r * rate;
+    double yy = 0.0, dyy = 0.0;
+    for (int k = 0; k < 4; ++k) {
+      const double ex = exp(-zbl.a[k] * rzd);
+      yy += zbl.c[k] * ex;
+      dyy -= zbl.c[k] * zbl.a[k] * rate * ex;
+    }
+    e_dir = 0.5 * sw * xx * yy;
+    de_pair = 2.0 * (0.5 * (dsw * xx * yy + sw * dxx * yy + sw * xx * dyy));
+  }
+  double *gp = geo + (size_t)p * kGeo;
+  gp[0] = r; gp[1] = ux; gp[2] = uy; gp[3] = uz;
+  gp[4] = phi; gp[5] = dphi; gp[6] = e_dir; gp[7] = de_pair;
+  gv[3 * p] = de_pair * ux;
+  gv[3 * p + 1] = de_pair * uy;
+  gv[3 * p + 2] = de_pair * uz;
+}
+
+void launch_pair_geometry(int P, const NeighborState &nb, const int *z, ZblDev zbl, double sr_cutoff,
+                          double *geo, double *sh, double *gv, cudaStream_t s) {
+  if (P == 0) return;
+  k_pair_geometry<<<(P + 127) / 128, 128, 0, s>>>(P, nb.pair_a, nb.pair_b, nb.pair_img, nb.xw, nb.grid, z, zbl,
+                                                   sr_cutoff, geo, sh, gv);
+  SO3_LAUNCH("pair_geometry");
+}
+
+// ---------------------------------------------------------------------------
+// long range: erf-screened shifted-force Coulomb + QDO dispersion
+// ---------------------------------------------------------------------------
+__device__ inline void smooth_switch(double r, double cuton, double cutoff, double &v, double &dv) {
+  if (r >= cutoff) {
+    v = 0.0;
+    dv = 0.0;
+    return;
+  }
+  const double width = cutoff - cuton;
+  const double c = (r - cuton) / width;
+  const double left = 1.0 - c, right = c;
+  const double sl = left > 1.0e-12 ? left : 1.0e-12, sr = right > 1.0e-12 ? right : 1.0e-12;
+  const double sig_l = left > 0.0 ? exp(-1.0 / sl) : 0.0;
+  const double sig_r = right > 0.0 ? exp(-1.0 / sr) : 0.0;
+  const double den = sig_l + sig_r + 1.0e-12;
+  v = sig_l / den;
+  const double dl = left > 0.0 ? -sig_l / (sl * sl) : 0.0;
+  const double dr = right > 0.0 ? sig_r / (sr * sr) : 0.0;
+  dv = ((dl * den - sig_l * (dl + dr)) / (den * den)) / width;
+}
+
+struct LrPair {
+  double e_elec, e_disp, dq, dh, radial;
+};
+
+// One unordered pair seen from atom i (its partner j); r > 0 and r < cutoff.
+__device__ inline LrPair lr_pair(const LrDev &p, double r, double qi, double qj, double hi, double hj, int zi,
+                                 int zj, const double *__restrict__ aref, const double *__restrict__ cref,
+                                 int table) {
+  constexpr double inv_sqrt_pi = 0.56418958354775628695;
+  LrPair o{0, 0, 0, 0, 0};
+  double esw, desw;
+  smooth_switch(r, p.elec_cuton, p.cutoff, esw, desw);
+  const double ratio = r / p.sigma;
+  const double erf_t = erf(ratio);
+  const double exp_t = exp(-(ratio * ratio));
+  const double pot = erf_t / r;
+  const double dpot = (2.0 * r * exp_t * inv_sqrt_pi / p.sigma - erf_t) / (r * r);
+  const double disp = r - p.cutoff;
+  const double shifted = pot - p.shift - p.fshift * disp;
+  const double kernel = esw * (pot - p.shift) + (1.0 - esw) * shifted;
+  const double rkernel = dpot - (1.0 - esw) * p.fshift + desw * p.fshift * disp;
+  o.e_elec = p.full_scale * p.ke * qi * qj * kernel;
+  o.dq = p.full_scale * p.ke * kernel * qj;
+  const double erad = p.full_scale * p.ke * qi * qj * rkernel;
+  double drad = 0.0;
+  const int zi0 = zi - 1, zj0 = zj - 1;
+  if (zi0 >= 0 && zj0 >= 0 && zi0 < table && zj0 < table) {
+    const double ai0 = aref[zi0], aj0 = aref[zj0], ci0 = cref[zi0], cj0 = cref[zj0];
+    const double ai = ai0 * hi, aj = aj0 * hj;
+    const double c6i = ci0 * hi * hi, c6j = cj0 * hj * hj;
+    const double alpha = 0.5 * (ai + aj);
+    const double num = 2.0 * c6i * c6j * aj * ai;
+    const double den = ai * ai * c6j + aj * aj * c6i;
+    if (alpha > 0.0 && den > 1.0e-30) {
+      const double c6 = num / den;
+      const double inv_den2 = 1.0 / (den * den);
+      const double dc6i = 2.0 * ci0 * hi;
+      const double dn_dhi = 2.0 * (dc6i * c6j * aj * ai + c6i * c6j * aj * ai0);
+      const double dd_dhi = 2.0 * ai * ai0 * c6j + aj * aj * dc6i;
+      const double dc6_dhi = (dn_dhi * den - num * dd_dhi) * inv_den2;
+      const double a7 = pow(alpha, 1.0 / 7.0);
+      const double rv = p.fine_factor * a7;
+      constexpr double b0 = -0.00433008, b1 = 0.24428889, b2 = 0.04125273, b3 = -0.00078893;
+      const double sig = b3 * rv * rv * rv + b2 * rv * rv + b1 * rv + b0;
+      const double gam = 0.5 / (sig * sig);
+      const double drv = rv / (7.0 * alpha);
+      const double dsig = (3.0 * b3 * rv * rv + 2.0 * b2 * rv + b1) * drv;
+      const double dgam = -2.0 * gam * dsig / sig;
+      const double c8 = 5.0 * c6 / gam;
+      const double c10 = 245.0 * c6 / (8.0 * gam * gam);
+      const double damp = p.disp_scale * 2.0 * 2.54 * a7;
+      const double ddamp = damp / (7.0 * alpha);
+      const double ra = r / p.bohr;
+      const double r2 = ra * ra, r4 = r2 * r2, r6 = r4 * r2, r8 = r4 * r4, r10 = r8 * r2;
+      const double p2 = damp * damp, p4 = p2 * p2, p6 = p4 * p2, p8 = p4 * p4, p10 = p8 * p2;
+      const double d6 = r6 + p6, d8 = r8 + p8, d10 = r10 + p10;
+      const double qdo = -c6 / d6 - c8 / d8 - c10 / d10;
+      const double rad_au = 6.0 * c6 * r4 * ra / (d6 * d6) + 8.0 * c8 * r6 * ra / (d8 * d8) +
+                            10.0 * c10 * r8 * ra / (d10 * d10);
+      const double dc8 = -c8 * dgam / gam;
+      const double dc10 = -2.0 * c10 * dgam / gam;
+      const double dd6 = 6.0 * p4 * damp * ddamp;
+      const double dd8 = 8.0 * p6 * damp * ddamp;
+      const double dd10 = 10.0 * p8 * damp * ddamp;
+      const double dpot_da = c6 * dd6 / (d6 * d6) - dc8 / d8 + c8 * dd8 / (d8 * d8) - dc10 / d10 +
+                             c10 * dd10 / (d10 * d10);
+      const double dpot_dc6 = -1.0 / d6 - (5.0 / gam) / d8 - (245.0 / (8.0 * gam * gam)) / d10;
+      const double dpot_dhi = dpot_dc6 * dc6_dhi + dpot_da * 0.5 * ai0;
+      double dsw, ddsw;
+      smooth_switch(r, p.disp_cuton, p.cutoff, dsw, ddsw);
+      o.e_disp = p.full_scale * p.hartree * qdo * dsw;
+      drad = p.full_scale * p.hartree * (rad_au * dsw / p.bohr + qdo * ddsw);
+      o.dh = p.full_scale * p.hartree * dsw * dpot_dhi;
+    }
+  }
+  o.radial = erad + drad;
+  return o;
+}
+
+__device__ inline double warp_sum(double v) {
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// one warp per atom; lanes stride over the candidates of each cell
+__global__ void __launch_bounds__(256) k_long_range(
+    int n, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
+    const int *__restrict__ cell_start, const int *__restrict__ cell_count, const int *__restrict__ cell_atoms,
+    const int *__restrict__ image_of, const int *__restrict__ image_start, int reach, double rc2,
+    const int *__restrict__ z, const double *__restrict__ q, const double *__restrict__ h,
+    const double *__restrict__ aref, const double *__restrict__ cref, int table, LrDev p,
+    double *__restrict__ e_lr, double *__restrict__ e_elec, double *__restrict__ e_disp, double *__restrict__ dq,
+    double *__restrict__ dh, double *__restrict__ f_lr, double *__restrict__ w_lr) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= n) return;
+  const int i = warp;
+  const double xi = xw[3 * i], yi = xw[3 * i + 1], zi = xw[3 * i + 2];
+  const double qi = q[i], hi = h[i];
+  const int Zi = z[i];
+  double acc_ee = 0, acc_ed = 0, acc_dq = 0, acc_dh = 0, fx = 0, fy = 0, fz = 0;
+  double wxx = 0, wyy = 0, wzz = 0, wxy = 0, wxz = 0, wyz = 0;
+  auto visit = [&](int j, double shx, double shy, double shz) {
+    const double vx = xw[3 * j] + shx - xi, vy = xw[3 * j + 1] + shy - yi, vz = xw[3 * j + 2] + shz - zi;
+    const double r2 = vx * vx + vy * vy + vz * vz;
+    if (!(r2 > 0.0 && r2 < rc2)) return;
+    const double r = sqrt(r2);
+    if (!(r > 1.0e-12)) return;
+    const LrPair o = lr_pair(p, r, qi, q[j], hi, h[j], Zi, z[j], aref, cref, table);
+    acc_ee += o.e_elec;
+    acc_ed += o.e_disp;
+    acc_dq += o.dq;
+    acc_dh += o.dh;
+    const double s = o.radial / r;
+    fx += s * vx;
+    fy += s * vy;
+    fz += s * vz;
+    wxx -= 0.5 * s * vx * vx;
+    wyy -= 0.5 * s * vy * vy;
+    wzz -= 0.5 * s * vz * vz;
+    wxy -= 0.5 * s * vx * vy;
+    wxz -= 0.5 * s * vx * vz;
+    wyz -= 0.5 * s * vy * vz;
+  };
+  if (!g.periodic) {
+    const int im = image_of[i];
+    for (int j = image_start[im] + lane; j < image_start[im + 1]; j += 32) visit(j, 0.0, 0.0, 0.0);
+  } else {
+    const int c = cell[i];
+    const int cx = c % g.ncell[0], cy = (c / g.ncell[0]) % g.ncell[1], cz = c / (g.ncell[0] * g.ncell[1]);
+    for (int oz = -reach; oz <= reach; ++oz) {
+      int wz = cz + oz, sz = 0;
+      while (wz < 0) { wz += g.ncell[2]; --sz; }
+      while (wz >= g.ncell[2]) { wz -= g.ncell[2]; ++sz; }
+      for (int oy = -reach; oy <= reach; ++oy) {
+        int wy = cy + oy, sy = 0;
+        while (wy < 0) { wy += g.ncell[1]; --sy; }
+        while (wy >= g.ncell[1]) { wy -= g.ncell[1]; ++sy; }
+        for (int ox = -reach; ox <= reach; ++ox) {
+          int wx = cx + ox, sx = 0;
+          while (wx < 0) { wx += g.ncell[0]; --sx; }
+          while (wx >= g.ncell[0]) { wx -= g.ncell[0]; ++sx; }
+          const int cc = (wz * g.ncell[1] + wy) * g.ncell[0] + wx;
+          const int *a = cell_atoms + cell_start[cc];
+          const int m = cell_count[cc];
+          const double shx = sx * g.len[0], shy = sy * g.len[1], shz = sz * g.len[2];
+          for (int t = lane; t < m; t += 32) visit(a[t], shx, shy, shz);
+        }
+      }
+    }
+  }
+  acc_ee = warp_sum(acc_ee);
+  acc_ed = warp_sum(acc_ed);
+  acc_dq = warp_sum(acc_dq);
+  acc_dh = warp_sum(acc_dh);
+  fx = warp_sum(fx);
+  fy = warp_sum(fy);
+  fz = warp_sum(fz);
+  wxx = warp_sum(wxx);
+  wyy = warp_sum(wyy);
+  wzz = warp_sum(wzz);
+  wxy = warp_sum(wxy);
+  wxz = warp_sum(wxz);
+  wyz = warp_sum(wyz);
+  if (lane == 0) {
+    e_elec[i] = 0.5 * acc_ee;
+    e_disp[i] = 0.5 * acc_ed;
+    e_lr[i] = 0.5 * acc_ee + 0.5 * acc_ed;
+    dq[i] = acc_dq;
+    dh[i] = acc_dh;
+    f_lr[3 * i] = fx;
+    f_lr[3 * i + 1] = fy;
+    f_lr[3 * i + 2] = fz;
+    double *w = w_lr + 6 * i;
+    w[0] = wxx; w[1] = wyy; w[2] = wzz; w[3] = wxy; w[4] = wxz; w[5] = wyz;
+  }
+}
+
+void launch_long_range(int n, const NeighborState &nb, double rc_lr, const int *z, const double *q,
+                       const double *h, const double *alpha_ref, const double *c6_ref, int table_size,
+                       LrDev p, double *e_lr, double *e_elec, double *e_disp, double *dq, double *dh,
+                       double *f_lr, double *w_lr, cudaStream_t s) {
+  if (n == 0) return;
+  const int reach = sr_reach(nb.grid, rc_lr);
+  const int threads = 256;
+  const int blocks = (n * 32 + threads - 1) / threads;
+  k_long_range<<<blocks, threads, 0, s>>>(n, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count, nb.cell_atoms,
+                                          nb.image_of, nb.image_start, reach, rc_lr * rc_lr, z, q, h, alpha_ref,
+                                          c6_ref, table_size, p, e_lr, e_elec, e_disp, dq, dh, f_lr, w_lr);
+  SO3_LAUNCH("long_range");
+}
+
+// ---------------------------------------------------------------------------
+// assembly: forces, per-atom energies, per-atom virial (gathers over the CSR)
+// ---------------------------------------------------------------------------
+__global__ void k_assemble(int n, const int *__restrict__ row_start, const int *__restrict__ edge_pair,
+                           const double *__restrict__ geo, const double *__restrict__ gv,
+                           const double *__restrict__ e_nn, const double *__restrict__ e_lr,
+                           const double *__restrict__ f_lr, const double *__restrict__ w_lr,
+                           double *__restrict__ force, double *__restrict__ e_atom, double *__restrict__ e_zbl,
+                           double *__restrict__ w_atom) {
+  const int a = blockIdx.x * blockDim.x + threadIdx.x;
+  if (a >= n) return;
+  double fx = 0, fy = 0, fz = 0, ez = 0;
+  double w[6] = {0, 0, 0, 0, 0, 0};
+  for (int e = row_start[a]; e < row_start[a + 1]; ++e) {
+    const int code = edge_pair[e];
+    const int p = code >= 0 ? code : ~code;
+    const double gx = gv[3 * p], gy = gv[3 * p + 1], gz = gv[3 * p + 2];
+    const double *gp = geo + (size_t)p * kGeo;
+    ez += gp[6];
+    if (code >= 0) {
+      fx -= gx; fy -= gy; fz -= gz;
+      const double r = gp[0];
+      const double vx = r * gp[1], vy = r * gp[2], vz = r * gp[3];
+      w[0] -= vx * gx;
+      w[1] -= vy * gy;
+      w[2] -= vz * gz;
+      w[3] -= 0.5 * (vx * gy + vy * gx);
+      w[4] -= 0.5 * (vx * gz + vz * gx);
+      w[5] -= 0.5 * (vy * gz + vz * gy);
+    } else {
+      fx += gx; fy += gy; fz += gz;
+    }
+  }
+  force[3 * a] = fx + f_lr[3 * a];
+  force[3 * a + 1] = fy + f_lr[3 * a + 1];
+  force[3 * a + 2] = fz + f_lr[3 * a + 2];
+  e_zbl[a] = ez;
+  e_atom[a] = e_nn[a] + ez + e_lr[a];
+  for (int k = 0; k < 6; ++k) w_atom[6 * a + k] = w[k] + w_lr[6 * a + k];
+}
+
+void launch_assemble(int n, const NeighborState &nb, const double *geo, const double *gv, const double *e_nn,
+                     const double *e_lr, const double *f_lr, const double *w_lr, double *force, double *e_atom,
+                     double *e_zbl, double *w_atom, cudaStream_t s) {
+  if (n == 0) return;
+  k_assemble<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row_start, nb.edge_pair, geo, gv, e_nn, e_lr, f_lr, w_lr, force,
+                                              e_atom, e_zbl, w_atom);
+  SO3_LAUNCH("assemble");
+}
+
+// ---------------------------------------------------------------------------
+// deterministic segmented sums (fixed thread order + fixed tree)
+// ---------------------------------------------------------------------------
+__global__ void k_segment_sum(const int *__restrict__ start, const double *__restrict__ v, int stride, int ncol,
+                              double *__restrict__ out) {
+  __shared__ double buf[256];
+  const int s = blockIdx.x;
+  const int b = start[s], e = start[s + 1];
+  for (int col = 0; col < ncol; ++col) {
+    double acc = 0.0;
+    for (int i = b + threadIdx.x; i < e; i += blockDim.x) acc += v[(size_t)i * stride + col];
+    buf[threadIdx.x] = acc;
+    __syncthreads();
+    for (int off = 128; off > 0; off >>= 1) {
+      if (threadIdx.x < off) buf[threadIdx.x] += buf[threadIdx.x + off];
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) out[(size_t)s * ncol + col] = buf[0];
+    __syncthreads();
+  }
+}
+
+void launch_segment_sum(int nseg, const int *start, const double *v, int stride, int ncol, double *out,
+                        cudaStream_t s) {
+  if (nseg == 0) return;
+  k_segment_sum<<<nseg, 256, 0, s>>>(start, v, stride, ncol, out);
+  SO3_LAUNCH("segment_sum");
+}
+
+// q = raw + (Q_img - sum_img raw) / N_img (output_heads.cpp:441-451; image_segments.cpp:49-98);
+// also the per-image mean of the charge seeds (image_segments.cpp:104-141).
+__global__ void k_charge_correct(int n, const double *__restrict__ raw, const double *__restrict__ raw_sum,
+                                 const double *__restrict__ qtot, const int *__restrict__ image_of,
+                                 const int *__restrict__ image_start, double *__restrict__ q) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int im = image_of[i];
+  const double count = double(image_start[im + 1] - image_start[im]);
+  q[i] = raw[i] + (qtot[im] - raw_sum[im]) / count;
+}
+__global__ void k_seed_mean(int nimg, const double *__restrict__ dq_sum, const int *__restrict__ image_start,
+                            double *__restrict__ mean) {
+  const int im = blockIdx.x * blockDim.x + threadIdx.x;
+  if (im >= nimg) return;
+  mean[im] = dq_sum[im] / double(image_start[im + 1] - image_start[im]);
+}
+
+void launch_charge_correct(int n, const double *raw, const double *raw_sum, const double *qtot,
+                           const int *image_of_atom, const int *image_start, double *q, double *dq_mean_out,
+                           const double *dq_sum, cudaStream_t s) {
+  if (q) {
+    k_charge_correct<<<(n + 255) / 256, 256, 0, s>>>(n, raw, raw_sum, qtot, image_of_atom, image_start, q);
+    SO3_LAUNCH("charge_correct");
+  }
+  if (dq_mean_out) {
+    // n here is the image count
+    k_seed_mean<<<(n + 255) / 256, 256, 0, s>>>(n, dq_sum, image_start, dq_mean_out);
+    SO3_LAUNCH("seed_mean");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// velocity Verlet (LAMMPS fix nve, metal units)
+// ---------------------------------------------------------------------------
+__global__ void k_verlet_first(int n, double *__restrict__ x, double *__restrict__ v, const double *__restrict__ f,
+                               const double *__restrict__ inv_mass, double dt, double dtf) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= 3 * n) return;
+  const double im = inv_mass[k / 3];
+  const double vv = v[k] + dtf * f[k] * im;
+  v[k] = vv;
+  x[k] += dt * vv;
+}
+__global__ void k_verlet_second(int n, double *__restrict__ v, const double *__restrict__ f,
+                                const double *__restrict__ inv_mass, double dtf) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= 3 * n) return;
+  v[k] += dtf * f[k] * inv_mass[k / 3];
+}
+void launch_verlet_first(int n, double *x, double *v, const double *f, const double *inv_mass, double dt,
+                         double ftm2v, cudaStream_t s) {
+  k_verlet_first<<<(3 * n + 255) / 256, 256, 0, s>>>(n, x, v, f, inv_mass, dt, 0.5 * dt * ftm2v);
+  SO3_LAUNCH("verlet_first");
+}
+void launch_verlet_second(int n, double *v, const double *f, const double *inv_mass, double dt, double ftm2v,
+                          cudaStream_t s) {
+  k_verlet_second<<<(3 * n + 255) / 256, 256, 0, s>>>(n, v, f, inv_mass, 0.5 * dt * ftm2v);
+  SO3_LAUNCH("verlet_second");
+}
+
+}  // namespace so3lr_b200

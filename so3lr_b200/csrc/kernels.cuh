@@ -1,0 +1,155 @@
+// Kernel launchers and device-state structures shared by the evaluator.
+#pragma once
+
+#include <algorithm>
+#include <cmath>
+
+#include "common.cuh"
+
+namespace so3lr_b200 {
+
+struct CellGrid {
+  int periodic = 0;
+  double lo[3] = {0, 0, 0};
+  double len[3] = {1, 1, 1};
+  int ncell[3] = {1, 1, 1};
+};
+
+struct NeighborState {
+  CellGrid grid;
+  int ncells = 0;
+  double *xw = nullptr;  // wrapped positions (N x 3)
+  int *cell = nullptr, *cell_count = nullptr, *cell_start = nullptr, *cell_fill = nullptr, *cell_atoms = nullptr;
+  int *image_of = nullptr, *image_start = nullptr;  // open boundaries: atom -> image, image CSR
+  int *deg = nullptr, *row_start = nullptr, *nbr = nullptr, *img = nullptr, *primary = nullptr, *rev = nullptr;
+  int *pair_scan = nullptr, *edge_pair = nullptr;
+  int *pair_a = nullptr, *pair_b = nullptr, *pair_img = nullptr, *pair_edge = nullptr;
+  int *scan_total = nullptr, *scan_scratch = nullptr, *error_flag = nullptr;
+};
+
+void exclusive_scan(const int *in, int *out, int n, int *total, int *scratch, cudaStream_t s);
+std::size_t scan_scratch_ints(std::size_t n);
+void build_cells(NeighborState &nb, int n, const double *x, cudaStream_t s);
+int sr_reach(const CellGrid &g, double rc);
+void count_sr(NeighborState &nb, int n, double rc, cudaStream_t s);
+void fill_sr(NeighborState &nb, int n, double rc, int E, cudaStream_t s);
+void fill_pairs(NeighborState &nb, int n, int E, cudaStream_t s);
+
+// ---- per-pair geometry -------------------------------------------------------
+// geo[p*8 + {0..7}] = r, ux, uy, uz, phi, dphi/dr, zbl directed energy, zbl pair dE/dr
+constexpr int kGeo = 8;
+struct ZblDev {
+  double ke, cutoff, switch_off, p, d, a[4], c[4];
+};
+void launch_pair_geometry(int P, const NeighborState &nb, const int *z, ZblDev zbl, double sr_cutoff,
+                          double *geo, double *sh, double *gv, cudaStream_t s);
+
+struct LrDev {
+  double ke, sigma, cutoff, elec_cuton, disp_cuton, fine_factor, bohr, hartree, disp_scale, full_scale;
+  double shift, fshift;
+};
+// Long-range Coulomb + dispersion over the full neighbour set of every atom
+// (cell stencil or image range). Per-atom outputs (N): energy (total, elec,
+// disp), dE/dq, dE/dh, direct force (3), virial (6).
+void launch_long_range(int n, const NeighborState &nb, double rc_lr, const int *z, const double *q,
+                       const double *h, const double *alpha_ref, const double *c6_ref, int table_size,
+                       LrDev p, double *e_lr, double *e_elec, double *e_disp, double *dq, double *dh,
+                       double *f_lr, double *w_lr, cudaStream_t s);
+
+// ---- filters (pair tiles, FP64 tensor cores) --------------------------------
+void launch_filter_forward(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
+                           const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,
+                           double *f_inv, double *f_ev, cudaStream_t s);
+void launch_filter_reverse(int P, const double *geo, const double *sh, const int *pair_a, const int *pair_b,
+                           const double *ev, const double *cg_att, const FilterW &finv, const FilterW &fev,
+                           const RadialW &rad, const double *qkv, const double *gA, const double *pair_sc,
+                           double norm, bool need_l0, double *gv, double *gl0, cudaStream_t s);
+
+// ---- attention (receiver CSR gathers) ----------------------------------------
+void launch_attention_forward(int n, const NeighborState &nb, const double *geo, const double *sh,
+                              const double *qkv, const double *f_inv, const double *f_ev, double norm,
+                              double *d_inv, double *d_ev, cudaStream_t s);
+void launch_attention_reverse(int n, const NeighborState &nb, const double *geo, const double *sh,
+                              const double *qkv, const double *f_inv, const double *f_ev, const double *g_a,
+                              const double *g_A, double norm, double *g_qkv, double *pair_sc,
+                              cudaStream_t s);
+void launch_ev_l0_reverse(int n, const NeighborState &nb, const double *ev, const double *cg_att,
+                          const double *gl0, const double *g_A, double *g_ev, cudaStream_t s);
+
+// ---- node GEMM (FP64 tensor cores) ------------------------------------------
+enum class Epi { None, Bias, BiasSilu, BiasStorePre, AddResidual, SiluPrimeMul, BiasResidual, GateSiluResidual };
+// C[M x N] = A[M x K] * B, B(k, n) = transB ? W[n*ldw + k] : W[k*ldw + n].
+// Epilogues:
+//   Bias:            C = acc + bias[n]
+//   BiasSilu:        C = silu(acc + bias[n])
+//   BiasStorePre:    pre = acc + bias[n] -> aux[m*ldaux+n]; C = silu(pre)
+//   AddResidual:     C = acc + aux[m*ldaux+n]
+//   BiasResidual:    C = acc + bias[n] + aux[m*ldaux+n]
+//   SiluPrimeMul:    C = acc * silu'(aux[m*ldaux+n])
+//   GateSiluResidual:C = aux2[m*ldaux+n] + acc * silu'(aux[m*ldaux+n])
+struct GemmArgs {
+  int M, N, K;
+  const double *A;
+  int lda;
+  const double *W;
+  int ldw;
+  bool transB;
+  double *C;
+  int ldc;
+  const double *bias = nullptr;
+  const double *aux = nullptr;
+  const double *aux2 = nullptr;
+  int ldaux = 0;
+  double *aux_out = nullptr;
+  Epi epi = Epi::None;
+  // batched over gridDim.z with per-batch strides (elements)
+  int batch = 1;
+  long long strideA = 0, strideW = 0, strideC = 0, strideAux = 0, strideBias = 0;
+};
+void launch_gemm(const GemmArgs &g, cudaStream_t s);
+// aux added only to columns < aux_cols; aux2 row stride ldaux2
+void launch_gemm_ex(const GemmArgs &g, int aux_cols, int ldaux2, cudaStream_t s);
+
+// ---- node elementwise / row kernels -----------------------------------------
+void launch_embedding(int n, const int *z, const double *emb_w, const double *cs_table, const int *image_of_atom,
+                      double inv_scale, double *x, cudaStream_t s);
+void launch_post_attn_pre(int n, const double *x, const double *d_inv, const double *ev, const double *d_ev,
+                          const double *lnw, const double *lnb, const double *cg_int, double *xhat1,
+                          double *rstd1, double *n1, double *act, double *A, double *cat, cudaStream_t s);
+void launch_post_attn_final(int n, const double *cat, const double *t, const double *A, const double *lnw,
+                            const double *lnb, double *xhat2, double *rstd2, double *gate, double *x_out,
+                            double *ev_out, cudaStream_t s);
+void launch_post_attn_rev_final(int n, const double *g_x, const double *g_ev, const double *xhat2,
+                                const double *rstd2, const double *lnw2, const double *A, const double *gate,
+                                double *g_t, double *g_A, cudaStream_t s);
+void launch_post_attn_rev_ln1(int n, const double *g_n1, const double *xhat1, const double *rstd1,
+                              const double *lnw1, const double *A, const double *cg_int, const double *g_cat,
+                              double *g_a, double *g_A, cudaStream_t s);
+void launch_add(int count, const double *a, double *b, cudaStream_t s);
+
+// heads
+void launch_heads_finalize(int n, const int *z, const double *hcat, const HeadsW &hw, double *hk_out,
+                           double *e_nn, double *raw_q, double *ratio, cudaStream_t s);
+void launch_heads_seed(int n, const int *z, const double *hpre, const double *hk, const HeadsW &hw,
+                       const double *dq, const double *dq_mean, const int *image_of_atom, const double *dh,
+                       double *g_hcat, cudaStream_t s);
+
+// deterministic segmented sums: out[s] = sum_{i in [start[s], start[s+1])} v[i*stride + col]
+void launch_segment_sum(int nseg, const int *start, const double *v, int stride, int ncol, double *out,
+                        cudaStream_t s);
+void launch_charge_correct(int n, const double *raw, const double *raw_sum, const double *qtot,
+                           const int *image_of_atom, const int *image_start, double *q, double *dq_mean_out,
+                           const double *dq_sum, cudaStream_t s);
+
+// final assembly: per-atom forces and energies, per-atom SR virial
+void launch_assemble(int n, const NeighborState &nb, const double *geo, const double *gv, const double *e_nn,
+                     const double *e_lr, const double *f_lr, const double *w_lr, double *force, double *e_atom,
+                     double *e_zbl, double *w_atom, cudaStream_t s);
+
+// MD integration (velocity Verlet, LAMMPS metal units)
+void launch_verlet_first(int n, double *x, double *v, const double *f, const double *inv_mass, double dt,
+                         double ftm2v, cudaStream_t s);
+void launch_verlet_second(int n, double *v, const double *f, const double *inv_mass, double dt, double ftm2v,
+                          cudaStream_t s);
+
+}  // namespace so3lr_b200

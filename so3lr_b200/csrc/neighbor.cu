@@ -1,0 +1,285 @@
+// Edge builder: cell lists -> deterministic short-range CSR -> undirected pairs.
+//
+// Replaces the reference's LAMMPS-list snapshot + candidate compaction
+// (plugins/lammps/pair_so3lr_native_mpi.cpp:76-105, 258-373;
+// src/lammps_neighbor_adapter.cpp:122-212). The reference keeps every directed
+// candidate with 0 < r^2 < rc^2 (pair_so3lr_native_mpi.cpp:283-286); so does this
+// builder, from positions alone, every step.
+//
+// Output layout (all device, int32 indices):
+//   row_start[N+1]            CSR over receivers
+//   nbr[E], img[E]            sender atom and packed periodic image of the sender
+//   edge_pair[E]              pair id (>= 0: edge is the pair's primary direction,
+//                             ~pid: reverse direction)
+//   pair_a[P], pair_b[P], pair_img[P], pair_edge[P]   primary receiver, sender,
+//                             sender image, primary edge
+// The edge vector is v = xw[r] - (xw[s] + img * L) with xw the wrapped positions.
+// Each receiver's entries are sorted by (sender, image), so the CSR does not depend
+// on the cell layout or on thread scheduling.
+#include "cells.cuh"
+
+namespace so3lr_b200 {
+
+// ---- exclusive scan (deterministic, three-phase) --------------------------
+namespace {
+constexpr int kScanBlock = 1024;
+
+__global__ void k_scan_blocks(const int *in, int *out, int *block_sums, int n) {
+  __shared__ int buf[kScanBlock];
+  const int i = blockIdx.x * kScanBlock + threadIdx.x;
+  const int v = i < n ? in[i] : 0;
+  buf[threadIdx.x] = v;
+  __syncthreads();
+  for (int off = 1; off < kScanBlock; off <<= 1) {
+    const int t = threadIdx.x >= off ? buf[threadIdx.x - off] : 0;
+    __syncthreads();
+    buf[threadIdx.x] += t;
+    __syncthreads();
+  }
+  if (i < n) out[i] = buf[threadIdx.x] - v;
+  if (threadIdx.x == kScanBlock - 1) block_sums[blockIdx.x] = buf[threadIdx.x];
+}
+
+__global__ void k_scan_add(int *out, const int *block_offsets, int n, int *total, const int *block_sums,
+                           int nblocks) {
+  const int i = blockIdx.x * kScanBlock + threadIdx.x;
+  if (i < n) out[i] += block_offsets[blockIdx.x];
+  if (i == 0) *total = block_offsets[nblocks - 1] + block_sums[nblocks - 1];
+}
+}  // namespace
+
+// out[i] = sum_{j<i} in[i]; *total = sum. scratch must hold 2*ceil(n/1024)+2 ints.
+void exclusive_scan(const int *in, int *out, int n, int *total, int *scratch, cudaStream_t s) {
+  const int nb = (n + kScanBlock - 1) / kScanBlock;
+  if (nb == 0) {
+    SO3_CUDA(cudaMemsetAsync(total, 0, sizeof(int), s));
+    return;
+  }
+  int *bsum = scratch;
+  int *boff = scratch + nb + 1;
+  k_scan_blocks<<<nb, kScanBlock, 0, s>>>(in, out, bsum, n);
+  SO3_LAUNCH("scan_blocks");
+  if (nb > 1) {
+    if (nb > kScanBlock) {
+      // recursive for very large inputs
+      exclusive_scan(bsum, boff, nb, boff + nb, scratch + 2 * nb + 2, s);
+    } else {
+      int *dummy = boff + nb;
+      k_scan_blocks<<<1, kScanBlock, 0, s>>>(bsum, boff, dummy, nb);
+      SO3_LAUNCH("scan_top");
+    }
+  } else {
+    SO3_CUDA(cudaMemsetAsync(boff, 0, sizeof(int), s));
+  }
+  k_scan_add<<<nb, kScanBlock, 0, s>>>(out, boff, n, total, bsum, nb);
+  SO3_LAUNCH("scan_add");
+}
+std::size_t scan_scratch_ints(std::size_t n) {
+  std::size_t nb = (n + kScanBlock - 1) / kScanBlock;
+  std::size_t need = 2 * nb + 2;
+  if (nb > kScanBlock) need += scan_scratch_ints(nb);
+  return need + 8;
+}
+
+// ---- cell list ---------------------------------------------------------------
+__global__ void k_wrap_assign(int n, const double *__restrict__ x, CellGrid g, double *__restrict__ xw,
+                              int *__restrict__ cell, int *__restrict__ cell_count) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int cc[3];
+  for (int d = 0; d < 3; ++d) {
+    double p = x[3 * i + d] - g.lo[d];
+    p -= floor(p / g.len[d]) * g.len[d];
+    if (p >= g.len[d]) p -= g.len[d];
+    if (p < 0.0) p = 0.0;
+    xw[3 * i + d] = p + g.lo[d];
+    int c = int(p * g.ncell[d] / g.len[d]);
+    cc[d] = c < 0 ? 0 : (c >= g.ncell[d] ? g.ncell[d] - 1 : c);
+  }
+  const int c = (cc[2] * g.ncell[1] + cc[1]) * g.ncell[0] + cc[0];
+  cell[i] = c;
+  atomicAdd(&cell_count[c], 1);
+}
+
+__global__ void k_cell_fill(int n, const int *__restrict__ cell, const int *__restrict__ cell_start,
+                            int *__restrict__ cell_fill, int *__restrict__ cell_atoms) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int c = cell[i];
+  const int slot = atomicAdd(&cell_fill[c], 1);
+  cell_atoms[cell_start[c] + slot] = i;
+}
+
+// Sort the atoms of every cell ascending: the fill above is scheduling-dependent.
+__global__ void k_cell_sort(int ncells, const int *__restrict__ cell_start, const int *__restrict__ cell_count,
+                            int *__restrict__ cell_atoms) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= ncells) return;
+  int *a = cell_atoms + cell_start[c];
+  const int m = cell_count[c];
+  for (int i = 1; i < m; ++i) {
+    const int v = a[i];
+    int j = i - 1;
+    while (j >= 0 && a[j] > v) {
+      a[j + 1] = a[j];
+      --j;
+    }
+    a[j + 1] = v;
+  }
+}
+
+__global__ void k_sr_count(int n, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
+                           const int *__restrict__ cell_start, const int *__restrict__ cell_count,
+                           const int *__restrict__ cell_atoms, const int *__restrict__ image_of,
+                           const int *__restrict__ image_start, double rc2, int reach, int *__restrict__ deg) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int count = 0;
+  for_each_candidate(i, xw, g, cell, cell_start, cell_count, cell_atoms, image_of, image_start, reach,
+                     [&](int, int, double dx, double dy, double dz) {
+                       const double r2 = dx * dx + dy * dy + dz * dz;
+                       if (r2 > 0.0 && r2 < rc2) ++count;
+                     });
+  deg[i] = count;
+}
+
+__global__ void k_sr_fill(int n, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
+                          const int *__restrict__ cell_start, const int *__restrict__ cell_count,
+                          const int *__restrict__ cell_atoms, const int *__restrict__ image_of,
+                          const int *__restrict__ image_start, double rc2, int reach,
+                          const int *__restrict__ row_start, int *__restrict__ nbr, int *__restrict__ img) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int base = row_start[i];
+  int count = 0;
+  for_each_candidate(i, xw, g, cell, cell_start, cell_count, cell_atoms, image_of, image_start, reach,
+                     [&](int j, int code, double dx, double dy, double dz) {
+                       const double r2 = dx * dx + dy * dy + dz * dz;
+                       if (r2 > 0.0 && r2 < rc2) {
+                         nbr[base + count] = j;
+                         img[base + count] = code;
+                         ++count;
+                       }
+                     });
+  // canonical order: (sender, image)
+  for (int a = 1; a < count; ++a) {
+    const int vj = nbr[base + a], vc = img[base + a];
+    int b = a - 1;
+    while (b >= 0 && (nbr[base + b] > vj || (nbr[base + b] == vj && img[base + b] > vc))) {
+      nbr[base + b + 1] = nbr[base + b];
+      img[base + b + 1] = img[base + b];
+      --b;
+    }
+    nbr[base + b + 1] = vj;
+    img[base + b + 1] = vc;
+  }
+}
+
+// primary flag + reverse-edge lookup (binary search in the sender's sorted row)
+__global__ void k_edge_primary(int n, const int *__restrict__ row_start, const int *__restrict__ nbr,
+                               const int *__restrict__ img, int *__restrict__ primary, int *__restrict__ rev,
+                               int *__restrict__ error_flag) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  for (int e = row_start[i]; e < row_start[i + 1]; ++e) {
+    const int j = nbr[e], code = img[e];
+    primary[e] = (i < j || (i == j && code > kZeroImage)) ? 1 : 0;
+    const int want = negate_image(code);
+    int lo = row_start[j], hi = row_start[j + 1] - 1, found = -1;
+    while (lo <= hi) {
+      const int mid = (lo + hi) >> 1;
+      const int mj = nbr[mid], mc = img[mid];
+      if (mj == i && mc == want) { found = mid; break; }
+      if (mj < i || (mj == i && mc < want)) lo = mid + 1; else hi = mid - 1;
+    }
+    rev[e] = found;
+    if (found < 0) atomicExch(error_flag, 1);
+  }
+}
+
+__global__ void k_pair_fill(int n, const int *__restrict__ row_start, const int *__restrict__ nbr,
+                            const int *__restrict__ img, const int *__restrict__ primary,
+                            const int *__restrict__ pair_scan, int *__restrict__ edge_pair,
+                            int *__restrict__ pair_a, int *__restrict__ pair_b, int *__restrict__ pair_img,
+                            int *__restrict__ pair_edge) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  for (int e = row_start[i]; e < row_start[i + 1]; ++e) {
+    if (!primary[e]) continue;
+    const int p = pair_scan[e];
+    edge_pair[e] = p;
+    pair_a[p] = i;
+    pair_b[p] = nbr[e];
+    pair_img[p] = img[e];
+    pair_edge[p] = e;
+  }
+}
+
+__global__ void k_pair_reverse(int E, const int *__restrict__ primary, const int *__restrict__ rev,
+                               int *__restrict__ edge_pair) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= E) return;
+  if (!primary[e]) edge_pair[e] = ~edge_pair[rev[e]];
+}
+
+// ---- host driver ---------------------------------------------------------------
+void build_cells(NeighborState &nb, int n, const double *x, cudaStream_t s) {
+  const int nc = nb.grid.periodic ? nb.grid.ncell[0] * nb.grid.ncell[1] * nb.grid.ncell[2] : 1;
+  nb.ncells = nc;
+  if (!nb.grid.periodic) {
+    SO3_CUDA(cudaMemcpyAsync(nb.xw, x, sizeof(double) * 3 * n, cudaMemcpyDeviceToDevice, s));
+    return;
+  }
+  SO3_CUDA(cudaMemsetAsync(nb.cell_count, 0, sizeof(int) * nc, s));
+  SO3_CUDA(cudaMemsetAsync(nb.cell_fill, 0, sizeof(int) * nc, s));
+  k_wrap_assign<<<(n + 255) / 256, 256, 0, s>>>(n, x, nb.grid, nb.xw, nb.cell, nb.cell_count);
+  SO3_LAUNCH("wrap_assign");
+  exclusive_scan(nb.cell_count, nb.cell_start, nc, nb.scan_total, nb.scan_scratch, s);
+  k_cell_fill<<<(n + 255) / 256, 256, 0, s>>>(n, nb.cell, nb.cell_start, nb.cell_fill, nb.cell_atoms);
+  SO3_LAUNCH("cell_fill");
+  k_cell_sort<<<(nc + 127) / 128, 128, 0, s>>>(nc, nb.cell_start, nb.cell_count, nb.cell_atoms);
+  SO3_LAUNCH("cell_sort");
+}
+
+int sr_reach(const CellGrid &g, double rc) {
+  if (!g.periodic) return 0;
+  int reach = 1;
+  for (int d = 0; d < 3; ++d) {
+    const double cl = g.len[d] / g.ncell[d];
+    reach = std::max(reach, int(std::ceil(rc / cl - 1e-12)));
+  }
+  return reach;
+}
+
+void count_sr(NeighborState &nb, int n, double rc, cudaStream_t s) {
+  const int reach = sr_reach(nb.grid, rc);
+  k_sr_count<<<(n + 127) / 128, 128, 0, s>>>(n, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count,
+                                              nb.cell_atoms, nb.image_of, nb.image_start, rc * rc, reach,
+                                              nb.deg);
+  SO3_LAUNCH("sr_count");
+  exclusive_scan(nb.deg, nb.row_start, n, nb.row_start + n, nb.scan_scratch, s);
+}
+
+void fill_sr(NeighborState &nb, int n, double rc, int E, cudaStream_t s) {
+  const int reach = sr_reach(nb.grid, rc);
+  k_sr_fill<<<(n + 127) / 128, 128, 0, s>>>(n, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count,
+                                             nb.cell_atoms, nb.image_of, nb.image_start, rc * rc, reach,
+                                             nb.row_start, nb.nbr, nb.img);
+  SO3_LAUNCH("sr_fill");
+  k_edge_primary<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row_start, nb.nbr, nb.img, nb.primary, nb.rev,
+                                                  nb.error_flag);
+  SO3_LAUNCH("edge_primary");
+  exclusive_scan(nb.primary, nb.pair_scan, E, nb.scan_total, nb.scan_scratch, s);
+}
+
+void fill_pairs(NeighborState &nb, int n, int E, cudaStream_t s) {
+  k_pair_fill<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row_start, nb.nbr, nb.img, nb.primary, nb.pair_scan,
+                                               nb.edge_pair, nb.pair_a, nb.pair_b, nb.pair_img, nb.pair_edge);
+  SO3_LAUNCH("pair_fill");
+  if (E > 0) {
+    k_pair_reverse<<<(E + 255) / 256, 256, 0, s>>>(E, nb.primary, nb.rev, nb.edge_pair);
+    SO3_LAUNCH("pair_reverse");
+  }
+}
+
+}  // namespace so3lr_b200

@@ -1,0 +1,478 @@
+// Per-atom ("node") work: dense layers over atoms on FP64 tensor cores with
+// fused epilogues, plus the row kernels (residuals, LayerNorm forward/backward,
+// degree gate, L0 contraction, output heads).
+//
+// Reference: src/kokkos_post_attention_block0.cpp:97-300 (post-attention forward),
+// src/kokkos_post_attention_reverse.cpp:107-449 (its reverse),
+// src/kokkos_integrated_block0.cpp:257-286 (per-head QKV projections),
+// src/kokkos_output_heads.cpp:137-222, 341-581 (energy, charge and Hirshfeld heads
+// and their reverse), src/kokkos_local_energy_reverse.cpp:192-218 (embedding).
+// The reference runs each dense layer as a cuBLAS DGEMM followed by separate
+// elementwise kernels; here the bias/activation/residual work is fused into the
+// GEMM epilogue.
+#include "kernels.cuh"
+
+namespace so3lr_b200 {
+namespace {
+
+constexpr int BM = 64, BN = 64, BK = 16, LDS = BK + 4;
+
+template <bool TRANSB, Epi EPI>
+__global__ void __launch_bounds__(128) k_gemm(GemmArgs g, int aux_cols, int ldaux2) {
+  __shared__ double As[BM * LDS];
+  __shared__ double Bs[BN * LDS];
+  const int z = blockIdx.z;
+  const double *A = g.A + z * g.strideA;
+  const double *W = g.W + z * g.strideW;
+  double *C = g.C + z * g.strideC;
+  const double *aux = g.aux ? g.aux + z * g.strideAux : nullptr;
+  const double *bias = g.bias ? g.bias + z * g.strideBias : nullptr;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
+  const int wm = warp >> 1, wn = warp & 1;
+  double acc[4][4][2];
+#pragma unroll
+  for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
+  for (int k0 = 0; k0 < g.K; k0 += BK) {
+    // A tile 64 x 16: 1024 elements, 8 per thread
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int idx = tid + r * 128;
+      const int row = idx >> 4, col = idx & 15;
+      const int gm = m0 + row, gk = k0 + col;
+      As[row * LDS + col] = (gm < g.M && gk < g.K) ? A[(size_t)gm * g.lda + gk] : 0.0;
+    }
+    // B tile stored as Bs[n][k]
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int idx = tid + r * 128;
+      int nn, kk;
+      if (TRANSB) {
+        nn = idx >> 4;
+        kk = idx & 15;
+      } else {
+        kk = idx >> 6;
+        nn = idx & 63;
+      }
+      const int gn = n0 + nn, gk = k0 + kk;
+      double v = 0.0;
+      if (gn < g.N && gk < g.K) v = TRANSB ? W[(size_t)gn * g.ldw + gk] : W[(size_t)gk * g.ldw + gn];
+      Bs[nn * LDS + kk] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < BK; kk += 4) {
+      double a[4], b[4];
+#pragma unroll
+      for (int mi = 0; mi < 4; ++mi) a[mi] = As[(wm * 32 + mi * 8 + gq) * LDS + kk + tq];
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) b[ni] = Bs[(wn * 32 + ni * 8 + gq) * LDS + kk + tq];
+#pragma unroll
+      for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+        for (int ni = 0; ni < 4; ++ni) dmma(acc[mi][ni][0], acc[mi][ni][1], a[mi], b[ni]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int mi = 0; mi < 4; ++mi) {
+    const int row = m0 + wm * 32 + mi * 8 + gq;
+    if (row >= g.M) continue;
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int col = n0 + wn * 32 + ni * 8 + 2 * tq + h;
+        if (col >= g.N) continue;
+        double v = acc[mi][ni][h];
+        if (EPI == Epi::Bias) {
+          v += bias[col];
+        } else if (EPI == Epi::BiasSilu) {
+          v = silu(v + bias[col]);
+        } else if (EPI == Epi::BiasStorePre) {
+          const double pre = v + bias[col];
+          g.aux_out[(size_t)row * g.ldaux + col] = pre;
+          v = silu(pre);
+        } else if (EPI == Epi::AddResidual) {
+          if (col < aux_cols) v += aux[(size_t)row * g.ldaux + col];
+        } else if (EPI == Epi::BiasResidual) {
+          v = v + bias[col] + aux[(size_t)row * g.ldaux + col];
+        } else if (EPI == Epi::SiluPrimeMul) {
+          v *= silu_prime(aux[(size_t)row * g.ldaux + col]);
+        } else if (EPI == Epi::GateSiluResidual) {
+          v = g.aux2[(size_t)row * ldaux2 + col] + v * silu_prime(aux[(size_t)row * g.ldaux + col]);
+        }
+        C[(size_t)row * g.ldc + col] = v;
+      }
+    }
+  }
+}
+
+template <bool T>
+void dispatch_epi(const GemmArgs &g, dim3 grid, cudaStream_t s, int aux_cols, int ldaux2) {
+  switch (g.epi) {
+    case Epi::None: k_gemm<T, Epi::None><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
+    case Epi::Bias: k_gemm<T, Epi::Bias><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
+    case Epi::BiasSilu: k_gemm<T, Epi::BiasSilu><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
+    case Epi::BiasStorePre: k_gemm<T, Epi::BiasStorePre><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
+    case Epi::AddResidual: k_gemm<T, Epi::AddResidual><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
+    case Epi::BiasResidual: k_gemm<T, Epi::BiasResidual><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
+    case Epi::SiluPrimeMul: k_gemm<T, Epi::SiluPrimeMul><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
+    case Epi::GateSiluResidual: k_gemm<T, Epi::GateSiluResidual><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
+  }
+}
+
+}  // namespace
+
+void launch_gemm_ex(const GemmArgs &g, int aux_cols, int ldaux2, cudaStream_t s) {
+  if (g.M == 0) return;
+  dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.batch);
+  if (g.transB) dispatch_epi<true>(g, grid, s, aux_cols, ldaux2);
+  else dispatch_epi<false>(g, grid, s, aux_cols, ldaux2);
+  SO3_LAUNCH("gemm");
+}
+void launch_gemm(const GemmArgs &g, cudaStream_t s) { launch_gemm_ex(g, g.N, g.ldaux, s); }
+
+// ---------------------------------------------------------------------------
+// embedding: x0 = W_emb[:, Z-1] / s + offset_table[image][Z-1] / s
+// ---------------------------------------------------------------------------
+__global__ void k_embedding(int n, const int *__restrict__ z, const double *__restrict__ w,
+                            const double *__restrict__ table, const int *__restrict__ table_of_atom,
+                            double inv_scale, double *__restrict__ x) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * kF) return;
+  const int i = idx / kF, c = idx % kF;
+  const int zz = z[i];
+  double v = (zz > 0 && zz <= 118) ? w[c * 118 + zz - 1] * inv_scale : 0.0;
+  if (table != nullptr) {
+    const int tab = table_of_atom[i];
+    if (tab >= 0 && zz > 0 && zz <= 118) v += table[((size_t)tab * 118 + zz - 1) * kF + c] * inv_scale;
+  }
+  x[idx] = v;
+}
+void launch_embedding(int n, const int *z, const double *emb_w, const double *cs_table, const int *table_of_atom,
+                      double inv_scale, double *x, cudaStream_t s) {
+  if (n == 0) return;
+  k_embedding<<<(n * kF + 255) / 256, 256, 0, s>>>(n, z, emb_w, cs_table, table_of_atom, inv_scale, x);
+  SO3_LAUNCH("embedding");
+}
+
+namespace {
+__device__ inline double warp_sum(double v) {
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+}  // namespace
+
+// a = x + d_inv; A = ev + d_ev; n1 = LN1(a); act = silu(n1);
+// cat[:, 128:132] = L0'(A) (interaction cg), cat[:, 132:136] = 0. One warp per atom.
+__global__ void k_post_attn_pre(int n, const double *__restrict__ x, const double *__restrict__ d_inv,
+                                const double *__restrict__ ev, const double *__restrict__ d_ev,
+                                const double *__restrict__ lnw, const double *__restrict__ lnb,
+                                const double *__restrict__ cg_int, double *__restrict__ xhat1,
+                                double *__restrict__ rstd1, double *__restrict__ n1_out, double *__restrict__ act,
+                                double *__restrict__ A_out, double *__restrict__ cat) {
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= n) return;
+  double a[4];
+  double s = 0.0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = lane * 4 + j;
+    a[j] = x[(size_t)i * kF + c] + d_inv[(size_t)i * kF + c];
+    s += a[j];
+  }
+  const double mean = warp_sum(s) / double(kF);
+  double var = 0.0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const double d = a[j] - mean;
+    var += d * d;
+  }
+  var = warp_sum(var) / double(kF);
+  const double rs = 1.0 / sqrt(var + 1.0e-6);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = lane * 4 + j;
+    const double xh = (a[j] - mean) * rs;
+    const double y = xh * lnw[c] + lnb[c];
+    xhat1[(size_t)i * kF + c] = xh;
+    n1_out[(size_t)i * kF + c] = y;
+    act[(size_t)i * kF + c] = silu(y);
+  }
+  if (lane == 0) rstd1[i] = rs;
+  double Am = 0.0;
+  if (lane < kEV) {
+    Am = ev[(size_t)i * kEV + lane] + d_ev[(size_t)i * kEV + lane];
+    A_out[(size_t)i * kEV + lane] = Am;
+  }
+  const int d = lane < kEV ? degree_of_channel(lane) : -1;
+  const double term = lane < kEV ? Am * Am * cg_int[lane] : 0.0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const double sk = warp_sum(d == k ? term : 0.0);
+    if (lane == 0) cat[(size_t)i * kIntW + kF + k] = sk;
+  }
+  if (lane < 4) cat[(size_t)i * kIntW + kF + 4 + lane] = 0.0;
+}
+
+void launch_post_attn_pre(int n, const double *x, const double *d_inv, const double *ev, const double *d_ev,
+                          const double *lnw, const double *lnb, const double *cg_int, double *xhat1,
+                          double *rstd1, double *n1, double *act, double *A, double *cat, cudaStream_t s) {
+  k_post_attn_pre<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, x, d_inv, ev, d_ev, lnw, lnb, cg_int, xhat1, rstd1, n1,
+                                                       act, A, cat);
+  SO3_LAUNCH("post_attn_pre");
+}
+
+// pre2 = post + t[:128]; x' = LN2(pre2); ev' = A (1 + t_gate). One warp per atom.
+__global__ void k_post_attn_final(int n, const double *__restrict__ cat, const double *__restrict__ t,
+                                  const double *__restrict__ A, const double *__restrict__ lnw,
+                                  const double *__restrict__ lnb, double *__restrict__ xhat2,
+                                  double *__restrict__ rstd2, double *__restrict__ gate,
+                                  double *__restrict__ x_out, double *__restrict__ ev_out) {
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= n) return;
+  double v[4];
+  double s = 0.0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = lane * 4 + j;
+    v[j] = cat[(size_t)i * kIntW + c] + t[(size_t)i * kIntW + c];
+    s += v[j];
+  }
+  const double mean = warp_sum(s) / double(kF);
+  double var = 0.0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const double d = v[j] - mean;
+    var += d * d;
+  }
+  var = warp_sum(var) / double(kF);
+  const double rs = 1.0 / sqrt(var + 1.0e-6);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = lane * 4 + j;
+    const double xh = (v[j] - mean) * rs;
+    xhat2[(size_t)i * kF + c] = xh;
+    x_out[(size_t)i * kF + c] = xh * lnw[c] + lnb[c];
+  }
+  if (lane == 0) rstd2[i] = rs;
+  if (lane < 4) gate[(size_t)i * 4 + lane] = t[(size_t)i * kIntW + kF + lane];
+  if (lane < kEV) {
+    const int d = degree_of_channel(lane);
+    ev_out[(size_t)i * kEV + lane] = A[(size_t)i * kEV + lane] * (1.0 + t[(size_t)i * kIntW + kF + d]);
+  }
+}
+
+void launch_post_attn_final(int n, const double *cat, const double *t, const double *A, const double *lnw,
+                            const double *lnb, double *xhat2, double *rstd2, double *gate, double *x_out,
+                            double *ev_out, cudaStream_t s) {
+  k_post_attn_final<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, cat, t, A, lnw, lnb, xhat2, rstd2, gate, x_out, ev_out);
+  SO3_LAUNCH("post_attn_final");
+}
+
+// LayerNorm backward (affine): g_x = rstd (g_xh - mean(g_xh) - xh mean(g_xh xh)), g_xh = g_y w
+__device__ inline void ln_backward(const double (&gy)[4], const double (&xh)[4], const double *w, int lane,
+                                   double rs, double (&gx)[4]) {
+  double gxh[4], s1 = 0.0, s2 = 0.0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    gxh[j] = gy[j] * w[lane * 4 + j];
+    s1 += gxh[j];
+    s2 += gxh[j] * xh[j];
+  }
+  s1 = warp_sum(s1) / double(kF);
+  s2 = warp_sum(s2) / double(kF);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) gx[j] = rs * (gxh[j] - s1 - xh[j] * s2);
+}
+
+// reverse of k_post_attn_final: g_t[:128] = LN2^T(g_x), g_t[128+d] = sum g_ev A, g_A = g_ev (1 + gate)
+__global__ void k_post_attn_rev_final(int n, const double *__restrict__ g_x, const double *__restrict__ g_ev,
+                                      const double *__restrict__ xhat2, const double *__restrict__ rstd2,
+                                      const double *__restrict__ lnw2, const double *__restrict__ A,
+                                      const double *__restrict__ gate, double *__restrict__ g_t,
+                                      double *__restrict__ g_A) {
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= n) return;
+  double gy[4], xh[4], gx[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    gy[j] = g_x[(size_t)i * kF + lane * 4 + j];
+    xh[j] = xhat2[(size_t)i * kF + lane * 4 + j];
+  }
+  ln_backward(gy, xh, lnw2, lane, rstd2[i], gx);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) g_t[(size_t)i * kIntW + lane * 4 + j] = gx[j];
+  double ge = 0.0, Am = 0.0;
+  int d = -1;
+  if (lane < kEV && g_ev != nullptr) {
+    ge = g_ev[(size_t)i * kEV + lane];
+    Am = A[(size_t)i * kEV + lane];
+    d = degree_of_channel(lane);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const double sk = warp_sum(d == k ? ge * Am : 0.0);
+    if (lane == 0) g_t[(size_t)i * kIntW + kF + k] = sk;
+  }
+  if (lane < 4) g_t[(size_t)i * kIntW + kF + 4 + lane] = 0.0;
+  if (lane < kEV) g_A[(size_t)i * kEV + lane] = d >= 0 ? ge * (1.0 + gate[(size_t)i * 4 + d]) : 0.0;
+}
+
+void launch_post_attn_rev_final(int n, const double *g_x, const double *g_ev, const double *xhat2,
+                                const double *rstd2, const double *lnw2, const double *A, const double *gate,
+                                double *g_t, double *g_A, cudaStream_t s) {
+  k_post_attn_rev_final<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, g_x, g_ev, xhat2, rstd2, lnw2, A, gate, g_t, g_A);
+  SO3_LAUNCH("post_attn_rev_final");
+}
+
+// g_a = LN1^T(g_n1); g_A += 2 A cg_int g_l0'[deg]
+__global__ void k_post_attn_rev_ln1(int n, const double *__restrict__ g_n1, const double *__restrict__ xhat1,
+                                    const double *__restrict__ rstd1, const double *__restrict__ lnw1,
+                                    const double *__restrict__ A, const double *__restrict__ cg_int,
+                                    const double *__restrict__ g_cat, double *__restrict__ g_a,
+                                    double *__restrict__ g_A) {
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= n) return;
+  double gy[4], xh[4], gx[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    gy[j] = g_n1[(size_t)i * kF + lane * 4 + j];
+    xh[j] = xhat1[(size_t)i * kF + lane * 4 + j];
+  }
+  ln_backward(gy, xh, lnw1, lane, rstd1[i], gx);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) g_a[(size_t)i * kF + lane * 4 + j] = gx[j];
+  if (lane < kEV) {
+    const int d = degree_of_channel(lane);
+    const double Am = A[(size_t)i * kEV + lane];
+    g_A[(size_t)i * kEV + lane] += 2.0 * Am * cg_int[lane] * g_cat[(size_t)i * kIntW + kF + d];
+  }
+}
+
+void launch_post_attn_rev_ln1(int n, const double *g_n1, const double *xhat1, const double *rstd1,
+                              const double *lnw1, const double *A, const double *cg_int, const double *g_cat,
+                              double *g_a, double *g_A, cudaStream_t s) {
+  k_post_attn_rev_ln1<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, g_n1, xhat1, rstd1, lnw1, A, cg_int, g_cat, g_a, g_A);
+  SO3_LAUNCH("post_attn_rev_ln1");
+}
+
+__global__ void k_add(int count, const double *__restrict__ a, double *__restrict__ b) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < count) b[i] += a[i];
+}
+void launch_add(int count, const double *a, double *b, cudaStream_t s) {
+  if (count == 0) return;
+  k_add<<<(count + 255) / 256, 256, 0, s>>>(count, a, b);
+  SO3_LAUNCH("add");
+}
+
+// ---------------------------------------------------------------------------
+// output heads (output_heads.cpp:137-176, 341-451): hcat = silu(x W1cat^T + b1cat)
+// energy  = (hcat[0:128] . w2 + b2) * scale[Z-1] + shift[Z-1]
+// raw q   =  hcat[128:256] . w2c + b2c + emb[Z]
+// ratio   = | v_shift[Z] + q_emb[Z] . (hcat[256:320] Wh2^T + bh2) / 8 |
+// ---------------------------------------------------------------------------
+__global__ void k_heads_finalize(int n, const int *__restrict__ z, const double *__restrict__ hcat, HeadsW hw,
+                                 double *__restrict__ hk_out, double *__restrict__ e_nn, double *__restrict__ raw_q,
+                                 double *__restrict__ ratio) {
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= n) return;
+  const double *h = hcat + (size_t)i * kHeadCat;
+  double se = 0.0, sq = 0.0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    se += h[lane * 4 + j] * hw.e_w2[lane * 4 + j];
+    sq += h[kHeadHidden + lane * 4 + j] * hw.c_w2[lane * 4 + j];
+  }
+  se = warp_sum(se);
+  sq = warp_sum(sq);
+  const int zz = z[i];
+  // Hirshfeld keys: lane owns keys 2*lane, 2*lane+1
+  double k0 = hw.h_b2[2 * lane], k1 = hw.h_b2[2 * lane + 1];
+  const double *hh = h + 2 * kHeadHidden;
+  double s0 = 0.0, s1 = 0.0;
+  for (int j = 0; j < kHirsh; ++j) {
+    const double hv = hh[j];
+    s0 += hv * hw.h_w2[(2 * lane) * kHirsh + j];
+    s1 += hv * hw.h_w2[(2 * lane + 1) * kHirsh + j];
+  }
+  k0 += s0;
+  k1 += s1;
+  hk_out[(size_t)i * kHirsh + 2 * lane] = k0;
+  hk_out[(size_t)i * kHirsh + 2 * lane + 1] = k1;
+  double qk = hw.h_qemb[zz * kHirsh + 2 * lane] * k0 + hw.h_qemb[zz * kHirsh + 2 * lane + 1] * k1;
+  qk = warp_sum(qk);
+  if (lane == 0) {
+    e_nn[i] = (se + hw.e_b2) * hw.e_scale[zz - 1] + hw.e_shift[zz - 1];
+    raw_q[i] = sq + hw.c_b2 + hw.c_emb[zz];
+    ratio[i] = fabs(hw.h_vshift[zz] + qk / 8.0);
+  }
+}
+
+void launch_heads_finalize(int n, const int *z, const double *hcat, const HeadsW &hw, double *hk_out,
+                           double *e_nn, double *raw_q, double *ratio, cudaStream_t s) {
+  if (n == 0) return;
+  k_heads_finalize<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, z, hcat, hw, hk_out, e_nn, raw_q, ratio);
+  SO3_LAUNCH("heads_finalize");
+}
+
+// seeds of the heads' reverse: energy seed 1, charge seed dE/dq - image mean,
+// Hirshfeld seed dE/dh (output_heads.cpp:493-581). Writes g_hcat = dL/d(pre-activation).
+__global__ void k_heads_seed(int n, const int *__restrict__ z, const double *__restrict__ hpre,
+                             const double *__restrict__ hk, HeadsW hw, const double *__restrict__ dq,
+                             const double *__restrict__ dq_mean, const int *__restrict__ image_of,
+                             const double *__restrict__ dh, double *__restrict__ g_hcat) {
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= n) return;
+  const int zz = z[i];
+  const double *pre = hpre + (size_t)i * kHeadCat;
+  double *g = g_hcat + (size_t)i * kHeadCat;
+  const double scale = hw.e_scale[zz - 1];
+  const double qseed = dq[i] - dq_mean[image_of[i]];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = lane * 4 + j;
+    g[c] = scale * hw.e_w2[c] * silu_prime(pre[c]);
+    g[kHeadHidden + c] = qseed * hw.c_w2[c] * silu_prime(pre[kHeadHidden + c]);
+  }
+  // Hirshfeld: effective = v_shift + q_emb . k / 8
+  const double k0 = hk[(size_t)i * kHirsh + 2 * lane], k1 = hk[(size_t)i * kHirsh + 2 * lane + 1];
+  const double qe0 = hw.h_qemb[zz * kHirsh + 2 * lane], qe1 = hw.h_qemb[zz * kHirsh + 2 * lane + 1];
+  double eff = qe0 * k0 / 8.0 + qe1 * k1 / 8.0;
+  eff = warp_sum(eff) + hw.h_vshift[zz];
+  const double sign = eff > 0.0 ? 1.0 : (eff < 0.0 ? -1.0 : 0.0);
+  const double seed = dh[i] * sign / 8.0;
+  // g_k = seed * q_emb; g_h1[j] = sum_k g_k[k] Wh2[k][j]; lane owns j = 2 lane, 2 lane + 1
+  __shared__ double gk_s[8][kHirsh];
+  const int w = (threadIdx.x >> 5);
+  gk_s[w][2 * lane] = seed * qe0;
+  gk_s[w][2 * lane + 1] = seed * qe1;
+  __syncwarp();
+#pragma unroll
+  for (int jj = 0; jj < 2; ++jj) {
+    const int j = 2 * lane + jj;
+    double s = 0.0;
+    for (int k = 0; k < kHirsh; ++k) s += gk_s[w][k] * hw.h_w2[k * kHirsh + j];
+    g[2 * kHeadHidden + j] = s * silu_prime(pre[2 * kHeadHidden + j]);
+  }
+}
+
+void launch_heads_seed(int n, const int *z, const double *hpre, const double *hk, const HeadsW &hw,
+                       const double *dq, const double *dq_mean, const int *image_of_atom, const double *dh,
+                       double *g_hcat, cudaStream_t s) {
+  if (n == 0) return;
+  k_heads_seed<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, z, hpre, hk, hw, dq, dq_mean, image_of_atom, dh, g_hcat);
+  SO3_LAUNCH("heads_seed");
+}
+
+}  // namespace so3lr_b200

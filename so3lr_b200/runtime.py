@@ -1,0 +1,264 @@
+"""ctypes binding of the C ABI in include/so3lr_b200.h.
+
+The library ``so3lr_b200/libso3lr_b200.so`` is the only compute path: if it is
+missing, or a call fails, this module raises. There is no CPU fallback.
+
+The class mirrors what the reference's pair styles do on the host
+(plugins/lammps/pair_so3lr_native_mpi.cpp, plugins/lammps/pair_so3lr_turbo.cpp):
+load a model, describe its architecture (cutoffs for init_style/init_one),
+validate charge and multiplicity, and evaluate energy, forces, per-atom
+energies and the virial once per step.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import pathlib
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+LIB_PATH = HERE / "libso3lr_b200.so"
+DEFAULT_MODEL = HERE.parent / "models" / "so3lr.so3lr"
+
+# every function the header declares (checked by the CPU tests)
+EXPORTED = (
+    "so3lr_create", "so3lr_describe", "so3lr_validate_charge_spin", "so3lr_element_from_token",
+    "so3lr_inspect_model", "so3lr_compute", "so3lr_compute_device", "so3lr_compute_batch",
+    "so3lr_md_init", "so3lr_md_run", "so3lr_md_state", "so3lr_stream", "so3lr_last_stats", "so3lr_destroy",
+)
+
+_dp = C.POINTER(C.c_double)
+_ip = C.POINTER(C.c_int)
+_lp = C.POINTER(C.c_longlong)
+
+
+class ArchInfo(C.Structure):
+    _fields_ = [("abi_version", C.c_int), ("layers", C.c_int), ("features", C.c_int), ("heads", C.c_int),
+                ("head_width", C.c_int), ("degrees", C.c_int), ("ev_width", C.c_int), ("rbf", C.c_int),
+                ("sr_cutoff", C.c_double), ("lr_cutoff", C.c_double), ("attention_norm", C.c_double),
+                ("embedding_scale", C.c_double), ("parameter_count", C.c_longlong), ("summary", C.c_char * 512)]
+
+
+class Frame(C.Structure):
+    _fields_ = [("natoms", C.c_longlong), ("x", _dp), ("z", _ip), ("periodic", C.c_int),
+                ("boxlo", C.c_double * 3), ("boxlen", C.c_double * 3), ("total_charge", C.c_double),
+                ("multiplicity", C.c_double)]
+
+
+class Result(C.Structure):
+    _fields_ = [("f", _dp), ("eatom", _dp), ("charges", _dp), ("ratios", _dp), ("e_learned", _dp),
+                ("e_zbl", _dp), ("e_lr", _dp), ("e_elec", _dp), ("e_disp", _dp), ("energy", C.c_double),
+                ("virial", C.c_double * 6)]
+
+
+class Batch(C.Structure):
+    _fields_ = [("natoms", C.c_longlong), ("nimages", C.c_int), ("x", _dp), ("z", _ip), ("image_offsets", _lp),
+                ("image_charge", _dp), ("image_multiplicity", _dp)]
+
+
+class BatchResult(C.Structure):
+    _fields_ = [("f", _dp), ("eatom", _dp), ("charges", _dp), ("image_energy", _dp)]
+
+
+class So3lrError(RuntimeError):
+    pass
+
+
+_LIB = None
+
+
+def load_library(path: os.PathLike | str | None = None) -> C.CDLL:
+    """Load libso3lr_b200.so (raises when it has not been built)."""
+    global _LIB
+    if _LIB is not None and path is None:
+        return _LIB
+    p = pathlib.Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise So3lrError(f"{p} is missing: build it with `python -m so3lr_b200.build` (there is no CPU fallback)")
+    lib = C.CDLL(str(p))
+    lib.so3lr_create.argtypes = [C.c_char_p, C.c_int, C.POINTER(C.c_void_p), C.c_char_p, C.c_size_t]
+    lib.so3lr_describe.argtypes = [C.c_void_p, C.POINTER(ArchInfo)]
+    lib.so3lr_inspect_model.argtypes = [C.c_char_p, C.POINTER(ArchInfo), C.c_char_p, C.c_size_t]
+    lib.so3lr_validate_charge_spin.argtypes = [_lp, C.c_double, C.c_double, C.c_char_p, C.c_size_t]
+    lib.so3lr_element_from_token.argtypes = [C.c_char_p]
+    lib.so3lr_compute.argtypes = [C.c_void_p, C.POINTER(Frame), C.POINTER(Result), C.c_char_p, C.c_size_t]
+    lib.so3lr_compute_device.argtypes = [C.c_void_p, C.POINTER(Frame), C.c_void_p, C.c_void_p, _dp, _dp,
+                                         C.c_char_p, C.c_size_t]
+    lib.so3lr_compute_batch.argtypes = [C.c_void_p, C.POINTER(Batch), C.POINTER(BatchResult), C.c_char_p,
+                                        C.c_size_t]
+    lib.so3lr_md_init.argtypes = [C.c_void_p, C.POINTER(Frame), _dp, _dp, C.c_char_p, C.c_size_t]
+    lib.so3lr_md_run.argtypes = [C.c_void_p, C.c_int, C.c_double, C.c_char_p, C.c_size_t]
+    lib.so3lr_md_state.argtypes = [C.c_void_p, _dp, _dp, _dp, _dp, C.c_char_p, C.c_size_t]
+    lib.so3lr_stream.argtypes = [C.c_void_p]
+    lib.so3lr_stream.restype = C.c_void_p
+    lib.so3lr_last_stats.argtypes = [C.c_void_p, _lp, _lp, _lp]
+    lib.so3lr_destroy.argtypes = [C.c_void_p]
+    lib.so3lr_destroy.restype = None
+    if path is None:
+        _LIB = lib
+    return lib
+
+
+def _ptr(a: np.ndarray | None, ctype=C.c_double):
+    if a is None:
+        return None
+    return a.ctypes.data_as(C.POINTER(ctype))
+
+
+def _check(rc: int, err: C.Array) -> None:
+    if rc != 0:
+        raise So3lrError(err.value.decode(errors="replace") or f"status {rc}")
+
+
+def element_from_token(token: str) -> int:
+    return int(load_library().so3lr_element_from_token(token.encode()))
+
+
+def validate_charge_spin(z, total_charge: float, multiplicity: float) -> str:
+    """'' when valid, else the reason (so3lr_charge_spin.cpp:116-141)."""
+    counts = np.zeros(119, dtype=np.int64)
+    for zi in np.asarray(z).ravel():
+        counts[int(zi)] += 1
+    err = C.create_string_buffer(512)
+    rc = load_library().so3lr_validate_charge_spin(_ptr(counts, C.c_longlong), float(total_charge),
+                                                   float(multiplicity), err, 512)
+    return "" if rc == 0 else err.value.decode()
+
+
+def inspect_model(path: os.PathLike | str = DEFAULT_MODEL) -> dict:
+    """Load, verify and capability-check a model on the host only (no GPU needed)."""
+    info = ArchInfo()
+    err = C.create_string_buffer(4096)
+    _check(load_library().so3lr_inspect_model(str(path).encode(), C.byref(info), err, 4096), err)
+    return _arch_dict(info)
+
+
+def _arch_dict(info: ArchInfo) -> dict:
+    return {k: (getattr(info, k).decode() if k == "summary" else getattr(info, k)) for k, _ in ArchInfo._fields_}
+
+
+class So3lrB200:
+    """One model on one GPU (the drop-in evaluator behind the pair styles)."""
+
+    def __init__(self, model_path: os.PathLike | str = DEFAULT_MODEL, device: int = 0):
+        self._lib = load_library()
+        handle = C.c_void_p()
+        err = C.create_string_buffer(4096)
+        _check(self._lib.so3lr_create(str(model_path).encode(), int(device), C.byref(handle), err, 4096), err)
+        self._h = handle
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._lib.so3lr_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def describe(self) -> dict:
+        info = ArchInfo()
+        self._lib.so3lr_describe(self._h, C.byref(info))
+        return _arch_dict(info)
+
+    @property
+    def stream(self) -> int:
+        return int(self._lib.so3lr_stream(self._h) or 0)
+
+    def stats(self) -> dict:
+        e, p, b = C.c_longlong(), C.c_longlong(), C.c_longlong()
+        self._lib.so3lr_last_stats(self._h, C.byref(e), C.byref(p), C.byref(b))
+        return {"sr_edges": e.value, "sr_pairs": p.value, "device_bytes": b.value}
+
+    @staticmethod
+    def _frame(x, z, cell, boxlo, charge, multiplicity):
+        x = np.ascontiguousarray(x, dtype=np.float64)
+        z = np.ascontiguousarray(z, dtype=np.int32)
+        fr = Frame()
+        fr.natoms = len(z)
+        fr.x = _ptr(x)
+        fr.z = _ptr(z, C.c_int)
+        fr.periodic = 1 if cell is not None else 0
+        lo = np.zeros(3) if boxlo is None else np.asarray(boxlo, dtype=np.float64)
+        ln = np.zeros(3) if cell is None else np.asarray(cell, dtype=np.float64)
+        for d in range(3):
+            fr.boxlo[d] = float(lo[d])
+            fr.boxlen[d] = float(ln[d])
+        fr.total_charge = float(charge)
+        fr.multiplicity = float(multiplicity)
+        return fr, x, z
+
+    def compute(self, x, z, cell=None, boxlo=None, charge: float = 0.0, multiplicity: float = 1.0,
+                terms: bool = True) -> dict:
+        fr, x, z = self._frame(x, z, cell, boxlo, charge, multiplicity)
+        n = len(z)
+        out = {k: np.empty(n) for k in ("eatom", "charges", "ratios", "e_learned", "e_zbl", "e_lr", "e_elec",
+                                        "e_disp")} if terms else {}
+        out["forces"] = np.empty((n, 3))
+        res = Result()
+        res.f = _ptr(out["forces"])
+        for k in ("eatom", "charges", "ratios", "e_learned", "e_zbl", "e_lr", "e_elec", "e_disp"):
+            setattr(res, k, _ptr(out.get(k)))
+        err = C.create_string_buffer(4096)
+        _check(self._lib.so3lr_compute(self._h, C.byref(fr), C.byref(res), err, 4096), err)
+        out["energy"] = res.energy
+        out["virial"] = np.array(res.virial[:])
+        return out
+
+    def compute_batch(self, x, z, image_offsets, image_charge, image_multiplicity) -> dict:
+        x = np.ascontiguousarray(x, dtype=np.float64)
+        z = np.ascontiguousarray(z, dtype=np.int32)
+        off = np.ascontiguousarray(image_offsets, dtype=np.int64)
+        q = np.ascontiguousarray(image_charge, dtype=np.float64)
+        m = np.ascontiguousarray(image_multiplicity, dtype=np.float64)
+        n, nimg = len(z), len(off) - 1
+        out = {"forces": np.empty((n, 3)), "eatom": np.empty(n), "charges": np.empty(n),
+               "image_energy": np.empty(nimg)}
+        b = Batch(natoms=n, nimages=nimg, x=_ptr(x), z=_ptr(z, C.c_int), image_offsets=_ptr(off, C.c_longlong),
+                  image_charge=_ptr(q), image_multiplicity=_ptr(m))
+        r = BatchResult(f=_ptr(out["forces"]), eatom=_ptr(out["eatom"]), charges=_ptr(out["charges"]),
+                        image_energy=_ptr(out["image_energy"]))
+        err = C.create_string_buffer(4096)
+        _check(self._lib.so3lr_compute_batch(self._h, C.byref(b), C.byref(r), err, 4096), err)
+        return out
+
+    def compute_device(self, x_ptr: int, z, cell, boxlo, f_ptr: int, charge=0.0, multiplicity=1.0):
+        """Positions/forces already in device memory of this handle's GPU."""
+        z = np.ascontiguousarray(z, dtype=np.int32)
+        fr = Frame()
+        fr.natoms = len(z)
+        fr.x = C.cast(C.c_void_p(x_ptr), _dp)
+        fr.z = _ptr(z, C.c_int)
+        fr.periodic = 1 if cell is not None else 0
+        for d in range(3):
+            fr.boxlo[d] = 0.0 if boxlo is None else float(boxlo[d])
+            fr.boxlen[d] = 0.0 if cell is None else float(cell[d])
+        fr.total_charge = float(charge)
+        fr.multiplicity = float(multiplicity)
+        e = C.c_double()
+        vir = (C.c_double * 6)()
+        err = C.create_string_buffer(4096)
+        _check(self._lib.so3lr_compute_device(self._h, C.byref(fr), C.c_void_p(f_ptr), None, C.byref(e),
+                                              C.cast(vir, _dp), err, 4096), err)
+        return e.value, np.array(vir[:])
+
+    def md_init(self, x, z, cell, boxlo, v, mass, charge=0.0, multiplicity=1.0):
+        fr, x, z = self._frame(x, z, cell, boxlo, charge, multiplicity)
+        v = np.ascontiguousarray(v, dtype=np.float64)
+        mass = np.ascontiguousarray(mass, dtype=np.float64)
+        err = C.create_string_buffer(4096)
+        _check(self._lib.so3lr_md_init(self._h, C.byref(fr), _ptr(v), _ptr(mass), err, 4096), err)
+
+    def md_run(self, nsteps: int, dt_ps: float) -> None:
+        err = C.create_string_buffer(4096)
+        _check(self._lib.so3lr_md_run(self._h, int(nsteps), float(dt_ps), err, 4096), err)
+
+    def md_state(self, n: int) -> dict:
+        x, v, f = np.empty((n, 3)), np.empty((n, 3)), np.empty((n, 3))
+        e = C.c_double()
+        err = C.create_string_buffer(4096)
+        _check(self._lib.so3lr_md_state(self._h, _ptr(x), _ptr(v), _ptr(f), C.byref(e), err, 4096), err)
+        return {"x": x, "v": v, "f": f, "energy": e.value}
