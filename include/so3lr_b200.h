@@ -166,6 +166,19 @@ int so3lr_md_run(so3lr_handle *h, int nsteps, double dt_ps, char *err, size_t er
  * potential energy of the last force evaluation. Synchronises the stream. */
 int so3lr_md_state(so3lr_handle *h, double *x, double *v, double *f, double *energy, char *err, size_t errlen);
 
+/* Optional timing of the dominant kernels (the pair-filter MLPs) with CUDA
+ * events on the handle's stream. kernel 0 = filter forward, 1 = filter
+ * reverse. so3lr_profile_read synchronises, returns the summed device time,
+ * the number of timed launches and their algorithmic FLOPs, and resets. The
+ * reference has per-phase timing behind SO3_NATIVE_MPI_PROFILE
+ * (pair_so3lr_native_mpi.cpp:1259-1266, 1887-1956); this is its per-kernel form. */
+int so3lr_profile(so3lr_handle *h, int enable);
+int so3lr_profile_read(so3lr_handle *h, int kernel, double *total_ms, long long *launches, double *flops, char *err,
+                       size_t errlen);
+
+/* Total number of CUDA kernels this library has launched in the process. */
+long long so3lr_launch_count(void);
+
 /* The handle's CUDA stream (cudaStream_t), for callers that time or order work. */
 void *so3lr_stream(so3lr_handle *h);
 

@@ -15,6 +15,11 @@ using so3lr_b200::Error;
 using so3lr_b200::Evaluator;
 using so3lr_b200::SystemSpec;
 
+long long &so3lr_b200::launch_counter() {
+  static long long count = 0;
+  return count;
+}
+
 struct so3lr_handle {
   std::unique_ptr<Evaluator> eval;
   std::string last_error;
@@ -244,6 +249,25 @@ int so3lr_md_state(so3lr_handle *h, double *x, double *v, double *f, double *ene
     return report(e, err, errlen, h);
   }
 }
+
+int so3lr_profile(so3lr_handle *h, int enable) {
+  if (!h) return 2;
+  h->eval->set_profiling(enable != 0);
+  return 0;
+}
+
+int so3lr_profile_read(so3lr_handle *h, int kernel, double *total_ms, long long *launches, double *flops, char *err,
+                       size_t errlen) {
+  if (!h) return report_msg("so3lr_profile_read: NULL handle", err, errlen);
+  try {
+    h->eval->read_profile(kernel, total_ms, launches, flops);
+    return 0;
+  } catch (const std::exception &e) {
+    return report(e, err, errlen, h);
+  }
+}
+
+long long so3lr_launch_count(void) { return so3lr_b200::launch_counter(); }
 
 void *so3lr_stream(so3lr_handle *h) { return h ? static_cast<void *>(h->eval->stream()) : nullptr; }
 

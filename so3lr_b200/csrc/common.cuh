@@ -27,12 +27,19 @@ constexpr int kHirsh = 64;
 constexpr int kHeadCat = 2 * kHeadHidden + kHirsh;  // fused first layers of the 3 heads
 constexpr int kMaxLayers = 8;
 constexpr int kPairScalars = 32;  // per pair, per block: alpha / s for both directions
+// Algorithmic FLOPs of the two filter MLPs of one pair, one direction of the
+// pass (forward, or the reverse input gradients): 2 filters x (R F + F F + 4 H + H F)
+// multiply-adds x 2. The reverse's first-layer recompute is not counted.
+constexpr double kFilterFlopsPerPair = 2.0 * (kR * kF + kF * kF + 4 * kEH + kEH * kF) * 2.0;
 
 inline void cuda_check(cudaError_t e, const char *what) {
   if (e != cudaSuccess) throw std::runtime_error(std::string("CUDA error in ") + what + ": " + cudaGetErrorString(e));
 }
+// number of kernels this library has launched in the process (every launcher
+// calls SO3_LAUNCH exactly once per kernel launch)
+long long &launch_counter();
 #define SO3_CUDA(x) ::so3lr_b200::cuda_check((x), #x)
-#define SO3_LAUNCH(what) ::so3lr_b200::cuda_check(cudaGetLastError(), what)
+#define SO3_LAUNCH(what) (++::so3lr_b200::launch_counter(), ::so3lr_b200::cuda_check(cudaGetLastError(), what))
 
 // degree slot of equivariant channel m (0..23): 3 + 5 + 7 + 9
 __host__ __device__ inline int degree_of_channel(int m) { return m < 3 ? 0 : (m < 8 ? 1 : (m < 15 ? 2 : 3)); }

@@ -26,6 +26,8 @@ Evaluator::~Evaluator() {
   if (stream_) {
     cudaSetDevice(device_);
     cudaStreamSynchronize(stream_);
+    for (auto &p : prof_)
+      for (auto ev : p.events) cudaEventDestroy(ev);
     cudaStreamDestroy(stream_);
   }
   if (host_small_) cudaFreeHost(host_small_);
@@ -383,6 +385,47 @@ std::size_t Evaluator::device_bytes() const {
 }
 
 // ---------------------------------------------------------------------------
+// kernel timing (CUDA events on the launching stream)
+// ---------------------------------------------------------------------------
+void Evaluator::prof_begin(int k) {
+  if (!profiling_) return;
+  KernelProfile &p = prof_[k];
+  if (p.used + 2 > int(p.events.size())) {
+    for (int i = 0; i < 64; ++i) {
+      cudaEvent_t ev;
+      SO3_CUDA(cudaEventCreate(&ev));
+      p.events.push_back(ev);
+    }
+  }
+  SO3_CUDA(cudaEventRecord(p.events[p.used], stream_));
+}
+void Evaluator::prof_end(int k, double flops) {
+  if (!profiling_) return;
+  KernelProfile &p = prof_[k];
+  SO3_CUDA(cudaEventRecord(p.events[p.used + 1], stream_));
+  p.used += 2;
+  p.launches += 1;
+  p.flops += flops;
+}
+void Evaluator::read_profile(int k, double *ms, long long *launches, double *flops) {
+  if (k < 0 || k > 1) throw Error("SO3LR: unknown profiled kernel");
+  SO3_CUDA(cudaStreamSynchronize(stream_));
+  KernelProfile &p = prof_[k];
+  double total = 0;
+  for (int i = 0; i < p.used; i += 2) {
+    float t = 0;
+    SO3_CUDA(cudaEventElapsedTime(&t, p.events[i], p.events[i + 1]));
+    total += t;
+  }
+  if (ms) *ms = total;
+  if (launches) *launches = p.launches;
+  if (flops) *flops = p.flops;
+  p.used = 0;
+  p.launches = 0;
+  p.flops = 0;
+}
+
+// ---------------------------------------------------------------------------
 // neighbour lists
 // ---------------------------------------------------------------------------
 void Evaluator::build_neighbors() {
@@ -446,8 +489,10 @@ void Evaluator::compute() {
 
   for (int b = 0; b < layers_; ++b) {
     const BlockW &w = blocks_[b];
+    prof_begin(0);
     launch_filter_forward(P, geo_.get(), nb_.pair_a, nb_.pair_b, b == 0 ? nullptr : evb_[b]->get(), w.cg_att, w.finv,
                           w.fev, rad_, f_inv_[b]->get(), f_ev_[b]->get(), s);
+    prof_end(0, kFilterFlopsPerPair * double(P));
     {  // per-head projections: qkv[n][h][5][32] = x[n][h*32:(h+1)*32] W_h
       GemmArgs g{};
       g.M = n; g.N = 160; g.K = 32;
@@ -570,9 +615,11 @@ void Evaluator::compute() {
                              g_cat_.get(), g_a_.get(), g_A_.get(), s);
     launch_attention_reverse(n, nb_, geo_.get(), sh_.get(), qkv_[b]->get(), f_inv_[b]->get(), f_ev_[b]->get(),
                              g_a_.get(), g_A_.get(), norm_, b > 0 ? g_qkv_.get() : nullptr, pair_sc_.get(), s);
+    prof_begin(1);
     launch_filter_reverse(P, geo_.get(), sh_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr,
                           w.cg_att, w.finv, w.fev, rad_, qkv_[b]->get(), g_A_.get(), pair_sc_.get(), norm_, b > 0,
                           gv_.get(), gl0_.get(), s);
+    prof_end(1, kFilterFlopsPerPair * double(P));
     if (b > 0) {
       GemmArgs g{};  // g_x_in = g_a + per-head (g_qkv W^T)
       g.M = n; g.N = 32; g.K = 160;

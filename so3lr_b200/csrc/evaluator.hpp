@@ -98,6 +98,12 @@ class Evaluator {
   StepStats stats() const { return stats_; }
   std::size_t device_bytes() const;
 
+  // Optional CUDA-event timing of the pair-filter kernels on stream(): kernel 0 =
+  // filter forward, 1 = filter reverse. read_profile() synchronises, returns
+  // the summed device time, launch count and algorithmic FLOPs, and resets.
+  void set_profiling(bool on) { profiling_ = on; }
+  void read_profile(int kernel, double *ms, long long *launches, double *flops);
+
   // velocity-Verlet MD on the device (LAMMPS metal units); masses in g/mol
   void md_setup(const double *host_v, const double *host_mass);
   void md_steps(int nsteps, double dt_ps);
@@ -147,6 +153,17 @@ class Evaluator {
   DeviceArray<double> e_lr_, e_elec_, e_disp_, dq_, dh_, f_lr_, w_lr_, img_sums_, dq_mean_;
   DeviceArray<double> g_hcat_, g_x_, g_x2_, g_ev_, g_ev2_, g_t_, g_cat_, g_hp_, g_n1_, g_a_, g_A_, g_qkv_;
   DeviceArray<double> e_atom_, e_zbl_, w_atom_, totals_, image_energy_;
+
+  struct KernelProfile {
+    std::vector<cudaEvent_t> events;
+    int used = 0;
+    long long launches = 0;
+    double flops = 0;
+  };
+  bool profiling_ = false;
+  KernelProfile prof_[2];
+  void prof_begin(int k);
+  void prof_end(int k, double flops);
 
   void upload_weights();
   void alloc_atoms();

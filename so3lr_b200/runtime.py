@@ -25,7 +25,8 @@ DEFAULT_MODEL = HERE.parent / "models" / "so3lr.so3lr"
 EXPORTED = (
     "so3lr_create", "so3lr_describe", "so3lr_validate_charge_spin", "so3lr_element_from_token",
     "so3lr_inspect_model", "so3lr_compute", "so3lr_compute_device", "so3lr_compute_batch",
-    "so3lr_md_init", "so3lr_md_run", "so3lr_md_state", "so3lr_stream", "so3lr_last_stats", "so3lr_destroy",
+    "so3lr_md_init", "so3lr_md_run", "so3lr_md_state", "so3lr_profile", "so3lr_profile_read",
+    "so3lr_launch_count", "so3lr_stream", "so3lr_last_stats", "so3lr_destroy",
 )
 
 _dp = C.POINTER(C.c_double)
@@ -90,6 +91,10 @@ def load_library(path: os.PathLike | str | None = None) -> C.CDLL:
     lib.so3lr_md_init.argtypes = [C.c_void_p, C.POINTER(Frame), _dp, _dp, C.c_char_p, C.c_size_t]
     lib.so3lr_md_run.argtypes = [C.c_void_p, C.c_int, C.c_double, C.c_char_p, C.c_size_t]
     lib.so3lr_md_state.argtypes = [C.c_void_p, _dp, _dp, _dp, _dp, C.c_char_p, C.c_size_t]
+    lib.so3lr_profile.argtypes = [C.c_void_p, C.c_int]
+    lib.so3lr_profile_read.argtypes = [C.c_void_p, C.c_int, _dp, _lp, _dp, C.c_char_p, C.c_size_t]
+    lib.so3lr_launch_count.argtypes = []
+    lib.so3lr_launch_count.restype = C.c_longlong
     lib.so3lr_stream.argtypes = [C.c_void_p]
     lib.so3lr_stream.restype = C.c_void_p
     lib.so3lr_last_stats.argtypes = [C.c_void_p, _lp, _lp, _lp]
@@ -167,6 +172,19 @@ class So3lrB200:
     @property
     def stream(self) -> int:
         return int(self._lib.so3lr_stream(self._h) or 0)
+
+    def profile(self, enable: bool) -> None:
+        self._lib.so3lr_profile(self._h, 1 if enable else 0)
+
+    def profile_read(self, kernel: int) -> dict:
+        ms, n, fl = C.c_double(), C.c_longlong(), C.c_double()
+        err = C.create_string_buffer(1024)
+        _check(self._lib.so3lr_profile_read(self._h, int(kernel), C.byref(ms), C.byref(n), C.byref(fl), err, 1024),
+               err)
+        return {"ms": ms.value, "launches": n.value, "flops": fl.value}
+
+    def launch_count(self) -> int:
+        return int(self._lib.so3lr_launch_count())
 
     def stats(self) -> dict:
         e, p, b = C.c_longlong(), C.c_longlong(), C.c_longlong()

@@ -1,0 +1,159 @@
+"""Host side of the boundary, no GPU: the C-ABI library loads and exports every
+declared symbol; the `.so3lr` loader verifies integrity and refuses models the
+kernels do not implement; element tokens and charge/multiplicity validation
+behave like the reference's.
+
+Reference tests mirrored: tests/test_element_map.cpp,
+source/so3lr-lammps-native/tests/test_capability_rejection.py (mutated
+manifests must be refused), test_loader_and_inputs.cpp (integrity checks),
+so3lr_charge_spin parity rules (src/so3lr_charge_spin.cpp:116-141).
+"""
+import hashlib
+import json
+import pathlib
+import re
+import struct
+
+import numpy as np
+import pytest
+
+from conftest import MODEL, ROOT
+
+HEADER = ROOT / "include" / "so3lr_b200.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from so3lr_b200 import load_library
+    return load_library()
+
+
+def test_library_exports_every_declared_symbol(lib):
+    text = HEADER.read_text()
+    declared = set(re.findall(r"^\s*(?:int|void|long long)\s*\**\s*(so3lr_\w+)\s*\(", text, re.M))
+    assert len(declared) >= 15
+    from so3lr_b200.runtime import EXPORTED
+    assert declared == set(EXPORTED), declared ^ set(EXPORTED)
+    for name in declared:
+        assert hasattr(lib, name), name
+
+
+def test_inspect_shipped_model():
+    from so3lr_b200 import inspect_model
+    info = inspect_model(MODEL)
+    assert info["layers"] == 3 and info["features"] == 128 and info["heads"] == 4 and info["head_width"] == 32
+    assert info["degrees"] == 4 and info["ev_width"] == 24 and info["rbf"] == 32
+    assert info["sr_cutoff"] == 4.5 and info["lr_cutoff"] == 12.0
+    assert abs(info["attention_norm"] - 13.168995780096482) < 1e-12
+    assert "zbl_learned" in info["summary"]
+
+
+def _rewrite(tmp_path: pathlib.Path, mutate_manifest=None, mutate_bytes=None) -> pathlib.Path:
+    data = bytearray(MODEL.read_bytes())
+    msize, psize = struct.unpack_from("<QQ", data, 16)
+    manifest = json.loads(bytes(data[128:128 + msize]))
+    payload = bytes(data[128 + msize:])
+    if mutate_manifest:
+        mutate_manifest(manifest)
+        mbytes = json.dumps(manifest, sort_keys=True, separators=(",", ":")).encode()
+        data = bytearray(data[:128]) + mbytes + payload
+        struct.pack_into("<QQ", data, 16, len(mbytes), len(payload))
+        data[32:64] = hashlib.sha256(mbytes).digest()
+    if mutate_bytes:
+        mutate_bytes(data)
+    out = tmp_path / "mutated.so3lr"
+    out.write_bytes(bytes(data))
+    return out
+
+
+@pytest.mark.parametrize("change, message", [
+    (lambda m: m["architecture"].__setitem__("invariant_features", 256), "invariant_features"),
+    (lambda m: m["architecture"].__setitem__("use_rms_norm", True), "use_rms_norm"),
+    (lambda m: m["architecture"].__setitem__("qk_norm", True), "qk_norm"),
+    (lambda m: m["architecture"].__setitem__("use_residual_scalars", True), "residual scalars"),
+    (lambda m: m["architecture"].__setitem__("repulsion_type", "nlh"), "repulsion_type"),
+    (lambda m: m["architecture"].__setitem__("brand_new_flag", 1), "unknown architecture key"),
+    (lambda m: m["architecture"]["output_heads"].append("c6_ratios_output_block"), "output heads"),
+    (lambda m: m["architecture"].__setitem__("message_normalization", "softmax"), "message_normalization"),
+    (lambda m: m.__setitem__("schema", "so3lr-native-model-v1"), "schema"),
+    (lambda m: m["architecture"].__setitem__("interaction_blocks", 9), "interaction_blocks"),
+])
+def test_capability_rejection(tmp_path, change, message):
+    from so3lr_b200 import So3lrError, inspect_model
+    path = _rewrite(tmp_path, mutate_manifest=change)
+    with pytest.raises(So3lrError, match=message):
+        inspect_model(path)
+
+
+@pytest.mark.parametrize("corrupt, message", [
+    (lambda d: d.__setitem__(slice(0, 8), b"SO3LRN2\x00"), "magic"),
+    (lambda d: d.__setitem__(len(d) - 1, (d[-1] ^ 0x5A) or 1), "payload SHA-256"),
+    (lambda d: d.__setitem__(200, d[200] ^ 0x01), "SHA-256|JSON"),
+    (lambda d: d.__setitem__(100, 1), "reserved"),
+    (lambda d: d.__setitem__(8, 2), "version"),
+])
+def test_integrity_checks(tmp_path, corrupt, message):
+    from so3lr_b200 import So3lrError, inspect_model
+    path = _rewrite(tmp_path, mutate_bytes=corrupt)
+    with pytest.raises(So3lrError, match=message):
+        inspect_model(path)
+
+
+def test_truncated_and_missing_model(tmp_path):
+    from so3lr_b200 import So3lrError, inspect_model
+    short = tmp_path / "short.so3lr"
+    short.write_bytes(MODEL.read_bytes()[:100])
+    with pytest.raises(So3lrError, match="shorter"):
+        inspect_model(short)
+    with pytest.raises(So3lrError, match="cannot open"):
+        inspect_model(tmp_path / "nope.so3lr")
+
+
+def test_python_and_native_loaders_agree():
+    """Both readers accept the shipped model and see the same architecture."""
+    from oracle.model_io import load_model
+    from so3lr_b200 import inspect_model
+    m = load_model(str(MODEL))
+    info = inspect_model(MODEL)
+    a = m.manifest["architecture"]
+    assert a["interaction_blocks"] == info["layers"]
+    assert a["invariant_features"] == info["features"]
+    assert a["short_range_cutoff_angstrom"] == info["sr_cutoff"]
+
+
+def test_element_tokens():
+    from so3lr_b200 import element_from_token
+    # reference tests/test_element_map.cpp: symbols are case-insensitive, numbers 1..99
+    assert element_from_token("H") == 1 and element_from_token("o") == 8 and element_from_token("CL") == 17
+    assert element_from_token("Es") == 99 and element_from_token("8") == 8 and element_from_token("99") == 99
+    for bad in ("0", "100", "Xx", "", "-1", "Fm"):
+        assert element_from_token(bad) == 0, bad
+
+
+@pytest.mark.parametrize("z, q, m, ok", [
+    ([8, 1, 1], 0, 1, True),
+    ([8, 1, 1], 1, 2, True),       # H2O+ doublet
+    ([8, 1, 1], 1, 1, False),      # 9 electrons cannot be a singlet
+    ([8, 8], 0, 3, True),          # O2 triplet
+    ([8, 8], 0, 2, False),
+    ([6, 1, 1, 1], 0, 2, True),    # methyl radical
+    ([1], 0, 3, False),            # more unpaired electrons than electrons
+    ([1], 2, 1, False),            # negative electron count
+    ([8, 1, 1], 0.5, 1, False),    # non-integer charge
+    ([8, 1, 1], 0, 0, False),      # multiplicity below 1
+    ([8, 1, 1], 0, 1.5, False),
+])
+def test_charge_multiplicity_validation(z, q, m, ok):
+    from so3lr_b200 import validate_charge_spin
+    problem = validate_charge_spin(z, q, m)
+    assert (problem == "") == ok, problem
+
+
+def test_create_without_gpu_fails_cleanly():
+    """On a host without a usable GPU the handle is refused with a message, never a crash."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    from so3lr_b200 import So3lrB200, So3lrError
+    with pytest.raises(So3lrError, match="CUDA|device"):
+        So3lrB200(MODEL, 0)
