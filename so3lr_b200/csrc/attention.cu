@@ -119,7 +119,8 @@ __global__ void __launch_bounds__(256) k_attention_reverse(
     int n, const int *__restrict__ row_start, const int *__restrict__ nbr, const int *__restrict__ edge_pair,
     const double *__restrict__ geo, const double *__restrict__ sh, const double *__restrict__ qkv,
     const double *__restrict__ f_inv, const double *__restrict__ f_ev, const double *__restrict__ g_a,
-    const double *__restrict__ g_A, double norm, double *__restrict__ g_qkv, double *__restrict__ pair_sc) {
+    const double *__restrict__ g_A, double norm, double *__restrict__ g_qkv, double *__restrict__ pair_sc,
+    double *__restrict__ g_filt_inv, double *__restrict__ g_filt_ev) {
   const int a = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (a >= n) return;
@@ -189,6 +190,18 @@ __global__ void __launch_bounds__(256) k_attention_reverse(
       gk[j] += c_k * (qb[j] * fi[j]);
       gke[j] += c_ke * (qeb[j] * fe[j]);
     }
+    if (code >= 0 && g_filt_inv != nullptr) {
+      // primary edge: the filter gradient of the pair, both directions summed
+      //   g_f_inv[c] = phi/norm (s_in[h] q_a[c] k_b[c] + s_out[h] q_b[c] k_a[c]), same for ev
+      double gi[4], ge[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        gi[j] = c_q * (qa[j] * kb[j]) + c_k * (qb[j] * ka[j]);
+        ge[j] = c_qe * (qea[j] * keb[j]) + c_ke * (qeb[j] * kea[j]);
+      }
+      store4(g_filt_inv + (size_t)p * kF + lane * 4, gi);
+      store4(g_filt_ev + (size_t)p * kF + lane * 4, ge);
+    }
     if (code >= 0) {
       // primary edge: "in" is into the pair's primary receiver a
       // lanes: quantity = lane / 4, head = lane % 4
@@ -225,11 +238,12 @@ __global__ void __launch_bounds__(256) k_attention_reverse(
 
 void launch_attention_reverse(int n, const NeighborState &nb, const double *geo, const double *sh,
                               const double *qkv, const double *f_inv, const double *f_ev, const double *g_a,
-                              const double *g_A, double norm, double *g_qkv, double *pair_sc,
-                              cudaStream_t s) {
+                              const double *g_A, double norm, double *g_qkv, double *pair_sc, double *g_filt_inv,
+                              double *g_filt_ev, cudaStream_t s) {
   if (n == 0) return;
   k_attention_reverse<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, nb.row_start, nb.nbr, nb.edge_pair, geo, sh, qkv,
-                                                           f_inv, f_ev, g_a, g_A, norm, g_qkv, pair_sc);
+                                                           f_inv, f_ev, g_a, g_A, norm, g_qkv, pair_sc, g_filt_inv,
+                                                           g_filt_ev);
   SO3_LAUNCH("attention_reverse");
 }
 

@@ -462,6 +462,8 @@ void Evaluator::build_neighbors() {
   gv_.reserve(std::size_t(P) * 3, 1.25);
   gl0_.reserve(std::size_t(P) * 4, 1.25);
   pair_sc_.reserve(std::size_t(P) * kPairScalars, 1.25);
+  g_filt_inv_.reserve(std::size_t(P) * kF, 1.25);
+  g_filt_ev_.reserve(std::size_t(P) * kF, 1.25);
   while (int(f_inv_.size()) < layers_) {
     f_inv_.emplace_back(new DeviceArray<double>());
     f_ev_.emplace_back(new DeviceArray<double>());
@@ -614,10 +616,11 @@ void Evaluator::compute() {
     launch_post_attn_rev_ln1(n, g_n1_.get(), xhat1_[b]->get(), rstd1_[b]->get(), w.ln1w, A_[b]->get(), w.cg_int,
                              g_cat_.get(), g_a_.get(), g_A_.get(), s);
     launch_attention_reverse(n, nb_, geo_.get(), sh_.get(), qkv_[b]->get(), f_inv_[b]->get(), f_ev_[b]->get(),
-                             g_a_.get(), g_A_.get(), norm_, b > 0 ? g_qkv_.get() : nullptr, pair_sc_.get(), s);
+                             g_a_.get(), g_A_.get(), norm_, b > 0 ? g_qkv_.get() : nullptr, pair_sc_.get(),
+                             g_filt_inv_.get(), g_filt_ev_.get(), s);
     prof_begin(1);
-    launch_filter_reverse(P, geo_.get(), sh_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr,
-                          w.cg_att, w.finv, w.fev, rad_, qkv_[b]->get(), g_A_.get(), pair_sc_.get(), norm_, b > 0,
+    launch_filter_reverse(P, geo_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr, w.cg_att, w.finv,
+                          w.fev, rad_, g_filt_inv_.get(), g_filt_ev_.get(), g_A_.get(), pair_sc_.get(), b > 0,
                           gv_.get(), gl0_.get(), s);
     prof_end(1, kFilterFlopsPerPair * double(P));
     if (b > 0) {

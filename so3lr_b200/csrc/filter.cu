@@ -199,25 +199,89 @@ void launch_filter_forward(int P, const double *geo, const int *pair_a, const in
 // reverse: filter input gradients for both directions of every pair, then the
 // radial, cutoff and spherical-harmonic gradients accumulated into gv[p] (3)
 // and, when ev is live, the L0 gradient gl0[p][4].
-// pair_sc[p][32] = alpha_inv, alpha_ev, s_inv, s_ev for the direction into the
-// pair's primary receiver ("in", [0:16]) and out of it ("out", [16:32]).
+// g_filt_inv/g_filt_ev[p][128]: dL/d(filter) with both directions summed,
+// written by the attention reverse. pair_sc[p][32] = alpha_inv, alpha_ev, s_inv,
+// s_ev for the direction into the pair's primary receiver ([0:16]) and out of it.
+// All per-tile inputs are streamed into shared memory with cp.async at kernel
+// start so the tensor-core work never waits on a gather.
 // ---------------------------------------------------------------------------
+namespace {
+__device__ inline void cp_async16(void *smem, const void *gmem) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ inline void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ inline void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+// copy a TP x width block of a row-major global array (row stride = width) to
+// shared memory with row stride lds; rows beyond P are zero-filled
+template <int WIDTH>
+__device__ inline void stage_rows(double *dst, int lds, const double *src, int p0, int P) {
+  constexpr int chunks = WIDTH / 2;  // 16-byte chunks per row
+  for (int idx = threadIdx.x; idx < TP * chunks; idx += blockDim.x) {
+    const int row = idx / chunks, c = idx % chunks;
+    double *d = dst + row * lds + 2 * c;
+    if (p0 + row < P) {
+      cp_async16(d, src + (size_t)(p0 + row) * WIDTH + 2 * c);
+    } else {
+      d[0] = 0.0;
+      d[1] = 0.0;
+    }
+  }
+}
+
+// acc (8 rows x 32 cols per warp, two independent K halves) += A(64 x 128, smem LDU) * B(128 x 32),
+// B(k, n) = W[k*32 + n]
+__device__ inline void mma_8x32_w2(double (&acc)[4][2], const double *A, int row0, const double *__restrict__ W,
+                                   int g, int t) {
+  double acc2[4][2];
+#pragma unroll
+  for (int ni = 0; ni < 4; ++ni) acc2[ni][0] = acc2[ni][1] = 0.0;
+#pragma unroll 4
+  for (int k0 = 0; k0 < 64; k0 += 4) {
+    const double a0 = A[(row0 + g) * LDU + k0 + t];
+    const double a1 = A[(row0 + g) * LDU + 64 + k0 + t];
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni) {
+      const double b0 = __ldg(W + (k0 + t) * 32 + ni * 8 + g);
+      const double b1 = __ldg(W + (64 + k0 + t) * 32 + ni * 8 + g);
+      dmma(acc[ni][0], acc[ni][1], a0, b0);
+      dmma(acc2[ni][0], acc2[ni][1], a1, b1);
+    }
+  }
+#pragma unroll
+  for (int ni = 0; ni < 4; ++ni) {
+    acc[ni][0] += acc2[ni][0];
+    acc[ni][1] += acc2[ni][1];
+  }
+}
+}  // namespace
+
 __global__ void __launch_bounds__(256) k_filter_reverse(
-    int P, const double *__restrict__ geo, const double *__restrict__ sh, const int *__restrict__ pa,
-    const int *__restrict__ pb, const double *__restrict__ ev, const double *__restrict__ cg, FilterW finv,
-    FilterW fev, RadialW rad, const double *__restrict__ qkv, const double *__restrict__ gA,
-    const double *__restrict__ pair_sc, double norm, int need_l0, double *__restrict__ gv,
-    double *__restrict__ gl0) {
+    int P, const double *__restrict__ geo, const int *__restrict__ pa, const int *__restrict__ pb,
+    const double *__restrict__ ev, const double *__restrict__ cg, FilterW finv, FilterW fev, RadialW rad,
+    const double *__restrict__ g_filt_inv, const double *__restrict__ g_filt_ev, const double *__restrict__ gA,
+    const double *__restrict__ pair_sc, int need_l0, double *__restrict__ gv, double *__restrict__ gl0) {
   extern __shared__ double sm[];
-  double *rbf = sm;             // TP x LDR
-  double *gF = rbf + TP * LDR;  // TP x LDU
-  double *gw = gF + TP * LDU;   // TP x LDR
-  double *l0 = gw + TP * LDR;   // TP x 4
-  double *gl = l0 + TP * 4;     // TP x 4 (L0 gradient accumulator)
-  double *rr = gl + TP * 4;     // TP
+  double *gFi = sm;                    // TP x LDU  (filter-inv gradient, later its hidden gradient)
+  double *gFe = gFi + TP * LDU;        // TP x LDU  (filter-ev gradient)
+  double *rbf = gFe + TP * LDU;        // TP x LDR
+  double *gw = rbf + TP * LDR;         // TP x LDR
+  double *sc = gw + TP * LDR;          // TP x 32
+  double *geos = sc + TP * kPairScalars;  // TP x 8
+  double *l0 = geos + TP * kGeo;       // TP x 4
+  double *gl = l0 + TP * 4;            // TP x 4
+  double *rr = gl + TP * 4;            // TP
   const int p0 = blockIdx.x * TP;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int wm = warp >> 2, wn = warp & 3;
+  stage_rows<kF>(gFi, LDU, g_filt_inv, p0, P);
+  stage_rows<kPairScalars>(sc, kPairScalars, pair_sc, p0, P);
+  stage_rows<kGeo>(geos, kGeo, geo, p0, P);
+  cp_async_commit();
+  stage_rows<kF>(gFe, LDU, g_filt_ev, p0, P);
+  cp_async_commit();
   if (tid < TP) {
     const int p = p0 + tid;
     rr[tid] = p < P ? geo[(size_t)p * kGeo] : 1.0;
@@ -232,29 +296,8 @@ __global__ void __launch_bounds__(256) k_filter_reverse(
 
   for (int filt = 0; filt < 2; ++filt) {
     const FilterW &W = filt ? fev : finv;
-    const int qproj = filt ? 3 : 0, kproj = filt ? 4 : 1;
-    const int sc_in = filt ? 12 : 8, sc_out = filt ? 28 : 24;
-    // gF[pl][c] = phi/norm * (s_in[h] q_a[c] k_b[c] + s_out[h] q_b[c] k_a[c]); warp per pair, lane owns 4 channels
-    for (int pl = warp; pl < TP; pl += 8) {
-      const int p = p0 + pl;
-      double v[4] = {0, 0, 0, 0};
-      if (p < P) {
-        const int a = pa[p], b = pb[p];
-        const int h = lane >> 3, o = (lane & 7) * 4;
-        const double phi = geo[(size_t)p * kGeo + 4];
-        const double s_in = pair_sc[(size_t)p * kPairScalars + sc_in + h];
-        const double s_out = pair_sc[(size_t)p * kPairScalars + sc_out + h];
-        const double ci = phi / norm * s_in, co = phi / norm * s_out;
-        const double *qa = qkv + (size_t)a * kQKV + h * 160 + qproj * 32 + o;
-        const double *ka = qkv + (size_t)a * kQKV + h * 160 + kproj * 32 + o;
-        const double *qb = qkv + (size_t)b * kQKV + h * 160 + qproj * 32 + o;
-        const double *kb = qkv + (size_t)b * kQKV + h * 160 + kproj * 32 + o;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = ci * (qa[j] * kb[j]) + co * (qb[j] * ka[j]);
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) gF[pl * LDU + lane * 4 + j] = v[j];
-    }
+    double *gF = filt ? gFe : gFi;
+    if (filt == 0) cp_async_wait<1>(); else cp_async_wait<0>();
     __syncthreads();
     // recompute the hidden pre-activation of the rbf branch: sp = silu'(rbf W0^T + b0)
     double sp[4][4][2];
@@ -282,7 +325,7 @@ __global__ void __launch_bounds__(256) k_filter_reverse(
     double gwa[4][2];
 #pragma unroll
     for (int ni = 0; ni < 4; ++ni) gwa[ni][0] = gwa[ni][1] = 0.0;
-    mma_8x32_w(gwa, gF, warp * 8, W.v1, g, t);
+    mma_8x32_w2(gwa, gF, warp * 8, W.v1, g, t);
     __syncthreads();  // everyone is done reading gF
 #pragma unroll
     for (int mi = 0; mi < 4; ++mi)
@@ -300,16 +343,24 @@ __global__ void __launch_bounds__(256) k_filter_reverse(
     }
     __syncthreads();
     // g_rbf += g_pre W0 (B(k=j, n=k') = W0[j][k'], W0 is [128][32])
-    mma_8x32_w(grbf_acc, gF, warp * 8, W.w0, g, t);
-    // L0 gradient: g_pe = g_w * silu'(L0 V0^T + c0); gl[d] += sum_j g_pe[j] V0[j][d]
+    mma_8x32_w2(grbf_acc, gF, warp * 8, W.w0, g, t);
+    // L0 gradient: g_pe = g_w * silu'(L0 V0^T + c0) (one element per thread-slot,
+    // in place in gw), then gl[d] += sum_j g_pe[j] V0[j][d]
     if (need_l0) {
-      const int pl = tid >> 2, d = tid & 3;
-      const double l00 = l0[pl * 4], l01 = l0[pl * 4 + 1], l02 = l0[pl * 4 + 2], l03 = l0[pl * 4 + 3];
-      double s = 0.0;
-      for (int j = 0; j < kEH; ++j) {
-        const double pe = l00 * W.v0[j * 4] + l01 * W.v0[j * 4 + 1] + l02 * W.v0[j * 4 + 2] + l03 * W.v0[j * 4 + 3] + W.c0[j];
-        s += gw[pl * LDR + j] * silu_prime(pe) * W.v0[j * 4 + d];
+      {
+        const int pl = tid >> 2, j0 = (tid & 3) * 8;
+        const double l00 = l0[pl * 4], l01 = l0[pl * 4 + 1], l02 = l0[pl * 4 + 2], l03 = l0[pl * 4 + 3];
+#pragma unroll
+        for (int j = j0; j < j0 + 8; ++j) {
+          const double pe = l00 * W.v0[j * 4] + l01 * W.v0[j * 4 + 1] + l02 * W.v0[j * 4 + 2] + l03 * W.v0[j * 4 + 3] + W.c0[j];
+          gw[pl * LDR + j] *= silu_prime(pe);
+        }
       }
+      __syncthreads();
+      const int pl = tid >> 2, d = tid & 3;
+      double s = 0.0;
+#pragma unroll 8
+      for (int j = 0; j < kEH; ++j) s += gw[pl * LDR + j] * W.v0[j * 4 + d];
       gl[pl * 4 + d] += s;
     }
     __syncthreads();
@@ -322,12 +373,15 @@ __global__ void __launch_bounds__(256) k_filter_reverse(
     gw[row * LDR + col + 1] = grbf_acc[ni][1];
   }
   __syncthreads();
-  // per pair: radial + cutoff + SH gradients -> gv; warp per pair
+  // per pair, phase 1 (warp per pair): radial + cutoff gradient and the
+  // harmonic gradient gY (pair orientation) -> shared memory
+  double *grs = l0;     // TP radial gradients (the L0 inputs are no longer needed)
+  double *ybuf = gFe;   // TP x kEV harmonic gradients (the ev filter tile is no longer needed)
   for (int pl = warp; pl < TP; pl += 8) {
     const int p = p0 + pl;
     if (p >= P) continue;
-    const double *gp = geo + (size_t)p * kGeo;
-    const double r = gp[0], ux = gp[1], uy = gp[2], uz = gp[3], phi = gp[4], dphi = gp[5];
+    const double *gp = geos + pl * kGeo;
+    const double r = gp[0], phi = gp[4], dphi = gp[5];
     // Bernstein derivative (block2_attention_input_reverse.cpp:322-333)
     const double raw_x = exp(-rad.gamma * r);
     double gr = 0.0;
@@ -336,54 +390,54 @@ __global__ void __launch_bounds__(256) k_filter_reverse(
       gr = gw[pl * LDR + lane] * rbf[pl * LDR + lane] * dl;
     }
     // cutoff gradient: sum over heads of alpha*s for both directions
-    const double *sc = pair_sc + (size_t)p * kPairScalars;
-    const int h = lane & 3, which = lane >> 2;  // which: 0..7 -> (alpha, s) pairs below
-    double gphi_term = 0.0;
+    const double *s = sc + pl * kPairScalars;
+    const int h = lane & 3, which = lane >> 2;
     if (which < 4) {
       // (alpha_in_inv, s_in_inv), (alpha_in_ev, s_in_ev), (alpha_out_inv, s_out_inv), (alpha_out_ev, s_out_ev)
       const int ao = which == 0 ? 0 : (which == 1 ? 4 : (which == 2 ? 16 : 20));
-      gphi_term = sc[ao + h] * sc[ao + 8 + h];
+      gr += s[ao + h] * s[ao + 8 + h] * dphi;
     }
-    gr += gphi_term * dphi;
-    // spherical-harmonic gradient (pair orientation)
-    double gy = 0.0;
     if (lane < kEV) {
       const int d = degree_of_channel(lane);
-      const double a_in = sc[4 + d], a_out = sc[20 + d];
       const double gAa = gA[(size_t)pa[p] * kEV + lane], gAb = gA[(size_t)pb[p] * kEV + lane];
-      gy = phi * (a_in * gAa + parity_sign(d) * a_out * gAb);
+      ybuf[pl * kEV + lane] = phi * (s[4 + d] * gAa + parity_sign(d) * s[20 + d] * gAb);
     }
-    __shared__ double ybuf[8][kEV];
-    if (lane < kEV) ybuf[warp][lane] = gy;
     for (int off = 16; off > 0; off >>= 1) gr += __shfl_xor_sync(0xffffffffu, gr, off);
-    __syncwarp();
-    if (lane == 0) {
-      double gux, guy, guz;
-      real_sh_vjp(ux, uy, uz, ybuf[warp], gux, guy, guz);
-      const double rad_c = ux * gux + uy * guy + uz * guz;
-      const double ir = r > 1.0e-14 ? 1.0 / r : 0.0;
-      gv[3 * p] += gr * ux + (gux - ux * rad_c) * ir;
-      gv[3 * p + 1] += gr * uy + (guy - uy * rad_c) * ir;
-      gv[3 * p + 2] += gr * uz + (guz - uz * rad_c) * ir;
-    }
+    if (lane == 0) grs[pl] = gr;
     if (need_l0 && lane < 4) gl0[(size_t)p * 4 + lane] = gl[pl * 4 + lane];
-    __syncwarp();
+  }
+  __syncthreads();
+  // phase 2 (thread per pair): spherical-harmonic VJP and the Cartesian pair gradient
+  if (tid < TP && p0 + tid < P) {
+    const int p = p0 + tid;
+    const double *gp = geos + tid * kGeo;
+    const double r = gp[0], ux = gp[1], uy = gp[2], uz = gp[3];
+    double gux, guy, guz;
+    real_sh_vjp(ux, uy, uz, ybuf + tid * kEV, gux, guy, guz);
+    const double rad_c = ux * gux + uy * guy + uz * guz;
+    const double ir = r > 1.0e-14 ? 1.0 / r : 0.0;
+    const double gr = grs[tid];
+    gv[3 * p] += gr * ux + (gux - ux * rad_c) * ir;
+    gv[3 * p + 1] += gr * uy + (guy - uy * rad_c) * ir;
+    gv[3 * p + 2] += gr * uz + (guz - uz * rad_c) * ir;
   }
 }
 
-void launch_filter_reverse(int P, const double *geo, const double *sh, const int *pair_a, const int *pair_b,
-                           const double *ev, const double *cg_att, const FilterW &finv, const FilterW &fev,
-                           const RadialW &rad, const double *qkv, const double *gA, const double *pair_sc,
-                           double norm, bool need_l0, double *gv, double *gl0, cudaStream_t s) {
+void launch_filter_reverse(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
+                           const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,
+                           const double *g_filt_inv, const double *g_filt_ev, const double *gA,
+                           const double *pair_sc, bool need_l0, double *gv, double *gl0, cudaStream_t s) {
   if (P == 0) return;
-  const size_t smem = sizeof(double) * (TP * LDR * 2 + TP * LDU + TP * 8 + TP);
+  const size_t smem =
+      sizeof(double) * (2 * TP * LDU + 2 * TP * LDR + TP * kPairScalars + TP * kGeo + TP * 8 + TP);
   static bool configured = false;
   if (!configured) {
     SO3_CUDA(cudaFuncSetAttribute(k_filter_reverse, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     configured = true;
   }
-  k_filter_reverse<<<(P + TP - 1) / TP, 256, smem, s>>>(P, geo, sh, pair_a, pair_b, ev, cg_att, finv, fev, rad, qkv,
-                                                         gA, pair_sc, norm, need_l0 ? 1 : 0, gv, gl0);
+  k_filter_reverse<<<(P + TP - 1) / TP, 256, smem, s>>>(P, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad,
+                                                         g_filt_inv, g_filt_ev, gA, pair_sc, need_l0 ? 1 : 0, gv,
+                                                         gl0);
   SO3_LAUNCH("filter_reverse");
 }
 

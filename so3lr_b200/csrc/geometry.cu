@@ -199,8 +199,15 @@ __device__ inline double warp_sum(double v) {
   return v;
 }
 
-// one warp per atom; lanes stride over the candidates of each cell
-__global__ void __launch_bounds__(256) k_long_range(
+// One warp per atom. Lanes test the candidates of each stencil cell 32 at a
+// time; the ones inside the cutoff are compacted (ballot + prefix) into a
+// per-warp queue in shared memory, and the expensive pair math runs only on full
+// batches of 32 queued pairs, so no lane idles on an out-of-range candidate.
+// Every lane accumulates its queue slots in a fixed order, so the result is
+// deterministic.
+constexpr int kLrWarps = 8;
+constexpr int kLrQueue = 64;
+__global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
     int n, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
     const int *__restrict__ cell_start, const int *__restrict__ cell_count, const int *__restrict__ cell_atoms,
     const int *__restrict__ image_of, const int *__restrict__ image_start, int reach, double rc2,
@@ -208,6 +215,9 @@ __global__ void __launch_bounds__(256) k_long_range(
     const double *__restrict__ aref, const double *__restrict__ cref, int table, LrDev p,
     double *__restrict__ e_lr, double *__restrict__ e_elec, double *__restrict__ e_disp, double *__restrict__ dq,
     double *__restrict__ dh, double *__restrict__ f_lr, double *__restrict__ w_lr) {
+  __shared__ int qj[kLrWarps][kLrQueue];
+  __shared__ double qv[kLrWarps][kLrQueue][3];
+  const int wl = threadIdx.x >> 5;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= n) return;
@@ -217,12 +227,11 @@ __global__ void __launch_bounds__(256) k_long_range(
   const int Zi = z[i];
   double acc_ee = 0, acc_ed = 0, acc_dq = 0, acc_dh = 0, fx = 0, fy = 0, fz = 0;
   double wxx = 0, wyy = 0, wzz = 0, wxy = 0, wxz = 0, wyz = 0;
-  auto visit = [&](int j, double shx, double shy, double shz) {
-    const double vx = xw[3 * j] + shx - xi, vy = xw[3 * j + 1] + shy - yi, vz = xw[3 * j + 2] + shz - zi;
-    const double r2 = vx * vx + vy * vy + vz * vz;
-    if (!(r2 > 0.0 && r2 < rc2)) return;
-    const double r = sqrt(r2);
-    if (!(r > 1.0e-12)) return;
+  int count = 0;  // warp-uniform queue length
+  auto evaluate = [&](int slot) {
+    const int j = qj[wl][slot];
+    const double vx = qv[wl][slot][0], vy = qv[wl][slot][1], vz = qv[wl][slot][2];
+    const double r = sqrt(vx * vx + vy * vy + vz * vz);
     const LrPair o = lr_pair(p, r, qi, q[j], hi, h[j], Zi, z[j], aref, cref, table);
     acc_ee += o.e_elec;
     acc_ed += o.e_disp;
@@ -239,9 +248,54 @@ __global__ void __launch_bounds__(256) k_long_range(
     wxz -= 0.5 * s * vx * vz;
     wyz -= 0.5 * s * vy * vz;
   };
+  // test 32 candidates (one per lane), enqueue the ones inside the cutoff, drain full batches
+  auto offer = [&](bool have, int j, double shx, double shy, double shz) {
+    bool valid = false;
+    double vx = 0, vy = 0, vz = 0;
+    if (have) {
+      vx = xw[3 * j] + shx - xi;
+      vy = xw[3 * j + 1] + shy - yi;
+      vz = xw[3 * j + 2] + shz - zi;
+      const double r2 = vx * vx + vy * vy + vz * vz;
+      valid = r2 > 0.0 && r2 < rc2 && r2 > 1.0e-24;
+    }
+    const unsigned mask = __ballot_sync(0xffffffffu, valid);
+    if (valid) {
+      const int slot = count + __popc(mask & ((1u << lane) - 1u));
+      qj[wl][slot] = j;
+      qv[wl][slot][0] = vx;
+      qv[wl][slot][1] = vy;
+      qv[wl][slot][2] = vz;
+    }
+    count += __popc(mask);
+    __syncwarp();
+    if (count >= 32) {
+      evaluate(lane);
+      __syncwarp();
+      const int rest = count - 32;
+      int mj = 0;
+      double m0 = 0, m1 = 0, m2 = 0;
+      if (lane < rest) {
+        mj = qj[wl][32 + lane];
+        m0 = qv[wl][32 + lane][0];
+        m1 = qv[wl][32 + lane][1];
+        m2 = qv[wl][32 + lane][2];
+      }
+      __syncwarp();
+      if (lane < rest) {
+        qj[wl][lane] = mj;
+        qv[wl][lane][0] = m0;
+        qv[wl][lane][1] = m1;
+        qv[wl][lane][2] = m2;
+      }
+      count = rest;
+      __syncwarp();
+    }
+  };
   if (!g.periodic) {
     const int im = image_of[i];
-    for (int j = image_start[im] + lane; j < image_start[im + 1]; j += 32) visit(j, 0.0, 0.0, 0.0);
+    const int s = image_start[im], e = image_start[im + 1];
+    for (int base = s; base < e; base += 32) offer(base + lane < e, base + lane, 0.0, 0.0, 0.0);
   } else {
     const int c = cell[i];
     const int cx = c % g.ncell[0], cy = (c / g.ncell[0]) % g.ncell[1], cz = c / (g.ncell[0] * g.ncell[1]);
@@ -261,11 +315,13 @@ __global__ void __launch_bounds__(256) k_long_range(
           const int *a = cell_atoms + cell_start[cc];
           const int m = cell_count[cc];
           const double shx = sx * g.len[0], shy = sy * g.len[1], shz = sz * g.len[2];
-          for (int t = lane; t < m; t += 32) visit(a[t], shx, shy, shz);
+          for (int base = 0; base < m; base += 32)
+            offer(base + lane < m, base + lane < m ? a[base + lane] : 0, shx, shy, shz);
         }
       }
     }
   }
+  if (lane < count) evaluate(lane);
   acc_ee = warp_sum(acc_ee);
   acc_ed = warp_sum(acc_ed);
   acc_dq = warp_sum(acc_dq);
@@ -299,7 +355,7 @@ void launch_long_range(int n, const NeighborState &nb, double rc_lr, const int *
                        double *f_lr, double *w_lr, cudaStream_t s) {
   if (n == 0) return;
   const int reach = sr_reach(nb.grid, rc_lr);
-  const int threads = 256;
+  const int threads = kLrWarps * 32;
   const int blocks = (n * 32 + threads - 1) / threads;
   k_long_range<<<blocks, threads, 0, s>>>(n, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count, nb.cell_atoms,
                                           nb.image_of, nb.image_start, reach, rc_lr * rc_lr, z, q, h, alpha_ref,

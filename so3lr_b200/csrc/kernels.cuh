@@ -60,10 +60,12 @@ void launch_long_range(int n, const NeighborState &nb, double rc_lr, const int *
 void launch_filter_forward(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
                            const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,
                            double *f_inv, double *f_ev, cudaStream_t s);
-void launch_filter_reverse(int P, const double *geo, const double *sh, const int *pair_a, const int *pair_b,
-                           const double *ev, const double *cg_att, const FilterW &finv, const FilterW &fev,
-                           const RadialW &rad, const double *qkv, const double *gA, const double *pair_sc,
-                           double norm, bool need_l0, double *gv, double *gl0, cudaStream_t s);
+// g_filt_inv / g_filt_ev: per-pair gradient w.r.t. the two filter outputs (written by
+// the attention reverse at each pair's primary edge)
+void launch_filter_reverse(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
+                           const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,
+                           const double *g_filt_inv, const double *g_filt_ev, const double *gA,
+                           const double *pair_sc, bool need_l0, double *gv, double *gl0, cudaStream_t s);
 
 // ---- attention (receiver CSR gathers) ----------------------------------------
 void launch_attention_forward(int n, const NeighborState &nb, const double *geo, const double *sh,
@@ -71,8 +73,8 @@ void launch_attention_forward(int n, const NeighborState &nb, const double *geo,
                               double *d_inv, double *d_ev, cudaStream_t s);
 void launch_attention_reverse(int n, const NeighborState &nb, const double *geo, const double *sh,
                               const double *qkv, const double *f_inv, const double *f_ev, const double *g_a,
-                              const double *g_A, double norm, double *g_qkv, double *pair_sc,
-                              cudaStream_t s);
+                              const double *g_A, double norm, double *g_qkv, double *pair_sc, double *g_filt_inv,
+                              double *g_filt_ev, cudaStream_t s);
 void launch_ev_l0_reverse(int n, const NeighborState &nb, const double *ev, const double *cg_att,
                           const double *gl0, const double *g_A, double *g_ev, cudaStream_t s);
 
