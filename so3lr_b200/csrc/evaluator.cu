@@ -347,6 +347,8 @@ void Evaluator::alloc_atoms() {
   dq_.reserve(n);
   dh_.reserve(n);
   f_lr_.reserve(3 * n);
+  lr_pos4_.reserve(4 * n);
+  lr_par4_.reserve(4 * n);
   w_lr_.reserve(6 * n);
   img_sums_.reserve(nimg + 1);
   dq_mean_.reserve(nimg + 1);
@@ -560,6 +562,7 @@ void Evaluator::compute() {
 
   // ---- long range ----------------------------------------------------------
   launch_long_range(n, nb_, lr_cut_, z_.get(), q_.get(), ratio_.get(), alpha_ref_, c6_ref_, ref_table_, lr_,
+                    reinterpret_cast<double4 *>(lr_pos4_.get()), reinterpret_cast<double4 *>(lr_par4_.get()),
                     e_lr_.get(), e_elec_.get(), e_disp_.get(), dq_.get(), dh_.get(), f_lr_.get(), w_lr_.get(), s);
   launch_segment_sum(nimg, image_start_.get(), dq_.get(), 1, 1, img_sums_.get(), s);
   launch_charge_correct(nimg, nullptr, nullptr, nullptr, nullptr, image_start_.get(), nullptr, dq_mean_.get(),

@@ -120,9 +120,10 @@ struct LrPair {
 };
 
 // One unordered pair seen from atom i (its partner j); r > 0 and r < cutoff.
-__device__ inline LrPair lr_pair(const LrDev &p, double r, double qi, double qj, double hi, double hj, int zi,
-                                 int zj, const double *__restrict__ aref, const double *__restrict__ cref,
-                                 int table) {
+// ai0/aj0, ci0/cj0: reference polarisabilities and C6 of the two elements
+// (aj0 < 0 marks an element without reference data: no dispersion).
+__device__ inline LrPair lr_pair_tab(const LrDev &p, double r, double qi, double qj, double hi, double hj,
+                                     double ai0, double aj0, double ci0, double cj0) {
   constexpr double inv_sqrt_pi = 0.56418958354775628695;
   LrPair o{0, 0, 0, 0, 0};
   double esw, desw;
@@ -140,9 +141,7 @@ __device__ inline LrPair lr_pair(const LrDev &p, double r, double qi, double qj,
   o.dq = p.full_scale * p.ke * kernel * qj;
   const double erad = p.full_scale * p.ke * qi * qj * rkernel;
   double drad = 0.0;
-  const int zi0 = zi - 1, zj0 = zj - 1;
-  if (zi0 >= 0 && zj0 >= 0 && zi0 < table && zj0 < table) {
-    const double ai0 = aref[zi0], aj0 = aref[zj0], ci0 = cref[zi0], cj0 = cref[zj0];
+  if (ai0 >= 0.0 && aj0 >= 0.0) {
     const double ai = ai0 * hi, aj = aj0 * hj;
     const double c6i = ci0 * hi * hi, c6j = cj0 * hj * hj;
     const double alpha = 0.5 * (ai + aj);
@@ -199,23 +198,39 @@ __device__ inline double warp_sum(double v) {
   return v;
 }
 
-// One warp per atom. Lanes test the candidates of each stencil cell 32 at a
-// time; the ones inside the cutoff are compacted (ballot + prefix) into a
-// per-warp queue in shared memory, and the expensive pair math runs only on full
-// batches of 32 queued pairs, so no lane idles on an out-of-range candidate.
-// Every lane accumulates its queue slots in a fixed order, so the result is
-// deterministic.
+// Cell-ordered copy of what the long-range pair term reads from a partner atom:
+// pos4[k] = (x, y, z, q) and par4[k] = (h, alpha_ref, C6_ref, 0) of atom
+// cell_atoms[k] (atom k itself for open boundaries), so that every stencil row
+// of cells is one contiguous, coalesced range of candidates.
+__global__ void k_lr_gather(int n, int periodic, const int *__restrict__ cell_atoms, const double *__restrict__ xw,
+                            const double *__restrict__ q, const double *__restrict__ h, const int *__restrict__ z,
+                            const double *__restrict__ aref, const double *__restrict__ cref, int table,
+                            double4 *__restrict__ pos4, double4 *__restrict__ par4) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  const int j = periodic ? cell_atoms[k] : k;
+  const int zj = z[j] - 1;
+  const bool known = zj >= 0 && zj < table;
+  pos4[k] = make_double4(xw[3 * j], xw[3 * j + 1], xw[3 * j + 2], q[j]);
+  par4[k] = make_double4(h[j], known ? aref[zj] : -1.0, known ? cref[zj] : 0.0, 0.0);
+}
+
+// One warp per atom. Lanes test 32 consecutive candidates of a contiguous
+// stencil range at a time; the ones inside the cutoff are compacted (ballot +
+// prefix) into a per-warp queue in shared memory, and the pair math runs only
+// on full batches of 32 queued pairs. Every lane accumulates its queue slots in
+// a fixed order, so the result is deterministic.
 constexpr int kLrWarps = 8;
 constexpr int kLrQueue = 64;
 __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
     int n, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
-    const int *__restrict__ cell_start, const int *__restrict__ cell_count, const int *__restrict__ cell_atoms,
-    const int *__restrict__ image_of, const int *__restrict__ image_start, int reach, double rc2,
-    const int *__restrict__ z, const double *__restrict__ q, const double *__restrict__ h,
-    const double *__restrict__ aref, const double *__restrict__ cref, int table, LrDev p,
-    double *__restrict__ e_lr, double *__restrict__ e_elec, double *__restrict__ e_disp, double *__restrict__ dq,
-    double *__restrict__ dh, double *__restrict__ f_lr, double *__restrict__ w_lr) {
-  __shared__ int qj[kLrWarps][kLrQueue];
+    const int *__restrict__ cell_start, const int *__restrict__ cell_count, const int *__restrict__ image_of,
+    const int *__restrict__ image_start, int reach, double rc2, const double4 *__restrict__ pos4,
+    const double4 *__restrict__ par4, const int *__restrict__ z, const double *__restrict__ q,
+    const double *__restrict__ h, const double *__restrict__ aref, const double *__restrict__ cref, int table,
+    LrDev p, double *__restrict__ e_lr, double *__restrict__ e_elec, double *__restrict__ e_disp,
+    double *__restrict__ dq, double *__restrict__ dh, double *__restrict__ f_lr, double *__restrict__ w_lr) {
+  __shared__ int qk[kLrWarps][kLrQueue];
   __shared__ double qv[kLrWarps][kLrQueue][3];
   const int wl = threadIdx.x >> 5;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -225,14 +240,17 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
   const double xi = xw[3 * i], yi = xw[3 * i + 1], zi = xw[3 * i + 2];
   const double qi = q[i], hi = h[i];
   const int Zi = z[i];
+  const double ai0 = (Zi - 1 >= 0 && Zi - 1 < table) ? aref[Zi - 1] : -1.0;
+  const double ci0 = (Zi - 1 >= 0 && Zi - 1 < table) ? cref[Zi - 1] : 0.0;
   double acc_ee = 0, acc_ed = 0, acc_dq = 0, acc_dh = 0, fx = 0, fy = 0, fz = 0;
   double wxx = 0, wyy = 0, wzz = 0, wxy = 0, wxz = 0, wyz = 0;
   int count = 0;  // warp-uniform queue length
   auto evaluate = [&](int slot) {
-    const int j = qj[wl][slot];
+    const int k = qk[wl][slot];
     const double vx = qv[wl][slot][0], vy = qv[wl][slot][1], vz = qv[wl][slot][2];
     const double r = sqrt(vx * vx + vy * vy + vz * vz);
-    const LrPair o = lr_pair(p, r, qi, q[j], hi, h[j], Zi, z[j], aref, cref, table);
+    const double4 pj = pos4[k], hj = par4[k];
+    const LrPair o = lr_pair_tab(p, r, qi, pj.w, hi, hj.x, ai0, hj.y, ci0, hj.z);
     acc_ee += o.e_elec;
     acc_ed += o.e_disp;
     acc_dq += o.dq;
@@ -248,75 +266,78 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
     wxz -= 0.5 * s * vx * vz;
     wyz -= 0.5 * s * vy * vz;
   };
-  // test 32 candidates (one per lane), enqueue the ones inside the cutoff, drain full batches
-  auto offer = [&](bool have, int j, double shx, double shy, double shz) {
-    bool valid = false;
-    double vx = 0, vy = 0, vz = 0;
-    if (have) {
-      vx = xw[3 * j] + shx - xi;
-      vy = xw[3 * j + 1] + shy - yi;
-      vz = xw[3 * j + 2] + shz - zi;
-      const double r2 = vx * vx + vy * vy + vz * vz;
-      valid = r2 > 0.0 && r2 < rc2 && r2 > 1.0e-24;
-    }
-    const unsigned mask = __ballot_sync(0xffffffffu, valid);
-    if (valid) {
-      const int slot = count + __popc(mask & ((1u << lane) - 1u));
-      qj[wl][slot] = j;
-      qv[wl][slot][0] = vx;
-      qv[wl][slot][1] = vy;
-      qv[wl][slot][2] = vz;
-    }
-    count += __popc(mask);
-    __syncwarp();
-    if (count >= 32) {
-      evaluate(lane);
-      __syncwarp();
-      const int rest = count - 32;
-      int mj = 0;
-      double m0 = 0, m1 = 0, m2 = 0;
-      if (lane < rest) {
-        mj = qj[wl][32 + lane];
-        m0 = qv[wl][32 + lane][0];
-        m1 = qv[wl][32 + lane][1];
-        m2 = qv[wl][32 + lane][2];
+  // test the candidates [s, e) of the cell-ordered arrays, shifted by (shx, shy, shz)
+  auto scan_range = [&](int s, int e, double shx, double shy, double shz) {
+    for (int base = s; base < e; base += 32) {
+      const int k = base + lane;
+      bool valid = false;
+      double vx = 0, vy = 0, vz = 0;
+      if (k < e) {
+        const double4 pk = pos4[k];
+        vx = pk.x + shx - xi;
+        vy = pk.y + shy - yi;
+        vz = pk.z + shz - zi;
+        const double r2 = vx * vx + vy * vy + vz * vz;
+        valid = r2 > 1.0e-24 && r2 < rc2;
       }
-      __syncwarp();
-      if (lane < rest) {
-        qj[wl][lane] = mj;
-        qv[wl][lane][0] = m0;
-        qv[wl][lane][1] = m1;
-        qv[wl][lane][2] = m2;
+      const unsigned mask = __ballot_sync(0xffffffffu, valid);
+      if (valid) {
+        const int slot = count + __popc(mask & ((1u << lane) - 1u));
+        qk[wl][slot] = k;
+        qv[wl][slot][0] = vx;
+        qv[wl][slot][1] = vy;
+        qv[wl][slot][2] = vz;
       }
-      count = rest;
+      count += __popc(mask);
       __syncwarp();
+      if (count >= 32) {
+        evaluate(lane);
+        __syncwarp();
+        const int rest = count - 32;
+        int mk = 0;
+        double m0 = 0, m1 = 0, m2 = 0;
+        if (lane < rest) {
+          mk = qk[wl][32 + lane];
+          m0 = qv[wl][32 + lane][0];
+          m1 = qv[wl][32 + lane][1];
+          m2 = qv[wl][32 + lane][2];
+        }
+        __syncwarp();
+        if (lane < rest) {
+          qk[wl][lane] = mk;
+          qv[wl][lane][0] = m0;
+          qv[wl][lane][1] = m1;
+          qv[wl][lane][2] = m2;
+        }
+        count = rest;
+        __syncwarp();
+      }
     }
   };
   if (!g.periodic) {
     const int im = image_of[i];
-    const int s = image_start[im], e = image_start[im + 1];
-    for (int base = s; base < e; base += 32) offer(base + lane < e, base + lane, 0.0, 0.0, 0.0);
+    scan_range(image_start[im], image_start[im + 1], 0.0, 0.0, 0.0);
   } else {
+    const int nx = g.ncell[0], ny = g.ncell[1], nz = g.ncell[2];
     const int c = cell[i];
-    const int cx = c % g.ncell[0], cy = (c / g.ncell[0]) % g.ncell[1], cz = c / (g.ncell[0] * g.ncell[1]);
+    const int cx = c % nx, cy = (c / nx) % ny, cz = c / (nx * ny);
+    // x runs of constant periodic shift: cells [lo, hi] of one row are contiguous
+    const int sx_lo = (cx - reach >= 0) ? 0 : -((reach - cx + nx - 1) / nx);
+    const int sx_hi = (cx + reach) / nx;
     for (int oz = -reach; oz <= reach; ++oz) {
       int wz = cz + oz, sz = 0;
-      while (wz < 0) { wz += g.ncell[2]; --sz; }
-      while (wz >= g.ncell[2]) { wz -= g.ncell[2]; ++sz; }
+      while (wz < 0) { wz += nz; --sz; }
+      while (wz >= nz) { wz -= nz; ++sz; }
       for (int oy = -reach; oy <= reach; ++oy) {
         int wy = cy + oy, sy = 0;
-        while (wy < 0) { wy += g.ncell[1]; --sy; }
-        while (wy >= g.ncell[1]) { wy -= g.ncell[1]; ++sy; }
-        for (int ox = -reach; ox <= reach; ++ox) {
-          int wx = cx + ox, sx = 0;
-          while (wx < 0) { wx += g.ncell[0]; --sx; }
-          while (wx >= g.ncell[0]) { wx -= g.ncell[0]; ++sx; }
-          const int cc = (wz * g.ncell[1] + wy) * g.ncell[0] + wx;
-          const int *a = cell_atoms + cell_start[cc];
-          const int m = cell_count[cc];
-          const double shx = sx * g.len[0], shy = sy * g.len[1], shz = sz * g.len[2];
-          for (int base = 0; base < m; base += 32)
-            offer(base + lane < m, base + lane < m ? a[base + lane] : 0, shx, shy, shz);
+        while (wy < 0) { wy += ny; --sy; }
+        while (wy >= ny) { wy -= ny; ++sy; }
+        const int row = (wz * ny + wy) * nx;
+        const double shy = sy * g.len[1], shz = sz * g.len[2];
+        for (int sx = sx_lo; sx <= sx_hi; ++sx) {
+          const int lo = max(0, cx - reach - sx * nx), hi = min(nx - 1, cx + reach - sx * nx);
+          if (lo > hi) continue;
+          scan_range(cell_start[row + lo], cell_start[row + hi] + cell_count[row + hi], sx * g.len[0], shy, shz);
         }
       }
     }
@@ -351,14 +372,17 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
 
 void launch_long_range(int n, const NeighborState &nb, double rc_lr, const int *z, const double *q,
                        const double *h, const double *alpha_ref, const double *c6_ref, int table_size,
-                       LrDev p, double *e_lr, double *e_elec, double *e_disp, double *dq, double *dh,
-                       double *f_lr, double *w_lr, cudaStream_t s) {
+                       LrDev p, double4 *pos4, double4 *par4, double *e_lr, double *e_elec, double *e_disp,
+                       double *dq, double *dh, double *f_lr, double *w_lr, cudaStream_t s) {
   if (n == 0) return;
+  k_lr_gather<<<(n + 255) / 256, 256, 0, s>>>(n, nb.grid.periodic, nb.cell_atoms, nb.xw, q, h, z, alpha_ref, c6_ref,
+                                              table_size, pos4, par4);
+  SO3_LAUNCH("lr_gather");
   const int reach = sr_reach(nb.grid, rc_lr);
   const int threads = kLrWarps * 32;
   const int blocks = (n * 32 + threads - 1) / threads;
-  k_long_range<<<blocks, threads, 0, s>>>(n, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count, nb.cell_atoms,
-                                          nb.image_of, nb.image_start, reach, rc_lr * rc_lr, z, q, h, alpha_ref,
+  k_long_range<<<blocks, threads, 0, s>>>(n, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count, nb.image_of,
+                                          nb.image_start, reach, rc_lr * rc_lr, pos4, par4, z, q, h, alpha_ref,
                                           c6_ref, table_size, p, e_lr, e_elec, e_disp, dq, dh, f_lr, w_lr);
   SO3_LAUNCH("long_range");
 }

@@ -51,10 +51,11 @@ struct LrDev {
 // Long-range Coulomb + dispersion over the full neighbour set of every atom
 // (cell stencil or image range). Per-atom outputs (N): energy (total, elec,
 // disp), dE/dq, dE/dh, direct force (3), virial (6).
+// pos4 / par4: N-element scratch for the cell-ordered partner data.
 void launch_long_range(int n, const NeighborState &nb, double rc_lr, const int *z, const double *q,
                        const double *h, const double *alpha_ref, const double *c6_ref, int table_size,
-                       LrDev p, double *e_lr, double *e_elec, double *e_disp, double *dq, double *dh,
-                       double *f_lr, double *w_lr, cudaStream_t s);
+                       LrDev p, double4 *pos4, double4 *par4, double *e_lr, double *e_elec, double *e_disp,
+                       double *dq, double *dh, double *f_lr, double *w_lr, cudaStream_t s);
 
 // ---- filters (pair tiles, FP64 tensor cores) --------------------------------
 void launch_filter_forward(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
