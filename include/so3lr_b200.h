@@ -179,6 +179,27 @@ int so3lr_profile_read(so3lr_handle *h, int kernel, double *total_ms, long long 
 /* Total number of CUDA kernels this library has launched in the process. */
 long long so3lr_launch_count(void);
 
+/* Allocation-free long-range step (no counterpart in the reference).
+ * For callers that cannot let a library call cudaMalloc or cudaFree once their
+ * run has started -- e.g. an MD engine that owns all device memory through its
+ * own pool and only hands out the buffers to be filled. Evaluates the
+ * electrostatic + dispersion term of one open-boundary system of at most 16384
+ * atoms from its positions, partial charges, Hirshfeld ratios and atomic numbers,
+ * exactly as the full evaluation does, writing per-atom energy (total,
+ * electrostatic, dispersion), dE/dq, dE/d(ratio), the direct force (3 per atom)
+ * and the per-atom virial (6 per atom, xx yy zz xy xz yz). All pointers are device
+ * memory of the handle's GPU; `stream` (a cudaStream_t, NULL = the handle's
+ * stream) orders the work, which is asynchronous. Larger systems are refused
+ * with an error. The scratch is a fixed file-scope device array (about 1 MiB,
+ * held by every GPU that loads the library until exit); the first call on a
+ * device resolves its address, so make that first call before any stream
+ * capture. Calls share the scratch: calls that overlap on the GPU race and must
+ * be serialised by the caller. */
+int so3lr_long_range_noalloc(so3lr_handle *h, long long natoms, const double *x, const double *q,
+                             const double *ratios, const int *z, double *e_lr, double *e_elec, double *e_disp,
+                             double *dq, double *dh, double *f, double *virial_atom, void *stream, char *err,
+                             size_t errlen);
+
 /* The handle's CUDA stream (cudaStream_t), for callers that time or order work. */
 void *so3lr_stream(so3lr_handle *h);
 

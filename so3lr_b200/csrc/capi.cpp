@@ -269,6 +269,31 @@ int so3lr_profile_read(so3lr_handle *h, int kernel, double *total_ms, long long 
 
 long long so3lr_launch_count(void) { return so3lr_b200::launch_counter(); }
 
+int so3lr_long_range_noalloc(so3lr_handle *h, long long natoms, const double *x, const double *q,
+                             const double *ratios, const int *z, double *e_lr, double *e_elec, double *e_disp,
+                             double *dq, double *dh, double *f, double *virial_atom, void *stream, char *err,
+                             size_t errlen) {
+  if (!h || !x || !q || !ratios || !z || !e_lr || !e_elec || !e_disp || !dq || !dh || !f || !virial_atom)
+    return report_msg("so3lr_long_range_noalloc: NULL argument", err, errlen);
+  try {
+    if (natoms <= 0 || natoms > so3lr_b200::noalloc_max_atoms())
+      throw Error("SO3LR no-alloc long range: natoms = " + std::to_string(natoms) + " is outside 1.." +
+                  std::to_string(so3lr_b200::noalloc_max_atoms()));
+    Evaluator &ev = *h->eval;
+    int previous = 0;
+    SO3_CUDA(cudaGetDevice(&previous));
+    if (previous != ev.device()) SO3_CUDA(cudaSetDevice(ev.device()));
+    const auto t = ev.long_range_tables();
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ev.stream();
+    so3lr_b200::long_range_noalloc(int(natoms), x, q, ratios, z, t.alpha_ref, t.c6_ref, t.table_size, t.params,
+                                   t.cutoff, e_lr, e_elec, e_disp, dq, dh, f, virial_atom, s);
+    if (previous != ev.device()) SO3_CUDA(cudaSetDevice(previous));
+    return 0;
+  } catch (const std::exception &e) {
+    return report(e, err, errlen, h);
+  }
+}
+
 void *so3lr_stream(so3lr_handle *h) { return h ? static_cast<void *>(h->eval->stream()) : nullptr; }
 
 int so3lr_last_stats(const so3lr_handle *h, long long *sr_edges, long long *sr_pairs, long long *device_bytes) {

@@ -96,6 +96,14 @@ class Evaluator {
   const double *forces() const { return force_.get(); }
   const double *energy_device() const { return totals_.get(); }  // [0] energy, [1..6] virial
   StepStats stats() const { return stats_; }
+  // long-range constants and reference tables (device) of the loaded model
+  struct LongRangeTables {
+    LrDev params;
+    const double *alpha_ref, *c6_ref;
+    int table_size;
+    double cutoff;
+  };
+  LongRangeTables long_range_tables() const { return {lr_, alpha_ref_, c6_ref_, ref_table_, lr_cut_}; }
   std::size_t device_bytes() const;
 
   // Optional CUDA-event timing of the pair-filter kernels on stream(): kernel 0 =

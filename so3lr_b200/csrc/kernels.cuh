@@ -57,6 +57,14 @@ void launch_long_range(int n, const NeighborState &nb, double rc_lr, const int *
                        LrDev p, double4 *pos4, double4 *par4, double *e_lr, double *e_elec, double *e_disp,
                        double *dq, double *dh, double *f_lr, double *w_lr, cudaStream_t s);
 
+// Allocation-free variant of the long-range step for open-boundary systems of
+// at most noalloc_max_atoms() atoms (scratch in file-scope device arrays, noalloc.cu).
+int noalloc_max_atoms();
+void long_range_noalloc(int n, const double *x, const double *q, const double *h, const int *z,
+                        const double *alpha_ref, const double *c6_ref, int table_size, const LrDev &p, double rc_lr,
+                        double *e_lr, double *e_elec, double *e_disp, double *dq, double *dh, double *f,
+                        double *w_atom, cudaStream_t s);
+
 // ---- filters (pair tiles, FP64 tensor cores) --------------------------------
 void launch_filter_forward(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
                            const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,

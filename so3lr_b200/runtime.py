@@ -26,7 +26,7 @@ EXPORTED = (
     "so3lr_create", "so3lr_describe", "so3lr_validate_charge_spin", "so3lr_element_from_token",
     "so3lr_inspect_model", "so3lr_compute", "so3lr_compute_device", "so3lr_compute_batch",
     "so3lr_md_init", "so3lr_md_run", "so3lr_md_state", "so3lr_profile", "so3lr_profile_read",
-    "so3lr_launch_count", "so3lr_stream", "so3lr_last_stats", "so3lr_destroy",
+    "so3lr_launch_count", "so3lr_long_range_noalloc", "so3lr_stream", "so3lr_last_stats", "so3lr_destroy",
 )
 
 _dp = C.POINTER(C.c_double)
@@ -95,6 +95,8 @@ def load_library(path: os.PathLike | str | None = None) -> C.CDLL:
     lib.so3lr_profile_read.argtypes = [C.c_void_p, C.c_int, _dp, _lp, _dp, C.c_char_p, C.c_size_t]
     lib.so3lr_launch_count.argtypes = []
     lib.so3lr_launch_count.restype = C.c_longlong
+    lib.so3lr_long_range_noalloc.argtypes = [C.c_void_p, C.c_longlong] + [C.c_void_p] * 11 + [C.c_void_p, C.c_char_p,
+                                                                                              C.c_size_t]
     lib.so3lr_stream.argtypes = [C.c_void_p]
     lib.so3lr_stream.restype = C.c_void_p
     lib.so3lr_last_stats.argtypes = [C.c_void_p, _lp, _lp, _lp]
@@ -262,6 +264,16 @@ class So3lrB200:
         _check(self._lib.so3lr_compute_device(self._h, C.byref(fr), C.c_void_p(f_ptr), None, C.byref(e),
                                               C.cast(vir, _dp), err, 4096), err)
         return e.value, np.array(vir[:])
+
+    def long_range_noalloc(self, natoms: int, x_ptr: int, q_ptr: int, ratio_ptr: int, z_ptr: int, e_lr_ptr: int,
+                           e_elec_ptr: int, e_disp_ptr: int, dq_ptr: int, dh_ptr: int, f_ptr: int, w_ptr: int,
+                           stream: int = 0) -> None:
+        """Allocation-free long-range step on device buffers (see include/so3lr_b200.h)."""
+        err = C.create_string_buffer(1024)
+        ptrs = [C.c_void_p(v) for v in (x_ptr, q_ptr, ratio_ptr, z_ptr, e_lr_ptr, e_elec_ptr, e_disp_ptr, dq_ptr,
+                                        dh_ptr, f_ptr, w_ptr)]
+        _check(self._lib.so3lr_long_range_noalloc(self._h, int(natoms), *ptrs, C.c_void_p(stream or None), err,
+                                                  1024), err)
 
     def md_init(self, x, z, cell, boxlo, v, mass, charge=0.0, multiplicity=1.0):
         fr, x, z = self._frame(x, z, cell, boxlo, charge, multiplicity)
