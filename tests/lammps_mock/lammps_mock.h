@@ -1,0 +1,140 @@
+// Minimal stand-in for the parts of the LAMMPS API a pair style touches
+// (LAMMPS_NS::Pair, Atom, Domain, Force, Comm, Error, Memory, utils::logmesg),
+// so the so3lr/b200 pair style compiles and runs in tests without LAMMPS.
+// Member names and meanings follow LAMMPS; behaviour is reduced to what the
+// style uses. Error::all throws std::runtime_error with the message.
+#pragma once
+#include <cstddef>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#define FLERR __FILE__, __LINE__
+
+namespace LAMMPS_NS {
+
+class LAMMPS;
+
+class Error {
+ public:
+  [[noreturn]] void all(const char *, int, const std::string &msg) { throw std::runtime_error(msg); }
+};
+
+class Memory {
+ public:
+  template <class T>
+  T **create(T **&array, int n1, int n2, const char *) {
+    array = new T *[n1];
+    T *data = new T[static_cast<std::size_t>(n1) * n2]();
+    for (int i = 0; i < n1; ++i) array[i] = data + static_cast<std::size_t>(i) * n2;
+    return array;
+  }
+  template <class T>
+  void destroy(T **&array) {
+    if (!array) return;
+    delete[] array[0];
+    delete[] array;
+    array = nullptr;
+  }
+};
+
+class Atom {
+ public:
+  int ntypes = 0, nlocal = 0;
+  std::vector<int> type_storage;
+  std::vector<double *> x_rows, f_rows;
+  std::vector<double> x_data, f_data;
+  int *type = nullptr;
+  double **x = nullptr, **f = nullptr;
+  void resize(int n) {
+    nlocal = n;
+    type_storage.assign(n, 1);
+    x_data.assign(3 * static_cast<std::size_t>(n), 0.0);
+    f_data.assign(3 * static_cast<std::size_t>(n), 0.0);
+    x_rows.resize(n);
+    f_rows.resize(n);
+    for (int i = 0; i < n; ++i) {
+      x_rows[i] = &x_data[3 * static_cast<std::size_t>(i)];
+      f_rows[i] = &f_data[3 * static_cast<std::size_t>(i)];
+    }
+    type = type_storage.data();
+    x = x_rows.data();
+    f = f_rows.data();
+  }
+};
+
+class Domain {
+ public:
+  int xperiodic = 1, yperiodic = 1, zperiodic = 1, triclinic = 0;
+  double boxlo[3] = {0, 0, 0}, prd[3] = {0, 0, 0};
+};
+
+class Force {
+ public:
+  int newton_pair = 1;
+};
+
+class Comm {
+ public:
+  int me = 0, nprocs = 1;
+};
+
+class LAMMPS {
+ public:
+  Error error;
+  Memory memory;
+  Atom atom;
+  Domain domain;
+  Force force;
+  Comm comm;
+  std::string log;
+};
+
+namespace utils {
+inline void logmesg(LAMMPS *lmp, const std::string &msg) { lmp->log += msg; }
+}  // namespace utils
+
+class Pair {
+ public:
+  explicit Pair(LAMMPS *l)
+      : lmp(l), error(&l->error), memory(&l->memory), atom(&l->atom), domain(&l->domain), force(&l->force),
+        comm(&l->comm) {}
+  virtual ~Pair() { delete[] eatom; }
+  virtual void compute(int, int) = 0;
+  virtual void settings(int, char **) = 0;
+  virtual void coeff(int, char **) = 0;
+  virtual void init_style() {}
+  virtual double init_one(int, int) { return 0.0; }
+
+  LAMMPS *lmp;
+  Error *error;
+  Memory *memory;
+  Atom *atom;
+  Domain *domain;
+  Force *force;
+  Comm *comm;
+  int manybody_flag = 0, one_coeff = 0, restartinfo = 1, single_enable = 1, no_virial_fdotr_compute = 0;
+  int allocated = 0;
+  int **setflag = nullptr;
+  double **cutsq = nullptr;
+  double eng_vdwl = 0.0, virial[6] = {0, 0, 0, 0, 0, 0};
+  double *eatom = nullptr;
+  int eflag_global = 0, eflag_atom = 0, vflag_global = 0, vflag_atom = 0;
+
+  // LAMMPS semantics: eflag bit 1 = global energy, bit 2 = per-atom energy;
+  // vflag bit 1/2 = global virial, bit 4/8 = per-atom virial
+  void ev_init(int eflag, int vflag) {
+    eflag_global = eflag & 1;
+    eflag_atom = (eflag & 2) ? 1 : 0;
+    vflag_global = (vflag & 3) ? 1 : 0;
+    vflag_atom = (vflag & 12) ? 1 : 0;
+    eng_vdwl = 0.0;
+    for (double &v : virial) v = 0.0;
+    if (eflag_atom) {
+      delete[] eatom;
+      eatom = new double[atom->nlocal]();
+    }
+  }
+};
+
+}  // namespace LAMMPS_NS
