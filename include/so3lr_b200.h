@@ -149,6 +149,25 @@ int so3lr_compute(so3lr_handle *h, const so3lr_frame *in, so3lr_result *out, cha
 int so3lr_compute_device(so3lr_handle *h, const so3lr_frame *in_device_x, double *d_f, double *d_eatom,
                          double *energy, double virial[6], char *err, size_t errlen);
 
+/* Multi-GPU spatial decomposition (one process and one handle per GPU; replaces
+ * the MPI exchange plans and halo exchanges of pair_so3lr_native_mpi.cpp:455-930).
+ * Rank 0 makes a 128-byte NCCL unique id with so3lr_nccl_unique_id and the
+ * caller shares it (any transport); every rank then calls so3lr_comm_init on
+ * its own handle. After that, so3lr_compute and so3lr_md_* are collective: every
+ * rank passes the same whole system, the atoms are split into spatial bricks of
+ * the periodic box (1x1x2, 1x2x2, 2x2x2, ... for 2, 4, 8 ranks), each GPU computes
+ * its own atoms, rows owned by other GPUs are refreshed with NCCL all-gathers
+ * (positions, block features, charges and Hirshfeld ratios, block adjoints), and
+ * every rank returns the whole result. Global sums are exact, so energies and
+ * forces are bit-identical for any number of ranks. so3lr_owned_atoms returns
+ * the number of atoms this rank computes (after the first collective call). */
+int so3lr_nccl_unique_id(char out[128], char *err, size_t errlen);
+int so3lr_comm_init(so3lr_handle *h, int nranks, int rank, const char unique_id[128], char *err, size_t errlen);
+int so3lr_owned_atoms(const so3lr_handle *h);
+/* Host-only: the rank that owns each atom under the brick partition above. */
+int so3lr_partition(long long natoms, const double *x, const double boxlo[3], const double boxlen[3], int nranks,
+                    int *owner);
+
 /* Packed turbo evaluation: every image is an independent open-boundary system
  * with its own charge and multiplicity (replaces MpiTurboReplicaBroker::evaluate,
  * KokkosPackedSo3lrEvaluator::launch_device and the per-image charge constraint of

@@ -49,7 +49,7 @@ __device__ inline void store4(double *p, const double (&v)[4]) {
 
 }  // namespace
 
-__global__ void __launch_bounds__(256) k_attention_forward(int n, const int *__restrict__ row_start,
+__global__ void __launch_bounds__(256) k_attention_forward(int n, int row0, const int *__restrict__ row_start,
                                                            const int *__restrict__ nbr,
                                                            const int *__restrict__ edge_pair,
                                                            const double *__restrict__ geo,
@@ -58,9 +58,10 @@ __global__ void __launch_bounds__(256) k_attention_forward(int n, const int *__r
                                                            const double *__restrict__ f_inv,
                                                            const double *__restrict__ f_ev, double norm,
                                                            double *__restrict__ d_inv, double *__restrict__ d_ev) {
-  const int a = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (a >= n) return;
+  if (r >= n) return;
+  const int a = row0 + r;
   const int h = lane >> 3, o = (lane & 7) * 4;
   const size_t head_off = size_t(h) * 160 + o;
   double qa[4], qea[4];
@@ -70,7 +71,7 @@ __global__ void __launch_bounds__(256) k_attention_forward(int n, const int *__r
   double acc_ev = 0.0;
   const int my_deg = lane < kEV ? degree_of_channel(lane) : 0;
   const double my_par = parity_sign(my_deg);
-  for (int e = row_start[a]; e < row_start[a + 1]; ++e) {
+  for (int e = row_start[r]; e < row_start[r + 1]; ++e) {
     const int b = nbr[e];
     const int code = edge_pair[e];
     const int p = code >= 0 ? code : ~code;
@@ -107,8 +108,8 @@ void launch_attention_forward(int n, const NeighborState &nb, const double *geo,
                               const double *qkv, const double *f_inv, const double *f_ev, double norm,
                               double *d_inv, double *d_ev, cudaStream_t s) {
   if (n == 0) return;
-  k_attention_forward<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, nb.row_start, nb.nbr, nb.edge_pair, geo, sh, qkv,
-                                                           f_inv, f_ev, norm, d_inv, d_ev);
+  k_attention_forward<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.edge_pair, geo, sh,
+                                                           qkv, f_inv, f_ev, norm, d_inv, d_ev);
   SO3_LAUNCH("attention_forward");
 }
 
@@ -116,14 +117,15 @@ void launch_attention_forward(int n, const NeighborState &nb, const double *geo,
 // produce dL/d{q,k,v,q_ev,k_ev} per atom and, for the primary edge of every pair,
 // the scalars the filter reverse needs.
 __global__ void __launch_bounds__(256) k_attention_reverse(
-    int n, const int *__restrict__ row_start, const int *__restrict__ nbr, const int *__restrict__ edge_pair,
+    int n, int row0, const int *__restrict__ row_start, const int *__restrict__ nbr, const int *__restrict__ edge_pair,
     const double *__restrict__ geo, const double *__restrict__ sh, const double *__restrict__ qkv,
     const double *__restrict__ f_inv, const double *__restrict__ f_ev, const double *__restrict__ g_a,
     const double *__restrict__ g_A, double norm, double *__restrict__ g_qkv, double *__restrict__ pair_sc,
     double *__restrict__ g_filt_inv, double *__restrict__ g_filt_ev) {
-  const int a = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (a >= n) return;
+  if (r >= n) return;
+  const int a = row0 + r;
   const int h = lane >> 3, o = (lane & 7) * 4;
   const size_t head_off = size_t(h) * 160 + o;
   const double *qa_row = qkv + (size_t)a * kQKV + head_off;
@@ -140,7 +142,7 @@ __global__ void __launch_bounds__(256) k_attention_reverse(
   double gq[4] = {0, 0, 0, 0}, gk[4] = {0, 0, 0, 0}, gv[4] = {0, 0, 0, 0}, gqe[4] = {0, 0, 0, 0},
          gke[4] = {0, 0, 0, 0};
   const double inv_norm = 1.0 / norm;
-  for (int e = row_start[a]; e < row_start[a + 1]; ++e) {
+  for (int e = row_start[r]; e < row_start[r + 1]; ++e) {
     const int b = nbr[e];
     const int code = edge_pair[e];
     const int p = code >= 0 ? code : ~code;
@@ -194,10 +196,13 @@ __global__ void __launch_bounds__(256) k_attention_reverse(
       // primary edge: the filter gradient of the pair, both directions summed
       //   g_f_inv[c] = phi/norm (s_in[h] q_a[c] k_b[c] + s_out[h] q_b[c] k_a[c]), same for ev
       double gi[4], ge[4];
+      // explicitly rounded products and sum (no FMA contraction): the two
+      // directions' terms swap when the pair is held from its other endpoint,
+      // and a rounded sum is exactly commutative
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        gi[j] = c_q * (qa[j] * kb[j]) + c_k * (qb[j] * ka[j]);
-        ge[j] = c_qe * (qea[j] * keb[j]) + c_ke * (qeb[j] * kea[j]);
+        gi[j] = __dadd_rn(__dmul_rn(c_q, __dmul_rn(qa[j], kb[j])), __dmul_rn(c_k, __dmul_rn(qb[j], ka[j])));
+        ge[j] = __dadd_rn(__dmul_rn(c_qe, __dmul_rn(qea[j], keb[j])), __dmul_rn(c_ke, __dmul_rn(qeb[j], kea[j])));
       }
       store4(g_filt_inv + (size_t)p * kF + lane * 4, gi);
       store4(g_filt_ev + (size_t)p * kF + lane * 4, ge);
@@ -241,25 +246,26 @@ void launch_attention_reverse(int n, const NeighborState &nb, const double *geo,
                               const double *g_A, double norm, double *g_qkv, double *pair_sc, double *g_filt_inv,
                               double *g_filt_ev, cudaStream_t s) {
   if (n == 0) return;
-  k_attention_reverse<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, nb.row_start, nb.nbr, nb.edge_pair, geo, sh, qkv,
-                                                           f_inv, f_ev, g_a, g_A, norm, g_qkv, pair_sc, g_filt_inv,
-                                                           g_filt_ev);
+  k_attention_reverse<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.edge_pair, geo, sh,
+                                                           qkv, f_inv, f_ev, g_a, g_A, norm, g_qkv, pair_sc,
+                                                           g_filt_inv, g_filt_ev);
   SO3_LAUNCH("attention_reverse");
 }
 
 // g_ev[a][m] = g_A[a][m] + sum over a's pairs of 2 (ev_a - ev_b)[m] cg[m] gl0[p][deg m]
-__global__ void k_ev_l0_reverse(int n, const int *__restrict__ row_start, const int *__restrict__ nbr,
+__global__ void k_ev_l0_reverse(int n, int row0, const int *__restrict__ row_start, const int *__restrict__ nbr,
                                 const int *__restrict__ edge_pair, const double *__restrict__ ev,
                                 const double *__restrict__ cg, const double *__restrict__ gl0,
                                 const double *__restrict__ g_A, double *__restrict__ g_ev) {
-  const int a = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (a >= n || lane >= kEV) return;
+  if (r >= n || lane >= kEV) return;
+  const int a = row0 + r;
   const int d = degree_of_channel(lane);
   const double eva = ev[(size_t)a * kEV + lane];
   const double c = 2.0 * cg[lane];
   double acc = 0.0;
-  for (int e = row_start[a]; e < row_start[a + 1]; ++e) {
+  for (int e = row_start[r]; e < row_start[r + 1]; ++e) {
     const int b = nbr[e];
     const int code = edge_pair[e];
     const int p = code >= 0 ? code : ~code;
@@ -271,8 +277,8 @@ __global__ void k_ev_l0_reverse(int n, const int *__restrict__ row_start, const 
 void launch_ev_l0_reverse(int n, const NeighborState &nb, const double *ev, const double *cg_att,
                           const double *gl0, const double *g_A, double *g_ev, cudaStream_t s) {
   if (n == 0) return;
-  k_ev_l0_reverse<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, nb.row_start, nb.nbr, nb.edge_pair, ev, cg_att, gl0, g_A,
-                                                       g_ev);
+  k_ev_l0_reverse<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.edge_pair, ev, cg_att,
+                                                       gl0, g_A, g_ev);
   SO3_LAUNCH("ev_l0_reverse");
 }
 

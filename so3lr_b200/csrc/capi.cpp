@@ -9,6 +9,8 @@
 #include <memory>
 #include <string>
 
+#include <nccl.h>
+
 #include "evaluator.hpp"
 
 using so3lr_b200::Error;
@@ -70,8 +72,8 @@ bool same_system(const SystemSpec &a, const SystemSpec &b) {
   return true;
 }
 
-void ensure_prepared(Evaluator &ev, const SystemSpec &spec) {
-  if (ev.spec().n == 0 || !same_system(ev.spec(), spec)) ev.prepare(spec);
+void ensure_prepared(Evaluator &ev, const SystemSpec &spec, const double *host_x) {
+  if (ev.spec().n == 0 || !same_system(ev.spec(), spec)) ev.prepare(spec, host_x);
 }
 
 }  // namespace
@@ -145,7 +147,7 @@ int so3lr_compute(so3lr_handle *h, const so3lr_frame *in, so3lr_result *out, cha
   if (!h || !in || !out) return report_msg("so3lr_compute: NULL argument", err, errlen);
   try {
     Evaluator &ev = *h->eval;
-    ensure_prepared(ev, spec_from_frame(*in));
+    ensure_prepared(ev, spec_from_frame(*in), in->x);
     ev.upload_positions(in->x);
     ev.compute();
     const auto r = ev.download(out->f, out->eatom, out->charges, out->ratios, out->e_learned, out->e_zbl, out->e_lr,
@@ -163,7 +165,8 @@ int so3lr_compute_device(so3lr_handle *h, const so3lr_frame *in, double *d_f, do
   if (!h || !in || !d_f) return report_msg("so3lr_compute_device: NULL argument", err, errlen);
   try {
     Evaluator &ev = *h->eval;
-    ensure_prepared(ev, spec_from_frame(*in));
+    if (ev.nranks() > 1) throw Error("so3lr_compute_device: not available on a multi-GPU handle");
+    ensure_prepared(ev, spec_from_frame(*in), nullptr);
     const std::size_t n = std::size_t(in->natoms);
     SO3_CUDA(cudaSetDevice(ev.device()));
     SO3_CUDA(cudaMemcpyAsync(ev.positions(), in->x, sizeof(double) * 3 * n, cudaMemcpyDeviceToDevice, ev.stream()));
@@ -202,7 +205,8 @@ int so3lr_compute_batch(so3lr_handle *h, const so3lr_batch *in, so3lr_batch_resu
     s.image_charge.assign(in->image_charge, in->image_charge + in->nimages);
     s.image_mult.assign(in->image_multiplicity, in->image_multiplicity + in->nimages);
     Evaluator &ev = *h->eval;
-    ensure_prepared(ev, s);
+    if (ev.nranks() > 1) throw Error("so3lr_compute_batch: turbo packs run one handle per GPU, without a communicator");
+    ensure_prepared(ev, s, in->x);
     ev.upload_positions(in->x);
     ev.compute();
     ev.download(out->f, out->eatom, out->charges, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
@@ -218,7 +222,7 @@ int so3lr_md_init(so3lr_handle *h, const so3lr_frame *in, const double *v, const
   if (!h || !in || !v || !mass) return report_msg("so3lr_md_init: NULL argument", err, errlen);
   try {
     Evaluator &ev = *h->eval;
-    ensure_prepared(ev, spec_from_frame(*in));
+    ensure_prepared(ev, spec_from_frame(*in), in->x);
     ev.upload_positions(in->x);
     ev.md_setup(v, mass);
     return 0;
@@ -248,6 +252,44 @@ int so3lr_md_state(so3lr_handle *h, double *x, double *v, double *f, double *ene
   } catch (const std::exception &e) {
     return report(e, err, errlen, h);
   }
+}
+
+int so3lr_nccl_unique_id(char out[128], char *err, size_t errlen) {
+  if (!out) return report_msg("so3lr_nccl_unique_id: NULL argument", err, errlen);
+  static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+  ncclUniqueId id;
+  const ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess) return report_msg(ncclGetErrorString(r), err, errlen);
+  std::memcpy(out, &id, sizeof(id));
+  return 0;
+}
+
+int so3lr_comm_init(so3lr_handle *h, int nranks, int rank, const char unique_id[128], char *err, size_t errlen) {
+  if (!h || (nranks > 1 && !unique_id)) return report_msg("so3lr_comm_init: NULL argument", err, errlen);
+  try {
+    h->eval->set_comm(nranks, rank, unique_id);
+    return 0;
+  } catch (const std::exception &e) {
+    return report(e, err, errlen, h);
+  }
+}
+
+int so3lr_owned_atoms(const so3lr_handle *h) { return h ? h->eval->owned_atoms() : -1; }
+
+int so3lr_partition(long long natoms, const double *x, const double boxlo[3], const double boxlen[3], int nranks,
+                    int *owner) {
+  if (natoms <= 0 || !x || !boxlo || !boxlen || nranks < 1 || !owner) return 2;
+  SystemSpec s;
+  s.n = int(natoms);
+  s.periodic = true;
+  for (int d = 0; d < 3; ++d) {
+    s.lo[d] = boxlo[d];
+    s.len[d] = boxlen[d];
+    if (!(s.len[d] > 0)) return 2;
+  }
+  const auto o = so3lr_b200::partition_atoms(s, x, nranks);
+  for (long long i = 0; i < natoms; ++i) owner[i] = o[std::size_t(i)];
+  return 0;
 }
 
 int so3lr_profile(so3lr_handle *h, int enable) {

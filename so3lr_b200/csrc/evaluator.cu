@@ -1,5 +1,7 @@
 #include "evaluator.hpp"
 
+#include <nccl.h>
+
 #include <cmath>
 #include <cstring>
 #include <numeric>
@@ -26,6 +28,7 @@ Evaluator::~Evaluator() {
   if (stream_) {
     cudaSetDevice(device_);
     cudaStreamSynchronize(stream_);
+    if (comm_) ncclCommDestroy(comm_);
     for (auto &p : prof_)
       for (auto ev : p.events) cudaEventDestroy(ev);
     cudaStreamDestroy(stream_);
@@ -206,7 +209,91 @@ void Evaluator::upload_weights() {
 // ---------------------------------------------------------------------------
 // system preparation
 // ---------------------------------------------------------------------------
-void Evaluator::prepare(const SystemSpec &spec_in) {
+// ---------------------------------------------------------------------------
+// multi-GPU
+// ---------------------------------------------------------------------------
+void Evaluator::set_comm(int nranks, int rank, const void *unique_id) {
+  if (nranks < 1 || rank < 0 || rank >= nranks) throw Error("SO3LR: invalid rank / rank count");
+  SO3_CUDA(cudaSetDevice(device_));
+  if (comm_) {
+    ncclCommDestroy(comm_);
+    comm_ = nullptr;
+  }
+  nranks_ = nranks;
+  rank_ = rank;
+  spec_ = SystemSpec();  // force a new partition on the next prepare
+  if (nranks == 1) return;
+  ncclUniqueId id;
+  std::memcpy(&id, unique_id, sizeof(id));
+  const ncclResult_t r = ncclCommInitRank(&comm_, nranks, id, rank);
+  if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclCommInitRank failed: ") + ncclGetErrorString(r));
+}
+
+void Evaluator::allgather_rows(double *a, int width) {
+  if (nranks_ == 1) return;
+  const std::size_t count = std::size_t(stride_) * width;
+  const ncclResult_t r = ncclAllGather(a + std::size_t(rank_) * count, a, count, ncclDouble, comm_, stream_);
+  if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclAllGather failed: ") + ncclGetErrorString(r));
+}
+
+// exact sums over segments of the owned rows (global over ranks when decomposed);
+// seg: device [nseg + 1] row offsets; out: device [nseg * ncol]
+void Evaluator::exact_sums(const double *v, int stride, int ncol, int nseg, const int *seg, double *out) {
+  const int count = nseg * ncol;
+  long long *local = parts_.reserve(std::size_t(count) * 2 * (nranks_ + 1));
+  long long *all = local + std::size_t(count) * 2;
+  launch_fixed_segment_sum(nseg, seg, v, stride, ncol, local, stream_);
+  if (nranks_ > 1) {
+    const ncclResult_t r = ncclAllGather(local, all, std::size_t(count) * 2, ncclInt64, comm_, stream_);
+    if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclAllGather failed: ") + ncclGetErrorString(r));
+    launch_fixed_finish(all, nranks_, count, out, stream_);
+  } else {
+    launch_fixed_finish(local, 1, count, out, stream_);
+  }
+}
+
+// brick index of a position (the same arithmetic on every rank)
+static int brick_of(const double *x, const SystemSpec &s, const int dims[3]) {
+  int idx[3];
+  for (int d = 0; d < 3; ++d) {
+    double p = x[d] - s.lo[d];
+    p -= std::floor(p / s.len[d]) * s.len[d];
+    int c = int(p * dims[d] / s.len[d]);
+    idx[d] = c < 0 ? 0 : (c >= dims[d] ? dims[d] - 1 : c);
+  }
+  return (idx[2] * dims[1] + idx[1]) * dims[0] + idx[0];
+}
+
+void brick_dims(int nranks, int dims[3]) {
+  dims[0] = dims[1] = dims[2] = 1;
+  int rest = nranks;
+  for (int f = 2; rest > 1;) {
+    if (rest % f == 0) {
+      // give the factor to the dimension with the fewest bricks, z first
+      int k = 2;
+      if (dims[1] < dims[k]) k = 1;
+      if (dims[0] < dims[k]) k = 0;
+      dims[k] *= f;
+      rest /= f;
+    } else {
+      ++f;
+    }
+  }
+}
+
+std::vector<int> partition_atoms(const SystemSpec &s, const double *x, int nranks) {
+  std::vector<int> owner(std::size_t(s.n), 0);
+  if (nranks == 1) return owner;
+  int dims[3];
+  brick_dims(nranks, dims);
+  for (int i = 0; i < s.n; ++i) owner[std::size_t(i)] = brick_of(x + 3 * std::size_t(i), s, dims);
+  return owner;
+}
+
+// ---------------------------------------------------------------------------
+// system preparation
+// ---------------------------------------------------------------------------
+void Evaluator::prepare(const SystemSpec &spec_in, const double *host_x) {
   SO3_CUDA(cudaSetDevice(device_));
   SystemSpec spec = spec_in;
   const int n = spec.n;
@@ -231,6 +318,10 @@ void Evaluator::prepare(const SystemSpec &spec_in) {
     for (int i = 0; i < nimg; ++i)
       if (spec.image_start[i + 1] - spec.image_start[i] > 20000)
         throw Error("SO3LR: open-boundary images are limited to 20000 atoms; use a periodic box with vacuum");
+  }
+  if (nranks_ > 1) {
+    if (!spec.periodic) throw Error("SO3LR: multi-GPU decomposition needs a periodic box");
+    if (host_x == nullptr) throw Error("SO3LR: multi-GPU decomposition needs positions to partition");
   }
 
   // charge / spin tables, cached by (composition, Q, M)
@@ -264,19 +355,55 @@ void Evaluator::prepare(const SystemSpec &spec_in) {
     for (int i = spec.image_start[im]; i < spec.image_start[im + 1]; ++i) table_of_atom[i] = tab;
     any_charge_spin_ = true;
   }
+
+  // row layout: rank-major bricks of `stride` rows; input atom i -> row_of_[i]
+  const std::vector<int> owner = partition_atoms(spec, host_x, nranks_);
+  std::vector<int> per_rank(nranks_, 0);
+  for (int i = 0; i < n; ++i) per_rank[owner[i]]++;
+  stride_ = nranks_ == 1 ? n : *std::max_element(per_rank.begin(), per_rank.end());
+  if (stride_ == 0) stride_ = 1;
+  n_rows_ = nranks_ * stride_;
+  row0_ = rank_ * stride_;
+  n_own_ = per_rank[rank_];
+  identity_ = nranks_ == 1;
+  row_of_.assign(n, 0);
+  tag_of_row_.assign(n_rows_, -1);
+  {
+    std::vector<int> fill(nranks_, 0);
+    for (int i = 0; i < n; ++i) {
+      const int row = owner[i] * stride_ + fill[owner[i]]++;
+      row_of_[i] = row;
+      tag_of_row_[row] = i;
+    }
+  }
+  std::vector<int> z_rows(n_rows_, 1), image_rows(n_rows_, 0), table_rows(n_rows_, -1);
+  for (int i = 0; i < n; ++i) {
+    z_rows[row_of_[i]] = spec.z[i];
+    image_rows[row_of_[i]] = image_of[i];
+    table_rows[row_of_[i]] = table_of_atom[i];
+  }
   spec_ = spec;
   alloc_atoms();
-  SO3_CUDA(cudaMemcpyAsync(z_.reserve(n), spec.z.data(), sizeof(int) * n, cudaMemcpyHostToDevice, stream_));
-  SO3_CUDA(cudaMemcpyAsync(image_of_.reserve(n), image_of.data(), sizeof(int) * n, cudaMemcpyHostToDevice, stream_));
+  const int nr = n_rows_;
+  SO3_CUDA(cudaMemcpyAsync(z_.reserve(nr), z_rows.data(), sizeof(int) * nr, cudaMemcpyHostToDevice, stream_));
+  SO3_CUDA(cudaMemcpyAsync(image_of_.reserve(nr), image_rows.data(), sizeof(int) * nr, cudaMemcpyHostToDevice, stream_));
+  SO3_CUDA(cudaMemcpyAsync(table_of_atom_.reserve(nr), table_rows.data(), sizeof(int) * nr, cudaMemcpyHostToDevice,
+                           stream_));
+  SO3_CUDA(cudaMemcpyAsync(tag_.reserve(nr), tag_of_row_.data(), sizeof(int) * nr, cudaMemcpyHostToDevice, stream_));
   SO3_CUDA(cudaMemcpyAsync(image_start_.reserve(nimg + 1), spec.image_start.data(), sizeof(int) * (nimg + 1),
                            cudaMemcpyHostToDevice, stream_));
   SO3_CUDA(cudaMemcpyAsync(image_charge_.reserve(nimg), spec.image_charge.data(), sizeof(double) * nimg,
                            cudaMemcpyHostToDevice, stream_));
-  SO3_CUDA(cudaMemcpyAsync(table_of_atom_.reserve(n), table_of_atom.data(), sizeof(int) * n, cudaMemcpyHostToDevice,
-                           stream_));
   if (any_charge_spin_) {
     SO3_CUDA(cudaMemcpyAsync(cs_tables_.reserve(tables.size()), tables.data(), sizeof(double) * tables.size(),
                              cudaMemcpyHostToDevice, stream_));
+  }
+  // segments: [0..1] owned rows, [2..3] image count of the (single, global) image,
+  // [4..5] image-energy segment over images
+  {
+    const int seg[6] = {row0_, row0_ + n_own_, 0, n, 0, nimg};
+    std::memcpy(host_seg_, seg, sizeof(seg));
+    SO3_CUDA(cudaMemcpyAsync(seg_.reserve(8), host_seg_, sizeof(seg), cudaMemcpyHostToDevice, stream_));
   }
   // cell grid: cells no smaller than the short-range cutoff
   CellGrid g;
@@ -289,28 +416,27 @@ void Evaluator::prepare(const SystemSpec &spec_in) {
   const long long ncells = (long long)g.ncell[0] * g.ncell[1] * g.ncell[2];
   if (ncells > (1 << 26)) throw Error("SO3LR: periodic box is too large for the cell grid");
   nb_.grid = g;
-  nb_.xw = xw_.reserve(3 * std::size_t(n));
-  nb_.cell = cell_.reserve(n);
+  nb_.tag = identity_ ? nullptr : tag_.get();
+  nb_.row0 = row0_;
+  nb_.n_own = n_own_;
+  nb_.xw = xw_.reserve(3 * std::size_t(nr));
+  nb_.cell = cell_.reserve(nr);
   nb_.cell_count = cell_count_.reserve(ncells);
   nb_.cell_start = cell_start_.reserve(ncells + 1);
   nb_.cell_fill = cell_fill_.reserve(ncells);
-  nb_.cell_atoms = cell_atoms_.reserve(n);
+  nb_.cell_atoms = cell_atoms_.reserve(nr);
   nb_.image_of = image_of_.get();
   nb_.image_start = image_start_.get();
-  nb_.deg = deg_.reserve(n);
-  nb_.row_start = row_start_.reserve(n + 1);
-  nb_.scan_scratch = scan_scratch_.reserve(scan_scratch_ints(std::max<long long>(ncells, 64LL * n)));
+  nb_.deg = deg_.reserve(nr);
+  nb_.row_start = row_start_.reserve(nr + 1);
+  nb_.scan_scratch = scan_scratch_.reserve(scan_scratch_ints(std::max<long long>(ncells, 64LL * nr)));
   nb_.scan_total = small_ints_.reserve(16);
   nb_.error_flag = nb_.scan_total + 4;
-  {
-    const int seg[4] = {0, nimg, 0, n};  // [6..7]: image-energy segment, [8..9]: atom segment
-    SO3_CUDA(cudaMemcpyAsync(nb_.scan_total + 6, seg, sizeof(seg), cudaMemcpyHostToDevice, stream_));
-  }
   SO3_CUDA(cudaStreamSynchronize(stream_));
 }
 
 void Evaluator::alloc_atoms() {
-  const std::size_t n = std::size_t(spec_.n);
+  const std::size_t n = std::size_t(n_rows_);
   const int nimg = int(spec_.image_start.size()) - 1;
   auto ensure_vec = [&](std::vector<std::unique_ptr<DeviceArray<double>>> &v, int count, std::size_t elems) {
     while (int(v.size()) < count) v.emplace_back(new DeviceArray<double>());
@@ -369,11 +495,20 @@ void Evaluator::alloc_atoms() {
   w_atom_.reserve(6 * n);
   totals_.reserve(8);
   image_energy_.reserve(nimg);
+  stage_.resize(n * 6);
 }
 
 void Evaluator::upload_positions(const double *host_x) {
   SO3_CUDA(cudaSetDevice(device_));
-  SO3_CUDA(cudaMemcpyAsync(x_.get(), host_x, sizeof(double) * 3 * spec_.n, cudaMemcpyHostToDevice, stream_));
+  if (identity_) {
+    SO3_CUDA(cudaMemcpyAsync(x_.get(), host_x, sizeof(double) * 3 * spec_.n, cudaMemcpyHostToDevice, stream_));
+    return;
+  }
+  std::fill(stage_.begin(), stage_.begin() + 3 * std::size_t(n_rows_), 0.0);
+  for (int i = 0; i < spec_.n; ++i)
+    for (int d = 0; d < 3; ++d) stage_[3 * std::size_t(row_of_[i]) + d] = host_x[3 * std::size_t(i) + d];
+  SO3_CUDA(cudaMemcpyAsync(x_.get(), stage_.data(), sizeof(double) * 3 * n_rows_, cudaMemcpyHostToDevice, stream_));
+  SO3_CUDA(cudaStreamSynchronize(stream_));  // stage_ is reused
 }
 
 std::size_t Evaluator::device_bytes() const {
@@ -431,33 +566,35 @@ void Evaluator::read_profile(int k, double *ms, long long *launches, double *flo
 // neighbour lists
 // ---------------------------------------------------------------------------
 void Evaluator::build_neighbors() {
-  const int n = spec_.n;
-  build_cells(nb_, n, x_.get(), stream_);
-  count_sr(nb_, n, sr_cut_, stream_);
-  SO3_CUDA(cudaMemcpyAsync(host_small_, nb_.row_start + n, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+  build_cells(nb_, n_rows_, x_.get(), stream_);
+  count_sr(nb_, sr_cut_, stream_);
+  SO3_CUDA(cudaMemcpyAsync(host_small_, nb_.row_start + n_own_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
   SO3_CUDA(cudaStreamSynchronize(stream_));
   const int E = host_small_[0];
   if (E < 0) throw Error("SO3LR: edge count overflow");
-  if (E % 2 != 0) throw Error("SO3LR: short-range list is not symmetric");
-  const int P = E / 2;
   stats_.edges = E;
-  stats_.pairs = P;
   nb_.nbr = nbr_.reserve(E, 1.25);
   nb_.img = img_.reserve(E, 1.25);
   nb_.primary = primary_.reserve(E, 1.25);
   nb_.rev = rev_.reserve(E, 1.25);
   nb_.pair_scan = pair_scan_.reserve(E, 1.25);
   nb_.edge_pair = edge_pair_.reserve(E, 1.25);
-  nb_.pair_a = pair_a_.reserve(P, 1.25);
-  nb_.pair_b = pair_b_.reserve(P, 1.25);
-  nb_.pair_img = pair_img_.reserve(P, 1.25);
-  nb_.pair_edge = pair_edge_.reserve(P, 1.25);
   if (scan_scratch_.capacity() < scan_scratch_ints(std::size_t(E) + 1)) {
     nb_.scan_scratch = scan_scratch_.reserve(scan_scratch_ints(std::size_t(E) * 2 + 1));
   }
   SO3_CUDA(cudaMemsetAsync(nb_.error_flag, 0, sizeof(int), stream_));
-  fill_sr(nb_, n, sr_cut_, E, stream_);
-  fill_pairs(nb_, n, E, stream_);
+  fill_sr(nb_, sr_cut_, E, stream_);
+  SO3_CUDA(cudaMemcpyAsync(host_small_ + 1, nb_.scan_total, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+  SO3_CUDA(cudaStreamSynchronize(stream_));
+  const int P = host_small_[1];
+  if (identity_ && 2 * P != E) throw Error("SO3LR: short-range list is not symmetric");
+  stats_.pairs = P;
+  nb_.pair_a = pair_a_.reserve(P, 1.25);
+  nb_.pair_b = pair_b_.reserve(P, 1.25);
+  nb_.pair_img = pair_img_.reserve(P, 1.25);
+  nb_.pair_edge = pair_edge_.reserve(P, 1.25);
+  nb_.pair_canon = pair_canon_.reserve(P, 1.25);
+  fill_pairs(nb_, E, stream_);
   // per-pair storage
   geo_.reserve(std::size_t(P) * kGeo, 1.25);
   sh_.reserve(std::size_t(P) * kEV, 1.25);
@@ -478,18 +615,28 @@ void Evaluator::build_neighbors() {
 
 // ---------------------------------------------------------------------------
 // the evaluation
+//
+// Rows [row0, row0 + n_own) are this GPU's atoms; every other row is a copy of
+// another GPU's atom, refreshed by an all-gather right after its owner
+// computed it. Everything an owned atom sums over (its CSR row, its cell
+// stencil) is complete locally, so no partial sum ever crosses GPUs; the only
+// global sums (charge, charge seeds, energy, virial) are exact.
 // ---------------------------------------------------------------------------
 void Evaluator::compute() {
   SO3_CUDA(cudaSetDevice(device_));
-  const int n = spec_.n;
+  const int N = n_rows_;          // all rows
+  const int n = n_own_;           // owned rows
+  const std::size_t r0 = std::size_t(row0_);
   const int nimg = int(spec_.image_start.size()) - 1;
   cudaStream_t s = stream_;
+  const int *own_seg = seg_.get();
+  const int *count_seg = identity_ ? image_start_.get() : seg_.get() + 2;
   build_neighbors();
   const int P = int(stats_.pairs);
   launch_pair_geometry(P, nb_, z_.get(), zbl_, sr_cut_, geo_.get(), sh_.get(), gv_.get(), s);
-  launch_embedding(n, z_.get(), emb_w_, any_charge_spin_ ? cs_tables_.get() : nullptr, table_of_atom_.get(),
+  launch_embedding(N, z_.get(), emb_w_, any_charge_spin_ ? cs_tables_.get() : nullptr, table_of_atom_.get(),
                    inv_emb_scale_, xb_[0]->get(), s);
-  SO3_CUDA(cudaMemsetAsync(evb_[0]->get(), 0, sizeof(double) * n * kEV, s));
+  SO3_CUDA(cudaMemsetAsync(evb_[0]->get(), 0, sizeof(double) * N * kEV, s));
 
   for (int b = 0; b < layers_; ++b) {
     const BlockW &w = blocks_[b];
@@ -497,9 +644,9 @@ void Evaluator::compute() {
     launch_filter_forward(P, geo_.get(), nb_.pair_a, nb_.pair_b, b == 0 ? nullptr : evb_[b]->get(), w.cg_att, w.finv,
                           w.fev, rad_, f_inv_[b]->get(), f_ev_[b]->get(), s);
     prof_end(0, kFilterFlopsPerPair * double(P));
-    {  // per-head projections: qkv[n][h][5][32] = x[n][h*32:(h+1)*32] W_h
+    {  // per-head projections for every row: qkv[n][h][5][32] = x[n][h*32:(h+1)*32] W_h
       GemmArgs g{};
-      g.M = n; g.N = 160; g.K = 32;
+      g.M = N; g.N = 160; g.K = 32;
       g.A = xb_[b]->get(); g.lda = kF; g.strideA = 32;
       g.W = w.qkv_fwd; g.ldw = 32; g.transB = true; g.strideW = 160 * 32;
       g.C = qkv_[b]->get(); g.ldc = kQKV; g.strideC = 160;
@@ -508,116 +655,140 @@ void Evaluator::compute() {
     }
     launch_attention_forward(n, nb_, geo_.get(), sh_.get(), qkv_[b]->get(), f_inv_[b]->get(), f_ev_[b]->get(), norm_,
                              d_inv_.get(), d_ev_.get(), s);
-    launch_post_attn_pre(n, xb_[b]->get(), d_inv_.get(), evb_[b]->get(), d_ev_.get(), w.ln1w, w.ln1b, w.cg_int,
-                         xhat1_[b]->get(), rstd1_[b]->get(), n1_[b]->get(), act_.get(), A_[b]->get(), cat_.get(), s);
+    launch_post_attn_pre(n, xb_[b]->get() + r0 * kF, d_inv_.get() + r0 * kF, evb_[b]->get() + r0 * kEV,
+                         d_ev_.get() + r0 * kEV, w.ln1w, w.ln1b, w.cg_int, xhat1_[b]->get() + r0 * kF,
+                         rstd1_[b]->get() + r0, n1_[b]->get() + r0 * kF, act_.get() + r0 * kF,
+                         A_[b]->get() + r0 * kEV, cat_.get() + r0 * kIntW, s);
     {  // hidden = silu(act W1^T + b1), pre-activation kept for the reverse
       GemmArgs g{};
       g.M = n; g.N = kF; g.K = kF;
-      g.A = act_.get(); g.lda = kF;
+      g.A = act_.get() + r0 * kF; g.lda = kF;
       g.W = w.mlp1w; g.ldw = kF; g.transB = true;
-      g.C = d_inv_.get(); g.ldc = kF;  // reuse d_inv as the hidden activation
-      g.bias = w.mlp1b; g.aux_out = hp_[b]->get(); g.ldaux = kF;
+      g.C = d_inv_.get() + r0 * kF; g.ldc = kF;  // reuse d_inv as the hidden activation
+      g.bias = w.mlp1b; g.aux_out = hp_[b]->get() + r0 * kF; g.ldaux = kF;
       g.epi = Epi::BiasStorePre;
       launch_gemm(g, s);
     }
     {  // post = n1 + hidden W2^T + b2  -> cat[:, :128]
       GemmArgs g{};
       g.M = n; g.N = kF; g.K = kF;
-      g.A = d_inv_.get(); g.lda = kF;
+      g.A = d_inv_.get() + r0 * kF; g.lda = kF;
       g.W = w.mlp2w; g.ldw = kF; g.transB = true;
-      g.C = cat_.get(); g.ldc = kIntW;
-      g.bias = w.mlp2b; g.aux = n1_[b]->get(); g.ldaux = kF;
+      g.C = cat_.get() + r0 * kIntW; g.ldc = kIntW;
+      g.bias = w.mlp2b; g.aux = n1_[b]->get() + r0 * kF; g.ldaux = kF;
       g.epi = Epi::BiasResidual;
       launch_gemm(g, s);
     }
     {  // t = [post, L0'] W_int^T + b_int
       GemmArgs g{};
       g.M = n; g.N = kIntW; g.K = kIntW;
-      g.A = cat_.get(); g.lda = kIntW;
+      g.A = cat_.get() + r0 * kIntW; g.lda = kIntW;
       g.W = w.intw; g.ldw = kIntW; g.transB = true;
-      g.C = t_.get(); g.ldc = kIntW;
+      g.C = t_.get() + r0 * kIntW; g.ldc = kIntW;
       g.bias = w.intb;
       g.epi = Epi::Bias;
       launch_gemm(g, s);
     }
-    launch_post_attn_final(n, cat_.get(), t_.get(), A_[b]->get(), w.ln2w, w.ln2b, xhat2_[b]->get(), rstd2_[b]->get(),
-                           gate_[b]->get(), xb_[b + 1]->get(), evb_[b + 1]->get(), s);
+    launch_post_attn_final(n, cat_.get() + r0 * kIntW, t_.get() + r0 * kIntW, A_[b]->get() + r0 * kEV, w.ln2w,
+                           w.ln2b, xhat2_[b]->get() + r0 * kF, rstd2_[b]->get() + r0, gate_[b]->get() + r0 * 4,
+                           xb_[b + 1]->get() + r0 * kF, evb_[b + 1]->get() + r0 * kEV, s);
+    if (b + 1 < layers_) {  // other GPUs' rows of the next block's input
+      allgather_rows(xb_[b + 1]->get(), kF);
+      allgather_rows(evb_[b + 1]->get(), kEV);
+    }
   }
 
-  // ---- output heads --------------------------------------------------------
+  // ---- output heads (owned rows) --------------------------------------------
   {
     GemmArgs g{};
     g.M = n; g.N = kHeadCat; g.K = kF;
-    g.A = xb_[layers_]->get(); g.lda = kF;
+    g.A = xb_[layers_]->get() + r0 * kF; g.lda = kF;
     g.W = heads_.w1cat; g.ldw = kF; g.transB = true;
-    g.C = hcat_.get(); g.ldc = kHeadCat;
-    g.bias = heads_.b1cat; g.aux_out = hpre_.get(); g.ldaux = kHeadCat;
+    g.C = hcat_.get() + r0 * kHeadCat; g.ldc = kHeadCat;
+    g.bias = heads_.b1cat; g.aux_out = hpre_.get() + r0 * kHeadCat; g.ldaux = kHeadCat;
     g.epi = Epi::BiasStorePre;
     launch_gemm(g, s);
   }
-  launch_heads_finalize(n, z_.get(), hcat_.get(), heads_, hk_.get(), e_nn_.get(), raw_q_.get(), ratio_.get(), s);
-  launch_segment_sum(nimg, image_start_.get(), raw_q_.get(), 1, 1, img_sums_.get(), s);
-  launch_charge_correct(n, raw_q_.get(), img_sums_.get(), image_charge_.get(), image_of_.get(), image_start_.get(),
-                        q_.get(), nullptr, nullptr, s);
+  launch_heads_finalize(n, z_.get() + r0, hcat_.get() + r0 * kHeadCat, heads_, hk_.get() + r0 * kHirsh,
+                        e_nn_.get() + r0, raw_q_.get() + r0, ratio_.get() + r0, s);
+  // charge conservation: exact sum of the raw charges per image (over all GPUs)
+  if (identity_) {
+    exact_sums(raw_q_.get(), 1, 1, nimg, image_start_.get(), img_sums_.get());
+  } else {
+    exact_sums(raw_q_.get(), 1, 1, 1, own_seg, img_sums_.get());
+  }
+  launch_charge_correct(n, raw_q_.get() + r0, img_sums_.get(), image_charge_.get(), image_of_.get() + r0, count_seg,
+                        q_.get() + r0, nullptr, nullptr, s);
+  allgather_rows(q_.get(), 1);
+  allgather_rows(ratio_.get(), 1);
 
-  // ---- long range ----------------------------------------------------------
-  launch_long_range(n, nb_, lr_cut_, z_.get(), q_.get(), ratio_.get(), alpha_ref_, c6_ref_, ref_table_, lr_,
+  // ---- long range (owned rows) ------------------------------------------------
+  launch_long_range(n, spec_.n, nb_, lr_cut_, z_.get(), q_.get(), ratio_.get(), alpha_ref_, c6_ref_, ref_table_, lr_,
                     reinterpret_cast<double4 *>(lr_pos4_.get()), reinterpret_cast<double4 *>(lr_par4_.get()),
                     e_lr_.get(), e_elec_.get(), e_disp_.get(), dq_.get(), dh_.get(), f_lr_.get(), w_lr_.get(), s);
-  launch_segment_sum(nimg, image_start_.get(), dq_.get(), 1, 1, img_sums_.get(), s);
-  launch_charge_correct(nimg, nullptr, nullptr, nullptr, nullptr, image_start_.get(), nullptr, dq_mean_.get(),
+  if (identity_) {
+    exact_sums(dq_.get(), 1, 1, nimg, image_start_.get(), img_sums_.get());
+  } else {
+    exact_sums(dq_.get(), 1, 1, 1, own_seg, img_sums_.get());
+  }
+  launch_charge_correct(identity_ ? nimg : 1, nullptr, nullptr, nullptr, nullptr, count_seg, nullptr, dq_mean_.get(),
                         img_sums_.get(), s);
 
   // ---- reverse ---------------------------------------------------------------
-  launch_heads_seed(n, z_.get(), hpre_.get(), hk_.get(), heads_, dq_.get(), dq_mean_.get(), image_of_.get(),
-                    dh_.get(), g_hcat_.get(), s);
+  launch_heads_seed(n, z_.get() + r0, hpre_.get() + r0 * kHeadCat, hk_.get() + r0 * kHirsh, heads_, dq_.get() + r0,
+                    dq_mean_.get(), image_of_.get() + r0, dh_.get() + r0, g_hcat_.get() + r0 * kHeadCat, s);
   {
     GemmArgs g{};
     g.M = n; g.N = kF; g.K = kHeadCat;
-    g.A = g_hcat_.get(); g.lda = kHeadCat;
+    g.A = g_hcat_.get() + r0 * kHeadCat; g.lda = kHeadCat;
     g.W = heads_.w1cat; g.ldw = kF; g.transB = false;
-    g.C = g_x_.get(); g.ldc = kF;
+    g.C = g_x_.get() + r0 * kF; g.ldc = kF;
     launch_gemm(g, s);
   }
   double *gx = g_x_.get(), *gx_next = g_x2_.get();
   double *gev = nullptr, *gev_next = g_ev_.get();
   for (int b = layers_ - 1; b >= 0; --b) {
     const BlockW &w = blocks_[b];
-    launch_post_attn_rev_final(n, gx, gev, xhat2_[b]->get(), rstd2_[b]->get(), w.ln2w, A_[b]->get(), gate_[b]->get(),
-                               g_t_.get(), g_A_.get(), s);
+    launch_post_attn_rev_final(n, gx + r0 * kF, gev ? gev + r0 * kEV : nullptr, xhat2_[b]->get() + r0 * kF,
+                               rstd2_[b]->get() + r0, w.ln2w, A_[b]->get() + r0 * kEV, gate_[b]->get() + r0 * 4,
+                               g_t_.get() + r0 * kIntW, g_A_.get() + r0 * kEV, s);
     {  // g_cat = g_t W_int; g_post = g_cat[:, :128] + g_t[:, :128]
       GemmArgs g{};
       g.M = n; g.N = kIntW; g.K = kIntW;
-      g.A = g_t_.get(); g.lda = kIntW;
+      g.A = g_t_.get() + r0 * kIntW; g.lda = kIntW;
       g.W = w.intw; g.ldw = kIntW; g.transB = false;
-      g.C = g_cat_.get(); g.ldc = kIntW;
-      g.aux = g_t_.get(); g.ldaux = kIntW;
+      g.C = g_cat_.get() + r0 * kIntW; g.ldc = kIntW;
+      g.aux = g_t_.get() + r0 * kIntW; g.ldaux = kIntW;
       g.epi = Epi::AddResidual;
       launch_gemm_ex(g, kF, 0, s);
     }
     {  // g_hp = (g_post W2) * silu'(hp)
       GemmArgs g{};
       g.M = n; g.N = kF; g.K = kF;
-      g.A = g_cat_.get(); g.lda = kIntW;
+      g.A = g_cat_.get() + r0 * kIntW; g.lda = kIntW;
       g.W = w.mlp2w; g.ldw = kF; g.transB = false;
-      g.C = g_hp_.get(); g.ldc = kF;
-      g.aux = hp_[b]->get(); g.ldaux = kF;
+      g.C = g_hp_.get() + r0 * kF; g.ldc = kF;
+      g.aux = hp_[b]->get() + r0 * kF; g.ldaux = kF;
       g.epi = Epi::SiluPrimeMul;
       launch_gemm(g, s);
     }
     {  // g_n1 = g_post + (g_hp W1) * silu'(n1)
       GemmArgs g{};
       g.M = n; g.N = kF; g.K = kF;
-      g.A = g_hp_.get(); g.lda = kF;
+      g.A = g_hp_.get() + r0 * kF; g.lda = kF;
       g.W = w.mlp1w; g.ldw = kF; g.transB = false;
-      g.C = g_n1_.get(); g.ldc = kF;
-      g.aux = n1_[b]->get(); g.ldaux = kF;
-      g.aux2 = g_cat_.get();
+      g.C = g_n1_.get() + r0 * kF; g.ldc = kF;
+      g.aux = n1_[b]->get() + r0 * kF; g.ldaux = kF;
+      g.aux2 = g_cat_.get() + r0 * kIntW;
       g.epi = Epi::GateSiluResidual;
       launch_gemm_ex(g, kF, kIntW, s);
     }
-    launch_post_attn_rev_ln1(n, g_n1_.get(), xhat1_[b]->get(), rstd1_[b]->get(), w.ln1w, A_[b]->get(), w.cg_int,
-                             g_cat_.get(), g_a_.get(), g_A_.get(), s);
+    launch_post_attn_rev_ln1(n, g_n1_.get() + r0 * kF, xhat1_[b]->get() + r0 * kF, rstd1_[b]->get() + r0, w.ln1w,
+                             A_[b]->get() + r0 * kEV, w.cg_int, g_cat_.get() + r0 * kIntW, g_a_.get() + r0 * kF,
+                             g_A_.get() + r0 * kEV, s);
+    // the sender role of the attention reverse reads the neighbours' adjoints
+    allgather_rows(g_a_.get(), kF);
+    allgather_rows(g_A_.get(), kEV);
     launch_attention_reverse(n, nb_, geo_.get(), sh_.get(), qkv_[b]->get(), f_inv_[b]->get(), f_ev_[b]->get(),
                              g_a_.get(), g_A_.get(), norm_, b > 0 ? g_qkv_.get() : nullptr, pair_sc_.get(),
                              g_filt_inv_.get(), g_filt_ev_.get(), s);
@@ -629,10 +800,10 @@ void Evaluator::compute() {
     if (b > 0) {
       GemmArgs g{};  // g_x_in = g_a + per-head (g_qkv W^T)
       g.M = n; g.N = 32; g.K = 160;
-      g.A = g_qkv_.get(); g.lda = kQKV; g.strideA = 160;
+      g.A = g_qkv_.get() + r0 * kQKV; g.lda = kQKV; g.strideA = 160;
       g.W = w.qkv_rev; g.ldw = 160; g.transB = true; g.strideW = 32 * 160;
-      g.C = gx_next; g.ldc = kF; g.strideC = 32;
-      g.aux = g_a_.get(); g.ldaux = kF; g.strideAux = 32;
+      g.C = gx_next + r0 * kF; g.ldc = kF; g.strideC = 32;
+      g.aux = g_a_.get() + r0 * kF; g.ldaux = kF; g.strideAux = 32;
       g.epi = Epi::AddResidual;
       g.batch = 4;
       launch_gemm(g, s);
@@ -643,13 +814,17 @@ void Evaluator::compute() {
     }
   }
 
-  // ---- assembly --------------------------------------------------------------
-  launch_assemble(n, nb_, geo_.get(), gv_.get(), e_nn_.get(), e_lr_.get(), f_lr_.get(), w_lr_.get(), force_.get(),
+  // ---- assembly (owned rows) ----------------------------------------------------
+  launch_assemble(nb_, geo_.get(), gv_.get(), e_nn_.get(), e_lr_.get(), f_lr_.get(), w_lr_.get(), force_.get(),
                   e_atom_.get(), e_zbl_.get(), w_atom_.get(), s);
-  launch_segment_sum(nimg, image_start_.get(), e_atom_.get(), 1, 1, image_energy_.get(), s);
-  // virial: one segment [0, n) over atoms; energy: one segment [0, nimg) over image energies
-  launch_segment_sum(1, small_ints_.get() + 8, w_atom_.get(), 6, 6, totals_.get() + 1, s);
-  launch_segment_sum(1, small_ints_.get() + 6, image_energy_.get(), 1, 1, totals_.get(), s);
+  if (identity_) {
+    exact_sums(e_atom_.get(), 1, 1, nimg, image_start_.get(), image_energy_.get());
+    exact_sums(e_atom_.get(), 1, 1, 1, own_seg, totals_.get());
+  } else {
+    exact_sums(e_atom_.get(), 1, 1, 1, own_seg, image_energy_.get());
+    exact_sums(e_atom_.get(), 1, 1, 1, own_seg, totals_.get());
+  }
+  exact_sums(w_atom_.get(), 6, 6, 1, own_seg, totals_.get() + 1);
 }
 
 Evaluator::HostResult Evaluator::download(double *f, double *eatom, double *charges, double *ratios,
@@ -659,19 +834,30 @@ Evaluator::HostResult Evaluator::download(double *f, double *eatom, double *char
   const int n = spec_.n;
   const int nimg = int(spec_.image_start.size()) - 1;
   cudaStream_t s = stream_;
-  auto d2h = [&](double *dst, const double *src, std::size_t count) {
-    if (dst) SO3_CUDA(cudaMemcpyAsync(dst, src, sizeof(double) * count, cudaMemcpyDeviceToHost, s));
+  // every rank returns the whole system: gather the other GPUs' rows first
+  auto fetch = [&](double *dst, double *src, int width) {
+    if (!dst) return;
+    if (identity_) {
+      SO3_CUDA(cudaMemcpyAsync(dst, src, sizeof(double) * width * std::size_t(n), cudaMemcpyDeviceToHost, s));
+      return;
+    }
+    allgather_rows(src, width);
+    SO3_CUDA(cudaMemcpyAsync(stage_.data(), src, sizeof(double) * width * std::size_t(n_rows_), cudaMemcpyDeviceToHost,
+                             s));
+    SO3_CUDA(cudaStreamSynchronize(s));
+    for (int i = 0; i < n; ++i)
+      for (int k = 0; k < width; ++k) dst[std::size_t(i) * width + k] = stage_[std::size_t(row_of_[i]) * width + k];
   };
-  d2h(f, force_.get(), 3 * std::size_t(n));
-  d2h(eatom, e_atom_.get(), n);
-  d2h(charges, q_.get(), n);
-  d2h(ratios, ratio_.get(), n);
-  d2h(e_learned, e_nn_.get(), n);
-  d2h(e_zbl, e_zbl_.get(), n);
-  d2h(e_lr, e_lr_.get(), n);
-  d2h(e_elec, e_elec_.get(), n);
-  d2h(e_disp, e_disp_.get(), n);
-  d2h(image_energy, image_energy_.get(), nimg);
+  fetch(f, force_.get(), 3);
+  fetch(eatom, e_atom_.get(), 1);
+  fetch(charges, q_.get(), 1);
+  fetch(ratios, ratio_.get(), 1);
+  fetch(e_learned, e_nn_.get(), 1);
+  fetch(e_zbl, e_zbl_.get(), 1);
+  fetch(e_lr, e_lr_.get(), 1);
+  fetch(e_elec, e_elec_.get(), 1);
+  fetch(e_disp, e_disp_.get(), 1);
+  if (image_energy) SO3_CUDA(cudaMemcpyAsync(image_energy, image_energy_.get(), sizeof(double) * nimg, cudaMemcpyDeviceToHost, s));
   SO3_CUDA(cudaMemcpyAsync(host_totals_, totals_.get(), sizeof(double) * 7, cudaMemcpyDeviceToHost, s));
   SO3_CUDA(cudaMemcpyAsync(host_small_ + 8, nb_.error_flag, sizeof(int), cudaMemcpyDeviceToHost, s));
   SO3_CUDA(cudaStreamSynchronize(s));
@@ -683,38 +869,55 @@ Evaluator::HostResult Evaluator::download(double *f, double *eatom, double *char
 }
 
 // ---------------------------------------------------------------------------
-// device-resident MD (velocity Verlet, LAMMPS metal units: ftm2v = 1/1.0364269e-4)
+// device-resident MD (velocity Verlet, LAMMPS metal units: ftm2v = 1/1.0364269e-4);
+// each GPU integrates its own atoms and the new positions are all-gathered
 // ---------------------------------------------------------------------------
 void Evaluator::md_setup(const double *host_v, const double *host_mass) {
   SO3_CUDA(cudaSetDevice(device_));
   const int n = spec_.n;
-  std::vector<double> inv(n);
+  std::vector<double> v_rows(3 * std::size_t(n_rows_), 0.0), inv_rows(n_rows_, 0.0);
   for (int i = 0; i < n; ++i) {
     if (!(host_mass[i] > 0)) throw Error("SO3LR MD: masses must be positive");
-    inv[i] = 1.0 / host_mass[i];
+    inv_rows[row_of_[i]] = 1.0 / host_mass[i];
+    for (int d = 0; d < 3; ++d) v_rows[3 * std::size_t(row_of_[i]) + d] = host_v[3 * std::size_t(i) + d];
   }
-  SO3_CUDA(cudaMemcpyAsync(v_.reserve(3 * std::size_t(n)), host_v, sizeof(double) * 3 * n, cudaMemcpyHostToDevice,
-                           stream_));
-  SO3_CUDA(cudaMemcpyAsync(inv_mass_.reserve(n), inv.data(), sizeof(double) * n, cudaMemcpyHostToDevice, stream_));
+  SO3_CUDA(cudaMemcpyAsync(v_.reserve(3 * std::size_t(n_rows_)), v_rows.data(), sizeof(double) * 3 * n_rows_,
+                           cudaMemcpyHostToDevice, stream_));
+  SO3_CUDA(cudaMemcpyAsync(inv_mass_.reserve(n_rows_), inv_rows.data(), sizeof(double) * n_rows_,
+                           cudaMemcpyHostToDevice, stream_));
   compute();  // forces at the starting positions
   SO3_CUDA(cudaStreamSynchronize(stream_));
 }
 
 void Evaluator::md_steps(int nsteps, double dt) {
   constexpr double ftm2v = 1.0 / 1.0364269e-4;
-  const int n = spec_.n;
+  const std::size_t r0 = std::size_t(row0_);
   for (int step = 0; step < nsteps; ++step) {
-    launch_verlet_first(n, x_.get(), v_.get(), force_.get(), inv_mass_.get(), dt, ftm2v, stream_);
+    launch_verlet_first(n_own_, x_.get() + 3 * r0, v_.get() + 3 * r0, force_.get() + 3 * r0, inv_mass_.get() + r0, dt,
+                        ftm2v, stream_);
+    allgather_rows(x_.get(), 3);
     compute();
-    launch_verlet_second(n, v_.get(), force_.get(), inv_mass_.get(), dt, ftm2v, stream_);
+    launch_verlet_second(n_own_, v_.get() + 3 * r0, force_.get() + 3 * r0, inv_mass_.get() + r0, dt, ftm2v, stream_);
   }
 }
 
 void Evaluator::md_download(double *x, double *v) {
   const int n = spec_.n;
-  if (x) SO3_CUDA(cudaMemcpyAsync(x, x_.get(), sizeof(double) * 3 * n, cudaMemcpyDeviceToHost, stream_));
-  if (v) SO3_CUDA(cudaMemcpyAsync(v, v_.get(), sizeof(double) * 3 * n, cudaMemcpyDeviceToHost, stream_));
-  SO3_CUDA(cudaStreamSynchronize(stream_));
+  auto fetch = [&](double *dst, double *src) {
+    if (!dst) return;
+    if (identity_) {
+      SO3_CUDA(cudaMemcpyAsync(dst, src, sizeof(double) * 3 * n, cudaMemcpyDeviceToHost, stream_));
+      SO3_CUDA(cudaStreamSynchronize(stream_));
+      return;
+    }
+    allgather_rows(src, 3);
+    SO3_CUDA(cudaMemcpyAsync(stage_.data(), src, sizeof(double) * 3 * n_rows_, cudaMemcpyDeviceToHost, stream_));
+    SO3_CUDA(cudaStreamSynchronize(stream_));
+    for (int i = 0; i < n; ++i)
+      for (int d = 0; d < 3; ++d) dst[3 * std::size_t(i) + d] = stage_[3 * std::size_t(row_of_[i]) + d];
+  };
+  fetch(x, x_.get());
+  fetch(v, v_.get());
 }
 
 }  // namespace so3lr_b200

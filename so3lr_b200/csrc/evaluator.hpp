@@ -15,6 +15,8 @@
 #include <string>
 #include <vector>
 
+#include <nccl.h>
+
 #include "kernels.cuh"
 #include "model_host.hpp"
 
@@ -67,6 +69,11 @@ struct StepStats {
   long long edges = 0, pairs = 0;
 };
 
+// owner rank of every atom: spatial bricks of the periodic box (host-only, the
+// same arithmetic on every rank)
+std::vector<int> partition_atoms(const SystemSpec &s, const double *x, int nranks);
+void brick_dims(int nranks, int dims[3]);
+
 class Evaluator {
  public:
   Evaluator(const std::string &model_path, int device);
@@ -77,7 +84,14 @@ class Evaluator {
 
   // Validates Z, charges and multiplicities (so3lr_charge_spin.cpp:116-141),
   // builds the charge/spin offset tables, uploads static per-atom data.
-  void prepare(const SystemSpec &spec);
+  // host_x (N x 3, input order) is needed only to partition atoms over GPUs.
+  void prepare(const SystemSpec &spec, const double *host_x = nullptr);
+  // Join a group of nranks GPUs (one Evaluator per GPU, same model, same
+  // system); unique_id is an ncclUniqueId made by rank 0 and shared by the
+  // caller. Atoms are partitioned into spatial bricks of the periodic box.
+  void set_comm(int nranks, int rank, const void *unique_id);
+  int nranks() const { return nranks_; }
+  int owned_atoms() const { return n_own_; }
   const SystemSpec &spec() const { return spec_; }
 
   // Device positions buffer for the prepared system (N x 3). Callers may write
@@ -161,6 +175,19 @@ class Evaluator {
   DeviceArray<double> e_lr_, e_elec_, e_disp_, dq_, dh_, f_lr_, w_lr_, img_sums_, dq_mean_, lr_pos4_, lr_par4_;
   DeviceArray<double> g_hcat_, g_x_, g_x2_, g_ev_, g_ev2_, g_t_, g_cat_, g_hp_, g_n1_, g_a_, g_A_, g_qkv_;
   DeviceArray<double> e_atom_, e_zbl_, w_atom_, totals_, image_energy_;
+
+  // decomposition
+  int nranks_ = 1, rank_ = 0;
+  ncclComm_t comm_ = nullptr;
+  int n_rows_ = 0, stride_ = 0, row0_ = 0, n_own_ = 0;
+  bool identity_ = true;
+  std::vector<int> row_of_, tag_of_row_;
+  std::vector<double> stage_;
+  int host_seg_[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  DeviceArray<int> tag_, seg_, pair_canon_;
+  DeviceArray<long long> parts_;
+  void allgather_rows(double *a, int width);
+  void exact_sums(const double *v, int stride, int ncol, int nseg, const int *seg, double *out);
 
   struct KernelProfile {
     std::vector<cudaEvent_t> events;

@@ -389,18 +389,21 @@ __global__ void __launch_bounds__(256) k_filter_reverse(
       const double dl = -rad.gamma * rad.k[lane] + rad.gamma * rad.kr[lane] * raw_x / (1.0 - raw_x);
       gr = gw[pl * LDR + lane] * rbf[pl * LDR + lane] * dl;
     }
-    // cutoff gradient: sum over heads of alpha*s for both directions
+    // cutoff gradient: sum over heads of alpha*s for both directions; the two
+    // directions are added first (a commutative add), so the result does not
+    // depend on which endpoint the pair is stored from
     const double *s = sc + pl * kPairScalars;
     const int h = lane & 3, which = lane >> 2;
-    if (which < 4) {
-      // (alpha_in_inv, s_in_inv), (alpha_in_ev, s_in_ev), (alpha_out_inv, s_out_inv), (alpha_out_ev, s_out_ev)
-      const int ao = which == 0 ? 0 : (which == 1 ? 4 : (which == 2 ? 16 : 20));
-      gr += s[ao + h] * s[ao + 8 + h] * dphi;
+    if (which < 2) {
+      const int ai = which == 0 ? 0 : 4;  // (alpha_inv, s_inv) or (alpha_ev, s_ev)
+      gr += __dmul_rn(__dadd_rn(__dmul_rn(s[ai + h], s[ai + 8 + h]), __dmul_rn(s[16 + ai + h], s[16 + ai + 8 + h])),
+                      dphi);
     }
     if (lane < kEV) {
       const int d = degree_of_channel(lane);
       const double gAa = gA[(size_t)pa[p] * kEV + lane], gAb = gA[(size_t)pb[p] * kEV + lane];
-      ybuf[pl * kEV + lane] = phi * (s[4 + d] * gAa + parity_sign(d) * s[20 + d] * gAb);
+      ybuf[pl * kEV + lane] =
+          __dmul_rn(phi, __dadd_rn(__dmul_rn(s[4 + d], gAa), parity_sign(d) * __dmul_rn(s[20 + d], gAb)));
     }
     for (int off = 16; off > 0; off >>= 1) gr += __shfl_xor_sync(0xffffffffu, gr, off);
     if (lane == 0) grs[pl] = gr;

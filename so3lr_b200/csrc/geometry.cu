@@ -19,17 +19,29 @@ namespace so3lr_b200 {
 // geometry of every undirected short-range pair
 // ---------------------------------------------------------------------------
 __global__ void k_pair_geometry(int P, const int *__restrict__ pa, const int *__restrict__ pb,
-                                const int *__restrict__ pimg, const double *__restrict__ xw, CellGrid g,
-                                const int *__restrict__ z, ZblDev zbl, double rc, double *__restrict__ geo,
-                                double *__restrict__ sh, double *__restrict__ gv) {
+                                const int *__restrict__ pimg, const int *__restrict__ pcanon,
+                                const double *__restrict__ xw, CellGrid g, const int *__restrict__ z, ZblDev zbl,
+                                double rc, double *__restrict__ geo, double *__restrict__ sh,
+                                double *__restrict__ gv) {
   const int p = blockIdx.x * blockDim.x + threadIdx.x;
   if (p >= P) return;
   const int a = pa[p], b = pb[p];
   int sx, sy, sz;
   unpack_image(pimg[p], sx, sy, sz);
-  const double vx = xw[3 * a] - (xw[3 * b] + sx * g.len[0]);
-  const double vy = xw[3 * a + 1] - (xw[3 * b + 1] + sy * g.len[1]);
-  const double vz = xw[3 * a + 2] - (xw[3 * b + 2] + sz * g.len[2]);
+  // The vector is always formed in the pair's canonical orientation (smaller
+  // tag receives) and negated otherwise, so a pair that two GPUs both hold,
+  // each in its own orientation, gets bitwise opposite vectors.
+  double vx, vy, vz;
+  // explicitly rounded (no FMA contraction) so both branches round alike
+  if (pcanon == nullptr || pcanon[p]) {
+    vx = __dsub_rn(xw[3 * a], __dadd_rn(xw[3 * b], __dmul_rn(double(sx), g.len[0])));
+    vy = __dsub_rn(xw[3 * a + 1], __dadd_rn(xw[3 * b + 1], __dmul_rn(double(sy), g.len[1])));
+    vz = __dsub_rn(xw[3 * a + 2], __dadd_rn(xw[3 * b + 2], __dmul_rn(double(sz), g.len[2])));
+  } else {
+    vx = -__dsub_rn(xw[3 * b], __dadd_rn(xw[3 * a], __dmul_rn(double(-sx), g.len[0])));
+    vy = -__dsub_rn(xw[3 * b + 1], __dadd_rn(xw[3 * a + 1], __dmul_rn(double(-sy), g.len[1])));
+    vz = -__dsub_rn(xw[3 * b + 2], __dadd_rn(xw[3 * a + 2], __dmul_rn(double(-sz), g.len[2])));
+  }
   const double r = sqrt(vx * vx + vy * vy + vz * vz);
   const double inv = r > 1.0e-14 ? 1.0 / r : 0.0;
   const double ux = vx * inv, uy = vy * inv, uz = vz * inv;
@@ -88,8 +100,8 @@ __global__ void k_pair_geometry(int P, const int *__restrict__ pa, const int *__
 void launch_pair_geometry(int P, const NeighborState &nb, const int *z, ZblDev zbl, double sr_cutoff,
                           double *geo, double *sh, double *gv, cudaStream_t s) {
   if (P == 0) return;
-  k_pair_geometry<<<(P + 127) / 128, 128, 0, s>>>(P, nb.pair_a, nb.pair_b, nb.pair_img, nb.xw, nb.grid, z, zbl,
-                                                   sr_cutoff, geo, sh, gv);
+  k_pair_geometry<<<(P + 127) / 128, 128, 0, s>>>(P, nb.pair_a, nb.pair_b, nb.pair_img, nb.pair_canon, nb.xw,
+                                                   nb.grid, z, zbl, sr_cutoff, geo, sh, gv);
   SO3_LAUNCH("pair_geometry");
 }
 
@@ -223,7 +235,7 @@ __global__ void k_lr_gather(int n, int periodic, const int *__restrict__ cell_at
 constexpr int kLrWarps = 8;
 constexpr int kLrQueue = 64;
 __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
-    int n, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
+    int n, int row0, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
     const int *__restrict__ cell_start, const int *__restrict__ cell_count, const int *__restrict__ image_of,
     const int *__restrict__ image_start, int reach, double rc2, const double4 *__restrict__ pos4,
     const double4 *__restrict__ par4, const int *__restrict__ z, const double *__restrict__ q,
@@ -236,7 +248,7 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= n) return;
-  const int i = warp;
+  const int i = row0 + warp;
   const double xi = xw[3 * i], yi = xw[3 * i + 1], zi = xw[3 * i + 2];
   const double qi = q[i], hi = h[i];
   const int Zi = z[i];
@@ -370,18 +382,18 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
   }
 }
 
-void launch_long_range(int n, const NeighborState &nb, double rc_lr, const int *z, const double *q,
-                       const double *h, const double *alpha_ref, const double *c6_ref, int table_size,
-                       LrDev p, double4 *pos4, double4 *par4, double *e_lr, double *e_elec, double *e_disp,
-                       double *dq, double *dh, double *f_lr, double *w_lr, cudaStream_t s) {
+void launch_long_range(int n, int n_cells_atoms, const NeighborState &nb, double rc_lr, const int *z,
+                       const double *q, const double *h, const double *alpha_ref, const double *c6_ref,
+                       int table_size, LrDev p, double4 *pos4, double4 *par4, double *e_lr, double *e_elec,
+                       double *e_disp, double *dq, double *dh, double *f_lr, double *w_lr, cudaStream_t s) {
   if (n == 0) return;
-  k_lr_gather<<<(n + 255) / 256, 256, 0, s>>>(n, nb.grid.periodic, nb.cell_atoms, nb.xw, q, h, z, alpha_ref, c6_ref,
-                                              table_size, pos4, par4);
+  k_lr_gather<<<(n_cells_atoms + 255) / 256, 256, 0, s>>>(n_cells_atoms, nb.grid.periodic, nb.cell_atoms, nb.xw, q, h,
+                                                          z, alpha_ref, c6_ref, table_size, pos4, par4);
   SO3_LAUNCH("lr_gather");
   const int reach = sr_reach(nb.grid, rc_lr);
   const int threads = kLrWarps * 32;
   const int blocks = (n * 32 + threads - 1) / threads;
-  k_long_range<<<blocks, threads, 0, s>>>(n, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count, nb.image_of,
+  k_long_range<<<blocks, threads, 0, s>>>(n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count, nb.image_of,
                                           nb.image_start, reach, rc_lr * rc_lr, pos4, par4, z, q, h, alpha_ref,
                                           c6_ref, table_size, p, e_lr, e_elec, e_disp, dq, dh, f_lr, w_lr);
   SO3_LAUNCH("long_range");
@@ -390,17 +402,18 @@ void launch_long_range(int n, const NeighborState &nb, double rc_lr, const int *
 // ---------------------------------------------------------------------------
 // assembly: forces, per-atom energies, per-atom virial (gathers over the CSR)
 // ---------------------------------------------------------------------------
-__global__ void k_assemble(int n, const int *__restrict__ row_start, const int *__restrict__ edge_pair,
-                           const double *__restrict__ geo, const double *__restrict__ gv,
-                           const double *__restrict__ e_nn, const double *__restrict__ e_lr,
-                           const double *__restrict__ f_lr, const double *__restrict__ w_lr,
-                           double *__restrict__ force, double *__restrict__ e_atom, double *__restrict__ e_zbl,
-                           double *__restrict__ w_atom) {
-  const int a = blockIdx.x * blockDim.x + threadIdx.x;
-  if (a >= n) return;
+__global__ void k_assemble(int n, int row0, const int *__restrict__ row_start, const int *__restrict__ edge_pair,
+                           const int *__restrict__ pair_canon, const double *__restrict__ geo,
+                           const double *__restrict__ gv, const double *__restrict__ e_nn,
+                           const double *__restrict__ e_lr, const double *__restrict__ f_lr,
+                           const double *__restrict__ w_lr, double *__restrict__ force, double *__restrict__ e_atom,
+                           double *__restrict__ e_zbl, double *__restrict__ w_atom) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const int a = row0 + r;
   double fx = 0, fy = 0, fz = 0, ez = 0;
   double w[6] = {0, 0, 0, 0, 0, 0};
-  for (int e = row_start[a]; e < row_start[a + 1]; ++e) {
+  for (int e = row_start[r]; e < row_start[r + 1]; ++e) {
     const int code = edge_pair[e];
     const int p = code >= 0 ? code : ~code;
     const double gx = gv[3 * p], gy = gv[3 * p + 1], gz = gv[3 * p + 2];
@@ -408,16 +421,19 @@ __global__ void k_assemble(int n, const int *__restrict__ row_start, const int *
     ez += gp[6];
     if (code >= 0) {
       fx -= gx; fy -= gy; fz -= gz;
-      const double r = gp[0];
-      const double vx = r * gp[1], vy = r * gp[2], vz = r * gp[3];
+    } else {
+      fx += gx; fy += gy; fz += gz;
+    }
+    // each pair's virial is counted once, by the owner of its canonical receiver
+    if (code >= 0 && (pair_canon == nullptr || pair_canon[p])) {
+      const double rr = gp[0];
+      const double vx = rr * gp[1], vy = rr * gp[2], vz = rr * gp[3];
       w[0] -= vx * gx;
       w[1] -= vy * gy;
       w[2] -= vz * gz;
       w[3] -= 0.5 * (vx * gy + vy * gx);
       w[4] -= 0.5 * (vx * gz + vz * gx);
       w[5] -= 0.5 * (vy * gz + vz * gy);
-    } else {
-      fx += gx; fy += gy; fz += gz;
     }
   }
   force[3 * a] = fx + f_lr[3 * a];
@@ -428,12 +444,13 @@ __global__ void k_assemble(int n, const int *__restrict__ row_start, const int *
   for (int k = 0; k < 6; ++k) w_atom[6 * a + k] = w[k] + w_lr[6 * a + k];
 }
 
-void launch_assemble(int n, const NeighborState &nb, const double *geo, const double *gv, const double *e_nn,
+void launch_assemble(const NeighborState &nb, const double *geo, const double *gv, const double *e_nn,
                      const double *e_lr, const double *f_lr, const double *w_lr, double *force, double *e_atom,
                      double *e_zbl, double *w_atom, cudaStream_t s) {
+  const int n = nb.n_own;
   if (n == 0) return;
-  k_assemble<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row_start, nb.edge_pair, geo, gv, e_nn, e_lr, f_lr, w_lr, force,
-                                              e_atom, e_zbl, w_atom);
+  k_assemble<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row0, nb.row_start, nb.edge_pair, nb.pair_canon, geo, gv, e_nn,
+                                              e_lr, f_lr, w_lr, force, e_atom, e_zbl, w_atom);
   SO3_LAUNCH("assemble");
 }
 

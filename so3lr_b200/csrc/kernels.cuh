@@ -25,15 +25,24 @@ struct NeighborState {
   int *pair_scan = nullptr, *edge_pair = nullptr;
   int *pair_a = nullptr, *pair_b = nullptr, *pair_img = nullptr, *pair_edge = nullptr;
   int *scan_total = nullptr, *scan_scratch = nullptr, *error_flag = nullptr;
+  int *pair_canon = nullptr;  // pair stored in its canonical orientation (smaller tag receives)
+  const int *tag = nullptr;   // global tag of every row (-1: padding row); nullptr: tag = row
+  int row0 = 0, n_own = 0;    // rows [row0, row0 + n_own) are owned here and get CSR rows
 };
 
 void exclusive_scan(const int *in, int *out, int n, int *total, int *scratch, cudaStream_t s);
 std::size_t scan_scratch_ints(std::size_t n);
 void build_cells(NeighborState &nb, int n, const double *x, cudaStream_t s);
 int sr_reach(const CellGrid &g, double rc);
-void count_sr(NeighborState &nb, int n, double rc, cudaStream_t s);
-void fill_sr(NeighborState &nb, int n, double rc, int E, cudaStream_t s);
-void fill_pairs(NeighborState &nb, int n, int E, cudaStream_t s);
+void count_sr(NeighborState &nb, double rc, cudaStream_t s);
+void fill_sr(NeighborState &nb, double rc, int E, cudaStream_t s);
+void fill_pairs(NeighborState &nb, int E, cudaStream_t s);
+
+// exact fixed-point sums (reduce.cu): parts[(seg * ncol + col) * 2 + {hi, lo}]
+void launch_fixed_segment_sum(int nseg, const int *start, const double *v, int stride, int ncol, long long *parts,
+                              cudaStream_t s);
+// out[k] = sum over nparts consecutive blocks of `count` fixed-point values
+void launch_fixed_finish(const long long *parts, int nparts, int count, double *out, cudaStream_t s);
 
 // ---- per-pair geometry -------------------------------------------------------
 // geo[p*8 + {0..7}] = r, ux, uy, uz, phi, dphi/dr, zbl directed energy, zbl pair dE/dr
@@ -51,11 +60,13 @@ struct LrDev {
 // Long-range Coulomb + dispersion over the full neighbour set of every atom
 // (cell stencil or image range). Per-atom outputs (N): energy (total, elec,
 // disp), dE/dq, dE/dh, direct force (3), virial (6).
-// pos4 / par4: N-element scratch for the cell-ordered partner data.
-void launch_long_range(int n, const NeighborState &nb, double rc_lr, const int *z, const double *q,
-                       const double *h, const double *alpha_ref, const double *c6_ref, int table_size,
-                       LrDev p, double4 *pos4, double4 *par4, double *e_lr, double *e_elec, double *e_disp,
-                       double *dq, double *dh, double *f_lr, double *w_lr, cudaStream_t s);
+// n: owned rows (nb.row0 ..); n_cells_atoms: atoms in the cell list (all real
+// atoms; with open boundaries, every row). pos4 / par4: n_cells_atoms-element
+// scratch for the cell-ordered partner data.
+void launch_long_range(int n, int n_cells_atoms, const NeighborState &nb, double rc_lr, const int *z,
+                       const double *q, const double *h, const double *alpha_ref, const double *c6_ref,
+                       int table_size, LrDev p, double4 *pos4, double4 *par4, double *e_lr, double *e_elec,
+                       double *e_disp, double *dq, double *dh, double *f_lr, double *w_lr, cudaStream_t s);
 
 // Allocation-free variant of the long-range step for open-boundary systems of
 // at most noalloc_max_atoms() atoms (scratch in file-scope device arrays, noalloc.cu).
@@ -153,7 +164,7 @@ void launch_charge_correct(int n, const double *raw, const double *raw_sum, cons
                            const double *dq_sum, cudaStream_t s);
 
 // final assembly: per-atom forces and energies, per-atom SR virial
-void launch_assemble(int n, const NeighborState &nb, const double *geo, const double *gv, const double *e_nn,
+void launch_assemble(const NeighborState &nb, const double *geo, const double *gv, const double *e_nn,
                      const double *e_lr, const double *f_lr, const double *w_lr, double *force, double *e_atom,
                      double *e_zbl, double *w_atom, cudaStream_t s);
 

@@ -82,10 +82,15 @@ std::size_t scan_scratch_ints(std::size_t n) {
 }
 
 // ---- cell list ---------------------------------------------------------------
-__global__ void k_wrap_assign(int n, const double *__restrict__ x, CellGrid g, double *__restrict__ xw,
-                              int *__restrict__ cell, int *__restrict__ cell_count) {
+__global__ void k_wrap_assign(int n, const double *__restrict__ x, CellGrid g, const int *__restrict__ tag,
+                              double *__restrict__ xw, int *__restrict__ cell, int *__restrict__ cell_count) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
+  if (tag != nullptr && tag[i] < 0) {  // padding row of a rank-major layout: not an atom
+    cell[i] = -1;
+    xw[3 * i] = xw[3 * i + 1] = xw[3 * i + 2] = 0.0;
+    return;
+  }
   int cc[3];
   for (int d = 0; d < 3; ++d) {
     double p = x[3 * i + d] - g.lo[d];
@@ -106,21 +111,25 @@ __global__ void k_cell_fill(int n, const int *__restrict__ cell, const int *__re
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int c = cell[i];
+  if (c < 0) return;
   const int slot = atomicAdd(&cell_fill[c], 1);
   cell_atoms[cell_start[c] + slot] = i;
 }
 
-// Sort the atoms of every cell ascending: the fill above is scheduling-dependent.
+// Sort the atoms of every cell by global tag: the fill above is
+// scheduling-dependent, and the tag order does not depend on how rows are laid
+// out across GPUs.
 __global__ void k_cell_sort(int ncells, const int *__restrict__ cell_start, const int *__restrict__ cell_count,
-                            int *__restrict__ cell_atoms) {
+                            const int *__restrict__ tag, int *__restrict__ cell_atoms) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= ncells) return;
   int *a = cell_atoms + cell_start[c];
   const int m = cell_count[c];
   for (int i = 1; i < m; ++i) {
     const int v = a[i];
+    const int vt = tag ? tag[v] : v;
     int j = i - 1;
-    while (j >= 0 && a[j] > v) {
+    while (j >= 0 && (tag ? tag[a[j]] : a[j]) > vt) {
       a[j + 1] = a[j];
       --j;
     }
@@ -128,29 +137,31 @@ __global__ void k_cell_sort(int ncells, const int *__restrict__ cell_start, cons
   }
 }
 
-__global__ void k_sr_count(int n, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
+__global__ void k_sr_count(int n, int row0, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
                            const int *__restrict__ cell_start, const int *__restrict__ cell_count,
                            const int *__restrict__ cell_atoms, const int *__restrict__ image_of,
                            const int *__restrict__ image_start, double rc2, int reach, int *__restrict__ deg) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const int i = row0 + r;
   int count = 0;
   for_each_candidate(i, xw, g, cell, cell_start, cell_count, cell_atoms, image_of, image_start, reach,
                      [&](int, int, double dx, double dy, double dz) {
                        const double r2 = dx * dx + dy * dy + dz * dz;
                        if (r2 > 0.0 && r2 < rc2) ++count;
                      });
-  deg[i] = count;
+  deg[r] = count;
 }
 
-__global__ void k_sr_fill(int n, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
+__global__ void k_sr_fill(int n, int row0, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
                           const int *__restrict__ cell_start, const int *__restrict__ cell_count,
                           const int *__restrict__ cell_atoms, const int *__restrict__ image_of,
-                          const int *__restrict__ image_start, double rc2, int reach,
+                          const int *__restrict__ image_start, double rc2, int reach, const int *__restrict__ tag,
                           const int *__restrict__ row_start, int *__restrict__ nbr, int *__restrict__ img) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const int base = row_start[i];
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const int i = row0 + r;
+  const int base = row_start[r];
   int count = 0;
   for_each_candidate(i, xw, g, cell, cell_start, cell_count, cell_atoms, image_of, image_start, reach,
                      [&](int j, int code, double dx, double dy, double dz) {
@@ -161,11 +172,14 @@ __global__ void k_sr_fill(int n, const double *__restrict__ xw, CellGrid g, cons
                          ++count;
                        }
                      });
-  // canonical order: (sender, image)
+  // canonical order: (sender's global tag, image), independent of the local layout
   for (int a = 1; a < count; ++a) {
     const int vj = nbr[base + a], vc = img[base + a];
+    const int vt = tag ? tag[vj] : vj;
     int b = a - 1;
-    while (b >= 0 && (nbr[base + b] > vj || (nbr[base + b] == vj && img[base + b] > vc))) {
+    while (b >= 0) {
+      const int bt = tag ? tag[nbr[base + b]] : nbr[base + b];
+      if (!(bt > vt || (bt == vt && img[base + b] > vc))) break;
       nbr[base + b + 1] = nbr[base + b];
       img[base + b + 1] = img[base + b];
       --b;
@@ -175,43 +189,64 @@ __global__ void k_sr_fill(int n, const double *__restrict__ xw, CellGrid g, cons
   }
 }
 
-// primary flag + reverse-edge lookup (binary search in the sender's sorted row)
-__global__ void k_edge_primary(int n, const int *__restrict__ row_start, const int *__restrict__ nbr,
-                               const int *__restrict__ img, int *__restrict__ primary, int *__restrict__ rev,
-                               int *__restrict__ error_flag) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  for (int e = row_start[i]; e < row_start[i + 1]; ++e) {
+// Designated ("primary") edge of every pair and reverse-edge lookup. A pair is
+// owned by the designated edge's receiver. When both endpoints are owned here,
+// the designated edge is the canonical one (smaller global tag receives; for a
+// self-image pair, the positive image); when the sender is not owned here the
+// owned receiver's edge is designated and there is no local reverse edge.
+__global__ void k_edge_primary(int n, int row0, const int *__restrict__ row_start, const int *__restrict__ nbr,
+                               const int *__restrict__ img, const int *__restrict__ tag, int *__restrict__ primary,
+                               int *__restrict__ rev, int *__restrict__ error_flag) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const int i = row0 + r;
+  const int ti = tag ? tag[i] : i;
+  for (int e = row_start[r]; e < row_start[r + 1]; ++e) {
     const int j = nbr[e], code = img[e];
-    primary[e] = (i < j || (i == j && code > kZeroImage)) ? 1 : 0;
+    const int tj = tag ? tag[j] : j;
+    const bool canonical = ti < tj || (ti == tj && code > kZeroImage);
+    const bool owned_j = j >= row0 && j < row0 + n;
+    if (!owned_j) {
+      primary[e] = 1;
+      rev[e] = -1;
+      continue;
+    }
+    primary[e] = canonical ? 1 : 0;
     const int want = negate_image(code);
-    int lo = row_start[j], hi = row_start[j + 1] - 1, found = -1;
+    const int rj = j - row0;
+    int lo = row_start[rj], hi = row_start[rj + 1] - 1, found = -1;
     while (lo <= hi) {
       const int mid = (lo + hi) >> 1;
       const int mj = nbr[mid], mc = img[mid];
+      const int mt = tag ? tag[mj] : mj;
       if (mj == i && mc == want) { found = mid; break; }
-      if (mj < i || (mj == i && mc < want)) lo = mid + 1; else hi = mid - 1;
+      if (mt < ti || (mt == ti && mc < want)) lo = mid + 1; else hi = mid - 1;
     }
     rev[e] = found;
     if (found < 0) atomicExch(error_flag, 1);
   }
 }
 
-__global__ void k_pair_fill(int n, const int *__restrict__ row_start, const int *__restrict__ nbr,
-                            const int *__restrict__ img, const int *__restrict__ primary,
-                            const int *__restrict__ pair_scan, int *__restrict__ edge_pair,
-                            int *__restrict__ pair_a, int *__restrict__ pair_b, int *__restrict__ pair_img,
-                            int *__restrict__ pair_edge) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  for (int e = row_start[i]; e < row_start[i + 1]; ++e) {
+__global__ void k_pair_fill(int n, int row0, const int *__restrict__ row_start, const int *__restrict__ nbr,
+                            const int *__restrict__ img, const int *__restrict__ tag, const int *__restrict__ primary,
+                            const int *__restrict__ pair_scan, int *__restrict__ edge_pair, int *__restrict__ pair_a,
+                            int *__restrict__ pair_b, int *__restrict__ pair_img, int *__restrict__ pair_edge,
+                            int *__restrict__ pair_canon) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const int i = row0 + r;
+  const int ti = tag ? tag[i] : i;
+  for (int e = row_start[r]; e < row_start[r + 1]; ++e) {
     if (!primary[e]) continue;
     const int p = pair_scan[e];
+    const int j = nbr[e];
+    const int tj = tag ? tag[j] : j;
     edge_pair[e] = p;
     pair_a[p] = i;
-    pair_b[p] = nbr[e];
+    pair_b[p] = j;
     pair_img[p] = img[e];
     pair_edge[p] = e;
+    pair_canon[p] = (ti < tj || (ti == tj && img[e] > kZeroImage)) ? 1 : 0;
   }
 }
 
@@ -219,7 +254,7 @@ __global__ void k_pair_reverse(int E, const int *__restrict__ primary, const int
                                int *__restrict__ edge_pair) {
   const int e = blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= E) return;
-  if (!primary[e]) edge_pair[e] = ~edge_pair[rev[e]];
+  if (!primary[e] && rev[e] >= 0) edge_pair[e] = ~edge_pair[rev[e]];
 }
 
 // ---- host driver ---------------------------------------------------------------
@@ -232,12 +267,12 @@ void build_cells(NeighborState &nb, int n, const double *x, cudaStream_t s) {
   }
   SO3_CUDA(cudaMemsetAsync(nb.cell_count, 0, sizeof(int) * nc, s));
   SO3_CUDA(cudaMemsetAsync(nb.cell_fill, 0, sizeof(int) * nc, s));
-  k_wrap_assign<<<(n + 255) / 256, 256, 0, s>>>(n, x, nb.grid, nb.xw, nb.cell, nb.cell_count);
+  k_wrap_assign<<<(n + 255) / 256, 256, 0, s>>>(n, x, nb.grid, nb.tag, nb.xw, nb.cell, nb.cell_count);
   SO3_LAUNCH("wrap_assign");
   exclusive_scan(nb.cell_count, nb.cell_start, nc, nb.scan_total, nb.scan_scratch, s);
   k_cell_fill<<<(n + 255) / 256, 256, 0, s>>>(n, nb.cell, nb.cell_start, nb.cell_fill, nb.cell_atoms);
   SO3_LAUNCH("cell_fill");
-  k_cell_sort<<<(nc + 127) / 128, 128, 0, s>>>(nc, nb.cell_start, nb.cell_count, nb.cell_atoms);
+  k_cell_sort<<<(nc + 127) / 128, 128, 0, s>>>(nc, nb.cell_start, nb.cell_count, nb.tag, nb.cell_atoms);
   SO3_LAUNCH("cell_sort");
 }
 
@@ -251,30 +286,33 @@ int sr_reach(const CellGrid &g, double rc) {
   return reach;
 }
 
-void count_sr(NeighborState &nb, int n, double rc, cudaStream_t s) {
+void count_sr(NeighborState &nb, double rc, cudaStream_t s) {
   const int reach = sr_reach(nb.grid, rc);
-  k_sr_count<<<(n + 127) / 128, 128, 0, s>>>(n, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count,
-                                              nb.cell_atoms, nb.image_of, nb.image_start, rc * rc, reach,
-                                              nb.deg);
+  const int n = nb.n_own;
+  k_sr_count<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count,
+                                              nb.cell_atoms, nb.image_of, nb.image_start, rc * rc, reach, nb.deg);
   SO3_LAUNCH("sr_count");
   exclusive_scan(nb.deg, nb.row_start, n, nb.row_start + n, nb.scan_scratch, s);
 }
 
-void fill_sr(NeighborState &nb, int n, double rc, int E, cudaStream_t s) {
+void fill_sr(NeighborState &nb, double rc, int E, cudaStream_t s) {
   const int reach = sr_reach(nb.grid, rc);
-  k_sr_fill<<<(n + 127) / 128, 128, 0, s>>>(n, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count,
-                                             nb.cell_atoms, nb.image_of, nb.image_start, rc * rc, reach,
+  const int n = nb.n_own;
+  k_sr_fill<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count,
+                                             nb.cell_atoms, nb.image_of, nb.image_start, rc * rc, reach, nb.tag,
                                              nb.row_start, nb.nbr, nb.img);
   SO3_LAUNCH("sr_fill");
-  k_edge_primary<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row_start, nb.nbr, nb.img, nb.primary, nb.rev,
-                                                  nb.error_flag);
+  k_edge_primary<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.img, nb.tag, nb.primary,
+                                                  nb.rev, nb.error_flag);
   SO3_LAUNCH("edge_primary");
   exclusive_scan(nb.primary, nb.pair_scan, E, nb.scan_total, nb.scan_scratch, s);
 }
 
-void fill_pairs(NeighborState &nb, int n, int E, cudaStream_t s) {
-  k_pair_fill<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row_start, nb.nbr, nb.img, nb.primary, nb.pair_scan,
-                                               nb.edge_pair, nb.pair_a, nb.pair_b, nb.pair_img, nb.pair_edge);
+void fill_pairs(NeighborState &nb, int E, cudaStream_t s) {
+  const int n = nb.n_own;
+  k_pair_fill<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.img, nb.tag, nb.primary,
+                                               nb.pair_scan, nb.edge_pair, nb.pair_a, nb.pair_b, nb.pair_img,
+                                               nb.pair_edge, nb.pair_canon);
   SO3_LAUNCH("pair_fill");
   if (E > 0) {
     k_pair_reverse<<<(E + 255) / 256, 256, 0, s>>>(E, nb.primary, nb.rev, nb.edge_pair);

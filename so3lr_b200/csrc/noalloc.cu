@@ -100,8 +100,10 @@ void long_range_noalloc(int n, const double *x, const double *q, const double *h
   nb.image_start = sc.images + kNoAllocMaxAtoms;
   double4 *pos4 = reinterpret_cast<double4 *>(sc.partners);
   double4 *par4 = pos4 + kNoAllocMaxAtoms;
-  launch_long_range(n, nb, rc_lr, z, q, h, alpha_ref, c6_ref, table_size, p, pos4, par4, e_lr, e_elec, e_disp, dq,
-                    dh, f, w_atom, s);
+  nb.row0 = 0;
+  nb.n_own = n;
+  launch_long_range(n, n, nb, rc_lr, z, q, h, alpha_ref, c6_ref, table_size, p, pos4, par4, e_lr, e_elec, e_disp,
+                    dq, dh, f, w_atom, s);
 }
 
 }  // namespace so3lr_b200

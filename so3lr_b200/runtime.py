@@ -27,6 +27,7 @@ EXPORTED = (
     "so3lr_inspect_model", "so3lr_compute", "so3lr_compute_device", "so3lr_compute_batch",
     "so3lr_md_init", "so3lr_md_run", "so3lr_md_state", "so3lr_profile", "so3lr_profile_read",
     "so3lr_launch_count", "so3lr_long_range_noalloc", "so3lr_stream", "so3lr_last_stats", "so3lr_destroy",
+    "so3lr_nccl_unique_id", "so3lr_comm_init", "so3lr_owned_atoms", "so3lr_partition",
 )
 
 _dp = C.POINTER(C.c_double)
@@ -97,6 +98,10 @@ def load_library(path: os.PathLike | str | None = None) -> C.CDLL:
     lib.so3lr_launch_count.restype = C.c_longlong
     lib.so3lr_long_range_noalloc.argtypes = [C.c_void_p, C.c_longlong] + [C.c_void_p] * 11 + [C.c_void_p, C.c_char_p,
                                                                                               C.c_size_t]
+    lib.so3lr_nccl_unique_id.argtypes = [C.c_char_p, C.c_char_p, C.c_size_t]
+    lib.so3lr_comm_init.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_char_p, C.c_char_p, C.c_size_t]
+    lib.so3lr_owned_atoms.argtypes = [C.c_void_p]
+    lib.so3lr_partition.argtypes = [C.c_longlong, _dp, _dp, _dp, C.c_int, _ip]
     lib.so3lr_stream.argtypes = [C.c_void_p]
     lib.so3lr_stream.restype = C.c_void_p
     lib.so3lr_last_stats.argtypes = [C.c_void_p, _lp, _lp, _lp]
@@ -131,6 +136,18 @@ def validate_charge_spin(z, total_charge: float, multiplicity: float) -> str:
     rc = load_library().so3lr_validate_charge_spin(_ptr(counts, C.c_longlong), float(total_charge),
                                                    float(multiplicity), err, 512)
     return "" if rc == 0 else err.value.decode()
+
+
+def partition(x, boxlo, boxlen, nranks: int) -> np.ndarray:
+    """Owner rank of every atom under the library's spatial brick partition (host only)."""
+    x = np.ascontiguousarray(x, dtype=np.float64)
+    lo = np.ascontiguousarray(boxlo, dtype=np.float64)
+    ln = np.ascontiguousarray(boxlen, dtype=np.float64)
+    out = np.empty(len(x), dtype=np.int32)
+    rc = load_library().so3lr_partition(len(x), _ptr(x), _ptr(lo), _ptr(ln), int(nranks), _ptr(out, C.c_int))
+    if rc != 0:
+        raise So3lrError("so3lr_partition: invalid arguments")
+    return out
 
 
 def inspect_model(path: os.PathLike | str = DEFAULT_MODEL) -> dict:
@@ -174,6 +191,21 @@ class So3lrB200:
     @property
     def stream(self) -> int:
         return int(self._lib.so3lr_stream(self._h) or 0)
+
+    @staticmethod
+    def nccl_unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        err = C.create_string_buffer(512)
+        _check(load_library().so3lr_nccl_unique_id(buf, err, 512), err)
+        return buf.raw
+
+    def comm_init(self, nranks: int, rank: int, unique_id: bytes) -> None:
+        """Join a group of GPUs for spatial decomposition (see include/so3lr_b200.h)."""
+        err = C.create_string_buffer(1024)
+        _check(self._lib.so3lr_comm_init(self._h, int(nranks), int(rank), unique_id, err, 1024), err)
+
+    def owned_atoms(self) -> int:
+        return int(self._lib.so3lr_owned_atoms(self._h))
 
     def profile(self, enable: bool) -> None:
         self._lib.so3lr_profile(self._h, 1 if enable else 0)

@@ -45,9 +45,9 @@ def test_pair_style_compute_matches_c_abi(tmp_path, gpu_model):
     exe = _build(tmp_path)
     w = water_box(64, seed=21)
     inp = tmp_path / "box.txt"
-    lines = [f"{w.cell[0]!r} {len(w.z)}"]
+    lines = [f"{float(w.cell[0])!r} {len(w.z)}"]
     for zi, p in zip(w.z, w.pos):
-        lines.append(f"{1 if zi == 8 else 2} {p[0]!r} {p[1]!r} {p[2]!r}")
+        lines.append(f"{1 if zi == 8 else 2} {float(p[0])!r} {float(p[1])!r} {float(p[2])!r}")
     inp.write_text("\n".join(lines) + "\n")
     res = subprocess.run([str(exe), "run", str(MODEL), str(inp)], capture_output=True, text=True, timeout=300)
     assert res.returncode == 0, res.stdout + res.stderr
