@@ -79,7 +79,7 @@ def _gpu_worker(rank, world, uid, nmol, seed, result_q):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_multi_gpu_bit_identical(world, gpu_model):
     import torch
     if torch.cuda.device_count() < world:
