@@ -68,6 +68,15 @@ struct FilterW {
   const double *w1, *b1;  // [128][128], [128]  hidden -> filter
   const double *v0, *c0;  // [32][4], [32]      L0 -> ev hidden
   const double *v1, *c1;  // [128][32], [128]   ev hidden -> filter
+  // The same matrices as DMMA B operands in fragment-major order (see
+  // fragment_major in evaluator.cu): B(k, n) of a K x N operand sits at
+  // [k/4][n/32][lane = 4 (n%8) + k%4][(n%32)/8].
+  const double *w0t_f;    // K=32,  N=128: B(r, j) = w0[j][r]   forward layer 0 / reverse recompute
+  const double *w1t_f;    // K=128, N=128: B(j, o) = w1[o][j]   forward layer 1
+  const double *v1t_f;    // K=32,  N=128: B(h, o) = v1[o][h]   forward ev layer 1
+  const double *w1_f;     // K=128, N=128: B(o, j) = w1[o][j]   reverse through layer 1
+  const double *v1_f;     // K=128, N=32:  B(o, h) = v1[o][h]   reverse through ev layer 1
+  const double *w0_f;     // K=128, N=32:  B(j, r) = w0[j][r]   reverse through layer 0
 };
 struct BlockW {
   FilterW finv, fev;

@@ -4,6 +4,7 @@
 
 #include <cmath>
 #include <cstring>
+#include <functional>
 #include <numeric>
 #include <sstream>
 
@@ -40,6 +41,22 @@ Evaluator::~Evaluator() {
 // ---------------------------------------------------------------------------
 // weights
 // ---------------------------------------------------------------------------
+// A K x N matrix B(k, n) laid out as the B operand of m8n8k4 DMMA tiles 32
+// columns wide: lane (g = lane / 4, t = lane % 4) of a warp needs, for k-step
+// ks and column slab s, B(4 ks + t, 32 s + 8 ni + g) for ni = 0..3; those four
+// values are stored contiguously so one warp reads one k-step of a slab as
+// 1 KB of consecutive memory (two 16-byte loads per lane).
+static std::vector<double> fragment_major(int K, int N, const std::function<double(int, int)> &B) {
+  if (K % 4 != 0 || N % 32 != 0) throw Error("SO3LR: fragment-major operand needs K % 4 == 0 and N % 32 == 0");
+  std::vector<double> out(std::size_t(K) * N);
+  for (int k = 0; k < K; ++k)
+    for (int n = 0; n < N; ++n) {
+      const int ks = k / 4, t = k % 4, slab = n / 32, ni = (n % 32) / 8, g = n % 8;
+      out[((std::size_t(ks) * (N / 32) + slab) * 32 + (4 * g + t)) * 4 + ni] = B(k, n);
+    }
+  return out;
+}
+
 void Evaluator::upload_weights() {
   const Architecture &a = model_.arch();
   layers_ = a.layers;
@@ -56,7 +73,7 @@ void Evaluator::upload_weights() {
     return off;
   };
   const std::size_t F = kF, R = kR, H = kEH;
-  struct FOff { std::size_t w0, b0, w1, b1, v0, c0, v1, c1; };
+  struct FOff { std::size_t w0, b0, w1, b1, v0, c0, v1, c1, w0t_f, w1t_f, v1t_f, w1_f, v1_f, w0_f; };
   struct BOff {
     FOff finv, fev;
     std::size_t cg_att, cg_int, qf, qr, ln1w, ln1b, ln2w, ln2b, m1w, m1b, m2w, m2b, iw, ib;
@@ -64,14 +81,24 @@ void Evaluator::upload_weights() {
   std::vector<BOff> boff(layers_);
   auto filt = [&](const std::string &prefix) {
     FOff o;
-    o.w0 = push(model_.f64(prefix + ".mlp_rbf.0.weight", {F, R}));
+    const auto w0 = model_.f64(prefix + ".mlp_rbf.0.weight", {F, R});                  // [j][r]
+    const auto w1 = model_.f64(prefix + ".mlp_rbf.mlp_rbf_layer_1.0.weight", {F, F});  // [o][j]
+    const auto v1 = model_.f64(prefix + ".mlp_ev.mlp_ev_layer_1.0.weight", {F, H});    // [o][h]
+    o.w0 = push(w0);
     o.b0 = push(model_.f64(prefix + ".mlp_rbf.0.bias", {F}));
-    o.w1 = push(model_.f64(prefix + ".mlp_rbf.mlp_rbf_layer_1.0.weight", {F, F}));
+    o.w1 = push(w1);
     o.b1 = push(model_.f64(prefix + ".mlp_rbf.mlp_rbf_layer_1.0.bias", {F}));
     o.v0 = push(model_.f64(prefix + ".mlp_ev.0.weight", {H, 4}));
     o.c0 = push(model_.f64(prefix + ".mlp_ev.0.bias", {H}));
-    o.v1 = push(model_.f64(prefix + ".mlp_ev.mlp_ev_layer_1.0.weight", {F, H}));
+    o.v1 = push(v1);
     o.c1 = push(model_.f64(prefix + ".mlp_ev.mlp_ev_layer_1.0.bias", {F}));
+    const int iF = int(F), iR = int(R), iH = int(H);
+    o.w0t_f = push(fragment_major(iR, iF, [&](int r, int j) { return w0[std::size_t(j) * R + r]; }));
+    o.w1t_f = push(fragment_major(iF, iF, [&](int j, int oo) { return w1[std::size_t(oo) * F + j]; }));
+    o.v1t_f = push(fragment_major(iH, iF, [&](int h, int oo) { return v1[std::size_t(oo) * H + h]; }));
+    o.w1_f = push(fragment_major(iF, iF, [&](int oo, int j) { return w1[std::size_t(oo) * F + j]; }));
+    o.v1_f = push(fragment_major(iF, iH, [&](int oo, int h) { return v1[std::size_t(oo) * H + h]; }));
+    o.w0_f = push(fragment_major(iF, iR, [&](int j, int r) { return w0[std::size_t(j) * R + r]; }));
     return o;
   };
   for (int b = 0; b < layers_; ++b) {
@@ -159,7 +186,8 @@ void Evaluator::upload_weights() {
     const BOff &o = boff[b];
     BlockW &w = blocks_[b];
     auto fw = [&](const FOff &f) {
-      return FilterW{P(f.w0), P(f.b0), P(f.w1), P(f.b1), P(f.v0), P(f.c0), P(f.v1), P(f.c1)};
+      return FilterW{P(f.w0),    P(f.b0),    P(f.w1),    P(f.b1),   P(f.v0),   P(f.c0),  P(f.v1),
+                     P(f.c1),    P(f.w0t_f), P(f.w1t_f), P(f.v1t_f), P(f.w1_f), P(f.v1_f), P(f.w0_f)};
     };
     w.finv = fw(o.finv);
     w.fev = fw(o.fev);

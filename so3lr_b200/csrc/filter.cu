@@ -17,6 +17,8 @@
 // Tile: 64 pairs per CTA, 8 warps, each warp owns a 32x32 block of the 64x128
 // output and issues m8n8k4 DMMA on fragments read from shared memory (pair
 // activations) and L2-resident weights.
+#include <cooperative_groups.h>
+
 #include "kernels.cuh"
 #include "sh.cuh"
 
@@ -56,17 +58,30 @@ __device__ inline void compute_l0(int P, int p0, const int *pa, const int *pb, c
   l0[pl * 4 + d] = v;
 }
 
-// acc[mi][ni][2] += A(64 x K, smem, row stride lda) * B(K x 128), B(k, n) = W[n * K + k]
+// b[ni] = B(4 ks + t, 32 slab + 8 ni + g) of a fragment-major operand with
+// `nslab` column slabs: 32 contiguous bytes per lane, 1 KB per warp
+__device__ __forceinline__ void load_bfrag(const double *__restrict__ Bf, int ks, int nslab, int slab, int lane,
+                                           double (&b)[4]) {
+  const double2 *q = reinterpret_cast<const double2 *>(Bf + ((size_t)(ks * nslab + slab) * 32 + lane) * 4);
+  const double2 x = __ldg(q), y = __ldg(q + 1);
+  b[0] = x.x;
+  b[1] = x.y;
+  b[2] = y.x;
+  b[3] = y.y;
+}
+
+// warp tile 32 x 32 (rows 32 wm.., cols 32 wn..):
+// acc += A(64 x K, smem, row stride lda) * B(K x 128, fragment-major)
 template <int K>
-__device__ inline void mma_rows_wT(double (&acc)[4][4][2], const double *A, int lda, const double *__restrict__ W,
-                                   int wm, int wn, int g, int t) {
+__device__ inline void mma_32x32(double (&acc)[4][4][2], const double *A, int lda, const double *__restrict__ Bf,
+                                 int wm, int wn, int lane) {
+  const int g = lane >> 2, t = lane & 3;
 #pragma unroll 4
-  for (int k0 = 0; k0 < K; k0 += 4) {
+  for (int ks = 0; ks < K / 4; ++ks) {
     double a[4], b[4];
 #pragma unroll
-    for (int mi = 0; mi < 4; ++mi) a[mi] = A[(wm * 32 + mi * 8 + g) * lda + k0 + t];
-#pragma unroll
-    for (int ni = 0; ni < 4; ++ni) b[ni] = __ldg(W + (wn * 32 + ni * 8 + g) * K + k0 + t);
+    for (int mi = 0; mi < 4; ++mi) a[mi] = A[(wm * 32 + mi * 8 + g) * lda + 4 * ks + t];
+    load_bfrag(Bf, ks, 4, wn, lane, b);
 #pragma unroll
     for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
@@ -74,34 +89,32 @@ __device__ inline void mma_rows_wT(double (&acc)[4][4][2], const double *A, int 
   }
 }
 
-// acc[mi][ni][2] += A(64 x 128, smem) * B(128 x 128), B(k, n) = W[k * 128 + n]
-__device__ inline void mma_rows_w(double (&acc)[4][4][2], const double *A, const double *__restrict__ W, int wm,
-                                  int wn, int g, int t) {
+// warp tile 8 x 32 (rows row0..row0+7, all 32 columns), two K halves as
+// independent accumulation chains: acc += A(rows, K, smem lda) * B(K x 32, fragment-major)
+template <int K>
+__device__ inline void mma_8x32(double (&acc)[4][2], const double *A, int lda, int row0,
+                                const double *__restrict__ Bf, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  double acc2[4][2];
+#pragma unroll
+  for (int ni = 0; ni < 4; ++ni) acc2[ni][0] = acc2[ni][1] = 0.0;
 #pragma unroll 4
-  for (int k0 = 0; k0 < 128; k0 += 4) {
-    double a[4], b[4];
-#pragma unroll
-    for (int mi = 0; mi < 4; ++mi) a[mi] = A[(wm * 32 + mi * 8 + g) * LDU + k0 + t];
-#pragma unroll
-    for (int ni = 0; ni < 4; ++ni) b[ni] = __ldg(W + (k0 + t) * 128 + wn * 32 + ni * 8 + g);
-#pragma unroll
-    for (int mi = 0; mi < 4; ++mi)
-#pragma unroll
-      for (int ni = 0; ni < 4; ++ni) dmma(acc[mi][ni][0], acc[mi][ni][1], a[mi], b[ni]);
-  }
-}
-
-// acc[ni][2] (8 rows x 32 cols per warp) += A(8 rows at row0, K=128, smem LDU) * B(128 x 32), B(k, n) = W[k*32 + n]
-__device__ inline void mma_8x32_w(double (&acc)[4][2], const double *A, int row0, const double *__restrict__ W, int g,
-                                  int t) {
-#pragma unroll 4
-  for (int k0 = 0; k0 < 128; k0 += 4) {
-    const double a = A[(row0 + g) * LDU + k0 + t];
+  for (int ks = 0; ks < K / 8; ++ks) {
+    const double a0 = A[(row0 + g) * lda + 4 * ks + t];
+    const double a1 = A[(row0 + g) * lda + K / 2 + 4 * ks + t];
+    double b0[4], b1[4];
+    load_bfrag(Bf, ks, 1, 0, lane, b0);
+    load_bfrag(Bf, ks + K / 8, 1, 0, lane, b1);
 #pragma unroll
     for (int ni = 0; ni < 4; ++ni) {
-      const double b = __ldg(W + (k0 + t) * 32 + ni * 8 + g);
-      dmma(acc[ni][0], acc[ni][1], a, b);
+      dmma(acc[ni][0], acc[ni][1], a0, b0[ni]);
+      dmma(acc2[ni][0], acc2[ni][1], a1, b1[ni]);
     }
+  }
+#pragma unroll
+  for (int ni = 0; ni < 4; ++ni) {
+    acc[ni][0] += acc2[ni][0];
+    acc[ni][1] += acc2[ni][1];
   }
 }
 
@@ -149,7 +162,7 @@ __global__ void __launch_bounds__(256) k_filter_forward(int P, const double *__r
     for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
       for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
-    mma_rows_wT<kR>(acc, rbf, LDR, W.w0, wm, wn, g, t);
+    mma_32x32<kR>(acc, rbf, LDR, W.w0t_f, wm, wn, lane);
 #pragma unroll
     for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
@@ -160,8 +173,8 @@ __global__ void __launch_bounds__(256) k_filter_forward(int P, const double *__r
         acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
       }
     __syncthreads();
-    mma_rows_wT<kF>(acc, u, LDU, W.w1, wm, wn, g, t);
-    mma_rows_wT<kEH>(acc, w, LDR, W.v1, wm, wn, g, t);
+    mma_32x32<kF>(acc, u, LDU, W.w1t_f, wm, wn, lane);
+    mma_32x32<kEH>(acc, w, LDR, W.v1t_f, wm, wn, lane);
 #pragma unroll
     for (int mi = 0; mi < 4; ++mi) {
       const int row = wm * 32 + mi * 8 + g;
@@ -231,56 +244,43 @@ __device__ inline void stage_rows(double *dst, int lds, const double *src, int p
   }
 }
 
-// acc (8 rows x 32 cols per warp, two independent K halves) += A(64 x 128, smem LDU) * B(128 x 32),
-// B(k, n) = W[k*32 + n]
-__device__ inline void mma_8x32_w2(double (&acc)[4][2], const double *A, int row0, const double *__restrict__ W,
-                                   int g, int t) {
-  double acc2[4][2];
-#pragma unroll
-  for (int ni = 0; ni < 4; ++ni) acc2[ni][0] = acc2[ni][1] = 0.0;
-#pragma unroll 4
-  for (int k0 = 0; k0 < 64; k0 += 4) {
-    const double a0 = A[(row0 + g) * LDU + k0 + t];
-    const double a1 = A[(row0 + g) * LDU + 64 + k0 + t];
-#pragma unroll
-    for (int ni = 0; ni < 4; ++ni) {
-      const double b0 = __ldg(W + (k0 + t) * 32 + ni * 8 + g);
-      const double b1 = __ldg(W + (64 + k0 + t) * 32 + ni * 8 + g);
-      dmma(acc[ni][0], acc[ni][1], a0, b0);
-      dmma(acc2[ni][0], acc2[ni][1], a1, b1);
-    }
-  }
-#pragma unroll
-  for (int ni = 0; ni < 4; ++ni) {
-    acc[ni][0] += acc2[ni][0];
-    acc[ni][1] += acc2[ni][1];
-  }
-}
 }  // namespace
 
-__global__ void __launch_bounds__(256) k_filter_reverse(
+// One cluster of two CTAs per tile of TP pairs: CTA rank 0 pushes the gradient
+// of the invariant filter through its MLP, rank 1 that of the ev filter. Each
+// CTA holds one 64 x 128 gradient tile (109 KB of shared memory, <= 128
+// registers per thread), so two CTAs fit on an SM. The radial-basis and L0
+// gradients of rank 1 are read by rank 0 through distributed shared memory and
+// added to its own (rank 0 + rank 1, a fixed order), and rank 0 finishes the
+// pair: radial/cutoff derivative, spherical-harmonic VJP, Cartesian gradient.
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_reverse(
     int P, const double *__restrict__ geo, const int *__restrict__ pa, const int *__restrict__ pb,
     const double *__restrict__ ev, const double *__restrict__ cg, FilterW finv, FilterW fev, RadialW rad,
     const double *__restrict__ g_filt_inv, const double *__restrict__ g_filt_ev, const double *__restrict__ gA,
     const double *__restrict__ pair_sc, int need_l0, double *__restrict__ gv, double *__restrict__ gl0) {
+  namespace cgrp = cooperative_groups;
+  cgrp::cluster_group cluster = cgrp::this_cluster();
+  const int f = static_cast<int>(cluster.block_rank());  // 0: invariant filter, 1: ev filter
   extern __shared__ double sm[];
-  double *gFi = sm;                    // TP x LDU  (filter-inv gradient, later its hidden gradient)
-  double *gFe = gFi + TP * LDU;        // TP x LDU  (filter-ev gradient)
-  double *rbf = gFe + TP * LDU;        // TP x LDR
-  double *gw = rbf + TP * LDR;         // TP x LDR
-  double *sc = gw + TP * LDR;          // TP x 32
-  double *geos = sc + TP * kPairScalars;  // TP x 8
-  double *l0 = geos + TP * kGeo;       // TP x 4
-  double *gl = l0 + TP * 4;            // TP x 4
-  double *rr = gl + TP * 4;            // TP
-  const int p0 = blockIdx.x * TP;
+  double *gF = sm;                // TP x LDU: filter gradient, then the hidden pre-activation gradient
+  double *rbf = gF + TP * LDU;    // TP x LDR
+  double *gw = rbf + TP * LDR;    // TP x LDR: ev-hidden gradient, then the radial-basis gradient
+  double *l0 = gw + TP * LDR;     // TP x 4
+  double *gl = l0 + TP * 4;       // TP x 4
+  double *rr = gl + TP * 4;       // TP
+  const int p0 = (blockIdx.x >> 1) * TP;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int wm = warp >> 2, wn = warp & 3;
-  stage_rows<kF>(gFi, LDU, g_filt_inv, p0, P);
-  stage_rows<kPairScalars>(sc, kPairScalars, pair_sc, p0, P);
-  stage_rows<kGeo>(geos, kGeo, geo, p0, P);
-  cp_async_commit();
-  stage_rows<kF>(gFe, LDU, g_filt_ev, p0, P);
+  // this CTA's filter (selected field by field so the parameters stay in registers)
+  const double *w1_f = f ? fev.w1_f : finv.w1_f;
+  const double *w0t_f = f ? fev.w0t_f : finv.w0t_f;
+  const double *v1_f = f ? fev.v1_f : finv.v1_f;
+  const double *w0_f = f ? fev.w0_f : finv.w0_f;
+  const double *b0 = f ? fev.b0 : finv.b0;
+  const double *v0 = f ? fev.v0 : finv.v0;
+  const double *c0 = f ? fev.c0 : finv.c0;
+
+  stage_rows<kF>(gF, LDU, f ? g_filt_ev : g_filt_inv, p0, P);
   cp_async_commit();
   if (tid < TP) {
     const int p = p0 + tid;
@@ -290,93 +290,114 @@ __global__ void __launch_bounds__(256) k_filter_reverse(
   compute_l0(P, p0, pa, pb, need_l0 ? ev : nullptr, cg, l0);
   __syncthreads();
   compute_rbf(rr, rbf, rad);
-  double grbf_acc[4][2];
-#pragma unroll
-  for (int ni = 0; ni < 4; ++ni) grbf_acc[ni][0] = grbf_acc[ni][1] = 0.0;
+  cp_async_wait<0>();
+  __syncthreads();
 
-  for (int filt = 0; filt < 2; ++filt) {
-    const FilterW &W = filt ? fev : finv;
-    double *gF = filt ? gFe : gFi;
-    if (filt == 0) cp_async_wait<1>(); else cp_async_wait<0>();
-    __syncthreads();
-    // recompute the hidden pre-activation of the rbf branch: sp = silu'(rbf W0^T + b0)
-    double sp[4][4][2];
+  // gradient of the hidden layer: (gF W1) * silu'(rbf W0^T + b0), warp tile 32 x 32
+  double acc[4][4][2];
 #pragma unroll
-    for (int mi = 0; mi < 4; ++mi)
+  for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
-      for (int ni = 0; ni < 4; ++ni) sp[mi][ni][0] = sp[mi][ni][1] = 0.0;
-    mma_rows_wT<kR>(sp, rbf, LDR, W.w0, wm, wn, g, t);
+    for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
+  mma_32x32<kF>(acc, gF, LDU, w1_f, wm, wn, lane);
 #pragma unroll
-    for (int mi = 0; mi < 4; ++mi)
+  for (int mi = 0; mi < 4; ++mi) {  // recompute the pre-activation one 8-row block at a time
+    double pre[4][2];
 #pragma unroll
-      for (int ni = 0; ni < 4; ++ni) {
-        const int col = wn * 32 + ni * 8 + 2 * t;
-        sp[mi][ni][0] = silu_prime(sp[mi][ni][0] + W.b0[col]);
-        sp[mi][ni][1] = silu_prime(sp[mi][ni][1] + W.b0[col + 1]);
-      }
-    // g_hidden = gF W1 (B(k=c, n=j) = W1[c][j]) then times silu'
-    double acc[4][4][2];
+    for (int ni = 0; ni < 4; ++ni) pre[ni][0] = pre[ni][1] = 0.0;
 #pragma unroll
-    for (int mi = 0; mi < 4; ++mi)
+    for (int ks = 0; ks < kR / 4; ++ks) {
+      const double a = rbf[(wm * 32 + mi * 8 + g) * LDR + 4 * ks + t];
+      double b[4];
+      load_bfrag(w0t_f, ks, 4, wn, lane, b);
 #pragma unroll
-      for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
-    mma_rows_w(acc, gF, W.w1, wm, wn, g, t);
-    // ev branch: g_w = gF V1 (64 x 32), warp w owns rows 8w..8w+7
-    double gwa[4][2];
-#pragma unroll
-    for (int ni = 0; ni < 4; ++ni) gwa[ni][0] = gwa[ni][1] = 0.0;
-    mma_8x32_w2(gwa, gF, warp * 8, W.v1, g, t);
-    __syncthreads();  // everyone is done reading gF
-#pragma unroll
-    for (int mi = 0; mi < 4; ++mi)
-#pragma unroll
-      for (int ni = 0; ni < 4; ++ni) {
-        const int row = wm * 32 + mi * 8 + g, col = wn * 32 + ni * 8 + 2 * t;
-        gF[row * LDU + col] = acc[mi][ni][0] * sp[mi][ni][0];
-        gF[row * LDU + col + 1] = acc[mi][ni][1] * sp[mi][ni][1];
-      }
+      for (int ni = 0; ni < 4; ++ni) dmma(pre[ni][0], pre[ni][1], a, b[ni]);
+    }
 #pragma unroll
     for (int ni = 0; ni < 4; ++ni) {
-      const int row = warp * 8 + g, col = ni * 8 + 2 * t;
-      gw[row * LDR + col] = gwa[ni][0];
-      gw[row * LDR + col + 1] = gwa[ni][1];
+      const int col = wn * 32 + ni * 8 + 2 * t;
+      acc[mi][ni][0] *= silu_prime(pre[ni][0] + b0[col]);
+      acc[mi][ni][1] *= silu_prime(pre[ni][1] + b0[col + 1]);
     }
-    __syncthreads();
-    // g_rbf += g_pre W0 (B(k=j, n=k') = W0[j][k'], W0 is [128][32])
-    mma_8x32_w2(grbf_acc, gF, warp * 8, W.w0, g, t);
-    // L0 gradient: g_pe = g_w * silu'(L0 V0^T + c0) (one element per thread-slot,
-    // in place in gw), then gl[d] += sum_j g_pe[j] V0[j][d]
-    if (need_l0) {
-      {
-        const int pl = tid >> 2, j0 = (tid & 3) * 8;
-        const double l00 = l0[pl * 4], l01 = l0[pl * 4 + 1], l02 = l0[pl * 4 + 2], l03 = l0[pl * 4 + 3];
-#pragma unroll
-        for (int j = j0; j < j0 + 8; ++j) {
-          const double pe = l00 * W.v0[j * 4] + l01 * W.v0[j * 4 + 1] + l02 * W.v0[j * 4 + 2] + l03 * W.v0[j * 4 + 3] + W.c0[j];
-          gw[pl * LDR + j] *= silu_prime(pe);
-        }
-      }
-      __syncthreads();
-      const int pl = tid >> 2, d = tid & 3;
-      double s = 0.0;
-#pragma unroll 8
-      for (int j = 0; j < kEH; ++j) s += gw[pl * LDR + j] * W.v0[j * 4 + d];
-      gl[pl * 4 + d] += s;
-    }
-    __syncthreads();
   }
-  // g_rbf -> smem (reuse gw)
+  // ev branch: g_w = gF V1 (64 x 32), warp w owns rows 8w..8w+7
+  double gwa[4][2];
+#pragma unroll
+  for (int ni = 0; ni < 4; ++ni) gwa[ni][0] = gwa[ni][1] = 0.0;
+  mma_8x32<kF>(gwa, gF, LDU, warp * 8, v1_f, lane);
+  __syncthreads();  // every warp is done reading gF
+#pragma unroll
+  for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni) {
+      const int row = wm * 32 + mi * 8 + g, col = wn * 32 + ni * 8 + 2 * t;
+      gF[row * LDU + col] = acc[mi][ni][0];
+      gF[row * LDU + col + 1] = acc[mi][ni][1];
+    }
 #pragma unroll
   for (int ni = 0; ni < 4; ++ni) {
     const int row = warp * 8 + g, col = ni * 8 + 2 * t;
-    gw[row * LDR + col] = grbf_acc[ni][0];
-    gw[row * LDR + col + 1] = grbf_acc[ni][1];
+    gw[row * LDR + col] = gwa[ni][0];
+    gw[row * LDR + col + 1] = gwa[ni][1];
   }
   __syncthreads();
+  // radial-basis gradient g_rbf = g_pre W0 (64 x 32)
+  double grb[4][2];
+#pragma unroll
+  for (int ni = 0; ni < 4; ++ni) grb[ni][0] = grb[ni][1] = 0.0;
+  mma_8x32<kF>(grb, gF, LDU, warp * 8, w0_f, lane);
+  // L0 gradient: g_pe = g_w * silu'(L0 V0^T + c0), gl[d] = sum_j g_pe[j] V0[j][d]
+  if (need_l0) {
+    {
+      const int pl = tid >> 2, j0 = (tid & 3) * 8;
+      const double l00 = l0[pl * 4], l01 = l0[pl * 4 + 1], l02 = l0[pl * 4 + 2], l03 = l0[pl * 4 + 3];
+#pragma unroll
+      for (int j = j0; j < j0 + 8; ++j) {
+        const double pe = l00 * v0[j * 4] + l01 * v0[j * 4 + 1] + l02 * v0[j * 4 + 2] + l03 * v0[j * 4 + 3] + c0[j];
+        gw[pl * LDR + j] *= silu_prime(pe);
+      }
+    }
+    __syncthreads();
+    const int pl = tid >> 2, d = tid & 3;
+    double s = 0.0;
+#pragma unroll 8
+    for (int j = 0; j < kEH; ++j) s += gw[pl * LDR + j] * v0[j * 4 + d];
+    gl[pl * 4 + d] = s;
+  }
+  __syncthreads();  // gw and gF reads are done
+#pragma unroll
+  for (int ni = 0; ni < 4; ++ni) {
+    const int row = warp * 8 + g, col = ni * 8 + 2 * t;
+    gw[row * LDR + col] = grb[ni][0];
+    gw[row * LDR + col + 1] = grb[ni][1];
+  }
+  // rank 0 prefetches the tail's per-pair inputs into the free gF region
+  double *sc = gF;                        // TP x 32
+  double *geos = sc + TP * kPairScalars;  // TP x 8
+  double *ybuf = geos + TP * kGeo;        // TP x kEV
+  if (f == 0) {
+    stage_rows<kPairScalars>(sc, kPairScalars, pair_sc, p0, P);
+    stage_rows<kGeo>(geos, kGeo, geo, p0, P);
+    cp_async_commit();
+  }
+  cluster.sync();  // both CTAs' radial-basis and L0 gradients are in shared memory
+  if (f == 0) {
+    const double *rgw = cluster.map_shared_rank(gw, 1);
+    const double *rgl = cluster.map_shared_rank(gl, 1);
+    for (int idx = tid; idx < TP * kR; idx += blockDim.x) {
+      const int row = idx / kR, c = idx % kR;
+      gw[row * LDR + c] += rgw[row * LDR + c];
+    }
+    gl[tid] += rgl[tid];
+  }
+  cluster.sync();  // rank 1 stays resident until rank 0 has read its shared memory
+  if (f != 0) return;
+  cp_async_wait<0>();
+  __syncthreads();
+
   // per pair, phase 1 (warp per pair): radial + cutoff gradient and the
   // harmonic gradient gY (pair orientation) -> shared memory
-  double *grs = l0;     // TP radial gradients (the L0 inputs are no longer needed)
-  double *ybuf = gFe;   // TP x kEV harmonic gradients (the ev filter tile is no longer needed)
+  double *grs = l0;  // TP radial gradients (the L0 inputs are no longer needed)
   for (int pl = warp; pl < TP; pl += 8) {
     const int p = p0 + pl;
     if (p >= P) continue;
@@ -431,16 +452,16 @@ void launch_filter_reverse(int P, const double *geo, const int *pair_a, const in
                            const double *g_filt_inv, const double *g_filt_ev, const double *gA,
                            const double *pair_sc, bool need_l0, double *gv, double *gl0, cudaStream_t s) {
   if (P == 0) return;
-  const size_t smem =
-      sizeof(double) * (2 * TP * LDU + 2 * TP * LDR + TP * kPairScalars + TP * kGeo + TP * 8 + TP);
+  const size_t smem = sizeof(double) * (TP * LDU + 2 * TP * LDR + 8 * TP + TP);
+  static_assert(TP * (kPairScalars + kGeo + kEV) <= TP * LDU, "tail inputs must fit in the gradient tile");
   static bool configured = false;
   if (!configured) {
     SO3_CUDA(cudaFuncSetAttribute(k_filter_reverse, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     configured = true;
   }
-  k_filter_reverse<<<(P + TP - 1) / TP, 256, smem, s>>>(P, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad,
-                                                         g_filt_inv, g_filt_ev, gA, pair_sc, need_l0 ? 1 : 0, gv,
-                                                         gl0);
+  const int tiles = (P + TP - 1) / TP;
+  k_filter_reverse<<<2 * tiles, 256, smem, s>>>(P, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad, g_filt_inv,
+                                                g_filt_ev, gA, pair_sc, need_l0 ? 1 : 0, gv, gl0);
   SO3_LAUNCH("filter_reverse");
 }
 
