@@ -37,6 +37,11 @@ __device__ inline void degree_sums(double v, double out[4]) {
   }
 }
 
+// v[i] for a runtime index without dynamic register-array indexing
+__device__ inline double pick4(const double (&v)[4], int i) {
+  return i == 0 ? v[0] : (i == 1 ? v[1] : (i == 2 ? v[2] : v[3]));
+}
+
 __device__ inline void load4(const double *p, double (&v)[4]) {
   const double2 a = *reinterpret_cast<const double2 *>(p);
   const double2 b = *reinterpret_cast<const double2 *>(p + 2);
@@ -142,10 +147,28 @@ __global__ void __launch_bounds__(256) k_attention_reverse(
   double gq[4] = {0, 0, 0, 0}, gk[4] = {0, 0, 0, 0}, gv[4] = {0, 0, 0, 0}, gqe[4] = {0, 0, 0, 0},
          gke[4] = {0, 0, 0, 0};
   const double inv_norm = 1.0 / norm;
-  for (int e = row_start[r]; e < row_start[r + 1]; ++e) {
-    const int b = nbr[e];
-    const int code = edge_pair[e];
+  const int e0 = row_start[r], e1 = row_start[r + 1];
+  int b_nx = 0, code_nx = 0;
+  if (e0 < e1) { b_nx = nbr[e0]; code_nx = edge_pair[e0]; }
+  for (int e = e0; e < e1; ++e) {
+    const int b = b_nx;
+    const int code = code_nx;
+    if (e + 1 < e1) { b_nx = nbr[e + 1]; code_nx = edge_pair[e + 1]; }
     const int p = code >= 0 ? code : ~code;
+    if (e + 1 < e1) {  // pull the next edge's rows into L1 while this one is processed
+      const int p_nx = code_nx >= 0 ? code_nx : ~code_nx;
+      // 68 prefetches: qkv row (40 lines of 128 B), g_a, f_inv, f_ev (8 each), g_A and sh (two 96-byte halves each)
+      for (int c = lane; c < 68; c += 32) {
+        const char *addr;
+        if (c < 40) addr = reinterpret_cast<const char *>(qkv + (size_t)b_nx * kQKV) + 128 * c;
+        else if (c < 48) addr = reinterpret_cast<const char *>(g_a + (size_t)b_nx * kF) + 128 * (c - 40);
+        else if (c < 56) addr = reinterpret_cast<const char *>(f_inv + (size_t)p_nx * kF) + 128 * (c - 48);
+        else if (c < 64) addr = reinterpret_cast<const char *>(f_ev + (size_t)p_nx * kF) + 128 * (c - 56);
+        else if (c < 66) addr = reinterpret_cast<const char *>(g_A + (size_t)b_nx * kEV) + 96 * (c - 64);
+        else addr = reinterpret_cast<const char *>(sh + (size_t)p_nx * kEV) + 96 * (c - 66);
+        asm volatile("prefetch.global.L1 [%0];\n" ::"l"(addr));
+      }
+    }
     const double phi = geo[(size_t)p * kGeo + 4];
     const double *b_row = qkv + (size_t)b * kQKV + head_off;
     double qb[4], kb[4], vb[4], qeb[4], keb[4], gb[4], fi[4], fe[4];
@@ -159,7 +182,6 @@ __global__ void __launch_bounds__(256) k_attention_reverse(
     load4(f_ev + (size_t)p * kF + lane * 4, fe);
     const double gAb = lane < kEV ? g_A[(size_t)b * kEV + lane] : 0.0;
     double y = lane < kEV ? sh[(size_t)p * kEV + lane] : 0.0;
-    // y_in: harmonic of edge b->a; y_out: of a->b (= parity * y_in)
     const double y_in = code < 0 ? y * my_par : y;
     const double y_out = y_in * my_par;
     double ai_in = 0, ae_in = 0, ai_out = 0, ae_out = 0, si_in = 0, si_out = 0;
@@ -178,10 +200,15 @@ __global__ void __launch_bounds__(256) k_attention_reverse(
     ae_out = head_sum(ae_out) / norm;
     si_in = head_sum(si_in);
     si_out = head_sum(si_out);
+    double se_in, se_out, se_in_q, se_out_q;
+    const int qsel = lane >> 2, hh = lane & 3;
     double se_in_d[4], se_out_d[4];
     degree_sums(gAa * y_in, se_in_d);
     degree_sums(gAb * y_out, se_out_d);
-    const double se_in = se_in_d[h], se_out = se_out_d[h];
+    se_in = pick4(se_in_d, h);
+    se_out = pick4(se_out_d, h);
+    se_in_q = pick4(se_in_d, hh);
+    se_out_q = pick4(se_out_d, hh);
     const double c_q = phi * si_in * inv_norm, c_qe = phi * se_in * inv_norm;
     const double c_v = phi * ai_out, c_k = phi * si_out * inv_norm, c_ke = phi * se_out * inv_norm;
 #pragma unroll
@@ -193,12 +220,7 @@ __global__ void __launch_bounds__(256) k_attention_reverse(
       gke[j] += c_ke * (qeb[j] * fe[j]);
     }
     if (code >= 0 && g_filt_inv != nullptr) {
-      // primary edge: the filter gradient of the pair, both directions summed
-      //   g_f_inv[c] = phi/norm (s_in[h] q_a[c] k_b[c] + s_out[h] q_b[c] k_a[c]), same for ev
       double gi[4], ge[4];
-      // explicitly rounded products and sum (no FMA contraction): the two
-      // directions' terms swap when the pair is held from its other endpoint,
-      // and a rounded sum is exactly commutative
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         gi[j] = __dadd_rn(__dmul_rn(c_q, __dmul_rn(qa[j], kb[j])), __dmul_rn(c_k, __dmul_rn(qb[j], ka[j])));
@@ -208,9 +230,6 @@ __global__ void __launch_bounds__(256) k_attention_reverse(
       store4(g_filt_ev + (size_t)p * kF + lane * 4, ge);
     }
     if (code >= 0) {
-      // primary edge: "in" is into the pair's primary receiver a
-      // lanes: quantity = lane / 4, head = lane % 4
-      const int qsel = lane >> 2, hh = lane & 3;
       const double v_ai_in = __shfl_sync(0xffffffffu, ai_in, hh * 8);
       const double v_ae_in = __shfl_sync(0xffffffffu, ae_in, hh * 8);
       const double v_si_in = __shfl_sync(0xffffffffu, si_in, hh * 8);
@@ -222,11 +241,11 @@ __global__ void __launch_bounds__(256) k_attention_reverse(
         case 0: val = v_ai_in; break;
         case 1: val = v_ae_in; break;
         case 2: val = v_si_in; break;
-        case 3: val = se_in_d[hh]; break;
+        case 3: val = se_in_q; break;
         case 4: val = v_ai_out; break;
         case 5: val = v_ae_out; break;
         case 6: val = v_si_out; break;
-        default: val = se_out_d[hh]; break;
+        default: val = se_out_q; break;
       }
       pair_sc[(size_t)p * kPairScalars + lane] = val;
     }

@@ -108,43 +108,70 @@ void launch_pair_geometry(int P, const NeighborState &nb, const int *z, ZblDev z
 // ---------------------------------------------------------------------------
 // long range: erf-screened shifted-force Coulomb + QDO dispersion
 // ---------------------------------------------------------------------------
-__device__ inline void smooth_switch(double r, double cuton, double cutoff, double &v, double &dv) {
+// Smooth switch of physical_long_range.cpp: v = s_l / (s_l + s_r + 1e-12) with
+// s_l = exp(-1/left), s_r = exp(-1/right), c = (r - cuton) / width, left = 1 - c,
+// right = c (each clamped below at 1e-12 inside the exponent), and its derivative
+// dv/dr. The divisions of the textbook form are folded into two reciprocals.
+__device__ inline void smooth_switch(double r, double cuton, double cutoff, double inv_width, double &v,
+                                     double &dv) {
   if (r >= cutoff) {
     v = 0.0;
     dv = 0.0;
     return;
   }
-  const double width = cutoff - cuton;
-  const double c = (r - cuton) / width;
+  const double c = (r - cuton) * inv_width;
   const double left = 1.0 - c, right = c;
   const double sl = left > 1.0e-12 ? left : 1.0e-12, sr = right > 1.0e-12 ? right : 1.0e-12;
-  const double sig_l = left > 0.0 ? exp(-1.0 / sl) : 0.0;
-  const double sig_r = right > 0.0 ? exp(-1.0 / sr) : 0.0;
+  const double inv_lr = 1.0 / (sl * sr);
+  const double isl = sr * inv_lr, isr = sl * inv_lr;  // 1/sl, 1/sr
+  const double sig_l = left > 0.0 ? exp(-isl) : 0.0;
+  const double sig_r = right > 0.0 ? exp(-isr) : 0.0;
   const double den = sig_l + sig_r + 1.0e-12;
-  v = sig_l / den;
-  const double dl = left > 0.0 ? -sig_l / (sl * sl) : 0.0;
-  const double dr = right > 0.0 ? sig_r / (sr * sr) : 0.0;
-  dv = ((dl * den - sig_l * (dl + dr)) / (den * den)) / width;
+  const double iden = 1.0 / den;
+  v = sig_l * iden;
+  const double dl = left > 0.0 ? -sig_l * isl * isl : 0.0;
+  const double dr = right > 0.0 ? sig_r * isr * isr : 0.0;
+  // (dl den - s_l (dl + dr)) / den^2 / width
+  dv = (dl - v * (dl + dr)) * iden * inv_width;
 }
 
 struct LrPair {
   double e_elec, e_disp, dq, dh, radial;
 };
 
+// per-launch constants of the pair term, computed once per thread
+struct LrConst {
+  double inv_sigma, inv_elec_width, inv_disp_width, inv_bohr;
+};
+__device__ inline LrConst lr_const(const LrDev &p) {
+  LrConst c;
+  c.inv_sigma = 1.0 / p.sigma;
+  c.inv_elec_width = 1.0 / (p.cutoff - p.elec_cuton);
+  c.inv_disp_width = 1.0 / (p.cutoff - p.disp_cuton);
+  c.inv_bohr = 1.0 / p.bohr;
+  return c;
+}
+
 // One unordered pair seen from atom i (its partner j); r > 0 and r < cutoff.
 // ai0/aj0, ci0/cj0: reference polarisabilities and C6 of the two elements
 // (aj0 < 0 marks an element without reference data: no dispersion).
-__device__ inline LrPair lr_pair_tab(const LrDev &p, double r, double qi, double qj, double hi, double hj,
-                                     double ai0, double aj0, double ci0, double cj0) {
+// Arithmetic of physical_long_range.cpp:11-380 (erf-screened shifted-force
+// Coulomb with its switch; QDO dispersion with C6 mixing, the fitted sigma(R_vdW)
+// polynomial and its switch), with shared reciprocals instead of repeated
+// divisions (about 10 divisions per pair instead of 49).
+__device__ inline LrPair lr_pair_tab(const LrDev &p, const LrConst &k, double r, double qi, double qj, double hi,
+                                     double hj, double ai0, double aj0, double ci0, double cj0) {
   constexpr double inv_sqrt_pi = 0.56418958354775628695;
+  constexpr double inv7 = 1.0 / 7.0;
   LrPair o{0, 0, 0, 0, 0};
   double esw, desw;
-  smooth_switch(r, p.elec_cuton, p.cutoff, esw, desw);
-  const double ratio = r / p.sigma;
+  smooth_switch(r, p.elec_cuton, p.cutoff, k.inv_elec_width, esw, desw);
+  const double inv_r = 1.0 / r;
+  const double ratio = r * k.inv_sigma;
   const double erf_t = erf(ratio);
   const double exp_t = exp(-(ratio * ratio));
-  const double pot = erf_t / r;
-  const double dpot = (2.0 * r * exp_t * inv_sqrt_pi / p.sigma - erf_t) / (r * r);
+  const double pot = erf_t * inv_r;
+  const double dpot = (2.0 * r * exp_t * inv_sqrt_pi * k.inv_sigma - erf_t) * (inv_r * inv_r);
   const double disp = r - p.cutoff;
   const double shifted = pot - p.shift - p.fshift * disp;
   const double kernel = esw * (pot - p.shift) + (1.0 - esw) * shifted;
@@ -160,44 +187,48 @@ __device__ inline LrPair lr_pair_tab(const LrDev &p, double r, double qi, double
     const double num = 2.0 * c6i * c6j * aj * ai;
     const double den = ai * ai * c6j + aj * aj * c6i;
     if (alpha > 0.0 && den > 1.0e-30) {
-      const double c6 = num / den;
-      const double inv_den2 = 1.0 / (den * den);
+      const double iden = 1.0 / den;
+      const double c6 = num * iden;
       const double dc6i = 2.0 * ci0 * hi;
       const double dn_dhi = 2.0 * (dc6i * c6j * aj * ai + c6i * c6j * aj * ai0);
       const double dd_dhi = 2.0 * ai * ai0 * c6j + aj * aj * dc6i;
-      const double dc6_dhi = (dn_dhi * den - num * dd_dhi) * inv_den2;
-      const double a7 = pow(alpha, 1.0 / 7.0);
+      const double dc6_dhi = (dn_dhi * den - num * dd_dhi) * (iden * iden);
+      const double ialpha7 = inv7 / alpha;  // 1 / (7 alpha)
+      const double a7 = exp(log(alpha) * inv7);
       const double rv = p.fine_factor * a7;
       constexpr double b0 = -0.00433008, b1 = 0.24428889, b2 = 0.04125273, b3 = -0.00078893;
       const double sig = b3 * rv * rv * rv + b2 * rv * rv + b1 * rv + b0;
-      const double gam = 0.5 / (sig * sig);
-      const double drv = rv / (7.0 * alpha);
+      const double isig = 1.0 / sig;
+      const double gam = 0.5 * isig * isig;
+      const double igam = 2.0 * sig * sig;  // 1 / gam
+      const double drv = rv * ialpha7;
       const double dsig = (3.0 * b3 * rv * rv + 2.0 * b2 * rv + b1) * drv;
-      const double dgam = -2.0 * gam * dsig / sig;
-      const double c8 = 5.0 * c6 / gam;
-      const double c10 = 245.0 * c6 / (8.0 * gam * gam);
+      const double dgam = -2.0 * gam * dsig * isig;
+      const double c8 = 5.0 * c6 * igam;
+      const double c10 = 245.0 * c6 * (igam * igam) * 0.125;
       const double damp = p.disp_scale * 2.0 * 2.54 * a7;
-      const double ddamp = damp / (7.0 * alpha);
-      const double ra = r / p.bohr;
+      const double ddamp = damp * ialpha7;
+      const double ra = r * k.inv_bohr;
       const double r2 = ra * ra, r4 = r2 * r2, r6 = r4 * r2, r8 = r4 * r4, r10 = r8 * r2;
       const double p2 = damp * damp, p4 = p2 * p2, p6 = p4 * p2, p8 = p4 * p4, p10 = p8 * p2;
       const double d6 = r6 + p6, d8 = r8 + p8, d10 = r10 + p10;
-      const double qdo = -c6 / d6 - c8 / d8 - c10 / d10;
-      const double rad_au = 6.0 * c6 * r4 * ra / (d6 * d6) + 8.0 * c8 * r6 * ra / (d8 * d8) +
-                            10.0 * c10 * r8 * ra / (d10 * d10);
-      const double dc8 = -c8 * dgam / gam;
-      const double dc10 = -2.0 * c10 * dgam / gam;
+      const double id6 = 1.0 / d6, id8 = 1.0 / d8, id10 = 1.0 / d10;
+      const double qdo = -c6 * id6 - c8 * id8 - c10 * id10;
+      const double rad_au =
+          (6.0 * c6 * r4 * id6 * id6 + 8.0 * c8 * r6 * id8 * id8 + 10.0 * c10 * r8 * id10 * id10) * ra;
+      const double dc8 = -c8 * dgam * igam;
+      const double dc10 = -2.0 * c10 * dgam * igam;
       const double dd6 = 6.0 * p4 * damp * ddamp;
       const double dd8 = 8.0 * p6 * damp * ddamp;
       const double dd10 = 10.0 * p8 * damp * ddamp;
-      const double dpot_da = c6 * dd6 / (d6 * d6) - dc8 / d8 + c8 * dd8 / (d8 * d8) - dc10 / d10 +
-                             c10 * dd10 / (d10 * d10);
-      const double dpot_dc6 = -1.0 / d6 - (5.0 / gam) / d8 - (245.0 / (8.0 * gam * gam)) / d10;
+      const double dpot_da = c6 * dd6 * id6 * id6 - dc8 * id8 + c8 * dd8 * id8 * id8 - dc10 * id10 +
+                             c10 * dd10 * id10 * id10;
+      const double dpot_dc6 = -id6 - 5.0 * igam * id8 - 245.0 * 0.125 * (igam * igam) * id10;
       const double dpot_dhi = dpot_dc6 * dc6_dhi + dpot_da * 0.5 * ai0;
       double dsw, ddsw;
-      smooth_switch(r, p.disp_cuton, p.cutoff, dsw, ddsw);
+      smooth_switch(r, p.disp_cuton, p.cutoff, k.inv_disp_width, dsw, ddsw);
       o.e_disp = p.full_scale * p.hartree * qdo * dsw;
-      drad = p.full_scale * p.hartree * (rad_au * dsw / p.bohr + qdo * ddsw);
+      drad = p.full_scale * p.hartree * (rad_au * dsw * k.inv_bohr + qdo * ddsw);
       o.dh = p.full_scale * p.hartree * dsw * dpot_dhi;
     }
   }
@@ -254,6 +285,7 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
   const int Zi = z[i];
   const double ai0 = (Zi - 1 >= 0 && Zi - 1 < table) ? aref[Zi - 1] : -1.0;
   const double ci0 = (Zi - 1 >= 0 && Zi - 1 < table) ? cref[Zi - 1] : 0.0;
+  const LrConst kc = lr_const(p);
   double acc_ee = 0, acc_ed = 0, acc_dq = 0, acc_dh = 0, fx = 0, fy = 0, fz = 0;
   double wxx = 0, wyy = 0, wzz = 0, wxy = 0, wxz = 0, wyz = 0;
   int count = 0;  // warp-uniform queue length
@@ -262,12 +294,12 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
     const double vx = qv[wl][slot][0], vy = qv[wl][slot][1], vz = qv[wl][slot][2];
     const double r = sqrt(vx * vx + vy * vy + vz * vz);
     const double4 pj = pos4[k], hj = par4[k];
-    const LrPair o = lr_pair_tab(p, r, qi, pj.w, hi, hj.x, ai0, hj.y, ci0, hj.z);
+    const LrPair o = lr_pair_tab(p, kc, r, qi, pj.w, hi, hj.x, ai0, hj.y, ci0, hj.z);
     acc_ee += o.e_elec;
     acc_ed += o.e_disp;
     acc_dq += o.dq;
     acc_dh += o.dh;
-    const double s = o.radial / r;
+    const double s = o.radial / r;  // one division per pair; r is the queue's own distance
     fx += s * vx;
     fy += s * vy;
     fz += s * vz;
