@@ -76,9 +76,37 @@ __global__ void __launch_bounds__(256) k_attention_forward(int n, int row0, cons
   double acc_ev = 0.0;
   const int my_deg = lane < kEV ? degree_of_channel(lane) : 0;
   const double my_par = parity_sign(my_deg);
-  for (int e = row_start[r]; e < row_start[r + 1]; ++e) {
-    const int b = nbr[e];
-    const int code = edge_pair[e];
+  const int e0 = row_start[r], e1 = row_start[r + 1];
+  int b_nx = 0, code_nx = 0;  // indices of the next edge, loaded one iteration ahead
+  if (e0 < e1) {
+    b_nx = nbr[e0];
+    code_nx = edge_pair[e0];
+  }
+  for (int e = e0; e < e1; ++e) {
+    const int b = b_nx;
+    const int code = code_nx;
+    if (e + 1 < e1) {
+      b_nx = nbr[e + 1];
+      code_nx = edge_pair[e + 1];
+      // pull the next edge's rows into L1 while this one is processed: the k, v
+      // and k_ev lines of each head (lines 2-5 and 8-9 of the head's ten 128-byte
+      // lines), both filters (8 lines each) and the harmonics (two 96-byte halves)
+      const int p_nx = code_nx >= 0 ? code_nx : ~code_nx;
+      for (int c = lane; c < 42; c += 32) {
+        const char *addr;
+        if (c < 24) {
+          const int j = c % 6;
+          addr = reinterpret_cast<const char *>(qkv + (size_t)b_nx * kQKV) + 128 * ((c / 6) * 10 + (j < 4 ? 2 + j : 4 + j));
+        } else if (c < 32) {
+          addr = reinterpret_cast<const char *>(f_inv + (size_t)p_nx * kF) + 128 * (c - 24);
+        } else if (c < 40) {
+          addr = reinterpret_cast<const char *>(f_ev + (size_t)p_nx * kF) + 128 * (c - 32);
+        } else {
+          addr = reinterpret_cast<const char *>(sh + (size_t)p_nx * kEV) + 96 * (c - 40);
+        }
+        asm volatile("prefetch.global.L1 [%0];\n" ::"l"(addr));
+      }
+    }
     const int p = code >= 0 ? code : ~code;
     const double phi = geo[(size_t)p * kGeo + 4];
     double kb[4], vb[4], keb[4], fi[4], fe[4];

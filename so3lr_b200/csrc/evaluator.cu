@@ -268,15 +268,20 @@ void Evaluator::allgather_rows(double *a, int width) {
 // seg: device [nseg + 1] row offsets; out: device [nseg * ncol]
 void Evaluator::exact_sums(const double *v, int stride, int ncol, int nseg, const int *seg, double *out) {
   const int count = nseg * ncol;
-  long long *local = parts_.reserve(std::size_t(count) * 2 * (nranks_ + 1));
-  long long *all = local + std::size_t(count) * 2;
-  launch_fixed_segment_sum(nseg, seg, v, stride, ncol, local, stream_);
+  // one segment (a global sum over this GPU's atoms): spread it over many blocks;
+  // the block count depends only on the rank stride, so every rank sends the
+  // same number of partial sums
+  const int nblk = nseg == 1 ? std::max(1, std::min(64, (stride_ + 2047) / 2048)) : 1;
+  const std::size_t per_rank = std::size_t(count) * 2 * nblk;
+  long long *local = parts_.reserve(per_rank * (nranks_ + 1));
+  long long *all = local + per_rank;
+  launch_fixed_segment_sum(nseg, nblk, seg, v, stride, ncol, local, stream_);
   if (nranks_ > 1) {
-    const ncclResult_t r = ncclAllGather(local, all, std::size_t(count) * 2, ncclInt64, comm_, stream_);
+    const ncclResult_t r = ncclAllGather(local, all, per_rank, ncclInt64, comm_, stream_);
     if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclAllGather failed: ") + ncclGetErrorString(r));
-    launch_fixed_finish(all, nranks_, count, out, stream_);
+    launch_fixed_finish(all, nranks_ * nblk, count, out, stream_);
   } else {
-    launch_fixed_finish(local, 1, count, out, stream_);
+    launch_fixed_finish(local, nblk, count, out, stream_);
   }
 }
 

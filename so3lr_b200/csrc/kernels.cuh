@@ -38,9 +38,10 @@ void count_sr(NeighborState &nb, double rc, cudaStream_t s);
 void fill_sr(NeighborState &nb, double rc, int E, cudaStream_t s);
 void fill_pairs(NeighborState &nb, int E, cudaStream_t s);
 
-// exact fixed-point sums (reduce.cu): parts[(seg * ncol + col) * 2 + {hi, lo}]
-void launch_fixed_segment_sum(int nseg, const int *start, const double *v, int stride, int ncol, long long *parts,
-                              cudaStream_t s);
+// exact fixed-point sums (reduce.cu): nblk partial sums per segment and column,
+// parts[((blk * nseg + seg) * ncol + col) * 2 + {hi, lo}]
+void launch_fixed_segment_sum(int nseg, int nblk, const int *start, const double *v, int stride, int ncol,
+                              long long *parts, cudaStream_t s);
 // out[k] = sum over nparts consecutive blocks of `count` fixed-point values
 void launch_fixed_finish(const long long *parts, int nparts, int count, double *out, cudaStream_t s);
 

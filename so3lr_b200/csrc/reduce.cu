@@ -41,16 +41,21 @@ __device__ inline double from_fixed(__int128 s) {
   return neg ? -v : v;
 }
 
-// out[(seg * ncol + col) * 2 + {0,1}] = (hi, lo) of sum over rows of segment seg
+// Block (seg, blk) of a grid of nseg x nblk blocks sums the rows of segment seg
+// with index = blk * blockDim + tid (mod nblk * blockDim) and writes
+// out[(blk * nseg * ncol + seg * ncol + col) * 2 + {0,1}] = (hi, lo). Integer
+// addition is exact, so how the rows are split over blocks does not matter.
 __global__ void k_fixed_segment_sum(const int *__restrict__ start, const double *__restrict__ v, int stride, int ncol,
                                     long long *__restrict__ out) {
   __shared__ long long buf_hi[256];
   __shared__ unsigned long long buf_lo[256];
-  const int seg = blockIdx.x;
+  const int seg = blockIdx.x, blk = blockIdx.y, nblk = gridDim.y;
+  const int count = gridDim.x * ncol;
   const int b = start[seg], e = start[seg + 1];
   for (int col = 0; col < ncol; ++col) {
     __int128 acc = 0;
-    for (int i = b + threadIdx.x; i < e; i += blockDim.x) acc += to_fixed(v[(size_t)i * stride + col]);
+    for (int i = b + blk * blockDim.x + threadIdx.x; i < e; i += nblk * blockDim.x)
+      acc += to_fixed(v[(size_t)i * stride + col]);
     buf_hi[threadIdx.x] = static_cast<long long>(acc >> 64);
     buf_lo[threadIdx.x] = static_cast<unsigned long long>(acc);
     __syncthreads();
@@ -58,8 +63,9 @@ __global__ void k_fixed_segment_sum(const int *__restrict__ start, const double 
       __int128 total = 0;
       for (int t = 0; t < blockDim.x; ++t)
         total += (static_cast<__int128>(buf_hi[t]) << 64) | static_cast<__int128>(buf_lo[t]);
-      out[((size_t)seg * ncol + col) * 2] = static_cast<long long>(total >> 64);
-      out[((size_t)seg * ncol + col) * 2 + 1] = static_cast<long long>(static_cast<unsigned long long>(total));
+      const size_t k = (size_t)blk * count + (size_t)seg * ncol + col;
+      out[k * 2] = static_cast<long long>(total >> 64);
+      out[k * 2 + 1] = static_cast<long long>(static_cast<unsigned long long>(total));
     }
     __syncthreads();
   }
@@ -80,10 +86,10 @@ __global__ void k_fixed_finish(const long long *__restrict__ parts, int nparts, 
 
 }  // namespace
 
-void launch_fixed_segment_sum(int nseg, const int *start, const double *v, int stride, int ncol, long long *parts,
-                              cudaStream_t s) {
+void launch_fixed_segment_sum(int nseg, int nblk, const int *start, const double *v, int stride, int ncol,
+                              long long *parts, cudaStream_t s) {
   if (nseg == 0) return;
-  k_fixed_segment_sum<<<nseg, 256, 0, s>>>(start, v, stride, ncol, parts);
+  k_fixed_segment_sum<<<dim3(nseg, nblk), 256, 0, s>>>(start, v, stride, ncol, parts);
   SO3_LAUNCH("fixed_segment_sum");
 }
 
