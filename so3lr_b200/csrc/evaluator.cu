@@ -548,6 +548,7 @@ std::size_t Evaluator::device_bytes() const {
   std::size_t total = wbuf_.bytes() + geo_.bytes() + sh_.bytes() + gv_.bytes() + gl0_.bytes() + pair_sc_.bytes();
   for (auto &v : f_inv_) total += v->bytes();
   for (auto &v : f_ev_) total += v->bytes();
+  for (auto &v : sp_) total += v->bytes();
   for (auto *vec : {&xb_, &evb_, &qkv_, &xhat1_, &rstd1_, &n1_, &A_, &hp_, &gate_, &xhat2_, &rstd2_})
     for (auto &v : *vec) total += v->bytes();
   total += nbr_.bytes() * 8;
@@ -639,10 +640,12 @@ void Evaluator::build_neighbors() {
   while (int(f_inv_.size()) < layers_) {
     f_inv_.emplace_back(new DeviceArray<double>());
     f_ev_.emplace_back(new DeviceArray<double>());
+    sp_.emplace_back(new DeviceArray<double>());
   }
   for (int b = 0; b < layers_; ++b) {
     f_inv_[b]->reserve(std::size_t(P) * kF, 1.25);
     f_ev_[b]->reserve(std::size_t(P) * kF, 1.25);
+    sp_[b]->reserve(filter_sp_doubles(P), 1.25);
   }
 }
 
@@ -675,7 +678,7 @@ void Evaluator::compute() {
     const BlockW &w = blocks_[b];
     prof_begin(0);
     launch_filter_forward(P, geo_.get(), nb_.pair_a, nb_.pair_b, b == 0 ? nullptr : evb_[b]->get(), w.cg_att, w.finv,
-                          w.fev, rad_, f_inv_[b]->get(), f_ev_[b]->get(), s);
+                          w.fev, rad_, f_inv_[b]->get(), f_ev_[b]->get(), sp_[b]->get(), s);
     prof_end(0, kFilterFlopsPerPair * double(P));
     {  // per-head projections for every row: qkv[n][h][5][32] = x[n][h*32:(h+1)*32] W_h
       GemmArgs g{};
@@ -827,7 +830,7 @@ void Evaluator::compute() {
                              g_filt_inv_.get(), g_filt_ev_.get(), s);
     prof_begin(1);
     launch_filter_reverse(P, geo_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr, w.cg_att, w.finv,
-                          w.fev, rad_, g_filt_inv_.get(), g_filt_ev_.get(), g_A_.get(), pair_sc_.get(), b > 0,
+                          w.fev, rad_, g_filt_inv_.get(), g_filt_ev_.get(), sp_[b]->get(), g_A_.get(), pair_sc_.get(), b > 0,
                           gv_.get(), gl0_.get(), s);
     prof_end(1, kFilterFlopsPerPair * double(P));
     if (b > 0) {

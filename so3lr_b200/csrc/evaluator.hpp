@@ -166,7 +166,7 @@ class Evaluator {
 
   // per-pair arrays
   DeviceArray<double> geo_, sh_, gv_, gl0_, pair_sc_, g_filt_inv_, g_filt_ev_;
-  std::vector<std::unique_ptr<DeviceArray<double>>> f_inv_, f_ev_;
+  std::vector<std::unique_ptr<DeviceArray<double>>> f_inv_, f_ev_, sp_;
 
   // per-atom arrays
   DeviceArray<double> x_, v_, inv_mass_, force_;

@@ -29,6 +29,14 @@ constexpr int TP = 64;     // pairs per tile
 constexpr int LDU = 132;   // padded stride of 128-wide smem tiles (conflict-free fragment reads)
 constexpr int LDR = 36;    // padded stride of 32-wide smem tiles
 
+// silu'(hidden pre-activation) of the rbf branch, written by the forward and
+// read by the reverse in the accumulator order of their common warp tiling:
+// [tile][filter][warp][mi][ni][lane][2] (64 x 128 values per tile and filter,
+// 512 contiguous bytes per warp and (mi, ni))
+__device__ __forceinline__ size_t sp_offset(int tile, int filt, int warp) {
+  return (((size_t)tile * 2 + filt) * 8 + warp) * (16 * 64);
+}
+
 __device__ inline void compute_rbf(const double *rr, double *rbf, const RadialW &rad) {
   const int pl = threadIdx.x >> 2;
   const int k0 = (threadIdx.x & 3) * 8;
@@ -38,7 +46,7 @@ __device__ inline void compute_rbf(const double *rr, double *rbf, const RadialW 
   if (x > 1.0 - 1.0e-6) x = 1.0 - 1.0e-6;
   const double lx = log(x), l1x = log(1.0 - x);
 #pragma unroll
-  for (int k = k0; k < k0 + 8; ++k) rbf[pl * LDR + k] = exp(rad.b[k] + rad.k[k] * lx + rad.kr[k] * l1x);
+  for (int k = k0; k < k0 + 8; ++k) rbf[pl * LDR + k] = exp_tang(rad.b[k] + rad.k[k] * lx + rad.kr[k] * l1x);
 }
 
 __device__ inline void compute_l0(int P, int p0, const int *pa, const int *pb, const double *ev, const double *cg,
@@ -127,7 +135,8 @@ __global__ void __launch_bounds__(256) k_filter_forward(int P, const double *__r
                                                         const int *__restrict__ pa, const int *__restrict__ pb,
                                                         const double *__restrict__ ev, const double *__restrict__ cg,
                                                         FilterW finv, FilterW fev, RadialW rad,
-                                                        double *__restrict__ f_inv, double *__restrict__ f_ev) {
+                                                        double *__restrict__ f_inv, double *__restrict__ f_ev,
+                                                        double *__restrict__ sp) {
   extern __shared__ double sm[];
   double *rbf = sm;               // TP x LDR
   double *u = rbf + TP * LDR;     // TP x LDU
@@ -163,13 +172,20 @@ __global__ void __launch_bounds__(256) k_filter_forward(int P, const double *__r
 #pragma unroll
       for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
     mma_32x32<kR>(acc, rbf, LDR, W.w0t_f, wm, wn, lane);
+    // hidden layer u = silu(pre) to shared memory, and silu'(pre) for the
+    // reverse pass straight from the accumulators in fragment order
+    double *sp_tile = sp + sp_offset(blockIdx.x, filt, warp);
 #pragma unroll
     for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
       for (int ni = 0; ni < 4; ++ni) {
         const int row = wm * 32 + mi * 8 + g, col = wn * 32 + ni * 8 + 2 * t;
-        u[row * LDU + col] = silu(acc[mi][ni][0] + W.b0[col]);
-        u[row * LDU + col + 1] = silu(acc[mi][ni][1] + W.b0[col + 1]);
+        const double x0 = acc[mi][ni][0] + W.b0[col], x1 = acc[mi][ni][1] + W.b0[col + 1];
+        const double s0 = sigmoid(x0), s1 = sigmoid(x1);
+        u[row * LDU + col] = x0 * s0;
+        u[row * LDU + col + 1] = x1 * s1;
+        *reinterpret_cast<double2 *>(sp_tile + (mi * 4 + ni) * 64 + lane * 2) =
+            make_double2(s0 * (1.0 + x0 * (1.0 - s0)), s1 * (1.0 + x1 * (1.0 - s1)));
         acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
       }
     __syncthreads();
@@ -195,7 +211,7 @@ __global__ void __launch_bounds__(256) k_filter_forward(int P, const double *__r
 
 void launch_filter_forward(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
                            const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,
-                           double *f_inv, double *f_ev, cudaStream_t s) {
+                           double *f_inv, double *f_ev, double *sp, cudaStream_t s) {
   if (P == 0) return;
   const size_t smem = sizeof(double) * (TP * LDR * 2 + TP * LDU + TP * 4 + TP);
   static bool configured = false;
@@ -204,7 +220,7 @@ void launch_filter_forward(int P, const double *geo, const int *pair_a, const in
     configured = true;
   }
   k_filter_forward<<<(P + TP - 1) / TP, 256, smem, s>>>(P, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad, f_inv,
-                                                         f_ev);
+                                                         f_ev, sp);
   SO3_LAUNCH("filter_forward");
 }
 
@@ -256,44 +272,40 @@ __device__ inline void stage_rows(double *dst, int lds, const double *src, int p
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_reverse(
     int P, const double *__restrict__ geo, const int *__restrict__ pa, const int *__restrict__ pb,
     const double *__restrict__ ev, const double *__restrict__ cg, FilterW finv, FilterW fev, RadialW rad,
-    const double *__restrict__ g_filt_inv, const double *__restrict__ g_filt_ev, const double *__restrict__ gA,
-    const double *__restrict__ pair_sc, int need_l0, double *__restrict__ gv, double *__restrict__ gl0) {
+    const double *__restrict__ g_filt_inv, const double *__restrict__ g_filt_ev, const double *__restrict__ sp,
+    const double *__restrict__ gA, const double *__restrict__ pair_sc, int need_l0, double *__restrict__ gv,
+    double *__restrict__ gl0) {
   namespace cgrp = cooperative_groups;
   cgrp::cluster_group cluster = cgrp::this_cluster();
   const int f = static_cast<int>(cluster.block_rank());  // 0: invariant filter, 1: ev filter
   extern __shared__ double sm[];
   double *gF = sm;                // TP x LDU: filter gradient, then the hidden pre-activation gradient
-  double *rbf = gF + TP * LDU;    // TP x LDR
-  double *gw = rbf + TP * LDR;    // TP x LDR: ev-hidden gradient, then the radial-basis gradient
+  double *gw = gF + TP * LDU;     // TP x LDR: ev-hidden gradient, then the radial-basis gradient
   double *l0 = gw + TP * LDR;     // TP x 4
   double *gl = l0 + TP * 4;       // TP x 4
-  double *rr = gl + TP * 4;       // TP
-  const int p0 = (blockIdx.x >> 1) * TP;
+  const int tile = blockIdx.x >> 1;
+  const int p0 = tile * TP;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int wm = warp >> 2, wn = warp & 3;
   // this CTA's filter (selected field by field so the parameters stay in registers)
   const double *w1_f = f ? fev.w1_f : finv.w1_f;
-  const double *w0t_f = f ? fev.w0t_f : finv.w0t_f;
   const double *v1_f = f ? fev.v1_f : finv.v1_f;
   const double *w0_f = f ? fev.w0_f : finv.w0_f;
-  const double *b0 = f ? fev.b0 : finv.b0;
   const double *v0 = f ? fev.v0 : finv.v0;
   const double *c0 = f ? fev.c0 : finv.c0;
+  const double *sp_tile = sp + sp_offset(tile, f, warp);
 
   stage_rows<kF>(gF, LDU, f ? g_filt_ev : g_filt_inv, p0, P);
   cp_async_commit();
-  if (tid < TP) {
-    const int p = p0 + tid;
-    rr[tid] = p < P ? geo[(size_t)p * kGeo] : 1.0;
-  }
+  // the forward's silu' values of this warp's part of the tile (8 KB) into L2
+  for (int c = lane; c < 16 * 64 * 8 / 128; c += 32)
+    asm volatile("prefetch.global.L2 [%0];\n" ::"l"(reinterpret_cast<const char *>(sp_tile) + 128 * c));
   gl[tid] = 0.0;
   compute_l0(P, p0, pa, pb, need_l0 ? ev : nullptr, cg, l0);
-  __syncthreads();
-  compute_rbf(rr, rbf, rad);
   cp_async_wait<0>();
   __syncthreads();
 
-  // gradient of the hidden layer: (gF W1) * silu'(rbf W0^T + b0), warp tile 32 x 32
+  // gradient of the hidden layer: (gF W1) * silu'(pre), warp tile 32 x 32
   double acc[4][4][2];
 #pragma unroll
   for (int mi = 0; mi < 4; ++mi)
@@ -301,25 +313,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
     for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
   mma_32x32<kF>(acc, gF, LDU, w1_f, wm, wn, lane);
 #pragma unroll
-  for (int mi = 0; mi < 4; ++mi) {  // recompute the pre-activation one 8-row block at a time
-    double pre[4][2];
-#pragma unroll
-    for (int ni = 0; ni < 4; ++ni) pre[ni][0] = pre[ni][1] = 0.0;
-#pragma unroll
-    for (int ks = 0; ks < kR / 4; ++ks) {
-      const double a = rbf[(wm * 32 + mi * 8 + g) * LDR + 4 * ks + t];
-      double b[4];
-      load_bfrag(w0t_f, ks, 4, wn, lane, b);
-#pragma unroll
-      for (int ni = 0; ni < 4; ++ni) dmma(pre[ni][0], pre[ni][1], a, b[ni]);
-    }
+  for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
     for (int ni = 0; ni < 4; ++ni) {
-      const int col = wn * 32 + ni * 8 + 2 * t;
-      acc[mi][ni][0] *= silu_prime(pre[ni][0] + b0[col]);
-      acc[mi][ni][1] *= silu_prime(pre[ni][1] + b0[col + 1]);
+      const double2 s = __ldg(reinterpret_cast<const double2 *>(sp_tile + (mi * 4 + ni) * 64 + lane * 2));
+      acc[mi][ni][0] *= s.x;
+      acc[mi][ni][1] *= s.y;
     }
-  }
   // ev branch: g_w = gF V1 (64 x 32), warp w owns rows 8w..8w+7
   double gwa[4][2];
 #pragma unroll
@@ -403,12 +403,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
     if (p >= P) continue;
     const double *gp = geos + pl * kGeo;
     const double r = gp[0], phi = gp[4], dphi = gp[5];
-    // Bernstein derivative (block2_attention_input_reverse.cpp:322-333)
+    // Bernstein derivative (block2_attention_input_reverse.cpp:322-333); lane k
+    // evaluates basis function k (the same arithmetic as compute_rbf)
     const double raw_x = exp(-rad.gamma * r);
     double gr = 0.0;
     if (raw_x > 1.0e-6 && raw_x < 1.0 - 1.0e-6) {
+      const double rbf_k = exp_tang(rad.b[lane] + rad.k[lane] * log(raw_x) + rad.kr[lane] * log(1.0 - raw_x));
       const double dl = -rad.gamma * rad.k[lane] + rad.gamma * rad.kr[lane] * raw_x / (1.0 - raw_x);
-      gr = gw[pl * LDR + lane] * rbf[pl * LDR + lane] * dl;
+      gr = gw[pl * LDR + lane] * rbf_k * dl;
     }
     // cutoff gradient: sum over heads of alpha*s for both directions; the two
     // directions are added first (a commutative add), so the result does not
@@ -449,10 +451,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
 
 void launch_filter_reverse(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
                            const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,
-                           const double *g_filt_inv, const double *g_filt_ev, const double *gA,
+                           const double *g_filt_inv, const double *g_filt_ev, const double *sp, const double *gA,
                            const double *pair_sc, bool need_l0, double *gv, double *gl0, cudaStream_t s) {
   if (P == 0) return;
-  const size_t smem = sizeof(double) * (TP * LDU + 2 * TP * LDR + 8 * TP + TP);
+  const size_t smem = sizeof(double) * (TP * LDU + TP * LDR + 8 * TP);
   static_assert(TP * (kPairScalars + kGeo + kEV) <= TP * LDU, "tail inputs must fit in the gradient tile");
   static bool configured = false;
   if (!configured) {
@@ -461,7 +463,7 @@ void launch_filter_reverse(int P, const double *geo, const int *pair_a, const in
   }
   const int tiles = (P + TP - 1) / TP;
   k_filter_reverse<<<2 * tiles, 256, smem, s>>>(P, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad, g_filt_inv,
-                                                g_filt_ev, gA, pair_sc, need_l0 ? 1 : 0, gv, gl0);
+                                                g_filt_ev, sp, gA, pair_sc, need_l0 ? 1 : 0, gv, gl0);
   SO3_LAUNCH("filter_reverse");
 }
 

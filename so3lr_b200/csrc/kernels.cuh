@@ -78,14 +78,16 @@ void long_range_noalloc(int n, const double *x, const double *q, const double *h
                         double *w_atom, cudaStream_t s);
 
 // ---- filters (pair tiles, FP64 tensor cores) --------------------------------
+// sp: silu' of the rbf-branch hidden layer for the reverse pass, filter_sp_doubles(P) doubles
 void launch_filter_forward(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
                            const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,
-                           double *f_inv, double *f_ev, cudaStream_t s);
+                           double *f_inv, double *f_ev, double *sp, cudaStream_t s);
+inline std::size_t filter_sp_doubles(int P) { return std::size_t((P + 63) / 64) * 2 * 64 * 128; }
 // g_filt_inv / g_filt_ev: per-pair gradient w.r.t. the two filter outputs (written by
 // the attention reverse at each pair's primary edge)
 void launch_filter_reverse(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
                            const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,
-                           const double *g_filt_inv, const double *g_filt_ev, const double *gA,
+                           const double *g_filt_inv, const double *g_filt_ev, const double *sp, const double *gA,
                            const double *pair_sc, bool need_l0, double *gv, double *gl0, cudaStream_t s);
 
 // ---- attention (receiver CSR gathers) ----------------------------------------
