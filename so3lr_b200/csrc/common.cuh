@@ -100,6 +100,17 @@ __device__ __forceinline__ double rcp_newton(double d) {
   return fma(y, e, y);
 }
 __device__ __forceinline__ double sigmoid(double x) { return rcp_newton(1.0 + exp_tang(-x)); }
+// FP64 tensor-core MMA: D(16x8) = A(16x8, row) * B(8x8, col) + C. Fragment
+// ownership (g = lane >> 2, t = lane & 3; k slots s0 = t, s1 = t + 4):
+//   a = {A[g][s0], A[g+8][s0], A[g][s1], A[g+8][s1]}, b = {B[s0][g], B[s1][g]},
+//   c = {C[g][2t], C[g][2t+1], C[g+8][2t], C[g+8][2t+1]}.
+__device__ __forceinline__ void dmma16(double (&c)[4], const double (&a)[4], const double (&b)[2]) {
+  asm volatile("mma.sync.aligned.m16n8k8.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+               "{%0,%1,%2,%3};\n"
+               : "+d"(c[0]), "+d"(c[1]), "+d"(c[2]), "+d"(c[3])
+               : "d"(a[0]), "d"(a[1]), "d"(a[2]), "d"(a[3]), "d"(b[0]), "d"(b[1]));
+}
+
 __device__ __forceinline__ double silu(double x) { return x * sigmoid(x); }
 __device__ __forceinline__ double silu_prime(double x) {
   const double s = sigmoid(x);
@@ -113,9 +124,9 @@ struct FilterW {
   const double *w1, *b1;  // [128][128], [128]  hidden -> filter
   const double *v0, *c0;  // [32][4], [32]      L0 -> ev hidden
   const double *v1, *c1;  // [128][32], [128]   ev hidden -> filter
-  // The same matrices as DMMA B operands in fragment-major order (see
+  // The same matrices as m16n8k8 DMMA B operands in fragment-major order (see
   // fragment_major in evaluator.cu): B(k, n) of a K x N operand sits at
-  // [k/4][n/32][lane = 4 (n%8) + k%4][(n%32)/8].
+  // [k/8][n/32][lane = 4 (n%8) + (k%8)/2][(n%32)/8][k%2].
   const double *w0t_f;    // K=32,  N=128: B(r, j) = w0[j][r]   forward layer 0 / reverse recompute
   const double *w1t_f;    // K=128, N=128: B(j, o) = w1[o][j]   forward layer 1
   const double *v1t_f;    // K=32,  N=128: B(h, o) = v1[o][h]   forward ev layer 1

@@ -41,18 +41,20 @@ Evaluator::~Evaluator() {
 // ---------------------------------------------------------------------------
 // weights
 // ---------------------------------------------------------------------------
-// A K x N matrix B(k, n) laid out as the B operand of m8n8k4 DMMA tiles 32
-// columns wide: lane (g = lane / 4, t = lane % 4) of a warp needs, for k-step
-// ks and column slab s, B(4 ks + t, 32 s + 8 ni + g) for ni = 0..3; those four
-// values are stored contiguously so one warp reads one k-step of a slab as
-// 1 KB of consecutive memory (two 16-byte loads per lane).
+// A K x N matrix B(k, n) laid out as the B operand of m16n8k8 DMMA tiles 32
+// columns wide. The kernels read the MMA's k slots t and t + 4 of k-step ks
+// from columns 8 ks + 2t and 8 ks + 2t + 1 of their activation tiles, so lane
+// (g = lane / 4, t = lane % 4) needs, for column slab s and column block ni,
+// {B(8 ks + 2t, n), B(8 ks + 2t + 1, n)} with n = 32 s + 8 ni + g; its eight
+// values of one k-step and slab are stored contiguously (one warp reads 2 KB of
+// consecutive memory).
 static std::vector<double> fragment_major(int K, int N, const std::function<double(int, int)> &B) {
-  if (K % 4 != 0 || N % 32 != 0) throw Error("SO3LR: fragment-major operand needs K % 4 == 0 and N % 32 == 0");
+  if (K % 8 != 0 || N % 32 != 0) throw Error("SO3LR: fragment-major operand needs K % 8 == 0 and N % 32 == 0");
   std::vector<double> out(std::size_t(K) * N);
   for (int k = 0; k < K; ++k)
     for (int n = 0; n < N; ++n) {
-      const int ks = k / 4, t = k % 4, slab = n / 32, ni = (n % 32) / 8, g = n % 8;
-      out[((std::size_t(ks) * (N / 32) + slab) * 32 + (4 * g + t)) * 4 + ni] = B(k, n);
+      const int ks = k / 8, t = (k % 8) / 2, h = k % 2, slab = n / 32, ni = (n % 32) / 8, g = n % 8;
+      out[(((std::size_t(ks) * (N / 32) + slab) * 32 + (4 * g + t)) * 4 + ni) * 2 + h] = B(k, n);
     }
   return out;
 }
@@ -637,6 +639,9 @@ void Evaluator::build_neighbors() {
   pair_sc_.reserve(std::size_t(P) * kPairScalars, 1.25);
   g_filt_inv_.reserve(std::size_t(P) * kF, 1.25);
   g_filt_ev_.reserve(std::size_t(P) * kF, 1.25);
+  drbf_.reserve(std::size_t(P) * kR, 1.25);
+  g_r_.reserve(std::size_t(P), 1.25);
+  g_y_.reserve(std::size_t(P) * kEV, 1.25);
   while (int(f_inv_.size()) < layers_) {
     f_inv_.emplace_back(new DeviceArray<double>());
     f_ev_.emplace_back(new DeviceArray<double>());
@@ -678,7 +683,8 @@ void Evaluator::compute() {
     const BlockW &w = blocks_[b];
     prof_begin(0);
     launch_filter_forward(P, geo_.get(), nb_.pair_a, nb_.pair_b, b == 0 ? nullptr : evb_[b]->get(), w.cg_att, w.finv,
-                          w.fev, rad_, f_inv_[b]->get(), f_ev_[b]->get(), sp_[b]->get(), s);
+                          w.fev, rad_, f_inv_[b]->get(), f_ev_[b]->get(), sp_[b]->get(),
+                          b == 0 ? drbf_.get() : nullptr, s);
     prof_end(0, kFilterFlopsPerPair * double(P));
     {  // per-head projections for every row: qkv[n][h][5][32] = x[n][h*32:(h+1)*32] W_h
       GemmArgs g{};
@@ -830,8 +836,8 @@ void Evaluator::compute() {
                              g_filt_inv_.get(), g_filt_ev_.get(), s);
     prof_begin(1);
     launch_filter_reverse(P, geo_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr, w.cg_att, w.finv,
-                          w.fev, rad_, g_filt_inv_.get(), g_filt_ev_.get(), sp_[b]->get(), g_A_.get(), pair_sc_.get(), b > 0,
-                          gv_.get(), gl0_.get(), s);
+                          w.fev, rad_, g_filt_inv_.get(), g_filt_ev_.get(), sp_[b]->get(), drbf_.get(), g_A_.get(),
+                          pair_sc_.get(), b > 0, b < layers_ - 1, g_r_.get(), g_y_.get(), gl0_.get(), s);
     prof_end(1, kFilterFlopsPerPair * double(P));
     if (b > 0) {
       GemmArgs g{};  // g_x_in = g_a + per-head (g_qkv W^T)
@@ -849,6 +855,8 @@ void Evaluator::compute() {
       gev_next = (gev == g_ev_.get()) ? g_ev2_.get() : g_ev_.get();
     }
   }
+
+  launch_pair_tail(P, geo_.get(), g_r_.get(), g_y_.get(), gv_.get(), s);
 
   // ---- assembly (owned rows) ----------------------------------------------------
   launch_assemble(nb_, geo_.get(), gv_.get(), e_nn_.get(), e_lr_.get(), f_lr_.get(), w_lr_.get(), force_.get(),

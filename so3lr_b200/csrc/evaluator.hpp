@@ -165,7 +165,7 @@ class Evaluator {
   double *host_totals_ = nullptr;
 
   // per-pair arrays
-  DeviceArray<double> geo_, sh_, gv_, gl0_, pair_sc_, g_filt_inv_, g_filt_ev_;
+  DeviceArray<double> geo_, sh_, gv_, gl0_, pair_sc_, g_filt_inv_, g_filt_ev_, drbf_, g_r_, g_y_;
   std::vector<std::unique_ptr<DeviceArray<double>>> f_inv_, f_ev_, sp_;
 
   // per-atom arrays

@@ -15,8 +15,9 @@
 // first and pushed through the MLP once.
 //
 // Tile: 64 pairs per CTA, 8 warps, each warp owns a 32x32 block of the 64x128
-// output and issues m8n8k4 DMMA on fragments read from shared memory (pair
-// activations) and L2-resident weights.
+// output and issues m16n8k8 DMMA on fragments read from shared memory (pair
+// activations, one 16-byte load per row) and L2-resident weights prepared in
+// fragment order (four 16-byte loads per lane and k-step).
 #include <cooperative_groups.h>
 
 #include "kernels.cuh"
@@ -26,13 +27,16 @@ namespace so3lr_b200 {
 namespace {
 
 constexpr int TP = 64;     // pairs per tile
-constexpr int LDU = 132;   // padded stride of 128-wide smem tiles (conflict-free fragment reads)
-constexpr int LDR = 36;    // padded stride of 32-wide smem tiles
+// Row strides of the shared-memory tiles. A quarter-warp's 16-byte fragment
+// access covers 64 bytes of two rows; a stride of 8 (mod 16) doubles puts the
+// second row in the other half of the 32 banks.
+constexpr int LDU = 136;   // 128-wide tiles
+constexpr int LDR = 40;    // 32-wide tiles
 
 // silu'(hidden pre-activation) of the rbf branch, written by the forward and
 // read by the reverse in the accumulator order of their common warp tiling:
-// [tile][filter][warp][mi][ni][lane][2] (64 x 128 values per tile and filter,
-// 512 contiguous bytes per warp and (mi, ni))
+// [tile][filter][warp][mi][ni][half][lane][2] (64 x 128 values per tile and
+// filter, 512 contiguous bytes per warp and (mi, ni, half))
 __device__ __forceinline__ size_t sp_offset(int tile, int filt, int warp) {
   return (((size_t)tile * 2 + filt) * 8 + warp) * (16 * 64);
 }
@@ -66,64 +70,80 @@ __device__ inline void compute_l0(int P, int p0, const int *pa, const int *pb, c
   l0[pl * 4 + d] = v;
 }
 
-// b[ni] = B(4 ks + t, 32 slab + 8 ni + g) of a fragment-major operand with
-// `nslab` column slabs: 32 contiguous bytes per lane, 1 KB per warp
-__device__ __forceinline__ void load_bfrag(const double *__restrict__ Bf, int ks, int nslab, int slab, int lane,
-                                           double (&b)[4]) {
-  const double2 *q = reinterpret_cast<const double2 *>(Bf + ((size_t)(ks * nslab + slab) * 32 + lane) * 4);
-  const double2 x = __ldg(q), y = __ldg(q + 1);
-  b[0] = x.x;
-  b[1] = x.y;
-  b[2] = y.x;
-  b[3] = y.y;
+// The MMA's k slots t and t + 4 of k-step ks are the physical columns 8 ks + 2t
+// and 8 ks + 2t + 1 (a permutation of the contraction index; the weight copies
+// use the same one), so a lane's A values of one row are adjacent.
+// a = {A[r+g][.], A[r+g+8][.], A[r+g][.+1], A[r+g+8][.+1]} at column 8 ks + 2t
+__device__ __forceinline__ void load_afrag(const double *A, int lda, int r, int ks, int g, int t, double (&a)[4]) {
+  const double2 x = *reinterpret_cast<const double2 *>(A + (r + g) * lda + 8 * ks + 2 * t);
+  const double2 y = *reinterpret_cast<const double2 *>(A + (r + g + 8) * lda + 8 * ks + 2 * t);
+  a[0] = x.x;
+  a[1] = y.x;
+  a[2] = x.y;
+  a[3] = y.y;
 }
 
-// warp tile 32 x 32 (rows 32 wm.., cols 32 wn..):
-// acc += A(64 x K, smem, row stride lda) * B(K x 128, fragment-major)
-template <int K>
-__device__ inline void mma_32x32(double (&acc)[4][4][2], const double *A, int lda, const double *__restrict__ Bf,
-                                 int wm, int wn, int lane) {
-  const int g = lane >> 2, t = lane & 3;
-#pragma unroll 4
-  for (int ks = 0; ks < K / 4; ++ks) {
-    double a[4], b[4];
+// b[j] = {B(8 ks + 2t, n), B(8 ks + 2t + 1, n)}, n = 32 slab + 8 (ni0 + j) + g, for
+// j < NB, from a fragment-major operand with `nslab` column slabs (8
+// contiguous doubles per lane and k-step)
+template <int NB>
+__device__ __forceinline__ void load_bfrag(const double *__restrict__ Bf, int ks, int nslab, int slab, int ni0,
+                                           int lane, double (&b)[NB][2]) {
+  const double2 *q = reinterpret_cast<const double2 *>(Bf + ((size_t)(ks * nslab + slab) * 32 + lane) * 8) + ni0;
 #pragma unroll
-    for (int mi = 0; mi < 4; ++mi) a[mi] = A[(wm * 32 + mi * 8 + g) * lda + 4 * ks + t];
-    load_bfrag(Bf, ks, 4, wn, lane, b);
-#pragma unroll
-    for (int mi = 0; mi < 4; ++mi)
-#pragma unroll
-      for (int ni = 0; ni < 4; ++ni) dmma(acc[mi][ni][0], acc[mi][ni][1], a[mi], b[ni]);
+  for (int j = 0; j < NB; ++j) {
+    const double2 v = __ldg(q + j);
+    b[j][0] = v.x;
+    b[j][1] = v.y;
   }
 }
 
-// warp tile 8 x 32 (rows row0..row0+7, all 32 columns), two K halves as
-// independent accumulation chains: acc += A(rows, K, smem lda) * B(K x 32, fragment-major)
+// warp tile 32 x 32 (rows 32 wm.., cols 32 wn..) as 2 x 4 m16n8 blocks:
+// acc += A(64 x K, smem, row stride lda) * B(K x 128, fragment-major)
 template <int K>
-__device__ inline void mma_8x32(double (&acc)[4][2], const double *A, int lda, int row0,
-                                const double *__restrict__ Bf, int lane) {
+__device__ inline void mma_32x32(double (&acc)[2][4][4], const double *A, int lda, const double *__restrict__ Bf,
+                                 int wm, int wn, int lane) {
   const int g = lane >> 2, t = lane & 3;
-  double acc2[4][2];
-#pragma unroll
-  for (int ni = 0; ni < 4; ++ni) acc2[ni][0] = acc2[ni][1] = 0.0;
-#pragma unroll 4
+#pragma unroll 2
   for (int ks = 0; ks < K / 8; ++ks) {
-    const double a0 = A[(row0 + g) * lda + 4 * ks + t];
-    const double a1 = A[(row0 + g) * lda + K / 2 + 4 * ks + t];
-    double b0[4], b1[4];
-    load_bfrag(Bf, ks, 1, 0, lane, b0);
-    load_bfrag(Bf, ks + K / 8, 1, 0, lane, b1);
+    double a[2][4], b[4][2];
+    load_afrag(A, lda, wm * 32, ks, g, t, a[0]);
+    load_afrag(A, lda, wm * 32 + 16, ks, g, t, a[1]);
+    load_bfrag<4>(Bf, ks, 4, wn, 0, lane, b);
 #pragma unroll
-    for (int ni = 0; ni < 4; ++ni) {
-      dmma(acc[ni][0], acc[ni][1], a0, b0[ni]);
-      dmma(acc2[ni][0], acc2[ni][1], a1, b1[ni]);
+    for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) dmma16(acc[mi][ni], a[mi], b[ni]);
+  }
+}
+
+// warp tile 16 x 16 (rows r0.., cols 16 wc..) of a 64 x 32 output, the two K
+// halves as independent accumulation chains:
+// acc += A(rows, K, smem lda) * B(K x 32, fragment-major)
+template <int K>
+__device__ inline void mma_16x16(double (&acc)[2][4], const double *A, int lda, int r0,
+                                 const double *__restrict__ Bf, int wc, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  double acc2[2][4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) acc2[j][0] = acc2[j][1] = acc2[j][2] = acc2[j][3] = 0.0;
+#pragma unroll 2
+  for (int ks = 0; ks < K / 16; ++ks) {
+    double a0[4], a1[4], b0[2][2], b1[2][2];
+    load_afrag(A, lda, r0, ks, g, t, a0);
+    load_afrag(A, lda, r0, ks + K / 16, g, t, a1);
+    load_bfrag<2>(Bf, ks, 1, 0, 2 * wc, lane, b0);
+    load_bfrag<2>(Bf, ks + K / 16, 1, 0, 2 * wc, lane, b1);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      dmma16(acc[j], a0, b0[j]);
+      dmma16(acc2[j], a1, b1[j]);
     }
   }
 #pragma unroll
-  for (int ni = 0; ni < 4; ++ni) {
-    acc[ni][0] += acc2[ni][0];
-    acc[ni][1] += acc2[ni][1];
-  }
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) acc[j][v] += acc2[j][v];
 }
 
 }  // namespace
@@ -131,12 +151,12 @@ __device__ inline void mma_8x32(double (&acc)[4][2], const double *A, int lda, i
 // ---------------------------------------------------------------------------
 // forward: f_inv[p][128], f_ev[p][128]
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) k_filter_forward(int P, const double *__restrict__ geo,
+__global__ void __launch_bounds__(256, 2) k_filter_forward(int P, const double *__restrict__ geo,
                                                         const int *__restrict__ pa, const int *__restrict__ pb,
                                                         const double *__restrict__ ev, const double *__restrict__ cg,
                                                         FilterW finv, FilterW fev, RadialW rad,
                                                         double *__restrict__ f_inv, double *__restrict__ f_ev,
-                                                        double *__restrict__ sp) {
+                                                        double *__restrict__ sp, double *__restrict__ drbf) {
   extern __shared__ double sm[];
   double *rbf = sm;               // TP x LDR
   double *u = rbf + TP * LDR;     // TP x LDU
@@ -154,6 +174,26 @@ __global__ void __launch_bounds__(256) k_filter_forward(int P, const double *__r
   __syncthreads();
   compute_rbf(rr, rbf, rad);
   __syncthreads();
+  if (drbf != nullptr) {
+    // d rbf_k / dr for the reverse pass (Bernstein derivative,
+    // block2_attention_input_reverse.cpp:322-333): zero where the basis is clamped
+    const int pl = tid >> 2, k0 = (tid & 3) * 8;
+    const int p = p0 + pl;
+    if (p < P) {
+      const double raw_x = exp(-rad.gamma * rr[pl]);
+      const bool live = raw_x > 1.0e-6 && raw_x < 1.0 - 1.0e-6;
+      const double ratio = live ? raw_x / (1.0 - raw_x) : 0.0;
+      double d[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int k = k0 + j;
+        d[j] = live ? rbf[pl * LDR + k] * (-rad.gamma * rad.k[k] + rad.gamma * rad.kr[k] * ratio) : 0.0;
+      }
+      double2 *dst = reinterpret_cast<double2 *>(drbf + (size_t)p * kR + k0);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dst[j] = make_double2(d[2 * j], d[2 * j + 1]);
+    }
+  }
   for (int filt = 0; filt < 2; ++filt) {
     const FilterW &W = filt ? fev : finv;
     double *out = filt ? f_ev : f_inv;
@@ -166,52 +206,58 @@ __global__ void __launch_bounds__(256) k_filter_forward(int P, const double *__r
         w[pl * LDR + j] = silu(s + W.c0[j]);
       }
     }
-    double acc[4][4][2];
+    double acc[2][4][4];
 #pragma unroll
-    for (int mi = 0; mi < 4; ++mi)
+    for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
-      for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
+      for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.0;
     mma_32x32<kR>(acc, rbf, LDR, W.w0t_f, wm, wn, lane);
     // hidden layer u = silu(pre) to shared memory, and silu'(pre) for the
     // reverse pass straight from the accumulators in fragment order
     double *sp_tile = sp + sp_offset(blockIdx.x, filt, warp);
 #pragma unroll
-    for (int mi = 0; mi < 4; ++mi)
+    for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
       for (int ni = 0; ni < 4; ++ni) {
-        const int row = wm * 32 + mi * 8 + g, col = wn * 32 + ni * 8 + 2 * t;
-        const double x0 = acc[mi][ni][0] + W.b0[col], x1 = acc[mi][ni][1] + W.b0[col + 1];
-        const double s0 = sigmoid(x0), s1 = sigmoid(x1);
-        u[row * LDU + col] = x0 * s0;
-        u[row * LDU + col + 1] = x1 * s1;
-        *reinterpret_cast<double2 *>(sp_tile + (mi * 4 + ni) * 64 + lane * 2) =
-            make_double2(s0 * (1.0 + x0 * (1.0 - s0)), s1 * (1.0 + x1 * (1.0 - s1)));
-        acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
+        const int col = wn * 32 + ni * 8 + 2 * t;
+        const double bb0 = W.b0[col], bb1 = W.b0[col + 1];
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {  // rows g and g + 8 of the m16 block
+          const int row = wm * 32 + mi * 16 + hf * 8 + g;
+          const double x0 = acc[mi][ni][2 * hf] + bb0, x1 = acc[mi][ni][2 * hf + 1] + bb1;
+          const double s0 = sigmoid(x0), s1 = sigmoid(x1);
+          *reinterpret_cast<double2 *>(u + row * LDU + col) = make_double2(x0 * s0, x1 * s1);
+          *reinterpret_cast<double2 *>(sp_tile + ((mi * 4 + ni) * 2 + hf) * 64 + lane * 2) =
+              make_double2(s0 * (1.0 + x0 * (1.0 - s0)), s1 * (1.0 + x1 * (1.0 - s1)));
+        }
+        acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.0;
       }
     __syncthreads();
     mma_32x32<kF>(acc, u, LDU, W.w1t_f, wm, wn, lane);
     mma_32x32<kEH>(acc, w, LDR, W.v1t_f, wm, wn, lane);
 #pragma unroll
-    for (int mi = 0; mi < 4; ++mi) {
-      const int row = wm * 32 + mi * 8 + g;
-      const int p = p0 + row;
-      if (p >= P) continue;
+    for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
-      for (int ni = 0; ni < 4; ++ni) {
-        const int col = wn * 32 + ni * 8 + 2 * t;
-        double2 v;
-        v.x = (acc[mi][ni][0] + W.b1[col]) + W.c1[col];
-        v.y = (acc[mi][ni][1] + W.b1[col + 1]) + W.c1[col + 1];
-        *reinterpret_cast<double2 *>(out + (size_t)p * kF + col) = v;
+      for (int hf = 0; hf < 2; ++hf) {
+        const int row = wm * 32 + mi * 16 + hf * 8 + g;
+        const int p = p0 + row;
+        if (p >= P) continue;
+#pragma unroll
+        for (int ni = 0; ni < 4; ++ni) {
+          const int col = wn * 32 + ni * 8 + 2 * t;
+          double2 v;
+          v.x = (acc[mi][ni][2 * hf] + W.b1[col]) + W.c1[col];
+          v.y = (acc[mi][ni][2 * hf + 1] + W.b1[col + 1]) + W.c1[col + 1];
+          *reinterpret_cast<double2 *>(out + (size_t)p * kF + col) = v;
+        }
       }
-    }
     __syncthreads();
   }
 }
 
 void launch_filter_forward(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
                            const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,
-                           double *f_inv, double *f_ev, double *sp, cudaStream_t s) {
+                           double *f_inv, double *f_ev, double *sp, double *drbf, cudaStream_t s) {
   if (P == 0) return;
   const size_t smem = sizeof(double) * (TP * LDR * 2 + TP * LDU + TP * 4 + TP);
   static bool configured = false;
@@ -220,7 +266,7 @@ void launch_filter_forward(int P, const double *geo, const int *pair_a, const in
     configured = true;
   }
   k_filter_forward<<<(P + TP - 1) / TP, 256, smem, s>>>(P, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad, f_inv,
-                                                         f_ev, sp);
+                                                         f_ev, sp, drbf);
   SO3_LAUNCH("filter_forward");
 }
 
@@ -273,8 +319,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
     int P, const double *__restrict__ geo, const int *__restrict__ pa, const int *__restrict__ pb,
     const double *__restrict__ ev, const double *__restrict__ cg, FilterW finv, FilterW fev, RadialW rad,
     const double *__restrict__ g_filt_inv, const double *__restrict__ g_filt_ev, const double *__restrict__ sp,
-    const double *__restrict__ gA, const double *__restrict__ pair_sc, int need_l0, double *__restrict__ gv,
-    double *__restrict__ gl0) {
+    const double *__restrict__ drbf, const double *__restrict__ gA, const double *__restrict__ pair_sc, int need_l0,
+    int accumulate, double *__restrict__ g_r, double *__restrict__ g_y, double *__restrict__ gl0) {
   namespace cgrp = cooperative_groups;
   cgrp::cluster_group cluster = cgrp::this_cluster();
   const int f = static_cast<int>(cluster.block_rank());  // 0: invariant filter, 1: ev filter
@@ -306,46 +352,51 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
   __syncthreads();
 
   // gradient of the hidden layer: (gF W1) * silu'(pre), warp tile 32 x 32
-  double acc[4][4][2];
+  double acc[2][4][4];
 #pragma unroll
-  for (int mi = 0; mi < 4; ++mi)
+  for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
-    for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
+    for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.0;
   mma_32x32<kF>(acc, gF, LDU, w1_f, wm, wn, lane);
 #pragma unroll
-  for (int mi = 0; mi < 4; ++mi)
+  for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
-    for (int ni = 0; ni < 4; ++ni) {
-      const double2 s = __ldg(reinterpret_cast<const double2 *>(sp_tile + (mi * 4 + ni) * 64 + lane * 2));
-      acc[mi][ni][0] *= s.x;
-      acc[mi][ni][1] *= s.y;
-    }
-  // ev branch: g_w = gF V1 (64 x 32), warp w owns rows 8w..8w+7
-  double gwa[4][2];
+    for (int ni = 0; ni < 4; ++ni)
 #pragma unroll
-  for (int ni = 0; ni < 4; ++ni) gwa[ni][0] = gwa[ni][1] = 0.0;
-  mma_8x32<kF>(gwa, gF, LDU, warp * 8, v1_f, lane);
+      for (int hf = 0; hf < 2; ++hf) {
+        const double2 s = __ldg(reinterpret_cast<const double2 *>(sp_tile + ((mi * 4 + ni) * 2 + hf) * 64 + lane * 2));
+        acc[mi][ni][2 * hf] *= s.x;
+        acc[mi][ni][2 * hf + 1] *= s.y;
+      }
+  // ev branch: g_w = gF V1 (64 x 32), warp tile 16 x 16
+  const int wr = warp >> 1, wc = warp & 1;
+  double gwa[2][4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) gwa[j][0] = gwa[j][1] = gwa[j][2] = gwa[j][3] = 0.0;
+  mma_16x16<kF>(gwa, gF, LDU, wr * 16, v1_f, wc, lane);
   __syncthreads();  // every warp is done reading gF
 #pragma unroll
-  for (int mi = 0; mi < 4; ++mi)
+  for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
-    for (int ni = 0; ni < 4; ++ni) {
-      const int row = wm * 32 + mi * 8 + g, col = wn * 32 + ni * 8 + 2 * t;
-      gF[row * LDU + col] = acc[mi][ni][0];
-      gF[row * LDU + col + 1] = acc[mi][ni][1];
+    for (int ni = 0; ni < 4; ++ni)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int row = wm * 32 + mi * 16 + hf * 8 + g, col = wn * 32 + ni * 8 + 2 * t;
+        *reinterpret_cast<double2 *>(gF + row * LDU + col) = make_double2(acc[mi][ni][2 * hf], acc[mi][ni][2 * hf + 1]);
+      }
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int row = wr * 16 + hf * 8 + g, col = wc * 16 + j * 8 + 2 * t;
+      *reinterpret_cast<double2 *>(gw + row * LDR + col) = make_double2(gwa[j][2 * hf], gwa[j][2 * hf + 1]);
     }
-#pragma unroll
-  for (int ni = 0; ni < 4; ++ni) {
-    const int row = warp * 8 + g, col = ni * 8 + 2 * t;
-    gw[row * LDR + col] = gwa[ni][0];
-    gw[row * LDR + col + 1] = gwa[ni][1];
-  }
   __syncthreads();
   // radial-basis gradient g_rbf = g_pre W0 (64 x 32)
-  double grb[4][2];
+  double grb[2][4];
 #pragma unroll
-  for (int ni = 0; ni < 4; ++ni) grb[ni][0] = grb[ni][1] = 0.0;
-  mma_8x32<kF>(grb, gF, LDU, warp * 8, w0_f, lane);
+  for (int j = 0; j < 2; ++j) grb[j][0] = grb[j][1] = grb[j][2] = grb[j][3] = 0.0;
+  mma_16x16<kF>(grb, gF, LDU, wr * 16, w0_f, wc, lane);
   // L0 gradient: g_pe = g_w * silu'(L0 V0^T + c0), gl[d] = sum_j g_pe[j] V0[j][d]
   if (need_l0) {
     {
@@ -366,18 +417,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
   }
   __syncthreads();  // gw and gF reads are done
 #pragma unroll
-  for (int ni = 0; ni < 4; ++ni) {
-    const int row = warp * 8 + g, col = ni * 8 + 2 * t;
-    gw[row * LDR + col] = grb[ni][0];
-    gw[row * LDR + col + 1] = grb[ni][1];
-  }
-  // rank 0 prefetches the tail's per-pair inputs into the free gF region
-  double *sc = gF;                        // TP x 32
-  double *geos = sc + TP * kPairScalars;  // TP x 8
-  double *ybuf = geos + TP * kGeo;        // TP x kEV
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int row = wr * 16 + hf * 8 + g, col = wc * 16 + j * 8 + 2 * t;
+      *reinterpret_cast<double2 *>(gw + row * LDR + col) = make_double2(grb[j][2 * hf], grb[j][2 * hf + 1]);
+    }
+  // rank 0 prefetches the per-pair inputs of the radial and harmonic gradients
+  // into the free gF region
+  double *sc = gF;                        // TP x 32 pair scalars
+  double *geos = sc + TP * kPairScalars;  // TP x 8 geometry
+  double *drs = geos + TP * kGeo;         // TP x 32 radial-basis derivatives
   if (f == 0) {
     stage_rows<kPairScalars>(sc, kPairScalars, pair_sc, p0, P);
     stage_rows<kGeo>(geos, kGeo, geo, p0, P);
+    stage_rows<kR>(drs, kR, drbf, p0, P);
     cp_async_commit();
   }
   cluster.sync();  // both CTAs' radial-basis and L0 gradients are in shared memory
@@ -395,67 +449,56 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
   cp_async_wait<0>();
   __syncthreads();
 
-  // per pair, phase 1 (warp per pair): radial + cutoff gradient and the
-  // harmonic gradient gY (pair orientation) -> shared memory
-  double *grs = l0;  // TP radial gradients (the L0 inputs are no longer needed)
-  for (int pl = warp; pl < TP; pl += 8) {
-    const int p = p0 + pl;
-    if (p >= P) continue;
-    const double *gp = geos + pl * kGeo;
-    const double r = gp[0], phi = gp[4], dphi = gp[5];
-    // Bernstein derivative (block2_attention_input_reverse.cpp:322-333); lane k
-    // evaluates basis function k (the same arithmetic as compute_rbf)
-    const double raw_x = exp(-rad.gamma * r);
-    double gr = 0.0;
-    if (raw_x > 1.0e-6 && raw_x < 1.0 - 1.0e-6) {
-      const double rbf_k = exp_tang(rad.b[lane] + rad.k[lane] * log(raw_x) + rad.kr[lane] * log(1.0 - raw_x));
-      const double dl = -rad.gamma * rad.k[lane] + rad.gamma * rad.kr[lane] * raw_x / (1.0 - raw_x);
-      gr = gw[pl * LDR + lane] * rbf_k * dl;
-    }
+  // Per pair: the radial gradient g_r = sum_k g_rbf[k] d rbf_k/dr + the cutoff
+  // term, and the harmonic gradient g_Y[m]; both are summed over the blocks
+  // (written by the first block reversed, added by the others) and turned into
+  // the Cartesian pair gradient once per evaluation (launch_pair_tail).
+  // Four threads per pair: thread q sums basis functions 8q..8q+7 and handles
+  // harmonic channels 6q..6q+5.
+  const int pl = tid >> 2, q = tid & 3;
+  const int p = p0 + pl;
+  double gr = 0.0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) gr += gw[pl * LDR + 8 * q + j] * drs[pl * kR + 8 * q + j];
+  const double *s = sc + pl * kPairScalars;
+  const double dphi = geos[pl * kGeo + 5], phi = geos[pl * kGeo + 4];
+  if (q == 0) {
     // cutoff gradient: sum over heads of alpha*s for both directions; the two
     // directions are added first (a commutative add), so the result does not
     // depend on which endpoint the pair is stored from
-    const double *s = sc + pl * kPairScalars;
-    const int h = lane & 3, which = lane >> 2;
-    if (which < 2) {
-      const int ai = which == 0 ? 0 : 4;  // (alpha_inv, s_inv) or (alpha_ev, s_ev)
-      gr += __dmul_rn(__dadd_rn(__dmul_rn(s[ai + h], s[ai + 8 + h]), __dmul_rn(s[16 + ai + h], s[16 + ai + 8 + h])),
-                      dphi);
-    }
-    if (lane < kEV) {
-      const int d = degree_of_channel(lane);
-      const double gAa = gA[(size_t)pa[p] * kEV + lane], gAb = gA[(size_t)pb[p] * kEV + lane];
-      ybuf[pl * kEV + lane] =
-          __dmul_rn(phi, __dadd_rn(__dmul_rn(s[4 + d], gAa), parity_sign(d) * __dmul_rn(s[20 + d], gAb)));
-    }
-    for (int off = 16; off > 0; off >>= 1) gr += __shfl_xor_sync(0xffffffffu, gr, off);
-    if (lane == 0) grs[pl] = gr;
-    if (need_l0 && lane < 4) gl0[(size_t)p * 4 + lane] = gl[pl * 4 + lane];
+#pragma unroll
+    for (int h = 0; h < 4; ++h)
+#pragma unroll
+      for (int ai = 0; ai <= 4; ai += 4)
+        gr += __dmul_rn(__dadd_rn(__dmul_rn(s[ai + h], s[ai + 8 + h]), __dmul_rn(s[16 + ai + h], s[16 + ai + 8 + h])),
+                        dphi);
   }
-  __syncthreads();
-  // phase 2 (thread per pair): spherical-harmonic VJP and the Cartesian pair gradient
-  if (tid < TP && p0 + tid < P) {
-    const int p = p0 + tid;
-    const double *gp = geos + tid * kGeo;
-    const double r = gp[0], ux = gp[1], uy = gp[2], uz = gp[3];
-    double gux, guy, guz;
-    real_sh_vjp(ux, uy, uz, ybuf + tid * kEV, gux, guy, guz);
-    const double rad_c = ux * gux + uy * guy + uz * guz;
-    const double ir = r > 1.0e-14 ? 1.0 / r : 0.0;
-    const double gr = grs[tid];
-    gv[3 * p] += gr * ux + (gux - ux * rad_c) * ir;
-    gv[3 * p + 1] += gr * uy + (guy - uy * rad_c) * ir;
-    gv[3 * p + 2] += gr * uz + (guz - uz * rad_c) * ir;
+  gr += __shfl_xor_sync(0xffffffffu, gr, 1);
+  gr += __shfl_xor_sync(0xffffffffu, gr, 2);
+  if (p < P) {
+    if (q == 0) g_r[p] = accumulate ? g_r[p] + gr : gr;
+    const int a = pa[p], b = pb[p];
+#pragma unroll
+    for (int j = 0; j < 6; ++j) {
+      const int m = 6 * q + j;
+      const int d = degree_of_channel(m);
+      const double y = __dmul_rn(phi, __dadd_rn(__dmul_rn(s[4 + d], gA[(size_t)a * kEV + m]),
+                                                parity_sign(d) * __dmul_rn(s[20 + d], gA[(size_t)b * kEV + m])));
+      double *dst = g_y + (size_t)p * kEV + m;
+      *dst = accumulate ? *dst + y : y;
+    }
+    if (need_l0) gl0[(size_t)p * 4 + q] = gl[pl * 4 + q];
   }
 }
 
 void launch_filter_reverse(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
                            const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,
-                           const double *g_filt_inv, const double *g_filt_ev, const double *sp, const double *gA,
-                           const double *pair_sc, bool need_l0, double *gv, double *gl0, cudaStream_t s) {
+                           const double *g_filt_inv, const double *g_filt_ev, const double *sp, const double *drbf,
+                           const double *gA, const double *pair_sc, bool need_l0, bool accumulate, double *g_r,
+                           double *g_y, double *gl0, cudaStream_t s) {
   if (P == 0) return;
   const size_t smem = sizeof(double) * (TP * LDU + TP * LDR + 8 * TP);
-  static_assert(TP * (kPairScalars + kGeo + kEV) <= TP * LDU, "tail inputs must fit in the gradient tile");
+  static_assert(TP * (kPairScalars + kGeo + kR) <= TP * LDU, "per-pair inputs must fit in the gradient tile");
   static bool configured = false;
   if (!configured) {
     SO3_CUDA(cudaFuncSetAttribute(k_filter_reverse, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
@@ -463,8 +506,43 @@ void launch_filter_reverse(int P, const double *geo, const int *pair_a, const in
   }
   const int tiles = (P + TP - 1) / TP;
   k_filter_reverse<<<2 * tiles, 256, smem, s>>>(P, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad, g_filt_inv,
-                                                g_filt_ev, sp, gA, pair_sc, need_l0 ? 1 : 0, gv, gl0);
+                                                g_filt_ev, sp, drbf, gA, pair_sc, need_l0 ? 1 : 0,
+                                                accumulate ? 1 : 0, g_r, g_y, gl0);
   SO3_LAUNCH("filter_reverse");
+}
+
+// ---------------------------------------------------------------------------
+// Cartesian pair gradient from the block-summed radial and harmonic gradients:
+// gv[p] += g_r u + (J_Y^T g_Y - u (u . J_Y^T g_Y)) / r, with J_Y the Jacobian of
+// the harmonic polynomials (learned_energy_forces.cpp:241-306)
+// ---------------------------------------------------------------------------
+__global__ void k_pair_tail(int P, const double *__restrict__ geo, const double *__restrict__ g_r,
+                            const double *__restrict__ g_y, double *__restrict__ gv) {
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= P) return;
+  const double *gp = geo + (size_t)p * kGeo;
+  const double r = gp[0], ux = gp[1], uy = gp[2], uz = gp[3];
+  double y[kEV];
+#pragma unroll
+  for (int m = 0; m < kEV; m += 2) {
+    const double2 v = *reinterpret_cast<const double2 *>(g_y + (size_t)p * kEV + m);
+    y[m] = v.x;
+    y[m + 1] = v.y;
+  }
+  double gux, guy, guz;
+  real_sh_vjp(ux, uy, uz, y, gux, guy, guz);
+  const double rad_c = ux * gux + uy * guy + uz * guz;
+  const double ir = r > 1.0e-14 ? 1.0 / r : 0.0;
+  const double gr = g_r[p];
+  gv[3 * (size_t)p] += gr * ux + (gux - ux * rad_c) * ir;
+  gv[3 * (size_t)p + 1] += gr * uy + (guy - uy * rad_c) * ir;
+  gv[3 * (size_t)p + 2] += gr * uz + (guz - uz * rad_c) * ir;
+}
+
+void launch_pair_tail(int P, const double *geo, const double *g_r, const double *g_y, double *gv, cudaStream_t s) {
+  if (P == 0) return;
+  k_pair_tail<<<(P + 127) / 128, 128, 0, s>>>(P, geo, g_r, g_y, gv);
+  SO3_LAUNCH("pair_tail");
 }
 
 }  // namespace so3lr_b200

@@ -78,17 +78,23 @@ void long_range_noalloc(int n, const double *x, const double *q, const double *h
                         double *w_atom, cudaStream_t s);
 
 // ---- filters (pair tiles, FP64 tensor cores) --------------------------------
-// sp: silu' of the rbf-branch hidden layer for the reverse pass, filter_sp_doubles(P) doubles
+// sp: silu' of the rbf-branch hidden layer for the reverse pass, filter_sp_doubles(P) doubles;
+// drbf (optional, P x 32): d rbf_k / dr of every pair (it depends on the geometry only)
 void launch_filter_forward(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
                            const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,
-                           double *f_inv, double *f_ev, double *sp, cudaStream_t s);
+                           double *f_inv, double *f_ev, double *sp, double *drbf, cudaStream_t s);
 inline std::size_t filter_sp_doubles(int P) { return std::size_t((P + 63) / 64) * 2 * 64 * 128; }
 // g_filt_inv / g_filt_ev: per-pair gradient w.r.t. the two filter outputs (written by
 // the attention reverse at each pair's primary edge)
+// g_r (P) and g_y (P x 24): per-pair radial and harmonic gradients, written
+// (accumulate = false) or added to (accumulate = true); launch_pair_tail turns
+// their block sums into the Cartesian pair gradient gv (P x 3, +=)
 void launch_filter_reverse(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
                            const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,
-                           const double *g_filt_inv, const double *g_filt_ev, const double *sp, const double *gA,
-                           const double *pair_sc, bool need_l0, double *gv, double *gl0, cudaStream_t s);
+                           const double *g_filt_inv, const double *g_filt_ev, const double *sp, const double *drbf,
+                           const double *gA, const double *pair_sc, bool need_l0, bool accumulate, double *g_r,
+                           double *g_y, double *gl0, cudaStream_t s);
+void launch_pair_tail(int P, const double *geo, const double *g_r, const double *g_y, double *gv, cudaStream_t s);
 
 // ---- attention (receiver CSR gathers) ----------------------------------------
 void launch_attention_forward(int n, const NeighborState &nb, const double *geo, const double *sh,
