@@ -24,24 +24,6 @@ __device__ inline double head_sum(double v) {  // sum over the 8 lanes of a head
   return v;
 }
 
-// per-degree sums of a value held by lanes 0..23; returns the sum for degree `want`
-__device__ inline void degree_sums(double v, double out[4]) {
-  const int lane = threadIdx.x & 31;
-  const int d = lane < kEV ? degree_of_channel(lane) : -1;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    double s = d == k ? v : 0.0;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    out[k] = s;
-  }
-}
-
-// v[i] for a runtime index without dynamic register-array indexing
-__device__ inline double pick4(const double (&v)[4], int i) {
-  return i == 0 ? v[0] : (i == 1 ? v[1] : (i == 2 ? v[2] : v[3]));
-}
-
 __device__ inline void load4(const double *p, double (&v)[4]) {
   const double2 a = *reinterpret_cast<const double2 *>(p);
   const double2 b = *reinterpret_cast<const double2 *>(p + 2);
@@ -169,9 +151,17 @@ __global__ void __launch_bounds__(256) k_attention_reverse(
   load4(qa_row + 3 * 32, qea);
   load4(qa_row + 4 * 32, kea);
   load4(g_a + (size_t)a * kF + lane * 4, ga);
-  const double gAa = lane < kEV ? g_A[(size_t)a * kEV + lane] : 0.0;
-  const int my_deg = lane < kEV ? degree_of_channel(lane) : 0;
-  const double my_par = parity_sign(my_deg);
+  // Equivariant channels by degree group: the 8 lanes of head h hold the
+  // channels of degree slot h (3, 5, 7 and 9 channels; lane 24 holds the ninth
+  // channel of the last degree as well), so a 3-step reduction inside the group
+  // gives every lane the degree sum its head uses.
+  const int dbase = h == 0 ? 0 : (h == 1 ? 3 : (h == 2 ? 8 : 15));
+  const int dcount = h == 0 ? 3 : (h == 1 ? 5 : (h == 2 ? 7 : 8));
+  const int ch0 = (lane & 7) < dcount ? dbase + (lane & 7) : -1;
+  const int ch1 = lane == 24 ? 23 : -1;
+  const double par = parity_sign(h);
+  const double gAa0 = ch0 >= 0 ? g_A[(size_t)a * kEV + ch0] : 0.0;
+  const double gAa1 = ch1 >= 0 ? g_A[(size_t)a * kEV + ch1] : 0.0;
   double gq[4] = {0, 0, 0, 0}, gk[4] = {0, 0, 0, 0}, gv[4] = {0, 0, 0, 0}, gqe[4] = {0, 0, 0, 0},
          gke[4] = {0, 0, 0, 0};
   const double inv_norm = 1.0 / norm;
@@ -183,18 +173,22 @@ __global__ void __launch_bounds__(256) k_attention_reverse(
     const int code = code_nx;
     if (e + 1 < e1) { b_nx = nbr[e + 1]; code_nx = edge_pair[e + 1]; }
     const int p = code >= 0 ? code : ~code;
-    if (e + 1 < e1) {  // pull the next edge's rows into L1 while this one is processed
+    if (e + 1 < e1) {
+      // pull the next edge's rows into L1 while this one is processed: the qkv
+      // row (40 lines of 128 B), g_a, f_inv and f_ev (8 lines each), and the
+      // two 96-byte halves of g_A and of the harmonics
       const int p_nx = code_nx >= 0 ? code_nx : ~code_nx;
-      // 68 prefetches: qkv row (40 lines of 128 B), g_a, f_inv, f_ev (8 each), g_A and sh (two 96-byte halves each)
-      for (int c = lane; c < 68; c += 32) {
-        const char *addr;
-        if (c < 40) addr = reinterpret_cast<const char *>(qkv + (size_t)b_nx * kQKV) + 128 * c;
-        else if (c < 48) addr = reinterpret_cast<const char *>(g_a + (size_t)b_nx * kF) + 128 * (c - 40);
-        else if (c < 56) addr = reinterpret_cast<const char *>(f_inv + (size_t)p_nx * kF) + 128 * (c - 48);
-        else if (c < 64) addr = reinterpret_cast<const char *>(f_ev + (size_t)p_nx * kF) + 128 * (c - 56);
-        else if (c < 66) addr = reinterpret_cast<const char *>(g_A + (size_t)b_nx * kEV) + 96 * (c - 64);
-        else addr = reinterpret_cast<const char *>(sh + (size_t)p_nx * kEV) + 96 * (c - 66);
-        asm volatile("prefetch.global.L1 [%0];\n" ::"l"(addr));
+      const char *qrow = reinterpret_cast<const char *>(qkv + (size_t)b_nx * kQKV);
+      const char *l1 = lane < 8 ? qrow + 128 * (32 + lane)
+                     : lane < 16 ? reinterpret_cast<const char *>(g_a + (size_t)b_nx * kF) + 128 * (lane - 8)
+                     : lane < 24 ? reinterpret_cast<const char *>(f_inv + (size_t)p_nx * kF) + 128 * (lane - 16)
+                                 : reinterpret_cast<const char *>(f_ev + (size_t)p_nx * kF) + 128 * (lane - 24);
+      asm volatile("prefetch.global.L1 [%0];\n" ::"l"(qrow + 128 * lane));
+      asm volatile("prefetch.global.L1 [%0];\n" ::"l"(l1));
+      if (lane < 4) {
+        const char *l2 = lane < 2 ? reinterpret_cast<const char *>(g_A + (size_t)b_nx * kEV) + 96 * lane
+                                  : reinterpret_cast<const char *>(sh + (size_t)p_nx * kEV) + 96 * (lane - 2);
+        asm volatile("prefetch.global.L1 [%0];\n" ::"l"(l2));
       }
     }
     const double phi = geo[(size_t)p * kGeo + 4];
@@ -208,37 +202,32 @@ __global__ void __launch_bounds__(256) k_attention_reverse(
     load4(g_a + (size_t)b * kF + lane * 4, gb);
     load4(f_inv + (size_t)p * kF + lane * 4, fi);
     load4(f_ev + (size_t)p * kF + lane * 4, fe);
-    const double gAb = lane < kEV ? g_A[(size_t)b * kEV + lane] : 0.0;
-    double y = lane < kEV ? sh[(size_t)p * kEV + lane] : 0.0;
-    const double y_in = code < 0 ? y * my_par : y;
-    const double y_out = y_in * my_par;
-    double ai_in = 0, ae_in = 0, ai_out = 0, ae_out = 0, si_in = 0, si_out = 0;
+    // harmonic-weighted adjoint sums per degree, for edge b->a ("in": y of the
+    // edge into a) and a->b ("out": parity times that)
+    double s_in, s_out;
+    {
+      const double pin = code < 0 ? par : 1.0;  // harmonics are stored for the primary orientation
+      const double y0 = ch0 >= 0 ? sh[(size_t)p * kEV + ch0] * pin : 0.0;
+      const double y1 = ch1 >= 0 ? sh[(size_t)p * kEV + ch1] * pin : 0.0;
+      const double gAb0 = ch0 >= 0 ? g_A[(size_t)b * kEV + ch0] : 0.0;
+      const double gAb1 = ch1 >= 0 ? g_A[(size_t)b * kEV + ch1] : 0.0;
+      s_in = gAa0 * y0 + gAa1 * y1;
+      s_out = (gAb0 * y0 + gAb1 * y1) * par;
+      s_in = head_sum(s_in);
+      s_out = head_sum(s_out);
+    }
+    double ai_out = 0, si_in = 0, si_out = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      ai_in += qa[j] * kb[j] * fi[j];
-      ae_in += qea[j] * keb[j] * fe[j];
       ai_out += qb[j] * ka[j] * fi[j];
-      ae_out += qeb[j] * kea[j] * fe[j];
       si_in += ga[j] * vb[j];
       si_out += gb[j] * va[j];
     }
-    ai_in = head_sum(ai_in) / norm;
-    ae_in = head_sum(ae_in) / norm;
     ai_out = head_sum(ai_out) / norm;
-    ae_out = head_sum(ae_out) / norm;
     si_in = head_sum(si_in);
     si_out = head_sum(si_out);
-    double se_in, se_out, se_in_q, se_out_q;
-    const int qsel = lane >> 2, hh = lane & 3;
-    double se_in_d[4], se_out_d[4];
-    degree_sums(gAa * y_in, se_in_d);
-    degree_sums(gAb * y_out, se_out_d);
-    se_in = pick4(se_in_d, h);
-    se_out = pick4(se_out_d, h);
-    se_in_q = pick4(se_in_d, hh);
-    se_out_q = pick4(se_out_d, hh);
-    const double c_q = phi * si_in * inv_norm, c_qe = phi * se_in * inv_norm;
-    const double c_v = phi * ai_out, c_k = phi * si_out * inv_norm, c_ke = phi * se_out * inv_norm;
+    const double c_q = phi * si_in * inv_norm, c_qe = phi * s_in * inv_norm;
+    const double c_v = phi * ai_out, c_k = phi * si_out * inv_norm, c_ke = phi * s_out * inv_norm;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       gq[j] += c_q * (kb[j] * fi[j]);
@@ -247,33 +236,52 @@ __global__ void __launch_bounds__(256) k_attention_reverse(
       gk[j] += c_k * (qb[j] * fi[j]);
       gke[j] += c_ke * (qeb[j] * fe[j]);
     }
-    if (code >= 0 && g_filt_inv != nullptr) {
-      double gi[4], ge[4];
+    if (code >= 0) {
+      // primary edge: the pair's filter gradient and its per-head scalars
+      if (g_filt_inv != nullptr) {
+        // g_f_inv[c] = phi/norm (s_in[h] q_a[c] k_b[c] + s_out[h] q_b[c] k_a[c]), same for ev;
+        // explicitly rounded products and sum (no FMA contraction): the two
+        // directions' terms swap when the pair is held from its other endpoint,
+        // and a rounded sum is exactly commutative
+        double gi[4], ge[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          gi[j] = __dadd_rn(__dmul_rn(c_q, __dmul_rn(qa[j], kb[j])), __dmul_rn(c_k, __dmul_rn(qb[j], ka[j])));
+          ge[j] = __dadd_rn(__dmul_rn(c_qe, __dmul_rn(qea[j], keb[j])), __dmul_rn(c_ke, __dmul_rn(qeb[j], kea[j])));
+        }
+        store4(g_filt_inv + (size_t)p * kF + lane * 4, gi);
+        store4(g_filt_ev + (size_t)p * kF + lane * 4, ge);
+      }
+      double ai_in = 0, ae_in = 0, ae_out = 0;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        gi[j] = __dadd_rn(__dmul_rn(c_q, __dmul_rn(qa[j], kb[j])), __dmul_rn(c_k, __dmul_rn(qb[j], ka[j])));
-        ge[j] = __dadd_rn(__dmul_rn(c_qe, __dmul_rn(qea[j], keb[j])), __dmul_rn(c_ke, __dmul_rn(qeb[j], kea[j])));
+        ai_in += qa[j] * kb[j] * fi[j];
+        ae_in += qea[j] * keb[j] * fe[j];
+        ae_out += qeb[j] * kea[j] * fe[j];
       }
-      store4(g_filt_inv + (size_t)p * kF + lane * 4, gi);
-      store4(g_filt_ev + (size_t)p * kF + lane * 4, ge);
-    }
-    if (code >= 0) {
+      ai_in = head_sum(ai_in) / norm;
+      ae_in = head_sum(ae_in) / norm;
+      ae_out = head_sum(ae_out) / norm;
+      // "in" is into the pair's primary receiver a; lane = 4 quantity + head
+      const int qsel = lane >> 2, hh = lane & 3;
       const double v_ai_in = __shfl_sync(0xffffffffu, ai_in, hh * 8);
       const double v_ae_in = __shfl_sync(0xffffffffu, ae_in, hh * 8);
       const double v_si_in = __shfl_sync(0xffffffffu, si_in, hh * 8);
+      const double v_se_in = __shfl_sync(0xffffffffu, s_in, hh * 8);
       const double v_ai_out = __shfl_sync(0xffffffffu, ai_out, hh * 8);
       const double v_ae_out = __shfl_sync(0xffffffffu, ae_out, hh * 8);
       const double v_si_out = __shfl_sync(0xffffffffu, si_out, hh * 8);
+      const double v_se_out = __shfl_sync(0xffffffffu, s_out, hh * 8);
       double val;
       switch (qsel) {
         case 0: val = v_ai_in; break;
         case 1: val = v_ae_in; break;
         case 2: val = v_si_in; break;
-        case 3: val = se_in_q; break;
+        case 3: val = v_se_in; break;
         case 4: val = v_ai_out; break;
         case 5: val = v_ae_out; break;
         case 6: val = v_si_out; break;
-        default: val = se_out_q; break;
+        default: val = v_se_out; break;
       }
       pair_sc[(size_t)p * kPairScalars + lane] = val;
     }
