@@ -131,7 +131,7 @@ void launch_attention_forward(int n, const NeighborState &nb, const double *geo,
 // Reverse: given g_a = dL/d(d_inv) (= dL/da) and g_A = dL/d(d_ev) for every atom,
 // produce dL/d{q,k,v,q_ev,k_ev} per atom and, for the primary edge of every pair,
 // the scalars the filter reverse needs.
-__global__ void __launch_bounds__(256) k_attention_reverse(
+__global__ void __launch_bounds__(32) k_attention_reverse(
     int n, int row0, const int *__restrict__ row_start, const int *__restrict__ nbr, const int *__restrict__ edge_pair,
     const double *__restrict__ geo, const double *__restrict__ sh, const double *__restrict__ qkv,
     const double *__restrict__ f_inv, const double *__restrict__ f_ev, const double *__restrict__ g_a,
@@ -301,7 +301,9 @@ void launch_attention_reverse(int n, const NeighborState &nb, const double *geo,
                               const double *g_A, double norm, double *g_qkv, double *pair_sc, double *g_filt_inv,
                               double *g_filt_ev, cudaStream_t s) {
   if (n == 0) return;
-  k_attention_reverse<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.edge_pair, geo, sh,
+  // one warp per CTA: at ~190 registers per thread a CTA's registers are freed
+  // as soon as its own atom is done, instead of waiting for the slowest of eight
+  k_attention_reverse<<<n, 32, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.edge_pair, geo, sh,
                                                            qkv, f_inv, f_ev, g_a, g_A, norm, g_qkv, pair_sc,
                                                            g_filt_inv, g_filt_ev);
   SO3_LAUNCH("attention_reverse");
