@@ -111,6 +111,31 @@ __device__ __forceinline__ void dmma16(double (&c)[4], const double (&a)[4], con
                : "d"(a[0]), "d"(a[1]), "d"(a[2]), "d"(a[3]), "d"(b[0]), "d"(b[1]));
 }
 
+// A fragment of an m16n8k8 DMMA from a row-major shared-memory tile whose MMA k
+// slots t and t + 4 of k-step ks are the physical columns 8 ks + 2t and
+// 8 ks + 2t + 1 (a permutation of the contraction index; the B operand uses the
+// same one), so a lane's two values of a row are one 16-byte load:
+// a = {A[r+g][c], A[r+g+8][c], A[r+g][c+1], A[r+g+8][c+1]}, c = 8 ks + 2t
+__device__ __forceinline__ void load_afrag(const double *A, int lda, int r, int ks, int g, int t, double (&a)[4]) {
+  const double2 x = *reinterpret_cast<const double2 *>(A + (r + g) * lda + 8 * ks + 2 * t);
+  const double2 y = *reinterpret_cast<const double2 *>(A + (r + g + 8) * lda + 8 * ks + 2 * t);
+  a[0] = x.x;
+  a[1] = y.x;
+  a[2] = x.y;
+  a[3] = y.y;
+}
+
+// 16-byte global -> shared copies that bypass registers
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
 __device__ __forceinline__ double silu(double x) { return x * sigmoid(x); }
 __device__ __forceinline__ double silu_prime(double x) {
   const double s = sigmoid(x);
@@ -152,6 +177,7 @@ struct HeadsW {
   double c_b2;
   const double *c_emb;             // [100]
   const double *h_w2, *h_b2;       // [64][64], [64]
+  const double *h_w2t;             // [64][64]: h_w2 transposed ([in][out])
   const double *h_qemb, *h_vshift; // [100][64], [100]
 };
 struct RadialW {

@@ -163,7 +163,12 @@ void Evaluator::upload_weights() {
   const std::size_t o_cw2 = push(model_.f64(co + "transform_inv_features.2.weight", {1, 128}));
   const double c_b2 = model_.f64(co + "transform_inv_features.2.bias", {1})[0];
   const std::size_t o_cemb = push(model_.f64(co + "atomic_embedding.weight", {100, 1}));
-  const std::size_t o_hw2 = push(model_.f64(ho + "transform_features.2.weight", {64, 64}));
+  const auto hw2 = model_.f64(ho + "transform_features.2.weight", {64, 64});
+  const std::size_t o_hw2 = push(hw2);
+  std::vector<double> hw2t(64 * 64);
+  for (int k = 0; k < 64; ++k)
+    for (int j = 0; j < 64; ++j) hw2t[std::size_t(j) * 64 + k] = hw2[std::size_t(k) * 64 + j];
+  const std::size_t o_hw2t = push(hw2t);
   const std::size_t o_hb2 = push(model_.f64(ho + "transform_features.2.bias", {64}));
   const std::size_t o_hq = push(model_.f64(ho + "q_embedding.weight", {100, 64}));
   const std::size_t o_hv = push(model_.f64(ho + "v_shift_embedding.weight", {100, 1}));
@@ -211,6 +216,7 @@ void Evaluator::upload_weights() {
   heads_.c_b2 = c_b2;
   heads_.c_emb = P(o_cemb);
   heads_.h_w2 = P(o_hw2);
+  heads_.h_w2t = P(o_hw2t);
   heads_.h_b2 = P(o_hb2);
   heads_.h_qemb = P(o_hq);
   heads_.h_vshift = P(o_hv);

@@ -70,19 +70,6 @@ __device__ inline void compute_l0(int P, int p0, const int *pa, const int *pb, c
   l0[pl * 4 + d] = v;
 }
 
-// The MMA's k slots t and t + 4 of k-step ks are the physical columns 8 ks + 2t
-// and 8 ks + 2t + 1 (a permutation of the contraction index; the weight copies
-// use the same one), so a lane's A values of one row are adjacent.
-// a = {A[r+g][.], A[r+g+8][.], A[r+g][.+1], A[r+g+8][.+1]} at column 8 ks + 2t
-__device__ __forceinline__ void load_afrag(const double *A, int lda, int r, int ks, int g, int t, double (&a)[4]) {
-  const double2 x = *reinterpret_cast<const double2 *>(A + (r + g) * lda + 8 * ks + 2 * t);
-  const double2 y = *reinterpret_cast<const double2 *>(A + (r + g + 8) * lda + 8 * ks + 2 * t);
-  a[0] = x.x;
-  a[1] = y.x;
-  a[2] = x.y;
-  a[3] = y.y;
-}
-
 // b[j] = {B(8 ks + 2t, n), B(8 ks + 2t + 1, n)}, n = 32 slab + 8 (ni0 + j) + g, for
 // j < NB, from a fragment-major operand with `nslab` column slabs (8
 // contiguous doubles per lane and k-step)
@@ -281,13 +268,6 @@ void launch_filter_forward(int P, const double *geo, const int *pair_a, const in
 // start so the tensor-core work never waits on a gather.
 // ---------------------------------------------------------------------------
 namespace {
-__device__ inline void cp_async16(void *smem, const void *gmem) {
-  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
-}
-__device__ inline void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-__device__ inline void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
 // copy a TP x width block of a row-major global array (row stride = width) to
 // shared memory with row stride lds; rows beyond P are zero-filled

@@ -15,12 +15,26 @@
 namespace so3lr_b200 {
 namespace {
 
-constexpr int BM = 64, BN = 64, BK = 16, LDS = BK + 4;
+// 64 x 64 output tile per CTA, 4 warps of 32 x 32 (2 x 4 m16n8k8 blocks), K in
+// steps of 16 through a two-stage cp.async pipeline. A is staged as [m][k] and
+// B as [n][k] (transposed weights) or [k][n]; the shared-memory row strides keep
+// the fragment loads free of bank conflicts (24 = 8 mod 16 doubles for 16-byte
+// loads of two rows, 66 = 2 mod 16 for 8-byte loads of four k rows).
+constexpr int BM = 64, BN = 64, BK = 16;
+constexpr int LDA_S = BK + 8, LDBT_S = BK + 8, LDBN_S = BN + 2;
+constexpr int kGemmThreads = 128;
+template <bool TRANSB>
+constexpr int gemm_smem_doubles() {
+  return 2 * BM * LDA_S + 2 * (TRANSB ? BN * LDBT_S : BK * LDBN_S);
+}
 
 template <bool TRANSB, Epi EPI>
-__global__ void __launch_bounds__(128) k_gemm(GemmArgs g, int aux_cols, int ldaux2) {
-  __shared__ double As[BM * LDS];
-  __shared__ double Bs[BN * LDS];
+__global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols, int ldaux2) {
+  extern __shared__ double gsm[];
+  constexpr int ASTAGE = BM * LDA_S;
+  constexpr int BSTAGE = TRANSB ? BN * LDBT_S : BK * LDBN_S;
+  double *As = gsm;
+  double *Bs = gsm + 2 * ASTAGE;
   const int z = blockIdx.z;
   const double *A = g.A + z * g.strideA;
   const double *W = g.W + z * g.strideW;
@@ -30,97 +44,143 @@ __global__ void __launch_bounds__(128) k_gemm(GemmArgs g, int aux_cols, int ldau
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
   const int wm = warp >> 1, wn = warp & 1;
-  double acc[4][4][2];
-#pragma unroll
-  for (int mi = 0; mi < 4; ++mi)
-#pragma unroll
-    for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = 0.0;
-  for (int k0 = 0; k0 < g.K; k0 += BK) {
-    // A tile 64 x 16: 1024 elements, 8 per thread
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const int idx = tid + r * 128;
-      const int row = idx >> 4, col = idx & 15;
+  auto load_stage = [&](int stage, int k0) {
+    double *as = As + stage * ASTAGE;
+    for (int c = tid; c < BM * BK / 2; c += kGemmThreads) {
+      const int row = c / (BK / 2), col = (c % (BK / 2)) * 2;
       const int gm = m0 + row, gk = k0 + col;
-      As[row * LDS + col] = (gm < g.M && gk < g.K) ? A[(size_t)gm * g.lda + gk] : 0.0;
-    }
-    // B tile stored as Bs[n][k]
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const int idx = tid + r * 128;
-      int nn, kk;
-      if (TRANSB) {
-        nn = idx >> 4;
-        kk = idx & 15;
+      double *dst = as + row * LDA_S + col;
+      if (gm < g.M && gk < g.K) {
+        cp_async16(dst, A + (size_t)gm * g.lda + gk);
       } else {
-        kk = idx >> 6;
-        nn = idx & 63;
+        dst[0] = 0.0;
+        dst[1] = 0.0;
       }
-      const int gn = n0 + nn, gk = k0 + kk;
-      double v = 0.0;
-      if (gn < g.N && gk < g.K) v = TRANSB ? W[(size_t)gn * g.ldw + gk] : W[(size_t)gk * g.ldw + gn];
-      Bs[nn * LDS + kk] = v;
     }
-    __syncthreads();
-#pragma unroll
-    for (int kk = 0; kk < BK; kk += 4) {
-      double a[4], b[4];
-#pragma unroll
-      for (int mi = 0; mi < 4; ++mi) a[mi] = As[(wm * 32 + mi * 8 + gq) * LDS + kk + tq];
-#pragma unroll
-      for (int ni = 0; ni < 4; ++ni) b[ni] = Bs[(wn * 32 + ni * 8 + gq) * LDS + kk + tq];
-#pragma unroll
-      for (int mi = 0; mi < 4; ++mi)
-#pragma unroll
-        for (int ni = 0; ni < 4; ++ni) dmma(acc[mi][ni][0], acc[mi][ni][1], a[mi], b[ni]);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int mi = 0; mi < 4; ++mi) {
-    const int row = m0 + wm * 32 + mi * 8 + gq;
-    if (row >= g.M) continue;
-#pragma unroll
-    for (int ni = 0; ni < 4; ++ni) {
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int col = n0 + wn * 32 + ni * 8 + 2 * tq + h;
-        if (col >= g.N) continue;
-        double v = acc[mi][ni][h];
-        if (EPI == Epi::Bias) {
-          v += bias[col];
-        } else if (EPI == Epi::BiasSilu) {
-          v = silu(v + bias[col]);
-        } else if (EPI == Epi::BiasStorePre) {
-          const double pre = v + bias[col];
-          g.aux_out[(size_t)row * g.ldaux + col] = pre;
-          v = silu(pre);
-        } else if (EPI == Epi::AddResidual) {
-          if (col < aux_cols) v += aux[(size_t)row * g.ldaux + col];
-        } else if (EPI == Epi::BiasResidual) {
-          v = v + bias[col] + aux[(size_t)row * g.ldaux + col];
-        } else if (EPI == Epi::SiluPrimeMul) {
-          v *= silu_prime(aux[(size_t)row * g.ldaux + col]);
-        } else if (EPI == Epi::GateSiluResidual) {
-          v = g.aux2[(size_t)row * ldaux2 + col] + v * silu_prime(aux[(size_t)row * g.ldaux + col]);
+    double *bs = Bs + stage * BSTAGE;
+    if (TRANSB) {  // W[n][k]
+      for (int c = tid; c < BN * BK / 2; c += kGemmThreads) {
+        const int nn = c / (BK / 2), col = (c % (BK / 2)) * 2;
+        const int gn = n0 + nn, gk = k0 + col;
+        double *dst = bs + nn * LDBT_S + col;
+        if (gn < g.N && gk < g.K) {
+          cp_async16(dst, W + (size_t)gn * g.ldw + gk);
+        } else {
+          dst[0] = 0.0;
+          dst[1] = 0.0;
         }
-        C[(size_t)row * g.ldc + col] = v;
+      }
+    } else {  // W[k][n]
+      for (int c = tid; c < BK * BN / 2; c += kGemmThreads) {
+        const int kk = c / (BN / 2), col = (c % (BN / 2)) * 2;
+        const int gk = k0 + kk, gn = n0 + col;
+        double *dst = bs + kk * LDBN_S + col;
+        if (gk < g.K && gn < g.N) {
+          cp_async16(dst, W + (size_t)gk * g.ldw + gn);
+        } else {
+          dst[0] = 0.0;
+          dst[1] = 0.0;
+        }
       }
     }
+  };
+  double acc[2][4][4];
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.0;
+  const int nk = (g.K + BK - 1) / BK;
+  load_stage(0, 0);
+  cp_async_commit();
+  for (int kt = 0; kt < nk; ++kt) {
+    if (kt + 1 < nk) load_stage((kt + 1) & 1, (kt + 1) * BK);
+    cp_async_commit();
+    cp_async_wait<1>();  // stage kt has landed
+    __syncthreads();
+    const double *as = As + (kt & 1) * ASTAGE;
+    const double *bs = Bs + (kt & 1) * BSTAGE;
+#pragma unroll
+    for (int ks = 0; ks < BK / 8; ++ks) {
+      double a[2][4], b[4][2];
+      load_afrag(as, LDA_S, wm * 32, ks, gq, tq, a[0]);
+      load_afrag(as, LDA_S, wm * 32 + 16, ks, gq, tq, a[1]);
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) {
+        const int nn = wn * 32 + ni * 8 + gq;
+        if (TRANSB) {
+          const double2 v = *reinterpret_cast<const double2 *>(bs + nn * LDBT_S + 8 * ks + 2 * tq);
+          b[ni][0] = v.x;
+          b[ni][1] = v.y;
+        } else {
+          b[ni][0] = bs[(8 * ks + 2 * tq) * LDBN_S + nn];
+          b[ni][1] = bs[(8 * ks + 2 * tq + 1) * LDBN_S + nn];
+        }
+      }
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+        for (int ni = 0; ni < 4; ++ni) dmma16(acc[mi][ni], a[mi], b[ni]);
+    }
+    __syncthreads();  // the stage is refilled two iterations later
   }
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int row = m0 + wm * 32 + mi * 16 + hf * 8 + gq;
+      if (row >= g.M) continue;
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int col = n0 + wn * 32 + ni * 8 + 2 * tq + h;
+          if (col >= g.N) continue;
+          double v = acc[mi][ni][2 * hf + h];
+          if (EPI == Epi::Bias) {
+            v += bias[col];
+          } else if (EPI == Epi::BiasSilu) {
+            v = silu(v + bias[col]);
+          } else if (EPI == Epi::BiasStorePre) {
+            const double pre = v + bias[col];
+            g.aux_out[(size_t)row * g.ldaux + col] = pre;
+            v = silu(pre);
+          } else if (EPI == Epi::AddResidual) {
+            if (col < aux_cols) v += aux[(size_t)row * g.ldaux + col];
+          } else if (EPI == Epi::BiasResidual) {
+            v = v + bias[col] + aux[(size_t)row * g.ldaux + col];
+          } else if (EPI == Epi::SiluPrimeMul) {
+            v *= silu_prime(aux[(size_t)row * g.ldaux + col]);
+          } else if (EPI == Epi::GateSiluResidual) {
+            v = g.aux2[(size_t)row * ldaux2 + col] + v * silu_prime(aux[(size_t)row * g.ldaux + col]);
+          }
+          C[(size_t)row * g.ldc + col] = v;
+        }
+      }
+    }
+}
+
+template <bool T, Epi E>
+void launch_gemm_kernel(const GemmArgs &g, dim3 grid, cudaStream_t s, int aux_cols, int ldaux2) {
+  constexpr size_t smem = sizeof(double) * gemm_smem_doubles<T>();
+  static bool configured = false;
+  if (!configured) {
+    SO3_CUDA(cudaFuncSetAttribute(k_gemm<T, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    configured = true;
+  }
+  k_gemm<T, E><<<grid, kGemmThreads, smem, s>>>(g, aux_cols, ldaux2);
 }
 
 template <bool T>
 void dispatch_epi(const GemmArgs &g, dim3 grid, cudaStream_t s, int aux_cols, int ldaux2) {
   switch (g.epi) {
-    case Epi::None: k_gemm<T, Epi::None><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
-    case Epi::Bias: k_gemm<T, Epi::Bias><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
-    case Epi::BiasSilu: k_gemm<T, Epi::BiasSilu><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
-    case Epi::BiasStorePre: k_gemm<T, Epi::BiasStorePre><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
-    case Epi::AddResidual: k_gemm<T, Epi::AddResidual><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
-    case Epi::BiasResidual: k_gemm<T, Epi::BiasResidual><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
-    case Epi::SiluPrimeMul: k_gemm<T, Epi::SiluPrimeMul><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
-    case Epi::GateSiluResidual: k_gemm<T, Epi::GateSiluResidual><<<grid, 128, 0, s>>>(g, aux_cols, ldaux2); break;
+    case Epi::None: launch_gemm_kernel<T, Epi::None>(g, grid, s, aux_cols, ldaux2); break;
+    case Epi::Bias: launch_gemm_kernel<T, Epi::Bias>(g, grid, s, aux_cols, ldaux2); break;
+    case Epi::BiasSilu: launch_gemm_kernel<T, Epi::BiasSilu>(g, grid, s, aux_cols, ldaux2); break;
+    case Epi::BiasStorePre: launch_gemm_kernel<T, Epi::BiasStorePre>(g, grid, s, aux_cols, ldaux2); break;
+    case Epi::AddResidual: launch_gemm_kernel<T, Epi::AddResidual>(g, grid, s, aux_cols, ldaux2); break;
+    case Epi::BiasResidual: launch_gemm_kernel<T, Epi::BiasResidual>(g, grid, s, aux_cols, ldaux2); break;
+    case Epi::SiluPrimeMul: launch_gemm_kernel<T, Epi::SiluPrimeMul>(g, grid, s, aux_cols, ldaux2); break;
+    case Epi::GateSiluResidual: launch_gemm_kernel<T, Epi::GateSiluResidual>(g, grid, s, aux_cols, ldaux2); break;
   }
 }
 
@@ -402,8 +462,9 @@ __global__ void k_heads_finalize(int n, const int *__restrict__ z, const double 
   double s0 = 0.0, s1 = 0.0;
   for (int j = 0; j < kHirsh; ++j) {
     const double hv = hh[j];
-    s0 += hv * hw.h_w2[(2 * lane) * kHirsh + j];
-    s1 += hv * hw.h_w2[(2 * lane + 1) * kHirsh + j];
+    const double2 w = *reinterpret_cast<const double2 *>(hw.h_w2t + j * kHirsh + 2 * lane);  // coalesced
+    s0 += hv * w.x;
+    s1 += hv * w.y;
   }
   k0 += s0;
   k1 += s1;
