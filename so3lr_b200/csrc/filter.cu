@@ -354,16 +354,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
 #pragma unroll
   for (int j = 0; j < 2; ++j) gwa[j][0] = gwa[j][1] = gwa[j][2] = gwa[j][3] = 0.0;
   mma_16x16<kF>(gwa, gF, LDU, wr * 16, v1_f, wc, lane);
-  __syncthreads();  // every warp is done reading gF
-#pragma unroll
-  for (int mi = 0; mi < 2; ++mi)
-#pragma unroll
-    for (int ni = 0; ni < 4; ++ni)
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int row = wm * 32 + mi * 16 + hf * 8 + g, col = wn * 32 + ni * 8 + 2 * t;
-        *reinterpret_cast<double2 *>(gF + row * LDU + col) = make_double2(acc[mi][ni][2 * hf], acc[mi][ni][2 * hf + 1]);
-      }
 #pragma unroll
   for (int j = 0; j < 2; ++j)
 #pragma unroll
@@ -371,12 +361,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
       const int row = wr * 16 + hf * 8 + g, col = wc * 16 + j * 8 + 2 * t;
       *reinterpret_cast<double2 *>(gw + row * LDR + col) = make_double2(gwa[j][2 * hf], gwa[j][2 * hf + 1]);
     }
-  __syncthreads();
-  // radial-basis gradient g_rbf = g_pre W0 (64 x 32)
-  double grb[2][4];
+  __syncthreads();  // every warp is done reading gF
+  // radial-basis gradient g_rbf = g_pre W0 (64 x 32). Each warp multiplies the
+  // g_pre block it holds (rows 32 wm.., columns j = 32 wn..) by rows 32 wn.. of
+  // W0 straight from its accumulators: under the kernels' k-slot permutation an
+  // m16n8k8 accumulator block {c0, c2, c1, c3} is the A fragment of one k-step.
+  // The four partial products of a row block (wn = 0..3) go to shared memory in
+  // fragment order and are summed there in that fixed order.
+  double *red = gF;  // [2 wm][4 wn][32 values][32 lanes]
 #pragma unroll
-  for (int j = 0; j < 2; ++j) grb[j][0] = grb[j][1] = grb[j][2] = grb[j][3] = 0.0;
-  mma_16x16<kF>(grb, gF, LDU, wr * 16, w0_f, wc, lane);
+  for (int half = 0; half < 2; ++half) {  // output columns 16 half .. 16 half + 15
+    double part[2][2][4];
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) part[mi][j][0] = part[mi][j][1] = part[mi][j][2] = part[mi][j][3] = 0.0;
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni) {
+      double b[2][2];
+      load_bfrag<2>(w0_f, wn * 4 + ni, 1, 0, 2 * half, lane, b);
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi) {
+        const double a[4] = {acc[mi][ni][0], acc[mi][ni][2], acc[mi][ni][1], acc[mi][ni][3]};
+#pragma unroll
+        for (int j = 0; j < 2; ++j) dmma16(part[mi][j], a, b[j]);
+      }
+    }
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          red[((wm * 4 + wn) * 32 + (mi * 4 + 2 * half + j) * 4 + v) * 32 + lane] = part[mi][j][v];
+  }
+  __syncthreads();
+  // warp (rm, q) sums values 8q..8q+7 of row block rm over the four partials
+  double grb[8];
+  {
+    const int rm = warp >> 2, q = warp & 3;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int idx = 8 * q + k;
+      double s = red[((rm * 4 + 0) * 32 + idx) * 32 + lane];
+#pragma unroll
+      for (int w2 = 1; w2 < 4; ++w2) s += red[((rm * 4 + w2) * 32 + idx) * 32 + lane];
+      grb[k] = s;
+    }
+  }
   // L0 gradient: g_pe = g_w * silu'(L0 V0^T + c0), gl[d] = sum_j g_pe[j] V0[j][d]
   if (need_l0) {
     {
@@ -395,14 +427,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
     for (int j = 0; j < kEH; ++j) s += gw[pl * LDR + j] * v0[j * 4 + d];
     gl[pl * 4 + d] = s;
   }
-  __syncthreads();  // gw and gF reads are done
+  __syncthreads();  // gw and the partial sums are read
+  {
+    const int rm = warp >> 2, q = warp & 3;
 #pragma unroll
-  for (int j = 0; j < 2; ++j)
-#pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      const int row = wr * 16 + hf * 8 + g, col = wc * 16 + j * 8 + 2 * t;
-      *reinterpret_cast<double2 *>(gw + row * LDR + col) = make_double2(grb[j][2 * hf], grb[j][2 * hf + 1]);
+    for (int k = 0; k < 8; ++k) {
+      const int idx = 8 * q + k;
+      const int mi = idx >> 4, rb = (idx >> 2) & 3, v = idx & 3;
+      const int row = rm * 32 + mi * 16 + (v >> 1) * 8 + g, col = rb * 8 + 2 * t + (v & 1);
+      gw[row * LDR + col] = grb[k];
     }
+  }
   // rank 0 prefetches the per-pair inputs of the radial and harmonic gradients
   // into the free gF region
   double *sc = gF;                        // TP x 32 pair scalars
