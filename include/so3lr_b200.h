@@ -219,6 +219,16 @@ int so3lr_long_range_noalloc(so3lr_handle *h, long long natoms, const double *x,
                              double *dq, double *dh, double *f, double *virial_atom, void *stream, char *err,
                              size_t errlen);
 
+/* Per-atom virial of the last evaluation on this handle (so3lr_compute,
+ * so3lr_compute_device, so3lr_compute_batch or the last so3lr_md_run step):
+ * vatom[natoms * 6] in LAMMPS order xx, yy, zz, xy, xz, yz, eV, input atom
+ * order. Each short-range pair and each long-range pair gives half of its
+ * -v (x) dE/dv to each of its two atoms, so the rows sum to the global virial.
+ * The reference refuses per-atom virials (pair_so3lr_native_mpi.cpp:1248-1251);
+ * this is the LAMMPS `vflag_atom` quantity its global virial (:944-990) splits
+ * into. Collective on a multi-GPU handle. */
+int so3lr_virial_atom(so3lr_handle *h, double *vatom, char *err, size_t errlen);
+
 /* The handle's CUDA stream (cudaStream_t), for callers that time or order work. */
 void *so3lr_stream(so3lr_handle *h);
 

@@ -481,16 +481,21 @@ def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -
         g_pos, g_sr, g_lr = torch.autograd.grad(energy, [pos, sr_vec, lr_vec], allow_unused=True)
         out["forces"] = -g_pos.numpy()
         vir = np.zeros(6)
-        for vec, g in ((sr_vec, g_sr), (lr_vec, g_lr)):
+        # per-atom virial: half of every edge's / pair's term to each of its atoms
+        # (the split LAMMPS uses for vflag_atom; the rows sum to the global virial)
+        vir_atom = np.zeros((n, 6))
+        for vec, g, ia, ib in ((sr_vec, g_sr, sr_r, sr_s), (lr_vec, g_lr, lr_i, lr_j)):
             if g is None:
                 continue
             vv = vec.detach().numpy()
             gg = g.numpy()
-            vir[0] -= (vv[:, 0] * gg[:, 0]).sum()
-            vir[1] -= (vv[:, 1] * gg[:, 1]).sum()
-            vir[2] -= (vv[:, 2] * gg[:, 2]).sum()
-            vir[3] -= 0.5 * (vv[:, 0] * gg[:, 1] + vv[:, 1] * gg[:, 0]).sum()
-            vir[4] -= 0.5 * (vv[:, 0] * gg[:, 2] + vv[:, 2] * gg[:, 0]).sum()
-            vir[5] -= 0.5 * (vv[:, 1] * gg[:, 2] + vv[:, 2] * gg[:, 1]).sum()
+            w = np.stack([-(vv[:, 0] * gg[:, 0]), -(vv[:, 1] * gg[:, 1]), -(vv[:, 2] * gg[:, 2]),
+                          -0.5 * (vv[:, 0] * gg[:, 1] + vv[:, 1] * gg[:, 0]),
+                          -0.5 * (vv[:, 0] * gg[:, 2] + vv[:, 2] * gg[:, 0]),
+                          -0.5 * (vv[:, 1] * gg[:, 2] + vv[:, 2] * gg[:, 1])], axis=1)
+            vir += w.sum(axis=0)
+            np.add.at(vir_atom, ia.numpy(), 0.5 * w)
+            np.add.at(vir_atom, ib.numpy(), 0.5 * w)
         out["virial"] = vir
+        out["virial_atom"] = vir_atom
     return out

@@ -336,6 +336,17 @@ int so3lr_long_range_noalloc(so3lr_handle *h, long long natoms, const double *x,
   }
 }
 
+int so3lr_virial_atom(so3lr_handle *h, double *vatom, char *err, size_t errlen) {
+  if (!h || !vatom) return report_msg("so3lr_virial_atom: NULL argument", err, errlen);
+  try {
+    if (!h->eval->has_result()) throw Error("so3lr_virial_atom: no evaluation has run on this handle");
+    h->eval->download_virial_atom(vatom);
+    return 0;
+  } catch (const std::exception &e) {
+    return report(e, err, errlen, h);
+  }
+}
+
 void *so3lr_stream(so3lr_handle *h) { return h ? static_cast<void *>(h->eval->stream()) : nullptr; }
 
 int so3lr_last_stats(const so3lr_handle *h, long long *sr_edges, long long *sr_pairs, long long *device_bytes) {

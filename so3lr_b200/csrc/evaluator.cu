@@ -336,6 +336,7 @@ std::vector<int> partition_atoms(const SystemSpec &s, const double *x, int nrank
 // ---------------------------------------------------------------------------
 void Evaluator::prepare(const SystemSpec &spec_in, const double *host_x) {
   SO3_CUDA(cudaSetDevice(device_));
+  computed_ = false;
   SystemSpec spec = spec_in;
   const int n = spec.n;
   if (n <= 0) throw Error("SO3LR: the system has no atoms");
@@ -536,7 +537,7 @@ void Evaluator::alloc_atoms() {
   w_atom_.reserve(6 * n);
   totals_.reserve(8);
   image_energy_.reserve(nimg);
-  stage_.resize(n * 6);
+  stage_.resize(std::size_t(n) * 6);
 }
 
 void Evaluator::upload_positions(const double *host_x) {
@@ -875,6 +876,24 @@ void Evaluator::compute() {
     exact_sums(e_atom_.get(), 1, 1, 1, own_seg, totals_.get());
   }
   exact_sums(w_atom_.get(), 6, 6, 1, own_seg, totals_.get() + 1);
+  computed_ = true;
+}
+
+void Evaluator::download_virial_atom(double *vatom) {
+  SO3_CUDA(cudaSetDevice(device_));
+  const int n = spec_.n;
+  if (identity_) {
+    SO3_CUDA(cudaMemcpyAsync(vatom, w_atom_.get(), sizeof(double) * 6 * std::size_t(n), cudaMemcpyDeviceToHost,
+                             stream_));
+    SO3_CUDA(cudaStreamSynchronize(stream_));
+    return;
+  }
+  allgather_rows(w_atom_.get(), 6);
+  SO3_CUDA(cudaMemcpyAsync(stage_.data(), w_atom_.get(), sizeof(double) * 6 * std::size_t(n_rows_),
+                           cudaMemcpyDeviceToHost, stream_));
+  SO3_CUDA(cudaStreamSynchronize(stream_));
+  for (int i = 0; i < n; ++i)
+    for (int k = 0; k < 6; ++k) vatom[std::size_t(i) * 6 + k] = stage_[std::size_t(row_of_[i]) * 6 + k];
 }
 
 Evaluator::HostResult Evaluator::download(double *f, double *eatom, double *charges, double *ratios,

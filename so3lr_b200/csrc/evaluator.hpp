@@ -91,6 +91,8 @@ class Evaluator {
   // caller. Atoms are partitioned into spatial bricks of the periodic box.
   void set_comm(int nranks, int rank, const void *unique_id);
   int nranks() const { return nranks_; }
+  // true once compute() has run for the current system
+  bool has_result() const { return computed_; }
   int owned_atoms() const { return n_own_; }
   const SystemSpec &spec() const { return spec_; }
 
@@ -107,6 +109,9 @@ class Evaluator {
   };
   HostResult download(double *f, double *eatom, double *charges, double *ratios, double *e_learned, double *e_zbl,
                       double *e_lr, double *e_elec, double *e_disp, double *image_energy);
+  // per-atom virial (natoms x 6, xx yy zz xy xz yz) of the last compute(), input
+  // atom order; collective when decomposed (synchronises the stream)
+  void download_virial_atom(double *vatom);
   const double *forces() const { return force_.get(); }
   const double *energy_device() const { return totals_.get(); }  // [0] energy, [1..6] virial
   StepStats stats() const { return stats_; }
@@ -183,6 +188,7 @@ class Evaluator {
   bool identity_ = true;
   std::vector<int> row_of_, tag_of_row_;
   std::vector<double> stage_;
+  bool computed_ = false;
   int host_seg_[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   DeviceArray<int> tag_, seg_, pair_canon_;
   DeviceArray<long long> parts_;

@@ -435,7 +435,7 @@ void launch_long_range(int n, int n_cells_atoms, const NeighborState &nb, double
 // assembly: forces, per-atom energies, per-atom virial (gathers over the CSR)
 // ---------------------------------------------------------------------------
 __global__ void k_assemble(int n, int row0, const int *__restrict__ row_start, const int *__restrict__ edge_pair,
-                           const int *__restrict__ pair_canon, const double *__restrict__ geo,
+                           const double *__restrict__ geo,
                            const double *__restrict__ gv, const double *__restrict__ e_nn,
                            const double *__restrict__ e_lr, const double *__restrict__ f_lr,
                            const double *__restrict__ w_lr, double *__restrict__ force, double *__restrict__ e_atom,
@@ -456,16 +456,19 @@ __global__ void k_assemble(int n, int row0, const int *__restrict__ row_start, c
     } else {
       fx += gx; fy += gy; fz += gz;
     }
-    // each pair's virial is counted once, by the owner of its canonical receiver
-    if (code >= 0 && (pair_canon == nullptr || pair_canon[p])) {
+    // per-atom virial: half of the pair's -v (x) dE/dv to each of its two atoms.
+    // v and dE/dv are stored in the pair's canonical orientation, so both atoms
+    // (on any GPU) add bit-identical halves; the halves of every pair add up to
+    // the global virial of pair_so3lr_native_mpi.cpp:944-990
+    {
       const double rr = gp[0];
       const double vx = rr * gp[1], vy = rr * gp[2], vz = rr * gp[3];
-      w[0] -= vx * gx;
-      w[1] -= vy * gy;
-      w[2] -= vz * gz;
-      w[3] -= 0.5 * (vx * gy + vy * gx);
-      w[4] -= 0.5 * (vx * gz + vz * gx);
-      w[5] -= 0.5 * (vy * gz + vz * gy);
+      w[0] -= 0.5 * (vx * gx);
+      w[1] -= 0.5 * (vy * gy);
+      w[2] -= 0.5 * (vz * gz);
+      w[3] -= 0.25 * (vx * gy + vy * gx);
+      w[4] -= 0.25 * (vx * gz + vz * gx);
+      w[5] -= 0.25 * (vy * gz + vz * gy);
     }
   }
   force[3 * a] = fx + f_lr[3 * a];
@@ -481,7 +484,7 @@ void launch_assemble(const NeighborState &nb, const double *geo, const double *g
                      double *e_zbl, double *w_atom, cudaStream_t s) {
   const int n = nb.n_own;
   if (n == 0) return;
-  k_assemble<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row0, nb.row_start, nb.edge_pair, nb.pair_canon, geo, gv, e_nn,
+  k_assemble<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row0, nb.row_start, nb.edge_pair, geo, gv, e_nn,
                                               e_lr, f_lr, w_lr, force, e_atom, e_zbl, w_atom);
   SO3_LAUNCH("assemble");
 }

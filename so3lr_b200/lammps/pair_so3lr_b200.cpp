@@ -113,7 +113,6 @@ void PairSO3LRB200::init_style() {
 
 void PairSO3LRB200::compute(int eflag, int vflag) {
   ev_init(eflag, vflag);
-  if (vflag_atom) error->all(FLERR, "Pair style so3lr/b200 does not compute per-atom virials");
   const int n = atom->nlocal;
   x_.resize(3 * static_cast<std::size_t>(n));
   f_.resize(3 * static_cast<std::size_t>(n));
@@ -147,6 +146,15 @@ void PairSO3LRB200::compute(int eflag, int vflag) {
   if (eflag_global) eng_vdwl += res.energy;
   if (vflag_global)
     for (int k = 0; k < 6; ++k) virial[k] += res.virial[k];
+  if (vflag_atom) {
+    // per-atom virial (the reference refuses vflag_atom): half of every pair
+    // term to each of its atoms, rows summing to the global virial
+    va_.resize(6 * static_cast<std::size_t>(n));
+    if (so3lr_virial_atom(handle_, va_.data(), err, sizeof(err)) != 0)
+      error->all(FLERR, std::string("SO3LR per-atom virial failed: ") + err);
+    for (int i = 0; i < n; ++i)
+      for (int k = 0; k < 6; ++k) vatom[i][k] += va_[6 * static_cast<std::size_t>(i) + k];
+  }
   if (!reported_ && comm->me == 0) {
     reported_ = true;
     utils::logmesg(lmp, "SO3LR_B200_FORCE_PATH=PASS atoms=" + std::to_string(n) +

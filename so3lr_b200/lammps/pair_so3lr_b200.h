@@ -5,7 +5,9 @@
 //   pair_style so3lr/b200 MODEL [charge [multiplicity]]
 //   pair_coeff * * E1 ... Entypes        (element symbols H..Es or numbers 1..99)
 //
-// Same syntax, defaults and refusals as the reference style. The GPU builds
+// Same syntax, defaults and refusals as the reference style, except that
+// per-atom virials (compute ... stress/atom, vflag_atom) are supported; the
+// reference refuses them (pair_so3lr_native_mpi.cpp:1248-1251). The GPU builds
 // its own short- and long-range neighbour lists from the positions, so the
 // style requests no LAMMPS list and needs no ghost atoms beyond LAMMPS's
 // own bookkeeping; it runs on one MPI rank that owns every atom (periodic
@@ -52,7 +54,7 @@ class PairSO3LRB200 : public Pair {
   double lr_cutoff_ = 0.0;
   std::vector<int> type_to_z_;
   std::vector<int> z_;
-  std::vector<double> x_, f_, eatom_;
+  std::vector<double> x_, f_, eatom_, va_;
   so3lr_handle *handle_ = nullptr;
   bool reported_ = false;
 

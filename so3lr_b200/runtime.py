@@ -26,7 +26,8 @@ EXPORTED = (
     "so3lr_create", "so3lr_describe", "so3lr_validate_charge_spin", "so3lr_element_from_token",
     "so3lr_inspect_model", "so3lr_compute", "so3lr_compute_device", "so3lr_compute_batch",
     "so3lr_md_init", "so3lr_md_run", "so3lr_md_state", "so3lr_profile", "so3lr_profile_read",
-    "so3lr_launch_count", "so3lr_long_range_noalloc", "so3lr_stream", "so3lr_last_stats", "so3lr_destroy",
+    "so3lr_launch_count", "so3lr_long_range_noalloc", "so3lr_virial_atom", "so3lr_stream", "so3lr_last_stats",
+    "so3lr_destroy",
     "so3lr_nccl_unique_id", "so3lr_comm_init", "so3lr_owned_atoms", "so3lr_partition",
 )
 
@@ -105,6 +106,7 @@ def load_library(path: os.PathLike | str | None = None) -> C.CDLL:
     lib.so3lr_stream.argtypes = [C.c_void_p]
     lib.so3lr_stream.restype = C.c_void_p
     lib.so3lr_last_stats.argtypes = [C.c_void_p, _lp, _lp, _lp]
+    lib.so3lr_virial_atom.argtypes = [C.c_void_p, _dp, C.c_char_p, C.c_size_t]
     lib.so3lr_destroy.argtypes = [C.c_void_p]
     lib.so3lr_destroy.restype = None
     if path is None:
@@ -219,6 +221,13 @@ class So3lrB200:
 
     def launch_count(self) -> int:
         return int(self._lib.so3lr_launch_count())
+
+    def virial_atom(self, natoms: int) -> np.ndarray:
+        """Per-atom virial (natoms x 6, xx yy zz xy xz yz) of the last evaluation."""
+        out = np.empty((int(natoms), 6), dtype=np.float64)
+        err = C.create_string_buffer(1024)
+        _check(self._lib.so3lr_virial_atom(self._h, _ptr(out), err, 1024), err)
+        return out
 
     def stats(self) -> dict:
         e, p, b = C.c_longlong(), C.c_longlong(), C.c_longlong()

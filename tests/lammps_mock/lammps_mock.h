@@ -99,7 +99,10 @@ class Pair {
   explicit Pair(LAMMPS *l)
       : lmp(l), error(&l->error), memory(&l->memory), atom(&l->atom), domain(&l->domain), force(&l->force),
         comm(&l->comm) {}
-  virtual ~Pair() { delete[] eatom; }
+  virtual ~Pair() {
+    delete[] eatom;
+    release_vatom();
+  }
   virtual void compute(int, int) = 0;
   virtual void settings(int, char **) = 0;
   virtual void coeff(int, char **) = 0;
@@ -119,6 +122,7 @@ class Pair {
   double **cutsq = nullptr;
   double eng_vdwl = 0.0, virial[6] = {0, 0, 0, 0, 0, 0};
   double *eatom = nullptr;
+  double **vatom = nullptr;  // [nlocal][6], LAMMPS order xx yy zz xy xz yz
   int eflag_global = 0, eflag_atom = 0, vflag_global = 0, vflag_atom = 0;
 
   // LAMMPS semantics: eflag bit 1 = global energy, bit 2 = per-atom energy;
@@ -133,6 +137,21 @@ class Pair {
     if (eflag_atom) {
       delete[] eatom;
       eatom = new double[atom->nlocal]();
+    }
+    if (vflag_atom) {
+      release_vatom();
+      vatom = new double *[atom->nlocal];
+      double *rows = new double[6 * static_cast<std::size_t>(atom->nlocal)]();
+      for (int i = 0; i < atom->nlocal; ++i) vatom[i] = rows + 6 * static_cast<std::size_t>(i);
+    }
+  }
+
+ private:
+  void release_vatom() {
+    if (vatom) {
+      delete[] vatom[0];
+      delete[] vatom;
+      vatom = nullptr;
     }
   }
 };

@@ -116,7 +116,7 @@ static int run(const char *model, const char *input) {
   char *cargs[] = {(char *)"*", (char *)"*", (char *)"O", (char *)"H"};
   pair.coeff(4, cargs);
   pair.init_style();
-  pair.compute(1 | 2, 1);
+  pair.compute(1 | 2, 1 | 4);
   std::printf("{\"energy\": %.17g, \"virial\": [", pair.eng_vdwl);
   for (int k = 0; k < 6; ++k) std::printf(k ? ", %.17g" : "%.17g", pair.virial[k]);
   std::printf("], \"eatom_sum\": %.17g, \"forces\": [", [&] {
@@ -127,6 +127,12 @@ static int run(const char *model, const char *input) {
   for (int i = 0; i < n; ++i)
     std::printf(i ? ", [%.17g, %.17g, %.17g]" : "[%.17g, %.17g, %.17g]", lmp.atom.f[i][0], lmp.atom.f[i][1],
                 lmp.atom.f[i][2]);
+  std::printf("], \"vatom\": [");
+  for (int i = 0; i < n; ++i) {
+    std::printf(i ? ", [" : "[");
+    for (int k = 0; k < 6; ++k) std::printf(k ? ", %.17g" : "%.17g", pair.vatom[i][k]);
+    std::printf("]");
+  }
   std::printf("], \"log\": \"%s\"}\n", lmp.log.substr(0, lmp.log.size() - 1).c_str());
   return 0;
 }

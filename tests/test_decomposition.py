@@ -72,10 +72,11 @@ def _gpu_worker(rank, world, uid, nmol, seed, result_q):
         m.comm_init(world, rank, uid)
         w = water_box(nmol, seed=seed)
         out = m.compute(w.pos, w.z, cell=w.cell, boxlo=w.boxlo)
-        result_q.put((rank, out["energy"], out["forces"], out["virial"], out["charges"], m.owned_atoms(), None))
+        va = m.virial_atom(len(w.z))
+        result_q.put((rank, out["energy"], out["forces"], out["virial"], out["charges"], m.owned_atoms(), va, None))
         m.close()
     except Exception as exc:  # report to the parent instead of hanging it
-        result_q.put((rank, None, None, None, None, 0, repr(exc)))
+        result_q.put((rank, None, None, None, None, 0, None, repr(exc)))
 
 
 @pytest.mark.gpu
@@ -89,6 +90,7 @@ def test_multi_gpu_bit_identical(world, gpu_model):
     nmol, seed = 1000, 17
     w = water_box(nmol, seed=seed)
     ref = gpu_model.compute(w.pos, w.z, cell=w.cell, boxlo=w.boxlo)
+    ref_va = gpu_model.virial_atom(len(w.z))
     uid = So3lrB200.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -98,10 +100,11 @@ def test_multi_gpu_bit_identical(world, gpu_model):
     res = [q.get(timeout=300) for _ in procs]
     for p in procs:
         p.join(timeout=120)
-    for rank, e, f, vir, chg, owned, err in res:
+    for rank, e, f, vir, chg, owned, va, err in res:
         assert err is None, err
         assert 0 < owned < len(w.z)
         assert e == ref["energy"], (e, ref["energy"])
         assert np.array_equal(f, ref["forces"]), np.abs(f - ref["forces"]).max()
         assert np.array_equal(vir, ref["virial"])
         assert np.array_equal(chg, ref["charges"])
+        assert np.array_equal(va, ref_va)

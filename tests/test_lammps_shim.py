@@ -53,6 +53,8 @@ def test_pair_style_compute_matches_c_abi(tmp_path, gpu_model):
     assert res.returncode == 0, res.stdout + res.stderr
     out = json.loads(res.stdout.strip().splitlines()[-1])
     ref = gpu_model.compute(w.pos, w.z, cell=w.cell, boxlo=w.boxlo)
+    ref_va = gpu_model.virial_atom(len(w.z))
+    assert np.array_equal(np.array(out["vatom"]), ref_va)
     assert out["energy"] == ref["energy"]
     assert np.array_equal(np.array(out["forces"]), ref["forces"])
     assert np.allclose(out["virial"], ref["virial"], rtol=0, atol=1e-12)

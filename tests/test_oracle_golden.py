@@ -77,3 +77,14 @@ def test_oracle_virial_matches_finite_difference_strain(oracle_model):
             s = System(pos=w.pos @ strain.T, z=w.z, cell=w.cell * np.diag(strain))
             e.append(evaluate(oracle_model, s, want_forces=False)["energy"])
         assert abs(-(e[0] - e[1]) / (2 * eps) - base["virial"][comp]) < 1e-5 * max(1.0, abs(base["virial"][comp]))
+
+
+def test_oracle_per_atom_virial_sums_to_global(oracle_model):
+    """The oracle's per-atom virial (half of each pair term to each atom) adds
+    up to its global virial, in a periodic box with several images."""
+    from oracle.so3lr_oracle import System, evaluate
+    from so3lr_b200.systems import water_box
+    w = water_box(27, seed=6)
+    o = evaluate(oracle_model, System(pos=w.pos, z=w.z, cell=w.cell))
+    assert o["virial_atom"].shape == (len(w.z), 6)
+    assert np.abs(o["virial_atom"].sum(axis=0) - o["virial"]).max() <= 1e-10 * (1 + np.abs(o["virial"]).max())
