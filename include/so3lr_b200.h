@@ -181,6 +181,16 @@ int so3lr_compute_batch(so3lr_handle *h, const so3lr_batch *in, so3lr_batch_resu
 int so3lr_md_init(so3lr_handle *h, const so3lr_frame *in, const double *v, const double *mass, char *err,
                   size_t errlen);
 int so3lr_md_run(so3lr_handle *h, int nsteps, double dt_ps, char *err, size_t errlen);
+/* Nose-Hoover chain thermostat for the following so3lr_md_run calls (NVT, the
+ * ensemble of the reference's multi-GPU benchmark; LAMMPS `fix nvt` in the
+ * reference's inputs). Martyna-Tuckerman-Klein chain of `chain` thermostats
+ * (1..10), target temperature in K, damping time in ps; t_damp_ps <= 0 returns
+ * to NVE. Call after so3lr_md_init. The chain's kinetic-energy input is an
+ * exact sum, so NVT trajectories are bit-identical for any number of GPUs. */
+int so3lr_md_thermostat(so3lr_handle *h, double t_target_k, double t_damp_ps, int chain, char *err, size_t errlen);
+/* Energy stored in the chain (eV); with the kinetic and potential energy it
+ * forms the conserved quantity of the NVT run. 0 without a thermostat. */
+int so3lr_md_thermostat_energy(so3lr_handle *h, double *energy, char *err, size_t errlen);
 /* Copies the current state to host buffers (any may be NULL) and returns the
  * potential energy of the last force evaluation. Synchronises the stream. */
 int so3lr_md_state(so3lr_handle *h, double *x, double *v, double *f, double *energy, char *err, size_t errlen);

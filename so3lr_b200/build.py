@@ -67,7 +67,7 @@ def build(force: bool = False, verbose: bool = False) -> pathlib.Path:
     with concurrent.futures.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as pool:
         objs = list(pool.map(lambda s: _compile(s, newest_header, force, verbose), srcs))
     if force or not LIB.exists() or LIB.stat().st_mtime < max(o.stat().st_mtime for o in objs):
-        cmd = [nvcc(), "-shared", "-o", str(LIB)] + ARCH + [str(o) for o in objs] + ["-lcudart", "-lnccl", "-Xlinker", "-rpath=/usr/local/cuda/lib64"]
+        cmd = [nvcc(), "-shared", "-o", str(LIB)] + ARCH + [str(o) for o in objs] + ["-lcudart", "-ldl", "-Xlinker", "-rpath=/usr/local/cuda/lib64"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")

@@ -9,7 +9,7 @@
 #include <memory>
 #include <string>
 
-#include <nccl.h>
+#include "nccl_dyn.hpp"
 
 #include "evaluator.hpp"
 
@@ -241,6 +241,27 @@ int so3lr_md_run(so3lr_handle *h, int nsteps, double dt_ps, char *err, size_t er
   }
 }
 
+int so3lr_md_thermostat(so3lr_handle *h, double t_target_k, double t_damp_ps, int chain, char *err,
+                        size_t errlen) {
+  if (!h) return report_msg("so3lr_md_thermostat: NULL handle", err, errlen);
+  try {
+    h->eval->md_thermostat(t_target_k, t_damp_ps, chain);
+    return 0;
+  } catch (const std::exception &e) {
+    return report(e, err, errlen, h);
+  }
+}
+
+int so3lr_md_thermostat_energy(so3lr_handle *h, double *energy, char *err, size_t errlen) {
+  if (!h || !energy) return report_msg("so3lr_md_thermostat_energy: NULL argument", err, errlen);
+  try {
+    *energy = h->eval->md_thermostat_energy();
+    return 0;
+  } catch (const std::exception &e) {
+    return report(e, err, errlen, h);
+  }
+}
+
 int so3lr_md_state(so3lr_handle *h, double *x, double *v, double *f, double *energy, char *err, size_t errlen) {
   if (!h) return report_msg("so3lr_md_state: NULL handle", err, errlen);
   try {
@@ -257,11 +278,15 @@ int so3lr_md_state(so3lr_handle *h, double *x, double *v, double *f, double *ene
 int so3lr_nccl_unique_id(char out[128], char *err, size_t errlen) {
   if (!out) return report_msg("so3lr_nccl_unique_id: NULL argument", err, errlen);
   static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
-  ncclUniqueId id;
-  const ncclResult_t r = ncclGetUniqueId(&id);
-  if (r != ncclSuccess) return report_msg(ncclGetErrorString(r), err, errlen);
-  std::memcpy(out, &id, sizeof(id));
-  return 0;
+  try {
+    ncclUniqueId id;
+    const ncclResult_t r = so3lr_b200::nccl().get_unique_id(&id);
+    if (r != ncclSuccess) return report_msg(so3lr_b200::nccl().get_error_string(r), err, errlen);
+    std::memcpy(out, &id, sizeof(id));
+    return 0;
+  } catch (const std::exception &e) {
+    return report_msg(e.what(), err, errlen);
+  }
 }
 
 int so3lr_comm_init(so3lr_handle *h, int nranks, int rank, const char unique_id[128], char *err, size_t errlen) {

@@ -1,6 +1,6 @@
 #include "evaluator.hpp"
 
-#include <nccl.h>
+#include "nccl_dyn.hpp"
 
 #include <cmath>
 #include <cstring>
@@ -29,7 +29,7 @@ Evaluator::~Evaluator() {
   if (stream_) {
     cudaSetDevice(device_);
     cudaStreamSynchronize(stream_);
-    if (comm_) ncclCommDestroy(comm_);
+    if (comm_) nccl().comm_destroy(comm_);
     for (auto &p : prof_)
       for (auto ev : p.events) cudaEventDestroy(ev);
     cudaStreamDestroy(stream_);
@@ -252,7 +252,7 @@ void Evaluator::set_comm(int nranks, int rank, const void *unique_id) {
   if (nranks < 1 || rank < 0 || rank >= nranks) throw Error("SO3LR: invalid rank / rank count");
   SO3_CUDA(cudaSetDevice(device_));
   if (comm_) {
-    ncclCommDestroy(comm_);
+    nccl().comm_destroy(comm_);
     comm_ = nullptr;
   }
   nranks_ = nranks;
@@ -261,15 +261,15 @@ void Evaluator::set_comm(int nranks, int rank, const void *unique_id) {
   if (nranks == 1) return;
   ncclUniqueId id;
   std::memcpy(&id, unique_id, sizeof(id));
-  const ncclResult_t r = ncclCommInitRank(&comm_, nranks, id, rank);
-  if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclCommInitRank failed: ") + ncclGetErrorString(r));
+  const ncclResult_t r = nccl().comm_init_rank(&comm_, nranks, id, rank);
+  if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclCommInitRank failed: ") + nccl().get_error_string(r));
 }
 
 void Evaluator::allgather_rows(double *a, int width) {
   if (nranks_ == 1) return;
   const std::size_t count = std::size_t(stride_) * width;
-  const ncclResult_t r = ncclAllGather(a + std::size_t(rank_) * count, a, count, ncclDouble, comm_, stream_);
-  if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclAllGather failed: ") + ncclGetErrorString(r));
+  const ncclResult_t r = nccl().all_gather(a + std::size_t(rank_) * count, a, count, ncclDouble, comm_, stream_);
+  if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclAllGather failed: ") + nccl().get_error_string(r));
 }
 
 // exact sums over segments of the owned rows (global over ranks when decomposed);
@@ -285,8 +285,8 @@ void Evaluator::exact_sums(const double *v, int stride, int ncol, int nseg, cons
   long long *all = local + per_rank;
   launch_fixed_segment_sum(nseg, nblk, seg, v, stride, ncol, local, stream_);
   if (nranks_ > 1) {
-    const ncclResult_t r = ncclAllGather(local, all, per_rank, ncclInt64, comm_, stream_);
-    if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclAllGather failed: ") + ncclGetErrorString(r));
+    const ncclResult_t r = nccl().all_gather(local, all, per_rank, ncclInt64, comm_, stream_);
+    if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclAllGather failed: ") + nccl().get_error_string(r));
     launch_fixed_finish(all, nranks_ * nblk, count, out, stream_);
   } else {
     launch_fixed_finish(local, nblk, count, out, stream_);
@@ -337,6 +337,8 @@ std::vector<int> partition_atoms(const SystemSpec &s, const double *x, int nrank
 void Evaluator::prepare(const SystemSpec &spec_in, const double *host_x) {
   SO3_CUDA(cudaSetDevice(device_));
   computed_ = false;
+  md_ready_ = false;
+  nvt_ = false;
   SystemSpec spec = spec_in;
   const int n = spec.n;
   if (n <= 0) throw Error("SO3LR: the system has no atoms");
@@ -954,19 +956,80 @@ void Evaluator::md_setup(const double *host_v, const double *host_mass) {
                            cudaMemcpyHostToDevice, stream_));
   SO3_CUDA(cudaMemcpyAsync(inv_mass_.reserve(n_rows_), inv_rows.data(), sizeof(double) * n_rows_,
                            cudaMemcpyHostToDevice, stream_));
+  std::vector<double> mass_rows(n_rows_, 0.0);
+  for (int i = 0; i < n; ++i) mass_rows[row_of_[i]] = host_mass[i];
+  SO3_CUDA(cudaMemcpyAsync(mass_.reserve(n_rows_), mass_rows.data(), sizeof(double) * n_rows_,
+                           cudaMemcpyHostToDevice, stream_));
+  ke2_.reserve(n_rows_);
+  nvt_ = false;
   compute();  // forces at the starting positions
   SO3_CUDA(cudaStreamSynchronize(stream_));
+  md_ready_ = true;
+}
+
+void Evaluator::md_thermostat(double t_target_k, double t_damp_ps, int chain) {
+  SO3_CUDA(cudaSetDevice(device_));
+  if (!md_ready_) throw Error("SO3LR MD: call so3lr_md_init before setting a thermostat");
+  if (!(t_damp_ps > 0.0)) {
+    nvt_ = false;
+    return;
+  }
+  if (!(t_target_k > 0.0)) throw Error("SO3LR MD: the thermostat target temperature must be positive");
+  if (chain < 1 || chain > kMaxChain)
+    throw Error("SO3LR MD: Nose-Hoover chain length must be in 1.." + std::to_string(kMaxChain));
+  constexpr double kBoltzMetal = 8.617343e-5;  // eV / K
+  NhcState st{};
+  st.chain = chain;
+  st.kt = kBoltzMetal * t_target_k;
+  st.ndof = 3.0 * spec_.n - 3.0;
+  if (st.ndof < 1.0) throw Error("SO3LR MD: a thermostat needs at least two atoms");
+  const double tau2 = t_damp_ps * t_damp_ps;
+  for (int j = 0; j < chain; ++j) st.q[j] = (j == 0 ? st.ndof : 1.0) * st.kt * tau2;
+  constexpr std::size_t words = (sizeof(NhcState) + sizeof(double) - 1) / sizeof(double);
+  double *d = nhc_state_.reserve(words);
+  SO3_CUDA(cudaMemcpyAsync(d, &st, sizeof(NhcState), cudaMemcpyHostToDevice, stream_));
+  nhc_scalars_.reserve(2);
+  SO3_CUDA(cudaStreamSynchronize(stream_));
+  nvt_ = true;
+}
+
+double Evaluator::md_thermostat_energy() {
+  SO3_CUDA(cudaSetDevice(device_));
+  if (!nvt_) return 0.0;
+  NhcState st{};
+  SO3_CUDA(cudaMemcpyAsync(&st, nhc_state_.get(), sizeof(NhcState), cudaMemcpyDeviceToHost, stream_));
+  SO3_CUDA(cudaStreamSynchronize(stream_));
+  double e = 0.0;
+  for (int j = 0; j < st.chain; ++j) {
+    e += 0.5 * st.q[j] * st.veta[j] * st.veta[j];
+    e += (j == 0 ? st.ndof : 1.0) * st.kt * st.eta[j];
+  }
+  return e;
+}
+
+// half step of the chain: exact 2K over all GPUs, chain update, velocity scaling
+void Evaluator::nhc_half(double dt) {
+  constexpr double mvv2e = 1.0364269e-4;
+  const std::size_t r0 = std::size_t(row0_);
+  double *two_k = nhc_scalars_.get(), *scale = two_k + 1;
+  launch_two_ke(n_own_, v_.get() + 3 * r0, mass_.get() + r0, mvv2e, ke2_.get() + r0, stream_);
+  exact_sums(ke2_.get(), 1, 1, 1, seg_.get(), two_k);
+  launch_nhc_half(reinterpret_cast<NhcState *>(nhc_state_.get()), two_k, dt, scale, stream_);
+  launch_scale_v(n_own_, v_.get() + 3 * r0, scale, stream_);
 }
 
 void Evaluator::md_steps(int nsteps, double dt) {
   constexpr double ftm2v = 1.0 / 1.0364269e-4;
   const std::size_t r0 = std::size_t(row0_);
+  if (!md_ready_) throw Error("SO3LR MD: call so3lr_md_init first");
   for (int step = 0; step < nsteps; ++step) {
+    if (nvt_) nhc_half(dt);
     launch_verlet_first(n_own_, x_.get() + 3 * r0, v_.get() + 3 * r0, force_.get() + 3 * r0, inv_mass_.get() + r0, dt,
                         ftm2v, stream_);
     allgather_rows(x_.get(), 3);
     compute();
     launch_verlet_second(n_own_, v_.get() + 3 * r0, force_.get() + 3 * r0, inv_mass_.get() + r0, dt, ftm2v, stream_);
+    if (nvt_) nhc_half(dt);
   }
 }
 

@@ -15,7 +15,7 @@
 #include <string>
 #include <vector>
 
-#include <nccl.h>
+#include "nccl_dyn.hpp"
 
 #include "kernels.cuh"
 #include "model_host.hpp"
@@ -133,6 +133,11 @@ class Evaluator {
 
   // velocity-Verlet MD on the device (LAMMPS metal units); masses in g/mol
   void md_setup(const double *host_v, const double *host_mass);
+  // Nose-Hoover chain (thermostat.cu) for the following md_steps; t_damp_ps <= 0
+  // switches back to NVE
+  void md_thermostat(double t_target_k, double t_damp_ps, int chain);
+  // the chain's energy: sum_j Q_j v_j^2 / 2 + N_f kT eta_1 + kT sum_{j>1} eta_j (eV)
+  double md_thermostat_energy();
   void md_steps(int nsteps, double dt_ps);
   void md_download(double *x, double *v);
 
@@ -175,6 +180,9 @@ class Evaluator {
 
   // per-atom arrays
   DeviceArray<double> x_, v_, inv_mass_, force_;
+  DeviceArray<double> mass_, ke2_, nhc_scalars_, nhc_state_;
+  bool md_ready_ = false, nvt_ = false;
+  void nhc_half(double dt);
   std::vector<std::unique_ptr<DeviceArray<double>>> xb_, evb_, qkv_, xhat1_, rstd1_, n1_, A_, hp_, gate_, xhat2_, rstd2_;
   DeviceArray<double> d_inv_, d_ev_, act_, cat_, t_, hpre_, hcat_, hk_, e_nn_, raw_q_, q_, ratio_;
   DeviceArray<double> e_lr_, e_elec_, e_disp_, dq_, dh_, f_lr_, w_lr_, img_sums_, dq_mean_, lr_pos4_, lr_par4_;

@@ -178,6 +178,20 @@ void launch_assemble(const NeighborState &nb, const double *geo, const double *g
                      double *e_zbl, double *w_atom, cudaStream_t s);
 
 // MD integration (velocity Verlet, LAMMPS metal units)
+// ---- Nose-Hoover chain (thermostat.cu) ----------------------------------------
+constexpr int kMaxChain = 10;
+struct NhcState {
+  int chain;          // thermostats in the chain
+  double kt;          // k_B T (eV)
+  double ndof;        // degrees of freedom of the particles
+  double q[kMaxChain];     // masses (eV ps^2)
+  double eta[kMaxChain];   // positions
+  double veta[kMaxChain];  // velocities (1/ps)
+};
+void launch_two_ke(int n, const double *v, const double *mass, double mvv2e, double *out, cudaStream_t s);
+void launch_nhc_half(NhcState *st, const double *two_k, double dt, double *scale, cudaStream_t s);
+void launch_scale_v(int n, double *v, const double *scale, cudaStream_t s);
+
 void launch_verlet_first(int n, double *x, double *v, const double *f, const double *inv_mass, double dt,
                          double ftm2v, cudaStream_t s);
 void launch_verlet_second(int n, double *v, const double *f, const double *inv_mass, double dt, double ftm2v,

@@ -25,7 +25,7 @@ DEFAULT_MODEL = HERE.parent / "models" / "so3lr.so3lr"
 EXPORTED = (
     "so3lr_create", "so3lr_describe", "so3lr_validate_charge_spin", "so3lr_element_from_token",
     "so3lr_inspect_model", "so3lr_compute", "so3lr_compute_device", "so3lr_compute_batch",
-    "so3lr_md_init", "so3lr_md_run", "so3lr_md_state", "so3lr_profile", "so3lr_profile_read",
+    "so3lr_md_init", "so3lr_md_run", "so3lr_md_thermostat", "so3lr_md_thermostat_energy", "so3lr_md_state", "so3lr_profile", "so3lr_profile_read",
     "so3lr_launch_count", "so3lr_long_range_noalloc", "so3lr_virial_atom", "so3lr_stream", "so3lr_last_stats",
     "so3lr_destroy",
     "so3lr_nccl_unique_id", "so3lr_comm_init", "so3lr_owned_atoms", "so3lr_partition",
@@ -92,6 +92,8 @@ def load_library(path: os.PathLike | str | None = None) -> C.CDLL:
                                         C.c_size_t]
     lib.so3lr_md_init.argtypes = [C.c_void_p, C.POINTER(Frame), _dp, _dp, C.c_char_p, C.c_size_t]
     lib.so3lr_md_run.argtypes = [C.c_void_p, C.c_int, C.c_double, C.c_char_p, C.c_size_t]
+    lib.so3lr_md_thermostat.argtypes = [C.c_void_p, C.c_double, C.c_double, C.c_int, C.c_char_p, C.c_size_t]
+    lib.so3lr_md_thermostat_energy.argtypes = [C.c_void_p, _dp, C.c_char_p, C.c_size_t]
     lib.so3lr_md_state.argtypes = [C.c_void_p, _dp, _dp, _dp, _dp, C.c_char_p, C.c_size_t]
     lib.so3lr_profile.argtypes = [C.c_void_p, C.c_int]
     lib.so3lr_profile_read.argtypes = [C.c_void_p, C.c_int, _dp, _lp, _dp, C.c_char_p, C.c_size_t]
@@ -322,6 +324,17 @@ class So3lrB200:
         mass = np.ascontiguousarray(mass, dtype=np.float64)
         err = C.create_string_buffer(4096)
         _check(self._lib.so3lr_md_init(self._h, C.byref(fr), _ptr(v), _ptr(mass), err, 4096), err)
+
+    def md_thermostat(self, t_target_k: float, t_damp_ps: float, chain: int = 3) -> None:
+        """Nose-Hoover chain for the following md_run calls (t_damp_ps <= 0: NVE)."""
+        err = C.create_string_buffer(1024)
+        _check(self._lib.so3lr_md_thermostat(self._h, float(t_target_k), float(t_damp_ps), int(chain), err, 1024), err)
+
+    def md_thermostat_energy(self) -> float:
+        e = C.c_double(0.0)
+        err = C.create_string_buffer(1024)
+        _check(self._lib.so3lr_md_thermostat_energy(self._h, C.byref(e), err, 1024), err)
+        return e.value
 
     def md_run(self, nsteps: int, dt_ps: float) -> None:
         err = C.create_string_buffer(4096)

@@ -79,6 +79,56 @@ def _gpu_worker(rank, world, uid, nmol, seed, result_q):
         result_q.put((rank, None, None, None, None, 0, None, repr(exc)))
 
 
+def _nvt_worker(rank, world, uid, nmol, seed, steps, result_q):
+    try:
+        from so3lr_b200 import So3lrB200
+        from so3lr_b200.systems import maxwell_boltzmann, water_box
+        m = So3lrB200(MODEL, rank)
+        if world > 1:
+            m.comm_init(world, rank, uid)
+        w = water_box(nmol, seed=seed)
+        v = maxwell_boltzmann(w.mass, 300.0, seed=seed)
+        m.md_init(w.pos, w.z, w.cell, w.boxlo, v, w.mass)
+        m.md_thermostat(300.0, 0.05, 3)
+        m.md_run(steps, 0.0005)
+        st = m.md_state(len(w.z))
+        result_q.put((rank, st["x"], st["v"], st["energy"], m.md_thermostat_energy(), None))
+        m.close()
+    except Exception as exc:  # report to the parent instead of hanging it
+        result_q.put((rank, None, None, None, None, repr(exc)))
+
+
+@pytest.mark.gpu
+def test_multi_gpu_nvt_trajectory_bit_identical():
+    """A Nose-Hoover (NVT) trajectory on 2 GPUs equals the single-GPU one bit
+    for bit: the chain's kinetic energy is an exact sum and every rank updates
+    the chain identically."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from so3lr_b200 import So3lrB200
+    ctx = mp.get_context("spawn")
+    nmol, seed, steps = 1000, 23, 10
+    q1 = ctx.Queue()
+    p1 = ctx.Process(target=_nvt_worker, args=(0, 1, None, nmol, seed, steps, q1))
+    p1.start()
+    ref = q1.get(timeout=300)
+    p1.join(timeout=120)
+    assert ref[5] is None, ref[5]
+    uid = So3lrB200.nccl_unique_id()
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_nvt_worker, args=(r, 2, uid, nmol, seed, steps, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, x, v, e, ech, err in res:
+        assert err is None, err
+        assert np.array_equal(x, ref[1]) and np.array_equal(v, ref[2])
+        assert e == ref[3] and ech == ref[4]
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_multi_gpu_bit_identical(world, gpu_model):

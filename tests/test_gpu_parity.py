@@ -181,6 +181,32 @@ def test_gpu_nve_energy_conservation(gpu_model):
     assert abs(e1 - e0) / n < 2e-4
 
 
+def test_gpu_nvt_nose_hoover(gpu_model):
+    """Nose-Hoover chain on the device (config 2 box): the extended energy
+    (kinetic + potential + chain) is conserved, and a box started at 150 K is
+    heated toward the 300 K target."""
+    from so3lr_b200.systems import maxwell_boltzmann, water_box
+    w = water_box(1000, seed=8)
+    n = len(w.z)
+    mvv2e, kb = 1.0364269e-4, 8.617343e-5
+    v = maxwell_boltzmann(w.mass, 150.0, seed=2)
+    gpu_model.md_init(w.pos, w.z, w.cell, w.boxlo, v, w.mass)
+    gpu_model.md_thermostat(300.0, 0.025, 3)
+
+    def state():
+        st = gpu_model.md_state(n)
+        ke = 0.5 * mvv2e * (w.mass[:, None] * st["v"] ** 2).sum()
+        return st["energy"] + ke + gpu_model.md_thermostat_energy(), 2.0 * ke / ((3 * n - 3) * kb)
+
+    h0, t0 = state()
+    gpu_model.md_run(200, 0.0005)
+    h1, t1 = state()
+    assert abs(h1 - h0) / n < 2e-4, (h0, h1)
+    assert t1 > t0 + 50.0, (t0, t1)
+    gpu_model.md_thermostat(300.0, 0.0, 1)  # back to NVE
+    assert gpu_model.md_thermostat_energy() == 0.0
+
+
 def test_gpu_errors_are_reported_not_raised_as_crashes(gpu_model):
     from so3lr_b200 import So3lrError
     with pytest.raises(So3lrError, match="multiplicity"):
