@@ -20,13 +20,19 @@ __device__ inline int negate_image(int code) {
 constexpr int kZeroImage = (512 << 20) | (512 << 10) | 512;
 
 // Visit every candidate (j, image) of atom i: periodic cell stencil or the
-// atom's own image range (open boundaries / turbo packs).
+// atom's own image range (open boundaries / turbo packs). The separation
+// d = x_i - (x_j + shift) is evaluated in a canonical orientation: from the
+// endpoint with the smaller global tag (for an atom and its own periodic image,
+// from the positive image), the other endpoint negating the same rounded
+// result. Both atoms of a pair therefore see bit-identical |d|, so every
+// inclusion test is symmetric and the neighbour lists of different GPUs agree
+// exactly. tag: global tag per row (nullptr: the row index).
 template <class Visit>
 __device__ inline void for_each_candidate(int i, const double *__restrict__ xw, const CellGrid &g,
                                           const int *__restrict__ cell, const int *__restrict__ cell_start,
                                           const int *__restrict__ cell_count, const int *__restrict__ cell_atoms,
                                           const int *__restrict__ image_of, const int *__restrict__ image_start,
-                                          int reach, Visit &&visit) {
+                                          int reach, const int *__restrict__ tag, Visit &&visit) {
   const double xi = xw[3 * i], yi = xw[3 * i + 1], zi = xw[3 * i + 2];
   if (!g.periodic) {
     const int im = image_of[i];
@@ -58,9 +64,18 @@ __device__ inline void for_each_candidate(int i, const double *__restrict__ xw, 
         const int m = cell_count[cc];
         for (int t = 0; t < m; ++t) {
           const int j = a[t];
-          const double dx = xi - (xw[3 * j] + shx);
-          const double dy = yi - (xw[3 * j + 1] + shy);
-          const double dz = zi - (xw[3 * j + 2] + shz);
+          const int ti = tag ? tag[i] : i, tj = tag ? tag[j] : j;
+          const bool positive = sz > 0 || (sz == 0 && (sy > 0 || (sy == 0 && sx > 0)));
+          double dx, dy, dz;
+          if (ti < tj || (ti == tj && positive)) {
+            dx = xi - (xw[3 * j] + shx);
+            dy = yi - (xw[3 * j + 1] + shy);
+            dz = zi - (xw[3 * j + 2] + shz);
+          } else {  // the other endpoint's expression, negated
+            dx = -(xw[3 * j] - (xi - shx));
+            dy = -(xw[3 * j + 1] - (yi - shy));
+            dz = -(xw[3 * j + 2] - (zi - shz));
+          }
           visit(j, code, dx, dy, dz);
         }
       }

@@ -35,6 +35,7 @@ Evaluator::~Evaluator() {
     cudaStreamDestroy(stream_);
   }
   if (host_small_) cudaFreeHost(host_small_);
+  if (host_halo_) cudaFreeHost(host_halo_);
   if (host_totals_) cudaFreeHost(host_totals_);
 }
 
@@ -250,6 +251,7 @@ void Evaluator::upload_weights() {
 // ---------------------------------------------------------------------------
 void Evaluator::set_comm(int nranks, int rank, const void *unique_id) {
   if (nranks < 1 || rank < 0 || rank >= nranks) throw Error("SO3LR: invalid rank / rank count");
+  if (nranks > 63) throw Error("SO3LR: at most 63 GPUs per decomposition");
   SO3_CUDA(cudaSetDevice(device_));
   if (comm_) {
     nccl().comm_destroy(comm_);
@@ -270,6 +272,29 @@ void Evaluator::allgather_rows(double *a, int width) {
   const std::size_t count = std::size_t(stride_) * width;
   const ncclResult_t r = nccl().all_gather(a + std::size_t(rank_) * count, a, count, ncclDouble, comm_, stream_);
   if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclAllGather failed: ") + nccl().get_error_string(r));
+}
+
+void Evaluator::halo_exchange(double *a, int wa, double *b, int wb) {
+  if (nranks_ == 1) return;
+  const int w = wa + wb;
+  const long long nsend = halo_send_off_[nranks_], nrecv = halo_recv_off_[nranks_];
+  double *sbuf = halo_send_buf_.reserve(std::size_t(std::max(1LL, nsend)) * w, 1.25);
+  double *rbuf = halo_recv_buf_.reserve(std::size_t(std::max(1LL, nrecv)) * w, 1.25);
+  launch_halo_pack(int(nsend), halo_send_rows_.get(), a, wa, b, wb, sbuf, stream_);
+  const NcclApi &api = nccl();
+  auto check = [&](ncclResult_t r, const char *what) {
+    if (r != ncclSuccess) throw Error(std::string("SO3LR: ") + what + " failed: " + api.get_error_string(r));
+  };
+  check(api.group_start(), "ncclGroupStart");
+  for (int p = 0; p < nranks_; ++p) {
+    if (p == rank_) continue;
+    const long long cs = halo_send_off_[p + 1] - halo_send_off_[p];
+    const long long cr = halo_recv_off_[p + 1] - halo_recv_off_[p];
+    if (cs > 0) check(api.send(sbuf + halo_send_off_[p] * w, std::size_t(cs) * w, ncclDouble, p, comm_, stream_), "ncclSend");
+    if (cr > 0) check(api.recv(rbuf + halo_recv_off_[p] * w, std::size_t(cr) * w, ncclDouble, p, comm_, stream_), "ncclRecv");
+  }
+  check(api.group_end(), "ncclGroupEnd");
+  launch_halo_unpack(int(nrecv), halo_recv_rows_.get(), rbuf, a, wa, b, wb, stream_);
 }
 
 // exact sums over segments of the owned rows (global over ranks when decomposed);
@@ -630,7 +655,38 @@ void Evaluator::build_neighbors() {
   SO3_CUDA(cudaMemsetAsync(nb_.error_flag, 0, sizeof(int), stream_));
   fill_sr(nb_, sr_cut_, E, stream_);
   SO3_CUDA(cudaMemcpyAsync(host_small_ + 1, nb_.scan_total, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+  if (!identity_) {
+    // halo lists from this GPU's (symmetric) neighbour lists; every rank's
+    // per-peer counts are gathered so that all ranks can check them together
+    const int cnt = nranks_ * stride_;
+    int *flags = halo_flags_.reserve(2 * std::size_t(cnt));
+    int *pos = halo_pos_.reserve(2 * std::size_t(cnt));
+    const std::size_t nscratch = scan_scratch_ints(std::size_t(cnt) + 1);
+    if (scan_scratch_.capacity() < nscratch) nb_.scan_scratch = scan_scratch_.reserve(nscratch);
+    nb_.scan_scratch = scan_scratch_.get();
+    const int lo = 2 * (nranks_ + 1);
+    long long *off = halo_offsets_.reserve(lo);
+    long long *all = halo_all_offsets_.reserve(std::size_t(lo) * nranks_);
+    launch_halo_lists(n_own_, row0_, stride_, nranks_, rank_, nb_.row_start, nb_.nbr, flags, flags + cnt, pos,
+                      pos + cnt, halo_send_rows_.reserve(cnt), halo_recv_rows_.reserve(cnt), off,
+                      halo_totals_.reserve(2), nb_.scan_scratch, stream_);
+    const ncclResult_t r = nccl().all_gather(off, all, std::size_t(lo), ncclInt64, comm_, stream_);
+    if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclAllGather failed: ") + nccl().get_error_string(r));
+    if (!host_halo_) SO3_CUDA(cudaMallocHost(&host_halo_, sizeof(long long) * 2 * 64 * 64));
+    SO3_CUDA(cudaMemcpyAsync(host_halo_, all, sizeof(long long) * lo * nranks_, cudaMemcpyDeviceToHost, stream_));
+  }
   SO3_CUDA(cudaStreamSynchronize(stream_));
+  if (!identity_) {
+    const int lo = 2 * (nranks_ + 1);
+    auto sends = [&](int s, int p) { return host_halo_[s * lo + p + 1] - host_halo_[s * lo + p]; };
+    auto recvs = [&](int r, int p) { return host_halo_[r * lo + nranks_ + 2 + p] - host_halo_[r * lo + nranks_ + 1 + p]; };
+    for (int s = 0; s < nranks_; ++s)  // the same verdict on every rank
+      for (int p = 0; p < nranks_; ++p)
+        if (s != p && sends(s, p) != recvs(p, s))
+          throw Error("SO3LR: halo lists of GPUs " + std::to_string(s) + " and " + std::to_string(p) + " disagree");
+    halo_send_off_.assign(host_halo_ + rank_ * lo, host_halo_ + rank_ * lo + nranks_ + 1);
+    halo_recv_off_.assign(host_halo_ + rank_ * lo + nranks_ + 1, host_halo_ + rank_ * lo + lo);
+  }
   const int P = host_small_[1];
   if (identity_ && 2 * P != E) throw Error("SO3LR: short-range list is not symmetric");
   stats_.pairs = P;
@@ -695,14 +751,22 @@ void Evaluator::compute() {
                           w.fev, rad_, f_inv_[b]->get(), f_ev_[b]->get(), sp_[b]->get(),
                           b == 0 ? drbf_.get() : nullptr, s);
     prof_end(0, kFilterFlopsPerPair * double(P));
-    {  // per-head projections for every row: qkv[n][h][5][32] = x[n][h*32:(h+1)*32] W_h
+    {  // per-head projections qkv[row][h][5][32] = x[row][h*32:(h+1)*32] W_h of every
+       // row the attention reads: the owned rows and (decomposed) their halo
       GemmArgs g{};
-      g.M = N; g.N = 160; g.K = 32;
-      g.A = xb_[b]->get(); g.lda = kF; g.strideA = 32;
+      g.M = identity_ ? N : n; g.N = 160; g.K = 32;
+      g.A = xb_[b]->get() + (identity_ ? 0 : r0 * kF); g.lda = kF; g.strideA = 32;
       g.W = w.qkv_fwd; g.ldw = 32; g.transB = true; g.strideW = 160 * 32;
-      g.C = qkv_[b]->get(); g.ldc = kQKV; g.strideC = 160;
+      g.C = qkv_[b]->get() + (identity_ ? 0 : r0 * kQKV); g.ldc = kQKV; g.strideC = 160;
       g.batch = 4;
       launch_gemm(g, s);
+      if (!identity_ && halo_recv_off_[nranks_] > 0) {
+        g.M = int(halo_recv_off_[nranks_]);
+        g.A = xb_[b]->get();
+        g.C = qkv_[b]->get();
+        g.rows = halo_recv_rows_.get();
+        launch_gemm(g, s);
+      }
     }
     launch_attention_forward(n, nb_, geo_.get(), sh_.get(), qkv_[b]->get(), f_inv_[b]->get(), f_ev_[b]->get(), norm_,
                              d_inv_.get(), d_ev_.get(), s);
@@ -743,10 +807,8 @@ void Evaluator::compute() {
     launch_post_attn_final(n, cat_.get() + r0 * kIntW, t_.get() + r0 * kIntW, A_[b]->get() + r0 * kEV, w.ln2w,
                            w.ln2b, xhat2_[b]->get() + r0 * kF, rstd2_[b]->get() + r0, gate_[b]->get() + r0 * 4,
                            xb_[b + 1]->get() + r0 * kF, evb_[b + 1]->get() + r0 * kEV, s);
-    if (b + 1 < layers_) {  // other GPUs' rows of the next block's input
-      allgather_rows(xb_[b + 1]->get(), kF);
-      allgather_rows(evb_[b + 1]->get(), kEV);
-    }
+    if (b + 1 < layers_)  // the halo rows of the next block's input
+      halo_exchange(xb_[b + 1]->get(), kF, evb_[b + 1]->get(), kEV);
   }
 
   // ---- output heads (owned rows) --------------------------------------------
@@ -838,8 +900,7 @@ void Evaluator::compute() {
                              A_[b]->get() + r0 * kEV, w.cg_int, g_cat_.get() + r0 * kIntW, g_a_.get() + r0 * kF,
                              g_A_.get() + r0 * kEV, s);
     // the sender role of the attention reverse reads the neighbours' adjoints
-    allgather_rows(g_a_.get(), kF);
-    allgather_rows(g_A_.get(), kEV);
+    halo_exchange(g_a_.get(), kF, g_A_.get(), kEV);
     launch_attention_reverse(n, nb_, geo_.get(), sh_.get(), qkv_[b]->get(), f_inv_[b]->get(), f_ev_[b]->get(),
                              g_a_.get(), g_A_.get(), norm_, b > 0 ? g_qkv_.get() : nullptr, pair_sc_.get(),
                              g_filt_inv_.get(), g_filt_ev_.get(), s);

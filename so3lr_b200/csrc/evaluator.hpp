@@ -199,8 +199,17 @@ class Evaluator {
   bool computed_ = false;
   int host_seg_[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   DeviceArray<int> tag_, seg_, pair_canon_;
+  // halo lists of the current neighbour lists (multi-GPU only)
+  DeviceArray<int> halo_flags_, halo_pos_, halo_send_rows_, halo_recv_rows_, halo_totals_;
+  DeviceArray<long long> halo_offsets_, halo_all_offsets_;
+  DeviceArray<double> halo_send_buf_, halo_recv_buf_;
+  long long *host_halo_ = nullptr;  // pinned: all ranks' offsets
+  std::vector<long long> halo_send_off_, halo_recv_off_;
   DeviceArray<long long> parts_;
   void allgather_rows(double *a, int width);
+  // refresh the halo rows (other GPUs' atoms that neighbour this GPU's atoms)
+  // of two row arrays at once; the identity layout (one GPU) does nothing
+  void halo_exchange(double *a, int wa, double *b, int wb);
   void exact_sums(const double *v, int stride, int ncol, int nseg, const int *seg, double *out);
 
   struct KernelProfile {

@@ -38,6 +38,19 @@ void count_sr(NeighborState &nb, double rc, cudaStream_t s);
 void fill_sr(NeighborState &nb, double rc, int E, cudaStream_t s);
 void fill_pairs(NeighborState &nb, int E, cudaStream_t s);
 
+// halo rows of the decomposition (halo.cu). Flags and positions: nranks x stride
+// ints each; send_rows / recv_rows: owned / foreign global rows grouped by peer;
+// offsets[0..nranks] (sends) and offsets[nranks+1..2 nranks+1] (receives) are the
+// per-peer starts; totals[0..1]: scratch for the scan totals
+void launch_halo_lists(int n_own, int row0, int stride, int nranks, int rank, const int *row_start, const int *nbr,
+                       int *send_flag, int *recv_flag, int *send_pos, int *recv_pos, int *send_rows, int *recv_rows,
+                       long long *offsets, int *totals, int *scan_scratch, cudaStream_t s);
+// buf[k][0..wa+wb) = (a[rows[k]][0..wa), b[rows[k]][0..wb)) and back
+void launch_halo_pack(int count, const int *rows, const double *a, int wa, const double *b, int wb, double *buf,
+                      cudaStream_t s);
+void launch_halo_unpack(int count, const int *rows, const double *buf, double *a, int wa, double *b, int wb,
+                        cudaStream_t s);
+
 // exact fixed-point sums (reduce.cu): nblk partial sums per segment and column,
 // parts[((blk * nseg + seg) * ncol + col) * 2 + {hi, lo}]
 void launch_fixed_segment_sum(int nseg, int nblk, const int *start, const double *v, int stride, int ncol,
@@ -133,6 +146,8 @@ struct GemmArgs {
   int ldaux = 0;
   double *aux_out = nullptr;
   Epi epi = Epi::None;
+  // optional row list: logical row m of A, C and aux is physical row rows[m]
+  const int *rows = nullptr;
   // batched over gridDim.z with per-batch strides (elements)
   int batch = 1;
   long long strideA = 0, strideW = 0, strideC = 0, strideAux = 0, strideBias = 0;

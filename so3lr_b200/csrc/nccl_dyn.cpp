@@ -31,6 +31,10 @@ const NcclApi &nccl() {
   api.all_gather = reinterpret_cast<decltype(api.all_gather)>(sym("ncclAllGather"));
   api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
   api.get_error_string = reinterpret_cast<decltype(api.get_error_string)>(sym("ncclGetErrorString"));
+  api.send = reinterpret_cast<decltype(api.send)>(sym("ncclSend"));
+  api.recv = reinterpret_cast<decltype(api.recv)>(sym("ncclRecv"));
+  api.group_start = reinterpret_cast<decltype(api.group_start)>(sym("ncclGroupStart"));
+  api.group_end = reinterpret_cast<decltype(api.group_end)>(sym("ncclGroupEnd"));
   loaded = true;
   return api;
 }

@@ -15,6 +15,10 @@ struct NcclApi {
   ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int);
   ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
   ncclResult_t (*comm_destroy)(ncclComm_t);
+  ncclResult_t (*send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+  ncclResult_t (*recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+  ncclResult_t (*group_start)();
+  ncclResult_t (*group_end)();
   const char *(*get_error_string)(ncclResult_t);
 };
 

@@ -140,12 +140,13 @@ __global__ void k_cell_sort(int ncells, const int *__restrict__ cell_start, cons
 __global__ void k_sr_count(int n, int row0, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
                            const int *__restrict__ cell_start, const int *__restrict__ cell_count,
                            const int *__restrict__ cell_atoms, const int *__restrict__ image_of,
-                           const int *__restrict__ image_start, double rc2, int reach, int *__restrict__ deg) {
+                           const int *__restrict__ image_start, double rc2, int reach, const int *__restrict__ tag,
+                           int *__restrict__ deg) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= n) return;
   const int i = row0 + r;
   int count = 0;
-  for_each_candidate(i, xw, g, cell, cell_start, cell_count, cell_atoms, image_of, image_start, reach,
+  for_each_candidate(i, xw, g, cell, cell_start, cell_count, cell_atoms, image_of, image_start, reach, tag,
                      [&](int, int, double dx, double dy, double dz) {
                        const double r2 = dx * dx + dy * dy + dz * dz;
                        if (r2 > 0.0 && r2 < rc2) ++count;
@@ -163,7 +164,7 @@ __global__ void k_sr_fill(int n, int row0, const double *__restrict__ xw, CellGr
   const int i = row0 + r;
   const int base = row_start[r];
   int count = 0;
-  for_each_candidate(i, xw, g, cell, cell_start, cell_count, cell_atoms, image_of, image_start, reach,
+  for_each_candidate(i, xw, g, cell, cell_start, cell_count, cell_atoms, image_of, image_start, reach, tag,
                      [&](int j, int code, double dx, double dy, double dz) {
                        const double r2 = dx * dx + dy * dy + dz * dz;
                        if (r2 > 0.0 && r2 < rc2) {
@@ -290,7 +291,8 @@ void count_sr(NeighborState &nb, double rc, cudaStream_t s) {
   const int reach = sr_reach(nb.grid, rc);
   const int n = nb.n_own;
   k_sr_count<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count,
-                                              nb.cell_atoms, nb.image_of, nb.image_start, rc * rc, reach, nb.deg);
+                                              nb.cell_atoms, nb.image_of, nb.image_start, rc * rc, reach, nb.tag,
+                                              nb.deg);
   SO3_LAUNCH("sr_count");
   exclusive_scan(nb.deg, nb.row_start, n, nb.row_start + n, nb.scan_scratch, s);
 }

@@ -51,7 +51,7 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols,
       const int gm = m0 + row, gk = k0 + col;
       double *dst = as + row * LDA_S + col;
       if (gm < g.M && gk < g.K) {
-        cp_async16(dst, A + (size_t)gm * g.lda + gk);
+        cp_async16(dst, A + (size_t)(g.rows ? g.rows[gm] : gm) * g.lda + gk);
       } else {
         dst[0] = 0.0;
         dst[1] = 0.0;
@@ -127,8 +127,9 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols,
   for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
-      const int row = m0 + wm * 32 + mi * 16 + hf * 8 + gq;
-      if (row >= g.M) continue;
+      const int lrow = m0 + wm * 32 + mi * 16 + hf * 8 + gq;
+      if (lrow >= g.M) continue;
+      const int row = g.rows ? g.rows[lrow] : lrow;
 #pragma unroll
       for (int ni = 0; ni < 4; ++ni) {
 #pragma unroll
