@@ -365,21 +365,32 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
     const int nx = g.ncell[0], ny = g.ncell[1], nz = g.ncell[2];
     const int c = cell[i];
     const int cx = c % nx, cy = (c / nx) % ny, cz = c / (nx * ny);
-    // x runs of constant periodic shift: cells [lo, hi] of one row are contiguous
-    const int sx_lo = (cx - reach >= 0) ? 0 : -((reach - cx + nx - 1) / nx);
-    const int sx_hi = (cx + reach) / nx;
+    const double clx = g.len[0] / nx, cly = g.len[1] / ny, clz = g.len[2] / nz;
+    // cells farther than the cutoff from the home cell (nearest points) cannot
+    // hold a neighbour: rows with such (oy, oz) are skipped and each row's x run
+    // is trimmed to the cells that can; the candidates that remain are the same
+    // as before, in the same order
+    const double rcs = rc2 * (1.0 + 1e-12) + 1e-12;
     for (int oz = -reach; oz <= reach; ++oz) {
       int wz = cz + oz, sz = 0;
       while (wz < 0) { wz += nz; --sz; }
       while (wz >= nz) { wz -= nz; ++sz; }
+      const double dz = max(abs(oz) - 1, 0) * clz;
       for (int oy = -reach; oy <= reach; ++oy) {
+        const double dy = max(abs(oy) - 1, 0) * cly;
+        const double rem = rcs - dy * dy - dz * dz;
+        if (rem <= 0.0) continue;
+        const int rx = min(reach, int(floor(sqrt(rem) / clx)) + 1);
         int wy = cy + oy, sy = 0;
         while (wy < 0) { wy += ny; --sy; }
         while (wy >= ny) { wy -= ny; ++sy; }
         const int row = (wz * ny + wy) * nx;
         const double shy = sy * g.len[1], shz = sz * g.len[2];
+        // x runs of constant periodic shift: cells [lo, hi] of one row are contiguous
+        const int sx_lo = (cx - rx >= 0) ? 0 : -((rx - cx + nx - 1) / nx);
+        const int sx_hi = (cx + rx) / nx;
         for (int sx = sx_lo; sx <= sx_hi; ++sx) {
-          const int lo = max(0, cx - reach - sx * nx), hi = min(nx - 1, cx + reach - sx * nx);
+          const int lo = max(0, cx - rx - sx * nx), hi = min(nx - 1, cx + rx - sx * nx);
           if (lo > hi) continue;
           scan_range(cell_start[row + lo], cell_start[row + hi] + cell_count[row + hi], sx * g.len[0], shy, shz);
         }
