@@ -264,11 +264,17 @@ __global__ void k_lr_gather(int n, int periodic, const int *__restrict__ cell_at
 // on full batches of 32 queued pairs. Every lane accumulates its queue slots in
 // a fixed order, so the result is deterministic.
 constexpr int kLrWarps = 8;
+constexpr int kLrMaxReach = 8;
+// per (|oy|, |oz|) of the cell stencil: the x reach of the cells that can hold
+// a neighbour within the cutoff (-1: none)
+struct LrStencil {
+  signed char rx[kLrMaxReach + 1][kLrMaxReach + 1];
+};
 constexpr int kLrQueue = 64;
 __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
     int n, int row0, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
     const int *__restrict__ cell_start, const int *__restrict__ cell_count, const int *__restrict__ image_of,
-    const int *__restrict__ image_start, int reach, double rc2, const double4 *__restrict__ pos4,
+    const int *__restrict__ image_start, int reach, LrStencil st, double rc2, const double4 *__restrict__ pos4,
     const double4 *__restrict__ par4, const int *__restrict__ z, const double *__restrict__ q,
     const double *__restrict__ h, const double *__restrict__ aref, const double *__restrict__ cref, int table,
     LrDev p, double *__restrict__ e_lr, double *__restrict__ e_elec, double *__restrict__ e_disp,
@@ -365,22 +371,17 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
     const int nx = g.ncell[0], ny = g.ncell[1], nz = g.ncell[2];
     const int c = cell[i];
     const int cx = c % nx, cy = (c / nx) % ny, cz = c / (nx * ny);
-    const double clx = g.len[0] / nx, cly = g.len[1] / ny, clz = g.len[2] / nz;
     // cells farther than the cutoff from the home cell (nearest points) cannot
     // hold a neighbour: rows with such (oy, oz) are skipped and each row's x run
-    // is trimmed to the cells that can; the candidates that remain are the same
-    // as before, in the same order
-    const double rcs = rc2 * (1.0 + 1e-12) + 1e-12;
+    // is trimmed to the cells that can (st.rx, tabulated on the host); the
+    // candidates that remain are the same as before, in the same order
     for (int oz = -reach; oz <= reach; ++oz) {
       int wz = cz + oz, sz = 0;
       while (wz < 0) { wz += nz; --sz; }
       while (wz >= nz) { wz -= nz; ++sz; }
-      const double dz = max(abs(oz) - 1, 0) * clz;
       for (int oy = -reach; oy <= reach; ++oy) {
-        const double dy = max(abs(oy) - 1, 0) * cly;
-        const double rem = rcs - dy * dy - dz * dz;
-        if (rem <= 0.0) continue;
-        const int rx = min(reach, int(floor(sqrt(rem) / clx)) + 1);
+        const int rx = st.rx[abs(oy)][abs(oz)];
+        if (rx < 0) continue;
         int wy = cy + oy, sy = 0;
         while (wy < 0) { wy += ny; --sy; }
         while (wy >= ny) { wy -= ny; ++sy; }
@@ -434,10 +435,28 @@ void launch_long_range(int n, int n_cells_atoms, const NeighborState &nb, double
                                                           z, alpha_ref, c6_ref, table_size, pos4, par4);
   SO3_LAUNCH("lr_gather");
   const int reach = sr_reach(nb.grid, rc_lr);
+  LrStencil st;
+  {
+    const CellGrid &g = nb.grid;
+    const double clx = g.len[0] / g.ncell[0], cly = g.len[1] / g.ncell[1], clz = g.len[2] / g.ncell[2];
+    const double rcs = rc_lr * rc_lr * (1.0 + 1e-12) + 1e-12;
+    for (int a = 0; a <= kLrMaxReach; ++a)
+      for (int b = 0; b <= kLrMaxReach; ++b) {
+        int rx = reach;
+        if (g.periodic && reach <= kLrMaxReach) {
+          const double dy = std::max(a - 1, 0) * cly, dz = std::max(b - 1, 0) * clz;
+          const double rem = rcs - dy * dy - dz * dz;
+          rx = rem <= 0.0 ? -1 : std::min(reach, int(std::floor(std::sqrt(rem) / clx)) + 1);
+        }
+        st.rx[a][b] = static_cast<signed char>(rx);
+      }
+    if (g.periodic && reach > kLrMaxReach) throw std::runtime_error("SO3LR long range: cell stencil reach above " +
+                                                       std::to_string(kLrMaxReach));
+  }
   const int threads = kLrWarps * 32;
   const int blocks = (n * 32 + threads - 1) / threads;
   k_long_range<<<blocks, threads, 0, s>>>(n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count, nb.image_of,
-                                          nb.image_start, reach, rc_lr * rc_lr, pos4, par4, z, q, h, alpha_ref,
+                                          nb.image_start, reach, st, rc_lr * rc_lr, pos4, par4, z, q, h, alpha_ref,
                                           c6_ref, table_size, p, e_lr, e_elec, e_disp, dq, dh, f_lr, w_lr);
   SO3_LAUNCH("long_range");
 }
