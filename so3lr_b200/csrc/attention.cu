@@ -24,10 +24,12 @@ __device__ inline double head_sum(double v) {  // sum over the 8 lanes of a head
   return v;
 }
 
+// four consecutive doubles (32-byte aligned, read-only during the kernel) with
+// one 256-bit load
 __device__ inline void load4(const double *p, double (&v)[4]) {
-  const double2 a = *reinterpret_cast<const double2 *>(p);
-  const double2 b = *reinterpret_cast<const double2 *>(p + 2);
-  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+  asm("ld.global.nc.v4.f64 {%0,%1,%2,%3}, [%4];"
+               : "=d"(v[0]), "=d"(v[1]), "=d"(v[2]), "=d"(v[3])
+               : "l"(p));
 }
 __device__ inline void store4(double *p, const double (&v)[4]) {
   *reinterpret_cast<double2 *>(p) = make_double2(v[0], v[1]);
@@ -56,6 +58,7 @@ __global__ void __launch_bounds__(256) k_attention_forward(int n, int row0, cons
   load4(qkv + (size_t)a * kQKV + head_off + 3 * 32, qea);
   double acc[4] = {0, 0, 0, 0};
   double acc_ev = 0.0;
+  const double inv_norm = 1.0 / norm;  // one division per atom instead of two per edge
   const int my_deg = lane < kEV ? degree_of_channel(lane) : 0;
   const double my_par = parity_sign(my_deg);
   const int e0 = row_start[r], e1 = row_start[r + 1];
@@ -103,8 +106,8 @@ __global__ void __launch_bounds__(256) k_attention_forward(int n, int row0, cons
       ai += qa[j] * kb[j] * fi[j];
       ae += qea[j] * keb[j] * fe[j];
     }
-    ai = head_sum(ai) / norm;
-    ae = head_sum(ae) / norm;
+    ai = head_sum(ai) * inv_norm;
+    ae = head_sum(ae) * inv_norm;
     const double wi = phi * ai;
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[j] += wi * vb[j];
@@ -223,7 +226,7 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
       si_in += ga[j] * vb[j];
       si_out += gb[j] * va[j];
     }
-    ai_out = head_sum(ai_out) / norm;
+    ai_out = head_sum(ai_out) * inv_norm;
     si_in = head_sum(si_in);
     si_out = head_sum(si_out);
     const double c_q = phi * si_in * inv_norm, c_qe = phi * s_in * inv_norm;
@@ -259,9 +262,9 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
         ae_in += qea[j] * keb[j] * fe[j];
         ae_out += qeb[j] * kea[j] * fe[j];
       }
-      ai_in = head_sum(ai_in) / norm;
-      ae_in = head_sum(ae_in) / norm;
-      ae_out = head_sum(ae_out) / norm;
+      ai_in = head_sum(ai_in) * inv_norm;
+      ae_in = head_sum(ae_in) * inv_norm;
+      ae_out = head_sum(ae_out) * inv_norm;
       // "in" is into the pair's primary receiver a; lane = 4 quantity + head
       const int qsel = lane >> 2, hh = lane & 3;
       const double v_ai_in = __shfl_sync(0xffffffffu, ai_in, hh * 8);
