@@ -236,6 +236,13 @@ __device__ inline LrPair lr_pair_tab(const LrDev &p, const LrConst &k, double r,
   return o;
 }
 
+// one 256-bit read-only load of a 32-byte aligned double4
+__device__ inline double4 ld4(const double4 *p) {
+  double4 v;
+  asm("ld.global.nc.v4.f64 {%0,%1,%2,%3}, [%4];" : "=d"(v.x), "=d"(v.y), "=d"(v.z), "=d"(v.w) : "l"(p));
+  return v;
+}
+
 __device__ inline double warp_sum(double v) {
   for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
   return v;
@@ -299,7 +306,7 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
     const int k = qk[wl][slot];
     const double vx = qv[wl][slot][0], vy = qv[wl][slot][1], vz = qv[wl][slot][2];
     const double r = sqrt(vx * vx + vy * vy + vz * vz);
-    const double4 pj = pos4[k], hj = par4[k];
+    const double4 pj = ld4(pos4 + k), hj = ld4(par4 + k);
     const LrPair o = lr_pair_tab(p, kc, r, qi, pj.w, hi, hj.x, ai0, hj.y, ci0, hj.z);
     acc_ee += o.e_elec;
     acc_ed += o.e_disp;
@@ -323,7 +330,7 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
       bool valid = false;
       double vx = 0, vy = 0, vz = 0;
       if (k < e) {
-        const double4 pk = pos4[k];
+        const double4 pk = ld4(pos4 + k);
         vx = pk.x + shx - xi;
         vy = pk.y + shy - yi;
         vz = pk.z + shz - zi;
