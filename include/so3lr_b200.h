@@ -156,9 +156,11 @@ int so3lr_compute_device(so3lr_handle *h, const so3lr_frame *in_device_x, double
  * its own handle. After that, so3lr_compute and so3lr_md_* are collective: every
  * rank passes the same whole system, the atoms are split into spatial bricks of
  * the periodic box (1x1x2, 1x2x2, 2x2x2, ... for 2, 4, 8 ranks), each GPU computes
- * its own atoms, rows owned by other GPUs are refreshed with NCCL all-gathers
- * (positions, block features, charges and Hirshfeld ratios, block adjoints), and
- * every rank returns the whole result. Global sums are exact, so energies and
+ * its own atoms, rows owned by other GPUs are refreshed over NCCL (positions,
+ * charges and Hirshfeld ratios by all-gathers; block features and adjoints only
+ * for the halo rows that neighbour this GPU's atoms, by send/receive), and
+ * every rank returns the whole result. NCCL (libnccl.so.2) is loaded at the
+ * first multi-GPU call, not linked. Global sums are exact, so energies and
  * forces are bit-identical for any number of ranks. so3lr_owned_atoms returns
  * the number of atoms this rank computes (after the first collective call). */
 int so3lr_nccl_unique_id(char out[128], char *err, size_t errlen);

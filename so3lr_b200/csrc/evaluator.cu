@@ -723,10 +723,12 @@ void Evaluator::build_neighbors() {
 // the evaluation
 //
 // Rows [row0, row0 + n_own) are this GPU's atoms; every other row is a copy of
-// another GPU's atom, refreshed by an all-gather right after its owner
-// computed it. Everything an owned atom sums over (its CSR row, its cell
-// stencil) is complete locally, so no partial sum ever crosses GPUs; the only
-// global sums (charge, charge seeds, energy, virial) are exact.
+// another GPU's atom, refreshed right after its owner computed it: positions,
+// charges and Hirshfeld ratios by all-gathers, block features and adjoints only
+// for the halo rows (the other GPUs' short-range neighbours of this GPU's atoms,
+// halo.cu). Everything an owned atom sums over (its CSR row, its cell stencil)
+// is complete locally, so no partial sum ever crosses GPUs; the only global sums
+// (charge, charge seeds, energy, virial, kinetic energy) are exact.
 // ---------------------------------------------------------------------------
 void Evaluator::compute() {
   SO3_CUDA(cudaSetDevice(device_));

@@ -526,34 +526,6 @@ void launch_assemble(const NeighborState &nb, const double *geo, const double *g
   SO3_LAUNCH("assemble");
 }
 
-// ---------------------------------------------------------------------------
-// deterministic segmented sums (fixed thread order + fixed tree)
-// ---------------------------------------------------------------------------
-__global__ void k_segment_sum(const int *__restrict__ start, const double *__restrict__ v, int stride, int ncol,
-                              double *__restrict__ out) {
-  __shared__ double buf[256];
-  const int s = blockIdx.x;
-  const int b = start[s], e = start[s + 1];
-  for (int col = 0; col < ncol; ++col) {
-    double acc = 0.0;
-    for (int i = b + threadIdx.x; i < e; i += blockDim.x) acc += v[(size_t)i * stride + col];
-    buf[threadIdx.x] = acc;
-    __syncthreads();
-    for (int off = 128; off > 0; off >>= 1) {
-      if (threadIdx.x < off) buf[threadIdx.x] += buf[threadIdx.x + off];
-      __syncthreads();
-    }
-    if (threadIdx.x == 0) out[(size_t)s * ncol + col] = buf[0];
-    __syncthreads();
-  }
-}
-
-void launch_segment_sum(int nseg, const int *start, const double *v, int stride, int ncol, double *out,
-                        cudaStream_t s) {
-  if (nseg == 0) return;
-  k_segment_sum<<<nseg, 256, 0, s>>>(start, v, stride, ncol, out);
-  SO3_LAUNCH("segment_sum");
-}
 
 // q = raw + (Q_img - sum_img raw) / N_img (output_heads.cpp:441-451; image_segments.cpp:49-98);
 // also the per-image mean of the charge seeds (image_segments.cpp:104-141).

@@ -171,7 +171,6 @@ void launch_post_attn_rev_final(int n, const double *g_x, const double *g_ev, co
 void launch_post_attn_rev_ln1(int n, const double *g_n1, const double *xhat1, const double *rstd1,
                               const double *lnw1, const double *A, const double *cg_int, const double *g_cat,
                               double *g_a, double *g_A, cudaStream_t s);
-void launch_add(int count, const double *a, double *b, cudaStream_t s);
 
 // heads
 void launch_heads_finalize(int n, const int *z, const double *hcat, const HeadsW &hw, double *hk_out,
@@ -180,9 +179,6 @@ void launch_heads_seed(int n, const int *z, const double *hpre, const double *hk
                        const double *dq, const double *dq_mean, const int *image_of_atom, const double *dh,
                        double *g_hcat, cudaStream_t s);
 
-// deterministic segmented sums: out[s] = sum_{i in [start[s], start[s+1])} v[i*stride + col]
-void launch_segment_sum(int nseg, const int *start, const double *v, int stride, int ncol, double *out,
-                        cudaStream_t s);
 void launch_charge_correct(int n, const double *raw, const double *raw_sum, const double *qtot,
                            const int *image_of_atom, const int *image_start, double *q, double *dq_mean_out,
                            const double *dq_sum, cudaStream_t s);

@@ -425,15 +425,6 @@ void launch_post_attn_rev_ln1(int n, const double *g_n1, const double *xhat1, co
   SO3_LAUNCH("post_attn_rev_ln1");
 }
 
-__global__ void k_add(int count, const double *__restrict__ a, double *__restrict__ b) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < count) b[i] += a[i];
-}
-void launch_add(int count, const double *a, double *b, cudaStream_t s) {
-  if (count == 0) return;
-  k_add<<<(count + 255) / 256, 256, 0, s>>>(count, a, b);
-  SO3_LAUNCH("add");
-}
 
 // ---------------------------------------------------------------------------
 // output heads (output_heads.cpp:137-176, 341-451): hcat = silu(x W1cat^T + b1cat)
