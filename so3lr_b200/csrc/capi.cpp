@@ -17,8 +17,8 @@ using so3lr_b200::Error;
 using so3lr_b200::Evaluator;
 using so3lr_b200::SystemSpec;
 
-long long &so3lr_b200::launch_counter() {
-  static long long count = 0;
+std::atomic<long long> &so3lr_b200::launch_counter() {
+  static std::atomic<long long> count{0};
   return count;
 }
 
@@ -334,7 +334,7 @@ int so3lr_profile_read(so3lr_handle *h, int kernel, double *total_ms, long long 
   }
 }
 
-long long so3lr_launch_count(void) { return so3lr_b200::launch_counter(); }
+long long so3lr_launch_count(void) { return so3lr_b200::launch_counter().load(); }
 
 int so3lr_long_range_noalloc(so3lr_handle *h, long long natoms, const double *x, const double *q,
                              const double *ratios, const int *z, double *e_lr, double *e_elec, double *e_disp,

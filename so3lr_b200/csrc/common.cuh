@@ -8,6 +8,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <stdexcept>
 #include <string>
@@ -37,8 +38,13 @@ inline void cuda_check(cudaError_t e, const char *what) {
 }
 // number of kernels this library has launched in the process (every launcher
 // calls SO3_LAUNCH exactly once per kernel launch)
-long long &launch_counter();
+std::atomic<long long> &launch_counter();
 #define SO3_CUDA(x) ::so3lr_b200::cuda_check((x), #x)
+
+// Allow `bytes` of dynamic shared memory for kernel `func` on the current
+// device. The attribute is per device, so it is set once per (kernel, device),
+// thread-safely (launch.cpp).
+void allow_dynamic_smem(const void *func, std::size_t bytes);
 #define SO3_LAUNCH(what) (++::so3lr_b200::launch_counter(), ::so3lr_b200::cuda_check(cudaGetLastError(), what))
 
 // degree slot of equivariant channel m (0..23): 3 + 5 + 7 + 9

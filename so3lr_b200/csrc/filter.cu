@@ -247,11 +247,7 @@ void launch_filter_forward(int P, const double *geo, const int *pair_a, const in
                            double *f_inv, double *f_ev, double *sp, double *drbf, cudaStream_t s) {
   if (P == 0) return;
   const size_t smem = sizeof(double) * (TP * LDR * 2 + TP * LDU + TP * 4 + TP);
-  static bool configured = false;
-  if (!configured) {
-    SO3_CUDA(cudaFuncSetAttribute(k_filter_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    configured = true;
-  }
+  allow_dynamic_smem(reinterpret_cast<const void *>(k_filter_forward), smem);
   k_filter_forward<<<(P + TP - 1) / TP, 256, smem, s>>>(P, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad, f_inv,
                                                          f_ev, sp, drbf);
   SO3_LAUNCH("filter_forward");
@@ -514,11 +510,7 @@ void launch_filter_reverse(int P, const double *geo, const int *pair_a, const in
   if (P == 0) return;
   const size_t smem = sizeof(double) * (TP * LDU + TP * LDR + 8 * TP);
   static_assert(TP * (kPairScalars + kGeo + kR) <= TP * LDU, "per-pair inputs must fit in the gradient tile");
-  static bool configured = false;
-  if (!configured) {
-    SO3_CUDA(cudaFuncSetAttribute(k_filter_reverse, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    configured = true;
-  }
+  allow_dynamic_smem(reinterpret_cast<const void *>(k_filter_reverse), smem);
   const int tiles = (P + TP - 1) / TP;
   k_filter_reverse<<<2 * tiles, 256, smem, s>>>(P, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad, g_filt_inv,
                                                 g_filt_ev, sp, drbf, gA, pair_sc, need_l0 ? 1 : 0,

@@ -163,11 +163,7 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols,
 template <bool T, Epi E>
 void launch_gemm_kernel(const GemmArgs &g, dim3 grid, cudaStream_t s, int aux_cols, int ldaux2) {
   constexpr size_t smem = sizeof(double) * gemm_smem_doubles<T>();
-  static bool configured = false;
-  if (!configured) {
-    SO3_CUDA(cudaFuncSetAttribute(k_gemm<T, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    configured = true;
-  }
+  allow_dynamic_smem(reinterpret_cast<const void *>(k_gemm<T, E>), smem);
   k_gemm<T, E><<<grid, kGemmThreads, smem, s>>>(g, aux_cols, ldaux2);
 }
 

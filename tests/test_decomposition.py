@@ -158,3 +158,24 @@ def test_multi_gpu_bit_identical(world, gpu_model):
         assert np.array_equal(vir, ref["virial"])
         assert np.array_equal(chg, ref["charges"])
         assert np.array_equal(va, ref_va)
+
+
+@pytest.mark.gpu
+def test_two_devices_in_one_process():
+    """One process, one handle per GPU (how turbo packs are spread over GPUs):
+    each device gets its own kernel configuration, and the same pack gives the
+    same bits on both."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from so3lr_b200 import So3lrB200
+    from so3lr_b200.systems import turbo_batch
+    pos, z, off, q, m = turbo_batch(16, seed=31)
+    a = So3lrB200(MODEL, 0)
+    b = So3lrB200(MODEL, 1)
+    ra = a.compute_batch(pos, z, off, q, m)
+    rb = b.compute_batch(pos, z, off, q, m)
+    assert np.array_equal(ra["forces"], rb["forces"])
+    assert np.array_equal(ra["image_energy"], rb["image_energy"])
+    a.close()
+    b.close()
