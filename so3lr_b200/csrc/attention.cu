@@ -265,28 +265,23 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
       ai_in = head_sum(ai_in) * inv_norm;
       ae_in = head_sum(ae_in) * inv_norm;
       ae_out = head_sum(ae_out) * inv_norm;
-      // "in" is into the pair's primary receiver a; lane = 4 quantity + head
-      const int qsel = lane >> 2, hh = lane & 3;
-      const double v_ai_in = __shfl_sync(0xffffffffu, ai_in, hh * 8);
-      const double v_ae_in = __shfl_sync(0xffffffffu, ae_in, hh * 8);
-      const double v_si_in = __shfl_sync(0xffffffffu, si_in, hh * 8);
-      const double v_se_in = __shfl_sync(0xffffffffu, s_in, hh * 8);
-      const double v_ai_out = __shfl_sync(0xffffffffu, ai_out, hh * 8);
-      const double v_ae_out = __shfl_sync(0xffffffffu, ae_out, hh * 8);
-      const double v_si_out = __shfl_sync(0xffffffffu, si_out, hh * 8);
-      const double v_se_out = __shfl_sync(0xffffffffu, s_out, hh * 8);
-      double val;
-      switch (qsel) {
-        case 0: val = v_ai_in; break;
-        case 1: val = v_ae_in; break;
-        case 2: val = v_si_in; break;
-        case 3: val = v_se_in; break;
-        case 4: val = v_ai_out; break;
-        case 5: val = v_ae_out; break;
-        case 6: val = v_si_out; break;
-        default: val = v_se_out; break;
+      // pair scalars for the filter reverse: the cutoff-gradient weight
+      // sum_h (a_in s_in + a_out s_out) of the invariant and the ev attention,
+      // and the ev coefficients of both directions per head. The two
+      // directions' products are added with explicitly rounded (commutative)
+      // sums and the heads in a symmetric tree, so the values do not depend on
+      // which endpoint holds the pair.
+      double t = __dadd_rn(__dadd_rn(__dmul_rn(ai_in, si_in), __dmul_rn(ai_out, si_out)),
+                           __dadd_rn(__dmul_rn(ae_in, s_in), __dmul_rn(ae_out, s_out)));
+      t += __shfl_xor_sync(0xffffffffu, t, 8);
+      t += __shfl_xor_sync(0xffffffffu, t, 16);
+      double *ps = pair_sc + (size_t)p * kPairScalars;
+      if (lane == 0) ps[0] = t;
+      if (lane == 1) ps[9] = 0.0;
+      if ((lane & 7) == 0) {
+        ps[1 + h] = ae_in;
+        ps[5 + h] = ae_out;
       }
-      pair_sc[(size_t)p * kPairScalars + lane] = val;
     }
   }
   if (g_qkv != nullptr) {

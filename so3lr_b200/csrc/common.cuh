@@ -27,7 +27,9 @@ constexpr int kHeadHidden = 128;
 constexpr int kHirsh = 64;
 constexpr int kHeadCat = 2 * kHeadHidden + kHirsh;  // fused first layers of the 3 heads
 constexpr int kMaxLayers = 8;
-constexpr int kPairScalars = 32;  // per pair, per block: alpha / s for both directions
+// per pair, per block: the cutoff-gradient weight and the ev attention
+// coefficients of both directions per head (+1 pad: rows of 16-byte chunks)
+constexpr int kPairScalars = 10;
 // Algorithmic FLOPs of the two filter MLPs of one pair, one direction of the
 // pass (forward, or the reverse input gradients): 2 filters x (R F + F F + 4 H + H F)
 // multiply-adds x 2. The reverse's first-layer recompute is not counted.
@@ -155,6 +157,7 @@ struct FilterW {
   const double *w1, *b1;  // [128][128], [128]  hidden -> filter
   const double *v0, *c0;  // [32][4], [32]      L0 -> ev hidden
   const double *v1, *c1;  // [128][32], [128]   ev hidden -> filter
+  const double *bc1;      // [128]: b1 + c1, the filter's total output bias
   // The same matrices as m16n8k8 DMMA B operands in fragment-major order (see
   // fragment_major in evaluator.cu): B(k, n) of a K x N operand sits at
   // [k/8][n/32][lane = 4 (n%8) + (k%8)/2][(n%32)/8][k%2].

@@ -76,7 +76,7 @@ void Evaluator::upload_weights() {
     return off;
   };
   const std::size_t F = kF, R = kR, H = kEH;
-  struct FOff { std::size_t w0, b0, w1, b1, v0, c0, v1, c1, w0t_f, w1t_f, v1t_f, w1_f, v1_f, w0_f; };
+  struct FOff { std::size_t w0, b0, w1, b1, v0, c0, v1, c1, bc1, w0t_f, w1t_f, v1t_f, w1_f, v1_f, w0_f; };
   struct BOff {
     FOff finv, fev;
     std::size_t cg_att, cg_int, qf, qr, ln1w, ln1b, ln2w, ln2b, m1w, m1b, m2w, m2b, iw, ib;
@@ -94,7 +94,12 @@ void Evaluator::upload_weights() {
     o.v0 = push(model_.f64(prefix + ".mlp_ev.0.weight", {H, 4}));
     o.c0 = push(model_.f64(prefix + ".mlp_ev.0.bias", {H}));
     o.v1 = push(v1);
-    o.c1 = push(model_.f64(prefix + ".mlp_ev.mlp_ev_layer_1.0.bias", {F}));
+    const auto b1 = model_.f64(prefix + ".mlp_rbf.mlp_rbf_layer_1.0.bias", {F});
+    const auto c1 = model_.f64(prefix + ".mlp_ev.mlp_ev_layer_1.0.bias", {F});
+    o.c1 = push(c1);
+    std::vector<double> bc1(F);
+    for (std::size_t k = 0; k < F; ++k) bc1[k] = b1[k] + c1[k];
+    o.bc1 = push(bc1);
     const int iF = int(F), iR = int(R), iH = int(H);
     o.w0t_f = push(fragment_major(iR, iF, [&](int r, int j) { return w0[std::size_t(j) * R + r]; }));
     o.w1t_f = push(fragment_major(iF, iF, [&](int j, int oo) { return w1[std::size_t(oo) * F + j]; }));
@@ -194,8 +199,8 @@ void Evaluator::upload_weights() {
     const BOff &o = boff[b];
     BlockW &w = blocks_[b];
     auto fw = [&](const FOff &f) {
-      return FilterW{P(f.w0),    P(f.b0),    P(f.w1),    P(f.b1),   P(f.v0),   P(f.c0),  P(f.v1),
-                     P(f.c1),    P(f.w0t_f), P(f.w1t_f), P(f.v1t_f), P(f.w1_f), P(f.v1_f), P(f.w0_f)};
+      return FilterW{P(f.w0),  P(f.b0),    P(f.w1),    P(f.b1),    P(f.v0),   P(f.c0),   P(f.v1),  P(f.c1),
+                     P(f.bc1), P(f.w0t_f), P(f.w1t_f), P(f.v1t_f), P(f.w1_f), P(f.v1_f), P(f.w0_f)};
     };
     w.finv = fw(o.finv);
     w.fev = fw(o.fev);

@@ -233,8 +233,8 @@ __global__ void __launch_bounds__(256, 2) k_filter_forward(int P, const double *
         for (int ni = 0; ni < 4; ++ni) {
           const int col = wn * 32 + ni * 8 + 2 * t;
           double2 v;
-          v.x = (acc[mi][ni][2 * hf] + W.b1[col]) + W.c1[col];
-          v.y = (acc[mi][ni][2 * hf + 1] + W.b1[col + 1]) + W.c1[col + 1];
+          v.x = acc[mi][ni][2 * hf] + W.bc1[col];
+          v.y = acc[mi][ni][2 * hf + 1] + W.bc1[col + 1];
           *reinterpret_cast<double2 *>(out + (size_t)p * kF + col) = v;
         }
       }
@@ -258,8 +258,10 @@ void launch_filter_forward(int P, const double *geo, const int *pair_a, const in
 // radial, cutoff and spherical-harmonic gradients accumulated into gv[p] (3)
 // and, when ev is live, the L0 gradient gl0[p][4].
 // g_filt_inv/g_filt_ev[p][128]: dL/d(filter) with both directions summed,
-// written by the attention reverse. pair_sc[p][32] = alpha_inv, alpha_ev, s_inv,
-// s_ev for the direction into the pair's primary receiver ([0:16]) and out of it.
+// written by the attention reverse. pair_sc[p][10] = the cutoff-gradient weight
+// sum_h (alpha s) over both directions and both attentions, then the ev
+// attention coefficient per head into ([1:5]) and out of ([5:9]) the pair's
+// primary receiver.
 // All per-tile inputs are streamed into shared memory with cp.async at kernel
 // start so the tensor-core work never waits on a gather.
 // ---------------------------------------------------------------------------
@@ -473,17 +475,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
   for (int j = 0; j < 8; ++j) gr += gw[pl * LDR + 8 * q + j] * drs[pl * kR + 8 * q + j];
   const double *s = sc + pl * kPairScalars;
   const double dphi = geos[pl * kGeo + 5], phi = geos[pl * kGeo + 4];
-  if (q == 0) {
-    // cutoff gradient: sum over heads of alpha*s for both directions; the two
-    // directions are added first (a commutative add), so the result does not
-    // depend on which endpoint the pair is stored from
-#pragma unroll
-    for (int h = 0; h < 4; ++h)
-#pragma unroll
-      for (int ai = 0; ai <= 4; ai += 4)
-        gr += __dmul_rn(__dadd_rn(__dmul_rn(s[ai + h], s[ai + 8 + h]), __dmul_rn(s[16 + ai + h], s[16 + ai + 8 + h])),
-                        dphi);
-  }
+  if (q == 0) gr += __dmul_rn(s[0], dphi);  // cutoff gradient (its weight is orientation-independent)
   gr += __shfl_xor_sync(0xffffffffu, gr, 1);
   gr += __shfl_xor_sync(0xffffffffu, gr, 2);
   if (p < P) {
@@ -493,8 +485,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
     for (int j = 0; j < 6; ++j) {
       const int m = 6 * q + j;
       const int d = degree_of_channel(m);
-      const double y = __dmul_rn(phi, __dadd_rn(__dmul_rn(s[4 + d], gA[(size_t)a * kEV + m]),
-                                                parity_sign(d) * __dmul_rn(s[20 + d], gA[(size_t)b * kEV + m])));
+      const double y = __dmul_rn(phi, __dadd_rn(__dmul_rn(s[1 + d], gA[(size_t)a * kEV + m]),
+                                                parity_sign(d) * __dmul_rn(s[5 + d], gA[(size_t)b * kEV + m])));
       double *dst = g_y + (size_t)p * kEV + m;
       *dst = accumulate ? *dst + y : y;
     }

@@ -124,8 +124,8 @@ __device__ inline void smooth_switch(double r, double cuton, double cutoff, doub
   const double sl = left > 1.0e-12 ? left : 1.0e-12, sr = right > 1.0e-12 ? right : 1.0e-12;
   const double inv_lr = 1.0 / (sl * sr);
   const double isl = sr * inv_lr, isr = sl * inv_lr;  // 1/sl, 1/sr
-  const double sig_l = left > 0.0 ? exp(-isl) : 0.0;
-  const double sig_r = right > 0.0 ? exp(-isr) : 0.0;
+  const double sig_l = left > 0.0 ? exp_tang(-isl) : 0.0;
+  const double sig_r = right > 0.0 ? exp_tang(-isr) : 0.0;
   const double den = sig_l + sig_r + 1.0e-12;
   const double iden = 1.0 / den;
   v = sig_l * iden;
@@ -169,7 +169,7 @@ __device__ inline LrPair lr_pair_tab(const LrDev &p, const LrConst &k, double r,
   const double inv_r = 1.0 / r;
   const double ratio = r * k.inv_sigma;
   const double erf_t = erf(ratio);
-  const double exp_t = exp(-(ratio * ratio));
+  const double exp_t = exp_tang(-(ratio * ratio));
   const double pot = erf_t * inv_r;
   const double dpot = (2.0 * r * exp_t * inv_sqrt_pi * k.inv_sigma - erf_t) * (inv_r * inv_r);
   const double disp = r - p.cutoff;
@@ -194,7 +194,7 @@ __device__ inline LrPair lr_pair_tab(const LrDev &p, const LrConst &k, double r,
       const double dd_dhi = 2.0 * ai * ai0 * c6j + aj * aj * dc6i;
       const double dc6_dhi = (dn_dhi * den - num * dd_dhi) * (iden * iden);
       const double ialpha7 = inv7 / alpha;  // 1 / (7 alpha)
-      const double a7 = exp(log(alpha) * inv7);
+      const double a7 = exp_tang(log(alpha) * inv7);
       const double rv = p.fine_factor * a7;
       constexpr double b0 = -0.00433008, b1 = 0.24428889, b2 = 0.04125273, b3 = -0.00078893;
       const double sig = b3 * rv * rv * rv + b2 * rv * rv + b1 * rv + b0;
