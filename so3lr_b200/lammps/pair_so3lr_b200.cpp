@@ -6,6 +6,8 @@
 // eatom, eng_vdwl and virial[6].
 #include "pair_so3lr_b200.h"
 
+#include <mpi.h>
+
 #include <cstdlib>
 #include <cstring>
 
@@ -64,9 +66,13 @@ void PairSO3LRB200::settings(int narg, char **arg) {
     error->all(FLERR, std::string("Cannot initialize SO3LR model: ") + err);
   sr_cutoff_ = info.sr_cutoff;
   lr_cutoff_ = info.lr_cutoff;
+  // one GPU per MPI rank: $SO3LR_B200_DEVICE when set, else the rank number
+  // (ranks of one node on that node's GPUs)
   const char *dev = std::getenv("SO3LR_B200_DEVICE");
-  if (so3lr_create(model_path_.c_str(), dev ? std::atoi(dev) : 0, &handle_, err, sizeof(err)) != 0)
+  const int device = dev ? std::atoi(dev) : comm->me;
+  if (so3lr_create(model_path_.c_str(), device, &handle_, err, sizeof(err)) != 0)
     error->all(FLERR, std::string("Cannot initialize SO3LR model on the GPU: ") + err);
+  comm_ready_ = false;
 }
 
 void PairSO3LRB200::coeff(int narg, char **arg) {
@@ -96,32 +102,81 @@ void PairSO3LRB200::init_style() {
   if (!handle_) error->all(FLERR, "Pair style so3lr/b200 model was not initialized");
   if (type_to_z_.size() != static_cast<std::size_t>(atom->ntypes) + 1)
     error->all(FLERR, "Pair style so3lr/b200 coefficients are missing");
-  if (comm->nprocs != 1)
-    error->all(FLERR, "Pair style so3lr/b200 runs on one MPI rank that owns every atom; use one rank per "
-                      "partition (one GPU each)");
   const bool periodic = domain->xperiodic && domain->yperiodic && domain->zperiodic;
   const bool open = !domain->xperiodic && !domain->yperiodic && !domain->zperiodic;
   if (!periodic && !open) error->all(FLERR, "Pair style so3lr/b200 needs 'p p p' or fully open boundaries");
   if (domain->triclinic) error->all(FLERR, "Pair style so3lr/b200 supports orthorhombic boxes only");
-  // charge/multiplicity against the composition (pair_so3lr_native_mpi.cpp:1196-1235)
-  long long counts[119] = {0};
-  for (int i = 0; i < atom->nlocal; ++i) counts[type_to_z_[static_cast<std::size_t>(atom->type[i])]]++;
+  // charge/multiplicity against the composition of all ranks' atoms
+  // (pair_so3lr_native_mpi.cpp:1196-1235)
+  long long local[119] = {0}, counts[119] = {0};
+  for (int i = 0; i < atom->nlocal; ++i) local[type_to_z_[static_cast<std::size_t>(atom->type[i])]]++;
+  MPI_Allreduce(local, counts, 119, MPI_LONG_LONG, MPI_SUM, world);
   char err[512] = {0};
   if (so3lr_validate_charge_spin(counts, total_charge_, multiplicity_, err, sizeof(err)) != 0)
     error->all(FLERR, std::string("SO3LR charge/multiplicity: ") + err);
+  // several ranks: one NCCL communicator over the ranks' GPUs, id from rank 0
+  if (comm->nprocs > 1 && !comm_ready_) {
+    char uid[128] = {0};
+    int rc = 0;
+    if (comm->me == 0) rc = so3lr_nccl_unique_id(uid, err, sizeof(err));
+    MPI_Bcast(&rc, 1, MPI_INT, 0, world);
+    if (rc != 0) error->all(FLERR, std::string("SO3LR: cannot create the NCCL id on rank 0: ") + err);
+    MPI_Bcast(uid, 128, MPI_BYTE, 0, world);
+    if (so3lr_comm_init(handle_, comm->nprocs, comm->me, uid, err, sizeof(err)) != 0)
+      error->all(FLERR, std::string("SO3LR: cannot join the GPUs of the other ranks: ") + err);
+    comm_ready_ = true;
+  }
 }
 
 void PairSO3LRB200::compute(int eflag, int vflag) {
   ev_init(eflag, vflag);
-  const int n = atom->nlocal;
-  x_.resize(3 * static_cast<std::size_t>(n));
-  f_.resize(3 * static_cast<std::size_t>(n));
-  eatom_.resize(static_cast<std::size_t>(n));
-  z_.resize(static_cast<std::size_t>(n));
-  for (int i = 0; i < n; ++i) {
-    for (int d = 0; d < 3; ++d) x_[3 * i + d] = atom->x[i][d];
-    z_[i] = type_to_z_[static_cast<std::size_t>(atom->type[i])];
+  const int nlocal = atom->nlocal;
+  // the whole system on every rank, ordered by atom tag: the library splits it
+  // into its own spatial bricks (one per rank and GPU) and every rank gets the
+  // whole result back
+  const int nprocs = comm->nprocs;
+  counts_.assign(nprocs, 0);
+  displs_.assign(nprocs, 0);
+  MPI_Allgather(&nlocal, 1, MPI_INT, counts_.data(), 1, MPI_INT, world);
+  long long total = 0;
+  for (int r = 0; r < nprocs; ++r) {
+    displs_[r] = static_cast<int>(total);
+    total += counts_[r];
   }
+  if (total > (1LL << 30)) error->all(FLERR, "Pair style so3lr/b200: too many atoms");
+  const int n = static_cast<int>(total);
+  loc_tag_.resize(nlocal);
+  loc_x_.resize(3 * static_cast<std::size_t>(nlocal));
+  loc_z_.resize(nlocal);
+  for (int i = 0; i < nlocal; ++i) {
+    loc_tag_[i] = static_cast<int>(atom->tag[i]);
+    for (int d = 0; d < 3; ++d) loc_x_[3 * i + d] = atom->x[i][d];
+    loc_z_[i] = type_to_z_[static_cast<std::size_t>(atom->type[i])];
+  }
+  all_tag_.resize(n);
+  all_x_.resize(3 * static_cast<std::size_t>(n));
+  all_z_.resize(n);
+  MPI_Allgatherv(loc_tag_.data(), nlocal, MPI_INT, all_tag_.data(), counts_.data(), displs_.data(), MPI_INT, world);
+  MPI_Allgatherv(loc_z_.data(), nlocal, MPI_INT, all_z_.data(), counts_.data(), displs_.data(), MPI_INT, world);
+  for (int r = 0; r < nprocs; ++r) {
+    counts3_.resize(nprocs);
+    displs3_.resize(nprocs);
+    counts3_[r] = 3 * counts_[r];
+    displs3_[r] = 3 * displs_[r];
+  }
+  MPI_Allgatherv(loc_x_.data(), 3 * nlocal, MPI_DOUBLE, all_x_.data(), counts3_.data(), displs3_.data(), MPI_DOUBLE,
+                 world);
+  // tags 1..n: gathered slot k holds atom tag all_tag_[k]
+  x_.resize(3 * static_cast<std::size_t>(n));
+  z_.resize(n);
+  for (int k = 0; k < n; ++k) {
+    const int tg = all_tag_[k];
+    if (tg < 1 || tg > n) error->all(FLERR, "Pair style so3lr/b200 needs atom tags 1..natoms");
+    for (int d = 0; d < 3; ++d) x_[3 * static_cast<std::size_t>(tg - 1) + d] = all_x_[3 * static_cast<std::size_t>(k) + d];
+    z_[tg - 1] = all_z_[k];
+  }
+  f_.resize(3 * static_cast<std::size_t>(n));
+  eatom_.resize(n);
   so3lr_frame frame{};
   frame.natoms = n;
   frame.x = x_.data();
@@ -139,12 +194,17 @@ void PairSO3LRB200::compute(int eflag, int vflag) {
   char err[2048] = {0};
   if (so3lr_compute(handle_, &frame, &res, err, sizeof(err)) != 0)
     error->all(FLERR, std::string("SO3LR evaluation failed: ") + err);
-  for (int i = 0; i < n; ++i)
-    for (int d = 0; d < 3; ++d) atom->f[i][d] += f_[3 * i + d];
+  // each rank keeps its own atoms' forces and per-atom terms; the global energy
+  // and virial (exact sums, identical on every rank) are reported by rank 0 only,
+  // so LAMMPS's sum over ranks counts them once
+  for (int i = 0; i < nlocal; ++i) {
+    const std::size_t k = static_cast<std::size_t>(loc_tag_[i] - 1);
+    for (int d = 0; d < 3; ++d) atom->f[i][d] += f_[3 * k + d];
+  }
   if (eflag_atom)
-    for (int i = 0; i < n; ++i) eatom[i] += eatom_[i];
-  if (eflag_global) eng_vdwl += res.energy;
-  if (vflag_global)
+    for (int i = 0; i < nlocal; ++i) eatom[i] += eatom_[static_cast<std::size_t>(loc_tag_[i] - 1)];
+  if (eflag_global && comm->me == 0) eng_vdwl += res.energy;
+  if (vflag_global && comm->me == 0)
     for (int k = 0; k < 6; ++k) virial[k] += res.virial[k];
   if (vflag_atom) {
     // per-atom virial (the reference refuses vflag_atom): half of every pair
@@ -152,8 +212,10 @@ void PairSO3LRB200::compute(int eflag, int vflag) {
     va_.resize(6 * static_cast<std::size_t>(n));
     if (so3lr_virial_atom(handle_, va_.data(), err, sizeof(err)) != 0)
       error->all(FLERR, std::string("SO3LR per-atom virial failed: ") + err);
-    for (int i = 0; i < n; ++i)
-      for (int k = 0; k < 6; ++k) vatom[i][k] += va_[6 * static_cast<std::size_t>(i) + k];
+    for (int i = 0; i < nlocal; ++i) {
+      const std::size_t k = static_cast<std::size_t>(loc_tag_[i] - 1);
+      for (int c = 0; c < 6; ++c) vatom[i][c] += va_[6 * k + c];
+    }
   }
   if (!reported_ && comm->me == 0) {
     reported_ = true;

@@ -9,9 +9,12 @@
 // per-atom virials (compute ... stress/atom, vflag_atom) are supported; the
 // reference refuses them (pair_so3lr_native_mpi.cpp:1248-1251). The GPU builds
 // its own short- and long-range neighbour lists from the positions, so the
-// style requests no LAMMPS list and needs no ghost atoms beyond LAMMPS's
-// own bookkeeping; it runs on one MPI rank that owns every atom (periodic
-// orthorhombic or fully open boundaries).
+// style requests no LAMMPS list and needs no ghost atoms beyond LAMMPS's own
+// bookkeeping (periodic orthorhombic or fully open boundaries). On several MPI
+// ranks (one GPU each: $SO3LR_B200_DEVICE, else the rank number) every rank
+// gathers the atoms of all ranks by tag and the library evaluates them with its
+// own spatial decomposition over the ranks' GPUs; each rank keeps its atoms'
+// forces, and rank 0 reports the global energy and virial.
 #ifdef PAIR_CLASS
 // clang-format off
 PairStyle(so3lr/b200,PairSO3LRB200);
@@ -54,7 +57,9 @@ class PairSO3LRB200 : public Pair {
   double lr_cutoff_ = 0.0;
   std::vector<int> type_to_z_;
   std::vector<int> z_;
-  std::vector<double> x_, f_, eatom_, va_;
+  std::vector<double> x_, f_, eatom_, va_, loc_x_, all_x_;
+  std::vector<int> loc_tag_, loc_z_, all_tag_, all_z_, counts_, displs_, counts3_, displs3_;
+  bool comm_ready_ = false;
   so3lr_handle *handle_ = nullptr;
   bool reported_ = false;
 

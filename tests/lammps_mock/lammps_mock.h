@@ -4,14 +4,19 @@
 // Member names and meanings follow LAMMPS; behaviour is reduced to what the
 // style uses. Error::all throws std::runtime_error with the message.
 #pragma once
+#include <mpi.h>
+
 #include <cstddef>
 #include <stdexcept>
 #include <string>
 #include <vector>
 
 #define FLERR __FILE__, __LINE__
+#define MPI_LMP_TAGINT MPI_INT
 
 namespace LAMMPS_NS {
+
+typedef int tagint;  // LAMMPS's default (smallbig) tag type
 
 class LAMMPS;
 
@@ -41,14 +46,21 @@ class Memory {
 class Atom {
  public:
   int ntypes = 0, nlocal = 0;
+  long long natoms = 0;
   std::vector<int> type_storage;
+  std::vector<tagint> tag_storage;
+  tagint *tag = nullptr;
   std::vector<double *> x_rows, f_rows;
   std::vector<double> x_data, f_data;
   int *type = nullptr;
   double **x = nullptr, **f = nullptr;
   void resize(int n) {
     nlocal = n;
+    natoms = n;
     type_storage.assign(n, 1);
+    tag_storage.resize(n);
+    for (int i = 0; i < n; ++i) tag_storage[i] = i + 1;
+    tag = tag_storage.data();
     x_data.assign(3 * static_cast<std::size_t>(n), 0.0);
     f_data.assign(3 * static_cast<std::size_t>(n), 0.0);
     x_rows.resize(n);
@@ -116,6 +128,7 @@ class Pair {
   Domain *domain;
   Force *force;
   Comm *comm;
+  MPI_Comm world = MPI_COMM_WORLD;
   int manybody_flag = 0, one_coeff = 0, restartinfo = 1, single_enable = 1, no_virial_fdotr_compute = 0;
   int allocated = 0;
   int **setflag = nullptr;

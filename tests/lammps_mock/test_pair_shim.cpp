@@ -79,9 +79,6 @@ static int parse_checks(const char *model) {
       lmp.force.newton_pair = 0;
       fails += expect_error("newton off", [&] { pair.init_style(); }, "requires newton pair on");
       lmp.force.newton_pair = 1;
-      lmp.comm.nprocs = 2;
-      fails += expect_error("several ranks", [&] { pair.init_style(); }, "one MPI rank");
-      lmp.comm.nprocs = 1;
       lmp.domain.zperiodic = 0;
       fails += expect_error("mixed boundaries", [&] { pair.init_style(); }, "'p p p'");
       lmp.domain.zperiodic = 1;
