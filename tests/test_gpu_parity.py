@@ -213,3 +213,35 @@ def test_gpu_errors_are_reported_not_raised_as_crashes(gpu_model):
         gpu_model.compute(np.zeros((3, 3)) + np.arange(9).reshape(3, 3), np.array([8, 1, 1]), multiplicity=2)
     with pytest.raises(So3lrError, match="atomic number"):
         gpu_model.compute(np.arange(6, dtype=float).reshape(2, 3), np.array([8, 120]))
+
+
+@pytest.mark.parametrize("case", ["one_atom", "far_pair", "pack_with_lone_atom"])
+def test_gpu_edge_cases_without_short_range_pairs(case, gpu_model, oracle_model):
+    """Systems with no short-range pair at all: a lone atom (doublet H), two
+    atoms 6 A apart (long-range terms only), and a turbo pack one of whose
+    images is a single atom. Every pair-sized launch is empty."""
+    from oracle.so3lr_oracle import System, evaluate
+    if case == "one_atom":
+        s = System(pos=np.array([[0.1, -0.2, 0.3]]), z=np.array([1], dtype=np.int32), multiplicity=2)
+    elif case == "far_pair":
+        s = System(pos=np.array([[0.0, 0.0, 0.0], [6.0, 0.5, -0.3]]), z=np.array([8, 8], dtype=np.int32),
+                   multiplicity=1)
+    else:
+        from so3lr_b200.systems import turbo_batch
+        pos, z, off, q, m = turbo_batch(3, seed=4)
+        pos = np.concatenate([pos, [[40.0, 40.0, 40.0]]])
+        z = np.concatenate([z, [1]]).astype(np.int32)
+        off = np.concatenate([off, [off[-1] + 1]])
+        q = np.concatenate([q, [0.0]])
+        m = np.concatenate([m, [2.0]])
+        b = gpu_model.compute_batch(pos, z, off, q, m)
+        k = len(off) - 2
+        o = evaluate(oracle_model, System(pos=pos[off[k]:], z=z[off[k]:], charge=0, multiplicity=2))
+        assert abs(b["image_energy"][k] - o["energy"]) <= 1e-9
+        assert np.abs(b["forces"][off[k]:]).max() == 0.0
+        return
+    g = _gpu(gpu_model, s)
+    o = evaluate(oracle_model, s)
+    assert abs(g["energy"] - o["energy"]) / len(s.z) <= 1e-9
+    assert np.abs(g["forces"] - o["forces"]).max() <= 1e-9
+    assert np.abs(g["e_lr"] - o["lr_energy"]).max() <= 1e-10
