@@ -1,0 +1,100 @@
+// CPU stand-in for the parts of the C ABI (include/so3lr_b200.h) the LAMMPS
+// pair styles call, for testing their data routing without a GPU. The
+// "evaluation" returns values that encode each atom's image and coordinates, so
+// a test can check that every partition got back exactly its own atoms:
+//   f[i][d]       = (k + 1) * x[i][d]          (k = image of atom i)
+//   eatom[i]      = z[i] + 1000 k
+//   image_energy  = sum of eatom over the image
+//   vatom[i][c]   = x[i][c % 3] + k
+// Element tokens and the charge/multiplicity check are the real ones' simple
+// cases (symbols H and O or numbers; electron-count parity).
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "so3lr_b200.h"
+
+struct so3lr_handle {
+  std::vector<double> va;
+};
+
+static int fake_fail(const char *msg, char *err, size_t errlen) {
+  if (err && errlen) std::snprintf(err, errlen, "%s", msg);
+  return 1;
+}
+
+extern "C" {
+
+int so3lr_inspect_model(const char *model_path, so3lr_arch_info *out, char *err, size_t errlen) {
+  if (!model_path || std::strcmp(model_path, "fake") != 0) return fake_fail("SO3LR model: cannot open it", err, errlen);
+  std::memset(out, 0, sizeof(*out));
+  out->sr_cutoff = 4.5;
+  out->lr_cutoff = 12.0;
+  return 0;
+}
+
+int so3lr_create(const char *model_path, int, so3lr_handle **out, char *err, size_t errlen) {
+  so3lr_arch_info info;
+  if (so3lr_inspect_model(model_path, &info, err, errlen) != 0) return 1;
+  *out = new so3lr_handle();
+  return 0;
+}
+
+void so3lr_destroy(so3lr_handle *h) { delete h; }
+
+int so3lr_element_from_token(const char *token) {
+  if (!token) return 0;
+  if (std::strcmp(token, "H") == 0) return 1;
+  if (std::strcmp(token, "O") == 0) return 8;
+  const int z = std::atoi(token);
+  return z >= 1 && z <= 99 ? z : 0;
+}
+
+int so3lr_validate_charge_spin(const long long counts[119], double total_charge, double multiplicity, char *err,
+                               size_t errlen) {
+  long long electrons = 0;
+  for (int z = 1; z < 119; ++z) electrons += z * counts[z];
+  const long long e = electrons - std::llround(total_charge);
+  const long long unpaired = std::llround(multiplicity) - 1;
+  if (e < 0 || unpaired < 0 || (e - unpaired) % 2 != 0) return fake_fail("cannot have multiplicity", err, errlen);
+  return 0;
+}
+
+int so3lr_compute_batch(so3lr_handle *h, const so3lr_batch *in, so3lr_batch_result *out, char *err, size_t errlen) {
+  if (!h || in->nimages <= 0 || in->image_offsets[0] != 0 || in->image_offsets[in->nimages] != in->natoms)
+    return fake_fail("SO3LR batch: bad images", err, errlen);
+  h->va.assign(6 * static_cast<std::size_t>(in->natoms), 0.0);
+  for (int k = 0; k < in->nimages; ++k) {
+    if (in->image_offsets[k + 1] <= in->image_offsets[k])
+      return fake_fail("SO3LR: every image needs at least one atom", err, errlen);
+    double e = 0.0;
+    for (long long i = in->image_offsets[k]; i < in->image_offsets[k + 1]; ++i) {
+      for (int d = 0; d < 3; ++d) out->f[3 * i + d] = (k + 1) * in->x[3 * i + d];
+      const double ea = in->z[i] + 1000.0 * k;
+      if (out->eatom) out->eatom[i] = ea;
+      if (out->charges) out->charges[i] = 0.0;
+      e += ea;
+      for (int c = 0; c < 6; ++c) h->va[6 * i + c] = in->x[3 * i + c % 3] + k;
+    }
+    if (out->image_energy) out->image_energy[k] = e;
+  }
+  return 0;
+}
+
+int so3lr_virial_atom(so3lr_handle *h, double *vatom, char *, size_t) {
+  std::memcpy(vatom, h->va.data(), h->va.size() * sizeof(double));
+  return 0;
+}
+
+// the so3lr/b200 style's calls, not used by the turbo tests
+int so3lr_compute(so3lr_handle *, const so3lr_frame *, so3lr_result *, char *err, size_t errlen) {
+  return fake_fail("not in the CPU stand-in", err, errlen);
+}
+int so3lr_nccl_unique_id(char *, char *err, size_t errlen) { return fake_fail("not in the CPU stand-in", err, errlen); }
+int so3lr_comm_init(so3lr_handle *, int, int, const char *, char *err, size_t errlen) {
+  return fake_fail("not in the CPU stand-in", err, errlen);
+}
+
+}  // extern "C"

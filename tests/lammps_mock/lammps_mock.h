@@ -23,6 +23,8 @@ class LAMMPS;
 class Error {
  public:
   [[noreturn]] void all(const char *, int, const std::string &msg) { throw std::runtime_error(msg); }
+  [[noreturn]] void universe_all(const char *, int, const std::string &msg) { throw std::runtime_error(msg); }
+  [[noreturn]] void universe_one(const char *, int, const std::string &msg) { throw std::runtime_error(msg); }
 };
 
 class Memory {
@@ -45,7 +47,7 @@ class Memory {
 
 class Atom {
  public:
-  int ntypes = 0, nlocal = 0;
+  int ntypes = 0, nlocal = 0, nghost = 0;
   long long natoms = 0;
   std::vector<int> type_storage;
   std::vector<tagint> tag_storage;
@@ -91,8 +93,17 @@ class Comm {
   int me = 0, nprocs = 1;
 };
 
+// LAMMPS partitions: `nworlds` worlds, this process is rank `me` of the
+// universe communicator `uworld` and belongs to world `iworld`
+class Universe {
+ public:
+  int me = 0, nprocs = 1, nworlds = 1, iworld = 0;
+  MPI_Comm uworld = MPI_COMM_WORLD;
+};
+
 class LAMMPS {
  public:
+  Universe universe;
   Error error;
   Memory memory;
   Atom atom;
@@ -110,7 +121,7 @@ class Pair {
  public:
   explicit Pair(LAMMPS *l)
       : lmp(l), error(&l->error), memory(&l->memory), atom(&l->atom), domain(&l->domain), force(&l->force),
-        comm(&l->comm) {}
+        comm(&l->comm), universe(&l->universe) {}
   virtual ~Pair() {
     delete[] eatom;
     release_vatom();
@@ -128,6 +139,7 @@ class Pair {
   Domain *domain;
   Force *force;
   Comm *comm;
+  Universe *universe;
   MPI_Comm world = MPI_COMM_WORLD;
   int manybody_flag = 0, one_coeff = 0, restartinfo = 1, single_enable = 1, no_virial_fdotr_compute = 0;
   int allocated = 0;
@@ -136,14 +148,21 @@ class Pair {
   double eng_vdwl = 0.0, virial[6] = {0, 0, 0, 0, 0, 0};
   double *eatom = nullptr;
   double **vatom = nullptr;  // [nlocal][6], LAMMPS order xx yy zz xy xz yz
-  int eflag_global = 0, eflag_atom = 0, vflag_global = 0, vflag_atom = 0;
+  int eflag_global = 0, eflag_atom = 0, vflag_global = 0, vflag_atom = 0, vflag_fdotr = 0;
 
   // LAMMPS semantics: eflag bit 1 = global energy, bit 2 = per-atom energy;
-  // vflag bit 1/2 = global virial, bit 4/8 = per-atom virial
+  // vflag bit 1 = global virial summed by the style, bit 2 = global virial from
+  // F dot r (virial_fdotr_compute) when the style allows it, bit 4/8 = per-atom
+  // virial
   void ev_init(int eflag, int vflag) {
     eflag_global = eflag & 1;
     eflag_atom = (eflag & 2) ? 1 : 0;
     vflag_global = (vflag & 3) ? 1 : 0;
+    vflag_fdotr = 0;
+    if ((vflag & 3) == 2 && !no_virial_fdotr_compute) {
+      vflag_fdotr = 1;
+      vflag_global = 0;
+    }
     vflag_atom = (vflag & 12) ? 1 : 0;
     eng_vdwl = 0.0;
     for (double &v : virial) v = 0.0;
@@ -156,6 +175,20 @@ class Pair {
       vatom = new double *[atom->nlocal];
       double *rows = new double[6 * static_cast<std::size_t>(atom->nlocal)]();
       for (int i = 0; i < atom->nlocal; ++i) vatom[i] = rows + 6 * static_cast<std::size_t>(i);
+    }
+  }
+
+  // global virial as the sum over owned and ghost atoms of x (x) f
+  void virial_fdotr_compute() {
+    const int nall = atom->nlocal + atom->nghost;
+    for (int i = 0; i < nall; ++i) {
+      const double *x = atom->x[i], *f = atom->f[i];
+      virial[0] += f[0] * x[0];
+      virial[1] += f[1] * x[1];
+      virial[2] += f[2] * x[2];
+      virial[3] += f[1] * x[0];
+      virial[4] += f[2] * x[0];
+      virial[5] += f[2] * x[1];
     }
   }
 

@@ -1,15 +1,26 @@
-// Drives the so3lr/b200 pair style through the mock LAMMPS API.
+// Drives the so3lr/b200 and so3lr/b200/turbo pair styles through the mock LAMMPS API.
 //   test_pair_shim parse MODEL          pair_style/pair_coeff parsing and refusals
 //   test_pair_shim run MODEL INPUT      one compute; INPUT holds "L n" then n lines "type x y z"
 //                                       (types 1 = O, 2 = H); prints JSON with energy, virial, forces
+//   test_pair_shim turbo-parse MODEL    so3lr/b200/turbo parsing and refusals on one rank, and a
+//                                       coordinator failure reaching every partition of a universe
+//   test_pair_shim turbo-run MODEL INPUT
+//                                       one image per partition, partitions run as threads of a
+//                                       universe; INPUT holds "K" then per image "n charge mult" and
+//                                       n lines "type x y z"; prints one JSON line per image
+//   test_pair_shim turbo-refuse MODEL INPUT
+//                                       the same universe with image 1 periodic and image 2 given
+//                                       an impossible multiplicity: every partition must stop
 #include <cstdio>
 #include <cstring>
 #include <fstream>
 #include <functional>
+#include <sstream>
 #include <string>
 #include <vector>
 
 #include "pair_so3lr_b200.h"
+#include "pair_so3lr_b200_turbo.h"
 
 using namespace LAMMPS_NS;
 
@@ -134,9 +145,225 @@ static int run(const char *model, const char *input) {
   return 0;
 }
 
+static int turbo_parse_checks(const char *model) {
+  int fails = 0;
+  {
+    LAMMPS lmp;
+    lmp.atom.ntypes = 2;
+    lmp.atom.resize(3);
+    lmp.domain.xperiodic = lmp.domain.yperiodic = lmp.domain.zperiodic = 0;
+    PairSO3LRB200Turbo pair(&lmp);
+    char *many[] = {(char *)"a", (char *)"b", (char *)"c", (char *)"d"};
+    fails += expect_error("turbo: too many pair_style args", [&] { pair.settings(4, many); },
+                          "Illegal pair_style so3lr/b200/turbo");
+    char *missing[] = {(char *)"/nonexistent/model.so3lr"};
+    fails += expect_error("turbo: missing model", [&] { pair.settings(1, missing); }, "cannot open");
+    char *bad[] = {(char *)"*", (char *)"*", (char *)"O", (char *)"Qq"};
+    fails += expect_error("turbo: unknown element", [&] { pair.coeff(4, bad); }, "Unknown SO3LR element");
+    char *good[] = {(char *)"*", (char *)"*", (char *)"O", (char *)"H"};
+    pair.coeff(4, good);
+    if (pair.type_atomic_number(1) != 8 || pair.type_atomic_number(2) != 1) {
+      std::printf("FAIL turbo element map\n");
+      ++fails;
+    }
+    // a universe of one partition is refused (the reference needs at least two images)
+    char *args[] = {(char *)model};
+    bool gpu_ok = true;
+    try {
+      pair.settings(1, args);
+    } catch (const std::runtime_error &e) {
+      gpu_ok = false;
+      if (!std::strstr(e.what(), "coordinator SO3LR model on the GPU")) {
+        std::printf("FAIL turbo settings with a valid model: %s\n", e.what());
+        ++fails;
+      }
+    }
+    if (gpu_ok) {
+      if (pair.long_range_cutoff() != 12.0 || pair.init_one(1, 2) != 12.0) {
+        std::printf("FAIL turbo cutoffs\n");
+        ++fails;
+      }
+      fails += expect_error("turbo: one partition", [&] { pair.init_style(); }, "multiple one-rank partitions");
+    }
+  }
+  // two partitions: the coordinator's failure to load a model reaches both
+  std::vector<std::string> msgs(2);
+  auto errs = mpi_stub_run(2, [&](int r) {
+    LAMMPS lmp;
+    lmp.universe.me = r;
+    lmp.universe.nprocs = lmp.universe.nworlds = 2;
+    lmp.universe.iworld = r;
+    lmp.atom.ntypes = 2;
+    lmp.atom.resize(3);
+    PairSO3LRB200Turbo pair(&lmp);
+    pair.world = MPI_COMM_SELF;
+    char *missing[] = {(char *)"/nonexistent/model.so3lr"};
+    pair.settings(1, missing);
+  });
+  for (int r = 0; r < 2; ++r) {
+    std::string what = "no error";
+    if (errs[r]) {
+      try {
+        std::rethrow_exception(errs[r]);
+      } catch (const std::runtime_error &e) {
+        what = e.what();
+      }
+    }
+    if (what.find("Cannot initialize the coordinator SO3LR model: ") == std::string::npos) {
+      std::printf("FAIL turbo coordinator failure on partition %d: %s\n", r, what.c_str());
+      ++fails;
+    }
+  }
+  std::printf("%s\n", fails ? "TURBO PARSE FAIL" : "TURBO PARSE OK");
+  return fails ? 1 : 0;
+}
+
+struct TurboImage {
+  int n = 0;
+  double charge = 0.0, mult = 1.0;
+  std::vector<int> type;
+  std::vector<double> x;
+};
+
+static std::vector<TurboImage> read_images(const char *input) {
+  std::ifstream in(input);
+  int k = 0;
+  in >> k;
+  std::vector<TurboImage> images(k);
+  for (TurboImage &im : images) {
+    in >> im.n >> im.charge >> im.mult;
+    im.type.resize(im.n);
+    im.x.resize(3 * static_cast<std::size_t>(im.n));
+    for (int i = 0; i < im.n; ++i) in >> im.type[i] >> im.x[3 * i] >> im.x[3 * i + 1] >> im.x[3 * i + 2];
+  }
+  return images;
+}
+
+// one partition of the turbo universe: rank r holds image r
+static void setup_partition(LAMMPS &lmp, const TurboImage &im, int r, int nimg) {
+  lmp.universe.me = r;
+  lmp.universe.nprocs = lmp.universe.nworlds = nimg;
+  lmp.universe.iworld = r;
+  lmp.atom.ntypes = 2;
+  lmp.atom.resize(im.n);
+  for (int i = 0; i < im.n; ++i) {
+    lmp.atom.type[i] = im.type[i];
+    for (int d = 0; d < 3; ++d) lmp.atom.x[i][d] = im.x[3 * static_cast<std::size_t>(i) + d];
+  }
+  lmp.domain.xperiodic = lmp.domain.yperiodic = lmp.domain.zperiodic = 0;
+}
+
+static int turbo_run(const char *model, const char *input) {
+  const std::vector<TurboImage> images = read_images(input);
+  const int nimg = static_cast<int>(images.size());
+  std::vector<std::string> out(nimg);
+  auto errs = mpi_stub_run(nimg, [&](int r) {
+    const TurboImage &im = images[r];
+    LAMMPS lmp;
+    setup_partition(lmp, im, r, nimg);
+    PairSO3LRB200Turbo pair(&lmp);
+    pair.world = MPI_COMM_SELF;
+    std::string q = std::to_string(im.charge), m = std::to_string(im.mult);
+    char *sargs[] = {(char *)model, (char *)q.c_str(), (char *)m.c_str()};
+    pair.settings(3, sargs);
+    char *cargs[] = {(char *)"*", (char *)"*", (char *)"O", (char *)"H"};
+    pair.coeff(4, cargs);
+    pair.init_style();
+    // first step: every image wants F dot r and per-atom virials
+    pair.compute(1 | 2, 2 | 4);
+    std::ostringstream s;
+    s.precision(17);
+    double esum = 0.0;
+    for (int i = 0; i < im.n; ++i) esum += pair.eatom[i];
+    s << "{\"image\": " << r << ", \"energy\": " << pair.eng_vdwl << ", \"eatom_sum\": " << esum
+      << ", \"virial\": [";
+    for (int k = 0; k < 6; ++k) s << (k ? ", " : "") << pair.virial[k];
+    s << "], \"forces\": [";
+    for (int i = 0; i < im.n; ++i)
+      s << (i ? ", [" : "[") << lmp.atom.f[i][0] << ", " << lmp.atom.f[i][1] << ", " << lmp.atom.f[i][2] << "]";
+    s << "], \"vatom\": [";
+    for (int i = 0; i < im.n; ++i) {
+      s << (i ? ", [" : "[");
+      for (int k = 0; k < 6; ++k) s << (k ? ", " : "") << pair.vatom[i][k];
+      s << "]";
+    }
+    // second step: only image 0 wants per-atom virials; results must repeat
+    const std::vector<double> f1 = lmp.atom.f_data;
+    const double e1 = pair.eng_vdwl;
+    std::fill(lmp.atom.f_data.begin(), lmp.atom.f_data.end(), 0.0);
+    pair.compute(1, r == 0 ? (2 | 4) : 2);
+    const bool repeat = lmp.atom.f_data == f1 && pair.eng_vdwl == e1;
+    std::string log = lmp.log;
+    for (char &c : log)
+      if (c == '\n') c = '|';
+    s << "], \"repeat_equal\": " << (repeat ? "true" : "false") << ", \"evaluations\": " << pair.evaluations()
+      << ", \"log\": \"" << log << "\"}";
+    out[r] = s.str();
+  });
+  int rc = 0;
+  for (int r = 0; r < nimg; ++r) {
+    if (errs[r]) {
+      try {
+        std::rethrow_exception(errs[r]);
+      } catch (const std::exception &e) {
+        std::printf("ERROR image %d: %s\n", r, e.what());
+      }
+      rc = 1;
+    } else {
+      std::printf("%s\n", out[r].c_str());
+    }
+  }
+  return rc;
+}
+
+static int turbo_refuse(const char *model, const char *input) {
+  const std::vector<TurboImage> images = read_images(input);
+  const int nimg = static_cast<int>(images.size());
+  auto errs = mpi_stub_run(nimg, [&](int r) {
+    const TurboImage &im = images[r];
+    LAMMPS lmp;
+    setup_partition(lmp, im, r, nimg);
+    if (r == 1) lmp.domain.xperiodic = lmp.domain.yperiodic = lmp.domain.zperiodic = 1;
+    PairSO3LRB200Turbo pair(&lmp);
+    pair.world = MPI_COMM_SELF;
+    // image 2: an even electron count cannot be a doublet
+    std::string q = std::to_string(im.charge), m = r == 2 ? "2" : std::to_string(im.mult);
+    char *sargs[] = {(char *)model, (char *)q.c_str(), (char *)m.c_str()};
+    pair.settings(3, sargs);
+    char *cargs[] = {(char *)"*", (char *)"*", (char *)"O", (char *)"H"};
+    pair.coeff(4, cargs);
+    pair.init_style();
+    pair.compute(1, 0);
+  });
+  const char *expect[3] = {"another partition refused", "requires non-periodic boundaries",
+                           "so3lr/b200/turbo image 2: charge"};
+  int fails = 0;
+  for (int r = 0; r < nimg; ++r) {
+    std::string what = "no error";
+    if (errs[r]) {
+      try {
+        std::rethrow_exception(errs[r]);
+      } catch (const std::exception &e) {
+        what = e.what();
+      }
+    }
+    const char *want = expect[r < 3 ? r : 0];
+    if (what.find(want) == std::string::npos) {
+      std::printf("FAIL partition %d: expected '%s', got '%s'\n", r, want, what.c_str());
+      ++fails;
+    }
+  }
+  std::printf("%s\n", fails ? "TURBO REFUSE FAIL" : "TURBO REFUSE OK");
+  return fails ? 1 : 0;
+}
+
 int main(int argc, char **argv) {
   if (argc >= 3 && std::string(argv[1]) == "parse") return parse_checks(argv[2]);
   if (argc >= 4 && std::string(argv[1]) == "run") return run(argv[2], argv[3]);
-  std::printf("usage: test_pair_shim parse MODEL | run MODEL INPUT\n");
+  if (argc >= 3 && std::string(argv[1]) == "turbo-parse") return turbo_parse_checks(argv[2]);
+  if (argc >= 4 && std::string(argv[1]) == "turbo-run") return turbo_run(argv[2], argv[3]);
+  if (argc >= 4 && std::string(argv[1]) == "turbo-refuse") return turbo_refuse(argv[2], argv[3]);
+  std::printf("usage: test_pair_shim parse MODEL | run MODEL INPUT | turbo-parse MODEL | turbo-run MODEL INPUT | "
+              "turbo-refuse MODEL INPUT\n");
   return 2;
 }

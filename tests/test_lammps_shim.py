@@ -1,8 +1,12 @@
-"""The LAMMPS pair style so3lr/b200 (so3lr_b200/lammps/) compiled against a
-minimal mock of the LAMMPS Pair API (tests/lammps_mock/): pair_style and
-pair_coeff parsing and refusals mirror the reference style
-(plugins/lammps/pair_so3lr_native_mpi.cpp:1097-1192); on a GPU one compute()
-must return what the C ABI returns for the same atoms.
+"""The LAMMPS pair styles so3lr/b200 and so3lr/b200/turbo (so3lr_b200/lammps/)
+compiled against a minimal mock of the LAMMPS Pair API (tests/lammps_mock/):
+pair_style and pair_coeff parsing and refusals mirror the reference styles
+(plugins/lammps/pair_so3lr_native_mpi.cpp:1097-1192,
+pair_so3lr_turbo.cpp:110-223); on a GPU one compute() must return what the C
+ABI returns for the same atoms. The turbo style's partitions run as threads
+acting as the ranks of a LAMMPS universe (tests/lammps_mock/mpi.h); on the CPU a
+stand-in of the C ABI (tests/lammps_mock/fake_so3lr_b200.cpp) checks that every
+partition gets back exactly its own image.
 """
 import json
 import pathlib
@@ -15,21 +19,45 @@ import pytest
 from conftest import MODEL, ROOT
 
 
-def _build(tmp_path: pathlib.Path) -> pathlib.Path:
+def _build(tmp_path: pathlib.Path, fake: bool = False) -> pathlib.Path:
     gxx = shutil.which("g++")
     if gxx is None:
         pytest.skip("g++ not available")
     from so3lr_b200.runtime import LIB_PATH
-    if not LIB_PATH.exists():
+    if not fake and not LIB_PATH.exists():
         pytest.skip("library not built")
-    exe = tmp_path / "test_pair_shim"
-    cmd = [gxx, "-std=c++17", "-O1", "-I", str(ROOT / "tests" / "lammps_mock"), "-I",
-           str(ROOT / "so3lr_b200" / "lammps"), "-I", str(ROOT / "include"),
-           str(ROOT / "so3lr_b200" / "lammps" / "pair_so3lr_b200.cpp"),
-           str(ROOT / "tests" / "lammps_mock" / "test_pair_shim.cpp"), "-L", str(LIB_PATH.parent),
-           "-lso3lr_b200", f"-Wl,-rpath,{LIB_PATH.parent}", "-o", str(exe)]
-    subprocess.run(cmd, check=True, capture_output=True, text=True)
+    mock = ROOT / "tests" / "lammps_mock"
+    shim = ROOT / "so3lr_b200" / "lammps"
+    exe = tmp_path / ("test_pair_fake" if fake else "test_pair_shim")
+    cmd = [gxx, "-std=c++17", "-O1", "-pthread", "-I", str(mock), "-I", str(shim), "-I", str(ROOT / "include"),
+           str(shim / "pair_so3lr_b200.cpp"), str(shim / "pair_so3lr_b200_turbo.cpp"), str(mock / "test_pair_shim.cpp")]
+    if fake:
+        cmd += [str(mock / "fake_so3lr_b200.cpp")]
+    else:
+        cmd += ["-L", str(LIB_PATH.parent), "-lso3lr_b200", f"-Wl,-rpath,{LIB_PATH.parent}"]
+    subprocess.run(cmd + ["-o", str(exe)], check=True, capture_output=True, text=True)
     return exe
+
+
+def _write_images(path: pathlib.Path, pos, z, off, q, m) -> None:
+    lines = [str(len(off) - 1)]
+    for k in range(len(off) - 1):
+        lines.append(f"{int(off[k + 1] - off[k])} {float(q[k])!r} {float(m[k])!r}")
+        for i in range(off[k], off[k + 1]):
+            lines.append(f"{1 if z[i] == 8 else 2} {float(pos[i, 0])!r} {float(pos[i, 1])!r} {float(pos[i, 2])!r}")
+    path.write_text("\n".join(lines) + "\n")
+
+
+def _run_images(exe, model, inp):
+    res = subprocess.run([str(exe), "turbo-run", str(model), str(inp)], capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stdout + res.stderr
+    return [json.loads(line) for line in res.stdout.strip().splitlines()]
+
+
+def _fdotr(x, f):
+    """LAMMPS's virial_fdotr_compute: sum over atoms of x (x) f, order xx yy zz xy xz yz."""
+    return np.array([(f[:, 0] * x[:, 0]).sum(), (f[:, 1] * x[:, 1]).sum(), (f[:, 2] * x[:, 2]).sum(),
+                     (f[:, 1] * x[:, 0]).sum(), (f[:, 2] * x[:, 0]).sum(), (f[:, 2] * x[:, 1]).sum()])
 
 
 def test_pair_style_parsing_and_refusals(tmp_path):
@@ -37,6 +65,48 @@ def test_pair_style_parsing_and_refusals(tmp_path):
     res = subprocess.run([str(exe), "parse", str(MODEL)], capture_output=True, text=True, timeout=300)
     assert "PARSE OK" in res.stdout, res.stdout + res.stderr
     assert res.returncode == 0
+    res = subprocess.run([str(exe), "turbo-parse", str(MODEL)], capture_output=True, text=True, timeout=300)
+    assert "TURBO PARSE OK" in res.stdout, res.stdout + res.stderr
+    assert res.returncode == 0
+
+
+def test_turbo_routes_each_image_back_to_its_partition(tmp_path):
+    """Four partitions of different sizes and charges: the coordinator packs
+    them, and each partition gets back its own forces, per-atom energies and
+    virials, its image energy, and the F dot r virial of its atoms; a second
+    step where only image 0 asks for per-atom virials repeats the first."""
+    from so3lr_b200.systems import turbo_batch
+    exe = _build(tmp_path, fake=True)
+    pos, z, off, q, m = turbo_batch(4, seed=7)
+    inp = tmp_path / "images.txt"
+    _write_images(inp, pos, z, off, q, m)
+    out = _run_images(exe, "fake", inp)
+    assert len(out) == 4
+    for k, o in enumerate(out):
+        sl = slice(off[k], off[k + 1])
+        x = pos[sl]
+        f = np.array(o["forces"])
+        assert o["image"] == k
+        assert np.array_equal(f, (k + 1) * x)
+        assert o["energy"] == float((z[sl] + 1000 * k).sum())
+        assert o["eatom_sum"] == o["energy"]
+        assert np.array_equal(np.array(o["vatom"]), x[:, [0, 1, 2, 0, 1, 2]] + k)
+        assert np.allclose(o["virial"], _fdotr(x, f), rtol=1e-14, atol=0)
+        assert o["repeat_equal"] and o["evaluations"] == 2
+        assert f"SO3LR_TURBO_LIVE image={k} universe_rank={k} coordinator={int(k == 0)} images=4" in o["log"]
+        assert f"SO3LR turbo image {k}: total charge {q[k]:g}" in o["log"]
+
+
+def test_turbo_refusal_on_one_partition_stops_all(tmp_path):
+    """A periodic image and an impossible multiplicity on two partitions: each
+    reports its own problem and the others stop too, instead of waiting."""
+    from so3lr_b200.systems import turbo_batch
+    exe = _build(tmp_path, fake=True)
+    pos, z, off, q, m = turbo_batch(3, seed=7)
+    inp = tmp_path / "images.txt"
+    _write_images(inp, pos, z, off, q, m)
+    res = subprocess.run([str(exe), "turbo-refuse", "fake", str(inp)], capture_output=True, text=True, timeout=300)
+    assert "TURBO REFUSE OK" in res.stdout, res.stdout + res.stderr
 
 
 @pytest.mark.gpu
@@ -60,3 +130,32 @@ def test_pair_style_compute_matches_c_abi(tmp_path, gpu_model):
     assert np.allclose(out["virial"], ref["virial"], rtol=0, atol=1e-12)
     assert abs(out["eatom_sum"] - ref["energy"]) < 1e-8
     assert "SO3LR_B200_FORCE_PATH=PASS" in out["log"]
+
+
+@pytest.mark.gpu
+def test_turbo_pair_style_matches_c_abi(tmp_path, gpu_model):
+    """so3lr/b200/turbo over five partitions returns, per image, what
+    so3lr_compute_batch returns for the same pack (bit for bit), per-atom
+    virials equal to so3lr_virial_atom, and an F dot r virial equal to the
+    image's own pair virial (so3lr_compute on the lone image); refusals on one
+    partition stop all of them."""
+    from so3lr_b200.systems import turbo_batch
+    exe = _build(tmp_path)
+    pos, z, off, q, m = turbo_batch(5, seed=11)
+    inp = tmp_path / "images.txt"
+    _write_images(inp, pos, z, off, q, m)
+    out = _run_images(exe, MODEL, inp)
+    ref = gpu_model.compute_batch(pos, z, off, q, m)
+    ref_va = gpu_model.virial_atom(len(z))
+    for k, o in enumerate(out):
+        sl = slice(off[k], off[k + 1])
+        assert np.array_equal(np.array(o["forces"]), ref["forces"][sl])
+        assert o["energy"] == ref["image_energy"][k]
+        assert abs(o["eatom_sum"] - ref["image_energy"][k]) <= 1e-9
+        assert np.array_equal(np.array(o["vatom"]), ref_va[sl])
+        assert o["repeat_equal"] and o["evaluations"] == 2
+        single = gpu_model.compute(pos[sl], z[sl], charge=q[k], multiplicity=m[k])
+        assert np.allclose(o["virial"], single["virial"], rtol=0, atol=1e-8)
+    res = subprocess.run([str(exe), "turbo-refuse", str(MODEL), str(inp)], capture_output=True, text=True,
+                         timeout=600)
+    assert "TURBO REFUSE OK" in res.stdout, res.stdout + res.stderr
