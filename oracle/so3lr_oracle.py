@@ -19,7 +19,13 @@ CPradaL/so3lrxlammps 0.4.0 (paths relative to source/so3lr-lammps-native/):
   degree gate, LayerNorm): src/kokkos_post_attention_block0.cpp:97-300;
 * output heads and charge conservation: src/kokkos_output_heads.cpp:137-176, 341-451;
 * long-range Coulomb + dispersion: src/kokkos_physical_long_range.cpp:11-380;
-* learned ZBL repulsion: src/kokkos_physical_zbl.cpp:81-178;
+* learned ZBL repulsion and the NLH pair-table repulsion: src/kokkos_physical_zbl.cpp:81-178,
+  src/so3lr_repulsion_setup.cpp:9-55;
+* optional block operators of other checkpoints: RMSNorm without scale in either
+  norm position and no second norm (src/kokkos_post_attention_block0.cpp:124-162,
+  src/so3lr_architecture.cpp:383-389), query/key RMS normalisation per head
+  (src/kokkos_integrated_block0.cpp:288-328), residual scalars before every block
+  (src/kokkos_local_energy_reverse.cpp:121-170);
 * virial: plugins/lammps/pair_so3lr_native_mpi.cpp:944-990.
 
 The reverse pass is not restated line by line: the reference's hand-written
@@ -137,6 +143,12 @@ class OracleModel:
     degree_repeats: list
     degree_offsets: list
     deg_of_channel: torch.Tensor
+    norm1: str = "layer"          # "layer" (affine LayerNorm) or "rms" (RMSNorm, no scale)
+    norm2: str = "layer"          # "layer", "rms" or "identity"
+    qk_norm: bool = False
+    resid: list | None = None     # residual scalars per block, or None
+    x0_scale: list | None = None
+    repulsion: str = "zbl_learned"  # or "nlh"
 
     @staticmethod
     def load(path: str) -> "OracleModel":
@@ -146,13 +158,24 @@ class OracleModel:
         reps = [int(x) for x in f.t("model.euclidean_transformers.0.euclidean_attention_block.degree_repeats")]
         offs = list(np.cumsum([0] + reps[:-1]))
         deg = torch.tensor(sum(([d] * r for d, r in enumerate(reps)), []), dtype=torch.long)
+        # block norms (so3lr_architecture.cpp:369-389): one module choice for
+        # both positions, each position switchable
+        kind = "rms" if a.get("use_rms_norm", False) else "layer"
+        norm1 = kind if a.get("layer_normalization_1", True) else "identity"
+        norm2 = kind if a.get("layer_normalization_2", True) else "identity"
+        resid = x0s = None
+        if a.get("use_residual_scalars", False):
+            resid = [float(v) for v in f.t("model.resid_lambdas")]
+            x0s = [float(v) for v in f.t("model.x0_lambdas")]
         return OracleModel(
             file=f, p=p, layers=int(a["interaction_blocks"]),
             norm=float(a["avg_num_neighbors"]),
             r_sr=float(a["short_range_cutoff_angstrom"]),
             r_lr=float(a["long_range_cutoff_angstrom"]),
-            gamma=float(f.t("model.radial_embedding.radial_basis_fn.gamma")),
-            degree_repeats=reps, degree_offsets=[int(o) for o in offs], deg_of_channel=deg)
+            gamma=float(np.asarray(f.t("model.radial_embedding.radial_basis_fn.gamma")).reshape(-1)[0]),
+            degree_repeats=reps, degree_offsets=[int(o) for o in offs], deg_of_channel=deg,
+            norm1=norm1, norm2=norm2, qk_norm=bool(a.get("qk_norm", False)), resid=resid, x0_scale=x0s,
+            repulsion=str(a.get("repulsion_type", "zbl_learned")))
 
 
 # ---------------------------------------------------------------------------
@@ -207,6 +230,20 @@ def layer_norm(x, w, b, eps):
     mean = x.mean(dim=1, keepdim=True)
     var = ((x - mean) ** 2).mean(dim=1, keepdim=True)
     return (x - mean) * (1.0 / torch.sqrt(var + eps)) * w + b
+
+
+def rms_norm(x, eps):
+    """RMSNorm without scale, over the last axis: x / sqrt(mean(x^2) + eps)
+    (post_attention_block0.cpp:124-146; integrated_block0.cpp:295-313)."""
+    return x * (1.0 / torch.sqrt((x * x).mean(dim=-1, keepdim=True) + eps))
+
+
+def block_norm(kind, x, p, key, eps):
+    if kind == "layer":
+        return layer_norm(x, p[key + ".weight"], p[key + ".bias"], eps)
+    if kind == "rms":
+        return rms_norm(x, eps)
+    return x
 
 
 def smooth_switch(r, cuton, cutoff):
@@ -301,6 +338,7 @@ def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -
         tab = torch.from_numpy(_tables_for(m, znp[sel], charges[im], mults[im]))
         offset[torch.as_tensor(np.nonzero(sel)[0])] = tab[zi[torch.as_tensor(sel)]]
     x = x + offset * inv_scale
+    x_emb = x
     F = x.shape[1]
     E = len(m.deg_of_channel)
     ev = torch.zeros(n, E, dtype=DT)
@@ -317,6 +355,8 @@ def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -
 
     for b in range(m.layers):
         pre = f"model.euclidean_transformers.{b}."
+        if m.resid is not None:  # x = resid[b] x + x0[b] x0 (local_energy_reverse.cpp:145-157)
+            x = m.resid[b] * x + m.x0_scale[b] * x_emb
         att = pre + "euclidean_attention_block."
         cg_a = p[att + "so3_conv_invariants.cg_rep"]
         diff = ev[sr_s] - ev[sr_r]
@@ -338,6 +378,8 @@ def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -
         v = torch.einsum("nhi,hio->nho", xh, p[att + "W_v_inv"])
         qe = torch.einsum("nhi,hio->nho", xh, p[att + "W_q_ev"])
         ke = torch.einsum("nhi,hio->nho", xh, p[att + "W_k_ev"])
+        if m.qk_norm:  # per (atom, head) over the head channels, eps 1e-6
+            q, k, qe, ke = (rms_norm(t_, 1.0e-6) for t_ in (q, k, qe, ke))
         a_inv = (q[sr_r] * k[sr_s] * f_inv).sum(dim=2) / m.norm
         a_ev = (qe[sr_r] * ke[sr_s] * f_ev).sum(dim=2) / m.norm
         msg = cut[:, None, None] * a_inv[:, :, None] * v[sr_s]
@@ -349,7 +391,7 @@ def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -
         eps = float(m.file.arch["layer_norm_epsilon"])
         a = x + d_inv
         A = ev + d_ev
-        n1 = layer_norm(a, p[pre + "layer_norm_inv_1.weight"], p[pre + "layer_norm_inv_1.bias"], eps)
+        n1 = block_norm(m.norm1, a, p, pre + "layer_norm_inv_1", eps)
         hid = _silu(torch.nn.functional.linear(_silu(n1), p[pre + "mlp_1.1.weight"]) + p[pre + "mlp_1.1.bias"])
         mlp = torch.nn.functional.linear(hid, p[pre + "mlp_1.3.weight"]) + p[pre + "mlp_1.3.bias"]
         post = n1 + mlp
@@ -357,7 +399,7 @@ def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -
         l0n = torch.zeros(n, heads, dtype=DT).index_add(1, deg, A * A * cg_i[None, :])
         t = torch.nn.functional.linear(torch.cat([post, l0n], dim=1),
                                        p[pre + "interaction_block.linear_layer.weight"]) + p[pre + "interaction_block.linear_layer.bias"]
-        x = layer_norm(post + t[:, :F], p[pre + "layer_norm_inv_2.weight"], p[pre + "layer_norm_inv_2.bias"], eps)
+        x = block_norm(m.norm2, post + t[:, :F], p, pre + "layer_norm_inv_2", eps)
         ev = A * (1.0 + t[:, F + deg])
 
     # --- heads (output_heads.cpp:137-176, 341-451) -----------------------------
@@ -395,11 +437,25 @@ def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -
     switching = sl / (sl + srr + 1.0e-12)
     safe_r = torch.clamp(r, min=1.0e-6)
     xz = float(a["zbl_ke"]) * zcut * zz / safe_r
-    rate = (z[sr_r].to(DT) ** float(a["zbl_p"]) + z[sr_s].to(DT) ** float(a["zbl_p"])) * float(a["zbl_d"])
-    rzd = r * rate
     y = torch.zeros_like(r)
-    for kx in range(1, 5):
-        y = y + float(a[f"zbl_c{kx}"]) * torch.exp(-float(a[f"zbl_a{kx}"]) * rzd)
+    if m.repulsion == "nlh":
+        # pair tables indexed (min Z, max Z) from 1; pairs beyond the capacity
+        # get no screening term (physical_zbl.cpp:144-159)
+        ta, tb = p["physical.nlh_a"], p["physical.nlh_b"]
+        cap = ta.shape[0]
+        za = torch.minimum(z[sr_r], z[sr_s])
+        zb = torch.maximum(z[sr_r], z[sr_s])
+        inside = (za >= 1) & (zb <= cap)
+        ia = torch.clamp(za - 1, 0, cap - 1)
+        ib = torch.clamp(zb - 1, 0, cap - 1)
+        for kx in range(3):
+            term = ta[ia, ib, kx] * torch.exp(-tb[ia, ib, kx] * r)
+            y = y + torch.where(inside, term, torch.zeros_like(r))
+    else:
+        rate = (z[sr_r].to(DT) ** float(a["zbl_p"]) + z[sr_s].to(DT) ** float(a["zbl_p"])) * float(a["zbl_d"])
+        rzd = r * rate
+        for kx in range(1, 5):
+            y = y + float(a[f"zbl_c{kx}"]) * torch.exp(-float(a[f"zbl_a{kx}"]) * rzd)
     e_zbl_edge = 0.5 * switching * xz * y
     e_zbl = torch.zeros(n, dtype=DT).index_add(0, sr_r, e_zbl_edge)
 

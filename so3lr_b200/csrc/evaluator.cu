@@ -133,10 +133,16 @@ void Evaluator::upload_weights() {
           }
     o.qf = push(qf);
     o.qr = push(qr);
-    o.ln1w = push(model_.f64(blk + ".layer_norm_inv_1.weight", {F}));
-    o.ln1b = push(model_.f64(blk + ".layer_norm_inv_1.bias", {F}));
-    o.ln2w = push(model_.f64(blk + ".layer_norm_inv_2.weight", {F}));
-    o.ln2b = push(model_.f64(blk + ".layer_norm_inv_2.bias", {F}));
+    // only an affine LayerNorm has parameters (post_attention_block0.cpp:395-424)
+    o.ln1w = o.ln1b = o.ln2w = o.ln2b = kNoParam;
+    if (a.norm1 == kNormLayer) {
+      o.ln1w = push(model_.f64(blk + ".layer_norm_inv_1.weight", {F}));
+      o.ln1b = push(model_.f64(blk + ".layer_norm_inv_1.bias", {F}));
+    }
+    if (a.norm2 == kNormLayer) {
+      o.ln2w = push(model_.f64(blk + ".layer_norm_inv_2.weight", {F}));
+      o.ln2b = push(model_.f64(blk + ".layer_norm_inv_2.bias", {F}));
+    }
     o.m1w = push(model_.f64(blk + ".mlp_1.1.weight", {F, F}));
     o.m1b = push(model_.f64(blk + ".mlp_1.1.bias", {F}));
     o.m2w = push(model_.f64(blk + ".mlp_1.3.weight", {F, F}));
@@ -190,10 +196,27 @@ void Evaluator::upload_weights() {
   ref_table_ = int(ta.shape[0]);
   const std::size_t o_alpha = push(model_.f64("physical.reference_alphas", {std::size_t(ref_table_)}));
   const std::size_t o_c6 = push(model_.f64("physical.reference_c6", {std::size_t(ref_table_)}));
+  const ZblParams z = model_.zbl();
+  std::size_t o_nlh_a = kNoParam, o_nlh_b = kNoParam;
+  if (z.kind == 1) {
+    const std::size_t cap = std::size_t(z.nlh_cap);
+    o_nlh_a = push(model_.f64("physical.nlh_a", {cap, cap, 3}));
+    o_nlh_b = push(model_.f64("physical.nlh_b", {cap, cap, 3}));
+  }
+  norm1_ = a.norm1;
+  norm2_ = a.norm2;
+  qk_norm_ = a.qk_norm;
+  resid_.assign(layers_, 1.0);
+  x0s_.assign(layers_, 0.0);
+  if (a.residual_scalars) {
+    resid_ = model_.f64("model.resid_lambdas", {std::size_t(layers_)});
+    x0s_ = model_.f64("model.x0_lambdas", {std::size_t(layers_)});
+  }
+  residual_scalars_ = a.residual_scalars;
 
   double *d = wbuf_.reserve(host.size());
   SO3_CUDA(cudaMemcpy(d, host.data(), host.size() * sizeof(double), cudaMemcpyHostToDevice));
-  auto P = [&](std::size_t off) { return static_cast<const double *>(d + off); };
+  auto P = [&](std::size_t off) { return off == kNoParam ? nullptr : static_cast<const double *>(d + off); };
   blocks_.resize(layers_);
   for (int b = 0; b < layers_; ++b) {
     const BOff &o = boff[b];
@@ -233,9 +256,12 @@ void Evaluator::upload_weights() {
   rad_.gamma = model_.f64("model.radial_embedding.radial_basis_fn.gamma", {})[0];
   alpha_ref_ = P(o_alpha);
   c6_ref_ = P(o_c6);
-  const ZblParams z = model_.zbl();
   zbl_.ke = z.ke; zbl_.cutoff = z.cutoff; zbl_.switch_off = z.switch_off; zbl_.p = z.p; zbl_.d = z.d;
   for (int k = 0; k < 4; ++k) { zbl_.a[k] = z.a[k]; zbl_.c[k] = z.c[k]; }
+  zbl_.kind = z.kind;
+  zbl_.nlh_cap = z.nlh_cap;
+  zbl_.nlh_a = P(o_nlh_a);
+  zbl_.nlh_b = P(o_nlh_b);
   const LongRangeParams l = model_.long_range();
   lr_.ke = l.ke; lr_.sigma = l.sigma; lr_.cutoff = l.cutoff; lr_.elec_cuton = l.elec_cuton;
   lr_.disp_cuton = l.disp_cuton; lr_.bohr = l.bohr; lr_.hartree = l.hartree; lr_.disp_scale = l.disp_scale;
@@ -529,6 +555,8 @@ void Evaluator::alloc_atoms() {
   ensure_vec(gate_, layers_, n * 4);
   ensure_vec(xhat2_, layers_, n * kF);
   ensure_vec(rstd2_, layers_, n);
+  if (qk_norm_) ensure_vec(qkr_, layers_, n * 16);
+  if (residual_scalars_) x0_.reserve(n * kF);
   d_inv_.reserve(n * kF);
   d_ev_.reserve(n * kEV);
   act_.reserve(n * kF);
@@ -747,8 +775,11 @@ void Evaluator::compute() {
   build_neighbors();
   const int P = int(stats_.pairs);
   launch_pair_geometry(P, nb_, z_.get(), zbl_, sr_cut_, geo_.get(), sh_.get(), gv_.get(), s);
+  // with residual scalars the embedding x0 is kept apart: every block's input
+  // is resid[b] x + x0[b] x0
   launch_embedding(N, z_.get(), emb_w_, any_charge_spin_ ? cs_tables_.get() : nullptr, table_of_atom_.get(),
-                   inv_emb_scale_, xb_[0]->get(), s);
+                   inv_emb_scale_, residual_scalars_ ? x0_.get() : xb_[0]->get(), s);
+  if (residual_scalars_) launch_residual_combine(N, x0_.get(), x0_.get(), resid_[0], x0s_[0], xb_[0]->get(), s);
   SO3_CUDA(cudaMemsetAsync(evb_[0]->get(), 0, sizeof(double) * N * kEV, s));
 
   for (int b = 0; b < layers_; ++b) {
@@ -774,11 +805,17 @@ void Evaluator::compute() {
         g.rows = halo_recv_rows_.get();
         launch_gemm(g, s);
       }
+      if (qk_norm_) {
+        launch_qk_norm(identity_ ? N : n, nullptr, qkv_[b]->get() + (identity_ ? 0 : r0 * kQKV),
+                       qkr_[b]->get() + (identity_ ? 0 : r0 * 16), s);
+        if (!identity_ && halo_recv_off_[nranks_] > 0)
+          launch_qk_norm(int(halo_recv_off_[nranks_]), halo_recv_rows_.get(), qkv_[b]->get(), qkr_[b]->get(), s);
+      }
     }
     launch_attention_forward(n, nb_, geo_.get(), sh_.get(), qkv_[b]->get(), f_inv_[b]->get(), f_ev_[b]->get(), norm_,
                              d_inv_.get(), d_ev_.get(), s);
     launch_post_attn_pre(n, xb_[b]->get() + r0 * kF, d_inv_.get() + r0 * kF, evb_[b]->get() + r0 * kEV,
-                         d_ev_.get() + r0 * kEV, w.ln1w, w.ln1b, w.cg_int, xhat1_[b]->get() + r0 * kF,
+                         d_ev_.get() + r0 * kEV, norm1_, w.ln1w, w.ln1b, w.cg_int, xhat1_[b]->get() + r0 * kF,
                          rstd1_[b]->get() + r0, n1_[b]->get() + r0 * kF, act_.get() + r0 * kF,
                          A_[b]->get() + r0 * kEV, cat_.get() + r0 * kIntW, s);
     {  // hidden = silu(act W1^T + b1), pre-activation kept for the reverse
@@ -811,11 +848,16 @@ void Evaluator::compute() {
       g.epi = Epi::Bias;
       launch_gemm(g, s);
     }
-    launch_post_attn_final(n, cat_.get() + r0 * kIntW, t_.get() + r0 * kIntW, A_[b]->get() + r0 * kEV, w.ln2w,
-                           w.ln2b, xhat2_[b]->get() + r0 * kF, rstd2_[b]->get() + r0, gate_[b]->get() + r0 * 4,
-                           xb_[b + 1]->get() + r0 * kF, evb_[b + 1]->get() + r0 * kEV, s);
-    if (b + 1 < layers_)  // the halo rows of the next block's input
+    launch_post_attn_final(n, cat_.get() + r0 * kIntW, t_.get() + r0 * kIntW, A_[b]->get() + r0 * kEV, norm2_,
+                           w.ln2w, w.ln2b, xhat2_[b]->get() + r0 * kF, rstd2_[b]->get() + r0,
+                           gate_[b]->get() + r0 * 4, xb_[b + 1]->get() + r0 * kF, evb_[b + 1]->get() + r0 * kEV, s);
+    if (b + 1 < layers_) {
+      if (residual_scalars_)  // the next block's input, on this GPU's rows
+        launch_residual_combine(n, xb_[b + 1]->get() + r0 * kF, x0_.get() + r0 * kF, resid_[b + 1], x0s_[b + 1],
+                                xb_[b + 1]->get() + r0 * kF, s);
+      // the halo rows of the next block's input
       halo_exchange(xb_[b + 1]->get(), kF, evb_[b + 1]->get(), kEV);
+    }
   }
 
   // ---- output heads (owned rows) --------------------------------------------
@@ -870,8 +912,8 @@ void Evaluator::compute() {
   for (int b = layers_ - 1; b >= 0; --b) {
     const BlockW &w = blocks_[b];
     launch_post_attn_rev_final(n, gx + r0 * kF, gev ? gev + r0 * kEV : nullptr, xhat2_[b]->get() + r0 * kF,
-                               rstd2_[b]->get() + r0, w.ln2w, A_[b]->get() + r0 * kEV, gate_[b]->get() + r0 * 4,
-                               g_t_.get() + r0 * kIntW, g_A_.get() + r0 * kEV, s);
+                               rstd2_[b]->get() + r0, norm2_, w.ln2w, A_[b]->get() + r0 * kEV,
+                               gate_[b]->get() + r0 * 4, g_t_.get() + r0 * kIntW, g_A_.get() + r0 * kEV, s);
     {  // g_cat = g_t W_int; g_post = g_cat[:, :128] + g_t[:, :128]
       GemmArgs g{};
       g.M = n; g.N = kIntW; g.K = kIntW;
@@ -903,9 +945,9 @@ void Evaluator::compute() {
       g.epi = Epi::GateSiluResidual;
       launch_gemm_ex(g, kF, kIntW, s);
     }
-    launch_post_attn_rev_ln1(n, g_n1_.get() + r0 * kF, xhat1_[b]->get() + r0 * kF, rstd1_[b]->get() + r0, w.ln1w,
-                             A_[b]->get() + r0 * kEV, w.cg_int, g_cat_.get() + r0 * kIntW, g_a_.get() + r0 * kF,
-                             g_A_.get() + r0 * kEV, s);
+    launch_post_attn_rev_ln1(n, g_n1_.get() + r0 * kF, xhat1_[b]->get() + r0 * kF, rstd1_[b]->get() + r0, norm1_,
+                             w.ln1w, A_[b]->get() + r0 * kEV, w.cg_int, g_cat_.get() + r0 * kIntW,
+                             g_a_.get() + r0 * kF, g_A_.get() + r0 * kEV, s);
     // the sender role of the attention reverse reads the neighbours' adjoints
     halo_exchange(g_a_.get(), kF, g_A_.get(), kEV);
     launch_attention_reverse(n, nb_, geo_.get(), sh_.get(), qkv_[b]->get(), f_inv_[b]->get(), f_ev_[b]->get(),
@@ -917,6 +959,8 @@ void Evaluator::compute() {
                           pair_sc_.get(), b > 0, b < layers_ - 1, g_r_.get(), g_y_.get(), gl0_.get(), s);
     prof_end(1, kFilterFlopsPerPair * double(P));
     if (b > 0) {
+      if (qk_norm_)  // gradient w.r.t. the projections before their normalisation
+        launch_qk_norm_reverse(n, qkv_[b]->get() + r0 * kQKV, qkr_[b]->get() + r0 * 16, g_qkv_.get() + r0 * kQKV, s);
       GemmArgs g{};  // g_x_in = g_a + per-head (g_qkv W^T)
       g.M = n; g.N = 32; g.K = 160;
       g.A = g_qkv_.get() + r0 * kQKV; g.lda = kQKV; g.strideA = 160;
@@ -926,6 +970,8 @@ void Evaluator::compute() {
       g.epi = Epi::AddResidual;
       g.batch = 4;
       launch_gemm(g, s);
+      // block b's input is resid[b] y + x0[b] x0: the previous output y gets resid[b] of it
+      if (residual_scalars_) launch_scale_rows(n, gx_next + r0 * kF, resid_[b], s);
       launch_ev_l0_reverse(n, nb_, evb_[b]->get(), w.cg_att, gl0_.get(), g_A_.get(), gev_next, s);
       std::swap(gx, gx_next);
       gev = gev_next;

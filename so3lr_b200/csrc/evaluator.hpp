@@ -159,6 +159,12 @@ class Evaluator {
   int ref_table_ = 0;
   double inv_emb_scale_ = 1.0, norm_ = 1.0, sr_cut_ = 0, lr_cut_ = 0;
   int layers_ = 0;
+  // optional block operators of the model (norm kinds kNormLayer / kNormRms /
+  // kNormNone, query/key normalisation, residual scalars per block)
+  int norm1_ = 0, norm2_ = 0;
+  bool qk_norm_ = false, residual_scalars_ = false;
+  std::vector<double> resid_, x0s_;
+  static constexpr std::size_t kNoParam = ~std::size_t(0);
 
   // static per-system data
   DeviceArray<int> z_, image_of_, image_start_, table_of_atom_;
@@ -184,6 +190,8 @@ class Evaluator {
   bool md_ready_ = false, nvt_ = false;
   void nhc_half(double dt);
   std::vector<std::unique_ptr<DeviceArray<double>>> xb_, evb_, qkv_, xhat1_, rstd1_, n1_, A_, hp_, gate_, xhat2_, rstd2_;
+  std::vector<std::unique_ptr<DeviceArray<double>>> qkr_;  // inverse RMS of q, k, q_ev, k_ev [row][head][4]
+  DeviceArray<double> x0_;                                  // embedding, kept with residual scalars
   DeviceArray<double> d_inv_, d_ev_, act_, cat_, t_, hpre_, hcat_, hk_, e_nn_, raw_q_, q_, ratio_;
   DeviceArray<double> e_lr_, e_elec_, e_disp_, dq_, dh_, f_lr_, w_lr_, img_sums_, dq_mean_, lr_pos4_, lr_par4_;
   DeviceArray<double> g_hcat_, g_x_, g_x2_, g_ev_, g_ev2_, g_t_, g_cat_, g_hp_, g_n1_, g_a_, g_A_, g_qkv_;

@@ -56,7 +56,7 @@ __global__ void k_pair_geometry(int P, const int *__restrict__ pa, const int *__
     const double om = 1.0 - x;
     dphi = -30.0 * x * x * om * om / rc;
   }
-  // learned ZBL, directed edge b -> a (identical value for a -> b)
+  // repulsion (learned ZBL or NLH), directed edge b -> a (identical value for a -> b)
   double e_dir = 0.0, de_pair = 0.0;
   if (r > 0.0 && !(r > zbl.cutoff * (1.0 + 1.0e-12))) {
     const double zi = double(z[a]), zj = double(z[b]), zz = zi * zj;
@@ -78,13 +78,28 @@ __global__ void k_pair_geometry(int P, const int *__restrict__ pa, const int *__
     const double dir = r > 1.0e-6 ? -1.0 / (r * r) : 0.0;
     const double xx = zbl.ke * cut * zz * ir;
     const double dxx = zbl.ke * zz * (dcut * ir + cut * dir);
-    const double rate = (pow(zi, zbl.p) + pow(zj, zbl.p)) * zbl.d;
-    const double rzd = r * rate;
     double yy = 0.0, dyy = 0.0;
-    for (int k = 0; k < 4; ++k) {
-      const double ex = exp(-zbl.a[k] * rzd);
-      yy += zbl.c[k] * ex;
-      dyy -= zbl.c[k] * zbl.a[k] * rate * ex;
+    if (zbl.kind == 1) {
+      // NLH: three exponentials from the pair tables, indexed (min Z, max Z)
+      // from 1; pairs beyond the table capacity have no screening term
+      const int za = min(z[a], z[b]), zb = max(z[a], z[b]);
+      if (za >= 1 && zb <= zbl.nlh_cap) {
+        const size_t base = ((size_t)(za - 1) * zbl.nlh_cap + (zb - 1)) * 3;
+        for (int k = 0; k < 3; ++k) {
+          const double amp = zbl.nlh_a[base + k], rate = zbl.nlh_b[base + k];
+          const double ex = exp(-rate * r);
+          yy += amp * ex;
+          dyy -= rate * amp * ex;
+        }
+      }
+    } else {
+      const double rate = (pow(zi, zbl.p) + pow(zj, zbl.p)) * zbl.d;
+      const double rzd = r * rate;
+      for (int k = 0; k < 4; ++k) {
+        const double ex = exp(-zbl.a[k] * rzd);
+        yy += zbl.c[k] * ex;
+        dyy -= zbl.c[k] * zbl.a[k] * rate * ex;
+      }
     }
     e_dir = 0.5 * sw * xx * yy;
     de_pair = 2.0 * (0.5 * (dsw * xx * yy + sw * dxx * yy + sw * xx * dyy));

@@ -61,8 +61,12 @@ void launch_fixed_finish(const long long *parts, int nparts, int count, double *
 // ---- per-pair geometry -------------------------------------------------------
 // geo[p*8 + {0..7}] = r, ux, uy, uz, phi, dphi/dr, zbl directed energy, zbl pair dE/dr
 constexpr int kGeo = 8;
+// repulsion: kind 0 = learned ZBL (p, d, a, c); kind 1 = NLH pair tables
+// nlh_a / nlh_b [cap][cap][3] in device memory
 struct ZblDev {
   double ke, cutoff, switch_off, p, d, a[4], c[4];
+  int kind, nlh_cap;
+  const double *nlh_a, *nlh_b;
 };
 void launch_pair_geometry(int P, const NeighborState &nb, const int *z, ZblDev zbl, double sr_cutoff,
                           double *geo, double *sh, double *gv, cudaStream_t s);
@@ -159,18 +163,36 @@ void launch_gemm_ex(const GemmArgs &g, int aux_cols, int ldaux2, cudaStream_t s)
 // ---- node elementwise / row kernels -----------------------------------------
 void launch_embedding(int n, const int *z, const double *emb_w, const double *cs_table, const int *image_of_atom,
                       double inv_scale, double *x, cudaStream_t s);
+// Block norms: kNormLayer = affine LayerNorm (lnw, lnb), kNormRms = RMSNorm
+// without scale (no parameters), kNormNone = identity (second position only).
+// xhat holds the normalised value and rstd the inverse RMS / standard
+// deviation for the reverse.
+constexpr int kNormLayer = 0, kNormRms = 1, kNormNone = 2;
 void launch_post_attn_pre(int n, const double *x, const double *d_inv, const double *ev, const double *d_ev,
-                          const double *lnw, const double *lnb, const double *cg_int, double *xhat1,
+                          int norm, const double *lnw, const double *lnb, const double *cg_int, double *xhat1,
                           double *rstd1, double *n1, double *act, double *A, double *cat, cudaStream_t s);
-void launch_post_attn_final(int n, const double *cat, const double *t, const double *A, const double *lnw,
+void launch_post_attn_final(int n, const double *cat, const double *t, const double *A, int norm, const double *lnw,
                             const double *lnb, double *xhat2, double *rstd2, double *gate, double *x_out,
                             double *ev_out, cudaStream_t s);
 void launch_post_attn_rev_final(int n, const double *g_x, const double *g_ev, const double *xhat2,
-                                const double *rstd2, const double *lnw2, const double *A, const double *gate,
-                                double *g_t, double *g_A, cudaStream_t s);
-void launch_post_attn_rev_ln1(int n, const double *g_n1, const double *xhat1, const double *rstd1,
+                                const double *rstd2, int norm, const double *lnw2, const double *A,
+                                const double *gate, double *g_t, double *g_A, cudaStream_t s);
+void launch_post_attn_rev_ln1(int n, const double *g_n1, const double *xhat1, const double *rstd1, int norm,
                               const double *lnw1, const double *A, const double *cg_int, const double *g_cat,
                               double *g_a, double *g_A, cudaStream_t s);
+// residual scalars: out[i] = a in[i] + c x0[i] over rows [0, n) of width kF
+// (out may alias in)
+void launch_residual_combine(int n, const double *in, const double *x0, double a, double c, double *out,
+                             cudaStream_t s);
+// v[i] *= a over rows [0, n) of width kF
+void launch_scale_rows(int n, double *v, double a, cudaStream_t s);
+// query/key RMS normalisation of qkv rows ([row][head][5][32], slots q, k, v,
+// q_ev, k_ev; v untouched), in place, over rows [0, n) or rows[0..n) when rows
+// is given; rinv[row][head][4] keeps the inverse RMS of q, k, q_ev, k_ev
+void launch_qk_norm(int n, const int *rows, double *qkv, double *rinv, cudaStream_t s);
+// reverse: g[row] (same layout, gradient w.r.t. the normalised values) becomes
+// the gradient w.r.t. the raw projections: r (g - y mean(g y)) per 32-vector
+void launch_qk_norm_reverse(int n, const double *qkv, const double *rinv, double *g, cudaStream_t s);
 
 // heads
 void launch_heads_finalize(int n, const int *z, const double *hcat, const HeadsW &hw, double *hk_out,

@@ -391,6 +391,21 @@ ZblParams Model::zbl() const {
   z.ke = arch_number("zbl_ke");
   z.cutoff = arch_number("short_range_cutoff_angstrom");
   z.switch_off = arch_number("zbl_switch_off_angstrom");
+  for (double v : {z.ke, z.cutoff, z.switch_off})
+    if (!std::isfinite(v) || !(v > 0)) fail("invalid ZBL parameter");
+  if (arch_.repulsion == "nlh") {
+    // parameter-free NLH: the screening comes from the pair tables
+    // (so3lr_repulsion_setup.cpp:17-21, 37-55)
+    z.kind = 1;
+    const TensorRecord &ta = tensor("physical.nlh_a");
+    const TensorRecord &tb = tensor("physical.nlh_b");
+    if (ta.shape.size() != 3 || ta.shape[0] == 0 || ta.shape[1] != ta.shape[0] || ta.shape[2] != 3 ||
+        tb.shape != ta.shape || ta.dtype != "float64" || tb.dtype != "float64")
+      fail("NLH tables physical.nlh_a / nlh_b must be float64 [cap, cap, 3]");
+    if (ta.shape[0] > 118) fail("NLH table capacity exceeds 118 elements");
+    z.nlh_cap = int(ta.shape[0]);
+    return z;
+  }
   z.p = arch_number("zbl_p");
   z.d = arch_number("zbl_d");
   double csum = 0;
@@ -494,17 +509,27 @@ void Model::describe_and_negotiate() {
   }
   r.layer_norm_eps = a.has("layer_norm_epsilon") ? a.at("layer_norm_epsilon").num() : 1e-6;
   auto flag = [&](const char *k, bool dflt) { return a.has(k) ? a.at(k).boolean() : dflt; };
-  need(!flag("use_rms_norm", false), "use_rms_norm is not implemented by this build");
-  need(!flag("qk_norm", false), "qk_norm is not implemented by this build");
-  need(!flag("use_residual_scalars", false), "residual scalars are not implemented by this build");
-  need(flag("layer_normalization_1", true) && flag("layer_normalization_2", true),
-       "both block LayerNorms must be enabled");
+  // optional operators (so3lr_architecture.cpp:369-389): one norm module for
+  // both positions (affine LayerNorm or RMSNorm without scale), the second
+  // position switchable; the first norm and exactly the first residual MLP are
+  // required, as in the reference (post_attention_block0.cpp:386-390)
+  const int norm_kind = flag("use_rms_norm", false) ? 1 : 0;
+  need(flag("layer_normalization_1", true), "the first block norm must be enabled");
+  r.norm1 = norm_kind;
+  r.norm2 = flag("layer_normalization_2", true) ? norm_kind : 2;
+  r.qk_norm = flag("qk_norm", false);
+  r.residual_scalars = flag("use_residual_scalars", false);
   need(flag("residual_mlp_1", true) && !flag("residual_mlp_2", false),
        "exactly residual_mlp_1 must be enabled");
   if (a.has("qk_nonlinearity")) need(a.at("qk_nonlinearity").str() == "identity", "qk_nonlinearity must be identity");
   r.repulsion = a.has("repulsion_type") ? a.at("repulsion_type").str()
                                         : (flag("zbl_enabled", false) ? "zbl_learned" : "none");
-  need(r.repulsion == "zbl_learned", "repulsion_type '" + r.repulsion + "' is not implemented (zbl_learned only)");
+  need(r.repulsion == "zbl_learned" || r.repulsion == "nlh",
+       "repulsion_type '" + r.repulsion + "' is not implemented (zbl_learned or nlh)");
+  if (r.residual_scalars)
+    for (const char *k : {"model.resid_lambdas", "model.x0_lambdas"})
+      need(has_tensor(k) && tensor(k).dtype == "float64" && tensor(k).shape == std::vector<std::size_t>{std::size_t(r.layers)},
+           std::string(k) + " must be a float64 vector of length interaction_blocks");
   for (const Json &h : a.at("output_heads").array()) r.output_heads.push_back(h.str());
   need(r.output_heads == std::vector<std::string>({"atomic_energy_output_block", "partial_charges_output_block",
                                                    "hirshfeld_output_block"}),
@@ -519,6 +544,13 @@ void Model::describe_and_negotiate() {
   }
   need(r.hirshfeld_hidden == 64 && r.hirshfeld_keys == 64, "Hirshfeld head must be 64x64");
   need(std::abs(r.layer_norm_eps - 1e-6) < 1e-15, "layer_norm_epsilon must be 1e-6");
+  if (problems.empty()) {
+    try {  // repulsion parameters and tables
+      zbl();
+    } catch (const std::exception &e) {
+      problems.push_back(e.what());
+    }
+  }
   if (!problems.empty()) {
     std::string msg = "this build cannot execute the model:";
     for (const auto &p : problems) msg += "\n  - " + p;

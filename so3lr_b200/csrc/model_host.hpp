@@ -68,6 +68,11 @@ struct Architecture {
   std::vector<int> degree_repeats, degree_offsets;
   double sr_cutoff = 0, lr_cutoff = 0, embedding_scale = 1, attention_norm = 1;
   double layer_norm_eps = 1e-6;
+  // block norms: 0 = affine LayerNorm, 1 = RMSNorm without scale, 2 = none
+  // (second position only)
+  int norm1 = 0, norm2 = 0;
+  bool qk_norm = false;           // RMS normalisation of q, k per (atom, head)
+  bool residual_scalars = false;  // x = resid[b] x + x0[b] x0 before block b
   std::string attention_norm_kind, repulsion;
   std::vector<std::string> output_heads;
   std::string summary() const;
@@ -78,8 +83,11 @@ struct LongRangeParams {
   double ke, sigma, cutoff, elec_cuton, fine_structure, bohr, hartree, disp_scale,
       disp_cuton, pair_scale;
 };
+// Short-range repulsion: kind 0 = learned ZBL (p, d, a, c), kind 1 = NLH pair
+// tables physical.nlh_a / nlh_b of shape [cap, cap, 3].
 struct ZblParams {
   double ke, cutoff, switch_off, p, d, a[4], c[4];
+  int kind = 0, nlh_cap = 0;
 };
 
 class Model {

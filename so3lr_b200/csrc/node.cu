@@ -221,12 +221,37 @@ __device__ inline double warp_sum(double v) {
   for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
   return v;
 }
+
+// Block norm of one 128-wide row held as 4 values per lane: xh = normalised
+// row, returns the inverse standard deviation (LayerNorm) or inverse RMS
+// (RMSNorm without scale, post_attention_block0.cpp:124-146); identity for
+// kNormNone. eps = 1e-6 (the only value the model contract admits).
+__device__ inline double row_norm(int norm, const double (&v)[4], double (&xh)[4]) {
+  if (norm == kNormNone) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) xh[j] = v[j];
+    return 1.0;
+  }
+  double mean = 0.0;
+  if (norm == kNormLayer) mean = warp_sum(v[0] + v[1] + v[2] + v[3]) / double(kF);
+  double var = 0.0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const double d = v[j] - mean;
+    var += d * d;
+  }
+  var = warp_sum(var) / double(kF);
+  const double rs = 1.0 / sqrt(var + 1.0e-6);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) xh[j] = (v[j] - mean) * rs;
+  return rs;
+}
 }  // namespace
 
 // a = x + d_inv; A = ev + d_ev; n1 = LN1(a); act = silu(n1);
 // cat[:, 128:132] = L0'(A) (interaction cg), cat[:, 132:136] = 0. One warp per atom.
 __global__ void k_post_attn_pre(int n, const double *__restrict__ x, const double *__restrict__ d_inv,
-                                const double *__restrict__ ev, const double *__restrict__ d_ev,
+                                const double *__restrict__ ev, const double *__restrict__ d_ev, int norm,
                                 const double *__restrict__ lnw, const double *__restrict__ lnb,
                                 const double *__restrict__ cg_int, double *__restrict__ xhat1,
                                 double *__restrict__ rstd1, double *__restrict__ n1_out, double *__restrict__ act,
@@ -234,29 +259,18 @@ __global__ void k_post_attn_pre(int n, const double *__restrict__ x, const doubl
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
-  double a[4];
-  double s = 0.0;
+  double a[4], xh[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int c = lane * 4 + j;
     a[j] = x[(size_t)i * kF + c] + d_inv[(size_t)i * kF + c];
-    s += a[j];
   }
-  const double mean = warp_sum(s) / double(kF);
-  double var = 0.0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const double d = a[j] - mean;
-    var += d * d;
-  }
-  var = warp_sum(var) / double(kF);
-  const double rs = 1.0 / sqrt(var + 1.0e-6);
+  const double rs = row_norm(norm, a, xh);
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int c = lane * 4 + j;
-    const double xh = (a[j] - mean) * rs;
-    const double y = xh * lnw[c] + lnb[c];
-    xhat1[(size_t)i * kF + c] = xh;
+    const double y = norm == kNormLayer ? xh[j] * lnw[c] + lnb[c] : xh[j];
+    xhat1[(size_t)i * kF + c] = xh[j];
     n1_out[(size_t)i * kF + c] = y;
     act[(size_t)i * kF + c] = silu(y);
   }
@@ -277,45 +291,34 @@ __global__ void k_post_attn_pre(int n, const double *__restrict__ x, const doubl
 }
 
 void launch_post_attn_pre(int n, const double *x, const double *d_inv, const double *ev, const double *d_ev,
-                          const double *lnw, const double *lnb, const double *cg_int, double *xhat1,
+                          int norm, const double *lnw, const double *lnb, const double *cg_int, double *xhat1,
                           double *rstd1, double *n1, double *act, double *A, double *cat, cudaStream_t s) {
-  k_post_attn_pre<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, x, d_inv, ev, d_ev, lnw, lnb, cg_int, xhat1, rstd1, n1,
-                                                       act, A, cat);
+  k_post_attn_pre<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, x, d_inv, ev, d_ev, norm, lnw, lnb, cg_int, xhat1, rstd1,
+                                                       n1, act, A, cat);
   SO3_LAUNCH("post_attn_pre");
 }
 
 // pre2 = post + t[:128]; x' = LN2(pre2); ev' = A (1 + t_gate). One warp per atom.
 __global__ void k_post_attn_final(int n, const double *__restrict__ cat, const double *__restrict__ t,
-                                  const double *__restrict__ A, const double *__restrict__ lnw,
+                                  const double *__restrict__ A, int norm, const double *__restrict__ lnw,
                                   const double *__restrict__ lnb, double *__restrict__ xhat2,
                                   double *__restrict__ rstd2, double *__restrict__ gate,
                                   double *__restrict__ x_out, double *__restrict__ ev_out) {
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
-  double v[4];
-  double s = 0.0;
+  double v[4], xh[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int c = lane * 4 + j;
     v[j] = cat[(size_t)i * kIntW + c] + t[(size_t)i * kIntW + c];
-    s += v[j];
   }
-  const double mean = warp_sum(s) / double(kF);
-  double var = 0.0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const double d = v[j] - mean;
-    var += d * d;
-  }
-  var = warp_sum(var) / double(kF);
-  const double rs = 1.0 / sqrt(var + 1.0e-6);
+  const double rs = row_norm(norm, v, xh);
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int c = lane * 4 + j;
-    const double xh = (v[j] - mean) * rs;
-    xhat2[(size_t)i * kF + c] = xh;
-    x_out[(size_t)i * kF + c] = xh * lnw[c] + lnb[c];
+    xhat2[(size_t)i * kF + c] = xh[j];
+    x_out[(size_t)i * kF + c] = norm == kNormLayer ? xh[j] * lnw[c] + lnb[c] : xh[j];
   }
   if (lane == 0) rstd2[i] = rs;
   if (lane < 4) gate[(size_t)i * 4 + lane] = t[(size_t)i * kIntW + kF + lane];
@@ -325,24 +328,32 @@ __global__ void k_post_attn_final(int n, const double *__restrict__ cat, const d
   }
 }
 
-void launch_post_attn_final(int n, const double *cat, const double *t, const double *A, const double *lnw,
+void launch_post_attn_final(int n, const double *cat, const double *t, const double *A, int norm, const double *lnw,
                             const double *lnb, double *xhat2, double *rstd2, double *gate, double *x_out,
                             double *ev_out, cudaStream_t s) {
-  k_post_attn_final<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, cat, t, A, lnw, lnb, xhat2, rstd2, gate, x_out, ev_out);
+  k_post_attn_final<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, cat, t, A, norm, lnw, lnb, xhat2, rstd2, gate, x_out,
+                                                         ev_out);
   SO3_LAUNCH("post_attn_final");
 }
 
-// LayerNorm backward (affine): g_x = rstd (g_xh - mean(g_xh) - xh mean(g_xh xh)), g_xh = g_y w
-__device__ inline void ln_backward(const double (&gy)[4], const double (&xh)[4], const double *w, int lane,
-                                   double rs, double (&gx)[4]) {
+// Block-norm backward. LayerNorm (affine): g_x = rstd (g_xh - mean(g_xh) -
+// xh mean(g_xh xh)), g_xh = g_y w. RMSNorm without scale: g_x = rrms (g_y -
+// xh mean(g_y xh)). Identity: g_x = g_y.
+__device__ inline void norm_backward(int norm, const double (&gy)[4], const double (&xh)[4], const double *w,
+                                     int lane, double rs, double (&gx)[4]) {
+  if (norm == kNormNone) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) gx[j] = gy[j];
+    return;
+  }
   double gxh[4], s1 = 0.0, s2 = 0.0;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    gxh[j] = gy[j] * w[lane * 4 + j];
+    gxh[j] = norm == kNormLayer ? gy[j] * w[lane * 4 + j] : gy[j];
     s1 += gxh[j];
     s2 += gxh[j] * xh[j];
   }
-  s1 = warp_sum(s1) / double(kF);
+  s1 = norm == kNormLayer ? warp_sum(s1) / double(kF) : 0.0;
   s2 = warp_sum(s2) / double(kF);
 #pragma unroll
   for (int j = 0; j < 4; ++j) gx[j] = rs * (gxh[j] - s1 - xh[j] * s2);
@@ -350,7 +361,7 @@ __device__ inline void ln_backward(const double (&gy)[4], const double (&xh)[4],
 
 // reverse of k_post_attn_final: g_t[:128] = LN2^T(g_x), g_t[128+d] = sum g_ev A, g_A = g_ev (1 + gate)
 __global__ void k_post_attn_rev_final(int n, const double *__restrict__ g_x, const double *__restrict__ g_ev,
-                                      const double *__restrict__ xhat2, const double *__restrict__ rstd2,
+                                      const double *__restrict__ xhat2, const double *__restrict__ rstd2, int norm,
                                       const double *__restrict__ lnw2, const double *__restrict__ A,
                                       const double *__restrict__ gate, double *__restrict__ g_t,
                                       double *__restrict__ g_A) {
@@ -363,7 +374,7 @@ __global__ void k_post_attn_rev_final(int n, const double *__restrict__ g_x, con
     gy[j] = g_x[(size_t)i * kF + lane * 4 + j];
     xh[j] = xhat2[(size_t)i * kF + lane * 4 + j];
   }
-  ln_backward(gy, xh, lnw2, lane, rstd2[i], gx);
+  norm_backward(norm, gy, xh, lnw2, lane, rstd2[i], gx);
 #pragma unroll
   for (int j = 0; j < 4; ++j) g_t[(size_t)i * kIntW + lane * 4 + j] = gx[j];
   double ge = 0.0, Am = 0.0;
@@ -383,15 +394,16 @@ __global__ void k_post_attn_rev_final(int n, const double *__restrict__ g_x, con
 }
 
 void launch_post_attn_rev_final(int n, const double *g_x, const double *g_ev, const double *xhat2,
-                                const double *rstd2, const double *lnw2, const double *A, const double *gate,
-                                double *g_t, double *g_A, cudaStream_t s) {
-  k_post_attn_rev_final<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, g_x, g_ev, xhat2, rstd2, lnw2, A, gate, g_t, g_A);
+                                const double *rstd2, int norm, const double *lnw2, const double *A,
+                                const double *gate, double *g_t, double *g_A, cudaStream_t s) {
+  k_post_attn_rev_final<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, g_x, g_ev, xhat2, rstd2, norm, lnw2, A, gate, g_t,
+                                                             g_A);
   SO3_LAUNCH("post_attn_rev_final");
 }
 
 // g_a = LN1^T(g_n1); g_A += 2 A cg_int g_l0'[deg]
 __global__ void k_post_attn_rev_ln1(int n, const double *__restrict__ g_n1, const double *__restrict__ xhat1,
-                                    const double *__restrict__ rstd1, const double *__restrict__ lnw1,
+                                    const double *__restrict__ rstd1, int norm, const double *__restrict__ lnw1,
                                     const double *__restrict__ A, const double *__restrict__ cg_int,
                                     const double *__restrict__ g_cat, double *__restrict__ g_a,
                                     double *__restrict__ g_A) {
@@ -404,7 +416,7 @@ __global__ void k_post_attn_rev_ln1(int n, const double *__restrict__ g_n1, cons
     gy[j] = g_n1[(size_t)i * kF + lane * 4 + j];
     xh[j] = xhat1[(size_t)i * kF + lane * 4 + j];
   }
-  ln_backward(gy, xh, lnw1, lane, rstd1[i], gx);
+  norm_backward(norm, gy, xh, lnw1, lane, rstd1[i], gx);
 #pragma unroll
   for (int j = 0; j < 4; ++j) g_a[(size_t)i * kF + lane * 4 + j] = gx[j];
   if (lane < kEV) {
@@ -414,11 +426,87 @@ __global__ void k_post_attn_rev_ln1(int n, const double *__restrict__ g_n1, cons
   }
 }
 
-void launch_post_attn_rev_ln1(int n, const double *g_n1, const double *xhat1, const double *rstd1,
+void launch_post_attn_rev_ln1(int n, const double *g_n1, const double *xhat1, const double *rstd1, int norm,
                               const double *lnw1, const double *A, const double *cg_int, const double *g_cat,
                               double *g_a, double *g_A, cudaStream_t s) {
-  k_post_attn_rev_ln1<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, g_n1, xhat1, rstd1, lnw1, A, cg_int, g_cat, g_a, g_A);
+  k_post_attn_rev_ln1<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, g_n1, xhat1, rstd1, norm, lnw1, A, cg_int, g_cat, g_a,
+                                                           g_A);
   SO3_LAUNCH("post_attn_rev_ln1");
+}
+
+// ---------------------------------------------------------------------------
+// residual scalars (local_energy_reverse.cpp:121-170): the input of block b is
+// resid[b] x + x0[b] x0, x0 = the embedding; the reverse scales the gradient
+// reaching the previous block's output by resid[b]
+// ---------------------------------------------------------------------------
+__global__ void k_residual_combine(long long count, const double *__restrict__ in, const double *__restrict__ x0,
+                                   double a, double c, double *__restrict__ out) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < count) out[i] = a * in[i] + c * x0[i];
+}
+void launch_residual_combine(int n, const double *in, const double *x0, double a, double c, double *out,
+                             cudaStream_t s) {
+  const long long count = (long long)n * kF;
+  if (count == 0) return;
+  k_residual_combine<<<unsigned((count + 255) / 256), 256, 0, s>>>(count, in, x0, a, c, out);
+  SO3_LAUNCH("residual_combine");
+}
+
+__global__ void k_scale_rows(long long count, double *__restrict__ v, double a) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < count) v[i] *= a;
+}
+void launch_scale_rows(int n, double *v, double a, cudaStream_t s) {
+  const long long count = (long long)n * kF;
+  if (count == 0) return;
+  k_scale_rows<<<unsigned((count + 255) / 256), 256, 0, s>>>(count, v, a);
+  SO3_LAUNCH("scale_rows");
+}
+
+// ---------------------------------------------------------------------------
+// query/key RMS normalisation (integrated_block0.cpp:288-328): every 32-wide q,
+// k, q_ev, k_ev vector of a row is divided by sqrt(mean(v^2) + 1e-6). One warp
+// per (row, head, slot), lane = channel.
+// ---------------------------------------------------------------------------
+__device__ inline int qk_slot_offset(int slot) { return slot < 2 ? slot * 32 : (slot + 1) * 32; }  // q k | q_ev k_ev
+
+__global__ void k_qk_norm(int n, const int *__restrict__ rows, double *__restrict__ qkv, double *__restrict__ rinv) {
+  const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (long long)n * 16) return;
+  const int slot = int(w & 3), head = int((w >> 2) & 3);
+  const long long m = w >> 4;
+  const long long row = rows ? rows[m] : m;
+  double *v = qkv + row * kQKV + head * 160 + qk_slot_offset(slot);
+  const double x = v[lane];
+  const double r = 1.0 / sqrt(warp_sum(x * x) / 32.0 + 1.0e-6);
+  v[lane] = x * r;
+  if (lane == 0) rinv[row * 16 + head * 4 + slot] = r;
+}
+void launch_qk_norm(int n, const int *rows, double *qkv, double *rinv, cudaStream_t s) {
+  if (n == 0) return;
+  const long long threads = (long long)n * 16 * 32;
+  k_qk_norm<<<unsigned((threads + 255) / 256), 256, 0, s>>>(n, rows, qkv, rinv);
+  SO3_LAUNCH("qk_norm");
+}
+
+__global__ void k_qk_norm_reverse(int n, const double *__restrict__ qkv, const double *__restrict__ rinv,
+                                  double *__restrict__ g) {
+  const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (long long)n * 16) return;
+  const int slot = int(w & 3), head = int((w >> 2) & 3);
+  const long long row = w >> 4;
+  const long long off = row * kQKV + head * 160 + qk_slot_offset(slot);
+  const double y = qkv[off + lane], gy = g[off + lane];
+  const double mean_gy = warp_sum(gy * y) / 32.0;
+  g[off + lane] = rinv[row * 16 + head * 4 + slot] * (gy - y * mean_gy);
+}
+void launch_qk_norm_reverse(int n, const double *qkv, const double *rinv, double *g, cudaStream_t s) {
+  if (n == 0) return;
+  const long long threads = (long long)n * 16 * 32;
+  k_qk_norm_reverse<<<unsigned((threads + 255) / 256), 256, 0, s>>>(n, qkv, rinv, g);
+  SO3_LAUNCH("qk_norm_reverse");
 }
 
 

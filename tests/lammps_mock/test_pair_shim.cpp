@@ -8,10 +8,15 @@
 //                                       one image per partition, partitions run as threads of a
 //                                       universe; INPUT holds "K" then per image "n charge mult" and
 //                                       n lines "type x y z"; prints one JSON line per image
+//   test_pair_shim multirank MODEL INPUT NRANKS
+//                                       so3lr/b200 on NRANKS MPI ranks (threads, one GPU each);
+//                                       INPUT as for run; atom i lives on rank (7 i) % NRANKS with
+//                                       tag i + 1; prints one JSON line per rank
 //   test_pair_shim turbo-refuse MODEL INPUT
 //                                       the same universe with image 1 periodic and image 2 given
 //                                       an impossible multiplicity: every partition must stop
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <functional>
@@ -143,6 +148,75 @@ static int run(const char *model, const char *input) {
   }
   std::printf("], \"log\": \"%s\"}\n", lmp.log.substr(0, lmp.log.size() - 1).c_str());
   return 0;
+}
+
+static int multirank(const char *model, const char *input, int nranks) {
+  std::ifstream in(input);
+  double L;
+  int n;
+  in >> L >> n;
+  std::vector<int> type(n);
+  std::vector<double> x(3 * static_cast<std::size_t>(n));
+  for (int i = 0; i < n; ++i) in >> type[i] >> x[3 * i] >> x[3 * i + 1] >> x[3 * i + 2];
+  std::vector<std::string> out(nranks);
+  auto errs = mpi_stub_run(nranks, [&](int r) {
+    std::vector<int> mine;
+    for (int i = 0; i < n; ++i)
+      if ((7 * i) % nranks == r) mine.push_back(i);
+    LAMMPS lmp;
+    lmp.comm.me = r;
+    lmp.comm.nprocs = nranks;
+    lmp.atom.ntypes = 2;
+    lmp.atom.resize(static_cast<int>(mine.size()));
+    lmp.atom.natoms = n;
+    for (std::size_t j = 0; j < mine.size(); ++j) {
+      const int i = mine[j];
+      lmp.atom.tag[j] = i + 1;
+      lmp.atom.type[j] = type[i];
+      for (int d = 0; d < 3; ++d) lmp.atom.x[j][d] = x[3 * static_cast<std::size_t>(i) + d];
+    }
+    for (int d = 0; d < 3; ++d) lmp.domain.prd[d] = L;
+    PairSO3LRB200 pair(&lmp);
+    char *sargs[] = {(char *)model};
+    pair.settings(1, sargs);
+    char *cargs[] = {(char *)"*", (char *)"*", (char *)"O", (char *)"H"};
+    pair.coeff(4, cargs);
+    pair.init_style();
+    pair.compute(1 | 2, 1 | 4);
+    std::ostringstream s;
+    s.precision(17);
+    s << "{\"rank\": " << r << ", \"energy\": " << pair.eng_vdwl << ", \"virial\": [";
+    for (int k = 0; k < 6; ++k) s << (k ? ", " : "") << pair.virial[k];
+    s << "], \"tags\": [";
+    for (std::size_t j = 0; j < mine.size(); ++j) s << (j ? ", " : "") << lmp.atom.tag[j];
+    s << "], \"eatom\": [";
+    for (std::size_t j = 0; j < mine.size(); ++j) s << (j ? ", " : "") << pair.eatom[j];
+    s << "], \"forces\": [";
+    for (std::size_t j = 0; j < mine.size(); ++j)
+      s << (j ? ", [" : "[") << lmp.atom.f[j][0] << ", " << lmp.atom.f[j][1] << ", " << lmp.atom.f[j][2] << "]";
+    s << "], \"vatom\": [";
+    for (std::size_t j = 0; j < mine.size(); ++j) {
+      s << (j ? ", [" : "[");
+      for (int k = 0; k < 6; ++k) s << (k ? ", " : "") << pair.vatom[j][k];
+      s << "]";
+    }
+    s << "]}";
+    out[r] = s.str();
+  });
+  int rc = 0;
+  for (int r = 0; r < nranks; ++r) {
+    if (errs[r]) {
+      try {
+        std::rethrow_exception(errs[r]);
+      } catch (const std::exception &e) {
+        std::printf("ERROR rank %d: %s\n", r, e.what());
+      }
+      rc = 1;
+    } else {
+      std::printf("%s\n", out[r].c_str());
+    }
+  }
+  return rc;
 }
 
 static int turbo_parse_checks(const char *model) {
@@ -360,10 +434,11 @@ static int turbo_refuse(const char *model, const char *input) {
 int main(int argc, char **argv) {
   if (argc >= 3 && std::string(argv[1]) == "parse") return parse_checks(argv[2]);
   if (argc >= 4 && std::string(argv[1]) == "run") return run(argv[2], argv[3]);
+  if (argc >= 5 && std::string(argv[1]) == "multirank") return multirank(argv[2], argv[3], std::atoi(argv[4]));
   if (argc >= 3 && std::string(argv[1]) == "turbo-parse") return turbo_parse_checks(argv[2]);
   if (argc >= 4 && std::string(argv[1]) == "turbo-run") return turbo_run(argv[2], argv[3]);
   if (argc >= 4 && std::string(argv[1]) == "turbo-refuse") return turbo_refuse(argv[2], argv[3]);
-  std::printf("usage: test_pair_shim parse MODEL | run MODEL INPUT | turbo-parse MODEL | turbo-run MODEL INPUT | "
-              "turbo-refuse MODEL INPUT\n");
+  std::printf("usage: test_pair_shim parse MODEL | run MODEL INPUT | multirank MODEL INPUT NRANKS | turbo-parse MODEL | "
+              "turbo-run MODEL INPUT | turbo-refuse MODEL INPUT\n");
   return 2;
 }

@@ -64,11 +64,11 @@ def test_partition_consistent_across_gloo_ranks():
         assert counts.max() <= 1.35 * counts.mean(), counts
 
 
-def _gpu_worker(rank, world, uid, nmol, seed, result_q):
+def _gpu_worker(rank, world, uid, nmol, seed, result_q, model=MODEL):
     try:
         from so3lr_b200 import So3lrB200
         from so3lr_b200.systems import water_box
-        m = So3lrB200(MODEL, rank)
+        m = So3lrB200(model, rank)
         m.comm_init(world, rank, uid)
         w = water_box(nmol, seed=seed)
         out = m.compute(w.pos, w.z, cell=w.cell, boxlo=w.boxlo)
@@ -153,6 +153,44 @@ def test_multi_gpu_bit_identical(world, gpu_model):
     for rank, e, f, vir, chg, owned, va, err in res:
         assert err is None, err
         assert 0 < owned < len(w.z)
+        assert e == ref["energy"], (e, ref["energy"])
+        assert np.array_equal(f, ref["forces"]), np.abs(f - ref["forces"]).max()
+        assert np.array_equal(vir, ref["virial"])
+        assert np.array_equal(chg, ref["charges"])
+        assert np.array_equal(va, ref_va)
+
+
+@pytest.mark.gpu
+def test_multi_gpu_bit_identical_with_optional_operators(tmp_path):
+    """A model with RMSNorm, query/key normalisation (also on the halo rows each
+    GPU projects itself), residual scalars and NLH repulsion: 2 GPUs give the
+    single-GPU bits."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from model_variants import make_variant
+    from so3lr_b200 import So3lrB200
+    from so3lr_b200.systems import water_box
+    path = make_variant(MODEL, tmp_path / "all.so3lr", rms_norm=True, qk_norm=True,
+                        residual_scalars=([0.9, 1.1, 0.8], [0.1, -0.2, 0.3]), nlh_capacity=9, seed=2,
+                        attention_norm_factor=20.0)
+    nmol, seed = 1000, 19
+    w = water_box(nmol, seed=seed)
+    single = So3lrB200(path, 0)
+    ref = single.compute(w.pos, w.z, cell=w.cell, boxlo=w.boxlo)
+    ref_va = single.virial_atom(len(w.z))
+    single.close()
+    uid = So3lrB200.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gpu_worker, args=(r, 2, uid, nmol, seed, q, path)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, e, f, vir, chg, owned, va, err in res:
+        assert err is None, err
         assert e == ref["energy"], (e, ref["energy"])
         assert np.array_equal(f, ref["forces"]), np.abs(f - ref["forces"]).max()
         assert np.array_equal(vir, ref["virial"])

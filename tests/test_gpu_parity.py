@@ -145,6 +145,28 @@ def test_gpu_invariances_full_size(gpu_model):
     assert np.abs(a["forces"][perm] - c["forces"]).max() <= 1e-9
 
 
+def test_gpu_virial_is_strain_derivative_full_size(gpu_model):
+    """The pressure an NPT run sees, at config 3 size (24,000 atoms): each
+    diagonal virial component equals -dE/d(strain) by a central difference of
+    the GPU energy over a uniformly scaled box and positions (the reference
+    validates the virial through LAMMPS NPT runs, VALIDATION.md:112-116)."""
+    from so3lr_b200.systems import water_box
+    w = water_box(8000, seed=13)
+    base = gpu_model.compute(w.pos, w.z, cell=w.cell, boxlo=w.boxlo, terms=False)
+    eps = 1e-5
+    for a in range(3):
+        e = []
+        for sgn in (+1, -1):
+            s = np.ones(3)
+            s[a] += sgn * eps
+            lo = np.asarray(w.boxlo, dtype=np.float64)
+            out = gpu_model.compute(lo + (w.pos - lo) * s, w.z, cell=np.asarray(w.cell) * s, boxlo=lo, terms=False)
+            e.append(out["energy"])
+        w_fd = -(e[0] - e[1]) / (2 * eps)
+        tol = 1e-6 * max(1.0, abs(base["virial"][a])) + 1e-13 * abs(base["energy"]) / eps
+        assert abs(w_fd - base["virial"][a]) <= tol, (a, w_fd, base["virial"][a])
+
+
 def test_gpu_turbo_batch_matches_single_images(gpu_model, oracle_model):
     """A pack of independent clusters (neutral, OH-, H3O+) equals each cluster
     evaluated alone (the reference's packed-evaluator test tolerance is

@@ -68,10 +68,10 @@ def _rewrite(tmp_path: pathlib.Path, mutate_manifest=None, mutate_bytes=None) ->
 
 @pytest.mark.parametrize("change, message", [
     (lambda m: m["architecture"].__setitem__("invariant_features", 256), "invariant_features"),
-    (lambda m: m["architecture"].__setitem__("use_rms_norm", True), "use_rms_norm"),
-    (lambda m: m["architecture"].__setitem__("qk_norm", True), "qk_norm"),
-    (lambda m: m["architecture"].__setitem__("use_residual_scalars", True), "residual scalars"),
-    (lambda m: m["architecture"].__setitem__("repulsion_type", "nlh"), "repulsion_type"),
+    (lambda m: m["architecture"].__setitem__("use_residual_scalars", True), "model.resid_lambdas"),
+    (lambda m: m["architecture"].__setitem__("repulsion_type", "nlh"), "physical.nlh_a"),
+    (lambda m: m["architecture"].__setitem__("repulsion_type", "none"), "repulsion_type"),
+    (lambda m: m["architecture"].__setitem__("radial_basis_features", 64), "radial_basis_features"),
     (lambda m: m["architecture"].__setitem__("brand_new_flag", 1), "unknown architecture key"),
     (lambda m: m["architecture"]["output_heads"].append("c6_ratios_output_block"), "output heads"),
     (lambda m: m["architecture"].__setitem__("message_normalization", "softmax"), "message_normalization"),

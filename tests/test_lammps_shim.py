@@ -48,10 +48,18 @@ def _write_images(path: pathlib.Path, pos, z, off, q, m) -> None:
     path.write_text("\n".join(lines) + "\n")
 
 
-def _run_images(exe, model, inp):
-    res = subprocess.run([str(exe), "turbo-run", str(model), str(inp)], capture_output=True, text=True, timeout=600)
+def _json_lines(res, expected: int):
+    """The JSON records a driver mode printed (one per image or rank); other
+    lines (library or NCCL log output) are skipped."""
     assert res.returncode == 0, res.stdout + res.stderr
-    return [json.loads(line) for line in res.stdout.strip().splitlines()]
+    out = [json.loads(line) for line in res.stdout.splitlines() if line.startswith("{")]
+    assert len(out) == expected, res.stdout + res.stderr
+    return out
+
+
+def _run_images(exe, model, inp, nimg):
+    res = subprocess.run([str(exe), "turbo-run", str(model), str(inp)], capture_output=True, text=True, timeout=600)
+    return _json_lines(res, nimg)
 
 
 def _fdotr(x, f):
@@ -80,8 +88,7 @@ def test_turbo_routes_each_image_back_to_its_partition(tmp_path):
     pos, z, off, q, m = turbo_batch(4, seed=7)
     inp = tmp_path / "images.txt"
     _write_images(inp, pos, z, off, q, m)
-    out = _run_images(exe, "fake", inp)
-    assert len(out) == 4
+    out = _run_images(exe, "fake", inp, 4)
     for k, o in enumerate(out):
         sl = slice(off[k], off[k + 1])
         x = pos[sl]
@@ -133,6 +140,43 @@ def test_pair_style_compute_matches_c_abi(tmp_path, gpu_model):
 
 
 @pytest.mark.gpu
+def test_pair_style_on_two_ranks_matches_one_gpu(tmp_path, gpu_model):
+    """so3lr/b200 on two MPI ranks (threads of the mock universe, one GPU
+    each, atoms dealt to the ranks out of order): every rank's forces,
+    per-atom energies and virials equal the single-GPU result for its atoms'
+    tags, and rank 0 alone reports the global energy and virial."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from so3lr_b200.systems import water_box
+    exe = _build(tmp_path)
+    w = water_box(216, seed=23)
+    inp = tmp_path / "box.txt"
+    lines = [f"{float(w.cell[0])!r} {len(w.z)}"]
+    for zi, p in zip(w.z, w.pos):
+        lines.append(f"{1 if zi == 8 else 2} {float(p[0])!r} {float(p[1])!r} {float(p[2])!r}")
+    inp.write_text("\n".join(lines) + "\n")
+    res = subprocess.run([str(exe), "multirank", str(MODEL), str(inp), "2"], capture_output=True, text=True,
+                         timeout=600)
+    out = _json_lines(res, 2)
+    ref = gpu_model.compute(w.pos, w.z, cell=w.cell, boxlo=w.boxlo)
+    ref_va = gpu_model.virial_atom(len(w.z))
+    seen = []
+    for o in out:
+        rows = np.array(o["tags"]) - 1
+        seen += list(rows)
+        assert np.array_equal(np.array(o["forces"]), ref["forces"][rows])
+        assert np.array_equal(np.array(o["vatom"]), ref_va[rows])
+        assert np.array_equal(np.array(o["eatom"]), ref["eatom"][rows])
+        if o["rank"] == 0:
+            assert o["energy"] == ref["energy"]
+            assert np.array_equal(np.array(o["virial"]), ref["virial"])
+        else:
+            assert o["energy"] == 0.0 and not any(o["virial"])
+    assert sorted(seen) == list(range(len(w.z)))
+
+
+@pytest.mark.gpu
 def test_turbo_pair_style_matches_c_abi(tmp_path, gpu_model):
     """so3lr/b200/turbo over five partitions returns, per image, what
     so3lr_compute_batch returns for the same pack (bit for bit), per-atom
@@ -144,7 +188,7 @@ def test_turbo_pair_style_matches_c_abi(tmp_path, gpu_model):
     pos, z, off, q, m = turbo_batch(5, seed=11)
     inp = tmp_path / "images.txt"
     _write_images(inp, pos, z, off, q, m)
-    out = _run_images(exe, MODEL, inp)
+    out = _run_images(exe, MODEL, inp, 5)
     ref = gpu_model.compute_batch(pos, z, off, q, m)
     ref_va = gpu_model.virial_atom(len(z))
     for k, o in enumerate(out):
