@@ -25,7 +25,9 @@ CPradaL/so3lrxlammps 0.4.0 (paths relative to source/so3lr-lammps-native/):
   norm position and no second norm (src/kokkos_post_attention_block0.cpp:124-162,
   src/so3lr_architecture.cpp:383-389), query/key RMS normalisation per head
   (src/kokkos_integrated_block0.cpp:288-328), residual scalars before every block
-  (src/kokkos_local_energy_reverse.cpp:121-170);
+  (src/kokkos_local_energy_reverse.cpp:121-170), ratio heads with 1..64 keys and the
+  C6 ratio head (src/kokkos_output_heads.cpp:105-176, 273-283;
+  src/kokkos_physical_long_range.cpp:118-262);
 * virial: plugins/lammps/pair_so3lr_native_mpi.cpp:944-990.
 
 The reverse pass is not restated line by line: the reference's hand-written
@@ -411,11 +413,19 @@ def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -
     hc = _silu(torch.nn.functional.linear(x, p[co + "transform_inv_features.0.weight"]) + p[co + "transform_inv_features.0.bias"])
     raw = torch.nn.functional.linear(hc, p[co + "transform_inv_features.2.weight"])[:, 0] \
         + p[co + "transform_inv_features.2.bias"][0] + p[co + "atomic_embedding.weight"][z, 0]
-    ho = "model.hirshfeld_output_block."
-    h1 = _silu(torch.nn.functional.linear(x, p[ho + "transform_features.0.weight"]) + p[ho + "transform_features.0.bias"])
-    kk = torch.nn.functional.linear(h1, p[ho + "transform_features.2.weight"]) + p[ho + "transform_features.2.bias"]
-    K = kk.shape[1]
-    ratio = torch.abs(p[ho + "v_shift_embedding.weight"][z, 0] + (p[ho + "q_embedding.weight"][z] * kk).sum(dim=1) / math.sqrt(K))
+    def ratio_head(prefix):
+        """Hirshfeld / a0 or C6 ratio head with K keys (output_heads.cpp:135-176)."""
+        h1 = _silu(torch.nn.functional.linear(x, p[prefix + "transform_features.0.weight"])
+                   + p[prefix + "transform_features.0.bias"])
+        kk = torch.nn.functional.linear(h1, p[prefix + "transform_features.2.weight"]) + p[prefix + "transform_features.2.bias"]
+        K = kk.shape[1]
+        return torch.abs(p[prefix + "v_shift_embedding.weight"][z, 0]
+                         + (p[prefix + "q_embedding.weight"][z] * kk).sum(dim=1) / math.sqrt(K))
+
+    ratio = ratio_head("model.hirshfeld_output_block.")
+    # optional fourth head: C6 ratios; then alpha comes from `ratio` alone and
+    # C6_i = C6_ref c6_i (physical_long_range.cpp:118-121, 212-218)
+    c6r = ratio_head("model.c6_ratios_output_block.") if "c6_ratios_output_block" in m.file.arch["output_heads"] else None
     # charge conservation per image
     raw_sum = torch.zeros(n_img, dtype=DT).index_add(0, image, raw)
     count = torch.zeros(n_img, dtype=DT).index_add(0, image, torch.ones(n, dtype=DT))
@@ -484,7 +494,10 @@ def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -
     ai0, aj0 = alpha_ref[zi[lr_i]], alpha_ref[zi[lr_j]]
     ci0, cj0 = c6_ref[zi[lr_i]], c6_ref[zi[lr_j]]
     ai, aj = ai0 * hi, aj0 * hj
-    c6i, c6j = ci0 * hi * hi, cj0 * hj * hj
+    if c6r is None:
+        c6i, c6j = ci0 * hi * hi, cj0 * hj * hj
+    else:
+        c6i, c6j = ci0 * c6r[lr_i], cj0 * c6r[lr_j]
     alpha = 0.5 * (ai + aj)
     num = 2.0 * c6i * c6j * aj * ai
     den = ai * ai * c6j + aj * aj * c6i
@@ -531,6 +544,7 @@ def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -
         "dispersion_energy": e_disp_atom.detach().numpy(),
         "partial_charges": charge.detach().numpy(),
         "hirshfeld_ratios": ratio.detach().numpy(),
+        "c6_ratios": None if c6r is None else c6r.detach().numpy(),
         "image_energy": torch.zeros(n_img, dtype=DT).index_add(0, image, e_atom).detach().numpy(),
     }
     if want_forces:

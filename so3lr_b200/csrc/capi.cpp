@@ -347,6 +347,9 @@ int so3lr_long_range_noalloc(so3lr_handle *h, long long natoms, const double *x,
       throw Error("SO3LR no-alloc long range: natoms = " + std::to_string(natoms) + " is outside 1.." +
                   std::to_string(so3lr_b200::noalloc_max_atoms()));
     Evaluator &ev = *h->eval;
+    if (ev.has_c6_head())
+      throw Error("SO3LR no-alloc long range: the model has a C6-ratio head; this entry point takes Hirshfeld "
+                  "ratios only");
     int previous = 0;
     SO3_CUDA(cudaGetDevice(&previous));
     if (previous != ev.device()) SO3_CUDA(cudaSetDevice(ev.device()));

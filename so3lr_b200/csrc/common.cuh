@@ -26,6 +26,7 @@ constexpr int kIntW = 136;    // 132-wide interaction layer padded to a multiple
 constexpr int kHeadHidden = 128;
 constexpr int kHirsh = 64;
 constexpr int kHeadCat = 2 * kHeadHidden + kHirsh;  // fused first layers of the 3 heads
+constexpr int kHeadCatC6 = kHeadCat + kHirsh;        // ... and of the optional C6 ratio head
 constexpr int kMaxLayers = 8;
 // per pair, per block: the cutoff-gradient weight and the ev attention
 // coefficients of both directions per head (+1 pad: rows of 16-byte chunks)
@@ -178,7 +179,7 @@ struct BlockW {
   const double *intw, *intb;       // padded [136][136], [136]
 };
 struct HeadsW {
-  const double *w1cat, *b1cat;     // [320][128], [320]: energy, charge, Hirshfeld first layers
+  const double *w1cat, *b1cat;     // [ldh][128], [ldh]: energy, charge, Hirshfeld (, C6) first layers
   const double *e_w2;              // [128]
   double e_b2;
   const double *e_scale, *e_shift; // [118]
@@ -188,6 +189,11 @@ struct HeadsW {
   const double *h_w2, *h_b2;       // [64][64], [64]
   const double *h_w2t;             // [64][64]: h_w2 transposed ([in][out])
   const double *h_qemb, *h_vshift; // [100][64], [100]
+  double h_sqrt_k;                 // sqrt(number of keys); keys beyond it are zero-padded to 64
+  // optional C6 ratio head (c6_w2 == nullptr when absent), same layout
+  const double *c6_w2, *c6_b2, *c6_w2t, *c6_qemb, *c6_vshift;
+  double c6_sqrt_k;
+  int ldh;                         // row width of the fused first layers: kHeadCat or kHeadCatC6
 };
 struct RadialW {
   const double *b;                 // [32]

@@ -160,6 +160,7 @@ void Evaluator::upload_weights() {
   // heads
   const std::string eo = "model.atomic_energy_output_block.", co = "model.partial_charges_output_block.",
                     ho = "model.hirshfeld_output_block.";
+  const std::string c6o = "model.c6_ratios_output_block.";
   std::vector<double> w1cat, b1cat;
   for (auto &part : {model_.f64(eo + "layers.0.weight", {128, F}), model_.f64(co + "transform_inv_features.0.weight", {128, F}),
                      model_.f64(ho + "transform_features.0.weight", {64, F})})
@@ -167,6 +168,39 @@ void Evaluator::upload_weights() {
   for (auto &part : {model_.f64(eo + "layers.0.bias", {128}), model_.f64(co + "transform_inv_features.0.bias", {128}),
                      model_.f64(ho + "transform_features.0.bias", {64})})
     b1cat.insert(b1cat.end(), part.begin(), part.end());
+  if (a.has_c6) {  // the C6 ratio head's first layer joins the fused GEMM
+    const auto w = model_.f64(c6o + "transform_features.0.weight", {64, F});
+    const auto b = model_.f64(c6o + "transform_features.0.bias", {64});
+    w1cat.insert(w1cat.end(), w.begin(), w.end());
+    b1cat.insert(b1cat.end(), b.begin(), b.end());
+  }
+  // a ratio head with K keys, zero-padded to 64 keys: the padded keys are 0 and
+  // their embeddings 0, so they add nothing (output_heads.cpp:105-133)
+  struct RatioOff { std::size_t w2, w2t, b2, qemb, vshift; double sqrt_k; };
+  auto ratio_head = [&](const std::string &prefix, int K) {
+    const std::size_t k = std::size_t(K);
+    const auto w2 = model_.f64(prefix + "transform_features.2.weight", {k, 64});
+    const auto b2 = model_.f64(prefix + "transform_features.2.bias", {k});
+    const auto qe = model_.f64(prefix + "q_embedding.weight", {100, k});
+    std::vector<double> w2p(64 * 64, 0.0), w2tp(64 * 64, 0.0), b2p(64, 0.0), qep(100 * 64, 0.0);
+    for (std::size_t r = 0; r < k; ++r) {
+      b2p[r] = b2[r];
+      for (std::size_t j = 0; j < 64; ++j) {
+        w2p[r * 64 + j] = w2[r * 64 + j];
+        w2tp[j * 64 + r] = w2[r * 64 + j];
+      }
+    }
+    for (std::size_t zz = 0; zz < 100; ++zz)
+      for (std::size_t r = 0; r < k; ++r) qep[zz * 64 + r] = qe[zz * k + r];
+    RatioOff o;
+    o.w2 = push(w2p);
+    o.w2t = push(w2tp);
+    o.b2 = push(b2p);
+    o.qemb = push(qep);
+    o.vshift = push(model_.f64(prefix + "v_shift_embedding.weight", {100, 1}));
+    o.sqrt_k = std::sqrt(double(K));
+    return o;
+  };
   const std::size_t o_w1cat = push(w1cat), o_b1cat = push(b1cat);
   const std::size_t o_ew2 = push(model_.f64(eo + "final_layer.weight", {1, 128}));
   const double e_b2 = model_.f64(eo + "final_layer.bias", {1})[0];
@@ -175,15 +209,9 @@ void Evaluator::upload_weights() {
   const std::size_t o_cw2 = push(model_.f64(co + "transform_inv_features.2.weight", {1, 128}));
   const double c_b2 = model_.f64(co + "transform_inv_features.2.bias", {1})[0];
   const std::size_t o_cemb = push(model_.f64(co + "atomic_embedding.weight", {100, 1}));
-  const auto hw2 = model_.f64(ho + "transform_features.2.weight", {64, 64});
-  const std::size_t o_hw2 = push(hw2);
-  std::vector<double> hw2t(64 * 64);
-  for (int k = 0; k < 64; ++k)
-    for (int j = 0; j < 64; ++j) hw2t[std::size_t(j) * 64 + k] = hw2[std::size_t(k) * 64 + j];
-  const std::size_t o_hw2t = push(hw2t);
-  const std::size_t o_hb2 = push(model_.f64(ho + "transform_features.2.bias", {64}));
-  const std::size_t o_hq = push(model_.f64(ho + "q_embedding.weight", {100, 64}));
-  const std::size_t o_hv = push(model_.f64(ho + "v_shift_embedding.weight", {100, 1}));
+  const RatioOff o_h = ratio_head(ho, a.hirshfeld_keys);
+  RatioOff o_r6{kNoParam, kNoParam, kNoParam, kNoParam, kNoParam, 1.0};
+  if (a.has_c6) o_r6 = ratio_head(c6o, a.c6_keys);
   const std::size_t o_emb = push(model_.f64("model.inv_feature_embedding.embedding.weight", {F, 118}));
   const std::size_t o_rb = push(model_.f64("model.radial_embedding.radial_basis_fn.b", {R}));
   std::vector<double> kd, krd;
@@ -244,11 +272,19 @@ void Evaluator::upload_weights() {
   heads_.c_w2 = P(o_cw2);
   heads_.c_b2 = c_b2;
   heads_.c_emb = P(o_cemb);
-  heads_.h_w2 = P(o_hw2);
-  heads_.h_w2t = P(o_hw2t);
-  heads_.h_b2 = P(o_hb2);
-  heads_.h_qemb = P(o_hq);
-  heads_.h_vshift = P(o_hv);
+  heads_.h_w2 = P(o_h.w2);
+  heads_.h_w2t = P(o_h.w2t);
+  heads_.h_b2 = P(o_h.b2);
+  heads_.h_qemb = P(o_h.qemb);
+  heads_.h_vshift = P(o_h.vshift);
+  heads_.h_sqrt_k = o_h.sqrt_k;
+  heads_.c6_w2 = P(o_r6.w2);
+  heads_.c6_w2t = P(o_r6.w2t);
+  heads_.c6_b2 = P(o_r6.b2);
+  heads_.c6_qemb = P(o_r6.qemb);
+  heads_.c6_vshift = P(o_r6.vshift);
+  heads_.c6_sqrt_k = o_r6.sqrt_k;
+  heads_.ldh = a.has_c6 ? kHeadCatC6 : kHeadCat;
   emb_w_ = P(o_emb);
   rad_.b = P(o_rb);
   rad_.k = P(o_rk);
@@ -562,9 +598,14 @@ void Evaluator::alloc_atoms() {
   act_.reserve(n * kF);
   cat_.reserve(n * kIntW);
   t_.reserve(n * kIntW);
-  hpre_.reserve(n * kHeadCat);
-  hcat_.reserve(n * kHeadCat);
+  hpre_.reserve(n * heads_.ldh);
+  hcat_.reserve(n * heads_.ldh);
   hk_.reserve(n * kHirsh);
+  if (heads_.c6_w2 != nullptr) {
+    hk6_.reserve(n * kHirsh);
+    ratio6_.reserve(n);
+    dc6_.reserve(n);
+  }
   e_nn_.reserve(n);
   raw_q_.reserve(n);
   q_.reserve(n);
@@ -580,7 +621,7 @@ void Evaluator::alloc_atoms() {
   w_lr_.reserve(6 * n);
   img_sums_.reserve(nimg + 1);
   dq_mean_.reserve(nimg + 1);
-  g_hcat_.reserve(n * kHeadCat);
+  g_hcat_.reserve(n * heads_.ldh);
   g_x_.reserve(n * kF);
   g_x2_.reserve(n * kF);
   g_ev_.reserve(n * kEV);
@@ -863,16 +904,19 @@ void Evaluator::compute() {
   // ---- output heads (owned rows) --------------------------------------------
   {
     GemmArgs g{};
-    g.M = n; g.N = kHeadCat; g.K = kF;
+    const int ldh = heads_.ldh;
+    g.M = n; g.N = ldh; g.K = kF;
     g.A = xb_[layers_]->get() + r0 * kF; g.lda = kF;
     g.W = heads_.w1cat; g.ldw = kF; g.transB = true;
-    g.C = hcat_.get() + r0 * kHeadCat; g.ldc = kHeadCat;
-    g.bias = heads_.b1cat; g.aux_out = hpre_.get() + r0 * kHeadCat; g.ldaux = kHeadCat;
+    g.C = hcat_.get() + r0 * ldh; g.ldc = ldh;
+    g.bias = heads_.b1cat; g.aux_out = hpre_.get() + r0 * ldh; g.ldaux = ldh;
     g.epi = Epi::BiasStorePre;
     launch_gemm(g, s);
   }
-  launch_heads_finalize(n, z_.get() + r0, hcat_.get() + r0 * kHeadCat, heads_, hk_.get() + r0 * kHirsh,
-                        e_nn_.get() + r0, raw_q_.get() + r0, ratio_.get() + r0, s);
+  const bool c6 = heads_.c6_w2 != nullptr;
+  launch_heads_finalize(n, z_.get() + r0, hcat_.get() + r0 * heads_.ldh, heads_, hk_.get() + r0 * kHirsh,
+                        e_nn_.get() + r0, raw_q_.get() + r0, ratio_.get() + r0, c6 ? hk6_.get() + r0 * kHirsh : nullptr,
+                        c6 ? ratio6_.get() + r0 : nullptr, s);
   // charge conservation: exact sum of the raw charges per image (over all GPUs)
   if (identity_) {
     exact_sums(raw_q_.get(), 1, 1, nimg, image_start_.get(), img_sums_.get());
@@ -883,11 +927,14 @@ void Evaluator::compute() {
                         q_.get() + r0, nullptr, nullptr, s);
   allgather_rows(q_.get(), 1);
   allgather_rows(ratio_.get(), 1);
+  if (c6) allgather_rows(ratio6_.get(), 1);
 
   // ---- long range (owned rows) ------------------------------------------------
-  launch_long_range(n, spec_.n, nb_, lr_cut_, z_.get(), q_.get(), ratio_.get(), alpha_ref_, c6_ref_, ref_table_, lr_,
+  launch_long_range(n, spec_.n, nb_, lr_cut_, z_.get(), q_.get(), ratio_.get(), c6 ? ratio6_.get() : nullptr,
+                    alpha_ref_, c6_ref_, ref_table_, lr_,
                     reinterpret_cast<double4 *>(lr_pos4_.get()), reinterpret_cast<double4 *>(lr_par4_.get()),
-                    e_lr_.get(), e_elec_.get(), e_disp_.get(), dq_.get(), dh_.get(), f_lr_.get(), w_lr_.get(), s);
+                    e_lr_.get(), e_elec_.get(), e_disp_.get(), dq_.get(), dh_.get(), c6 ? dc6_.get() : nullptr,
+                    f_lr_.get(), w_lr_.get(), s);
   if (identity_) {
     exact_sums(dq_.get(), 1, 1, nimg, image_start_.get(), img_sums_.get());
   } else {
@@ -897,12 +944,13 @@ void Evaluator::compute() {
                         img_sums_.get(), s);
 
   // ---- reverse ---------------------------------------------------------------
-  launch_heads_seed(n, z_.get() + r0, hpre_.get() + r0 * kHeadCat, hk_.get() + r0 * kHirsh, heads_, dq_.get() + r0,
-                    dq_mean_.get(), image_of_.get() + r0, dh_.get() + r0, g_hcat_.get() + r0 * kHeadCat, s);
+  launch_heads_seed(n, z_.get() + r0, hpre_.get() + r0 * heads_.ldh, hk_.get() + r0 * kHirsh, heads_, dq_.get() + r0,
+                    dq_mean_.get(), image_of_.get() + r0, dh_.get() + r0, c6 ? hk6_.get() + r0 * kHirsh : nullptr,
+                    c6 ? dc6_.get() + r0 : nullptr, g_hcat_.get() + r0 * heads_.ldh, s);
   {
     GemmArgs g{};
-    g.M = n; g.N = kF; g.K = kHeadCat;
-    g.A = g_hcat_.get() + r0 * kHeadCat; g.lda = kHeadCat;
+    g.M = n; g.N = kF; g.K = heads_.ldh;
+    g.A = g_hcat_.get() + r0 * heads_.ldh; g.lda = heads_.ldh;
     g.W = heads_.w1cat; g.ldw = kF; g.transB = false;
     g.C = g_x_.get() + r0 * kF; g.ldc = kF;
     launch_gemm(g, s);

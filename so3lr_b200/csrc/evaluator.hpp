@@ -123,6 +123,7 @@ class Evaluator {
     double cutoff;
   };
   LongRangeTables long_range_tables() const { return {lr_, alpha_ref_, c6_ref_, ref_table_, lr_cut_}; }
+  bool has_c6_head() const { return heads_.c6_w2 != nullptr; }
   std::size_t device_bytes() const;
 
   // Optional CUDA-event timing of the pair-filter kernels on stream(): kernel 0 =
@@ -193,6 +194,7 @@ class Evaluator {
   std::vector<std::unique_ptr<DeviceArray<double>>> qkr_;  // inverse RMS of q, k, q_ev, k_ev [row][head][4]
   DeviceArray<double> x0_;                                  // embedding, kept with residual scalars
   DeviceArray<double> d_inv_, d_ev_, act_, cat_, t_, hpre_, hcat_, hk_, e_nn_, raw_q_, q_, ratio_;
+  DeviceArray<double> hk6_, ratio6_, dc6_;  // C6 ratio head (models that have one)
   DeviceArray<double> e_lr_, e_elec_, e_disp_, dq_, dh_, f_lr_, w_lr_, img_sums_, dq_mean_, lr_pos4_, lr_par4_;
   DeviceArray<double> g_hcat_, g_x_, g_x2_, g_ev_, g_ev2_, g_t_, g_cat_, g_hp_, g_n1_, g_a_, g_A_, g_qkv_;
   DeviceArray<double> e_atom_, e_zbl_, w_atom_, totals_, image_energy_;

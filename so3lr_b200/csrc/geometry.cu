@@ -151,7 +151,7 @@ __device__ inline void smooth_switch(double r, double cuton, double cutoff, doub
 }
 
 struct LrPair {
-  double e_elec, e_disp, dq, dh, radial;
+  double e_elec, e_disp, dq, dh, dc, radial;
 };
 
 // per-launch constants of the pair term, computed once per thread
@@ -174,11 +174,15 @@ __device__ inline LrConst lr_const(const LrDev &p) {
 // Coulomb with its switch; QDO dispersion with C6 mixing, the fitted sigma(R_vdW)
 // polynomial and its switch), with shared reciprocals instead of repeated
 // divisions (about 10 divisions per pair instead of 49).
+// kSepC6: the model has a C6 ratio head; si, sj are the two atoms' C6 ratios,
+// C6 = C6_ref s instead of C6_ref h^2, and dc = dE/ds_i (physical_long_range.cpp:118-262).
+template <bool kSepC6>
 __device__ inline LrPair lr_pair_tab(const LrDev &p, const LrConst &k, double r, double qi, double qj, double hi,
-                                     double hj, double ai0, double aj0, double ci0, double cj0) {
+                                     double hj, double ai0, double aj0, double ci0, double cj0, double si,
+                                     double sj) {
   constexpr double inv_sqrt_pi = 0.56418958354775628695;
   constexpr double inv7 = 1.0 / 7.0;
-  LrPair o{0, 0, 0, 0, 0};
+  LrPair o{0, 0, 0, 0, 0, 0};
   double esw, desw;
   smooth_switch(r, p.elec_cuton, p.cutoff, k.inv_elec_width, esw, desw);
   const double inv_r = 1.0 / r;
@@ -197,17 +201,27 @@ __device__ inline LrPair lr_pair_tab(const LrDev &p, const LrConst &k, double r,
   double drad = 0.0;
   if (ai0 >= 0.0 && aj0 >= 0.0) {
     const double ai = ai0 * hi, aj = aj0 * hj;
-    const double c6i = ci0 * hi * hi, c6j = cj0 * hj * hj;
+    const double c6i = kSepC6 ? ci0 * si : ci0 * hi * hi, c6j = kSepC6 ? cj0 * sj : cj0 * hj * hj;
     const double alpha = 0.5 * (ai + aj);
     const double num = 2.0 * c6i * c6j * aj * ai;
     const double den = ai * ai * c6j + aj * aj * c6i;
     if (alpha > 0.0 && den > 1.0e-30) {
       const double iden = 1.0 / den;
       const double c6 = num * iden;
-      const double dc6i = 2.0 * ci0 * hi;
-      const double dn_dhi = 2.0 * (dc6i * c6j * aj * ai + c6i * c6j * aj * ai0);
-      const double dd_dhi = 2.0 * ai * ai0 * c6j + aj * aj * dc6i;
-      const double dc6_dhi = (dn_dhi * den - num * dd_dhi) * (iden * iden);
+      double dc6_dhi, dc6_dsi = 0.0;
+      if (!kSepC6) {  // h_i drives both alpha_i and C6_i
+        const double dc6i = 2.0 * ci0 * hi;
+        const double dn_dhi = 2.0 * (dc6i * c6j * aj * ai + c6i * c6j * aj * ai0);
+        const double dd_dhi = 2.0 * ai * ai0 * c6j + aj * aj * dc6i;
+        dc6_dhi = (dn_dhi * den - num * dd_dhi) * (iden * iden);
+      } else {  // h_i through alpha_i only, s_i through C6_i only
+        const double dn_dai = 2.0 * c6i * c6j * aj * ai0;
+        const double dd_dai = 2.0 * ai * ai0 * c6j;
+        dc6_dhi = (dn_dai * den - num * dd_dai) * (iden * iden);
+        const double dn_dsi = 2.0 * ci0 * c6j * aj * ai;
+        const double dd_dsi = aj * aj * ci0;
+        dc6_dsi = (dn_dsi * den - num * dd_dsi) * (iden * iden);
+      }
       const double ialpha7 = inv7 / alpha;  // 1 / (7 alpha)
       const double a7 = exp_tang(log(alpha) * inv7);
       const double rv = p.fine_factor * a7;
@@ -245,6 +259,7 @@ __device__ inline LrPair lr_pair_tab(const LrDev &p, const LrConst &k, double r,
       o.e_disp = p.full_scale * p.hartree * qdo * dsw;
       drad = p.full_scale * p.hartree * (rad_au * dsw * k.inv_bohr + qdo * ddsw);
       o.dh = p.full_scale * p.hartree * dsw * dpot_dhi;
+      if (kSepC6) o.dc = p.full_scale * p.hartree * dsw * dpot_dc6 * dc6_dsi;
     }
   }
   o.radial = erad + drad;
@@ -264,11 +279,12 @@ __device__ inline double warp_sum(double v) {
 }
 
 // Cell-ordered copy of what the long-range pair term reads from a partner atom:
-// pos4[k] = (x, y, z, q) and par4[k] = (h, alpha_ref, C6_ref, 0) of atom
-// cell_atoms[k] (atom k itself for open boundaries), so that every stencil row
-// of cells is one contiguous, coalesced range of candidates.
+// pos4[k] = (x, y, z, q) and par4[k] = (h, alpha_ref, C6_ref, C6 ratio or 0)
+// of atom cell_atoms[k] (atom k itself for open boundaries), so that every
+// stencil row of cells is one contiguous, coalesced range of candidates.
 __global__ void k_lr_gather(int n, int periodic, const int *__restrict__ cell_atoms, const double *__restrict__ xw,
-                            const double *__restrict__ q, const double *__restrict__ h, const int *__restrict__ z,
+                            const double *__restrict__ q, const double *__restrict__ h,
+                            const double *__restrict__ c6r, const int *__restrict__ z,
                             const double *__restrict__ aref, const double *__restrict__ cref, int table,
                             double4 *__restrict__ pos4, double4 *__restrict__ par4) {
   const int k = blockIdx.x * blockDim.x + threadIdx.x;
@@ -277,7 +293,7 @@ __global__ void k_lr_gather(int n, int periodic, const int *__restrict__ cell_at
   const int zj = z[j] - 1;
   const bool known = zj >= 0 && zj < table;
   pos4[k] = make_double4(xw[3 * j], xw[3 * j + 1], xw[3 * j + 2], q[j]);
-  par4[k] = make_double4(h[j], known ? aref[zj] : -1.0, known ? cref[zj] : 0.0, 0.0);
+  par4[k] = make_double4(h[j], known ? aref[zj] : -1.0, known ? cref[zj] : 0.0, c6r ? c6r[j] : 0.0);
 }
 
 // One warp per atom. Lanes test 32 consecutive candidates of a contiguous
@@ -293,14 +309,16 @@ struct LrStencil {
   signed char rx[kLrMaxReach + 1][kLrMaxReach + 1];
 };
 constexpr int kLrQueue = 64;
+template <bool kSepC6>
 __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
     int n, int row0, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
     const int *__restrict__ cell_start, const int *__restrict__ cell_count, const int *__restrict__ image_of,
     const int *__restrict__ image_start, int reach, LrStencil st, double rc2, const double4 *__restrict__ pos4,
     const double4 *__restrict__ par4, const int *__restrict__ z, const double *__restrict__ q,
-    const double *__restrict__ h, const double *__restrict__ aref, const double *__restrict__ cref, int table,
-    LrDev p, double *__restrict__ e_lr, double *__restrict__ e_elec, double *__restrict__ e_disp,
-    double *__restrict__ dq, double *__restrict__ dh, double *__restrict__ f_lr, double *__restrict__ w_lr) {
+    const double *__restrict__ h, const double *__restrict__ c6r, const double *__restrict__ aref,
+    const double *__restrict__ cref, int table, LrDev p, double *__restrict__ e_lr, double *__restrict__ e_elec,
+    double *__restrict__ e_disp, double *__restrict__ dq, double *__restrict__ dh, double *__restrict__ dc6,
+    double *__restrict__ f_lr, double *__restrict__ w_lr) {
   __shared__ int qk[kLrWarps][kLrQueue];
   __shared__ double qv[kLrWarps][kLrQueue][3];
   const int wl = threadIdx.x >> 5;
@@ -309,12 +327,12 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
   if (warp >= n) return;
   const int i = row0 + warp;
   const double xi = xw[3 * i], yi = xw[3 * i + 1], zi = xw[3 * i + 2];
-  const double qi = q[i], hi = h[i];
+  const double qi = q[i], hi = h[i], si = kSepC6 ? c6r[i] : 0.0;
   const int Zi = z[i];
   const double ai0 = (Zi - 1 >= 0 && Zi - 1 < table) ? aref[Zi - 1] : -1.0;
   const double ci0 = (Zi - 1 >= 0 && Zi - 1 < table) ? cref[Zi - 1] : 0.0;
   const LrConst kc = lr_const(p);
-  double acc_ee = 0, acc_ed = 0, acc_dq = 0, acc_dh = 0, fx = 0, fy = 0, fz = 0;
+  double acc_ee = 0, acc_ed = 0, acc_dq = 0, acc_dh = 0, acc_dc = 0, fx = 0, fy = 0, fz = 0;
   double wxx = 0, wyy = 0, wzz = 0, wxy = 0, wxz = 0, wyz = 0;
   int count = 0;  // warp-uniform queue length
   auto evaluate = [&](int slot) {
@@ -322,11 +340,12 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
     const double vx = qv[wl][slot][0], vy = qv[wl][slot][1], vz = qv[wl][slot][2];
     const double r = sqrt(vx * vx + vy * vy + vz * vz);
     const double4 pj = ld4(pos4 + k), hj = ld4(par4 + k);
-    const LrPair o = lr_pair_tab(p, kc, r, qi, pj.w, hi, hj.x, ai0, hj.y, ci0, hj.z);
+    const LrPair o = lr_pair_tab<kSepC6>(p, kc, r, qi, pj.w, hi, hj.x, ai0, hj.y, ci0, hj.z, si, hj.w);
     acc_ee += o.e_elec;
     acc_ed += o.e_disp;
     acc_dq += o.dq;
     acc_dh += o.dh;
+    if (kSepC6) acc_dc += o.dc;
     const double s = o.radial / r;  // one division per pair; r is the queue's own distance
     fx += s * vx;
     fy += s * vy;
@@ -425,6 +444,7 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
   acc_ed = warp_sum(acc_ed);
   acc_dq = warp_sum(acc_dq);
   acc_dh = warp_sum(acc_dh);
+  if (kSepC6) acc_dc = warp_sum(acc_dc);
   fx = warp_sum(fx);
   fy = warp_sum(fy);
   fz = warp_sum(fz);
@@ -440,6 +460,7 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
     e_lr[i] = 0.5 * acc_ee + 0.5 * acc_ed;
     dq[i] = acc_dq;
     dh[i] = acc_dh;
+    if (kSepC6) dc6[i] = acc_dc;
     f_lr[3 * i] = fx;
     f_lr[3 * i + 1] = fy;
     f_lr[3 * i + 2] = fz;
@@ -449,12 +470,13 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
 }
 
 void launch_long_range(int n, int n_cells_atoms, const NeighborState &nb, double rc_lr, const int *z,
-                       const double *q, const double *h, const double *alpha_ref, const double *c6_ref,
-                       int table_size, LrDev p, double4 *pos4, double4 *par4, double *e_lr, double *e_elec,
-                       double *e_disp, double *dq, double *dh, double *f_lr, double *w_lr, cudaStream_t s) {
+                       const double *q, const double *h, const double *c6r, const double *alpha_ref,
+                       const double *c6_ref, int table_size, LrDev p, double4 *pos4, double4 *par4, double *e_lr,
+                       double *e_elec, double *e_disp, double *dq, double *dh, double *dc6, double *f_lr,
+                       double *w_lr, cudaStream_t s) {
   if (n == 0) return;
   k_lr_gather<<<(n_cells_atoms + 255) / 256, 256, 0, s>>>(n_cells_atoms, nb.grid.periodic, nb.cell_atoms, nb.xw, q, h,
-                                                          z, alpha_ref, c6_ref, table_size, pos4, par4);
+                                                          c6r, z, alpha_ref, c6_ref, table_size, pos4, par4);
   SO3_LAUNCH("lr_gather");
   const int reach = sr_reach(nb.grid, rc_lr);
   LrStencil st;
@@ -477,9 +499,16 @@ void launch_long_range(int n, int n_cells_atoms, const NeighborState &nb, double
   }
   const int threads = kLrWarps * 32;
   const int blocks = (n * 32 + threads - 1) / threads;
-  k_long_range<<<blocks, threads, 0, s>>>(n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count, nb.image_of,
-                                          nb.image_start, reach, st, rc_lr * rc_lr, pos4, par4, z, q, h, alpha_ref,
-                                          c6_ref, table_size, p, e_lr, e_elec, e_disp, dq, dh, f_lr, w_lr);
+  if (c6r != nullptr)
+    k_long_range<true><<<blocks, threads, 0, s>>>(n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count,
+                                                  nb.image_of, nb.image_start, reach, st, rc_lr * rc_lr, pos4, par4, z,
+                                                  q, h, c6r, alpha_ref, c6_ref, table_size, p, e_lr, e_elec, e_disp,
+                                                  dq, dh, dc6, f_lr, w_lr);
+  else
+    k_long_range<false><<<blocks, threads, 0, s>>>(n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count,
+                                                   nb.image_of, nb.image_start, reach, st, rc_lr * rc_lr, pos4, par4,
+                                                   z, q, h, nullptr, alpha_ref, c6_ref, table_size, p, e_lr, e_elec,
+                                                   e_disp, dq, dh, nullptr, f_lr, w_lr);
   SO3_LAUNCH("long_range");
 }
 

@@ -81,10 +81,14 @@ struct LrDev {
 // n: owned rows (nb.row0 ..); n_cells_atoms: atoms in the cell list (all real
 // atoms; with open boundaries, every row). pos4 / par4: n_cells_atoms-element
 // scratch for the cell-ordered partner data.
+// c6r: per-atom C6 ratios of a model with a C6 head (C6_i = C6_ref c6r_i,
+// alpha_i = alpha_ref h_i; dc6 = dE/dc6r), or nullptr (C6_i = C6_ref h_i^2, dc6
+// unused)
 void launch_long_range(int n, int n_cells_atoms, const NeighborState &nb, double rc_lr, const int *z,
-                       const double *q, const double *h, const double *alpha_ref, const double *c6_ref,
-                       int table_size, LrDev p, double4 *pos4, double4 *par4, double *e_lr, double *e_elec,
-                       double *e_disp, double *dq, double *dh, double *f_lr, double *w_lr, cudaStream_t s);
+                       const double *q, const double *h, const double *c6r, const double *alpha_ref,
+                       const double *c6_ref, int table_size, LrDev p, double4 *pos4, double4 *par4, double *e_lr,
+                       double *e_elec, double *e_disp, double *dq, double *dh, double *dc6, double *f_lr,
+                       double *w_lr, cudaStream_t s);
 
 // Allocation-free variant of the long-range step for open-boundary systems of
 // at most noalloc_max_atoms() atoms (scratch in file-scope device arrays, noalloc.cu).
@@ -195,11 +199,14 @@ void launch_qk_norm(int n, const int *rows, double *qkv, double *rinv, cudaStrea
 void launch_qk_norm_reverse(int n, const double *qkv, const double *rinv, double *g, cudaStream_t s);
 
 // heads
+// hk6_out / ratio6 (C6 ratio head keys and ratios) are written only when the
+// model has that head (hw.c6_w2 != nullptr)
 void launch_heads_finalize(int n, const int *z, const double *hcat, const HeadsW &hw, double *hk_out,
-                           double *e_nn, double *raw_q, double *ratio, cudaStream_t s);
+                           double *e_nn, double *raw_q, double *ratio, double *hk6_out, double *ratio6,
+                           cudaStream_t s);
 void launch_heads_seed(int n, const int *z, const double *hpre, const double *hk, const HeadsW &hw,
                        const double *dq, const double *dq_mean, const int *image_of_atom, const double *dh,
-                       double *g_hcat, cudaStream_t s);
+                       const double *hk6, const double *dc6, double *g_hcat, cudaStream_t s);
 
 void launch_charge_correct(int n, const double *raw, const double *raw_sum, const double *qtot,
                            const int *image_of_atom, const int *image_start, double *q, double *dq_mean_out,

@@ -531,18 +531,37 @@ void Model::describe_and_negotiate() {
       need(has_tensor(k) && tensor(k).dtype == "float64" && tensor(k).shape == std::vector<std::size_t>{std::size_t(r.layers)},
            std::string(k) + " must be a float64 vector of length interaction_blocks");
   for (const Json &h : a.at("output_heads").array()) r.output_heads.push_back(h.str());
-  need(r.output_heads == std::vector<std::string>({"atomic_energy_output_block", "partial_charges_output_block",
-                                                   "hirshfeld_output_block"}),
-       "output heads must be [atomic_energy, partial_charges, hirshfeld] (no C6 head in this build)");
+  // energy, charge and Hirshfeld (a0) heads in this order, optionally a fourth,
+  // the C6 ratio head (output_heads.cpp:273-283)
+  const std::vector<std::string> three = {"atomic_energy_output_block", "partial_charges_output_block",
+                                          "hirshfeld_output_block"};
+  std::vector<std::string> four = three;
+  four.push_back("c6_ratios_output_block");
+  need(r.output_heads == three || r.output_heads == four,
+       "output heads must be [atomic_energy, partial_charges, hirshfeld] or the same plus c6_ratios");
+  r.has_c6 = r.output_heads == four;
   r.head_hidden = has_tensor("model.atomic_energy_output_block.layers.0.weight")
                       ? int(tensor("model.atomic_energy_output_block.layers.0.weight").shape.at(0))
                       : 0;
   need(r.head_hidden == 128, "energy head hidden width must be 128");
-  if (has_tensor("model.hirshfeld_output_block.transform_features.0.weight")) {
-    r.hirshfeld_hidden = int(tensor("model.hirshfeld_output_block.transform_features.0.weight").shape.at(0));
-    r.hirshfeld_keys = int(tensor("model.hirshfeld_output_block.transform_features.2.weight").shape.at(0));
+  // ratio heads: 64 hidden units, 1..64 keys (output_heads.cpp:105-133)
+  auto ratio_head = [&](const std::string &prefix, int &hidden, int &keys) {
+    const std::string w1 = prefix + ".transform_features.0.weight", w2 = prefix + ".transform_features.2.weight";
+    if (!has_tensor(w1) || !has_tensor(w2) || tensor(w1).shape.size() != 2 || tensor(w2).shape.size() != 2) {
+      problems.push_back(prefix + ": ratio-head weights missing");
+      return;
+    }
+    hidden = int(tensor(w1).shape[0]);
+    keys = int(tensor(w2).shape[0]);
+    need(hidden == 64 && int(tensor(w1).shape[1]) == r.features && int(tensor(w2).shape[1]) == hidden &&
+             keys >= 1 && keys <= 64,
+         prefix + ": ratio heads must have 64 hidden units and 1..64 keys");
+  };
+  ratio_head("model.hirshfeld_output_block", r.hirshfeld_hidden, r.hirshfeld_keys);
+  if (r.has_c6) {
+    int c6_hidden = 0;
+    ratio_head("model.c6_ratios_output_block", c6_hidden, r.c6_keys);
   }
-  need(r.hirshfeld_hidden == 64 && r.hirshfeld_keys == 64, "Hirshfeld head must be 64x64");
   need(std::abs(r.layer_norm_eps - 1e-6) < 1e-15, "layer_norm_epsilon must be 1e-6");
   if (problems.empty()) {
     try {  // repulsion parameters and tables

@@ -65,6 +65,10 @@ struct Architecture {
   int layers = 0, features = 0, heads = 0, head_width = 0, ev_degrees = 0;
   int rbf = 0, ev_width = 0, sh_width = 0, max_degree = 0, interaction_width = 0;
   int head_hidden = 0, hirshfeld_hidden = 0, hirshfeld_keys = 0;
+  // optional fourth head: C6 ratios (dispersion C6_i = C6_ref c6_i, alpha from
+  // the Hirshfeld / a0 ratio); 0 keys when absent
+  bool has_c6 = false;
+  int c6_keys = 0;
   std::vector<int> degree_repeats, degree_offsets;
   double sr_cutoff = 0, lr_cutoff = 0, embedding_scale = 1, attention_norm = 1;
   double layer_norm_eps = 1e-6;

@@ -102,8 +102,8 @@ void long_range_noalloc(int n, const double *x, const double *q, const double *h
   double4 *par4 = pos4 + kNoAllocMaxAtoms;
   nb.row0 = 0;
   nb.n_own = n;
-  launch_long_range(n, n, nb, rc_lr, z, q, h, alpha_ref, c6_ref, table_size, p, pos4, par4, e_lr, e_elec, e_disp,
-                    dq, dh, f, w_atom, s);
+  launch_long_range(n, n, nb, rc_lr, z, q, h, nullptr, alpha_ref, c6_ref, table_size, p, pos4, par4, e_lr, e_elec,
+                    e_disp, dq, dh, nullptr, f, w_atom, s);
 }
 
 }  // namespace so3lr_b200

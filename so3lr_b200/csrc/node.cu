@@ -516,13 +516,38 @@ void launch_qk_norm_reverse(int n, const double *qkv, const double *rinv, double
 // raw q   =  hcat[128:256] . w2c + b2c + emb[Z]
 // ratio   = | v_shift[Z] + q_emb[Z] . (hcat[256:320] Wh2^T + bh2) / 8 |
 // ---------------------------------------------------------------------------
+// One ratio head (Hirshfeld / a0 or C6; 64 hidden units, keys zero-padded to
+// 64) of one atom: keys k = h1 W2^T + b2 (lane owns keys 2 lane, 2 lane + 1),
+// ratio = |v_shift[Z] + q_emb[Z] . k / sqrt(K)| (output_heads.cpp:135-176).
+__device__ inline double ratio_head(const double *__restrict__ hh, const double *__restrict__ w2t,
+                                    const double *__restrict__ b2, const double *__restrict__ qemb,
+                                    const double *__restrict__ vshift, double sqrt_k, int zz, int lane,
+                                    double *__restrict__ k_out) {
+  double k0 = b2[2 * lane], k1 = b2[2 * lane + 1];
+  double s0 = 0.0, s1 = 0.0;
+  for (int j = 0; j < kHirsh; ++j) {
+    const double hv = hh[j];
+    const double2 w = *reinterpret_cast<const double2 *>(w2t + j * kHirsh + 2 * lane);  // coalesced
+    s0 += hv * w.x;
+    s1 += hv * w.y;
+  }
+  k0 += s0;
+  k1 += s1;
+  k_out[2 * lane] = k0;
+  k_out[2 * lane + 1] = k1;
+  double qk = qemb[zz * kHirsh + 2 * lane] * k0 + qemb[zz * kHirsh + 2 * lane + 1] * k1;
+  qk = warp_sum(qk);
+  return fabs(vshift[zz] + qk / sqrt_k);
+}
+
 __global__ void k_heads_finalize(int n, const int *__restrict__ z, const double *__restrict__ hcat, HeadsW hw,
                                  double *__restrict__ hk_out, double *__restrict__ e_nn, double *__restrict__ raw_q,
-                                 double *__restrict__ ratio) {
+                                 double *__restrict__ ratio, double *__restrict__ hk6_out,
+                                 double *__restrict__ ratio6) {
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
-  const double *h = hcat + (size_t)i * kHeadCat;
+  const double *h = hcat + (size_t)i * hw.ldh;
   double se = 0.0, sq = 0.0;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -532,48 +557,68 @@ __global__ void k_heads_finalize(int n, const int *__restrict__ z, const double 
   se = warp_sum(se);
   sq = warp_sum(sq);
   const int zz = z[i];
-  // Hirshfeld keys: lane owns keys 2*lane, 2*lane+1
-  double k0 = hw.h_b2[2 * lane], k1 = hw.h_b2[2 * lane + 1];
-  const double *hh = h + 2 * kHeadHidden;
-  double s0 = 0.0, s1 = 0.0;
-  for (int j = 0; j < kHirsh; ++j) {
-    const double hv = hh[j];
-    const double2 w = *reinterpret_cast<const double2 *>(hw.h_w2t + j * kHirsh + 2 * lane);  // coalesced
-    s0 += hv * w.x;
-    s1 += hv * w.y;
-  }
-  k0 += s0;
-  k1 += s1;
-  hk_out[(size_t)i * kHirsh + 2 * lane] = k0;
-  hk_out[(size_t)i * kHirsh + 2 * lane + 1] = k1;
-  double qk = hw.h_qemb[zz * kHirsh + 2 * lane] * k0 + hw.h_qemb[zz * kHirsh + 2 * lane + 1] * k1;
-  qk = warp_sum(qk);
+  const double rh = ratio_head(h + 2 * kHeadHidden, hw.h_w2t, hw.h_b2, hw.h_qemb, hw.h_vshift, hw.h_sqrt_k, zz, lane,
+                               hk_out + (size_t)i * kHirsh);
+  double r6 = 0.0;
+  if (hw.c6_w2 != nullptr)
+    r6 = ratio_head(h + kHeadCat, hw.c6_w2t, hw.c6_b2, hw.c6_qemb, hw.c6_vshift, hw.c6_sqrt_k, zz, lane,
+                    hk6_out + (size_t)i * kHirsh);
   if (lane == 0) {
     e_nn[i] = (se + hw.e_b2) * hw.e_scale[zz - 1] + hw.e_shift[zz - 1];
     raw_q[i] = sq + hw.c_b2 + hw.c_emb[zz];
-    ratio[i] = fabs(hw.h_vshift[zz] + qk / 8.0);
+    ratio[i] = rh;
+    if (hw.c6_w2 != nullptr) ratio6[i] = r6;
   }
 }
 
 void launch_heads_finalize(int n, const int *z, const double *hcat, const HeadsW &hw, double *hk_out,
-                           double *e_nn, double *raw_q, double *ratio, cudaStream_t s) {
+                           double *e_nn, double *raw_q, double *ratio, double *hk6_out, double *ratio6,
+                           cudaStream_t s) {
   if (n == 0) return;
-  k_heads_finalize<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, z, hcat, hw, hk_out, e_nn, raw_q, ratio);
+  k_heads_finalize<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, z, hcat, hw, hk_out, e_nn, raw_q, ratio, hk6_out, ratio6);
   SO3_LAUNCH("heads_finalize");
 }
 
+// Reverse of one ratio head for one atom, seeded with d = dE/d(ratio):
+// g[j] = (sum_k g_k[k] W2[k][j]) silu'(pre[j]), g_k = d sign(eff) q_emb[Z] / sqrt(K);
+// lane owns hidden units j = 2 lane, 2 lane + 1. gk is this warp's 64-double scratch.
+__device__ inline void ratio_head_seed(const double *__restrict__ hk, const double *__restrict__ pre,
+                                       const double *__restrict__ w2, const double *__restrict__ qemb,
+                                       const double *__restrict__ vshift, double sqrt_k, double d, int zz, int lane,
+                                       double *gk, double *__restrict__ g) {
+  const double k0 = hk[2 * lane], k1 = hk[2 * lane + 1];
+  const double qe0 = qemb[zz * kHirsh + 2 * lane], qe1 = qemb[zz * kHirsh + 2 * lane + 1];
+  double eff = qe0 * k0 / sqrt_k + qe1 * k1 / sqrt_k;
+  eff = warp_sum(eff) + vshift[zz];
+  const double sign = eff > 0.0 ? 1.0 : (eff < 0.0 ? -1.0 : 0.0);
+  const double seed = d * sign / sqrt_k;
+  __syncwarp();
+  gk[2 * lane] = seed * qe0;
+  gk[2 * lane + 1] = seed * qe1;
+  __syncwarp();
+#pragma unroll
+  for (int jj = 0; jj < 2; ++jj) {
+    const int j = 2 * lane + jj;
+    double s = 0.0;
+    for (int k = 0; k < kHirsh; ++k) s += gk[k] * w2[k * kHirsh + j];
+    g[j] = s * silu_prime(pre[j]);
+  }
+}
+
 // seeds of the heads' reverse: energy seed 1, charge seed dE/dq - image mean,
-// Hirshfeld seed dE/dh (output_heads.cpp:493-581). Writes g_hcat = dL/d(pre-activation).
+// Hirshfeld seed dE/dh, C6 seed dE/dc6 (output_heads.cpp:493-581). Writes
+// g_hcat = dL/d(pre-activation).
 __global__ void k_heads_seed(int n, const int *__restrict__ z, const double *__restrict__ hpre,
                              const double *__restrict__ hk, HeadsW hw, const double *__restrict__ dq,
                              const double *__restrict__ dq_mean, const int *__restrict__ image_of,
-                             const double *__restrict__ dh, double *__restrict__ g_hcat) {
+                             const double *__restrict__ dh, const double *__restrict__ hk6,
+                             const double *__restrict__ dc6, double *__restrict__ g_hcat) {
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
   const int zz = z[i];
-  const double *pre = hpre + (size_t)i * kHeadCat;
-  double *g = g_hcat + (size_t)i * kHeadCat;
+  const double *pre = hpre + (size_t)i * hw.ldh;
+  double *g = g_hcat + (size_t)i * hw.ldh;
   const double scale = hw.e_scale[zz - 1];
   const double qseed = dq[i] - dq_mean[image_of[i]];
 #pragma unroll
@@ -582,33 +627,21 @@ __global__ void k_heads_seed(int n, const int *__restrict__ z, const double *__r
     g[c] = scale * hw.e_w2[c] * silu_prime(pre[c]);
     g[kHeadHidden + c] = qseed * hw.c_w2[c] * silu_prime(pre[kHeadHidden + c]);
   }
-  // Hirshfeld: effective = v_shift + q_emb . k / 8
-  const double k0 = hk[(size_t)i * kHirsh + 2 * lane], k1 = hk[(size_t)i * kHirsh + 2 * lane + 1];
-  const double qe0 = hw.h_qemb[zz * kHirsh + 2 * lane], qe1 = hw.h_qemb[zz * kHirsh + 2 * lane + 1];
-  double eff = qe0 * k0 / 8.0 + qe1 * k1 / 8.0;
-  eff = warp_sum(eff) + hw.h_vshift[zz];
-  const double sign = eff > 0.0 ? 1.0 : (eff < 0.0 ? -1.0 : 0.0);
-  const double seed = dh[i] * sign / 8.0;
-  // g_k = seed * q_emb; g_h1[j] = sum_k g_k[k] Wh2[k][j]; lane owns j = 2 lane, 2 lane + 1
   __shared__ double gk_s[8][kHirsh];
   const int w = (threadIdx.x >> 5);
-  gk_s[w][2 * lane] = seed * qe0;
-  gk_s[w][2 * lane + 1] = seed * qe1;
-  __syncwarp();
-#pragma unroll
-  for (int jj = 0; jj < 2; ++jj) {
-    const int j = 2 * lane + jj;
-    double s = 0.0;
-    for (int k = 0; k < kHirsh; ++k) s += gk_s[w][k] * hw.h_w2[k * kHirsh + j];
-    g[2 * kHeadHidden + j] = s * silu_prime(pre[2 * kHeadHidden + j]);
-  }
+  ratio_head_seed(hk + (size_t)i * kHirsh, pre + 2 * kHeadHidden, hw.h_w2, hw.h_qemb, hw.h_vshift, hw.h_sqrt_k,
+                  dh[i], zz, lane, gk_s[w], g + 2 * kHeadHidden);
+  if (hw.c6_w2 != nullptr)
+    ratio_head_seed(hk6 + (size_t)i * kHirsh, pre + kHeadCat, hw.c6_w2, hw.c6_qemb, hw.c6_vshift, hw.c6_sqrt_k,
+                    dc6[i], zz, lane, gk_s[w], g + kHeadCat);
 }
 
 void launch_heads_seed(int n, const int *z, const double *hpre, const double *hk, const HeadsW &hw,
                        const double *dq, const double *dq_mean, const int *image_of_atom, const double *dh,
-                       double *g_hcat, cudaStream_t s) {
+                       const double *hk6, const double *dc6, double *g_hcat, cudaStream_t s) {
   if (n == 0) return;
-  k_heads_seed<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, z, hpre, hk, hw, dq, dq_mean, image_of_atom, dh, g_hcat);
+  k_heads_seed<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, z, hpre, hk, hw, dq, dq_mean, image_of_atom, dh, hk6, dc6,
+                                                    g_hcat);
   SO3_LAUNCH("heads_seed");
 }
 

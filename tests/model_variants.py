@@ -58,11 +58,15 @@ def write_model(path, manifest: dict, tensors: list) -> pathlib.Path:
 
 def make_variant(base_path, out_path, *, rms_norm: bool = False, second_norm: bool = True, qk_norm: bool = False,
                  residual_scalars=None, nlh_capacity: int | None = None, attention_norm_factor: float = 1.0,
-                 seed: int = 0) -> pathlib.Path:
+                 c6_keys: int | None = None, hirshfeld_keys: int | None = None, seed: int = 0) -> pathlib.Path:
     """The shipped model with optional operators switched on.
 
     residual_scalars: (resid, x0) lists of length interaction_blocks, or None.
     nlh_capacity: size of the NLH pair tables (elements 1..capacity), or None.
+    c6_keys: add a C6 ratio head with this many keys (its first layer copied
+    from the Hirshfeld head, the rest seeded so that ratios stay near 1).
+    hirshfeld_keys: replace the Hirshfeld head's second layer by a seeded one
+    with this many keys (K = 1 is the a0 head of C6-head models).
     attention_norm_factor: multiplies avg_num_neighbors (the attention
     normaliser). The shipped weights were not trained for query/key
     normalisation or without the second norm; there the features grow without
@@ -91,9 +95,31 @@ def make_variant(base_path, out_path, *, rms_norm: bool = False, second_norm: bo
                 drop.add(f"model.euclidean_transformers.{b}.layer_norm_inv_2.{part}")
     if qk_norm:
         arch["qk_norm"] = True
+    rng = np.random.default_rng(seed)
+
+    def seeded_keys(prefix, keys):
+        """second layer, key embeddings and shifts of a ratio head with `keys` keys"""
+        out = {prefix + "transform_features.2.weight": 0.05 * rng.standard_normal((keys, 64)),
+               prefix + "transform_features.2.bias": 0.05 * rng.standard_normal(keys),
+               prefix + "q_embedding.weight": 0.5 * rng.standard_normal((100, keys)),
+               prefix + "v_shift_embedding.weight": 1.0 + 0.1 * rng.standard_normal((100, 1))}
+        return out
+
+    replace = {}
+    if hirshfeld_keys is not None:
+        replace.update(seeded_keys("model.hirshfeld_output_block.", int(hirshfeld_keys)))
     for key, rec in by_key.items():
         if key not in drop:
-            tensors.append((rec, base.tensors[key]))
+            tensors.append((rec, replace.get(key, base.tensors[key])))
+    if c6_keys is not None:
+        arch["output_heads"] = list(arch["output_heads"]) + ["c6_ratios_output_block"]
+        src = "model.hirshfeld_output_block."
+        dst = "model.c6_ratios_output_block."
+        new = {dst + "transform_features.0.weight": base.tensors[src + "transform_features.0.weight"],
+               dst + "transform_features.0.bias": base.tensors[src + "transform_features.0.bias"]}
+        new.update(seeded_keys(dst, int(c6_keys)))
+        for key, vals in new.items():
+            tensors.append(({"name": key, "state_key": key, "dtype": "float64", "role": "parameter"}, vals))
     if residual_scalars is not None:
         arch["use_residual_scalars"] = True
         resid, x0 = residual_scalars
@@ -103,7 +129,6 @@ def make_variant(base_path, out_path, *, rms_norm: bool = False, second_norm: bo
                             np.asarray(vals, dtype=np.float64)))
     if nlh_capacity is not None:
         arch["repulsion_type"] = "nlh"
-        rng = np.random.default_rng(seed)
         cap = int(nlh_capacity)
         amp = np.empty((cap, cap, 3))
         rate = np.empty((cap, cap, 3))

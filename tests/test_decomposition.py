@@ -163,7 +163,8 @@ def test_multi_gpu_bit_identical(world, gpu_model):
 @pytest.mark.gpu
 def test_multi_gpu_bit_identical_with_optional_operators(tmp_path):
     """A model with RMSNorm, query/key normalisation (also on the halo rows each
-    GPU projects itself), residual scalars and NLH repulsion: 2 GPUs give the
+    GPU projects itself), residual scalars, NLH repulsion and a C6 ratio head
+    (its ratios all-gathered like the Hirshfeld ratios): 2 GPUs give the
     single-GPU bits."""
     import torch
     if torch.cuda.device_count() < 2:
@@ -172,8 +173,8 @@ def test_multi_gpu_bit_identical_with_optional_operators(tmp_path):
     from so3lr_b200 import So3lrB200
     from so3lr_b200.systems import water_box
     path = make_variant(MODEL, tmp_path / "all.so3lr", rms_norm=True, qk_norm=True,
-                        residual_scalars=([0.9, 1.1, 0.8], [0.1, -0.2, 0.3]), nlh_capacity=9, seed=2,
-                        attention_norm_factor=20.0)
+                        residual_scalars=([0.9, 1.1, 0.8], [0.1, -0.2, 0.3]), nlh_capacity=9, hirshfeld_keys=1,
+                        c6_keys=1, seed=2, attention_norm_factor=20.0)
     nmol, seed = 1000, 19
     w = water_box(nmol, seed=seed)
     single = So3lrB200(path, 0)

@@ -73,7 +73,8 @@ def _rewrite(tmp_path: pathlib.Path, mutate_manifest=None, mutate_bytes=None) ->
     (lambda m: m["architecture"].__setitem__("repulsion_type", "none"), "repulsion_type"),
     (lambda m: m["architecture"].__setitem__("radial_basis_features", 64), "radial_basis_features"),
     (lambda m: m["architecture"].__setitem__("brand_new_flag", 1), "unknown architecture key"),
-    (lambda m: m["architecture"]["output_heads"].append("c6_ratios_output_block"), "output heads"),
+    (lambda m: m["architecture"]["output_heads"].append("c6_ratios_output_block"), "c6_ratios_output_block"),
+    (lambda m: m["architecture"]["output_heads"].append("dipole_vec_output_block"), "output heads"),
     (lambda m: m["architecture"].__setitem__("message_normalization", "softmax"), "message_normalization"),
     (lambda m: m.__setitem__("schema", "so3lr-native-model-v1"), "schema"),
     (lambda m: m["architecture"].__setitem__("interaction_blocks", 9), "interaction_blocks"),

@@ -1,6 +1,7 @@
 """Optional operators of other checkpoints (reference src/so3lr_capabilities.cpp:46-80):
 RMSNorm without scale, no second block norm, query/key normalisation,
-residual scalars and the NLH repulsion. Synthetic model files
+residual scalars, the NLH repulsion, ratio heads with fewer keys and the C6
+ratio head. Synthetic model files
 (tests/model_variants.py) switch each one on. CPU: the native loader accepts
 them and refuses what the reference refuses; the oracle's restatement reduces to
 the base model where it must. GPU: each variant against the oracle.
@@ -21,8 +22,10 @@ VARIANTS = {
     "qk_norm": dict(qk_norm=True, attention_norm_factor=20.0),
     "residual_scalars": dict(residual_scalars=RESID),
     "nlh": dict(nlh_capacity=10, seed=1),
-    "all": dict(rms_norm=True, qk_norm=True, residual_scalars=RESID, nlh_capacity=9, seed=2,
-                attention_norm_factor=20.0),
+    "c6_head": dict(c6_keys=64, seed=3),
+    "a0_c6_one_key": dict(hirshfeld_keys=1, c6_keys=1, seed=4),
+    "all": dict(rms_norm=True, qk_norm=True, residual_scalars=RESID, nlh_capacity=9, hirshfeld_keys=1, c6_keys=1,
+                seed=2, attention_norm_factor=20.0),
 }
 
 
@@ -157,5 +160,6 @@ def test_gpu_variant_matches_oracle(name, variant_dir):
             assert np.abs(r["forces"] - o["forces"]).max() <= 1e-9 * (1 + fmax), case
             assert np.abs(r["virial"] - o["virial"]).max() <= 1e-8 * (1 + np.abs(o["virial"]).max()), case
             assert np.abs(r["charges"] - o["partial_charges"]).max() <= 1e-10, case
+            assert np.abs(r["ratios"] - o["hirshfeld_ratios"]).max() <= 1e-10, case
     finally:
         g.close()
