@@ -255,12 +255,21 @@ class So3lrB200:
         return fr, x, z
 
     def compute(self, x, z, cell=None, boxlo=None, charge: float = 0.0, multiplicity: float = 1.0,
-                terms: bool = True) -> dict:
+                terms: bool = True, forces_out=None) -> dict:
+        """forces_out: optional caller-owned (n, 3) float64 C-contiguous array
+        (page-locked host memory makes the copy a direct DMA) that receives the
+        forces; returned as out["forces"]."""
         fr, x, z = self._frame(x, z, cell, boxlo, charge, multiplicity)
         n = len(z)
         out = {k: np.empty(n) for k in ("eatom", "charges", "ratios", "e_learned", "e_zbl", "e_lr", "e_elec",
                                         "e_disp")} if terms else {}
-        out["forces"] = np.empty((n, 3))
+        if forces_out is not None:
+            if (forces_out.shape != (n, 3) or forces_out.dtype != np.float64
+                    or not forces_out.flags["C_CONTIGUOUS"]):
+                raise ValueError("forces_out must be a C-contiguous float64 array of shape (natoms, 3)")
+            out["forces"] = forces_out
+        else:
+            out["forces"] = np.empty((n, 3))
         res = Result()
         res.f = _ptr(out["forces"])
         for k in ("eatom", "charges", "ratios", "e_learned", "e_zbl", "e_lr", "e_elec", "e_disp"):
