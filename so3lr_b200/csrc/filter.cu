@@ -14,10 +14,12 @@
 // linear in the incoming gradient, so the two directions' gradients are summed
 // first and pushed through the MLP once.
 //
-// Tile: 64 pairs per CTA, 8 warps, each warp owns a 32x32 block of the 64x128
-// output and issues m16n8k8 DMMA on fragments read from shared memory (pair
-// activations, one 16-byte load per row) and L2-resident weights prepared in
-// fragment order (four 16-byte loads per lane and k-step).
+// Tile: 64 pairs per CTA, 8 warps, m16n8k8 DMMA on fragments read from shared
+// memory (pair activations, one 16-byte load per row) and L2-resident weights
+// prepared in fragment order (16-byte loads per lane and k-step). The 128-wide
+// GEMMs give each warp a 64x16 column slab of the 64x128 output, so every
+// weight column is fetched from L2 by one warp of the CTA only; the 32-wide
+// ones use 16x16 warp blocks.
 #include <cooperative_groups.h>
 
 #include "kernels.cuh"
@@ -34,9 +36,10 @@ constexpr int LDU = 136;   // 128-wide tiles
 constexpr int LDR = 40;    // 32-wide tiles
 
 // silu'(hidden pre-activation) of the rbf branch, written by the forward and
-// read by the reverse in the accumulator order of their common warp tiling:
-// [tile][filter][warp][mi][ni][half][lane][2] (64 x 128 values per tile and
-// filter, 512 contiguous bytes per warp and (mi, ni, half))
+// read by the reverse in accumulator order:
+// [tile][filter][block][mi][ni][half][lane][2] with 32 x 32 blocks (block =
+// 4 (row / 32) + col / 32; 512 contiguous bytes per block and (mi, ni, half)).
+// A 64x16 warp slab's m16n8 block (mi, ni) is one such 512-byte run.
 __device__ __forceinline__ size_t sp_offset(int tile, int filt, int warp) {
   return (((size_t)tile * 2 + filt) * 8 + warp) * (16 * 64);
 }
@@ -85,22 +88,24 @@ __device__ __forceinline__ void load_bfrag(const double *__restrict__ Bf, int ks
   }
 }
 
-// warp tile 32 x 32 (rows 32 wm.., cols 32 wn..) as 2 x 4 m16n8 blocks:
+// warp tile 64 x 16 (all 64 rows, cols 16 wc..) as 4 x 2 m16n8 blocks: each
+// weight column is read by one warp of the CTA only
 // acc += A(64 x K, smem, row stride lda) * B(K x 128, fragment-major)
 template <int K>
-__device__ inline void mma_32x32(double (&acc)[2][4][4], const double *A, int lda, const double *__restrict__ Bf,
-                                 int wm, int wn, int lane) {
+__device__ inline void mma_64x16(double (&acc)[4][2][4], const double *A, int lda, const double *__restrict__ Bf,
+                                 int wc, int lane) {
   const int g = lane >> 2, t = lane & 3;
 #pragma unroll 2
   for (int ks = 0; ks < K / 8; ++ks) {
-    double a[2][4], b[4][2];
-    load_afrag(A, lda, wm * 32, ks, g, t, a[0]);
-    load_afrag(A, lda, wm * 32 + 16, ks, g, t, a[1]);
-    load_bfrag<4>(Bf, ks, 4, wn, 0, lane, b);
+    double b[2][2];
+    load_bfrag<2>(Bf, ks, 4, wc >> 1, (wc & 1) * 2, lane, b);
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi)
+    for (int mi = 0; mi < 4; ++mi) {
+      double a[4];
+      load_afrag(A, lda, mi * 16, ks, g, t, a);
 #pragma unroll
-      for (int ni = 0; ni < 4; ++ni) dmma16(acc[mi][ni], a[mi], b[ni]);
+      for (int ni = 0; ni < 2; ++ni) dmma16(acc[mi][ni], a, b[ni]);
+    }
   }
 }
 
@@ -152,7 +157,6 @@ __global__ void __launch_bounds__(256, 2) k_filter_forward(int P, const double *
   double *rr = l0 + TP * 4;       // TP
   const int p0 = blockIdx.x * TP;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-  const int wm = warp >> 2, wn = warp & 3;
   if (tid < TP) {
     const int p = p0 + tid;
     rr[tid] = p < P ? geo[(size_t)p * kGeo] : 1.0;
@@ -193,45 +197,46 @@ __global__ void __launch_bounds__(256, 2) k_filter_forward(int P, const double *
         w[pl * LDR + j] = silu(s + W.c0[j]);
       }
     }
-    double acc[2][4][4];
+    double acc[4][2][4];
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi)
+    for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
-      for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.0;
-    mma_32x32<kR>(acc, rbf, LDR, W.w0t_f, wm, wn, lane);
+      for (int ni = 0; ni < 2; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.0;
+    mma_64x16<kR>(acc, rbf, LDR, W.w0t_f, warp, lane);
     // hidden layer u = silu(pre) to shared memory, and silu'(pre) for the
-    // reverse pass straight from the accumulators in fragment order
-    double *sp_tile = sp + sp_offset(blockIdx.x, filt, warp);
+    // reverse pass in the accumulator order of the reverse's 32 x 32 warp tiling
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi)
+    for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
-      for (int ni = 0; ni < 4; ++ni) {
-        const int col = wn * 32 + ni * 8 + 2 * t;
+      for (int ni = 0; ni < 2; ++ni) {
+        const int col = warp * 16 + ni * 8 + 2 * t;
         const double bb0 = W.b0[col], bb1 = W.b0[col + 1];
+        double *sp_blk = sp + sp_offset(blockIdx.x, filt, (mi >> 1) * 4 + (warp >> 1)) +
+                         (((mi & 1) * 4 + (warp & 1) * 2 + ni) * 2) * 64;
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {  // rows g and g + 8 of the m16 block
-          const int row = wm * 32 + mi * 16 + hf * 8 + g;
+          const int row = mi * 16 + hf * 8 + g;
           const double x0 = acc[mi][ni][2 * hf] + bb0, x1 = acc[mi][ni][2 * hf + 1] + bb1;
           const double s0 = sigmoid(x0), s1 = sigmoid(x1);
           *reinterpret_cast<double2 *>(u + row * LDU + col) = make_double2(x0 * s0, x1 * s1);
-          *reinterpret_cast<double2 *>(sp_tile + ((mi * 4 + ni) * 2 + hf) * 64 + lane * 2) =
+          *reinterpret_cast<double2 *>(sp_blk + hf * 64 + lane * 2) =
               make_double2(s0 * (1.0 + x0 * (1.0 - s0)), s1 * (1.0 + x1 * (1.0 - s1)));
         }
         acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.0;
       }
     __syncthreads();
-    mma_32x32<kF>(acc, u, LDU, W.w1t_f, wm, wn, lane);
-    mma_32x32<kEH>(acc, w, LDR, W.v1t_f, wm, wn, lane);
+    mma_64x16<kF>(acc, u, LDU, W.w1t_f, warp, lane);
+    mma_64x16<kEH>(acc, w, LDR, W.v1t_f, warp, lane);
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi)
+    for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        const int row = wm * 32 + mi * 16 + hf * 8 + g;
+        const int row = mi * 16 + hf * 8 + g;
         const int p = p0 + row;
         if (p >= P) continue;
 #pragma unroll
-        for (int ni = 0; ni < 4; ++ni) {
-          const int col = wn * 32 + ni * 8 + 2 * t;
+        for (int ni = 0; ni < 2; ++ni) {
+          const int col = warp * 16 + ni * 8 + 2 * t;
           double2 v;
           v.x = acc[mi][ni][2 * hf] + W.bc1[col];
           v.y = acc[mi][ni][2 * hf + 1] + W.bc1[col + 1];
@@ -310,14 +315,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
   const int tile = blockIdx.x >> 1;
   const int p0 = tile * TP;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-  const int wm = warp >> 2, wn = warp & 3;
   // this CTA's filter (selected field by field so the parameters stay in registers)
   const double *w1_f = f ? fev.w1_f : finv.w1_f;
   const double *v1_f = f ? fev.v1_f : finv.v1_f;
   const double *w0_f = f ? fev.w0_f : finv.w0_f;
   const double *v0 = f ? fev.v0 : finv.v0;
   const double *c0 = f ? fev.c0 : finv.c0;
-  const double *sp_tile = sp + sp_offset(tile, f, warp);
+  const double *sp_tile = sp + sp_offset(tile, f, warp);  // prefetched below; read in slab order
 
   stage_rows<kF>(gF, LDU, f ? g_filt_ev : g_filt_inv, p0, P);
   cp_async_commit();
@@ -329,23 +333,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
   cp_async_wait<0>();
   __syncthreads();
 
-  // gradient of the hidden layer: (gF W1) * silu'(pre), warp tile 32 x 32
-  double acc[2][4][4];
+  // gradient of the hidden layer: (gF W1) * silu'(pre), warp slab 64 x 16
+  // (hidden units 16 warp ..); silu' is stored in the 32 x 32 warp-block order
+  // (sp_offset), whose (warp, mi, ni) block this slab's (mi, ni) maps to
+  double acc[4][2][4];
 #pragma unroll
-  for (int mi = 0; mi < 2; ++mi)
+  for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
-    for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.0;
-  mma_32x32<kF>(acc, gF, LDU, w1_f, wm, wn, lane);
+    for (int ni = 0; ni < 2; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.0;
+  mma_64x16<kF>(acc, gF, LDU, w1_f, warp, lane);
 #pragma unroll
-  for (int mi = 0; mi < 2; ++mi)
+  for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
-    for (int ni = 0; ni < 4; ++ni)
+    for (int ni = 0; ni < 2; ++ni) {
+      const double *sp_blk = sp + sp_offset(tile, f, (mi >> 1) * 4 + (warp >> 1)) +
+                             (((mi & 1) * 4 + (warp & 1) * 2 + ni) * 2) * 64;
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        const double2 s = __ldg(reinterpret_cast<const double2 *>(sp_tile + ((mi * 4 + ni) * 2 + hf) * 64 + lane * 2));
+        const double2 s = __ldg(reinterpret_cast<const double2 *>(sp_blk + hf * 64 + lane * 2));
         acc[mi][ni][2 * hf] *= s.x;
         acc[mi][ni][2 * hf + 1] *= s.y;
       }
+    }
   // ev branch: g_w = gF V1 (64 x 32), warp tile 16 x 16
   const int wr = warp >> 1, wc = warp & 1;
   double gwa[2][4];
@@ -360,53 +369,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
       *reinterpret_cast<double2 *>(gw + row * LDR + col) = make_double2(gwa[j][2 * hf], gwa[j][2 * hf + 1]);
     }
   __syncthreads();  // every warp is done reading gF
-  // radial-basis gradient g_rbf = g_pre W0 (64 x 32). Each warp multiplies the
-  // g_pre block it holds (rows 32 wm.., columns j = 32 wn..) by rows 32 wn.. of
-  // W0 straight from its accumulators: under the kernels' k-slot permutation an
-  // m16n8k8 accumulator block {c0, c2, c1, c3} is the A fragment of one k-step.
-  // The four partial products of a row block (wn = 0..3) go to shared memory in
-  // fragment order and are summed there in that fixed order.
-  double *red = gF;  // [2 wm][4 wn][32 values][32 lanes]
+  // the hidden pre-activation gradient replaces gF in shared memory
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {  // output columns 16 half .. 16 half + 15
-    double part[2][2][4];
+  for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
-    for (int mi = 0; mi < 2; ++mi)
+    for (int ni = 0; ni < 2; ++ni)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) part[mi][j][0] = part[mi][j][1] = part[mi][j][2] = part[mi][j][3] = 0.0;
-#pragma unroll
-    for (int ni = 0; ni < 4; ++ni) {
-      double b[2][2];
-      load_bfrag<2>(w0_f, wn * 4 + ni, 1, 0, 2 * half, lane, b);
-#pragma unroll
-      for (int mi = 0; mi < 2; ++mi) {
-        const double a[4] = {acc[mi][ni][0], acc[mi][ni][2], acc[mi][ni][1], acc[mi][ni][3]};
-#pragma unroll
-        for (int j = 0; j < 2; ++j) dmma16(part[mi][j], a, b[j]);
+      for (int hf = 0; hf < 2; ++hf) {
+        const int row = mi * 16 + hf * 8 + g, col = warp * 16 + ni * 8 + 2 * t;
+        *reinterpret_cast<double2 *>(gF + row * LDU + col) = make_double2(acc[mi][ni][2 * hf], acc[mi][ni][2 * hf + 1]);
       }
-    }
-#pragma unroll
-    for (int mi = 0; mi < 2; ++mi)
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int v = 0; v < 4; ++v)
-          red[((wm * 4 + wn) * 32 + (mi * 4 + 2 * half + j) * 4 + v) * 32 + lane] = part[mi][j][v];
-  }
   __syncthreads();
-  // warp (rm, q) sums values 8q..8q+7 of row block rm over the four partials
-  double grb[8];
-  {
-    const int rm = warp >> 2, q = warp & 3;
+  // radial-basis gradient g_rbf = g_pre W0 (64 x 32), warp tile 16 x 16
+  double grb[2][4];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int idx = 8 * q + k;
-      double s = red[((rm * 4 + 0) * 32 + idx) * 32 + lane];
-#pragma unroll
-      for (int w2 = 1; w2 < 4; ++w2) s += red[((rm * 4 + w2) * 32 + idx) * 32 + lane];
-      grb[k] = s;
-    }
-  }
+  for (int j = 0; j < 2; ++j) grb[j][0] = grb[j][1] = grb[j][2] = grb[j][3] = 0.0;
+  mma_16x16<kF>(grb, gF, LDU, wr * 16, w0_f, wc, lane);
   // L0 gradient: g_pe = g_w * silu'(L0 V0^T + c0), gl[d] = sum_j g_pe[j] V0[j][d]
   if (need_l0) {
     {
@@ -425,17 +403,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
     for (int j = 0; j < kEH; ++j) s += gw[pl * LDR + j] * v0[j * 4 + d];
     gl[pl * 4 + d] = s;
   }
-  __syncthreads();  // gw and the partial sums are read
-  {
-    const int rm = warp >> 2, q = warp & 3;
+  __syncthreads();  // gw is read
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int idx = 8 * q + k;
-      const int mi = idx >> 4, rb = (idx >> 2) & 3, v = idx & 3;
-      const int row = rm * 32 + mi * 16 + (v >> 1) * 8 + g, col = rb * 8 + 2 * t + (v & 1);
-      gw[row * LDR + col] = grb[k];
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int row = wr * 16 + hf * 8 + g, col = wc * 16 + j * 8 + 2 * t;
+      *reinterpret_cast<double2 *>(gw + row * LDR + col) = make_double2(grb[j][2 * hf], grb[j][2 * hf + 1]);
     }
-  }
   // rank 0 prefetches the per-pair inputs of the radial and harmonic gradients
   // into the free gF region
   double *sc = gF;                        // TP x 32 pair scalars
