@@ -4,57 +4,17 @@ RMSNorm without scale, no second block norm, query/key normalisation,
 residual scalars and the NLH pair-table repulsion. No released checkpoint uses
 them, so each variant is the shipped model with the manifest flags switched,
 the tensors the operator needs added (seeded values) and the tensors it no
-longer reads removed. The writer produces the container layout the loaders
-check (native_model.cpp:338-405): 128-byte header, canonical JSON manifest,
-64-byte aligned tensors with per-tensor SHA-256.
+longer reads removed, written by so3lr_b200.model_file.write_model.
 """
 from __future__ import annotations
 
 import copy
-import hashlib
-import json
 import pathlib
-import struct
 
 import numpy as np
 
 from oracle.model_io import load_model
-
-_NP = {"float64": "<f8", "float32": "<f4", "int64": "<i8", "int32": "<i4", "uint8": "u1", "bool": "u1"}
-
-
-def write_model(path, manifest: dict, tensors: list) -> pathlib.Path:
-    """tensors: list of (record, array) in file order; record holds name,
-    state_key, dtype, role; shape, offset, nbytes and sha256 are filled here."""
-    manifest = copy.deepcopy(manifest)
-    payload = bytearray()
-    records = []
-    for rec, arr in tensors:
-        rec = dict(rec)
-        arr = np.array(arr, dtype=_NP[rec["dtype"]], order="C")  # keeps 0-d tensors 0-d
-        while len(payload) % 64:
-            payload.append(0)
-        blob = arr.tobytes()
-        rec["shape"] = [int(s) for s in arr.shape]
-        rec["offset"] = len(payload)
-        rec["nbytes"] = len(blob)
-        rec["sha256"] = hashlib.sha256(blob).hexdigest()
-        payload += blob
-        records.append(rec)
-    manifest["tensors"] = records
-    manifest["tensor_count"] = len(records)
-    manifest["tensor_bytes"] = sum(r["nbytes"] for r in records)
-    manifest["architecture"]["state_tensor_count"] = len(records)
-    mbytes = json.dumps(manifest, sort_keys=True, separators=(",", ":"), ensure_ascii=False).encode("utf-8")
-    header = bytearray(128)
-    header[0:8] = b"SO3LRN1\x00"
-    struct.pack_into("<IIQQ", header, 8, 1, 0, len(mbytes), len(payload))
-    header[32:64] = hashlib.sha256(mbytes).digest()
-    header[64:96] = hashlib.sha256(bytes(payload)).digest()
-    path = pathlib.Path(path)
-    path.write_bytes(bytes(header) + mbytes + bytes(payload))
-    return path
-
+from so3lr_b200.model_file import write_model
 
 def make_variant(base_path, out_path, *, rms_norm: bool = False, second_norm: bool = True, qk_norm: bool = False,
                  residual_scalars=None, nlh_capacity: int | None = None, attention_norm_factor: float = 1.0,

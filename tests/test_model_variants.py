@@ -12,7 +12,8 @@ import numpy as np
 import pytest
 
 from conftest import MODEL
-from model_variants import make_variant, write_model
+from model_variants import make_variant
+from so3lr_b200.model_file import write_model
 
 RESID = ([0.9, 1.1, 0.8], [0.1, -0.2, 0.3])
 
@@ -62,6 +63,29 @@ def test_writer_round_trips_the_shipped_model(variant_dir):
         a, b = base.tensors[r["state_key"]], copy.tensors[r["state_key"]]
         assert a.shape == b.shape and a.dtype == b.dtype and a.tobytes() == b.tobytes(), r["state_key"]
     assert _inspect(path)[0] == 0
+
+
+def test_model_file_tool(variant_dir, capsys):
+    """python -m so3lr_b200.model_file: PASS and the summary for the shipped
+    model, FAIL with the loader's message for a corrupted copy; its tensor
+    reader agrees with the oracle's."""
+    from oracle.model_io import load_model
+    from so3lr_b200 import model_file
+    assert model_file.main([str(MODEL), "--manifest", str(variant_dir / "manifest.json")]) == 0
+    out = capsys.readouterr().out
+    assert "native_model_check=PASS" in out and "tensor_count=213" in out and "long_range_cutoff=12.0" in out
+    assert '"model_family": "SO3LR"' in (variant_dir / "manifest.json").read_text()
+    data = bytearray(MODEL.read_bytes())
+    data[-3] ^= 0x40
+    bad = variant_dir / "corrupt.so3lr"
+    bad.write_bytes(bytes(data))
+    assert model_file.main([str(bad)]) == 1
+    assert "SHA-256" in capsys.readouterr().out
+    ref = load_model(str(MODEL)).tensors
+    mine = model_file.tensors(MODEL)
+    assert ref.keys() == mine.keys()
+    for k in ref:
+        assert ref[k].shape == mine[k].shape and np.array_equal(ref[k], mine[k]), k
 
 
 @pytest.mark.parametrize("name", sorted(VARIANTS))
