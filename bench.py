@@ -16,11 +16,14 @@ Printed JSON line (rank 0):
   roofline  the pair-filter MLP kernels (the dominant FP64 tensor-core work),
           timed with CUDA events on the library's stream during the timed region,
           against the FP64 DGEMM throughput measured on this GPU before timing
+  step_roofline  the whole step's FP64 work (the reference algorithm's FLOP
+          count and the FLOP this build executes) against the FP64 peak
   cpu_baseline  the float64 CPU restatement (oracle/) on a bounded sample
 For N > 1 (torchrun) the box grows with N (N x 8,000 molecules, weak scaling:
 24,000 atoms per GPU, 192,000 atoms at N = 8 as in config 4) and is split into
 N spatial bricks; each rank owns the atoms of its brick, evaluates their pairs,
-and the library exchanges the owned rows with NCCL all-gathers. The N > 1 runs
+and the library exchanges rows with NCCL (all-gathers of positions, charges and
+ratios; send/receive of the halo rows of block features and adjoints). The N > 1 runs
 are NVT with a Nose-Hoover chain at 300 K (config 4). Times are the max over
 ranks.
 
@@ -301,6 +304,7 @@ def run_ours(args) -> None:
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
         steps_per_s = args.steps / (ms_max * 1e-3)
+        lr_pairs = count_lr_pairs(w.pos, w.boxlo, w.cell, 12.0)  # host only, after every timed region
         line = {
             "metric": "atom-steps/s", "value": value, "unit": "atom-steps/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
@@ -328,6 +332,10 @@ def run_ours(args) -> None:
                                                         / max(1e-12, (prof[1] if dom is prof[0] else prof[0])["ms"] * 1e-3)
                                                         / 1e12)},
                                    "filter_share_of_step": (prof[0]["ms"] + prof[1]["ms"]) / ms}},
+            # edge and pair counts are this rank's (its own rows and their halo
+            # pairs); the work of the other ranks' equal bricks is taken as the same
+            "step_roofline": step_roofline(n / world, stats["sr_edges"], stats["sr_pairs"], lr_pairs / world,
+                                           steps_per_s, peak, world),
             "cpu_baseline": cpu,
             "clocks": clock_info,
             "gpu_launches": launches,
@@ -338,6 +346,34 @@ def run_ours(args) -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def count_lr_pairs(pos, boxlo, cell, cutoff: float) -> int:
+    """Unordered atom pairs within the long-range cutoff (periodic minimum image
+    and beyond: every image inside the cutoff counts), counted on the host with
+    a k-d tree before the timed region."""
+    from scipy.spatial import cKDTree
+    x = np.mod(np.asarray(pos) - np.asarray(boxlo), np.asarray(cell))
+    tree = cKDTree(x, boxsize=np.asarray(cell))
+    return int((tree.count_neighbors(tree, cutoff) - len(x)) // 2)
+
+
+def step_roofline(n, sr_edges, sr_pairs, lr_pairs, steps_per_s, peak, world):
+    """Whole-step FP64 work against the FP64 peak of all GPUs (n, edges, pairs:
+    one rank's share). Reference-algorithm FLOP per
+    step (filters per directed edge and block: 197,632 forward + reverse, plus
+    about 6k for attention, L0 and radial terms; node GEMMs 288 kFLOP per atom
+    and block; heads 181 kFLOP per atom; 250 FLOP per long-range half pair) and
+    the FLOP this build executes (filters once per pair; each long-range pair
+    evaluated from both of its atoms)."""
+    ref = world * (3 * sr_edges * 203.6e3 + 3 * n * 288e3 + n * 181e3 + 250 * lr_pairs)
+    executed = world * (3 * sr_pairs * 197_632 + 3 * sr_edges * 6.0e3 + 3 * n * 288e3 + n * 181e3
+                        + 2 * 250 * lr_pairs)
+    return {"reference_flop_per_step": ref, "executed_flop_per_step": executed, "lr_half_pairs": lr_pairs * world,
+            "executed_tflops": executed * steps_per_s / 1e12,
+            "reference_equivalent_tflops": ref * steps_per_s / 1e12,
+            "frac_executed": executed * steps_per_s / 1e12 / (peak * world) if peak else None,
+            "peak_tflops_per_gpu": peak, "unit": "TFLOP/s"}
 
 
 def main():
