@@ -164,25 +164,35 @@ def run_reference(args) -> None:
     from oracle.so3lr_oracle import OracleModel, System, evaluate
     from so3lr_b200.systems import water_box
     om = OracleModel.load(str(ROOT / "models" / "so3lr.so3lr"))
-    w = water_box(216, seed=7)
-    s = System(pos=w.pos, z=w.z, cell=w.cell)
+    if args.config == 5:
+        from so3lr_b200.systems import turbo_batch
+        pos, z, off, q, mult = turbo_batch(32, seed=7)
+        image = np.repeat(np.arange(len(off) - 1), np.diff(off))
+        s = System(pos=pos, z=z, image=image, image_charge=q, image_multiplicity=mult)
+        n_sample, what = len(z), "a 32-cluster pack"
+        n_atoms = int(len(turbo_batch(TURBO_CLUSTERS, seed=7)[1]))
+        desc = f"config5: NVE MD of a turbo pack of {TURBO_CLUSTERS} water clusters ({n_atoms} atoms)"
+    else:
+        w = water_box(216, seed=7)
+        s = System(pos=w.pos, z=w.z, cell=w.cell)
+        n_sample, what = len(w.z), "a 648-atom periodic water box (216 H2O)"
+        n_atoms, desc = CONFIGS[args.config][0] * 3, CONFIGS[args.config][1]
     for _ in range(args.warmup):
         evaluate(om, s)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         evaluate(om, s)
     dt = time.perf_counter() - t0
-    value = len(w.z) * args.steps / dt
-    n_atoms, desc = CONFIGS[args.config][0] * 3, CONFIGS[args.config][1]
+    value = n_sample * args.steps / dt
     cores = torch.get_num_threads()
-    sample = (f"each step = one energy+force evaluation of a 648-atom periodic water box (216 H2O), a bounded "
+    sample = (f"each step = one energy+force evaluation of {what}, a bounded "
               f"sample of the {n_atoms}-atom workload, by the float64 CPU restatement of the reference kernels "
               f"(oracle/, torch CPU, {cores} threads); the reference's Kokkos/cuBLAS code has no CPU build")
     line = {
         "impl": "reference", "metric": "atom-steps/s", "value": value, "unit": "atom-steps/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": desc, "sample_atoms": len(w.z)},
+        "config": {"workload": desc, "sample_atoms": n_sample},
         "cpu_baseline": {"value": value, "unit": "atom-steps/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "atom-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -348,6 +358,121 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+TURBO_CLUSTERS = 4096
+
+
+def run_turbo(args) -> None:
+    """Config 5: a pack of 4,096 water clusters (4-16 H2O; half neutral, a
+    quarter OH-, a quarter H3O+), open boundaries, NVE velocity Verlet at 0.5 fs
+    through so3lr_compute_batch with host buffers (the turbo path has no
+    device-resident loop, so value and e2e are the same measurement). Under
+    torchrun the clusters are dealt to the ranks largest first, round robin;
+    the ranks never communicate (the reference gathers every image to one
+    coordinator rank instead, mpi_turbo_replica_broker.cpp:130-307)."""
+    import torch
+    import torch.distributed as dist
+    from so3lr_b200 import So3lrB200
+    from so3lr_b200.systems import MASS, maxwell_boltzmann, turbo_batch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        tt = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        return float(tt.item())
+
+    pos, z, off, q, mult = turbo_batch(TURBO_CLUSTERS, seed=7)
+    sizes = np.diff(off)
+    mine = np.argsort(-sizes, kind="stable")[rank::world]
+    x = np.concatenate([pos[off[k]:off[k + 1]] for k in mine])
+    zz = np.ascontiguousarray(np.concatenate([z[off[k]:off[k + 1]] for k in mine]), dtype=np.int32)
+    my_off = np.concatenate([[0], np.cumsum(sizes[mine])]).astype(np.int64)
+    my_q, my_m = q[mine], mult[mine]
+    n, n_total = len(zz), int(len(z))
+    mass = np.array([MASS[int(v)] for v in zz])
+    peak = measure_fp64_peak(local)
+    model = So3lrB200(ROOT / "models" / "so3lr.so3lr", local)
+    x_host = torch.empty((n, 3), dtype=torch.float64, pin_memory=True).numpy()
+    v_host = torch.empty((n, 3), dtype=torch.float64, pin_memory=True).numpy()
+    x_host[:] = x
+    v_host[:] = maxwell_boltzmann(mass, 300.0, seed=11 + rank)
+    kick = np.ascontiguousarray(np.broadcast_to((0.5 * DT_PS / 1.0364269e-4 / mass)[:, None], (n, 3)))
+    tmp = np.empty((n, 3))
+
+    def step(f):
+        np.multiply(f, kick, out=tmp)
+        v_host += tmp
+        np.multiply(v_host, DT_PS, out=tmp)
+        x_host += tmp
+        f = model.compute_batch(x_host, zz, my_off, my_q, my_m)["forces"]
+        np.multiply(f, kick, out=tmp)
+        v_host += tmp
+        return f
+
+    f = model.compute_batch(x_host, zz, my_off, my_q, my_m)["forces"]
+    for _ in range(args.warmup):
+        f = step(f)
+    stats = model.stats()
+    model.profile(True)
+    for k in (0, 1):
+        model.profile_read(k)
+    launches0 = model.launch_count()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        f = step(f)
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    clock_info = clocks.stop()
+    launches = model.launch_count() - launches0
+    prof = [model.profile_read(k) for k in (0, 1)]
+    model.profile(False)
+    t_max = max_over_ranks(elapsed)
+    value = n_total * args.steps / t_max
+    if rank == 0:
+        dom = max(prof, key=lambda p_: p_["ms"])
+        achieved = dom["flops"] / (dom["ms"] * 1e-3) / 1e12 if dom["ms"] > 0 else 0.0
+        line = {
+            "metric": "atom-steps/s", "value": value, "unit": "atom-steps/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_max * 1e3 / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": f"config5: NVE MD of a turbo pack of {TURBO_CLUSTERS} water clusters "
+                                   f"({n_total} atoms; 4-16 H2O, 50% neutral, 25% OH-, 25% H3O+), open boundaries, "
+                                   f"0.5 fs, float64, through so3lr_compute_batch with host buffers",
+                       "atoms": n_total, "atoms_rank0": n, "images_rank0": int(len(mine)),
+                       "sr_edges_rank0": stats["sr_edges"], "sr_pairs_rank0": stats["sr_pairs"],
+                       "parallelism": "single" if world == 1 else
+                       f"{world} independent GPUs, clusters dealt largest first, no communication",
+                       "l2": "no flush: per-step working set exceeds L2"},
+            "e2e": {"value": value, "unit": "atom-steps/s", "h2d_bytes_per_step": (3 * 8 + 4) * n_total,
+                    "d2h_bytes_per_step": (3 + 1 + 1) * 8 * n_total + 8 * TURBO_CLUSTERS},
+            "roofline": {"bound": "tensor", "kernel": "filter_forward" if dom is prof[0] else "filter_reverse",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak if peak else None, "traffic": None,
+                         "peak_source": "FP64 cuBLAS DGEMM 8192^3 measured on this GPU before the timed region"},
+            "cpu_baseline": None,
+            "clocks": clock_info,
+            "gpu_launches": launches,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def count_lr_pairs(pos, boxlo, cell, cutoff: float) -> int:
     """Unordered atom pairs within the long-range cutoff (periodic minimum image
     and beyond: every image inside the cutoff counts), counted on the host with
@@ -382,13 +507,16 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, choices=[1, 2, 3], default=3)
+    ap.add_argument("--config", type=int, choices=[1, 2, 3, 5], default=3,
+                    help="3 (default): the headline 24,000-atom box; 5: the turbo cluster pack")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == 5:
+        run_turbo(args)
     else:
         run_ours(args)
 
