@@ -412,12 +412,12 @@ def run_turbo(args) -> None:
 
     def step(f):
         np.multiply(f, kick, out=tmp)
-        v_host += tmp
+        np.add(v_host, tmp, out=v_host)
         np.multiply(v_host, DT_PS, out=tmp)
-        x_host += tmp
+        np.add(x_host, tmp, out=x_host)
         f = model.compute_batch(x_host, zz, my_off, my_q, my_m)["forces"]
         np.multiply(f, kick, out=tmp)
-        v_host += tmp
+        np.add(v_host, tmp, out=v_host)
         return f
 
     f = model.compute_batch(x_host, zz, my_off, my_q, my_m)["forces"]
