@@ -34,13 +34,29 @@ __device__ inline void for_each_candidate(int i, const double *__restrict__ xw, 
                                           const int *__restrict__ image_of, const int *__restrict__ image_start,
                                           int reach, const int *__restrict__ tag, Visit &&visit) {
   const double xi = xw[3 * i], yi = xw[3 * i + 1], zi = xw[3 * i + 2];
-  if (!g.periodic) {
+  if (!g.periodic && !g.open_cells) {
     const int im = image_of[i];
     const int s = image_start[im], e = image_start[im + 1];
     for (int j = s; j < e; ++j) {
       const double dx = xi - xw[3 * j], dy = yi - xw[3 * j + 1], dz = zi - xw[3 * j + 2];
       visit(j, kZeroImage, dx, dy, dz);
     }
+    return;
+  }
+  if (g.open_cells) {  // one open system on a clamped, non-wrapping grid
+    const int c = cell[i];
+    const int cx = c % g.ncell[0], cy = (c / g.ncell[0]) % g.ncell[1], cz = c / (g.ncell[0] * g.ncell[1]);
+    for (int wz = max(0, cz - reach); wz <= min(g.ncell[2] - 1, cz + reach); ++wz)
+      for (int wy = max(0, cy - reach); wy <= min(g.ncell[1] - 1, cy + reach); ++wy)
+        for (int wx = max(0, cx - reach); wx <= min(g.ncell[0] - 1, cx + reach); ++wx) {
+          const int cc = (wz * g.ncell[1] + wy) * g.ncell[0] + wx;
+          const int *a = cell_atoms + cell_start[cc];
+          const int m = cell_count[cc];
+          for (int t = 0; t < m; ++t) {
+            const int j = a[t];
+            visit(j, kZeroImage, xi - xw[3 * j], yi - xw[3 * j + 1], zi - xw[3 * j + 2]);
+          }
+        }
     return;
   }
   const int c = cell[i];

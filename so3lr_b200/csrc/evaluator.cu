@@ -450,10 +450,11 @@ void Evaluator::prepare(const SystemSpec &spec_in, const double *host_x) {
     if (nimg != 1) throw Error("SO3LR: batched images must be non-periodic");
     for (int d = 0; d < 3; ++d)
       if (!(spec.len[d] > 0.0)) throw Error("SO3LR: periodic box lengths must be positive");
-  } else {
+  } else if (!open_cells_possible(spec, host_x)) {
     for (int i = 0; i < nimg; ++i)
       if (spec.image_start[i + 1] - spec.image_start[i] > 20000)
-        throw Error("SO3LR: open-boundary images are limited to 20000 atoms; use a periodic box with vacuum");
+        throw Error("SO3LR: open-boundary images are limited to 20000 atoms when positions are not given on the "
+                    "host (so3lr_compute_device) or the system is a pack of images");
   }
   if (nranks_ > 1) {
     if (!spec.periodic) throw Error("SO3LR: multi-GPU decomposition needs a periodic box");
@@ -549,6 +550,26 @@ void Evaluator::prepare(const SystemSpec &spec_in, const double *host_x) {
     g.len[d] = spec.periodic ? spec.len[d] : 1.0;
     g.ncell[d] = spec.periodic ? std::max(1, int(std::floor(spec.len[d] / sr_cut_))) : 1;
   }
+  if (open_cells_possible(spec, host_x)) {
+    // one open system: a non-wrapping grid over the bounding box of the
+    // positions given now (atoms that later leave it go to the nearest
+    // boundary cell, which keeps the neighbour search exact)
+    double mn[3] = {1e300, 1e300, 1e300}, mx[3] = {-1e300, -1e300, -1e300};
+    for (int i = 0; i < n; ++i)
+      for (int d = 0; d < 3; ++d) {
+        const double v = host_x[3 * std::size_t(i) + d];
+        if (!std::isfinite(v)) throw Error("SO3LR: position of atom " + std::to_string(i) + " is not finite");
+        mn[d] = std::min(mn[d], v);
+        mx[d] = std::max(mx[d], v);
+      }
+    g.open_cells = 1;
+    for (int d = 0; d < 3; ++d) {
+      const double margin = 0.5;
+      g.lo[d] = mn[d] - margin;
+      g.len[d] = std::max(mx[d] - mn[d] + 2.0 * margin, sr_cut_);
+      g.ncell[d] = std::max(1, int(std::floor(g.len[d] / sr_cut_)));
+    }
+  }
   const long long ncells = (long long)g.ncell[0] * g.ncell[1] * g.ncell[2];
   if (ncells > (1 << 26)) throw Error("SO3LR: periodic box is too large for the cell grid");
   nb_.grid = g;
@@ -569,6 +590,14 @@ void Evaluator::prepare(const SystemSpec &spec_in, const double *host_x) {
   nb_.scan_total = small_ints_.reserve(16);
   nb_.error_flag = nb_.scan_total + 4;
   SO3_CUDA(cudaStreamSynchronize(stream_));
+}
+
+// A single open-boundary system with host positions and more than a few
+// hundred atoms gets a cell grid; smaller systems and packs of images scan
+// their image's index range.
+bool Evaluator::open_cells_possible(const SystemSpec &spec, const double *host_x) const {
+  const int nimg = spec.image_start.empty() ? 1 : int(spec.image_start.size()) - 1;
+  return !spec.periodic && nimg == 1 && host_x != nullptr && spec.n > kOpenCellsMinAtoms;
 }
 
 void Evaluator::alloc_atoms() {

@@ -166,6 +166,8 @@ class Evaluator {
   bool qk_norm_ = false, residual_scalars_ = false;
   std::vector<double> resid_, x0s_;
   static constexpr std::size_t kNoParam = ~std::size_t(0);
+  static constexpr int kOpenCellsMinAtoms = 512;
+  bool open_cells_possible(const SystemSpec &spec, const double *host_x) const;
 
   // static per-system data
   DeviceArray<int> z_, image_of_, image_start_, table_of_atom_;

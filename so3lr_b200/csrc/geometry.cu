@@ -282,14 +282,14 @@ __device__ inline double warp_sum(double v) {
 // pos4[k] = (x, y, z, q) and par4[k] = (h, alpha_ref, C6_ref, C6 ratio or 0)
 // of atom cell_atoms[k] (atom k itself for open boundaries), so that every
 // stencil row of cells is one contiguous, coalesced range of candidates.
-__global__ void k_lr_gather(int n, int periodic, const int *__restrict__ cell_atoms, const double *__restrict__ xw,
+__global__ void k_lr_gather(int n, int cell_ordered, const int *__restrict__ cell_atoms, const double *__restrict__ xw,
                             const double *__restrict__ q, const double *__restrict__ h,
                             const double *__restrict__ c6r, const int *__restrict__ z,
                             const double *__restrict__ aref, const double *__restrict__ cref, int table,
                             double4 *__restrict__ pos4, double4 *__restrict__ par4) {
   const int k = blockIdx.x * blockDim.x + threadIdx.x;
   if (k >= n) return;
-  const int j = periodic ? cell_atoms[k] : k;
+  const int j = cell_ordered ? cell_atoms[k] : k;
   const int zj = z[j] - 1;
   const bool known = zj >= 0 && zj < table;
   pos4[k] = make_double4(xw[3 * j], xw[3 * j + 1], xw[3 * j + 2], q[j]);
@@ -405,9 +405,28 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
       }
     }
   };
-  if (!g.periodic) {
+  if (!g.periodic && !g.open_cells) {
     const int im = image_of[i];
     scan_range(image_start[im], image_start[im + 1], 0.0, 0.0, 0.0);
+  } else if (g.open_cells) {
+    // one open system on a clamped grid: the same trimmed stencil, no wrap and
+    // no shift (an atom outside the grid is farther from every other cell than
+    // its boundary cell is, so the cell-distance bounds still hold)
+    const int nx = g.ncell[0], ny = g.ncell[1], nz = g.ncell[2];
+    const int c = cell[i];
+    const int cx = c % nx, cy = (c / nx) % ny, cz = c / (nx * ny);
+    for (int oz = -reach; oz <= reach; ++oz) {
+      const int wz = cz + oz;
+      if (wz < 0 || wz >= nz) continue;
+      for (int oy = -reach; oy <= reach; ++oy) {
+        const int wy = cy + oy;
+        const int rx = st.rx[abs(oy)][abs(oz)];
+        if (rx < 0 || wy < 0 || wy >= ny) continue;
+        const int row = (wz * ny + wy) * nx;
+        const int lo = max(0, cx - rx), hi = min(nx - 1, cx + rx);
+        scan_range(cell_start[row + lo], cell_start[row + hi] + cell_count[row + hi], 0.0, 0.0, 0.0);
+      }
+    }
   } else {
     const int nx = g.ncell[0], ny = g.ncell[1], nz = g.ncell[2];
     const int c = cell[i];
@@ -475,7 +494,8 @@ void launch_long_range(int n, int n_cells_atoms, const NeighborState &nb, double
                        double *e_elec, double *e_disp, double *dq, double *dh, double *dc6, double *f_lr,
                        double *w_lr, cudaStream_t s) {
   if (n == 0) return;
-  k_lr_gather<<<(n_cells_atoms + 255) / 256, 256, 0, s>>>(n_cells_atoms, nb.grid.periodic, nb.cell_atoms, nb.xw, q, h,
+  k_lr_gather<<<(n_cells_atoms + 255) / 256, 256, 0, s>>>(n_cells_atoms, nb.grid.periodic || nb.grid.open_cells,
+                                                          nb.cell_atoms, nb.xw, q, h,
                                                           c6r, z, alpha_ref, c6_ref, table_size, pos4, par4);
   SO3_LAUNCH("lr_gather");
   const int reach = sr_reach(nb.grid, rc_lr);
@@ -487,14 +507,15 @@ void launch_long_range(int n, int n_cells_atoms, const NeighborState &nb, double
     for (int a = 0; a <= kLrMaxReach; ++a)
       for (int b = 0; b <= kLrMaxReach; ++b) {
         int rx = reach;
-        if (g.periodic && reach <= kLrMaxReach) {
+        if ((g.periodic || g.open_cells) && reach <= kLrMaxReach) {
           const double dy = std::max(a - 1, 0) * cly, dz = std::max(b - 1, 0) * clz;
           const double rem = rcs - dy * dy - dz * dz;
           rx = rem <= 0.0 ? -1 : std::min(reach, int(std::floor(std::sqrt(rem) / clx)) + 1);
         }
         st.rx[a][b] = static_cast<signed char>(rx);
       }
-    if (g.periodic && reach > kLrMaxReach) throw std::runtime_error("SO3LR long range: cell stencil reach above " +
+    if ((g.periodic || g.open_cells) && reach > kLrMaxReach)
+      throw std::runtime_error("SO3LR long range: cell stencil reach above " +
                                                        std::to_string(kLrMaxReach));
   }
   const int threads = kLrWarps * 32;

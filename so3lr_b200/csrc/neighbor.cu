@@ -94,11 +94,16 @@ __global__ void k_wrap_assign(int n, const double *__restrict__ x, CellGrid g, c
   int cc[3];
   for (int d = 0; d < 3; ++d) {
     double p = x[3 * i + d] - g.lo[d];
-    p -= floor(p / g.len[d]) * g.len[d];
-    if (p >= g.len[d]) p -= g.len[d];
-    if (p < 0.0) p = 0.0;
-    xw[3 * i + d] = p + g.lo[d];
-    int c = int(p * g.ncell[d] / g.len[d]);
+    if (g.open_cells) {  // no wrap: the position stays, the cell is clamped
+      xw[3 * i + d] = x[3 * i + d];
+    } else {
+      p -= floor(p / g.len[d]) * g.len[d];
+      if (p >= g.len[d]) p -= g.len[d];
+      if (p < 0.0) p = 0.0;
+      xw[3 * i + d] = p + g.lo[d];
+    }
+    const double fc = p * g.ncell[d] / g.len[d];
+    const int c = fc < 0.0 ? 0 : (fc >= double(g.ncell[d]) ? g.ncell[d] - 1 : int(fc));
     cc[d] = c < 0 ? 0 : (c >= g.ncell[d] ? g.ncell[d] - 1 : c);
   }
   const int c = (cc[2] * g.ncell[1] + cc[1]) * g.ncell[0] + cc[0];
@@ -260,9 +265,10 @@ __global__ void k_pair_reverse(int E, const int *__restrict__ primary, const int
 
 // ---- host driver ---------------------------------------------------------------
 void build_cells(NeighborState &nb, int n, const double *x, cudaStream_t s) {
-  const int nc = nb.grid.periodic ? nb.grid.ncell[0] * nb.grid.ncell[1] * nb.grid.ncell[2] : 1;
+  const bool cells = nb.grid.periodic || nb.grid.open_cells;
+  const int nc = cells ? nb.grid.ncell[0] * nb.grid.ncell[1] * nb.grid.ncell[2] : 1;
   nb.ncells = nc;
-  if (!nb.grid.periodic) {
+  if (!cells) {
     SO3_CUDA(cudaMemcpyAsync(nb.xw, x, sizeof(double) * 3 * n, cudaMemcpyDeviceToDevice, s));
     return;
   }
@@ -278,7 +284,7 @@ void build_cells(NeighborState &nb, int n, const double *x, cudaStream_t s) {
 }
 
 int sr_reach(const CellGrid &g, double rc) {
-  if (!g.periodic) return 0;
+  if (!g.periodic && !g.open_cells) return 0;
   int reach = 1;
   for (int d = 0; d < 3; ++d) {
     const double cl = g.len[d] / g.ncell[d];

@@ -167,6 +167,60 @@ def test_gpu_virial_is_strain_derivative_full_size(gpu_model):
         assert abs(w_fd - base["virial"][a]) <= tol, (a, w_fd, base["virial"][a])
 
 
+def _droplet(nbox: int, radius: float):
+    """Whole water molecules whose oxygen lies within `radius` of the centre of
+    a periodic water box: an open-boundary droplet."""
+    from so3lr_b200.systems import water_box
+    w = water_box(nbox, seed=31)
+    c = w.boxlo + 0.5 * w.cell
+    o = w.pos[0::3]
+    keep = np.nonzero(np.linalg.norm(o - c, axis=1) < radius)[0]
+    idx = (3 * keep[:, None] + np.arange(3)[None, :]).ravel()
+    return w.pos[idx] - c, w.z[idx]
+
+
+def test_gpu_open_droplet_on_cell_grid(gpu_model, oracle_model):
+    """An open-boundary droplet of more than 512 atoms is searched on a
+    non-wrapping cell grid over its bounding box: it matches the oracle, and the
+    index-range search (taken when positions arrive in device memory) to
+    rounding of the long-range sums."""
+    import torch
+    from oracle.so3lr_oracle import System, evaluate
+    pos, z = _droplet(1000, 13.0)
+    n = len(z)
+    assert n > 512
+    g = gpu_model.compute(pos, z)
+    o = evaluate(oracle_model, System(pos=pos, z=z))
+    assert abs(g["energy"] - o["energy"]) / n <= 1e-9
+    assert np.abs(g["forces"] - o["forces"]).max() <= 1e-9
+    from so3lr_b200 import So3lrB200
+    from conftest import MODEL
+    other = So3lrB200(MODEL, 0)  # a fresh handle prepares from device positions: index-range search
+    try:
+        xd = torch.tensor(pos, dtype=torch.float64, device="cuda:0")
+        fd = torch.empty_like(xd)
+        e_range, _ = other.compute_device(xd.data_ptr(), z, None, None, fd.data_ptr())
+        torch.cuda.synchronize()
+    finally:
+        other.close()
+    assert abs(e_range - g["energy"]) <= 1e-11 * abs(g["energy"])
+    assert np.abs(fd.cpu().numpy() - g["forces"]).max() <= 1e-11
+
+
+def test_gpu_open_droplet_above_range_search_limit(gpu_model):
+    """More than 20,000 atoms with open boundaries (refused before the cell
+    grid): forces sum to zero and a translated copy gives the same result."""
+    pos, z = _droplet(27000, 37.0)
+    n = len(z)
+    assert n > 20000
+    a = gpu_model.compute(pos, z, terms=False)
+    b = gpu_model.compute(pos + np.array([5.3, -2.1, 0.7]), z, terms=False)
+    assert np.isfinite(a["energy"])
+    assert np.abs(a["forces"].sum(0)).max() <= 1e-8
+    assert abs(a["energy"] - b["energy"]) / n <= 1e-11
+    assert np.abs(a["forces"] - b["forces"]).max() <= 1e-9
+
+
 def test_gpu_turbo_batch_matches_single_images(gpu_model, oracle_model):
     """A pack of independent clusters (neutral, OH-, H3O+) equals each cluster
     evaluated alone (the reference's packed-evaluator test tolerance is
