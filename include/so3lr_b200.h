@@ -62,7 +62,9 @@ typedef struct {
   long long natoms;
   const double *x;       /* natoms * 3 */
   const int *z;          /* atomic number of every atom, 1..99 (so3lr_element_from_token maps pair_coeff tokens) */
-  int periodic;          /* 1: orthorhombic periodic box (boxlo, boxlen); 0: open boundaries */
+  int periodic;          /* 1: orthorhombic periodic box (boxlo, boxlen); 0: open boundaries (any size
+                            with host positions: a non-wrapping cell grid over the bounding box of the
+                            first call; at most 20,000 atoms through so3lr_compute_device) */
   double boxlo[3];
   double boxlen[3];
   double total_charge;   /* pair_style ... MODEL [charge [multiplicity]] (pair_so3lr_native_mpi.cpp:1097-1104) */
