@@ -241,6 +241,57 @@ def test_gpu_turbo_batch_matches_single_images(gpu_model, oracle_model):
             assert np.abs(b["forces"][sl] - o["forces"]).max() <= 1e-9
 
 
+def test_gpu_turbo_pack_trajectory_matches_single_images(gpu_model):
+    """The reference's turbo validation (tests/turbo/compare_turbo.py:43-44,
+    tolerance 1e-9): eleven images in one pack, neutral, charged and open-shell
+    (an OH radical and an H3O radical, doublets), run 40 NVE steps through the
+    pack and one by one; positions and image energies agree."""
+    from so3lr_b200.systems import MASS, maxwell_boltzmann, turbo_batch, water_cluster
+    pos, z, off, q, m = turbo_batch(8, seed=17)
+    images = [(pos[off[k]:off[k + 1]], z[off[k]:off[k + 1]], q[k], m[k]) for k in range(len(off) - 1)]
+    rng = np.random.default_rng(3)
+    p, zz, _ = water_cluster(5, rng, "hydroxide")
+    images.append((p, zz, 0.0, 2.0))      # OH radical among 4 waters: 49 electrons, doublet
+    p, zz, _ = water_cluster(6, rng, "hydronium")
+    images.append((p, zz, 0.0, 2.0))      # neutral H3O: 61 electrons, doublet
+    p, zz, _ = water_cluster(4, rng, "neutral")
+    images.append((p, zz, 0.0, 3.0))      # neutral triplet
+    x = [np.array(im[0], dtype=np.float64) for im in images]
+    v = [maxwell_boltzmann(np.array([MASS[int(t)] for t in im[1]]), 300.0, seed=5 + k) for k, im in enumerate(images)]
+    kick = [0.5 * 0.0005 / 1.0364269e-4 / np.array([MASS[int(t)] for t in im[1]])[:, None] for im in images]
+    offs = np.concatenate([[0], np.cumsum([len(im[1]) for im in images])]).astype(np.int64)
+    zs = np.concatenate([im[1] for im in images])
+    qs = np.array([im[2] for im in images])
+    ms = np.array([im[3] for im in images])
+    xp, vp = [a.copy() for a in x], [a.copy() for a in v]
+
+    def pack_forces():
+        b = gpu_model.compute_batch(np.concatenate(xp), zs, offs, qs, ms)
+        return [b["forces"][offs[k]:offs[k + 1]] for k in range(len(images))], b["image_energy"]
+
+    def single_forces():
+        out = [gpu_model.compute(x[k], images[k][1], charge=images[k][2], multiplicity=images[k][3], terms=False)
+               for k in range(len(images))]
+        return [o["forces"] for o in out], np.array([o["energy"] for o in out])
+
+    fp, _ = pack_forces()
+    fs, _ = single_forces()
+    for _ in range(40):
+        for k in range(len(images)):
+            vp[k] += kick[k] * fp[k]
+            xp[k] += 0.0005 * vp[k]
+            v[k] += kick[k] * fs[k]
+            x[k] += 0.0005 * v[k]
+        fp, ep = pack_forces()
+        fs, es = single_forces()
+        for k in range(len(images)):
+            vp[k] += kick[k] * fp[k]
+            v[k] += kick[k] * fs[k]
+    for k in range(len(images)):
+        assert np.abs(xp[k] - x[k]).max() <= 1e-9, k
+        assert abs(ep[k] - es[k]) <= 1e-9 * (1 + abs(es[k])), k
+
+
 def test_gpu_nve_energy_conservation(gpu_model):
     """Short NVE run on the device (config 2 box): total energy drift stays small."""
     from so3lr_b200.systems import maxwell_boltzmann, water_box
