@@ -2,14 +2,11 @@
 
 #include "nccl_dyn.hpp"
 
-#include <chrono>
 #include <cmath>
-#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <numeric>
 #include <sstream>
-#include <thread>
 
 namespace so3lr_b200 {
 
@@ -31,17 +28,8 @@ Evaluator::Evaluator(const std::string &model_path, int device) : model_(Model::
 Evaluator::~Evaluator() {
   if (stream_) {
     cudaSetDevice(device_);
-    if (comm_) {
-      try {  // drain this GPU's work, then leave the communicator in step with the others
-        wait_stream();
-        nccl_check(nccl().comm_finalize(comm_), "ncclCommFinalize");
-        nccl().comm_destroy(comm_);
-      } catch (const std::exception &) {
-        // abort_comm has already released the communicator
-      }
-      comm_ = nullptr;
-    }
     cudaStreamSynchronize(stream_);
+    if (comm_) nccl().comm_destroy(comm_);
     for (auto &p : prof_)
       for (auto ev : p.events) cudaEventDestroy(ev);
     cudaStreamDestroy(stream_);
@@ -333,15 +321,8 @@ void Evaluator::set_comm(int nranks, int rank, const void *unique_id) {
   if (nranks > 63) throw Error("SO3LR: at most 63 GPUs per decomposition");
   SO3_CUDA(cudaSetDevice(device_));
   if (comm_) {
-    wait_stream();
-    nccl_check(nccl().comm_finalize(comm_), "ncclCommFinalize");
     nccl().comm_destroy(comm_);
     comm_ = nullptr;
-  }
-  comm_failed_ = false;
-  if (const char *v = std::getenv("SO3LR_B200_COMM_TIMEOUT_S")) {
-    const double s = std::atof(v);
-    if (s > 0.0) comm_timeout_s_ = s;
   }
   nranks_ = nranks;
   rank_ = rank;
@@ -349,79 +330,15 @@ void Evaluator::set_comm(int nranks, int rank, const void *unique_id) {
   if (nranks == 1) return;
   ncclUniqueId id;
   std::memcpy(&id, unique_id, sizeof(id));
-  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
-  cfg.blocking = 0;
-  const ncclResult_t r = nccl().comm_init_rank_config(&comm_, nranks, id, rank, &cfg);
-  if (r != ncclSuccess && r != ncclInProgress) {
-    comm_ = nullptr;
-    nranks_ = 1;
-    throw Error(std::string("SO3LR: ncclCommInitRankConfig failed: ") + nccl().get_error_string(r));
-  }
-  nccl_check(r, "joining the other GPUs (ncclCommInitRankConfig)");
-}
-
-void Evaluator::abort_comm(const std::string &why) {
-  if (comm_) {
-    nccl().comm_abort(comm_);
-    comm_ = nullptr;
-  }
-  comm_failed_ = true;
-  cudaStreamSynchronize(stream_);  // the aborted collectives have left the stream
-  throw Error("SO3LR: multi-GPU communication failed: " + why +
-              "; the communicator was aborted (call so3lr_comm_init again to rebuild it)");
-}
-
-// An NCCL call on the non-blocking communicator: ncclInProgress is waited out
-// (bounded), anything else but success aborts.
-void Evaluator::nccl_check(ncclResult_t r, const char *what) {
-  if (comm_failed_ || comm_ == nullptr) throw Error("SO3LR: the multi-GPU communicator was aborted earlier");
-  if (r == ncclSuccess) return;
-  if (r != ncclInProgress) abort_comm(std::string(what) + ": " + nccl().get_error_string(r));
-  const auto t0 = std::chrono::steady_clock::now();
-  for (;;) {
-    ncclResult_t state = ncclSuccess;
-    nccl().comm_get_async_error(comm_, &state);
-    if (state == ncclSuccess) return;
-    if (state != ncclInProgress) abort_comm(std::string(what) + ": " + nccl().get_error_string(state));
-    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > comm_timeout_s_)
-      abort_comm(std::string(what) + ": the other GPUs did not respond within " + std::to_string(comm_timeout_s_) +
-                 " s");
-    std::this_thread::yield();
-  }
-}
-
-// Synchronise the library stream. With a communicator the wait polls the
-// stream and the communicator's error state and gives up after the timeout.
-void Evaluator::wait_stream() {
-  if (comm_ == nullptr) {
-    wait_stream();
-    return;
-  }
-  const auto t0 = std::chrono::steady_clock::now();
-  auto checked = t0;
-  for (;;) {
-    const cudaError_t q = cudaStreamQuery(stream_);
-    if (q == cudaSuccess) return;
-    if (q != cudaErrorNotReady) SO3_CUDA(q);
-    const auto now = std::chrono::steady_clock::now();
-    if (now - checked > std::chrono::milliseconds(1)) {
-      checked = now;
-      ncclResult_t state = ncclSuccess;
-      nccl().comm_get_async_error(comm_, &state);
-      if (state != ncclSuccess && state != ncclInProgress)
-        abort_comm(std::string("NCCL reported ") + nccl().get_error_string(state));
-      if (std::chrono::duration<double>(now - t0).count() > comm_timeout_s_)
-        abort_comm("no progress from the other GPUs within " + std::to_string(comm_timeout_s_) + " s");
-    }
-    std::this_thread::yield();
-  }
+  const ncclResult_t r = nccl().comm_init_rank(&comm_, nranks, id, rank);
+  if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclCommInitRank failed: ") + nccl().get_error_string(r));
 }
 
 void Evaluator::allgather_rows(double *a, int width) {
   if (nranks_ == 1) return;
   const std::size_t count = std::size_t(stride_) * width;
-  nccl_check(nccl().all_gather(a + std::size_t(rank_) * count, a, count, ncclDouble, comm_, stream_),
-             "ncclAllGather");
+  const ncclResult_t r = nccl().all_gather(a + std::size_t(rank_) * count, a, count, ncclDouble, comm_, stream_);
+  if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclAllGather failed: ") + nccl().get_error_string(r));
 }
 
 void Evaluator::halo_exchange(double *a, int wa, double *b, int wb) {
@@ -432,7 +349,9 @@ void Evaluator::halo_exchange(double *a, int wa, double *b, int wb) {
   double *rbuf = halo_recv_buf_.reserve(std::size_t(std::max(1LL, nrecv)) * w, 1.25);
   launch_halo_pack(int(nsend), halo_send_rows_.get(), a, wa, b, wb, sbuf, stream_);
   const NcclApi &api = nccl();
-  auto check = [&](ncclResult_t r, const char *what) { nccl_check(r, what); };
+  auto check = [&](ncclResult_t r, const char *what) {
+    if (r != ncclSuccess) throw Error(std::string("SO3LR: ") + what + " failed: " + api.get_error_string(r));
+  };
   check(api.group_start(), "ncclGroupStart");
   for (int p = 0; p < nranks_; ++p) {
     if (p == rank_) continue;
@@ -458,7 +377,8 @@ void Evaluator::exact_sums(const double *v, int stride, int ncol, int nseg, cons
   long long *all = local + per_rank;
   launch_fixed_segment_sum(nseg, nblk, seg, v, stride, ncol, local, stream_);
   if (nranks_ > 1) {
-    nccl_check(nccl().all_gather(local, all, per_rank, ncclInt64, comm_, stream_), "ncclAllGather");
+    const ncclResult_t r = nccl().all_gather(local, all, per_rank, ncclInt64, comm_, stream_);
+    if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclAllGather failed: ") + nccl().get_error_string(r));
     launch_fixed_finish(all, nranks_ * nblk, count, out, stream_);
   } else {
     launch_fixed_finish(local, nblk, count, out, stream_);
@@ -669,7 +589,7 @@ void Evaluator::prepare(const SystemSpec &spec_in, const double *host_x) {
   nb_.scan_scratch = scan_scratch_.reserve(scan_scratch_ints(std::max<long long>(ncells, 64LL * nr)));
   nb_.scan_total = small_ints_.reserve(16);
   nb_.error_flag = nb_.scan_total + 4;
-  wait_stream();
+  SO3_CUDA(cudaStreamSynchronize(stream_));
 }
 
 // A single open-boundary system with host positions and more than a few
@@ -760,7 +680,7 @@ void Evaluator::upload_positions(const double *host_x) {
   for (int i = 0; i < spec_.n; ++i)
     for (int d = 0; d < 3; ++d) stage_[3 * std::size_t(row_of_[i]) + d] = host_x[3 * std::size_t(i) + d];
   SO3_CUDA(cudaMemcpyAsync(x_.get(), stage_.data(), sizeof(double) * 3 * n_rows_, cudaMemcpyHostToDevice, stream_));
-  wait_stream();  // stage_ is reused
+  SO3_CUDA(cudaStreamSynchronize(stream_));  // stage_ is reused
 }
 
 std::size_t Evaluator::device_bytes() const {
@@ -799,7 +719,7 @@ void Evaluator::prof_end(int k, double flops) {
 }
 void Evaluator::read_profile(int k, double *ms, long long *launches, double *flops) {
   if (k < 0 || k > 1) throw Error("SO3LR: unknown profiled kernel");
-  wait_stream();
+  SO3_CUDA(cudaStreamSynchronize(stream_));
   KernelProfile &p = prof_[k];
   double total = 0;
   for (int i = 0; i < p.used; i += 2) {
@@ -822,7 +742,7 @@ void Evaluator::build_neighbors() {
   build_cells(nb_, n_rows_, x_.get(), stream_);
   count_sr(nb_, sr_cut_, stream_);
   SO3_CUDA(cudaMemcpyAsync(host_small_, nb_.row_start + n_own_, sizeof(int), cudaMemcpyDeviceToHost, stream_));
-  wait_stream();
+  SO3_CUDA(cudaStreamSynchronize(stream_));
   const int E = host_small_[0];
   if (E < 0) throw Error("SO3LR: edge count overflow");
   stats_.edges = E;
@@ -853,11 +773,12 @@ void Evaluator::build_neighbors() {
     launch_halo_lists(n_own_, row0_, stride_, nranks_, rank_, nb_.row_start, nb_.nbr, flags, flags + cnt, pos,
                       pos + cnt, halo_send_rows_.reserve(cnt), halo_recv_rows_.reserve(cnt), off,
                       halo_totals_.reserve(2), nb_.scan_scratch, stream_);
-    nccl_check(nccl().all_gather(off, all, std::size_t(lo), ncclInt64, comm_, stream_), "ncclAllGather");
+    const ncclResult_t r = nccl().all_gather(off, all, std::size_t(lo), ncclInt64, comm_, stream_);
+    if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclAllGather failed: ") + nccl().get_error_string(r));
     if (!host_halo_) SO3_CUDA(cudaMallocHost(&host_halo_, sizeof(long long) * 2 * 64 * 64));
     SO3_CUDA(cudaMemcpyAsync(host_halo_, all, sizeof(long long) * lo * nranks_, cudaMemcpyDeviceToHost, stream_));
   }
-  wait_stream();
+  SO3_CUDA(cudaStreamSynchronize(stream_));
   if (!identity_) {
     const int lo = 2 * (nranks_ + 1);
     auto sends = [&](int s, int p) { return host_halo_[s * lo + p + 1] - host_halo_[s * lo + p]; };
@@ -1157,13 +1078,13 @@ void Evaluator::download_virial_atom(double *vatom) {
   if (identity_) {
     SO3_CUDA(cudaMemcpyAsync(vatom, w_atom_.get(), sizeof(double) * 6 * std::size_t(n), cudaMemcpyDeviceToHost,
                              stream_));
-    wait_stream();
+    SO3_CUDA(cudaStreamSynchronize(stream_));
     return;
   }
   allgather_rows(w_atom_.get(), 6);
   SO3_CUDA(cudaMemcpyAsync(stage_.data(), w_atom_.get(), sizeof(double) * 6 * std::size_t(n_rows_),
                            cudaMemcpyDeviceToHost, stream_));
-  wait_stream();
+  SO3_CUDA(cudaStreamSynchronize(stream_));
   for (int i = 0; i < n; ++i)
     for (int k = 0; k < 6; ++k) vatom[std::size_t(i) * 6 + k] = stage_[std::size_t(row_of_[i]) * 6 + k];
 }
@@ -1185,7 +1106,7 @@ Evaluator::HostResult Evaluator::download(double *f, double *eatom, double *char
     allgather_rows(src, width);
     SO3_CUDA(cudaMemcpyAsync(stage_.data(), src, sizeof(double) * width * std::size_t(n_rows_), cudaMemcpyDeviceToHost,
                              s));
-    wait_stream();
+    SO3_CUDA(cudaStreamSynchronize(s));
     for (int i = 0; i < n; ++i)
       for (int k = 0; k < width; ++k) dst[std::size_t(i) * width + k] = stage_[std::size_t(row_of_[i]) * width + k];
   };
@@ -1201,7 +1122,7 @@ Evaluator::HostResult Evaluator::download(double *f, double *eatom, double *char
   if (image_energy) SO3_CUDA(cudaMemcpyAsync(image_energy, image_energy_.get(), sizeof(double) * nimg, cudaMemcpyDeviceToHost, s));
   SO3_CUDA(cudaMemcpyAsync(host_totals_, totals_.get(), sizeof(double) * 7, cudaMemcpyDeviceToHost, s));
   SO3_CUDA(cudaMemcpyAsync(host_small_ + 8, nb_.error_flag, sizeof(int), cudaMemcpyDeviceToHost, s));
-  wait_stream();
+  SO3_CUDA(cudaStreamSynchronize(s));
   if (host_small_[8] != 0) throw Error("SO3LR: short-range list has an edge without its reverse");
   HostResult r;
   r.energy = host_totals_[0];
@@ -1233,7 +1154,7 @@ void Evaluator::md_setup(const double *host_v, const double *host_mass) {
   ke2_.reserve(n_rows_);
   nvt_ = false;
   compute();  // forces at the starting positions
-  wait_stream();
+  SO3_CUDA(cudaStreamSynchronize(stream_));
   md_ready_ = true;
 }
 
@@ -1259,7 +1180,7 @@ void Evaluator::md_thermostat(double t_target_k, double t_damp_ps, int chain) {
   double *d = nhc_state_.reserve(words);
   SO3_CUDA(cudaMemcpyAsync(d, &st, sizeof(NhcState), cudaMemcpyHostToDevice, stream_));
   nhc_scalars_.reserve(2);
-  wait_stream();
+  SO3_CUDA(cudaStreamSynchronize(stream_));
   nvt_ = true;
 }
 
@@ -1268,7 +1189,7 @@ double Evaluator::md_thermostat_energy() {
   if (!nvt_) return 0.0;
   NhcState st{};
   SO3_CUDA(cudaMemcpyAsync(&st, nhc_state_.get(), sizeof(NhcState), cudaMemcpyDeviceToHost, stream_));
-  wait_stream();
+  SO3_CUDA(cudaStreamSynchronize(stream_));
   double e = 0.0;
   for (int j = 0; j < st.chain; ++j) {
     e += 0.5 * st.q[j] * st.veta[j] * st.veta[j];
@@ -1309,12 +1230,12 @@ void Evaluator::md_download(double *x, double *v) {
     if (!dst) return;
     if (identity_) {
       SO3_CUDA(cudaMemcpyAsync(dst, src, sizeof(double) * 3 * n, cudaMemcpyDeviceToHost, stream_));
-      wait_stream();
+      SO3_CUDA(cudaStreamSynchronize(stream_));
       return;
     }
     allgather_rows(src, 3);
     SO3_CUDA(cudaMemcpyAsync(stage_.data(), src, sizeof(double) * 3 * n_rows_, cudaMemcpyDeviceToHost, stream_));
-    wait_stream();
+    SO3_CUDA(cudaStreamSynchronize(stream_));
     for (int i = 0; i < n; ++i)
       for (int d = 0; d < 3; ++d) dst[3 * std::size_t(i) + d] = stage_[3 * std::size_t(row_of_[i]) + d];
   };

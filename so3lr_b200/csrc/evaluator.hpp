@@ -204,17 +204,6 @@ class Evaluator {
   // decomposition
   int nranks_ = 1, rank_ = 0;
   ncclComm_t comm_ = nullptr;
-  // Communicators are non-blocking; every wait on them (initialisation, calls
-  // that report ncclInProgress, stream synchronisation while collectives are in
-  // flight) gives up after comm_timeout_s_ seconds ($SO3LR_B200_COMM_TIMEOUT_S,
-  // default 600) or at the first asynchronous NCCL error, aborts the
-  // communicator and throws; the handle then refuses multi-GPU work until
-  // so3lr_comm_init is called again.
-  double comm_timeout_s_ = 600.0;
-  bool comm_failed_ = false;
-  [[noreturn]] void abort_comm(const std::string &why);
-  void nccl_check(ncclResult_t r, const char *what);
-  void wait_stream();
   int n_rows_ = 0, stride_ = 0, row0_ = 0, n_own_ = 0;
   bool identity_ = true;
   std::vector<int> row_of_, tag_of_row_;

@@ -35,10 +35,6 @@ const NcclApi &nccl() {
   api.recv = reinterpret_cast<decltype(api.recv)>(sym("ncclRecv"));
   api.group_start = reinterpret_cast<decltype(api.group_start)>(sym("ncclGroupStart"));
   api.group_end = reinterpret_cast<decltype(api.group_end)>(sym("ncclGroupEnd"));
-  api.comm_init_rank_config = reinterpret_cast<decltype(api.comm_init_rank_config)>(sym("ncclCommInitRankConfig"));
-  api.comm_get_async_error = reinterpret_cast<decltype(api.comm_get_async_error)>(sym("ncclCommGetAsyncError"));
-  api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(sym("ncclCommAbort"));
-  api.comm_finalize = reinterpret_cast<decltype(api.comm_finalize)>(sym("ncclCommFinalize"));
   loaded = true;
   return api;
 }

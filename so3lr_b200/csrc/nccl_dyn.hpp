@@ -20,12 +20,6 @@ struct NcclApi {
   ncclResult_t (*group_start)();
   ncclResult_t (*group_end)();
   const char *(*get_error_string)(ncclResult_t);
-  // non-blocking communicators: every call may return ncclInProgress, and the
-  // communicator's state is then polled until it leaves it
-  ncclResult_t (*comm_init_rank_config)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *);
-  ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t *);
-  ncclResult_t (*comm_abort)(ncclComm_t);
-  ncclResult_t (*comm_finalize)(ncclComm_t);
 };
 
 // Throws so3lr_b200::Error when no NCCL library can be loaded.
