@@ -567,8 +567,13 @@ void Evaluator::prepare(const SystemSpec &spec_in, const double *host_x) {
       const double margin = 0.5;
       g.lo[d] = mn[d] - margin;
       g.len[d] = std::max(mx[d] - mn[d] + 2.0 * margin, sr_cut_);
-      g.ncell[d] = std::max(1, int(std::floor(g.len[d] / sr_cut_)));
+      g.ncell[d] = int(std::min(std::floor(g.len[d] / sr_cut_), 4096.0));
+      if (g.ncell[d] < 1) g.ncell[d] = 1;
     }
+    // a sparse system (atoms far apart) would need more cells than atoms:
+    // coarser cells (still no smaller than the cutoff) keep the grid small
+    while ((long long)g.ncell[0] * g.ncell[1] * g.ncell[2] > (1LL << 22))
+      for (int d = 0; d < 3; ++d) g.ncell[d] = std::max(1, g.ncell[d] / 2);
   }
   const long long ncells = (long long)g.ncell[0] * g.ncell[1] * g.ncell[2];
   if (ncells > (1 << 26)) throw Error("SO3LR: periodic box is too large for the cell grid");
