@@ -474,9 +474,10 @@ def run_turbo(args) -> None:
 
 
 def count_lr_pairs(pos, boxlo, cell, cutoff: float) -> int:
-    """Unordered atom pairs within the long-range cutoff (periodic minimum image
-    and beyond: every image inside the cutoff counts), counted on the host with
-    a k-d tree before the timed region."""
+    """Unordered atom pairs within the long-range cutoff under the minimum-image
+    convention (exact for boxes at least twice the cutoff, as in every bench
+    configuration), counted on the host with a k-d tree after the timed
+    regions."""
     from scipy.spatial import cKDTree
     x = np.mod(np.asarray(pos) - np.asarray(boxlo), np.asarray(cell))
     tree = cKDTree(x, boxsize=np.asarray(cell))

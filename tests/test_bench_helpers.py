@@ -1,0 +1,37 @@
+"""Host-side helpers of bench.py: the long-range pair count of the whole-step
+roofline against a brute-force minimum-image count, and the FLOP formula."""
+import importlib.util
+
+import numpy as np
+
+from conftest import ROOT
+
+
+def _bench():
+    spec = importlib.util.spec_from_file_location("bench_module", ROOT / "bench.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_lr_pair_count_matches_brute_force():
+    from so3lr_b200.systems import water_box
+    b = _bench()
+    w = water_box(300, seed=4)  # 900 atoms, box 20.8 A > 2 x 10 A
+    cut = 10.0
+    d = w.pos[:, None, :] - w.pos[None, :, :]
+    d -= np.round(d / w.cell) * w.cell
+    r2 = (d * d).sum(-1)
+    brute = int((np.triu(r2 < cut * cut, k=1)).sum())
+    assert b.count_lr_pairs(w.pos, w.boxlo, w.cell, cut) == brute
+
+
+def test_step_flops_formula():
+    b = _bench()
+    r = b.step_roofline(24000, 946822, 473411, 8651195, 1 / 0.02125, 35.4, 1)
+    assert abs(r["reference_flop_per_step"] - (3 * 946822 * 203.6e3 + 3 * 24000 * 288e3 + 24000 * 181e3
+                                               + 250 * 8651195)) < 1.0
+    assert r["executed_flop_per_step"] < r["reference_flop_per_step"]
+    assert abs(r["frac_executed"] - r["executed_tflops"] / 35.4) < 1e-12
+    two = b.step_roofline(24000, 946822, 473411, 8651195, 1 / 0.02125, 35.4, 2)
+    assert abs(two["executed_tflops"] - 2 * r["executed_tflops"]) < 1e-9
