@@ -12,6 +12,8 @@
 //                                       so3lr/b200 on NRANKS MPI ranks (threads, one GPU each);
 //                                       INPUT as for run; atom i lives on rank (7 i) % NRANKS with
 //                                       tag i + 1; prints one JSON line per rank
+//   test_pair_shim plugin               lammpsplugin_init registers both styles; their
+//                                       creators build the pair objects
 //   test_pair_shim turbo-refuse MODEL INPUT
 //                                       the same universe with image 1 periodic and image 2 given
 //                                       an impossible multiplicity: every partition must stop
@@ -24,8 +26,11 @@
 #include <string>
 #include <vector>
 
+#include "lammpsplugin.h"
 #include "pair_so3lr_b200.h"
 #include "pair_so3lr_b200_turbo.h"
+
+extern "C" void lammpsplugin_init(void *lmp, void *handle, void *regfunc);
 
 using namespace LAMMPS_NS;
 
@@ -431,7 +436,27 @@ static int turbo_refuse(const char *model, const char *input) {
   return fails ? 1 : 0;
 }
 
+static std::vector<std::string> g_registered;
+static void register_style(lammpsplugin_t *p, void *lmp) {
+  g_registered.push_back(std::string(p->style) + " " + p->name);
+  Pair *pair = reinterpret_cast<Pair *>(p->creator.v1(lmp));
+  const bool ok = pair != nullptr && pair->manybody_flag == 1 && pair->one_coeff == 1;
+  std::printf("%s %s %s %s\n", p->style, p->name, ok ? "constructed" : "BAD", p->version);
+  delete pair;
+}
+
+static int plugin_check() {
+  LAMMPS lmp;
+  int handle = 0;
+  lammpsplugin_init(&lmp, &handle, reinterpret_cast<void *>(&register_style));
+  const bool ok = g_registered.size() == 2 && g_registered[0] == "pair so3lr/b200" &&
+                  g_registered[1] == "pair so3lr/b200/turbo";
+  std::printf("%s\n", ok ? "PLUGIN OK" : "PLUGIN FAIL");
+  return ok ? 0 : 1;
+}
+
 int main(int argc, char **argv) {
+  if (argc >= 2 && std::string(argv[1]) == "plugin") return plugin_check();
   if (argc >= 3 && std::string(argv[1]) == "parse") return parse_checks(argv[2]);
   if (argc >= 4 && std::string(argv[1]) == "run") return run(argv[2], argv[3]);
   if (argc >= 5 && std::string(argv[1]) == "multirank") return multirank(argv[2], argv[3], std::atoi(argv[4]));

@@ -30,7 +30,8 @@ def _build(tmp_path: pathlib.Path, fake: bool = False) -> pathlib.Path:
     shim = ROOT / "so3lr_b200" / "lammps"
     exe = tmp_path / ("test_pair_fake" if fake else "test_pair_shim")
     cmd = [gxx, "-std=c++17", "-O1", "-pthread", "-I", str(mock), "-I", str(shim), "-I", str(ROOT / "include"),
-           str(shim / "pair_so3lr_b200.cpp"), str(shim / "pair_so3lr_b200_turbo.cpp"), str(mock / "test_pair_shim.cpp")]
+           str(shim / "pair_so3lr_b200.cpp"), str(shim / "pair_so3lr_b200_turbo.cpp"),
+           str(shim / "so3lrb200plugin.cpp"), str(mock / "test_pair_shim.cpp")]
     if fake:
         cmd += [str(mock / "fake_so3lr_b200.cpp")]
     else:
@@ -76,6 +77,15 @@ def test_pair_style_parsing_and_refusals(tmp_path):
     res = subprocess.run([str(exe), "turbo-parse", str(MODEL)], capture_output=True, text=True, timeout=300)
     assert "TURBO PARSE OK" in res.stdout, res.stdout + res.stderr
     assert res.returncode == 0
+
+
+def test_plugin_registers_both_styles(tmp_path):
+    """`plugin load` entry point (lammpsplugin_init): both pair styles are
+    registered under their names and their creators construct the styles."""
+    exe = _build(tmp_path, fake=True)
+    res = subprocess.run([str(exe), "plugin"], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0 and "PLUGIN OK" in res.stdout, res.stdout + res.stderr
+    assert "pair so3lr/b200 constructed" in res.stdout and "pair so3lr/b200/turbo constructed" in res.stdout
 
 
 def test_turbo_routes_each_image_back_to_its_partition(tmp_path):
