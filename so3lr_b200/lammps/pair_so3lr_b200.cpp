@@ -8,8 +8,10 @@
 
 #include <mpi.h>
 
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 
 #include "atom.h"
 #include "comm.h"
@@ -128,6 +130,38 @@ void PairSO3LRB200::init_style() {
   }
 }
 
+// One JSON object per call: schema so3lr-native-debug-v1, the long-range
+// electrostatic and dispersion totals, and per local atom its tag, type and
+// energy terms, charge and Hirshfeld ratio.
+void PairSO3LRB200::write_debug_dump(const char *path, const so3lr_result &res, int n) {
+  FILE *out = std::fopen(path, "w");
+  if (out == nullptr) error->all(FLERR, std::string("cannot open SO3LR_NATIVE_DEBUG_DUMP ") + path);
+  double elec = 0.0, disp = 0.0;
+  for (int k = 0; k < n; ++k) {
+    elec += res.e_elec[k];
+    disp += res.e_disp[k];
+  }
+  const int nlocal = atom->nlocal;
+  auto array = [&](const char *name, const std::function<double(int)> &value, bool last) {
+    std::fprintf(out, "\"%s\":[", name);
+    for (int i = 0; i < nlocal; ++i) std::fprintf(out, i ? ",%.17g" : "%.17g", value(i));
+    std::fprintf(out, "]%s", last ? "" : ",");
+  };
+  // the library's arrays are in tag order; local atom i is row tag - 1
+  auto row = [&](int i) { return static_cast<std::size_t>(atom->tag[i] - 1); };
+  std::fprintf(out, "{\"schema\":\"so3lr-native-debug-v1\",\"natoms\":%d,", nlocal);
+  std::fprintf(out, "\"electrostatic_total\":%.17g,\"dispersion_total\":%.17g,", elec, disp);
+  array("tag", [&](int i) { return static_cast<double>(atom->tag[i]); }, false);
+  array("type", [&](int i) { return static_cast<double>(atom->type[i]); }, false);
+  array("learned_energy", [&](int i) { return res.e_learned[row(i)]; }, false);
+  array("zbl_energy", [&](int i) { return res.e_zbl[row(i)]; }, false);
+  array("physical_energy", [&](int i) { return res.e_lr[row(i)]; }, false);
+  array("partial_charges", [&](int i) { return res.charges[row(i)]; }, false);
+  array("hirshfeld_ratios", [&](int i) { return res.ratios[row(i)]; }, true);
+  std::fprintf(out, "}\n");
+  std::fclose(out);
+}
+
 void PairSO3LRB200::compute(int eflag, int vflag) {
   ev_init(eflag, vflag);
   const int nlocal = atom->nlocal;
@@ -191,9 +225,26 @@ void PairSO3LRB200::compute(int eflag, int vflag) {
   so3lr_result res{};
   res.f = f_.data();
   res.eatom = eatom_.data();
+  // opt-in per-atom terms for validation against the reference's JAX harness,
+  // in the reference's dump schema (pair_so3lr_native_mpi.cpp:1811-1862)
+  const char *dump_path = std::getenv("SO3LR_NATIVE_DEBUG_DUMP");
+  const bool dump = dump_path != nullptr && dump_path[0] != '\0';
+  if (dump) {
+    if (comm->nprocs != 1) error->all(FLERR, "SO3LR_NATIVE_DEBUG_DUMP requires a single MPI rank");
+    terms_.assign(7 * static_cast<std::size_t>(n), 0.0);
+    double *tp = terms_.data();
+    res.charges = tp;
+    res.ratios = tp + n;
+    res.e_learned = tp + 2 * static_cast<std::size_t>(n);
+    res.e_zbl = tp + 3 * static_cast<std::size_t>(n);
+    res.e_lr = tp + 4 * static_cast<std::size_t>(n);
+    res.e_elec = tp + 5 * static_cast<std::size_t>(n);
+    res.e_disp = tp + 6 * static_cast<std::size_t>(n);
+  }
   char err[2048] = {0};
   if (so3lr_compute(handle_, &frame, &res, err, sizeof(err)) != 0)
     error->all(FLERR, std::string("SO3LR evaluation failed: ") + err);
+  if (dump) write_debug_dump(dump_path, res, n);
   // each rank keeps its own atoms' forces and per-atom terms; the global energy
   // and virial (exact sums, identical on every rank) are reported by rank 0 only,
   // so LAMMPS's sum over ranks counts them once

@@ -28,8 +28,7 @@ PairStyle(so3lr/b200,PairSO3LRB200);
 #include <vector>
 
 #include "pair.h"
-
-struct so3lr_handle;
+#include "so3lr_b200.h"
 
 namespace LAMMPS_NS {
 
@@ -57,7 +56,7 @@ class PairSO3LRB200 : public Pair {
   double lr_cutoff_ = 0.0;
   std::vector<int> type_to_z_;
   std::vector<int> z_;
-  std::vector<double> x_, f_, eatom_, va_, loc_x_, all_x_;
+  std::vector<double> x_, f_, eatom_, va_, loc_x_, all_x_, terms_;
   std::vector<int> loc_tag_, loc_z_, all_tag_, all_z_, counts_, displs_, counts3_, displs3_;
   bool comm_ready_ = false;
   so3lr_handle *handle_ = nullptr;
@@ -65,6 +64,7 @@ class PairSO3LRB200 : public Pair {
 
   void allocate();
   void release();
+  void write_debug_dump(const char *path, const so3lr_result &res, int n);
 };
 
 }  // namespace LAMMPS_NS

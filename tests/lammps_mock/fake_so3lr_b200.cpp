@@ -88,9 +88,31 @@ int so3lr_virial_atom(so3lr_handle *h, double *vatom, char *, size_t) {
   return 0;
 }
 
-// the so3lr/b200 style's calls, not used by the turbo tests
-int so3lr_compute(so3lr_handle *, const so3lr_frame *, so3lr_result *, char *err, size_t errlen) {
-  return fake_fail("not in the CPU stand-in", err, errlen);
+// so3lr_compute (one rank): row k of the system (tag k + 1) gets
+//   f = -x, eatom = 0.5 z, charges = 0.01 k, ratios = 1 + 0.001 z,
+//   e_learned = 0.25 z, e_zbl = 0.125, e_lr = 0.25 z - 0.125,
+//   e_elec = e_disp = e_lr / 2; energy = sum of eatom; virial 0
+int so3lr_compute(so3lr_handle *h, const so3lr_frame *in, so3lr_result *out, char *err, size_t errlen) {
+  if (!h || !in || !out || !out->f) return fake_fail("so3lr_compute: NULL argument", err, errlen);
+  const long long n = in->natoms;
+  double e = 0.0;
+  h->va.assign(6 * static_cast<std::size_t>(n), 0.0);
+  for (long long k = 0; k < n; ++k) {
+    const double z = in->z[k];
+    for (int d = 0; d < 3; ++d) out->f[3 * k + d] = -in->x[3 * k + d];
+    if (out->eatom) out->eatom[k] = 0.5 * z;
+    if (out->charges) out->charges[k] = 0.01 * k;
+    if (out->ratios) out->ratios[k] = 1.0 + 0.001 * z;
+    if (out->e_learned) out->e_learned[k] = 0.25 * z;
+    if (out->e_zbl) out->e_zbl[k] = 0.125;
+    if (out->e_lr) out->e_lr[k] = 0.25 * z - 0.125;
+    if (out->e_elec) out->e_elec[k] = 0.5 * (0.25 * z - 0.125);
+    if (out->e_disp) out->e_disp[k] = 0.5 * (0.25 * z - 0.125);
+    e += 0.5 * z;
+  }
+  out->energy = e;
+  for (int c = 0; c < 6; ++c) out->virial[c] = 0.0;
+  return 0;
 }
 int so3lr_nccl_unique_id(char *, char *err, size_t errlen) { return fake_fail("not in the CPU stand-in", err, errlen); }
 int so3lr_comm_init(so3lr_handle *, int, int, const char *, char *err, size_t errlen) {

@@ -2,6 +2,8 @@
 //   test_pair_shim parse MODEL          pair_style/pair_coeff parsing and refusals
 //   test_pair_shim run MODEL INPUT      one compute; INPUT holds "L n" then n lines "type x y z"
 //                                       (types 1 = O, 2 = H); prints JSON with energy, virial, forces
+//   test_pair_shim run-reversed-tags MODEL INPUT
+//                                       the same with atom i tagged n - i
 //   test_pair_shim turbo-parse MODEL    so3lr/b200/turbo parsing and refusals on one rank, and a
 //                                       coordinator failure reaching every partition of a universe
 //   test_pair_shim turbo-run MODEL INPUT
@@ -118,7 +120,7 @@ static int parse_checks(const char *model) {
   return fails ? 1 : 0;
 }
 
-static int run(const char *model, const char *input) {
+static int run(const char *model, const char *input, bool reverse_tags = false) {
   std::ifstream in(input);
   double L;
   int n;
@@ -126,6 +128,8 @@ static int run(const char *model, const char *input) {
   LAMMPS lmp;
   lmp.atom.ntypes = 2;
   lmp.atom.resize(n);
+  if (reverse_tags)
+    for (int i = 0; i < n; ++i) lmp.atom.tag[i] = n - i;
   for (int i = 0; i < n; ++i) in >> lmp.atom.type[i] >> lmp.atom.x[i][0] >> lmp.atom.x[i][1] >> lmp.atom.x[i][2];
   for (int d = 0; d < 3; ++d) lmp.domain.prd[d] = L;
   PairSO3LRB200 pair(&lmp);
@@ -459,6 +463,7 @@ int main(int argc, char **argv) {
   if (argc >= 2 && std::string(argv[1]) == "plugin") return plugin_check();
   if (argc >= 3 && std::string(argv[1]) == "parse") return parse_checks(argv[2]);
   if (argc >= 4 && std::string(argv[1]) == "run") return run(argv[2], argv[3]);
+  if (argc >= 4 && std::string(argv[1]) == "run-reversed-tags") return run(argv[2], argv[3], true);
   if (argc >= 5 && std::string(argv[1]) == "multirank") return multirank(argv[2], argv[3], std::atoi(argv[4]));
   if (argc >= 3 && std::string(argv[1]) == "turbo-parse") return turbo_parse_checks(argv[2]);
   if (argc >= 4 && std::string(argv[1]) == "turbo-run") return turbo_run(argv[2], argv[3]);

@@ -79,6 +79,35 @@ def test_pair_style_parsing_and_refusals(tmp_path):
     assert res.returncode == 0
 
 
+def test_debug_dump_in_the_reference_schema(tmp_path, monkeypatch):
+    """SO3LR_NATIVE_DEBUG_DUMP (pair_so3lr_native_mpi.cpp:1811-1862): one JSON
+    object with schema so3lr-native-debug-v1, the long-range totals and, per
+    local atom, its tag, type and terms (here from the CPU stand-in of the
+    library, whose row k carries charge 0.01 k, so the tag mapping shows)."""
+    exe = _build(tmp_path, fake=True)
+    pos = np.array([[0.0, 0.0, 0.0], [0.96, 0.0, 0.0], [-0.24, 0.93, 0.0], [3.0, 3.0, 3.0]])
+    types = [1, 2, 2, 1]
+    inp = tmp_path / "atoms.txt"
+    inp.write_text("10.0 4\n" + "".join(f"{t} {float(p[0])!r} {float(p[1])!r} {float(p[2])!r}\n"
+                                          for t, p in zip(types, pos)))
+    dump = tmp_path / "dump.json"
+    monkeypatch.setenv("SO3LR_NATIVE_DEBUG_DUMP", str(dump))
+    res = subprocess.run([str(exe), "run-reversed-tags", "fake", str(inp)], capture_output=True, text=True,
+                         timeout=120)
+    assert res.returncode == 0, res.stdout + res.stderr
+    d = json.loads(dump.read_text())
+    assert d["schema"] == "so3lr-native-debug-v1" and d["natoms"] == 4
+    assert d["tag"] == [4, 3, 2, 1] and d["type"] == [1, 2, 2, 1]
+    z = np.array([8, 1, 1, 8])
+    assert np.allclose(d["learned_energy"], 0.25 * z)
+    assert np.allclose(d["zbl_energy"], 0.125)
+    assert np.allclose(d["physical_energy"], 0.25 * z - 0.125)
+    assert np.allclose(d["partial_charges"], [0.03, 0.02, 0.01, 0.0])  # row = tag - 1
+    assert np.allclose(d["hirshfeld_ratios"], 1.0 + 0.001 * z)
+    assert abs(d["electrostatic_total"] - 0.5 * (0.25 * z - 0.125).sum()) < 1e-12
+    assert abs(d["dispersion_total"] - d["electrostatic_total"]) < 1e-12
+
+
 def test_plugin_registers_both_styles(tmp_path):
     """`plugin load` entry point (lammpsplugin_init): both pair styles are
     registered under their names and their creators construct the styles."""
