@@ -75,6 +75,8 @@ void PairSO3LRB200::settings(int narg, char **arg) {
   if (so3lr_create(model_path_.c_str(), device, &handle_, err, sizeof(err)) != 0)
     error->all(FLERR, std::string("Cannot initialize SO3LR model on the GPU: ") + err);
   comm_ready_ = false;
+  profile_every_ = -1;  // the new handle gets profiling switched on again if asked for
+  profile_calls_ = 0;
 }
 
 void PairSO3LRB200::coeff(int narg, char **arg) {
@@ -164,6 +166,7 @@ void PairSO3LRB200::write_debug_dump(const char *path, const so3lr_result &res, 
 
 void PairSO3LRB200::compute(int eflag, int vflag) {
   ev_init(eflag, vflag);
+  setup_profile();
   const int nlocal = atom->nlocal;
   // the whole system on every rank, ordered by atom tag: the library splits it
   // into its own spatial bricks (one per rank and GPU) and every rank gets the
@@ -273,4 +276,36 @@ void PairSO3LRB200::compute(int eflag, int vflag) {
     utils::logmesg(lmp, "SO3LR_B200_FORCE_PATH=PASS atoms=" + std::to_string(n) +
                            " energy=" + std::to_string(res.energy) + "\n");
   }
+  report_profile();
+}
+
+// Opt-in timing, the counterpart of the reference's SO3_NATIVE_MPI_PROFILE
+// lines (pair_so3lr_native_mpi.cpp:1259-1266, 1887-1956): with
+// $SO3LR_B200_PROFILE set, every $SO3LR_B200_PROFILE_EVERY calls (default 100)
+// rank 0 logs the device time of the pair-filter kernels (CUDA events on the
+// library's stream) and their FP64 rate since the previous line.
+void PairSO3LRB200::setup_profile() {
+  if (profile_every_ >= 0) return;
+  const char *on = std::getenv("SO3LR_B200_PROFILE");
+  const char *every = std::getenv("SO3LR_B200_PROFILE_EVERY");
+  profile_every_ = (on && on[0] != '\0' && std::strcmp(on, "0") != 0) ? (every ? std::atoi(every) : 100) : 0;
+  if (profile_every_ > 0) so3lr_profile(handle_, 1);
+}
+
+void PairSO3LRB200::report_profile() {
+  if (profile_every_ <= 0 || ++profile_calls_ % profile_every_ != 0) return;
+  char err[512] = {0};
+  double ms[2] = {0, 0}, flops[2] = {0, 0};
+  long long launches[2] = {0, 0};
+  for (int k = 0; k < 2; ++k)
+    if (so3lr_profile_read(handle_, k, &ms[k], &launches[k], &flops[k], err, sizeof(err)) != 0)
+      error->all(FLERR, std::string("SO3LR profile read failed: ") + err);
+  if (comm->me != 0) return;
+  char line[320];
+  std::snprintf(line, sizeof(line),
+                "SO3LR_B200_PROFILE calls=%lld filter_forward_ms=%.4f launches=%lld tflops=%.2f "
+                "filter_reverse_ms=%.4f launches=%lld tflops=%.2f\n",
+                profile_calls_, ms[0], launches[0], ms[0] > 0 ? flops[0] / (ms[0] * 1e-3) / 1e12 : 0.0, ms[1],
+                launches[1], ms[1] > 0 ? flops[1] / (ms[1] * 1e-3) / 1e12 : 0.0);
+  utils::logmesg(lmp, line);
 }

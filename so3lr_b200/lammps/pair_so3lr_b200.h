@@ -65,6 +65,10 @@ class PairSO3LRB200 : public Pair {
   void allocate();
   void release();
   void write_debug_dump(const char *path, const so3lr_result &res, int n);
+  void setup_profile();
+  void report_profile();
+  int profile_every_ = -1;  // -1: not read yet, 0: off
+  long long profile_calls_ = 0;
 };
 
 }  // namespace LAMMPS_NS

@@ -88,6 +88,20 @@ int so3lr_virial_atom(so3lr_handle *h, double *vatom, char *, size_t) {
   return 0;
 }
 
+// profiling: each so3lr_compute counts as one launch of 1 ms and 1 GFLOP per kernel
+static long long g_profile_calls = 0;
+static int g_profile_on = 0;
+int so3lr_profile(so3lr_handle *, int enable) {
+  g_profile_on = enable;
+  return 0;
+}
+int so3lr_profile_read(so3lr_handle *, int kernel, double *ms, long long *launches, double *flops, char *, size_t) {
+  *ms = double(g_profile_calls);
+  *launches = g_profile_calls;
+  *flops = 1e9 * double(g_profile_calls);
+  if (kernel == 1) g_profile_calls = 0;
+  return 0;
+}
 // so3lr_compute (one rank): row k of the system (tag k + 1) gets
 //   f = -x, eatom = 0.5 z, charges = 0.01 k, ratios = 1 + 0.001 z,
 //   e_learned = 0.25 z, e_zbl = 0.125, e_lr = 0.25 z - 0.125,
@@ -112,6 +126,7 @@ int so3lr_compute(so3lr_handle *h, const so3lr_frame *in, so3lr_result *out, cha
   }
   out->energy = e;
   for (int c = 0; c < 6; ++c) out->virial[c] = 0.0;
+  if (g_profile_on) ++g_profile_calls;
   return 0;
 }
 int so3lr_nccl_unique_id(char *, char *err, size_t errlen) { return fake_fail("not in the CPU stand-in", err, errlen); }

@@ -4,6 +4,7 @@
 //                                       (types 1 = O, 2 = H); prints JSON with energy, virial, forces
 //   test_pair_shim run-reversed-tags MODEL INPUT
 //                                       the same with atom i tagged n - i
+//   test_pair_shim repeat MODEL INPUT   four computes; prints the style's log
 //   test_pair_shim turbo-parse MODEL    so3lr/b200/turbo parsing and refusals on one rank, and a
 //                                       coordinator failure reaching every partition of a universe
 //   test_pair_shim turbo-run MODEL INPUT
@@ -118,6 +119,28 @@ static int parse_checks(const char *model) {
   }
   std::printf("%s\n", fails ? "PARSE FAIL" : "PARSE OK");
   return fails ? 1 : 0;
+}
+
+// four computes of the atoms in INPUT; prints the pair style's log
+static int repeat(const char *model, const char *input) {
+  std::ifstream in(input);
+  double L;
+  int n;
+  in >> L >> n;
+  LAMMPS lmp;
+  lmp.atom.ntypes = 2;
+  lmp.atom.resize(n);
+  for (int i = 0; i < n; ++i) in >> lmp.atom.type[i] >> lmp.atom.x[i][0] >> lmp.atom.x[i][1] >> lmp.atom.x[i][2];
+  for (int d = 0; d < 3; ++d) lmp.domain.prd[d] = L;
+  PairSO3LRB200 pair(&lmp);
+  char *sargs[] = {(char *)model};
+  pair.settings(1, sargs);
+  char *cargs[] = {(char *)"*", (char *)"*", (char *)"O", (char *)"H"};
+  pair.coeff(4, cargs);
+  pair.init_style();
+  for (int k = 0; k < 4; ++k) pair.compute(1, 0);
+  std::printf("%s", lmp.log.c_str());
+  return 0;
 }
 
 static int run(const char *model, const char *input, bool reverse_tags = false) {
@@ -464,6 +487,7 @@ int main(int argc, char **argv) {
   if (argc >= 3 && std::string(argv[1]) == "parse") return parse_checks(argv[2]);
   if (argc >= 4 && std::string(argv[1]) == "run") return run(argv[2], argv[3]);
   if (argc >= 4 && std::string(argv[1]) == "run-reversed-tags") return run(argv[2], argv[3], true);
+  if (argc >= 4 && std::string(argv[1]) == "repeat") return repeat(argv[2], argv[3]);
   if (argc >= 5 && std::string(argv[1]) == "multirank") return multirank(argv[2], argv[3], std::atoi(argv[4]));
   if (argc >= 3 && std::string(argv[1]) == "turbo-parse") return turbo_parse_checks(argv[2]);
   if (argc >= 4 && std::string(argv[1]) == "turbo-run") return turbo_run(argv[2], argv[3]);

@@ -108,6 +108,23 @@ def test_debug_dump_in_the_reference_schema(tmp_path, monkeypatch):
     assert abs(d["dispersion_total"] - d["electrostatic_total"]) < 1e-12
 
 
+def test_profile_lines(tmp_path, monkeypatch):
+    """SO3LR_B200_PROFILE / SO3LR_B200_PROFILE_EVERY: every N-th compute logs
+    the pair-filter kernel times since the previous line (the counterpart of
+    the reference's SO3_NATIVE_MPI_PROFILE lines)."""
+    exe = _build(tmp_path, fake=True)
+    inp = tmp_path / "atoms.txt"
+    inp.write_text("10.0 3\n1 0.0 0.0 0.0\n2 0.96 0.0 0.0\n2 -0.24 0.93 0.0\n")
+    monkeypatch.setenv("SO3LR_B200_PROFILE", "1")
+    monkeypatch.setenv("SO3LR_B200_PROFILE_EVERY", "2")
+    res = subprocess.run([str(exe), "repeat", "fake", str(inp)], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0, res.stdout + res.stderr
+    lines = [ln for ln in res.stdout.splitlines() if ln.startswith("SO3LR_B200_PROFILE ")]
+    assert len(lines) == 2, res.stdout
+    assert "calls=2 filter_forward_ms=2.0000 launches=2 tflops=1.00" in lines[0]
+    assert "calls=4 " in lines[1] and "filter_reverse_ms=2.0000 launches=2" in lines[1]
+
+
 def test_plugin_registers_both_styles(tmp_path):
     """`plugin load` entry point (lammpsplugin_init): both pair styles are
     registered under their names and their creators construct the styles."""
