@@ -64,16 +64,26 @@ void PairSO3LRB200::settings(int narg, char **arg) {
   release();
   char err[2048] = {0};
   so3lr_arch_info info{};
-  if (so3lr_inspect_model(model_path_.c_str(), &info, err, sizeof(err)) != 0)
-    error->all(FLERR, std::string("Cannot initialize SO3LR model: ") + err);
-  sr_cutoff_ = info.sr_cutoff;
-  lr_cutoff_ = info.lr_cutoff;
-  // one GPU per MPI rank: $SO3LR_B200_DEVICE when set, else the rank number
-  // (ranks of one node on that node's GPUs)
-  const char *dev = std::getenv("SO3LR_B200_DEVICE");
-  const int device = dev ? std::atoi(dev) : comm->me;
-  if (so3lr_create(model_path_.c_str(), device, &handle_, err, sizeof(err)) != 0)
-    error->all(FLERR, std::string("Cannot initialize SO3LR model on the GPU: ") + err);
+  std::string problem;
+  if (so3lr_inspect_model(model_path_.c_str(), &info, err, sizeof(err)) != 0) {
+    problem = std::string("Cannot initialize SO3LR model: ") + err;
+  } else {
+    sr_cutoff_ = info.sr_cutoff;
+    lr_cutoff_ = info.lr_cutoff;
+    // one GPU per MPI rank: $SO3LR_B200_DEVICE when set, else the rank number
+    // (ranks of one node on that node's GPUs)
+    const char *dev = std::getenv("SO3LR_B200_DEVICE");
+    const int device = dev ? std::atoi(dev) : comm->me;
+    if (so3lr_create(model_path_.c_str(), device, &handle_, err, sizeof(err)) != 0)
+      problem = std::string("Cannot initialize SO3LR model on the GPU: ") + err;
+  }
+  // a failure on some ranks only (a missing GPU, a file one node cannot read)
+  // must not leave the others waiting in the next collective
+  int bad = problem.empty() ? 0 : 1, nbad = 0;
+  MPI_Allreduce(&bad, &nbad, 1, MPI_INT, MPI_SUM, world);
+  if (nbad == comm->nprocs) error->all(FLERR, problem);
+  if (bad) error->one(FLERR, problem);
+  if (nbad) error->all(FLERR, "SO3LR model initialization failed on another MPI rank");
   comm_ready_ = false;
   profile_every_ = -1;  // the new handle gets profiling switched on again if asked for
   profile_calls_ = 0;

@@ -25,6 +25,7 @@ class Error {
   [[noreturn]] void all(const char *, int, const std::string &msg) { throw std::runtime_error(msg); }
   [[noreturn]] void universe_all(const char *, int, const std::string &msg) { throw std::runtime_error(msg); }
   [[noreturn]] void universe_one(const char *, int, const std::string &msg) { throw std::runtime_error(msg); }
+  [[noreturn]] void one(const char *, int, const std::string &msg) { throw std::runtime_error(msg); }
 };
 
 class Memory {

@@ -15,6 +15,7 @@
 //                                       so3lr/b200 on NRANKS MPI ranks (threads, one GPU each);
 //                                       INPUT as for run; atom i lives on rank (7 i) % NRANKS with
 //                                       tag i + 1; prints one JSON line per rank
+//   test_pair_shim rank-failure MODEL   two ranks, only rank 1 cannot load the model
 //   test_pair_shim plugin               lammpsplugin_init registers both styles; their
 //                                       creators build the pair objects
 //   test_pair_shim turbo-refuse MODEL INPUT
@@ -251,6 +252,36 @@ static int multirank(const char *model, const char *input, int nranks) {
   return rc;
 }
 
+// two MPI ranks (threads) where only rank 1 cannot load the model: rank 1
+// reports its own error, rank 0 learns of it instead of waiting
+static int rank_failure(const char *model) {
+  std::vector<std::string> msgs(2, "no error");
+  auto errs = mpi_stub_run(2, [&](int r) {
+    LAMMPS lmp;
+    lmp.comm.me = r;
+    lmp.comm.nprocs = 2;
+    lmp.atom.ntypes = 2;
+    lmp.atom.resize(3);
+    PairSO3LRB200 pair(&lmp);
+    char *good[] = {(char *)model};
+    char *bad[] = {(char *)"/nonexistent/model.so3lr"};
+    pair.settings(1, r == 1 ? bad : good);
+  });
+  for (int r = 0; r < 2; ++r)
+    if (errs[r]) {
+      try {
+        std::rethrow_exception(errs[r]);
+      } catch (const std::exception &e) {
+        msgs[r] = e.what();
+      }
+    }
+  const bool ok = msgs[1].find("cannot open") != std::string::npos &&
+                  msgs[0].find("failed on another MPI rank") != std::string::npos;
+  std::printf("rank 0: %s\nrank 1: %s\n%s\n", msgs[0].c_str(), msgs[1].c_str(),
+              ok ? "RANK FAILURE OK" : "RANK FAILURE FAIL");
+  return ok ? 0 : 1;
+}
+
 static int turbo_parse_checks(const char *model) {
   int fails = 0;
   {
@@ -484,6 +515,7 @@ static int plugin_check() {
 
 int main(int argc, char **argv) {
   if (argc >= 2 && std::string(argv[1]) == "plugin") return plugin_check();
+  if (argc >= 3 && std::string(argv[1]) == "rank-failure") return rank_failure(argv[2]);
   if (argc >= 3 && std::string(argv[1]) == "parse") return parse_checks(argv[2]);
   if (argc >= 4 && std::string(argv[1]) == "run") return run(argv[2], argv[3]);
   if (argc >= 4 && std::string(argv[1]) == "run-reversed-tags") return run(argv[2], argv[3], true);

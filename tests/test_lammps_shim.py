@@ -125,6 +125,16 @@ def test_profile_lines(tmp_path, monkeypatch):
     assert "calls=4 " in lines[1] and "filter_reverse_ms=2.0000 launches=2" in lines[1]
 
 
+def test_model_failure_on_one_rank_stops_every_rank(tmp_path):
+    """so3lr/b200 on two ranks (threads) where only one cannot load the model:
+    that rank reports the loader's message, the other learns of it in the same
+    collective instead of waiting (the reference's allreduced error flags,
+    pair_so3lr_native_mpi.cpp:1293, 1388)."""
+    exe = _build(tmp_path, fake=True)
+    res = subprocess.run([str(exe), "rank-failure", "fake"], capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0 and "RANK FAILURE OK" in res.stdout, res.stdout + res.stderr
+
+
 def test_plugin_registers_both_styles(tmp_path):
     """`plugin load` entry point (lammpsplugin_init): both pair styles are
     registered under their names and their creators construct the styles."""
