@@ -50,6 +50,17 @@ static int host_checks(const char *model) {
 
   CHECK(so3lr_partition(2, x, lo, len, 2, owner) == 0 && owner[0] != owner[1], "two bricks split two far atoms");
 
+  /* NULL arguments come back as an error status with a message, never a crash */
+  err[0] = '\0';
+  CHECK(so3lr_compute(NULL, NULL, NULL, err, sizeof err) != 0 && strlen(err) > 0, "compute(NULL)");
+  err[0] = '\0';
+  CHECK(so3lr_compute_batch(NULL, NULL, NULL, err, sizeof err) != 0 && strlen(err) > 0, "compute_batch(NULL)");
+  err[0] = '\0';
+  CHECK(so3lr_virial_atom(NULL, NULL, err, sizeof err) != 0 && strlen(err) > 0, "virial_atom(NULL)");
+  err[0] = '\0';
+  CHECK(so3lr_md_run(NULL, 1, 0.0005, err, sizeof err) != 0 && strlen(err) > 0, "md_run(NULL)");
+  CHECK(so3lr_create(model, 0, NULL, err, sizeof err) != 0, "create without an output pointer");
+
   if (so3lr_create(model, 0, &h, err, sizeof err) == 0) {
     so3lr_destroy(h); /* a GPU is present */
   } else {
