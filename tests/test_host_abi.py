@@ -100,6 +100,30 @@ def test_integrity_checks(tmp_path, corrupt, message):
         inspect_model(path)
 
 
+def test_random_corruptions_are_refused(tmp_path):
+    """A model file is untrusted input: any single flipped byte (header,
+    manifest or any tensor) and any truncation is refused with an error, never
+    accepted and never a crash."""
+    from so3lr_b200 import So3lrError, inspect_model
+    rng = np.random.default_rng(2024)
+    good = MODEL.read_bytes()
+    msize = struct.unpack_from("<Q", good, 16)[0]
+    # a spread over the three regions: header, manifest, payload
+    positions = list(rng.integers(0, 128, 8)) + list(rng.integers(128, 128 + msize, 16)) + \
+        list(rng.integers(128 + msize, len(good), 24))
+    path = tmp_path / "corrupt.so3lr"
+    for pos in positions:
+        data = bytearray(good)
+        data[pos] ^= int(rng.integers(1, 256))
+        path.write_bytes(bytes(data))
+        with pytest.raises(So3lrError):
+            inspect_model(path)
+    for cut in rng.integers(0, len(good), 8):
+        path.write_bytes(good[:int(cut)])
+        with pytest.raises(So3lrError):
+            inspect_model(path)
+
+
 def test_truncated_and_missing_model(tmp_path):
     from so3lr_b200 import So3lrError, inspect_model
     short = tmp_path / "short.so3lr"
