@@ -168,7 +168,9 @@ int so3lr_compute_device(so3lr_handle *h, const so3lr_frame *in_device_x, double
 int so3lr_nccl_unique_id(char out[128], char *err, size_t errlen);
 int so3lr_comm_init(so3lr_handle *h, int nranks, int rank, const char unique_id[128], char *err, size_t errlen);
 int so3lr_owned_atoms(const so3lr_handle *h);
-/* Host-only: the rank that owns each atom under the brick partition above. */
+/* Host-only: the rank that owns each atom under the brick partition above.
+ * Returns 2 for a NULL pointer, natoms outside 1..2^30 or a box that is not
+ * finite and positive. */
 int so3lr_partition(long long natoms, const double *x, const double boxlo[3], const double boxlen[3], int nranks,
                     int *owner);
 

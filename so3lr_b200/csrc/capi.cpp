@@ -3,6 +3,7 @@
 // (plugins/lammps/pair_so3lr_native_mpi.cpp:1133-1136, 1974-1977).
 #include "../../include/so3lr_b200.h"
 
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <exception>
@@ -303,18 +304,22 @@ int so3lr_owned_atoms(const so3lr_handle *h) { return h ? h->eval->owned_atoms()
 
 int so3lr_partition(long long natoms, const double *x, const double boxlo[3], const double boxlen[3], int nranks,
                     int *owner) {
-  if (natoms <= 0 || !x || !boxlo || !boxlen || nranks < 1 || !owner) return 2;
+  if (natoms <= 0 || natoms > (1LL << 30) || !x || !boxlo || !boxlen || nranks < 1 || !owner) return 2;
   SystemSpec s;
   s.n = int(natoms);
   s.periodic = true;
   for (int d = 0; d < 3; ++d) {
     s.lo[d] = boxlo[d];
     s.len[d] = boxlen[d];
-    if (!(s.len[d] > 0)) return 2;
+    if (!(s.len[d] > 0) || !std::isfinite(s.len[d]) || !std::isfinite(s.lo[d])) return 2;
   }
-  const auto o = so3lr_b200::partition_atoms(s, x, nranks);
-  for (long long i = 0; i < natoms; ++i) owner[i] = o[std::size_t(i)];
-  return 0;
+  try {
+    const auto o = so3lr_b200::partition_atoms(s, x, nranks);
+    for (long long i = 0; i < natoms; ++i) owner[i] = o[std::size_t(i)];
+    return 0;
+  } catch (const std::exception &) {
+    return 1;
+  }
 }
 
 int so3lr_profile(so3lr_handle *h, int enable) {

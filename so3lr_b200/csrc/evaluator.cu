@@ -448,8 +448,11 @@ void Evaluator::prepare(const SystemSpec &spec_in, const double *host_x) {
     throw Error("SO3LR: per-image charge/multiplicity arrays have the wrong length");
   if (spec.periodic) {
     if (nimg != 1) throw Error("SO3LR: batched images must be non-periodic");
-    for (int d = 0; d < 3; ++d)
+    for (int d = 0; d < 3; ++d) {
       if (!(spec.len[d] > 0.0)) throw Error("SO3LR: periodic box lengths must be positive");
+      if (!std::isfinite(spec.len[d]) || !std::isfinite(spec.lo[d]))
+        throw Error("SO3LR: periodic box bounds must be finite");
+    }
   } else if (!open_cells_possible(spec, host_x)) {
     for (int i = 0; i < nimg; ++i)
       if (spec.image_start[i + 1] - spec.image_start[i] > 20000)
@@ -548,7 +551,8 @@ void Evaluator::prepare(const SystemSpec &spec_in, const double *host_x) {
   for (int d = 0; d < 3; ++d) {
     g.lo[d] = spec.lo[d];
     g.len[d] = spec.periodic ? spec.len[d] : 1.0;
-    g.ncell[d] = spec.periodic ? std::max(1, int(std::floor(spec.len[d] / sr_cut_))) : 1;
+    // clamped before the integer conversion; an oversized grid is refused below
+    g.ncell[d] = spec.periodic ? int(std::min(std::max(std::floor(spec.len[d] / sr_cut_), 1.0), double(1 << 20))) : 1;
   }
   if (open_cells_possible(spec, host_x)) {
     // one open system: a non-wrapping grid over the bounding box of the

@@ -49,6 +49,12 @@ static int host_checks(const char *model) {
   CHECK(so3lr_validate_charge_spin(counts, 1.0, 2.0, err, sizeof err) == 0, "cation doublet");
 
   CHECK(so3lr_partition(2, x, lo, len, 2, owner) == 0 && owner[0] != owner[1], "two bricks split two far atoms");
+  {
+    const double bad_len[3] = {10.0, HUGE_VAL, 10.0}, flat_len[3] = {10.0, 0.0, 10.0};
+    CHECK(so3lr_partition(2, x, lo, bad_len, 2, owner) == 2, "partition refuses an infinite box");
+    CHECK(so3lr_partition(2, x, lo, flat_len, 2, owner) == 2, "partition refuses a zero box length");
+    CHECK(so3lr_partition(0, x, lo, len, 2, owner) == 2, "partition refuses zero atoms");
+  }
 
   /* NULL arguments come back as an error status with a message, never a crash */
   err[0] = '\0';
