@@ -128,6 +128,19 @@ void PairSO3LRB200::init_style() {
   char err[512] = {0};
   if (so3lr_validate_charge_spin(counts, total_charge_, multiplicity_, err, sizeof(err)) != 0)
     error->all(FLERR, std::string("SO3LR charge/multiplicity: ") + err);
+  if (comm->me == 0) {
+    char line[160];
+    std::snprintf(line, sizeof(line), "SO3LR: total charge %g, spin multiplicity %g\n", total_charge_,
+                  multiplicity_);
+    utils::logmesg(lmp, line);
+    if (total_charge_ != 0.0 && periodic) {
+      std::snprintf(line, sizeof(line),
+                    "SO3LR: net charge %g in a periodic cell. SO3LR's long range is truncated real-space "
+                    "Coulomb, so the energy is defined, but there is no neutralizing background",
+                    total_charge_);
+      error->warning(FLERR, line);
+    }
+  }
   // several ranks: one NCCL communicator over the ranks' GPUs, id from rank 0
   if (comm->nprocs > 1 && !comm_ready_) {
     char uid[128] = {0};

@@ -4,7 +4,8 @@
 //                                       (types 1 = O, 2 = H); prints JSON with energy, virial, forces
 //   test_pair_shim run-reversed-tags MODEL INPUT
 //                                       the same with atom i tagged n - i
-//   test_pair_shim repeat MODEL INPUT   four computes; prints the style's log
+//   test_pair_shim repeat MODEL INPUT [CHARGE MULT]
+//                                       four computes; prints the style's log and warnings
 //   test_pair_shim turbo-parse MODEL    so3lr/b200/turbo parsing and refusals on one rank, and a
 //                                       coordinator failure reaching every partition of a universe
 //   test_pair_shim turbo-run MODEL INPUT
@@ -122,8 +123,8 @@ static int parse_checks(const char *model) {
   return fails ? 1 : 0;
 }
 
-// four computes of the atoms in INPUT; prints the pair style's log
-static int repeat(const char *model, const char *input) {
+// four computes of the atoms in INPUT; prints the pair style's log and warnings
+static int repeat(const char *model, const char *input, const char *charge = nullptr, const char *mult = nullptr) {
   std::ifstream in(input);
   double L;
   int n;
@@ -134,13 +135,13 @@ static int repeat(const char *model, const char *input) {
   for (int i = 0; i < n; ++i) in >> lmp.atom.type[i] >> lmp.atom.x[i][0] >> lmp.atom.x[i][1] >> lmp.atom.x[i][2];
   for (int d = 0; d < 3; ++d) lmp.domain.prd[d] = L;
   PairSO3LRB200 pair(&lmp);
-  char *sargs[] = {(char *)model};
-  pair.settings(1, sargs);
+  char *sargs[] = {(char *)model, (char *)charge, (char *)mult};
+  pair.settings(charge && mult ? 3 : 1, sargs);
   char *cargs[] = {(char *)"*", (char *)"*", (char *)"O", (char *)"H"};
   pair.coeff(4, cargs);
   pair.init_style();
   for (int k = 0; k < 4; ++k) pair.compute(1, 0);
-  std::printf("%s", lmp.log.c_str());
+  std::printf("%s%s", lmp.log.c_str(), lmp.error.warnings.c_str());
   return 0;
 }
 
@@ -179,7 +180,10 @@ static int run(const char *model, const char *input, bool reverse_tags = false) 
     for (int k = 0; k < 6; ++k) std::printf(k ? ", %.17g" : "%.17g", pair.vatom[i][k]);
     std::printf("]");
   }
-  std::printf("], \"log\": \"%s\"}\n", lmp.log.substr(0, lmp.log.size() - 1).c_str());
+  std::string log = lmp.log;  // one JSON string: the log's lines joined by " | "
+  while (!log.empty() && log.back() == '\n') log.pop_back();
+  for (std::size_t p = log.find('\n'); p != std::string::npos; p = log.find('\n', p)) log.replace(p, 1, " | ");
+  std::printf("], \"log\": \"%s\"}\n", log.c_str());
   return 0;
 }
 
@@ -519,6 +523,7 @@ int main(int argc, char **argv) {
   if (argc >= 3 && std::string(argv[1]) == "parse") return parse_checks(argv[2]);
   if (argc >= 4 && std::string(argv[1]) == "run") return run(argv[2], argv[3]);
   if (argc >= 4 && std::string(argv[1]) == "run-reversed-tags") return run(argv[2], argv[3], true);
+  if (argc >= 6 && std::string(argv[1]) == "repeat") return repeat(argv[2], argv[3], argv[4], argv[5]);
   if (argc >= 4 && std::string(argv[1]) == "repeat") return repeat(argv[2], argv[3]);
   if (argc >= 5 && std::string(argv[1]) == "multirank") return multirank(argv[2], argv[3], std::atoi(argv[4]));
   if (argc >= 3 && std::string(argv[1]) == "turbo-parse") return turbo_parse_checks(argv[2]);

@@ -94,7 +94,9 @@ def test_debug_dump_in_the_reference_schema(tmp_path, monkeypatch):
     monkeypatch.setenv("SO3LR_NATIVE_DEBUG_DUMP", str(dump))
     res = subprocess.run([str(exe), "run-reversed-tags", "fake", str(inp)], capture_output=True, text=True,
                          timeout=120)
-    assert res.returncode == 0, res.stdout + res.stderr
+    out = _json_lines(res, 1)[0]
+    assert "SO3LR: total charge 0, spin multiplicity 1" in out["log"]
+    assert "SO3LR_B200_FORCE_PATH=PASS" in out["log"]
     d = json.loads(dump.read_text())
     assert d["schema"] == "so3lr-native-debug-v1" and d["natoms"] == 4
     assert d["tag"] == [4, 3, 2, 1] and d["type"] == [1, 2, 2, 1]
@@ -123,6 +125,23 @@ def test_profile_lines(tmp_path, monkeypatch):
     assert len(lines) == 2, res.stdout
     assert "calls=2 filter_forward_ms=2.0000 launches=2 tflops=1.00" in lines[0]
     assert "calls=4 " in lines[1] and "filter_reverse_ms=2.0000 launches=2" in lines[1]
+
+
+def test_charge_log_line_and_periodic_charge_warning(tmp_path):
+    """init_style logs the total charge and multiplicity once and warns about a
+    net charge in a periodic cell (pair_so3lr_native_mpi.cpp:1225-1234)."""
+    exe = _build(tmp_path, fake=True)
+    inp = tmp_path / "atoms.txt"
+    inp.write_text("10.0 3\n1 0.0 0.0 0.0\n2 0.96 0.0 0.0\n2 -0.24 0.93 0.0\n")
+    res = subprocess.run([str(exe), "repeat", "fake", str(inp), "1", "2"], capture_output=True, text=True,
+                         timeout=120)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "SO3LR: total charge 1, spin multiplicity 2" in res.stdout
+    warn = [ln for ln in res.stdout.splitlines() if ln.startswith("WARNING:")]
+    assert len(warn) == 1 and "net charge 1 in a periodic cell" in warn[0], res.stdout
+    res = subprocess.run([str(exe), "repeat", "fake", str(inp)], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "SO3LR: total charge 0, spin multiplicity 1" in res.stdout and "WARNING" not in res.stdout
 
 
 def test_model_failure_on_one_rank_stops_every_rank(tmp_path):
@@ -193,8 +212,7 @@ def test_pair_style_compute_matches_c_abi(tmp_path, gpu_model):
         lines.append(f"{1 if zi == 8 else 2} {float(p[0])!r} {float(p[1])!r} {float(p[2])!r}")
     inp.write_text("\n".join(lines) + "\n")
     res = subprocess.run([str(exe), "run", str(MODEL), str(inp)], capture_output=True, text=True, timeout=300)
-    assert res.returncode == 0, res.stdout + res.stderr
-    out = json.loads(res.stdout.strip().splitlines()[-1])
+    out = _json_lines(res, 1)[0]
     ref = gpu_model.compute(w.pos, w.z, cell=w.cell, boxlo=w.boxlo)
     ref_va = gpu_model.virial_atom(len(w.z))
     assert np.array_equal(np.array(out["vatom"]), ref_va)
