@@ -122,6 +122,16 @@ def _ptr(a: np.ndarray | None, ctype=C.c_double):
     return a.ctypes.data_as(C.POINTER(ctype))
 
 
+def _array(a, dtype, shape: tuple, what: str) -> np.ndarray:
+    """C-contiguous copy-or-view of `a` with exactly `shape`: the library reads
+    and writes as many elements as the system has, so a short array is refused
+    here rather than overrun there."""
+    out = np.ascontiguousarray(a, dtype=dtype)
+    if out.shape != shape:
+        raise ValueError(f"{what} must have shape {shape}, got {out.shape}")
+    return out
+
+
 def _check(rc: int, err: C.Array) -> None:
     if rc != 0:
         raise So3lrError(err.value.decode(errors="replace") or f"status {rc}")
@@ -171,6 +181,7 @@ class So3lrB200:
 
     def __init__(self, model_path: os.PathLike | str = DEFAULT_MODEL, device: int = 0):
         self._lib = load_library()
+        self._natoms = None
         handle = C.c_void_p()
         err = C.create_string_buffer(4096)
         _check(self._lib.so3lr_create(str(model_path).encode(), int(device), C.byref(handle), err, 4096), err)
@@ -224,9 +235,19 @@ class So3lrB200:
     def launch_count(self) -> int:
         return int(self._lib.so3lr_launch_count())
 
-    def virial_atom(self, natoms: int) -> np.ndarray:
+    def _system_size(self, natoms) -> int:
+        """The atom count of the handle's current system (the library writes
+        that many rows); `natoms`, when given, must agree with it."""
+        n = getattr(self, "_natoms", None)
+        if n is None:
+            raise So3lrError("no evaluation has run on this handle")
+        if natoms is not None and int(natoms) != n:
+            raise ValueError(f"natoms = {natoms} but the last evaluation had {n} atoms")
+        return n
+
+    def virial_atom(self, natoms: int | None = None) -> np.ndarray:
         """Per-atom virial (natoms x 6, xx yy zz xy xz yz) of the last evaluation."""
-        out = np.empty((int(natoms), 6), dtype=np.float64)
+        out = np.empty((self._system_size(natoms), 6), dtype=np.float64)
         err = C.create_string_buffer(1024)
         _check(self._lib.so3lr_virial_atom(self._h, _ptr(out), err, 1024), err)
         return out
@@ -238,15 +259,17 @@ class So3lrB200:
 
     @staticmethod
     def _frame(x, z, cell, boxlo, charge, multiplicity):
-        x = np.ascontiguousarray(x, dtype=np.float64)
         z = np.ascontiguousarray(z, dtype=np.int32)
+        if z.ndim != 1 or len(z) == 0:
+            raise ValueError("atomic numbers must be a non-empty 1-D array")
+        x = _array(x, np.float64, (len(z), 3), "positions")
         fr = Frame()
         fr.natoms = len(z)
         fr.x = _ptr(x)
         fr.z = _ptr(z, C.c_int)
         fr.periodic = 1 if cell is not None else 0
-        lo = np.zeros(3) if boxlo is None else np.asarray(boxlo, dtype=np.float64)
-        ln = np.zeros(3) if cell is None else np.asarray(cell, dtype=np.float64)
+        lo = np.zeros(3) if boxlo is None else _array(boxlo, np.float64, (3,), "boxlo")
+        ln = np.zeros(3) if cell is None else _array(cell, np.float64, (3,), "cell (orthorhombic box lengths)")
         for d in range(3):
             fr.boxlo[d] = float(lo[d])
             fr.boxlen[d] = float(ln[d])
@@ -261,6 +284,7 @@ class So3lrB200:
         forces; returned as out["forces"]."""
         fr, x, z = self._frame(x, z, cell, boxlo, charge, multiplicity)
         n = len(z)
+        self._natoms = None  # unknown until the call succeeds
         out = {k: np.empty(n) for k in ("eatom", "charges", "ratios", "e_learned", "e_zbl", "e_lr", "e_elec",
                                         "e_disp")} if terms else {}
         if forces_out is not None:
@@ -276,17 +300,21 @@ class So3lrB200:
             setattr(res, k, _ptr(out.get(k)))
         err = C.create_string_buffer(4096)
         _check(self._lib.so3lr_compute(self._h, C.byref(fr), C.byref(res), err, 4096), err)
+        self._natoms = n
         out["energy"] = res.energy
         out["virial"] = np.array(res.virial[:])
         return out
 
     def compute_batch(self, x, z, image_offsets, image_charge, image_multiplicity) -> dict:
-        x = np.ascontiguousarray(x, dtype=np.float64)
         z = np.ascontiguousarray(z, dtype=np.int32)
         off = np.ascontiguousarray(image_offsets, dtype=np.int64)
-        q = np.ascontiguousarray(image_charge, dtype=np.float64)
-        m = np.ascontiguousarray(image_multiplicity, dtype=np.float64)
+        if z.ndim != 1 or len(z) == 0 or off.ndim != 1 or len(off) < 2:
+            raise ValueError("atomic numbers must be a non-empty 1-D array and image_offsets hold K + 1 entries")
         n, nimg = len(z), len(off) - 1
+        x = _array(x, np.float64, (n, 3), "positions")
+        q = _array(image_charge, np.float64, (nimg,), "image_charge")
+        m = _array(image_multiplicity, np.float64, (nimg,), "image_multiplicity")
+        self._natoms = None
         out = {"forces": np.empty((n, 3)), "eatom": np.empty(n), "charges": np.empty(n),
                "image_energy": np.empty(nimg)}
         b = Batch(natoms=n, nimages=nimg, x=_ptr(x), z=_ptr(z, C.c_int), image_offsets=_ptr(off, C.c_longlong),
@@ -295,11 +323,15 @@ class So3lrB200:
                         image_energy=_ptr(out["image_energy"]))
         err = C.create_string_buffer(4096)
         _check(self._lib.so3lr_compute_batch(self._h, C.byref(b), C.byref(r), err, 4096), err)
+        self._natoms = n
         return out
 
     def compute_device(self, x_ptr: int, z, cell, boxlo, f_ptr: int, charge=0.0, multiplicity=1.0):
         """Positions/forces already in device memory of this handle's GPU."""
         z = np.ascontiguousarray(z, dtype=np.int32)
+        if z.ndim != 1 or len(z) == 0:
+            raise ValueError("atomic numbers must be a non-empty 1-D array")
+        self._natoms = None
         fr = Frame()
         fr.natoms = len(z)
         fr.x = C.cast(C.c_void_p(x_ptr), _dp)
@@ -315,6 +347,7 @@ class So3lrB200:
         err = C.create_string_buffer(4096)
         _check(self._lib.so3lr_compute_device(self._h, C.byref(fr), C.c_void_p(f_ptr), None, C.byref(e),
                                               C.cast(vir, _dp), err, 4096), err)
+        self._natoms = len(z)
         return e.value, np.array(vir[:])
 
     def long_range_noalloc(self, natoms: int, x_ptr: int, q_ptr: int, ratio_ptr: int, z_ptr: int, e_lr_ptr: int,
@@ -329,10 +362,12 @@ class So3lrB200:
 
     def md_init(self, x, z, cell, boxlo, v, mass, charge=0.0, multiplicity=1.0):
         fr, x, z = self._frame(x, z, cell, boxlo, charge, multiplicity)
-        v = np.ascontiguousarray(v, dtype=np.float64)
-        mass = np.ascontiguousarray(mass, dtype=np.float64)
+        v = _array(v, np.float64, (len(z), 3), "velocities")
+        mass = _array(mass, np.float64, (len(z),), "masses")
+        self._natoms = None
         err = C.create_string_buffer(4096)
         _check(self._lib.so3lr_md_init(self._h, C.byref(fr), _ptr(v), _ptr(mass), err, 4096), err)
+        self._natoms = len(z)
 
     def md_thermostat(self, t_target_k: float, t_damp_ps: float, chain: int = 3) -> None:
         """Nose-Hoover chain for the following md_run calls (t_damp_ps <= 0: NVE)."""
@@ -349,7 +384,8 @@ class So3lrB200:
         err = C.create_string_buffer(4096)
         _check(self._lib.so3lr_md_run(self._h, int(nsteps), float(dt_ps), err, 4096), err)
 
-    def md_state(self, n: int) -> dict:
+    def md_state(self, n: int | None = None) -> dict:
+        n = self._system_size(n)
         x, v, f = np.empty((n, 3)), np.empty((n, 3)), np.empty((n, 3))
         e = C.c_double()
         err = C.create_string_buffer(4096)

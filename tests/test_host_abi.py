@@ -174,6 +174,40 @@ def test_charge_multiplicity_validation(z, q, m, ok):
     assert (problem == "") == ok, problem
 
 
+def test_python_binding_refuses_mismatched_arrays():
+    """The library reads and writes as many rows as the system has atoms, so
+    the binding checks every array's shape first: a short array is a
+    ValueError, never an overrun."""
+    from so3lr_b200 import So3lrB200, So3lrError
+    z = np.array([8, 1, 1])
+    with pytest.raises(ValueError, match="positions"):
+        So3lrB200._frame(np.zeros((2, 3)), z, None, None, 0.0, 1.0)
+    with pytest.raises(ValueError, match="cell"):
+        So3lrB200._frame(np.zeros((3, 3)), z, np.eye(3), None, 0.0, 1.0)
+    with pytest.raises(ValueError, match="atomic numbers"):
+        So3lrB200._frame(np.zeros((0, 3)), [], None, None, 0.0, 1.0)
+    fr, _, _ = So3lrB200._frame(np.zeros((3, 3)), z, [10.0, 11.0, 12.0], [0.0, 0.0, 0.0], 1.0, 2.0)
+    assert fr.natoms == 3 and fr.periodic == 1 and fr.boxlen[1] == 11.0 and fr.multiplicity == 2.0
+    h = So3lrB200.__new__(So3lrB200)  # no GPU here: only the host-side checks run
+    with pytest.raises(ValueError, match="image_charge"):
+        h.compute_batch(np.zeros((3, 3)), z, [0, 3], [0.0, 1.0], [1.0])
+    with pytest.raises(ValueError, match="positions"):
+        h.compute_batch(np.zeros((2, 3)), z, [0, 3], [0.0], [1.0])
+    with pytest.raises(ValueError, match="image_offsets"):
+        h.compute_batch(np.zeros((3, 3)), z, [0], [], [])
+    with pytest.raises(ValueError, match="velocities"):
+        h.md_init(np.zeros((3, 3)), z, None, None, np.zeros((2, 3)), np.ones(3))
+    with pytest.raises(ValueError, match="masses"):
+        h.md_init(np.zeros((3, 3)), z, None, None, np.zeros((3, 3)), np.ones(4))
+    with pytest.raises(So3lrError, match="no evaluation"):
+        h.virial_atom()
+    h._natoms = 3
+    with pytest.raises(ValueError, match="last evaluation had 3 atoms"):
+        h.virial_atom(5)
+    with pytest.raises(ValueError, match="last evaluation had 3 atoms"):
+        h.md_state(2)
+
+
 def test_create_without_gpu_fails_cleanly():
     """On a host without a usable GPU the handle is refused with a message, never a crash."""
     import torch
