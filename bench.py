@@ -96,20 +96,27 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        rows = []
-        for line in open(self.path).read().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
+        text = open(self.path).read()
         os.unlink(self.path)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k].lower().startswith("active")})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": reasons, "samples": len(rows)}
+        return summarize_clocks(text)
+
+
+def summarize_clocks(text: str) -> dict:
+    """Median SM clock, maximum SM clock and the throttle reasons seen Active in
+    nvidia-smi CSV rows of ClockSampler.FIELDS (noheader, nounits)."""
+    rows = []
+    for line in text.splitlines():
+        parts = [p.strip() for p in line.split(",")]
+        if len(parts) >= 9:
+            rows.append(parts)
+    if not rows:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+    sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+    smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k].lower().startswith("active")})
+    return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+            "reasons": reasons, "samples": len(rows)}
 
 
 def measure_fp64_peak(device: int) -> float:

@@ -35,3 +35,22 @@ def test_step_flops_formula():
     assert abs(r["frac_executed"] - r["executed_tflops"] / 35.4) < 1e-12
     two = b.step_roofline(24000, 946822, 473411, 8651195, 1 / 0.02125, 35.4, 2)
     assert abs(two["executed_tflops"] - 2 * r["executed_tflops"]) < 1e-9
+
+
+def test_clock_summary_reads_nvidia_smi_rows():
+    """The clocks record of the bench line: median SM clock under sampling, the
+    maximum, and every throttle reason that was Active in any sample (the
+    rejection rule looks for hw_slowdown and the thermal reasons)."""
+    b = _bench()
+    text = "\n".join([
+        "0, 1965, 1965, 650.1, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active",
+        "0, 1875, 1965, 998.7, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+        "0, 1830, 1965, 1003.2, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+        "garbage line",
+    ])
+    c = b.summarize_clocks(text)
+    assert c["sm_mhz"] == 1875.0 and c["sm_max_mhz"] == 1965.0 and c["samples"] == 3
+    assert c["reasons"] == ["sw_power_cap"]
+    hot = b.summarize_clocks("0, 1500, 1965, 900.0, 0x48, Active, Not Active, Active, Not Active")
+    assert hot["reasons"] == ["hw_slowdown", "sw_thermal_slowdown"]
+    assert b.summarize_clocks("")["reasons"] == ["no samples"]
