@@ -401,7 +401,7 @@ def run_turbo(args) -> None:
 
     pos, z, off, q, mult = turbo_batch(TURBO_CLUSTERS, seed=7)
     sizes = np.diff(off)
-    mine = np.argsort(-sizes, kind="stable")[rank::world]
+    mine = deal_clusters(sizes, rank, world)
     x = np.concatenate([pos[off[k]:off[k + 1]] for k in mine])
     zz = np.ascontiguousarray(np.concatenate([z[off[k]:off[k + 1]] for k in mine]), dtype=np.int32)
     my_off = np.concatenate([[0], np.cumsum(sizes[mine])]).astype(np.int64)
@@ -478,6 +478,13 @@ def run_turbo(args) -> None:
     model.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def deal_clusters(sizes, rank: int, world: int) -> np.ndarray:
+    """The clusters rank `rank` of `world` evaluates: sorted by size, largest
+    first (stable), then dealt round robin, so every cluster goes to exactly
+    one rank and the ranks' atom counts differ by at most the largest cluster."""
+    return np.argsort(-np.asarray(sizes), kind="stable")[rank::world]
 
 
 def count_lr_pairs(pos, boxlo, cell, cutoff: float) -> int:

@@ -54,3 +54,18 @@ def test_clock_summary_reads_nvidia_smi_rows():
     hot = b.summarize_clocks("0, 1500, 1965, 900.0, 0x48, Active, Not Active, Active, Not Active")
     assert hot["reasons"] == ["hw_slowdown", "sw_thermal_slowdown"]
     assert b.summarize_clocks("")["reasons"] == ["no samples"]
+
+
+def test_turbo_clusters_dealt_once_and_balanced():
+    """Config 5 under N ranks: every cluster on exactly one rank, atom counts
+    within one largest cluster of each other."""
+    from so3lr_b200.systems import turbo_batch
+    b = _bench()
+    _, _, off, _, _ = turbo_batch(512, seed=7)
+    sizes = np.diff(off)
+    for world in (1, 2, 4, 8):
+        parts = [b.deal_clusters(sizes, r, world) for r in range(world)]
+        allk = np.sort(np.concatenate(parts))
+        assert np.array_equal(allk, np.arange(len(sizes)))
+        atoms = [int(sizes[p].sum()) for p in parts]
+        assert max(atoms) - min(atoms) <= sizes.max(), (world, atoms)
