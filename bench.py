@@ -77,16 +77,30 @@ class ClockSampler:
         self.gpu = gpu
         self.proc = None
         self.path = None
+        self.skip = 0
 
     def start(self):
+        """Start sampling and return once nvidia-smi has written its first row
+        (at most 3 s), so that the rows kept by stop() (those after it) all
+        fall inside the region timed between start() and stop()."""
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
+        self.skip = 0
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 3.0 and self.proc.poll() is None:
+            with open(self.path) as fh:
+                lines = fh.read().splitlines()
+            if lines:
+                self.skip = len(lines)
+                break
+            time.sleep(0.02)
 
     def stop(self) -> dict:
         if self.proc is None:
@@ -96,7 +110,8 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        text = open(self.path).read()
+        with open(self.path) as fh:
+            text = "\n".join(fh.read().splitlines()[self.skip:])
         os.unlink(self.path)
         return summarize_clocks(text)
 
@@ -258,9 +273,9 @@ def run_ours(args) -> None:
     for k in (0, 1):
         model.profile_read(k)
     launches0 = model.launch_count()
-    barrier()
     clocks = ClockSampler(local)
-    clocks.start()
+    clocks.start()  # before the barrier: its wait for nvidia-smi must not skew the ranks' start
+    barrier()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_start.record(ext)
     model.md_run(args.steps, DT_PS)
@@ -435,9 +450,9 @@ def run_turbo(args) -> None:
     for k in (0, 1):
         model.profile_read(k)
     launches0 = model.launch_count()
-    barrier()
     clocks = ClockSampler(local)
-    clocks.start()
+    clocks.start()  # before the barrier: its wait for nvidia-smi must not skew the ranks' start
+    barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         f = step(f)
@@ -519,7 +534,7 @@ def step_roofline(n, sr_edges, sr_pairs, lr_pairs, steps_per_s, peak, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, choices=[1, 2, 3, 5], default=3,

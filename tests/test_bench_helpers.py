@@ -69,3 +69,25 @@ def test_turbo_clusters_dealt_once_and_balanced():
         assert np.array_equal(allk, np.arange(len(sizes)))
         atoms = [int(sizes[p].sum()) for p in parts]
         assert max(atoms) - min(atoms) <= sizes.max(), (world, atoms)
+
+
+def test_clock_sampler_keeps_only_rows_after_start(tmp_path, monkeypatch):
+    """ClockSampler.start returns after nvidia-smi's first row; stop() keeps
+    the rows written after that, i.e. those of the timed region (here a
+    stand-in nvidia-smi on PATH writes one row every 50 ms, the first with a
+    clock of 100 MHz)."""
+    fake = tmp_path / "nvidia-smi"
+    fake.write_text("#!/bin/sh\n"
+                    "echo '0, 100, 1965, 100.0, 0x0, Not Active, Not Active, Not Active, Not Active'\n"
+                    "while true; do sleep 0.05; "
+                    "echo '0, 1900, 1965, 900.0, 0x4, Not Active, Not Active, Not Active, Active'; done\n")
+    fake.chmod(0o755)
+    monkeypatch.setenv("PATH", f"{tmp_path}:{__import__('os').environ['PATH']}")
+    import time
+    b = _bench()
+    s = b.ClockSampler(0)
+    s.start()
+    assert s.skip >= 1
+    time.sleep(0.5)
+    c = s.stop()
+    assert c["samples"] >= 3 and c["sm_mhz"] == 1900.0 and c["reasons"] == ["sw_power_cap"], c
