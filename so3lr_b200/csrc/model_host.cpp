@@ -4,6 +4,7 @@
 #include <algorithm>
 #include <cctype>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <iomanip>
@@ -106,6 +107,30 @@ class JsonParser {
  private:
   const std::string &s_;
   std::size_t i_ = 0;
+  int depth_ = 0;  // nesting of objects and arrays, bounded so a hostile file cannot exhaust the stack
+  static constexpr int kMaxDepth = 64;
+  bool digit(std::size_t k) const { return k < s_.size() && s_[k] >= '0' && s_[k] <= '9'; }
+  // end of the JSON number starting at j: -?(0|[1-9][0-9]*)(.[0-9]+)?([eE][+-]?[0-9]+)?
+  std::size_t number_end(std::size_t j) const {
+    if (j < s_.size() && s_[j] == '-') ++j;
+    if (!digit(j)) fail("malformed manifest JSON value");
+    if (s_[j] == '0') {
+      ++j;
+    } else {
+      while (digit(j)) ++j;
+    }
+    if (j < s_.size() && s_[j] == '.') {
+      if (!digit(++j)) fail("malformed manifest JSON number");
+      while (digit(j)) ++j;
+    }
+    if (j < s_.size() && (s_[j] == 'e' || s_[j] == 'E')) {
+      ++j;
+      if (j < s_.size() && (s_[j] == '+' || s_[j] == '-')) ++j;
+      if (!digit(j)) fail("malformed manifest JSON number");
+      while (digit(j)) ++j;
+    }
+    return j;
+  }
   void ws() {
     while (i_ < s_.size() && std::isspace(static_cast<unsigned char>(s_[i_]))) ++i_;
   }
@@ -142,8 +167,15 @@ class JsonParser {
         case 't': out.push_back('\t'); break;
         case 'u': {
           if (i_ + 4 > s_.size()) fail("bad JSON unicode escape");
-          unsigned code = std::stoul(s_.substr(i_, 4), nullptr, 16);
-          i_ += 4;
+          unsigned code = 0;
+          for (int k = 0; k < 4; ++k) {
+            const char h = s_[i_++];
+            const int v = h >= '0' && h <= '9' ? h - '0'
+                          : h >= 'a' && h <= 'f' ? h - 'a' + 10
+                          : h >= 'A' && h <= 'F' ? h - 'A' + 10 : -1;
+            if (v < 0) fail("bad JSON unicode escape");
+            code = code * 16 + unsigned(v);
+          }
           if (code < 0x80) {
             out.push_back(char(code));
           } else if (code < 0x800) {
@@ -164,6 +196,7 @@ class JsonParser {
   Json value() {
     Json v;
     const char c = peek();
+    if ((c == '{' || c == '[') && ++depth_ > kMaxDepth) fail("manifest JSON is nested too deeply");
     if (c == '{') {
       ++i_;
       Json::Object obj;
@@ -180,6 +213,7 @@ class JsonParser {
         }
       }
       v.v_ = std::move(obj);
+      --depth_;
     } else if (c == '[') {
       ++i_;
       Json::Array arr;
@@ -194,6 +228,7 @@ class JsonParser {
         }
       }
       v.v_ = std::move(arr);
+      --depth_;
     } else if (c == '"') {
       v.v_ = string();
     } else if (s_.compare(i_, 4, "true") == 0) {
@@ -203,11 +238,10 @@ class JsonParser {
     } else if (s_.compare(i_, 4, "null") == 0) {
       i_ += 4; v.v_ = nullptr;
     } else {
-      const char *begin = s_.c_str() + i_;
-      char *end = nullptr;
-      const double d = std::strtod(begin, &end);
-      if (end == begin) fail("malformed manifest JSON value");
-      i_ += std::size_t(end - begin);
+      const std::size_t end = number_end(i_);
+      const double d = std::strtod(s_.substr(i_, end - i_).c_str(), nullptr);
+      if (!std::isfinite(d)) fail("manifest JSON number out of range");
+      i_ = end;
       v.v_ = d;
     }
     return v;

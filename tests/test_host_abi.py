@@ -100,6 +100,44 @@ def test_integrity_checks(tmp_path, corrupt, message):
         inspect_model(path)
 
 
+def _with_manifest_text(tmp_path: pathlib.Path, text: str) -> pathlib.Path:
+    """The shipped model with its manifest replaced by `text` (header sizes and
+    manifest SHA-256 recomputed, so only the parser can object)."""
+    data = bytearray(MODEL.read_bytes())
+    msize = struct.unpack_from("<Q", data, 16)[0]
+    payload = bytes(data[128 + msize:])
+    mbytes = text.encode()
+    out = bytearray(data[:128]) + mbytes + payload
+    struct.pack_into("<QQ", out, 16, len(mbytes), len(payload))
+    out[32:64] = hashlib.sha256(mbytes).digest()
+    path = tmp_path / "manifest.so3lr"
+    path.write_bytes(bytes(out))
+    return path
+
+
+@pytest.mark.parametrize("text, message", [
+    ("[" * 100000 + "]" * 100000, "nested too deeply"),
+    ('{"format": NaN}', "malformed manifest JSON value"),
+    ('{"format": Infinity}', "malformed manifest JSON value"),
+    ('{"format": 0x10}', "expected"),
+    ('{"format": 01}', "expected"),
+    ('{"format": 1.}', "malformed manifest JSON number"),
+    ('{"format": 2e}', "malformed manifest JSON number"),
+    ('{"format": 1e999}', "out of range"),
+    ('{"format": "\\uZZZZ"}', "unicode escape"),
+    ('{"format": "abc', "unterminated"),
+    ('{"format": 1} x', "trailing"),
+    ('{"format": 1, "format": 2}', "duplicate JSON key"),
+])
+def test_manifest_parser_refuses_malformed_json(tmp_path, text, message):
+    """The manifest is untrusted text: anything outside JSON's grammar, numbers
+    that overflow, and nesting deep enough to exhaust a recursive parser's stack
+    are refused with a message."""
+    from so3lr_b200 import So3lrError, inspect_model
+    with pytest.raises(So3lrError, match=message):
+        inspect_model(_with_manifest_text(tmp_path, text))
+
+
 def test_random_corruptions_are_refused(tmp_path):
     """A model file is untrusted input: any single flipped byte (header,
     manifest or any tensor) and any truncation is refused with an error, never
