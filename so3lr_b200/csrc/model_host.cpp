@@ -346,7 +346,11 @@ Model Model::load_bytes(std::vector<std::uint8_t> bytes, const std::string &orig
     t.nbytes = std::size_t(item.at("nbytes").uint());
     for (const Json &e : item.at("shape").array()) t.shape.push_back(std::size_t(e.uint()));
     if (!names.insert(t.name).second || !keys.insert(t.state_key).second) fail("duplicate tensor name/state key");
-    if (t.offset % 64 != 0 || t.nbytes != t.count() * dtype_width(t.dtype)) fail("tensor alignment/size mismatch: " + t.state_key);
+    std::size_t elems = 1, bytes_needed = 0;  // shape product without wrap-around
+    for (auto e : t.shape)
+      if (__builtin_mul_overflow(elems, e, &elems)) fail("tensor shape overflows: " + t.state_key);
+    if (__builtin_mul_overflow(elems, dtype_width(t.dtype), &bytes_needed)) fail("tensor shape overflows: " + t.state_key);
+    if (t.offset % 64 != 0 || t.nbytes != bytes_needed) fail("tensor alignment/size mismatch: " + t.state_key);
     if (t.offset < prev_end || t.offset > psize || t.nbytes > psize - t.offset) fail("tensor overlap/range error: " + t.state_key);
     for (std::size_t p = prev_end; p < t.offset; ++p)
       if (pdata[p]) fail("nonzero payload padding");

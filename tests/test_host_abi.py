@@ -78,6 +78,8 @@ def _rewrite(tmp_path: pathlib.Path, mutate_manifest=None, mutate_bytes=None) ->
     (lambda m: m["architecture"].__setitem__("message_normalization", "softmax"), "message_normalization"),
     (lambda m: m.__setitem__("schema", "so3lr-native-model-v1"), "schema"),
     (lambda m: m["architecture"].__setitem__("interaction_blocks", 9), "interaction_blocks"),
+    # a shape whose element count wraps around 2^64 to the stored byte count
+    (lambda m: m["tensors"][0].__setitem__("shape", [2 ** 52, 2 ** 12] + m["tensors"][0]["shape"]), "overflows"),
 ])
 def test_capability_rejection(tmp_path, change, message):
     from so3lr_b200 import So3lrError, inspect_model
