@@ -1222,6 +1222,8 @@ void Evaluator::md_steps(int nsteps, double dt) {
   constexpr double ftm2v = 1.0 / 1.0364269e-4;
   const std::size_t r0 = std::size_t(row0_);
   if (!md_ready_) throw Error("SO3LR MD: call so3lr_md_init first");
+  if (nsteps < 0) throw Error("SO3LR MD: the step count must not be negative");
+  if (!std::isfinite(dt)) throw Error("SO3LR MD: the timestep must be finite");
   for (int step = 0; step < nsteps; ++step) {
     if (nvt_) nhc_half(dt);
     launch_verlet_first(n_own_, x_.get() + 3 * r0, v_.get() + 3 * r0, force_.get() + 3 * r0, inv_mass_.get() + r0, dt,
