@@ -150,7 +150,7 @@ void PairSO3LRB200::init_style() {
     if (rc != 0) error->all(FLERR, std::string("SO3LR: cannot create the NCCL id on rank 0: ") + err);
     MPI_Bcast(uid, 128, MPI_BYTE, 0, world);
     if (so3lr_comm_init(handle_, comm->nprocs, comm->me, uid, err, sizeof(err)) != 0)
-      error->all(FLERR, std::string("SO3LR: cannot join the GPUs of the other ranks: ") + err);
+      fail_collective(std::string("SO3LR: cannot join the GPUs of the other ranks: ") + err);
     comm_ready_ = true;
   }
 }
@@ -185,6 +185,15 @@ void PairSO3LRB200::write_debug_dump(const char *path, const so3lr_result &res, 
   array("hirshfeld_ratios", [&](int i) { return res.ratios[row(i)]; }, true);
   std::fprintf(out, "}\n");
   std::fclose(out);
+}
+
+// A failure of a library call that all ranks make together (joining the GPUs,
+// an evaluation). With several ranks the others may be waiting inside the
+// library's collective communication, where error->all's barrier would never
+// return, so the failing rank stops the whole job itself (error->one).
+void PairSO3LRB200::fail_collective(const std::string &msg) {
+  if (comm->nprocs > 1) error->one(FLERR, msg);
+  error->all(FLERR, msg);
 }
 
 void PairSO3LRB200::compute(int eflag, int vflag) {
@@ -229,9 +238,11 @@ void PairSO3LRB200::compute(int eflag, int vflag) {
   // tags 1..n: gathered slot k holds atom tag all_tag_[k]
   x_.resize(3 * static_cast<std::size_t>(n));
   z_.resize(n);
+  seen_.assign(n, 0);
   for (int k = 0; k < n; ++k) {
     const int tg = all_tag_[k];
-    if (tg < 1 || tg > n) error->all(FLERR, "Pair style so3lr/b200 needs atom tags 1..natoms");
+    if (tg < 1 || tg > n || seen_[tg - 1]) error->all(FLERR, "Pair style so3lr/b200 needs unique atom tags 1..natoms");
+    seen_[tg - 1] = 1;
     for (int d = 0; d < 3; ++d) x_[3 * static_cast<std::size_t>(tg - 1) + d] = all_x_[3 * static_cast<std::size_t>(k) + d];
     z_[tg - 1] = all_z_[k];
   }
@@ -269,7 +280,7 @@ void PairSO3LRB200::compute(int eflag, int vflag) {
   }
   char err[2048] = {0};
   if (so3lr_compute(handle_, &frame, &res, err, sizeof(err)) != 0)
-    error->all(FLERR, std::string("SO3LR evaluation failed: ") + err);
+    fail_collective(std::string("SO3LR evaluation failed: ") + err);
   if (dump) write_debug_dump(dump_path, res, n);
   // each rank keeps its own atoms' forces and per-atom terms; the global energy
   // and virial (exact sums, identical on every rank) are reported by rank 0 only,
@@ -288,7 +299,7 @@ void PairSO3LRB200::compute(int eflag, int vflag) {
     // term to each of its atoms, rows summing to the global virial
     va_.resize(6 * static_cast<std::size_t>(n));
     if (so3lr_virial_atom(handle_, va_.data(), err, sizeof(err)) != 0)
-      error->all(FLERR, std::string("SO3LR per-atom virial failed: ") + err);
+      fail_collective(std::string("SO3LR per-atom virial failed: ") + err);
     for (int i = 0; i < nlocal; ++i) {
       const std::size_t k = static_cast<std::size_t>(loc_tag_[i] - 1);
       for (int c = 0; c < 6; ++c) vatom[i][c] += va_[6 * k + c];

@@ -58,6 +58,7 @@ class PairSO3LRB200 : public Pair {
   std::vector<int> z_;
   std::vector<double> x_, f_, eatom_, va_, loc_x_, all_x_, terms_;
   std::vector<int> loc_tag_, loc_z_, all_tag_, all_z_, counts_, displs_, counts3_, displs3_;
+  std::vector<char> seen_;
   bool comm_ready_ = false;
   so3lr_handle *handle_ = nullptr;
   bool reported_ = false;
@@ -65,6 +66,7 @@ class PairSO3LRB200 : public Pair {
   void allocate();
   void release();
   void write_debug_dump(const char *path, const so3lr_result &res, int n);
+  [[noreturn]] void fail_collective(const std::string &msg);
   void setup_profile();
   void report_profile();
   int profile_every_ = -1;  // -1: not read yet, 0: off

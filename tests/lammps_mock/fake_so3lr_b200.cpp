@@ -18,6 +18,7 @@
 
 struct so3lr_handle {
   std::vector<double> va;
+  int rank = 0;
 };
 
 static int fake_fail(const char *msg, char *err, size_t errlen) {
@@ -108,6 +109,8 @@ int so3lr_profile_read(so3lr_handle *, int kernel, double *ms, long long *launch
 //   e_elec = e_disp = e_lr / 2; energy = sum of eatom; virial 0
 int so3lr_compute(so3lr_handle *h, const so3lr_frame *in, so3lr_result *out, char *err, size_t errlen) {
   if (!h || !in || !out || !out->f) return fake_fail("so3lr_compute: NULL argument", err, errlen);
+  const char *fail_rank = std::getenv("FAKE_SO3LR_FAIL_RANK");  // a failure injected on one rank
+  if (fail_rank && std::atoi(fail_rank) == h->rank) return fake_fail("injected failure", err, errlen);
   const long long n = in->natoms;
   double e = 0.0;
   h->va.assign(6 * static_cast<std::size_t>(n), 0.0);
@@ -129,9 +132,16 @@ int so3lr_compute(so3lr_handle *h, const so3lr_frame *in, so3lr_result *out, cha
   if (g_profile_on) ++g_profile_calls;
   return 0;
 }
-int so3lr_nccl_unique_id(char *, char *err, size_t errlen) { return fake_fail("not in the CPU stand-in", err, errlen); }
-int so3lr_comm_init(so3lr_handle *, int, int, const char *, char *err, size_t errlen) {
-  return fake_fail("not in the CPU stand-in", err, errlen);
+// several ranks: no communication in the stand-in, every rank evaluates the
+// whole system it is given (as every rank of the real library returns it)
+int so3lr_nccl_unique_id(char *out, char *, size_t) {
+  std::memset(out, 0, 128);
+  return 0;
+}
+int so3lr_comm_init(so3lr_handle *h, int nranks, int rank, const char *, char *err, size_t errlen) {
+  if (!h || rank < 0 || rank >= nranks) return fake_fail("so3lr_comm_init: bad rank", err, errlen);
+  h->rank = rank;
+  return 0;
 }
 
 }  // extern "C"

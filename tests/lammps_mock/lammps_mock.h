@@ -25,7 +25,8 @@ class Error {
   [[noreturn]] void all(const char *, int, const std::string &msg) { throw std::runtime_error(msg); }
   [[noreturn]] void universe_all(const char *, int, const std::string &msg) { throw std::runtime_error(msg); }
   [[noreturn]] void universe_one(const char *, int, const std::string &msg) { throw std::runtime_error(msg); }
-  [[noreturn]] void one(const char *, int, const std::string &msg) { throw std::runtime_error(msg); }
+  // LAMMPS's one() aborts every rank from the calling one; the mock marks its message
+  [[noreturn]] void one(const char *, int, const std::string &msg) { throw std::runtime_error("ERROR on proc: " + msg); }
   // LAMMPS prints "WARNING: msg" to the screen and log file; the mock keeps it
   void warning(const char *, int, const std::string &msg) { warnings += "WARNING: " + msg + "\n"; }
   std::string warnings;

@@ -4,6 +4,8 @@
 //                                       (types 1 = O, 2 = H); prints JSON with energy, virial, forces
 //   test_pair_shim run-reversed-tags MODEL INPUT
 //                                       the same with atom i tagged n - i
+//   test_pair_shim run-duplicate-tag MODEL INPUT
+//                                       the same with atoms 0 and 1 sharing a tag (refused)
 //   test_pair_shim repeat MODEL INPUT [CHARGE MULT]
 //                                       four computes; prints the style's log and warnings
 //   test_pair_shim turbo-parse MODEL    so3lr/b200/turbo parsing and refusals on one rank, and a
@@ -145,7 +147,7 @@ static int repeat(const char *model, const char *input, const char *charge = nul
   return 0;
 }
 
-static int run(const char *model, const char *input, bool reverse_tags = false) {
+static int run(const char *model, const char *input, bool reverse_tags = false, bool duplicate_tag = false) {
   std::ifstream in(input);
   double L;
   int n;
@@ -155,6 +157,7 @@ static int run(const char *model, const char *input, bool reverse_tags = false) 
   lmp.atom.resize(n);
   if (reverse_tags)
     for (int i = 0; i < n; ++i) lmp.atom.tag[i] = n - i;
+  if (duplicate_tag && n > 1) lmp.atom.tag[1] = lmp.atom.tag[0];
   for (int i = 0; i < n; ++i) in >> lmp.atom.type[i] >> lmp.atom.x[i][0] >> lmp.atom.x[i][1] >> lmp.atom.x[i][2];
   for (int d = 0; d < 3; ++d) lmp.domain.prd[d] = L;
   PairSO3LRB200 pair(&lmp);
@@ -523,6 +526,7 @@ int main(int argc, char **argv) {
   if (argc >= 3 && std::string(argv[1]) == "parse") return parse_checks(argv[2]);
   if (argc >= 4 && std::string(argv[1]) == "run") return run(argv[2], argv[3]);
   if (argc >= 4 && std::string(argv[1]) == "run-reversed-tags") return run(argv[2], argv[3], true);
+  if (argc >= 4 && std::string(argv[1]) == "run-duplicate-tag") return run(argv[2], argv[3], false, true);
   if (argc >= 6 && std::string(argv[1]) == "repeat") return repeat(argv[2], argv[3], argv[4], argv[5]);
   if (argc >= 4 && std::string(argv[1]) == "repeat") return repeat(argv[2], argv[3]);
   if (argc >= 5 && std::string(argv[1]) == "multirank") return multirank(argv[2], argv[3], std::atoi(argv[4]));

@@ -144,6 +144,57 @@ def test_charge_log_line_and_periodic_charge_warning(tmp_path):
     assert "SO3LR: total charge 0, spin multiplicity 1" in res.stdout and "WARNING" not in res.stdout
 
 
+def _water_input(tmp_path, nmol=8, seed=5):
+    from so3lr_b200.systems import water_box
+    w = water_box(nmol, seed=seed)
+    inp = tmp_path / "box.txt"
+    lines = [f"{float(w.cell[0])!r} {len(w.z)}"]
+    for zi, p in zip(w.z, w.pos):
+        lines.append(f"{1 if zi == 8 else 2} {float(p[0])!r} {float(p[1])!r} {float(p[2])!r}")
+    inp.write_text("\n".join(lines) + "\n")
+    return w, inp
+
+
+def test_multirank_routing_with_the_cpu_stand_in(tmp_path, monkeypatch):
+    """so3lr/b200 on three ranks (threads) with atoms dealt out of order: every
+    rank gets back exactly its own atoms' forces and per-atom energies (the
+    stand-in returns f = -x and eatom = z / 2 by tag), and only rank 0 reports
+    the global energy."""
+    exe = _build(tmp_path, fake=True)
+    monkeypatch.delenv("FAKE_SO3LR_FAIL_RANK", raising=False)
+    w, inp = _water_input(tmp_path)
+    res = subprocess.run([str(exe), "multirank", "fake", str(inp), "3"], capture_output=True, text=True, timeout=120)
+    out = _json_lines(res, 3)
+    seen = []
+    for o in out:
+        rows = np.array(o["tags"]) - 1
+        seen += list(rows)
+        assert np.array_equal(np.array(o["forces"]), -w.pos[rows])
+        assert np.array_equal(np.array(o["eatom"]), 0.5 * w.z[rows])
+        assert o["energy"] == (0.5 * w.z.sum() if o["rank"] == 0 else 0.0)
+    assert sorted(seen) == list(range(len(w.z)))
+
+
+def test_evaluation_failure_on_one_rank_aborts_from_that_rank(tmp_path, monkeypatch):
+    """A library failure on one of several ranks is reported with error->one
+    from the failing rank (which aborts the job), not error->all, whose barrier
+    would wait for ranks that may be blocked in the library's collectives."""
+    exe = _build(tmp_path, fake=True)
+    monkeypatch.setenv("FAKE_SO3LR_FAIL_RANK", "1")
+    _, inp = _water_input(tmp_path)
+    res = subprocess.run([str(exe), "multirank", "fake", str(inp), "2"], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 1, res.stdout + res.stderr
+    assert "ERROR rank 1: ERROR on proc: SO3LR evaluation failed: injected failure" in res.stdout, res.stdout
+
+
+def test_duplicate_atom_tags_are_refused(tmp_path):
+    exe = _build(tmp_path, fake=True)
+    _, inp = _water_input(tmp_path, nmol=2)
+    res = subprocess.run([str(exe), "run-duplicate-tag", "fake", str(inp)], capture_output=True, text=True,
+                         timeout=120)
+    assert res.returncode != 0 and "unique atom tags" in res.stderr, res.stdout + res.stderr
+
+
 def test_model_failure_on_one_rank_stops_every_rank(tmp_path):
     """so3lr/b200 on two ranks (threads) where only one cannot load the model:
     that rank reports the loader's message, the other learns of it in the same
