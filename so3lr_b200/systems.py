@@ -58,6 +58,31 @@ class WaterSystem:
     multiplicity: float = 1.0
 
 
+def min_oo_distance(centers: np.ndarray, L: float, n_molecules: int) -> float:
+    """Smallest minimum-image distance between the molecule centres (the O
+    atoms): a dense comparison for small boxes, a periodic k-d tree for large
+    ones."""
+    if n_molecules < 2:
+        return math.inf
+    if n_molecules <= 4000:
+        d = centers[:, None, :] - centers[None, :, :]
+        d -= L * np.round(d / L)
+        return float((np.sqrt((d * d).sum(-1)) + np.eye(n_molecules) * 1e9).min())
+    from scipy.spatial import cKDTree
+    x = np.mod(centers, L)
+    dist, _ = cKDTree(x, boxsize=L).query(x, k=2)
+    return float(dist[:, 1].min())
+
+
+def close_molecules(centers: np.ndarray, L: float, min_oo: float) -> np.ndarray:
+    """One molecule (the first) of every pair closer than min_oo under the
+    minimum image, from a periodic k-d tree."""
+    from scipy.spatial import cKDTree
+    x = np.mod(centers, L)
+    pairs = cKDTree(x, boxsize=L).query_pairs(min_oo, output_type="ndarray")
+    return np.unique(pairs[:, 0]) if len(pairs) else np.zeros(0, dtype=np.int64)
+
+
 def water_box(n_molecules: int, seed: int, density: float = 0.997, jitter: float = 0.1,
               min_oo: float = 2.5) -> WaterSystem:
     """Periodic cubic water box."""
@@ -70,17 +95,25 @@ def water_box(n_molecules: int, seed: int, density: float = 0.997, jitter: float
     centers = (sites[np.sort(order)] + 0.5) * spacing
     base = molecule_frame()
     # jitter the lattice, keeping O-O >= min_oo under the minimum image
-    for attempt in range(50):
-        trial = centers + rng.uniform(-jitter, jitter, centers.shape) * spacing
-        d = trial[:, None, :] - trial[None, :, :] if n_molecules <= 4000 else None
-        if d is None:
-            break
-        d -= L * np.round(d / L)
-        r = np.sqrt((d * d).sum(-1)) + np.eye(n_molecules) * 1e9
-        if r.min() >= min_oo:
-            break
+    if n_molecules <= 4000:
+        # small boxes: redraw the whole jitter (fixes the boxes the tests use)
+        for attempt in range(50):
+            trial = centers + rng.uniform(-jitter, jitter, centers.shape) * spacing
+            if min_oo_distance(trial, L, n_molecules) >= min_oo:
+                break
+        else:
+            trial = centers
     else:
-        trial = centers
+        # large boxes: some pair is almost always too close, so only the
+        # molecules of close pairs get a new jitter, until none is left
+        trial = centers + rng.uniform(-jitter, jitter, centers.shape) * spacing
+        for attempt in range(200):
+            close = close_molecules(trial, L, min_oo)
+            if len(close) == 0:
+                break
+            trial[close] = centers[close] + rng.uniform(-jitter, jitter, (len(close), 3)) * spacing
+        else:
+            trial = centers
     centers = trial
     pos = np.empty((3 * n_molecules, 3))
     for m in range(n_molecules):
