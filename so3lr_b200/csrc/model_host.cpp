@@ -681,8 +681,14 @@ std::string charge_multiplicity_problem(const std::array<std::int64_t, 119> &cou
     return "the total charge must be an integer";
   if (!std::isfinite(multiplicity) || std::round(multiplicity) != multiplicity || multiplicity < 1.0)
     return "the spin multiplicity must be an integer >= 1";
+  // bounds that keep the integer arithmetic below exact (no overflow)
+  if (std::fabs(total_charge) > 1e15) return "the total charge is out of range";
+  if (multiplicity > 1e15) return "the spin multiplicity is out of range";
   std::int64_t protons = 0;
-  for (int z = 1; z <= 118; ++z) protons += counts[z] * z;
+  for (int z = 1; z <= 118; ++z) {
+    if (counts[z] < 0 || counts[z] > (std::int64_t(1) << 40)) return "element counts must be in 0..2^40";
+    protons += counts[z] * z;
+  }
   const std::int64_t electrons = protons - std::int64_t(total_charge);
   const std::int64_t unpaired = std::int64_t(multiplicity) - 1;
   if (electrons < 0) return "the total charge leaves a negative number of electrons";

@@ -207,6 +207,10 @@ def test_element_tokens():
     ([8, 1, 1], 0.5, 1, False),    # non-integer charge
     ([8, 1, 1], 0, 0, False),      # multiplicity below 1
     ([8, 1, 1], 0, 1.5, False),
+    ([8, 1, 1], float("nan"), 1, False),
+    ([8, 1, 1], 0, float("inf"), False),
+    ([8, 1, 1], 1e300, 1, False),     # out of range, not an overflowed conversion
+    ([8, 1, 1], 0, 1e300, False),
 ])
 def test_charge_multiplicity_validation(z, q, m, ok):
     from so3lr_b200 import validate_charge_spin
