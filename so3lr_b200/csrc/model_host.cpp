@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <filesystem>
 #include <fstream>
 #include <iomanip>
 #include <set>
@@ -293,9 +294,19 @@ std::uint64_t Json::uint() const {
 
 // ---- model file -------------------------------------------------------------
 Model Model::load(const std::string &path) {
+  // a regular file of bounded size (a device such as /dev/zero never ends)
+  std::error_code ec;
+  const auto st = std::filesystem::status(path, ec);
+  if (ec || !std::filesystem::exists(st)) fail("cannot open " + path);
+  if (!std::filesystem::is_regular_file(st)) fail("cannot open " + path + ": not a regular file");
+  const std::uintmax_t size = std::filesystem::file_size(path, ec);
+  if (ec) fail("cannot open " + path);
+  if (size > (std::uintmax_t(1) << 32)) fail(path + " is larger than 4 GiB");
   std::ifstream in(path, std::ios::binary);
   if (!in) fail("cannot open " + path);
-  std::vector<std::uint8_t> bytes((std::istreambuf_iterator<char>(in)), std::istreambuf_iterator<char>());
+  std::vector<std::uint8_t> bytes(static_cast<std::size_t>(size));
+  in.read(reinterpret_cast<char *>(bytes.data()), static_cast<std::streamsize>(size));
+  if (static_cast<std::uintmax_t>(in.gcount()) != size) fail("cannot read " + path);
   return load_bytes(std::move(bytes), path);
 }
 

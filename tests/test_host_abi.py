@@ -172,6 +172,10 @@ def test_truncated_and_missing_model(tmp_path):
         inspect_model(short)
     with pytest.raises(So3lrError, match="cannot open"):
         inspect_model(tmp_path / "nope.so3lr")
+    with pytest.raises(So3lrError, match="not a regular file"):
+        inspect_model(tmp_path)  # a directory
+    with pytest.raises(So3lrError, match="not a regular file"):
+        inspect_model("/dev/zero")  # a device that never ends is not read
 
 
 def test_python_and_native_loaders_agree():
