@@ -91,3 +91,29 @@ def test_clock_sampler_keeps_only_rows_after_start(tmp_path, monkeypatch):
     time.sleep(0.5)
     c = s.stop()
     assert c["samples"] >= 3 and c["sm_mhz"] == 1900.0 and c["reasons"] == ["sw_power_cap"], c
+
+
+def test_reference_arm_line_keeps_the_contract():
+    """`bench.py --impl reference` (the CPU restatement timed on the host) prints
+    one JSON line with the keys the driver reads, on the same metric and
+    workload as the GPU arm."""
+    import json
+    import subprocess
+    import sys
+    res = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "0"], capture_output=True, text=True, timeout=600, cwd=str(ROOT))
+    assert res.returncode == 0, res.stderr
+    lines = [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, res.stdout
+    d = json.loads(lines[0])
+    for k in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+              "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert k in d, k
+    assert d["impl"] == "reference" and d["metric"] == "atom-steps/s" and d["unit"] == "atom-steps/s"
+    assert d["steps"] == 1 and d["warmup"] == 3  # at least 3 warm-up steps, whatever is asked
+    assert d["value"] > 0 and d["higher_is_better"] is True and d["dtype"] == "f64"
+    assert d["config"]["workload"].startswith("config3")
+    cb = d["cpu_baseline"]
+    assert cb["value"] == d["value"] and cb["kind"] == "port" and cb["cores"] >= 1 and cb["sample"]
+    assert d["e2e"] == {"value": d["value"], "unit": "atom-steps/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}
