@@ -117,3 +117,15 @@ def test_reference_arm_line_keeps_the_contract():
     assert cb["value"] == d["value"] and cb["kind"] == "port" and cb["cores"] >= 1 and cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": "atom-steps/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_runs_on_rank_zero_only():
+    """Under torchrun the reference arm's rank 0 alone works and prints; the
+    other ranks exit 0 at once."""
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2", LOCAL_RANK="1")
+    res = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1"],
+                         capture_output=True, text=True, timeout=300, cwd=str(ROOT), env=env)
+    assert res.returncode == 0 and not [ln for ln in res.stdout.splitlines() if ln.startswith("{")], res.stdout
