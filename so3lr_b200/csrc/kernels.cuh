@@ -4,22 +4,11 @@
 #include <algorithm>
 #include <cmath>
 
+#include "cell_grid.hpp"
 #include "common.cuh"
 
 namespace so3lr_b200 {
 
-// periodic: cells tile the box and wrap. open_cells: a single open-boundary
-// system of many atoms on a non-wrapping grid over its bounding box; atoms
-// outside the grid go to the nearest boundary cell, which keeps every pair
-// within one cell size in neighbouring cells. Neither: every atom scans its
-// own image's index range (small open systems and turbo packs).
-struct CellGrid {
-  int periodic = 0;
-  int open_cells = 0;
-  double lo[3] = {0, 0, 0};
-  double len[3] = {1, 1, 1};
-  int ncell[3] = {1, 1, 1};
-};
 
 struct NeighborState {
   CellGrid grid;
