@@ -66,3 +66,18 @@ def test_turbo_pack_spec():
         c = pos[off[k]:off[k + 1]]
         radius = (3 * n_o * 30.0 / (4 * math.pi)) ** (1 / 3)
         assert np.linalg.norm(c, axis=1).max() <= radius + 1.5
+
+
+@pytest.mark.parametrize("kind, dq", [("neutral", 0), ("hydroxide", -1), ("hydronium", 1)])
+def test_cluster_kinds(kind, dq):
+    """Every cluster kind keeps whole O-H bonds of 0.9572 A; OH- lacks one H,
+    H3O+ carries one more H on one oxygen, and O-O distances are >= 2.6 A."""
+    from so3lr_b200.systems import water_cluster
+    rng = np.random.default_rng(11)
+    pos, z, q = water_cluster(8, rng, kind)
+    assert q == dq and int((z == 8).sum()) == 8 and int((z == 1).sum()) == 16 + dq
+    o = pos[z == 8]
+    d = np.linalg.norm(o[:, None] - o[None, :], axis=-1) + np.eye(8) * 1e9
+    assert d.min() >= 2.6
+    for h in pos[z == 1]:  # every hydrogen sits on an oxygen at the O-H bond length
+        assert abs(np.linalg.norm(o - h, axis=1).min() - 0.9572) < 1e-9
