@@ -229,7 +229,9 @@ long long so3lr_launch_count(void);
  * held by every GPU that loads the library until exit); the first call on a
  * device resolves its address, so make that first call before any stream
  * capture. Calls share the scratch: calls that overlap on the GPU race and must
- * be serialised by the caller. */
+ * be serialised by the caller. The resolved address is kept for the life of the
+ * process: after a cudaDeviceReset (or any other reset of the device's primary
+ * context) this entry point must not be called again in that process. */
 int so3lr_long_range_noalloc(so3lr_handle *h, long long natoms, const double *x, const double *q,
                              const double *ratios, const int *z, double *e_lr, double *e_elec, double *e_disp,
                              double *dq, double *dh, double *f, double *virial_atom, void *stream, char *err,

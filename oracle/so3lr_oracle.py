@@ -300,6 +300,73 @@ def _tables_for(m, z, charge, mult):
     return charge_spin_table(m.file, counts, float(charge), float(mult) - 1.0)
 
 
+def long_range_pairs(m: OracleModel, zi, charge, ratio, c6r, lr_i, lr_j, lr_vec):
+    """Electrostatic and dispersion energy of every long-range half pair
+    (physical_long_range.cpp:62-380): shifted-force erf Coulomb with the smooth
+    switch, QDO C6/C8/C10 dispersion with C6 mixing. ``zi`` = Z - 1 per atom;
+    ``charge``, ``ratio`` (Hirshfeld) and ``c6r`` (C6 ratios, or None) per atom."""
+    p = m.p
+    a = m.file.arch
+    rl = torch.sqrt((lr_vec * lr_vec).sum(dim=1))
+    cutoff = float(a["long_range_cutoff_angstrom"])
+    sigma = float(a["lr_electrostatic_sigma"])
+    ke = float(a["lr_electrostatic_ke"])
+    e_sw = smooth_switch(rl, float(a["lr_electrostatic_cuton_angstrom"]), cutoff)
+    ratio_c = cutoff / sigma
+    cutoff_erf = math.erf(ratio_c)
+    cutoff_exp = math.exp(-(ratio_c * ratio_c))
+    inv_sqrt_pi = 0.56418958354775628695
+    shift = cutoff_erf / cutoff
+    fshift = (2.0 * cutoff * cutoff_exp * inv_sqrt_pi / sigma - cutoff_erf) / (cutoff * cutoff)
+    potential = torch.erf(rl / sigma) / rl
+    displacement = rl - cutoff
+    shifted = potential - shift - fshift * displacement
+    kernel = e_sw * (potential - shift) + (1.0 - e_sw) * shifted
+    full_scale = 2.0 * float(a["lr_pair_scale"])
+    e_elec = full_scale * ke * charge[lr_i] * charge[lr_j] * kernel
+
+    alpha_ref = p["physical.reference_alphas"]
+    c6_ref = p["physical.reference_c6"]
+    hi, hj = ratio[lr_i], ratio[lr_j]
+    ai0, aj0 = alpha_ref[zi[lr_i]], alpha_ref[zi[lr_j]]
+    ci0, cj0 = c6_ref[zi[lr_i]], c6_ref[zi[lr_j]]
+    ai, aj = ai0 * hi, aj0 * hj
+    if c6r is None:
+        c6i, c6j = ci0 * hi * hi, cj0 * hj * hj
+    else:
+        c6i, c6j = ci0 * c6r[lr_i], cj0 * c6r[lr_j]
+    alpha = 0.5 * (ai + aj)
+    num = 2.0 * c6i * c6j * aj * ai
+    den = ai * ai * c6j + aj * aj * c6i
+    c6 = num / den
+    b0, b1, b2, b3 = -0.00433008, 0.24428889, 0.04125273, -0.00078893
+    fsf = float(a["lr_fine_structure"]) ** (-4.0 / 21.0)
+    a7 = alpha ** (1.0 / 7.0)
+    rvdw = fsf * a7
+    sig = b3 * rvdw * rvdw * rvdw + b2 * rvdw * rvdw + b1 * rvdw + b0
+    gam = 0.5 / (sig * sig)
+    c8 = 5.0 * c6 / gam
+    c10 = 245.0 * c6 / (8.0 * gam * gam)
+    damp = float(a["lr_dispersion_scale"]) * 2.0 * 2.54 * a7
+    dau = rl / float(a["lr_bohr_angstrom"])
+    r2 = dau * dau
+    r4 = r2 * r2
+    r6 = r4 * r2
+    r8 = r4 * r4
+    r10 = r8 * r2
+    p2 = damp * damp
+    p4 = p2 * p2
+    p6 = p4 * p2
+    p8 = p4 * p4
+    p10 = p8 * p2
+    qdo = -c6 / (r6 + p6) - c8 / (r8 + p8) - c10 / (r10 + p10)
+    d_sw = smooth_switch(rl, float(a["lr_dispersion_cuton_angstrom"]), cutoff)
+    e_disp = full_scale * float(a["lr_hartree_ev"]) * qdo * d_sw
+    valid = (alpha > 0.0) & (den > 1.0e-30)
+    e_disp = torch.where(valid, e_disp, torch.zeros_like(e_disp))
+    return e_elec, e_disp
+
+
 def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -> dict:
     """Energy, forces, virial and per-atom terms for one system (or a turbo pack)."""
     p = m.p
@@ -470,63 +537,7 @@ def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -
     e_zbl = torch.zeros(n, dtype=DT).index_add(0, sr_r, e_zbl_edge)
 
     # --- long range (physical_long_range.cpp:62-380) ------------------------------
-    rl = torch.sqrt((lr_vec * lr_vec).sum(dim=1))
-    cutoff = float(a["long_range_cutoff_angstrom"])
-    sigma = float(a["lr_electrostatic_sigma"])
-    ke = float(a["lr_electrostatic_ke"])
-    e_sw = smooth_switch(rl, float(a["lr_electrostatic_cuton_angstrom"]), cutoff)
-    ratio_c = cutoff / sigma
-    cutoff_erf = math.erf(ratio_c)
-    cutoff_exp = math.exp(-(ratio_c * ratio_c))
-    inv_sqrt_pi = 0.56418958354775628695
-    shift = cutoff_erf / cutoff
-    fshift = (2.0 * cutoff * cutoff_exp * inv_sqrt_pi / sigma - cutoff_erf) / (cutoff * cutoff)
-    potential = torch.erf(rl / sigma) / rl
-    displacement = rl - cutoff
-    shifted = potential - shift - fshift * displacement
-    kernel = e_sw * (potential - shift) + (1.0 - e_sw) * shifted
-    full_scale = 2.0 * float(a["lr_pair_scale"])
-    e_elec = full_scale * ke * charge[lr_i] * charge[lr_j] * kernel
-
-    alpha_ref = p["physical.reference_alphas"]
-    c6_ref = p["physical.reference_c6"]
-    hi, hj = ratio[lr_i], ratio[lr_j]
-    ai0, aj0 = alpha_ref[zi[lr_i]], alpha_ref[zi[lr_j]]
-    ci0, cj0 = c6_ref[zi[lr_i]], c6_ref[zi[lr_j]]
-    ai, aj = ai0 * hi, aj0 * hj
-    if c6r is None:
-        c6i, c6j = ci0 * hi * hi, cj0 * hj * hj
-    else:
-        c6i, c6j = ci0 * c6r[lr_i], cj0 * c6r[lr_j]
-    alpha = 0.5 * (ai + aj)
-    num = 2.0 * c6i * c6j * aj * ai
-    den = ai * ai * c6j + aj * aj * c6i
-    c6 = num / den
-    b0, b1, b2, b3 = -0.00433008, 0.24428889, 0.04125273, -0.00078893
-    fsf = float(a["lr_fine_structure"]) ** (-4.0 / 21.0)
-    a7 = alpha ** (1.0 / 7.0)
-    rvdw = fsf * a7
-    sig = b3 * rvdw * rvdw * rvdw + b2 * rvdw * rvdw + b1 * rvdw + b0
-    gam = 0.5 / (sig * sig)
-    c8 = 5.0 * c6 / gam
-    c10 = 245.0 * c6 / (8.0 * gam * gam)
-    damp = float(a["lr_dispersion_scale"]) * 2.0 * 2.54 * a7
-    dau = rl / float(a["lr_bohr_angstrom"])
-    r2 = dau * dau
-    r4 = r2 * r2
-    r6 = r4 * r2
-    r8 = r4 * r4
-    r10 = r8 * r2
-    p2 = damp * damp
-    p4 = p2 * p2
-    p6 = p4 * p2
-    p8 = p4 * p4
-    p10 = p8 * p2
-    qdo = -c6 / (r6 + p6) - c8 / (r8 + p8) - c10 / (r10 + p10)
-    d_sw = smooth_switch(rl, float(a["lr_dispersion_cuton_angstrom"]), cutoff)
-    e_disp = full_scale * float(a["lr_hartree_ev"]) * qdo * d_sw
-    valid = (alpha > 0.0) & (den > 1.0e-30)
-    e_disp = torch.where(valid, e_disp, torch.zeros_like(e_disp))
+    e_elec, e_disp = long_range_pairs(m, zi, charge, ratio, c6r, lr_i, lr_j, lr_vec)
     pair_e = e_elec + e_disp
     e_lr = torch.zeros(n, dtype=DT).index_add(0, lr_i, 0.5 * pair_e).index_add(0, lr_j, 0.5 * pair_e)
     e_elec_atom = torch.zeros(n, dtype=DT).index_add(0, lr_i, 0.5 * e_elec).index_add(0, lr_j, 0.5 * e_elec)
@@ -569,3 +580,40 @@ def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -
         out["virial"] = vir
         out["virial_atom"] = vir_atom
     return out
+
+
+def long_range_only(m: OracleModel, pos, z, charges, ratios, cell=None) -> dict:
+    """Long-range term alone for given partial charges and Hirshfeld ratios
+    (physical_long_range.cpp:62-380 for the energies, dE/dq, dE/dh and pair
+    forces; the per-atom virial split of pair_so3lr_native_mpi.cpp:944-990).
+
+    Returns per-atom ``e_lr``, ``e_elec``, ``e_disp``, ``dq`` (dE_lr/dq_i),
+    ``dh`` (dE_lr/dh_i), the direct force ``f`` = -dE_lr/dx at fixed charges and
+    ratios, and ``virial_atom`` (half of every pair's -v (x) dE/dv, symmetrised,
+    to each of its two atoms)."""
+    n = len(z)
+    zt = torch.as_tensor(np.asarray(z), dtype=torch.long)
+    lr_i, lr_j, lr_shift = half_pairs(np.asarray(pos, dtype=np.float64), cell, m.r_lr)
+    lr_i = torch.as_tensor(lr_i)
+    lr_j = torch.as_tensor(lr_j)
+    x = torch.tensor(np.asarray(pos, dtype=np.float64), dtype=DT, requires_grad=True)
+    q = torch.tensor(np.asarray(charges, dtype=np.float64), dtype=DT, requires_grad=True)
+    h = torch.tensor(np.asarray(ratios, dtype=np.float64), dtype=DT, requires_grad=True)
+    lr_vec = x[lr_j] + torch.as_tensor(lr_shift, dtype=DT) - x[lr_i]
+    e_elec, e_disp = long_range_pairs(m, zt - 1, q, h, None, lr_i, lr_j, lr_vec)
+    pair_e = e_elec + e_disp
+    e_lr = torch.zeros(n, dtype=DT).index_add(0, lr_i, 0.5 * pair_e).index_add(0, lr_j, 0.5 * pair_e)
+    e_el = torch.zeros(n, dtype=DT).index_add(0, lr_i, 0.5 * e_elec).index_add(0, lr_j, 0.5 * e_elec)
+    e_di = torch.zeros(n, dtype=DT).index_add(0, lr_i, 0.5 * e_disp).index_add(0, lr_j, 0.5 * e_disp)
+    g_x, g_q, g_h, g_v = torch.autograd.grad(e_lr.sum(), [x, q, h, lr_vec])
+    vv = lr_vec.detach().numpy()
+    gg = g_v.numpy()
+    w = np.stack([-(vv[:, 0] * gg[:, 0]), -(vv[:, 1] * gg[:, 1]), -(vv[:, 2] * gg[:, 2]),
+                  -0.5 * (vv[:, 0] * gg[:, 1] + vv[:, 1] * gg[:, 0]),
+                  -0.5 * (vv[:, 0] * gg[:, 2] + vv[:, 2] * gg[:, 0]),
+                  -0.5 * (vv[:, 1] * gg[:, 2] + vv[:, 2] * gg[:, 1])], axis=1)
+    vir_atom = np.zeros((n, 6))
+    np.add.at(vir_atom, lr_i.numpy(), 0.5 * w)
+    np.add.at(vir_atom, lr_j.numpy(), 0.5 * w)
+    return {"e_lr": e_lr.detach().numpy(), "e_elec": e_el.detach().numpy(), "e_disp": e_di.detach().numpy(),
+            "dq": g_q.numpy(), "dh": g_h.numpy(), "f": -g_x.numpy(), "virial_atom": vir_atom}

@@ -355,14 +355,23 @@ int so3lr_long_range_noalloc(so3lr_handle *h, long long natoms, const double *x,
     if (ev.has_c6_head())
       throw Error("SO3LR no-alloc long range: the model has a C6-ratio head; this entry point takes Hirshfeld "
                   "ratios only");
-    int previous = 0;
-    SO3_CUDA(cudaGetDevice(&previous));
-    if (previous != ev.device()) SO3_CUDA(cudaSetDevice(ev.device()));
+    // the caller's current device is restored on every exit, the error paths included
+    struct DeviceRestore {
+      int previous = -1;
+      ~DeviceRestore() {
+        if (previous >= 0) cudaSetDevice(previous);
+      }
+    } restore;
+    int current = 0;
+    SO3_CUDA(cudaGetDevice(&current));
+    if (current != ev.device()) {
+      restore.previous = current;
+      SO3_CUDA(cudaSetDevice(ev.device()));
+    }
     const auto t = ev.long_range_tables();
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ev.stream();
     so3lr_b200::long_range_noalloc(int(natoms), x, q, ratios, z, t.alpha_ref, t.c6_ref, t.table_size, t.params,
                                    t.cutoff, e_lr, e_elec, e_disp, dq, dh, f, virial_atom, s);
-    if (previous != ev.device()) SO3_CUDA(cudaSetDevice(previous));
     return 0;
   } catch (const std::exception &e) {
     return report(e, err, errlen, h);

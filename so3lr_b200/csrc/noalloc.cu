@@ -16,7 +16,9 @@
 // share them, so two calls that overlap on the GPU (on different streams, or on
 // different host threads) race on this scratch and must be serialised by the
 // caller. Each call overwrites every scratch element it reads before reading it,
-// so no clearing between calls is needed.
+// so no clearing between calls is needed. The scratch addresses are resolved
+// once per device and kept for the life of the process, so the entry point must
+// not be used after a reset of the device's primary context (cudaDeviceReset).
 #include <mutex>
 
 #include "kernels.cuh"

@@ -2,7 +2,7 @@
 // pair styles so3lr/b200 and so3lr/b200/turbo, the way the reference's plugin
 // registers so3lr/native/mpi (plugins/lammps/so3lrnativeplugin.cpp:17-35).
 // Build as a shared module against the LAMMPS src/ headers and
-// libso3lr_b200.so (recipe in INTEGRATION.md).
+// libso3lr_b200.so.
 #include "lammpsplugin.h"
 #include "version.h"
 
