@@ -19,6 +19,14 @@ Printed JSON line (rank 0):
   step_roofline  the whole step's FP64 work (the reference algorithm's FLOP
           count and the FLOP this build executes) against the FP64 peak
   cpu_baseline  the float64 CPU restatement (oracle/) on a bounded sample
+  identity  one single-point evaluation of the config-4 box (64,000 H2O,
+          192,000 atoms, seed 2026) at every GPU count, outside the timed
+          regions: energy and virial as exact hex floats and a SHA-256 of the
+          forces, so that runs at 1, 2, 4 and 8 GPUs compare bit for bit
+  stats.exchange_ms_per_step  (N > 1) device time per step of each exchange
+          phase (position all-gather, halo-list rebuild, feature and adjoint
+          halo exchanges, charge/ratio all-gathers, exact-sum all-gathers),
+          max over ranks
 For N > 1 (torchrun) the box grows with N (N x 8,000 molecules, weak scaling:
 24,000 atoms per GPU, 192,000 atoms at N = 8 as in config 4) and is split into
 N spatial bricks; each rank owns the atoms of its brick, evaluates their pairs,
@@ -27,9 +35,10 @@ ratios; send/receive of the halo rows of block features and adjoints). The N > 1
 are NVT with a Nose-Hoover chain at 300 K (config 4). Times are the max over
 ranks.
 
---impl reference times the reference algorithm's CPU restatement on the host
-cores (the reference's own CPU paths cannot be built here: its kernels require
-the Kokkos CUDA backend and cuBLAS).
+--impl reference times the reference algorithm's CPU restatement on all host
+threads, each step one energy+force evaluation of the same 24,000-atom box the
+GPU arm integrates (the reference's own CPU paths cannot be built here: its
+kernels require the Kokkos CUDA backend and cuBLAS).
 """
 from __future__ import annotations
 
@@ -57,6 +66,25 @@ CONFIGS = {
     2: (1000, "config2: NVE MD of 1,000 H2O (3,000 atoms), periodic cubic box, 0.5 fs, float64"),
     3: (8000, "config3: NVE MD of 8,000 H2O (24,000 atoms), periodic cubic box, 0.5 fs, float64"),
 }
+
+
+def workload(config: int, world: int):
+    """Molecule count and the `config` record of the timed workload, shared by
+    both arms so that their lines describe the same configuration."""
+    nmol, desc = CONFIGS[config]
+    if world > 1:
+        nmol *= world
+        desc = (f"config4 (weak-scaled): NVT MD of {nmol:,} H2O ({3 * nmol:,} atoms) on {world} GPUs, "
+                f"Nose-Hoover chain (3 thermostats, 300 K, 0.05 ps), spatial bricks, periodic cubic box, "
+                f"0.5 fs, float64")
+    from so3lr_b200.systems import box_length
+    cfg = {"workload": desc, "atoms": 3 * nmol, "atoms_per_gpu": 3 * nmol / world,
+           "box_A": float(box_length(nmol, 0.997)),
+           "seed": 2026, "timestep_fs": 0.5,
+           "parallelism": "single" if world == 1 else
+           f"spatial{world} (brick decomposition, NCCL all-gather of owned rows, max over ranks)",
+           "l2": "no flush: per-step working set (pair filters, HBM-resident activations) exceeds L2"}
+    return nmol, cfg
 
 
 def dist_env():
@@ -155,6 +183,36 @@ def measure_fp64_peak(device: int) -> float:
     return best
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (lscpu / /proc/cpuinfo), for the baseline record."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def oracle_checkpointing(natoms: int) -> bool:
+    """Whether the oracle keeps only block inputs for its reverse: about
+    2.6 MB per atom held otherwise, 1.4 MB per atom with it (measured on the
+    3,000-atom box); chosen when the host's available memory is short."""
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available
+    except Exception:
+        return True
+    return natoms * 2.6e6 * 1.5 > avail
+
+
 def cpu_baseline(seconds: float = 12.0) -> dict:
     """Oracle (float64 CPU restatement of the reference kernels) on a bounded sample."""
     import torch
@@ -173,49 +231,62 @@ def cpu_baseline(seconds: float = 12.0) -> dict:
             break
     dt = time.perf_counter() - t0
     return {"value": len(w.z) * count / dt, "unit": "atom-steps/s", "cores": torch.get_num_threads(),
-            "kind": "port",
+            "kind": "port", "cpu": cpu_model(),
             "sample": f"{count} energy+force evaluations of a 648-atom periodic water box (216 H2O) "
                       f"by the float64 CPU restatement in oracle/ (torch CPU, {torch.get_num_threads()} threads)"}
 
 
 def run_reference(args) -> None:
+    """The reference algorithm's float64 CPU restatement (oracle/, torch CPU, all
+    host threads) on the workload of our arm. At N = 1 every step is one
+    energy+force evaluation of the same 24,000-atom box (same seed) that the GPU
+    arm integrates; under torchrun rank 0 alone runs, and each step evaluates
+    that 24,000-atom box, which is one GPU's share of the weak-scaled workload
+    (the whole 192,000-atom box would take minutes per step on the CPU)."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
     import torch
-    from oracle.so3lr_oracle import OracleModel, System, evaluate
+    from oracle.so3lr_oracle import OracleModel, System, build_graphs, evaluate
     from so3lr_b200.systems import water_box
+    threads = host_threads()
+    torch.set_num_threads(threads)
     om = OracleModel.load(str(ROOT / "models" / "so3lr.so3lr"))
     if args.config == 5:
         from so3lr_b200.systems import turbo_batch
         pos, z, off, q, mult = turbo_batch(32, seed=7)
         image = np.repeat(np.arange(len(off) - 1), np.diff(off))
         s = System(pos=pos, z=z, image=image, image_charge=q, image_multiplicity=mult)
-        n_sample, what = len(z), "a 32-cluster pack"
+        n_sample, what = len(z), "a 32-cluster pack (a bounded sample)"
         n_atoms = int(len(turbo_batch(TURBO_CLUSTERS, seed=7)[1]))
-        desc = f"config5: NVE MD of a turbo pack of {TURBO_CLUSTERS} water clusters ({n_atoms} atoms)"
+        cfg = {"workload": f"config5: NVE MD of a turbo pack of {TURBO_CLUSTERS} water clusters ({n_atoms} atoms)"}
     else:
-        w = water_box(216, seed=7)
+        nmol, cfg = workload(args.config, world)
+        w = water_box(CONFIGS[args.config][0], seed=2026)
         s = System(pos=w.pos, z=w.z, cell=w.cell)
-        n_sample, what = len(w.z), "a 648-atom periodic water box (216 H2O)"
-        n_atoms, desc = CONFIGS[args.config][0] * 3, CONFIGS[args.config][1]
+        n_sample = len(w.z)
+        what = (f"the same {n_sample}-atom box the GPU arm integrates (seed 2026)" if world == 1 else
+                f"the {n_sample}-atom box of one GPU's share of the {3 * nmol}-atom workload (a bounded sample)")
+    ckpt = oracle_checkpointing(n_sample)
+    graphs = build_graphs(om, s)  # the reference rebuilds its lists only on reneighbouring steps
     for _ in range(args.warmup):
-        evaluate(om, s)
+        evaluate(om, s, graphs=graphs, checkpoint_blocks=ckpt)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        evaluate(om, s)
+        evaluate(om, s, graphs=graphs, checkpoint_blocks=ckpt)
     dt = time.perf_counter() - t0
     value = n_sample * args.steps / dt
-    cores = torch.get_num_threads()
-    sample = (f"each step = one energy+force evaluation of {what}, a bounded "
-              f"sample of the {n_atoms}-atom workload, by the float64 CPU restatement of the reference kernels "
-              f"(oracle/, torch CPU, {cores} threads); the reference's Kokkos/cuBLAS code has no CPU build")
+    sample = (f"each step = one energy+force evaluation of {what} by the float64 CPU restatement of the "
+              f"reference kernels (oracle/, torch CPU, {threads} threads"
+              f"{', block intermediates recomputed in the reverse' if ckpt else ''}); the reference's "
+              f"Kokkos/cuBLAS code has no CPU build")
     line = {
         "impl": "reference", "metric": "atom-steps/s", "value": value, "unit": "atom-steps/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": desc, "sample_atoms": n_sample},
-        "cpu_baseline": {"value": value, "unit": "atom-steps/s", "cores": cores, "kind": "port", "sample": sample},
+        "config": cfg,
+        "cpu_baseline": {"value": value, "unit": "atom-steps/s", "cores": threads, "kind": "port",
+                         "cpu": cpu_model(), "sample": sample, "sample_atoms": n_sample},
         "e2e": {"value": value, "unit": "atom-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -245,12 +316,7 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    nmol, desc = CONFIGS[args.config]
-    if world > 1:
-        nmol *= world
-        desc = (f"config4 (weak-scaled): NVT MD of {nmol:,} H2O ({3 * nmol:,} atoms) on {world} GPUs, "
-                f"Nose-Hoover chain (3 thermostats, 300 K, 0.05 ps), spatial bricks, periodic cubic box, "
-                f"0.5 fs, float64")
+    nmol, cfg = workload(args.config, world)
     w = water_box(nmol, seed=2026)
     n = len(w.z)
     v0 = maxwell_boltzmann(w.mass, 300.0, seed=11)
@@ -270,7 +336,7 @@ def run_ours(args) -> None:
     model.md_run(args.warmup, DT_PS)
     stats = model.stats()
     model.profile(True)
-    for k in (0, 1):
+    for k in range(len(PROFILE_KINDS)):
         model.profile_read(k)
     launches0 = model.launch_count()
     clocks = ClockSampler(local)
@@ -284,8 +350,14 @@ def run_ours(args) -> None:
     ms = t_start.elapsed_time(t_end)
     clock_info = clocks.stop()
     launches = model.launch_count() - launches0
-    prof = [model.profile_read(k) for k in (0, 1)]
+    prof_all = [model.profile_read(k) for k in range(len(PROFILE_KINDS))]
+    prof = prof_all[:2]
     model.profile(False)
+    # per-step device time of each exchange phase, max over ranks (N > 1)
+    exchange = None
+    if world > 1:
+        exchange = {name: max_over_ranks(prof_all[k]["ms"]) / args.steps
+                    for k, name in enumerate(PROFILE_KINDS) if k >= 2}
     state = model.md_state(n)
     owned = model.owned_atoms()
     ms_max = max_over_ranks(ms)
@@ -333,6 +405,9 @@ def run_ours(args) -> None:
         except (ValueError, KeyError):
             traffic = None
 
+    # ---- one fixed system at every GPU count (bit-identity across N) ----------
+    identity = None if args.no_identity else identity_check(model)
+
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
         steps_per_s = args.steps / (ms_max * 1e-3)
@@ -343,14 +418,11 @@ def run_ours(args) -> None:
             "higher_is_better": True, "scaling": "weak",
             "vs_baseline": (value / A100_24K_ATOM_STEPS) if (world == 1 and args.config == 3) else None,
             "dtype": "f64", "data": "synthetic",
-            "config": {"workload": desc, "atoms": n, "atoms_per_gpu": n / world, "atoms_owned_rank0": owned,
-                       "box_A": float(w.cell[0]),
-                       "sr_edges": stats["sr_edges"], "sr_pairs": stats["sr_pairs"],
-                       "ns_per_day": steps_per_s * 0.0432,
-                       "parallelism": "single" if world == 1 else
-                       f"spatial{world} (brick decomposition, NCCL all-gather of owned rows, max over ranks)",
-                       "l2": "no flush: per-step working set (pair filters, HBM-resident activations) exceeds L2",
-                       "timestep_fs": 0.5},
+            "config": cfg,
+            "stats": {"atoms_owned_rank0": owned, "sr_edges_rank0": stats["sr_edges"],
+                      "sr_pairs_rank0": stats["sr_pairs"], "ns_per_day": steps_per_s * 0.0432,
+                      "exchange_ms_per_step": exchange},
+            "identity": identity,
             "e2e": {"value": e2e_value, "unit": "atom-steps/s", "h2d_bytes_per_step": world * 3 * 8 * n,
                     "d2h_bytes_per_step": world * (3 * 8 * n + 7 * 8)},
             "roofline": {"bound": "tensor", "kernel": dom_name, "achieved": achieved, "peak": peak,
@@ -381,6 +453,10 @@ def run_ours(args) -> None:
 
 
 TURBO_CLUSTERS = 4096
+
+# so3lr_profile_read kinds: the pair-filter kernels and the multi-GPU exchange phases
+PROFILE_KINDS = ("filter_forward", "filter_reverse", "position_allgather", "halo_list_rebuild",
+                 "feature_halo_exchange", "adjoint_halo_exchange", "charge_ratio_allgather", "exact_sum_allgather")
 
 
 def run_turbo(args) -> None:
@@ -495,6 +571,28 @@ def run_turbo(args) -> None:
         dist.destroy_process_group()
 
 
+IDENTITY_MOLECULES = 64000
+
+
+def identity_check(model) -> dict:
+    """One single-point evaluation of the config-4 box (64,000 H2O, 192,000
+    atoms, seed 2026) through so3lr_compute, outside every timed region, at
+    whatever GPU count this run has (collective when decomposed). The energy
+    and virial as exact hexadecimal floats and a SHA-256 of the force array
+    (float64, little-endian, input atom order) let runs at 1, 2, 4 and 8 GPUs
+    be compared bit for bit."""
+    import hashlib
+    from so3lr_b200.systems import water_box
+    w = water_box(IDENTITY_MOLECULES, seed=2026)
+    r = model.compute(w.pos, w.z, cell=w.cell, boxlo=w.boxlo, terms=False)
+    f = np.ascontiguousarray(r["forces"], dtype="<f8")
+    return {"system": f"config4 box: {IDENTITY_MOLECULES:,} H2O ({3 * IDENTITY_MOLECULES:,} atoms), seed 2026, "
+                      f"single point through so3lr_compute",
+            "energy": r["energy"], "energy_hex": float(r["energy"]).hex(),
+            "virial_hex": [float(v).hex() for v in r["virial"]],
+            "forces_sha256": hashlib.sha256(f.tobytes()).hexdigest()}
+
+
 def deal_clusters(sizes, rank: int, world: int) -> np.ndarray:
     """The clusters rank `rank` of `world` evaluates: sorted by size, largest
     first (stable), then dealt round robin, so every cluster goes to exactly
@@ -540,6 +638,8 @@ def main():
     ap.add_argument("--config", type=int, choices=[1, 2, 3, 5], default=3,
                     help="3 (default): the headline 24,000-atom box; 5: the turbo cluster pack")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--no-identity", action="store_true",
+                    help="skip the single-point evaluation of the 192,000-atom box (energy and force hash)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

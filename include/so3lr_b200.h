@@ -201,12 +201,18 @@ int so3lr_md_thermostat_energy(so3lr_handle *h, double *energy, char *err, size_
  * potential energy of the last force evaluation. Synchronises the stream. */
 int so3lr_md_state(so3lr_handle *h, double *x, double *v, double *f, double *energy, char *err, size_t errlen);
 
-/* Optional timing of the dominant kernels (the pair-filter MLPs) with CUDA
- * events on the handle's stream. kernel 0 = filter forward, 1 = filter
- * reverse. so3lr_profile_read synchronises, returns the summed device time,
- * the number of timed launches and their algorithmic FLOPs, and resets. The
- * reference has per-phase timing behind SO3_NATIVE_MPI_PROFILE
- * (pair_so3lr_native_mpi.cpp:1259-1266, 1887-1956); this is its per-kernel form. */
+/* Optional timing of the dominant kernels (the pair-filter MLPs) and of the
+ * multi-GPU exchange phases with CUDA events on the handle's stream.
+ * kernel 0 = filter forward, 1 = filter reverse; on a multi-GPU handle also
+ * 2 = position all-gather after the Verlet drift, 3 = halo-list rebuild (lists,
+ * count all-gather and the host check, including the stream's wait for it),
+ * 4 = block-feature halo exchanges, 5 = block-adjoint halo exchanges,
+ * 6 = charge/ratio all-gathers before the long range, 7 = the integer
+ * all-gathers of the exact global sums. so3lr_profile_read synchronises,
+ * returns the summed device time, the number of timed spans and (filters
+ * only) their algorithmic FLOPs, and resets. The reference has per-phase
+ * timing behind SO3_NATIVE_MPI_PROFILE (pair_so3lr_native_mpi.cpp:1259-1266,
+ * 1887-1956); this is its per-kernel form. */
 int so3lr_profile(so3lr_handle *h, int enable);
 int so3lr_profile_read(so3lr_handle *h, int kernel, double *total_ms, long long *launches, double *flops, char *err,
                        size_t errlen);

@@ -43,6 +43,7 @@ from dataclasses import dataclass
 
 import numpy as np
 import torch
+import torch.utils.checkpoint
 
 from .model_io import NativeModelFile, load_model
 from .neighbors import directed_pairs, half_pairs
@@ -367,8 +368,12 @@ def long_range_pairs(m: OracleModel, zi, charge, ratio, c6r, lr_i, lr_j, lr_vec)
     return e_elec, e_disp
 
 
-def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -> dict:
-    """Energy, forces, virial and per-atom terms for one system (or a turbo pack)."""
+def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True, checkpoint_blocks: bool = False) -> dict:
+    """Energy, forces, virial and per-atom terms for one system (or a turbo pack).
+
+    checkpoint_blocks: keep only each block's inputs for the reverse and
+    recompute its intermediates there (torch.utils.checkpoint); the same
+    operations on the same inputs, a third of the peak memory."""
     p = m.p
     n = len(s.z)
     z = torch.as_tensor(np.asarray(s.z), dtype=torch.long)
@@ -422,7 +427,8 @@ def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -
     heads = 4
     hw = F // heads
 
-    for b in range(m.layers):
+    def block(b, x, ev):
+        """Interaction block b (integrated_block0.cpp:117-385, post_attention_block0.cpp:97-300)."""
         pre = f"model.euclidean_transformers.{b}."
         if m.resid is not None:  # x = resid[b] x + x0[b] x0 (local_energy_reverse.cpp:145-157)
             x = m.resid[b] * x + m.x0_scale[b] * x_emb
@@ -470,6 +476,13 @@ def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True) -
                                        p[pre + "interaction_block.linear_layer.weight"]) + p[pre + "interaction_block.linear_layer.bias"]
         x = block_norm(m.norm2, post + t[:, :F], p, pre + "layer_norm_inv_2", eps)
         ev = A * (1.0 + t[:, F + deg])
+        return x, ev
+
+    for b in range(m.layers):
+        if checkpoint_blocks:  # same arithmetic; the block's intermediates are recomputed in the reverse
+            x, ev = torch.utils.checkpoint.checkpoint(block, b, x, ev, use_reentrant=False)
+        else:
+            x, ev = block(b, x, ev)
 
     # --- heads (output_heads.cpp:137-176, 341-451) -----------------------------
     eo = "model.atomic_energy_output_block."

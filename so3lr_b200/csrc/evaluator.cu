@@ -334,15 +334,18 @@ void Evaluator::set_comm(int nranks, int rank, const void *unique_id) {
   if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclCommInitRank failed: ") + nccl().get_error_string(r));
 }
 
-void Evaluator::allgather_rows(double *a, int width) {
+void Evaluator::allgather_rows(double *a, int width, int prof) {
   if (nranks_ == 1) return;
+  if (prof >= 0) prof_begin(prof);
   const std::size_t count = std::size_t(stride_) * width;
   const ncclResult_t r = nccl().all_gather(a + std::size_t(rank_) * count, a, count, ncclDouble, comm_, stream_);
   if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclAllGather failed: ") + nccl().get_error_string(r));
+  if (prof >= 0) prof_end(prof, 0.0);
 }
 
-void Evaluator::halo_exchange(double *a, int wa, double *b, int wb) {
+void Evaluator::halo_exchange(double *a, int wa, double *b, int wb, int prof) {
   if (nranks_ == 1) return;
+  prof_begin(prof);
   const int w = wa + wb;
   const long long nsend = halo_send_off_[nranks_], nrecv = halo_recv_off_[nranks_];
   double *sbuf = halo_send_buf_.reserve(std::size_t(std::max(1LL, nsend)) * w, 1.25);
@@ -362,6 +365,7 @@ void Evaluator::halo_exchange(double *a, int wa, double *b, int wb) {
   }
   check(api.group_end(), "ncclGroupEnd");
   launch_halo_unpack(int(nrecv), halo_recv_rows_.get(), rbuf, a, wa, b, wb, stream_);
+  prof_end(prof, 0.0);
 }
 
 // exact sums over segments of the owned rows (global over ranks when decomposed);
@@ -377,8 +381,10 @@ void Evaluator::exact_sums(const double *v, int stride, int ncol, int nseg, cons
   long long *all = local + per_rank;
   launch_fixed_segment_sum(nseg, nblk, seg, v, stride, ncol, local, stream_);
   if (nranks_ > 1) {
+    prof_begin(kProfExactSums);
     const ncclResult_t r = nccl().all_gather(local, all, per_rank, ncclInt64, comm_, stream_);
     if (r != ncclSuccess) throw Error(std::string("SO3LR: ncclAllGather failed: ") + nccl().get_error_string(r));
+    prof_end(kProfExactSums, 0.0);
     launch_fixed_finish(all, nranks_ * nblk, count, out, stream_);
   } else {
     launch_fixed_finish(local, nblk, count, out, stream_);
@@ -695,7 +701,7 @@ void Evaluator::prof_end(int k, double flops) {
   p.flops += flops;
 }
 void Evaluator::read_profile(int k, double *ms, long long *launches, double *flops) {
-  if (k < 0 || k > 1) throw Error("SO3LR: unknown profiled kernel");
+  if (k < 0 || k >= kProfKinds) throw Error("SO3LR: unknown profiled kernel");
   SO3_CUDA(cudaStreamSynchronize(stream_));
   KernelProfile &p = prof_[k];
   double total = 0;
@@ -738,6 +744,7 @@ void Evaluator::build_neighbors() {
   if (!identity_) {
     // halo lists from this GPU's (symmetric) neighbour lists; every rank's
     // per-peer counts are gathered so that all ranks can check them together
+    prof_begin(kProfHaloLists);
     const int cnt = nranks_ * stride_;
     int *flags = halo_flags_.reserve(2 * std::size_t(cnt));
     int *pos = halo_pos_.reserve(2 * std::size_t(cnt));
@@ -766,6 +773,8 @@ void Evaluator::build_neighbors() {
           throw Error("SO3LR: halo lists of GPUs " + std::to_string(s) + " and " + std::to_string(p) + " disagree");
     halo_send_off_.assign(host_halo_ + rank_ * lo, host_halo_ + rank_ * lo + nranks_ + 1);
     halo_recv_off_.assign(host_halo_ + rank_ * lo + nranks_ + 1, host_halo_ + rank_ * lo + lo);
+    // recorded after the host check: the span includes the stream's wait for it
+    prof_end(kProfHaloLists, 0.0);
   }
   const int P = host_small_[1];
   if (identity_ && 2 * P != E) throw Error("SO3LR: short-range list is not symmetric");
@@ -831,11 +840,11 @@ void Evaluator::compute() {
 
   for (int b = 0; b < layers_; ++b) {
     const BlockW &w = blocks_[b];
-    prof_begin(0);
+    prof_begin(kProfFilterForward);
     launch_filter_forward(P, geo_.get(), nb_.pair_a, nb_.pair_b, b == 0 ? nullptr : evb_[b]->get(), w.cg_att, w.finv,
                           w.fev, rad_, f_inv_[b]->get(), f_ev_[b]->get(), sp_[b]->get(),
                           b == 0 ? drbf_.get() : nullptr, s);
-    prof_end(0, kFilterFlopsPerPair * double(P));
+    prof_end(kProfFilterForward, kFilterFlopsPerPair * double(P));
     {  // per-head projections qkv[row][h][5][32] = x[row][h*32:(h+1)*32] W_h of every
        // row the attention reads: the owned rows and (decomposed) their halo
       GemmArgs g{};
@@ -903,7 +912,7 @@ void Evaluator::compute() {
         launch_residual_combine(n, xb_[b + 1]->get() + r0 * kF, x0_.get() + r0 * kF, resid_[b + 1], x0s_[b + 1],
                                 xb_[b + 1]->get() + r0 * kF, s);
       // the halo rows of the next block's input
-      halo_exchange(xb_[b + 1]->get(), kF, evb_[b + 1]->get(), kEV);
+      halo_exchange(xb_[b + 1]->get(), kF, evb_[b + 1]->get(), kEV, kProfFeatureHalo);
     }
   }
 
@@ -931,9 +940,9 @@ void Evaluator::compute() {
   }
   launch_charge_correct(n, raw_q_.get() + r0, img_sums_.get(), image_charge_.get(), image_of_.get() + r0, count_seg,
                         q_.get() + r0, nullptr, nullptr, s);
-  allgather_rows(q_.get(), 1);
-  allgather_rows(ratio_.get(), 1);
-  if (c6) allgather_rows(ratio6_.get(), 1);
+  allgather_rows(q_.get(), 1, kProfLrGather);
+  allgather_rows(ratio_.get(), 1, kProfLrGather);
+  if (c6) allgather_rows(ratio6_.get(), 1, kProfLrGather);
 
   // ---- long range (owned rows) ------------------------------------------------
   launch_long_range(n, spec_.n, nb_, lr_cut_, z_.get(), q_.get(), ratio_.get(), c6 ? ratio6_.get() : nullptr,
@@ -1003,15 +1012,15 @@ void Evaluator::compute() {
                              w.ln1w, A_[b]->get() + r0 * kEV, w.cg_int, g_cat_.get() + r0 * kIntW,
                              g_a_.get() + r0 * kF, g_A_.get() + r0 * kEV, s);
     // the sender role of the attention reverse reads the neighbours' adjoints
-    halo_exchange(g_a_.get(), kF, g_A_.get(), kEV);
+    halo_exchange(g_a_.get(), kF, g_A_.get(), kEV, kProfAdjointHalo);
     launch_attention_reverse(n, nb_, geo_.get(), sh_.get(), qkv_[b]->get(), f_inv_[b]->get(), f_ev_[b]->get(),
                              g_a_.get(), g_A_.get(), norm_, b > 0 ? g_qkv_.get() : nullptr, pair_sc_.get(),
                              g_filt_inv_.get(), g_filt_ev_.get(), s);
-    prof_begin(1);
+    prof_begin(kProfFilterReverse);
     launch_filter_reverse(P, geo_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr, w.cg_att, w.finv,
                           w.fev, rad_, g_filt_inv_.get(), g_filt_ev_.get(), sp_[b]->get(), drbf_.get(), g_A_.get(),
                           pair_sc_.get(), b > 0, b < layers_ - 1, g_r_.get(), g_y_.get(), gl0_.get(), s);
-    prof_end(1, kFilterFlopsPerPair * double(P));
+    prof_end(kProfFilterReverse, kFilterFlopsPerPair * double(P));
     if (b > 0) {
       if (qk_norm_)  // gradient w.r.t. the projections before their normalisation
         launch_qk_norm_reverse(n, qkv_[b]->get() + r0 * kQKV, qkr_[b]->get() + r0 * 16, g_qkv_.get() + r0 * kQKV, s);
@@ -1196,7 +1205,7 @@ void Evaluator::md_steps(int nsteps, double dt) {
     if (nvt_) nhc_half(dt);
     launch_verlet_first(n_own_, x_.get() + 3 * r0, v_.get() + 3 * r0, force_.get() + 3 * r0, inv_mass_.get() + r0, dt,
                         ftm2v, stream_);
-    allgather_rows(x_.get(), 3);
+    allgather_rows(x_.get(), 3, kProfPositionGather);
     compute();
     launch_verlet_second(n_own_, v_.get() + 3 * r0, force_.get() + 3 * r0, inv_mass_.get() + r0, dt, ftm2v, stream_);
     if (nvt_) nhc_half(dt);

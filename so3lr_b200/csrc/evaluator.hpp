@@ -126,9 +126,20 @@ class Evaluator {
   bool has_c6_head() const { return heads_.c6_w2 != nullptr; }
   std::size_t device_bytes() const;
 
-  // Optional CUDA-event timing of the pair-filter kernels on stream(): kernel 0 =
-  // filter forward, 1 = filter reverse. read_profile() synchronises, returns
-  // the summed device time, launch count and algorithmic FLOPs, and resets.
+  // Optional CUDA-event timing on stream() of the pair-filter kernels and of the
+  // multi-GPU exchange phases (ProfileKind). read_profile() synchronises,
+  // returns the summed device time, launch count and algorithmic FLOPs, and resets.
+  enum ProfileKind {
+    kProfFilterForward = 0,
+    kProfFilterReverse = 1,
+    kProfPositionGather = 2,   // all-gather of positions after the drift
+    kProfHaloLists = 3,        // halo-list rebuild: lists, count all-gather, host check
+    kProfFeatureHalo = 4,      // block-feature halo exchanges (forward)
+    kProfAdjointHalo = 5,      // block-adjoint halo exchanges (reverse)
+    kProfLrGather = 6,         // all-gathers of charges and ratios before the long range
+    kProfExactSums = 7,        // exact global sums (integer all-gathers)
+    kProfKinds = 8
+  };
   void set_profiling(bool on) { profiling_ = on; }
   void read_profile(int kernel, double *ms, long long *launches, double *flops);
 
@@ -218,10 +229,10 @@ class Evaluator {
   long long *host_halo_ = nullptr;  // pinned: all ranks' offsets
   std::vector<long long> halo_send_off_, halo_recv_off_;
   DeviceArray<long long> parts_;
-  void allgather_rows(double *a, int width);
+  void allgather_rows(double *a, int width, int prof = -1);
   // refresh the halo rows (other GPUs' atoms that neighbour this GPU's atoms)
   // of two row arrays at once; the identity layout (one GPU) does nothing
-  void halo_exchange(double *a, int wa, double *b, int wb);
+  void halo_exchange(double *a, int wa, double *b, int wb, int prof);
   void exact_sums(const double *v, int stride, int ncol, int nseg, const int *seg, double *out);
 
   struct KernelProfile {
@@ -231,7 +242,7 @@ class Evaluator {
     double flops = 0;
   };
   bool profiling_ = false;
-  KernelProfile prof_[2];
+  KernelProfile prof_[kProfKinds];
   void prof_begin(int k);
   void prof_end(int k, double flops);
 

@@ -95,13 +95,17 @@ def test_clock_sampler_keeps_only_rows_after_start(tmp_path, monkeypatch):
 
 def test_reference_arm_line_keeps_the_contract():
     """`bench.py --impl reference` (the CPU restatement timed on the host) prints
-    one JSON line with the keys the driver reads, on the same metric and
-    workload as the GPU arm."""
+    one JSON line with the keys the driver reads, on the same metric, workload
+    and `config` record as the GPU arm (config 1 here, to keep the test short;
+    the default config 3 evaluates the same 24,000-atom box as the GPU arm)."""
     import json
     import subprocess
     import sys
+    sys.path.insert(0, str(ROOT))
+    import bench
     res = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
-                          "--warmup", "0"], capture_output=True, text=True, timeout=600, cwd=str(ROOT))
+                          "--warmup", "0", "--config", "1"], capture_output=True, text=True, timeout=600,
+                         cwd=str(ROOT))
     assert res.returncode == 0, res.stderr
     lines = [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
     assert len(lines) == 1, res.stdout
@@ -112,9 +116,11 @@ def test_reference_arm_line_keeps_the_contract():
     assert d["impl"] == "reference" and d["metric"] == "atom-steps/s" and d["unit"] == "atom-steps/s"
     assert d["steps"] == 1 and d["warmup"] == 3  # at least 3 warm-up steps, whatever is asked
     assert d["value"] > 0 and d["higher_is_better"] is True and d["dtype"] == "f64"
-    assert d["config"]["workload"].startswith("config3")
+    assert d["config"]["workload"].startswith("config1")
+    assert d["config"] == bench.workload(1, 1)[1]  # the GPU arm's config record
     cb = d["cpu_baseline"]
     assert cb["value"] == d["value"] and cb["kind"] == "port" and cb["cores"] >= 1 and cb["sample"]
+    assert cb["sample_atoms"] == 192 and "same 192-atom box" in cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": "atom-steps/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
 
