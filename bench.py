@@ -364,18 +364,32 @@ def run_ours(args) -> None:
     value = n * args.steps / (ms_max * 1e-3)
 
     # ---- end to end through the C ABI with host buffers (e2e) ---------------
-    x_host = torch.empty((n, 3), dtype=torch.float64, pin_memory=True).numpy()
-    v_host = torch.empty((n, 3), dtype=torch.float64, pin_memory=True).numpy()
-    f = torch.empty((n, 3), dtype=torch.float64, pin_memory=True).numpy()
-    x_host[:] = state["x"]
-    v_host[:] = state["v"]
-    z32 = np.ascontiguousarray(w.z, dtype=np.int32)
-    model.compute(x_host, z32, cell=w.cell, boxlo=w.boxlo, terms=False, forces_out=f)
+    # one GPU: so3lr_compute with the whole system; several: every rank holds
+    # only the atoms of its brick on the host (as a LAMMPS rank does) and calls
+    # so3lr_compute_local, the GPUs exchanging the ranks' atoms themselves
+    from so3lr_b200.runtime import partition
+    mine = np.arange(n) if world == 1 else np.nonzero(partition(state["x"], w.boxlo, w.cell, world) == rank)[0]
+    nl = len(mine)
+    x_host = torch.empty((nl, 3), dtype=torch.float64, pin_memory=True).numpy()
+    v_host = torch.empty((nl, 3), dtype=torch.float64, pin_memory=True).numpy()
+    f = torch.empty((nl, 3), dtype=torch.float64, pin_memory=True).numpy()
+    x_host[:] = state["x"][mine]
+    v_host[:] = state["v"][mine]
+    z32 = np.ascontiguousarray(w.z[mine], dtype=np.int32)
+    tags = mine + 1
+
+    def evaluate_host():
+        if world == 1:
+            model.compute(x_host, z32, cell=w.cell, boxlo=w.boxlo, terms=False, forces_out=f)
+        else:
+            model.compute_local(n, tags, x_host, z32, cell=w.cell, boxlo=w.boxlo, eatom=False, forces_out=f)
+
+    evaluate_host()
     ftm2v = 1.0 / 1.0364269e-4
     dtf = 0.5 * DT_PS * ftm2v
     # velocity-Verlet half kicks and drift in place (no temporaries per step)
-    kick = np.ascontiguousarray(np.broadcast_to((dtf / w.mass)[:, None], (n, 3)))
-    tmp = np.empty((n, 3))
+    kick = np.ascontiguousarray(np.broadcast_to((dtf / w.mass[mine])[:, None], (nl, 3)))
+    tmp = np.empty((nl, 3))
     barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
@@ -383,7 +397,7 @@ def run_ours(args) -> None:
         v_host += tmp
         np.multiply(v_host, DT_PS, out=tmp)
         x_host += tmp
-        model.compute(x_host, z32, cell=w.cell, boxlo=w.boxlo, terms=False, forces_out=f)
+        evaluate_host()
         np.multiply(f, kick, out=tmp)
         v_host += tmp
     torch.cuda.synchronize()
@@ -423,8 +437,12 @@ def run_ours(args) -> None:
                       "sr_pairs_rank0": stats["sr_pairs"], "ns_per_day": steps_per_s * 0.0432,
                       "exchange_ms_per_step": exchange},
             "identity": identity,
-            "e2e": {"value": e2e_value, "unit": "atom-steps/s", "h2d_bytes_per_step": world * 3 * 8 * n,
-                    "d2h_bytes_per_step": world * (3 * 8 * n + 7 * 8)},
+            # one GPU: positions in, forces + energy/virial out; several: each
+            # rank's (tag, x, y, z, Z) records in, its forces + energy/virial out
+            "e2e": {"value": e2e_value, "unit": "atom-steps/s",
+                    "h2d_bytes_per_step": 3 * 8 * n if world == 1 else 5 * 8 * n,
+                    "d2h_bytes_per_step": 3 * 8 * n + world * 7 * 8,
+                    "call": "so3lr_compute" if world == 1 else "so3lr_compute_local (each rank its brick's atoms)"},
             "roofline": {"bound": "tensor", "kernel": dom_name, "achieved": achieved, "peak": peak,
                          "unit": "TFLOP/s", "frac": achieved / peak if peak else None, "traffic": traffic,
                          "peak_source": "FP64 cuBLAS DGEMM 8192^3 (torch.matmul float64) measured on this GPU "

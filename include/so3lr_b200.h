@@ -151,6 +151,47 @@ int so3lr_compute(so3lr_handle *h, const so3lr_frame *in, so3lr_result *out, cha
 int so3lr_compute_device(so3lr_handle *h, const so3lr_frame *in_device_x, double *d_f, double *d_eatom,
                          double *energy, double virial[6], char *err, size_t errlen);
 
+/* Rank-local frame: the atoms one rank owns (LAMMPS atom->nlocal, identified by
+ * atom->tag), the input the reference's pair style hands its evaluator
+ * (pair_so3lr_native_mpi.cpp:1267-1280). No ghost atoms: the GPUs exchange the
+ * ranks' atoms themselves. */
+typedef struct {
+  long long natoms;       /* atoms of the whole system (the nlocal of all ranks add up to it) */
+  long long nlocal;       /* atoms this rank passes (0 allowed) */
+  const long long *tag;   /* nlocal global tags in 1..natoms, each on exactly one rank */
+  const double *x;        /* nlocal * 3 */
+  const int *z;           /* nlocal atomic numbers, 1..99 */
+  int periodic;           /* as in so3lr_frame */
+  double boxlo[3];
+  double boxlen[3];
+  double total_charge;
+  double multiplicity;
+} so3lr_local_frame;
+
+typedef struct {
+  double *f;              /* nlocal * 3, overwritten with the total force on this rank's atoms */
+  double *eatom;          /* nlocal, optional */
+  double *vatom;          /* nlocal * 6, optional: per-atom virial (as so3lr_virial_atom) */
+  double energy;          /* whole-system potential energy (identical on every rank) */
+  double virial[6];       /* whole-system virial (identical on every rank) */
+} so3lr_local_result;
+
+/* Energy, forces, per-atom energies and virials for rank-local frames
+ * (replaces PairSO3LRNativeMPI::compute, pair_so3lr_native_mpi.cpp:1246-1978,
+ * with its per-rank input and output). On a multi-GPU handle every rank calls
+ * it with its own atoms (any split of the tags over the ranks); the GPUs
+ * all-gather the ranks' (tag, position, Z) records over NCCL, evaluate the
+ * system in their spatial bricks exactly as so3lr_compute does, and each rank
+ * gets back the results of its own atoms only. Forces, energies and virials are
+ * bit-identical to so3lr_compute's on the same system, for any split and any
+ * number of GPUs. A refusal of one rank's input (counts, NULL arrays, tags
+ * outside 1..natoms or repeated) is returned on every rank. On a one-GPU handle
+ * nlocal must equal natoms (tags in any order). The first call, and any call
+ * whose box, charge, multiplicity, atom count or atomic numbers change,
+ * prepares the system from the gathered records. */
+int so3lr_compute_local(so3lr_handle *h, const so3lr_local_frame *in, so3lr_local_result *out, char *err,
+                        size_t errlen);
+
 /* Multi-GPU spatial decomposition (one process and one handle per GPU; replaces
  * the MPI exchange plans and halo exchanges of pair_so3lr_native_mpi.cpp:455-930).
  * Rank 0 makes a 128-byte NCCL unique id with so3lr_nccl_unique_id and the

@@ -161,6 +161,31 @@ int so3lr_compute(so3lr_handle *h, const so3lr_frame *in, so3lr_result *out, cha
   }
 }
 
+int so3lr_compute_local(so3lr_handle *h, const so3lr_local_frame *in, so3lr_local_result *out, char *err,
+                        size_t errlen) {
+  if (!h || !in || !out) return report_msg("so3lr_compute_local: NULL argument", err, errlen);
+  try {
+    SystemSpec s;
+    // out-of-range counts are refused collectively inside (every rank learns of them)
+    s.n = (in->natoms > 0 && in->natoms <= (1LL << 30)) ? int(in->natoms) : 0;
+    const int nlocal = (in->nlocal >= 0 && in->nlocal <= (1LL << 30)) ? int(in->nlocal) : -1;
+    s.periodic = in->periodic != 0;
+    for (int d = 0; d < 3; ++d) {
+      s.lo[d] = in->boxlo[d];
+      s.len[d] = in->boxlen[d];
+    }
+    s.image_start = {0, s.n};
+    s.image_charge = {in->total_charge};
+    s.image_mult = {in->multiplicity};
+    const auto r = h->eval->compute_local(s, nlocal, in->tag, in->x, in->z, out->f, out->eatom, out->vatom);
+    out->energy = r.energy;
+    for (int k = 0; k < 6; ++k) out->virial[k] = r.virial[k];
+    return 0;
+  } catch (const std::exception &e) {
+    return report(e, err, errlen, h);
+  }
+}
+
 int so3lr_compute_device(so3lr_handle *h, const so3lr_frame *in, double *d_f, double *d_eatom, double *energy,
                          double virial[6], char *err, size_t errlen) {
   if (!h || !in || !d_f) return report_msg("so3lr_compute_device: NULL argument", err, errlen);

@@ -37,6 +37,7 @@ Evaluator::~Evaluator() {
   if (host_small_) cudaFreeHost(host_small_);
   if (host_halo_) cudaFreeHost(host_halo_);
   if (host_totals_) cudaFreeHost(host_totals_);
+  if (host_rec_) cudaFreeHost(host_rec_);
 }
 
 // ---------------------------------------------------------------------------
@@ -437,6 +438,7 @@ void Evaluator::prepare(const SystemSpec &spec_in, const double *host_x) {
   computed_ = false;
   md_ready_ = false;
   nvt_ = false;
+  local_ready_ = false;
   SystemSpec spec = spec_in;
   const int n = spec.n;
   if (n <= 0) throw Error("SO3LR: the system has no atoms");

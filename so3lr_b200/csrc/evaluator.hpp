@@ -112,6 +112,12 @@ class Evaluator {
   // per-atom virial (natoms x 6, xx yy zz xy xz yz) of the last compute(), input
   // atom order; collective when decomposed (synchronises the stream)
   void download_virial_atom(double *vatom);
+  // Rank-local frame (local_frame.cu): this rank passes its own nlocal atoms
+  // (global tags 1..frame.n, positions, atomic numbers; frame.z unused) and gets
+  // the forces (nlocal x 3), and optionally per-atom energies and virials, of
+  // those atoms back. Collective on a multi-GPU handle.
+  HostResult compute_local(const SystemSpec &frame, int nlocal, const long long *tag, const double *x, const int *z,
+                           double *f, double *eatom, double *vatom);
   const double *forces() const { return force_.get(); }
   const double *energy_device() const { return totals_.get(); }  // [0] energy, [1..6] virial
   StepStats stats() const { return stats_; }
@@ -218,6 +224,13 @@ class Evaluator {
   int n_rows_ = 0, stride_ = 0, row0_ = 0, n_own_ = 0;
   bool identity_ = true;
   std::vector<int> row_of_, tag_of_row_;
+  // rank-local frames: row of every tag, the gathered records, flags
+  DeviceArray<int> row_of_tag_, local_seen_;
+  DeviceArray<long long> local_counts_;
+  DeviceArray<double> rec_send_, rec_all_, local_out_;
+  double *host_rec_ = nullptr;  // pinned
+  std::size_t host_rec_cap_ = 0;
+  bool local_ready_ = false;
   std::vector<double> stage_;
   bool computed_ = false;
   int host_seg_[8] = {0, 0, 0, 0, 0, 0, 0, 0};

@@ -196,13 +196,11 @@ void PairSO3LRB200::fail_collective(const std::string &msg) {
   error->all(FLERR, msg);
 }
 
-void PairSO3LRB200::compute(int eflag, int vflag) {
-  ev_init(eflag, vflag);
-  setup_profile();
+// The opt-in per-atom dump (one rank): the whole system by tag through
+// so3lr_compute, which also returns the per-atom terms the dump schema lists.
+void PairSO3LRB200::compute_with_dump(const char *dump_path) {
   const int nlocal = atom->nlocal;
-  // the whole system on every rank, ordered by atom tag: the library splits it
-  // into its own spatial bricks (one per rank and GPU) and every rank gets the
-  // whole result back
+  // the whole system ordered by atom tag (one rank: the gathers below are copies)
   const int nprocs = comm->nprocs;
   counts_.assign(nprocs, 0);
   displs_.assign(nprocs, 0);
@@ -262,12 +260,7 @@ void PairSO3LRB200::compute(int eflag, int vflag) {
   so3lr_result res{};
   res.f = f_.data();
   res.eatom = eatom_.data();
-  // opt-in per-atom terms for validation against the reference's JAX harness,
-  // in the reference's dump schema (pair_so3lr_native_mpi.cpp:1811-1862)
-  const char *dump_path = std::getenv("SO3LR_NATIVE_DEBUG_DUMP");
-  const bool dump = dump_path != nullptr && dump_path[0] != '\0';
-  if (dump) {
-    if (comm->nprocs != 1) error->all(FLERR, "SO3LR_NATIVE_DEBUG_DUMP requires a single MPI rank");
+  {
     terms_.assign(7 * static_cast<std::size_t>(n), 0.0);
     double *tp = terms_.data();
     res.charges = tp;
@@ -281,7 +274,7 @@ void PairSO3LRB200::compute(int eflag, int vflag) {
   char err[2048] = {0};
   if (so3lr_compute(handle_, &frame, &res, err, sizeof(err)) != 0)
     fail_collective(std::string("SO3LR evaluation failed: ") + err);
-  if (dump) write_debug_dump(dump_path, res, n);
+  write_debug_dump(dump_path, res, n);
   // each rank keeps its own atoms' forces and per-atom terms; the global energy
   // and virial (exact sums, identical on every rank) are reported by rank 0 only,
   // so LAMMPS's sum over ranks counts them once
@@ -308,6 +301,81 @@ void PairSO3LRB200::compute(int eflag, int vflag) {
   if (!reported_ && comm->me == 0) {
     reported_ = true;
     utils::logmesg(lmp, "SO3LR_B200_FORCE_PATH=PASS atoms=" + std::to_string(n) +
+                           " energy=" + std::to_string(res.energy) + "\n");
+  }
+}
+
+
+void PairSO3LRB200::compute(int eflag, int vflag) {
+  ev_init(eflag, vflag);
+  setup_profile();
+  // opt-in per-atom terms for validation against the reference's JAX harness,
+  // in the reference's dump schema (pair_so3lr_native_mpi.cpp:1811-1862)
+  const char *dump_path = std::getenv("SO3LR_NATIVE_DEBUG_DUMP");
+  if (dump_path != nullptr && dump_path[0] != '\0') {
+    if (comm->nprocs != 1) error->all(FLERR, "SO3LR_NATIVE_DEBUG_DUMP requires a single MPI rank");
+    compute_with_dump(dump_path);
+    report_profile();
+    return;
+  }
+  // this rank's own atoms only, identified by their tags, as the reference
+  // hands its evaluator the rank's atoms (pair_so3lr_native_mpi.cpp:1267-1280);
+  // the library's GPUs exchange the ranks' atoms among themselves and return
+  // this rank's forces, per-atom energies and virials
+  const int nlocal = atom->nlocal;
+  if (atom->natoms > (1LL << 30)) error->all(FLERR, "Pair style so3lr/b200: too many atoms");
+  loc_tag64_.resize(nlocal);
+  loc_x_.resize(3 * static_cast<std::size_t>(nlocal));
+  loc_z_.resize(nlocal);
+  for (int i = 0; i < nlocal; ++i) {
+    loc_tag64_[i] = static_cast<long long>(atom->tag[i]);
+    for (int d = 0; d < 3; ++d) loc_x_[3 * i + d] = atom->x[i][d];
+    loc_z_[i] = type_to_z_[static_cast<std::size_t>(atom->type[i])];
+  }
+  f_.resize(3 * static_cast<std::size_t>(nlocal));
+  so3lr_local_frame frame{};
+  frame.natoms = static_cast<long long>(atom->natoms);
+  frame.nlocal = nlocal;
+  frame.tag = loc_tag64_.data();
+  frame.x = loc_x_.data();
+  frame.z = loc_z_.data();
+  frame.periodic = domain->xperiodic ? 1 : 0;
+  for (int d = 0; d < 3; ++d) {
+    frame.boxlo[d] = domain->boxlo[d];
+    frame.boxlen[d] = domain->prd[d];
+  }
+  frame.total_charge = total_charge_;
+  frame.multiplicity = multiplicity_;
+  so3lr_local_result res{};
+  res.f = f_.data();
+  if (eflag_atom) {
+    eatom_.resize(nlocal);
+    res.eatom = eatom_.data();
+  }
+  // per-atom virial (the reference refuses vflag_atom): half of every pair
+  // term to each of its atoms, rows summing to the global virial
+  if (vflag_atom) {
+    va_.resize(6 * static_cast<std::size_t>(nlocal));
+    res.vatom = va_.data();
+  }
+  char err[2048] = {0};
+  if (so3lr_compute_local(handle_, &frame, &res, err, sizeof(err)) != 0)
+    fail_collective(std::string("SO3LR evaluation failed: ") + err);
+  for (int i = 0; i < nlocal; ++i)
+    for (int d = 0; d < 3; ++d) atom->f[i][d] += f_[3 * static_cast<std::size_t>(i) + d];
+  if (eflag_atom)
+    for (int i = 0; i < nlocal; ++i) eatom[i] += eatom_[i];
+  if (vflag_atom)
+    for (int i = 0; i < nlocal; ++i)
+      for (int c = 0; c < 6; ++c) vatom[i][c] += va_[6 * static_cast<std::size_t>(i) + c];
+  // the global energy and virial (exact sums, identical on every rank) are
+  // reported by rank 0 only, so LAMMPS's sum over ranks counts them once
+  if (eflag_global && comm->me == 0) eng_vdwl += res.energy;
+  if (vflag_global && comm->me == 0)
+    for (int k = 0; k < 6; ++k) virial[k] += res.virial[k];
+  if (!reported_ && comm->me == 0) {
+    reported_ = true;
+    utils::logmesg(lmp, "SO3LR_B200_FORCE_PATH=PASS atoms=" + std::to_string(atom->natoms) +
                            " energy=" + std::to_string(res.energy) + "\n");
   }
   report_profile();

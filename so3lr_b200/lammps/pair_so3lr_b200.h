@@ -58,6 +58,7 @@ class PairSO3LRB200 : public Pair {
   std::vector<int> z_;
   std::vector<double> x_, f_, eatom_, va_, loc_x_, all_x_, terms_;
   std::vector<int> loc_tag_, loc_z_, all_tag_, all_z_, counts_, displs_, counts3_, displs3_;
+  std::vector<long long> loc_tag64_;
   std::vector<char> seen_;
   bool comm_ready_ = false;
   so3lr_handle *handle_ = nullptr;
@@ -66,6 +67,7 @@ class PairSO3LRB200 : public Pair {
   void allocate();
   void release();
   void write_debug_dump(const char *path, const so3lr_result &res, int n);
+  void compute_with_dump(const char *dump_path);
   [[noreturn]] void fail_collective(const std::string &msg);
   void setup_profile();
   void report_profile();

@@ -8,6 +8,14 @@
 // broker (src/mpi_turbo_replica_broker.cpp:130-307) ships each image's
 // neighbour graph; here each image ships only its positions and atomic numbers
 // and the GPU builds the neighbour lists of the whole pack.
+//
+// Sharding over GPUs: with $SO3LR_B200_TURBO_GPUS = G (default 1) the K
+// partitions form G groups of consecutive universe ranks (partition k belongs
+// to group k G / K). Each group has its own coordinator (the group's lowest
+// universe rank) with its own GPU handle on device $SO3LR_B200_DEVICE + g, and
+// the gathers, the batch evaluation and the scatters of a step run inside the
+// group only: the groups never communicate during a step. With G = 1 this is
+// the reference's single coordinator.
 #include "pair_so3lr_b200_turbo.h"
 
 #include <mpi.h>
@@ -35,10 +43,19 @@ PairSO3LRB200Turbo::PairSO3LRB200Turbo(LAMMPS *lmp) : Pair(lmp) {
   single_enable = 0;
   MPI_Comm_rank(universe->uworld, &universe_rank_);
   MPI_Comm_size(universe->uworld, &universe_size_);
+  const char *g = std::getenv("SO3LR_B200_TURBO_GPUS");
+  groups_ = g ? std::atoi(g) : 1;
+  if (groups_ < 1) groups_ = 1;
+  if (groups_ > universe_size_) groups_ = universe_size_;
+  group_ = static_cast<int>((static_cast<long long>(universe_rank_) * groups_) / universe_size_);
+  MPI_Comm_split(universe->uworld, group_, universe_rank_, &group_comm_);
+  MPI_Comm_rank(group_comm_, &group_rank_);
+  MPI_Comm_size(group_comm_, &group_size_);
 }
 
 PairSO3LRB200Turbo::~PairSO3LRB200Turbo() {
   release();
+  MPI_Comm_free(&group_comm_);
   if (allocated) {
     memory->destroy(setflag);
     memory->destroy(cutsq);
@@ -69,12 +86,13 @@ void PairSO3LRB200Turbo::settings(int narg, char **arg) {
   total_charge_ = narg > 1 ? std::strtod(arg[1], nullptr) : 0.0;
   multiplicity_ = narg > 2 ? std::strtod(arg[2], nullptr) : 1.0;
   release();
-  // the coordinator (universe rank 0) loads the model onto its GPU
-  // ($SO3LR_B200_DEVICE, default 0) and tells the other images the outcome
+  // every group's coordinator loads the model onto its GPU
+  // ($SO3LR_B200_DEVICE + group, default 0 + group) and tells its group's images
+  // the outcome; all groups then agree, so a failure anywhere stops every image
   char msg[1024] = {0};
   int ok = 1;
   double cut[2] = {0.0, 0.0};
-  if (universe_rank_ == 0) {
+  if (group_rank_ == 0) {
     char err[960] = {0};
     so3lr_arch_info info{};
     if (so3lr_inspect_model(model_path_.c_str(), &info, err, sizeof(err)) != 0) {
@@ -84,17 +102,19 @@ void PairSO3LRB200Turbo::settings(int narg, char **arg) {
       cut[0] = info.sr_cutoff;
       cut[1] = info.lr_cutoff;
       const char *dev = std::getenv("SO3LR_B200_DEVICE");
-      if (so3lr_create(model_path_.c_str(), dev ? std::atoi(dev) : 0, &handle_, err, sizeof(err)) != 0) {
+      if (so3lr_create(model_path_.c_str(), (dev ? std::atoi(dev) : 0) + group_, &handle_, err, sizeof(err)) != 0) {
         ok = 0;
         std::snprintf(msg, sizeof(msg), " on the GPU: %s", err);
       }
     }
   }
-  MPI_Bcast(&ok, 1, MPI_INT, 0, universe->uworld);
-  if (!ok) {
-    MPI_Bcast(msg, sizeof(msg), MPI_BYTE, 0, universe->uworld);
-    error->universe_all(FLERR, std::string("Cannot initialize the coordinator SO3LR model") + msg);
-  }
+  MPI_Bcast(&ok, 1, MPI_INT, 0, group_comm_);
+  MPI_Bcast(msg, sizeof(msg), MPI_BYTE, 0, group_comm_);
+  int all_ok = 0;
+  MPI_Allreduce(&ok, &all_ok, 1, MPI_INT, MPI_MIN, universe->uworld);
+  if (!all_ok)
+    error->universe_all(FLERR, ok ? std::string("Cannot initialize the SO3LR model of another group's coordinator")
+                                  : std::string("Cannot initialize the coordinator SO3LR model") + msg);
   MPI_Bcast(cut, 2, MPI_DOUBLE, 0, universe->uworld);
   sr_cutoff_ = cut[0];
   lr_cutoff_ = cut[1];
@@ -163,12 +183,22 @@ void PairSO3LRB200Turbo::init_style() {
   utils::logmesg(lmp, line);
 }
 
+// A failed step, known to every image of the failing group. With one group
+// that is the whole universe (error->universe_all, as the reference); with
+// several the other groups do not share the step, so the failing group stops
+// the universe itself (error->universe_one) instead of waiting for them.
+void PairSO3LRB200Turbo::fail_step(const std::string &msg) {
+  if (groups_ > 1) error->universe_one(FLERR, msg);
+  error->universe_all(FLERR, msg);
+}
+
 void PairSO3LRB200Turbo::compute(int eflag, int vflag) {
   ev_init(eflag, vflag);
   const double t0 = MPI_Wtime();
-  const MPI_Comm uworld = universe->uworld;
-  const bool coordinator = universe_rank_ == 0;
-  const int nimg = universe_size_;
+  // every exchange of the step stays inside this image's group
+  const MPI_Comm gcomm = group_comm_;
+  const bool coordinator = group_rank_ == 0;
+  const int nimg = group_size_;
   const int n = atom->nlocal;
 
   // this image: atom count, whether it wants per-atom virials, charge and
@@ -179,8 +209,8 @@ void PairSO3LRB200Turbo::compute(int eflag, int vflag) {
     head_i_.resize(2 * static_cast<std::size_t>(nimg));
     head_d_.resize(2 * static_cast<std::size_t>(nimg));
   }
-  MPI_Gather(head, 2, MPI_INT, head_i_.data(), 2, MPI_INT, 0, uworld);
-  MPI_Gather(headd, 2, MPI_DOUBLE, head_d_.data(), 2, MPI_DOUBLE, 0, uworld);
+  MPI_Gather(head, 2, MPI_INT, head_i_.data(), 2, MPI_INT, 0, gcomm);
+  MPI_Gather(headd, 2, MPI_DOUBLE, head_d_.data(), 2, MPI_DOUBLE, 0, gcomm);
   x_.resize(3 * static_cast<std::size_t>(n));
   z_.resize(n);
   for (int i = 0; i < n; ++i) {
@@ -227,13 +257,13 @@ void PairSO3LRB200Turbo::compute(int eflag, int vflag) {
     std::snprintf(err, sizeof(err), "the pack of all images holds %lld atoms; at most %lld are supported", total,
                   (1LL << 26) - 1);
   }
-  MPI_Bcast(status, 2, MPI_INT, 0, uworld);
+  MPI_Bcast(status, 2, MPI_INT, 0, gcomm);
   if (status[0] != 0) {
-    MPI_Bcast(err, sizeof(err), MPI_BYTE, 0, uworld);
-    error->universe_all(FLERR, std::string("SO3LR turbo LAMMPS evaluation failed: ") + err);
+    MPI_Bcast(err, sizeof(err), MPI_BYTE, 0, gcomm);
+    fail_step(std::string("SO3LR turbo LAMMPS evaluation failed: ") + err);
   }
-  MPI_Gatherv(x_.data(), 3 * n, MPI_DOUBLE, all_x_.data(), counts3_.data(), displs3_.data(), MPI_DOUBLE, 0, uworld);
-  MPI_Gatherv(z_.data(), n, MPI_INT, all_z_.data(), counts_.data(), displs_.data(), MPI_INT, 0, uworld);
+  MPI_Gatherv(x_.data(), 3 * n, MPI_DOUBLE, all_x_.data(), counts3_.data(), displs3_.data(), MPI_DOUBLE, 0, gcomm);
+  MPI_Gatherv(z_.data(), n, MPI_INT, all_z_.data(), counts_.data(), displs_.data(), MPI_INT, 0, gcomm);
 
   if (coordinator) {
     const std::size_t nt = static_cast<std::size_t>(total);
@@ -259,22 +289,22 @@ void PairSO3LRB200Turbo::compute(int eflag, int vflag) {
     }
     status[1] = any_va;
   }
-  MPI_Bcast(status, 2, MPI_INT, 0, uworld);
+  MPI_Bcast(status, 2, MPI_INT, 0, gcomm);
   if (status[0] != 0) {
-    MPI_Bcast(err, sizeof(err), MPI_BYTE, 0, uworld);
-    error->universe_all(FLERR, std::string("SO3LR turbo LAMMPS evaluation failed: ") + err);
+    MPI_Bcast(err, sizeof(err), MPI_BYTE, 0, gcomm);
+    fail_step(std::string("SO3LR turbo LAMMPS evaluation failed: ") + err);
   }
   f_.resize(3 * static_cast<std::size_t>(n));
   eatom_.resize(n);
   double image_energy = 0.0;
-  MPI_Scatterv(all_f_.data(), counts3_.data(), displs3_.data(), MPI_DOUBLE, f_.data(), 3 * n, MPI_DOUBLE, 0, uworld);
+  MPI_Scatterv(all_f_.data(), counts3_.data(), displs3_.data(), MPI_DOUBLE, f_.data(), 3 * n, MPI_DOUBLE, 0, gcomm);
   MPI_Scatterv(all_eatom_.data(), counts_.data(), displs_.data(), MPI_DOUBLE, eatom_.data(), n, MPI_DOUBLE, 0,
-               uworld);
-  MPI_Scatter(image_e_.data(), 1, MPI_DOUBLE, &image_energy, 1, MPI_DOUBLE, 0, uworld);
+               gcomm);
+  MPI_Scatter(image_e_.data(), 1, MPI_DOUBLE, &image_energy, 1, MPI_DOUBLE, 0, gcomm);
   if (status[1]) {
     va_.resize(6 * static_cast<std::size_t>(n));
     MPI_Scatterv(all_va_.data(), counts6_.data(), displs6_.data(), MPI_DOUBLE, va_.data(), 6 * n, MPI_DOUBLE, 0,
-                 uworld);
+                 gcomm);
   }
 
   for (int i = 0; i < n; ++i)
@@ -295,9 +325,9 @@ void PairSO3LRB200Turbo::compute(int eflag, int vflag) {
     char line[256];
     std::snprintf(line, sizeof(line),
                   "SO3LR_TURBO_LIVE image=%d universe_rank=%d coordinator=%d images=%d atoms=%d "
-                  "energy=%.10g broker_ms=%.6g\n",
+                  "energy=%.10g broker_ms=%.6g gpu_group=%d of %d\n",
                   universe->iworld, universe_rank_, coordinator ? 1 : 0, nimg, n, image_energy,
-                  (MPI_Wtime() - t0) * 1000.0);
+                  (MPI_Wtime() - t0) * 1000.0, group_, groups_);
     utils::logmesg(lmp, line);
   }
 }

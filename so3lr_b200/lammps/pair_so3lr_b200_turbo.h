@@ -9,10 +9,13 @@
 //
 // Every one-rank LAMMPS partition holds one image (a molecule or cluster with
 // its own charge and multiplicity, read per partition, e.g. from world
-// variables). Each compute gathers the images' atoms over the universe
-// communicator to the coordinator (universe rank 0), which owns the GPU and
-// evaluates all images in one so3lr_compute_batch call, then scatters every
-// image's forces, per-atom energies and energy back. Same syntax, defaults and
+// variables). Each compute gathers the images' atoms to their coordinator,
+// which owns a GPU and evaluates all its images in one so3lr_compute_batch
+// call, then scatters every image's forces, per-atom energies and energy back.
+// By default one coordinator (universe rank 0) serves every partition, as in
+// the reference; with $SO3LR_B200_TURBO_GPUS = G the partitions form G groups of
+// consecutive universe ranks, each with its own coordinator and GPU
+// ($SO3LR_B200_DEVICE + group), and the groups never communicate during a step. Same syntax, defaults and
 // refusals as the reference style, except that per-atom virials are supported
 // (the reference refuses vflag_atom, pair_so3lr_turbo.cpp:238-240).
 #ifdef PAIR_CLASS
@@ -26,6 +29,8 @@ PairStyle(so3lr/b200/turbo,PairSO3LRB200Turbo);
 
 #include <string>
 #include <vector>
+
+#include <mpi.h>
 
 #include "pair.h"
 
@@ -57,6 +62,10 @@ class PairSO3LRB200Turbo : public Pair {
   double sr_cutoff_ = 0.0;
   double lr_cutoff_ = 0.0;
   int universe_rank_ = 0, universe_size_ = 1;
+  // GPU groups ($SO3LR_B200_TURBO_GPUS): this partition's group, its rank in
+  // the group's communicator (0 = the group's coordinator) and the group size
+  int groups_ = 1, group_ = 0, group_rank_ = 0, group_size_ = 1;
+  MPI_Comm group_comm_;
   bool model_ready_ = false;
   std::vector<int> type_to_z_;
   // this image
@@ -72,6 +81,7 @@ class PairSO3LRB200Turbo : public Pair {
 
   void allocate();
   void release();
+  [[noreturn]] void fail_step(const std::string &msg);
 };
 
 }  // namespace LAMMPS_NS

@@ -24,7 +24,7 @@ DEFAULT_MODEL = HERE.parent / "models" / "so3lr.so3lr"
 # every function the header declares (checked by the CPU tests)
 EXPORTED = (
     "so3lr_create", "so3lr_describe", "so3lr_validate_charge_spin", "so3lr_element_from_token",
-    "so3lr_inspect_model", "so3lr_compute", "so3lr_compute_device", "so3lr_compute_batch",
+    "so3lr_inspect_model", "so3lr_compute", "so3lr_compute_local", "so3lr_compute_device", "so3lr_compute_batch",
     "so3lr_md_init", "so3lr_md_run", "so3lr_md_thermostat", "so3lr_md_thermostat_energy", "so3lr_md_state", "so3lr_profile", "so3lr_profile_read",
     "so3lr_launch_count", "so3lr_long_range_noalloc", "so3lr_virial_atom", "so3lr_stream", "so3lr_last_stats",
     "so3lr_destroy",
@@ -53,6 +53,16 @@ class Result(C.Structure):
     _fields_ = [("f", _dp), ("eatom", _dp), ("charges", _dp), ("ratios", _dp), ("e_learned", _dp),
                 ("e_zbl", _dp), ("e_lr", _dp), ("e_elec", _dp), ("e_disp", _dp), ("energy", C.c_double),
                 ("virial", C.c_double * 6)]
+
+
+class LocalFrame(C.Structure):
+    _fields_ = [("natoms", C.c_longlong), ("nlocal", C.c_longlong), ("tag", _lp), ("x", _dp), ("z", _ip),
+                ("periodic", C.c_int), ("boxlo", C.c_double * 3), ("boxlen", C.c_double * 3),
+                ("total_charge", C.c_double), ("multiplicity", C.c_double)]
+
+
+class LocalResult(C.Structure):
+    _fields_ = [("f", _dp), ("eatom", _dp), ("vatom", _dp), ("energy", C.c_double), ("virial", C.c_double * 6)]
 
 
 class Batch(C.Structure):
@@ -86,6 +96,8 @@ def load_library(path: os.PathLike | str | None = None) -> C.CDLL:
     lib.so3lr_validate_charge_spin.argtypes = [_lp, C.c_double, C.c_double, C.c_char_p, C.c_size_t]
     lib.so3lr_element_from_token.argtypes = [C.c_char_p]
     lib.so3lr_compute.argtypes = [C.c_void_p, C.POINTER(Frame), C.POINTER(Result), C.c_char_p, C.c_size_t]
+    lib.so3lr_compute_local.argtypes = [C.c_void_p, C.POINTER(LocalFrame), C.POINTER(LocalResult), C.c_char_p,
+                                        C.c_size_t]
     lib.so3lr_compute_device.argtypes = [C.c_void_p, C.POINTER(Frame), C.c_void_p, C.c_void_p, _dp, _dp,
                                          C.c_char_p, C.c_size_t]
     lib.so3lr_compute_batch.argtypes = [C.c_void_p, C.POINTER(Batch), C.POINTER(BatchResult), C.c_char_p,
@@ -301,6 +313,55 @@ class So3lrB200:
         err = C.create_string_buffer(4096)
         _check(self._lib.so3lr_compute(self._h, C.byref(fr), C.byref(res), err, 4096), err)
         self._natoms = n
+        out["energy"] = res.energy
+        out["virial"] = np.array(res.virial[:])
+        return out
+
+    def compute_local(self, natoms: int, tags, x, z, cell=None, boxlo=None, charge: float = 0.0,
+                      multiplicity: float = 1.0, eatom: bool = True, vatom: bool = False, forces_out=None) -> dict:
+        """This rank's atoms only (global tags 1..natoms); collective on a
+        multi-GPU handle. Returns forces (nlocal x 3), optionally per-atom
+        energies and virials of these atoms, and the whole-system energy and
+        virial."""
+        tags = np.ascontiguousarray(tags, dtype=np.int64)
+        z = np.ascontiguousarray(z, dtype=np.int32)
+        nl = len(tags)
+        if tags.ndim != 1 or z.shape != (nl,):
+            raise ValueError("tags and atomic numbers must be 1-D arrays of the same length")
+        x = _array(x, np.float64, (nl, 3), "positions")
+        fr = LocalFrame()
+        fr.natoms = int(natoms)
+        fr.nlocal = nl
+        fr.tag = _ptr(tags, C.c_longlong)
+        fr.x = _ptr(x)
+        fr.z = _ptr(z, C.c_int)
+        fr.periodic = 1 if cell is not None else 0
+        lo = np.zeros(3) if boxlo is None else _array(boxlo, np.float64, (3,), "boxlo")
+        ln = np.zeros(3) if cell is None else _array(cell, np.float64, (3,), "cell (orthorhombic box lengths)")
+        for d in range(3):
+            fr.boxlo[d] = float(lo[d])
+            fr.boxlen[d] = float(ln[d])
+        fr.total_charge = float(charge)
+        fr.multiplicity = float(multiplicity)
+        if forces_out is not None:
+            if (forces_out.shape != (nl, 3) or forces_out.dtype != np.float64
+                    or not forces_out.flags["C_CONTIGUOUS"]):
+                raise ValueError("forces_out must be a C-contiguous float64 array of shape (nlocal, 3)")
+            out = {"forces": forces_out}
+        else:
+            out = {"forces": np.empty((nl, 3))}
+        if eatom:
+            out["eatom"] = np.empty(nl)
+        if vatom:
+            out["vatom"] = np.empty((nl, 6))
+        res = LocalResult()
+        res.f = _ptr(out["forces"])
+        res.eatom = _ptr(out.get("eatom"))
+        res.vatom = _ptr(out.get("vatom"))
+        err = C.create_string_buffer(4096)
+        self._natoms = None
+        _check(self._lib.so3lr_compute_local(self._h, C.byref(fr), C.byref(res), err, 4096), err)
+        self._natoms = int(natoms)
         out["energy"] = res.energy
         out["virial"] = np.array(res.virial[:])
         return out

@@ -132,6 +132,31 @@ int so3lr_compute(so3lr_handle *h, const so3lr_frame *in, so3lr_result *out, cha
   if (g_profile_on) ++g_profile_calls;
   return 0;
 }
+// so3lr_compute_local (any number of ranks, no communication in the stand-in):
+// local atom i gets f = -x, eatom = 0.5 z, vatom[c] = x[c % 3] + tag / 1000;
+// energy = natoms + 0.5 (a value every rank knows); virial = (1, 2, 3, 4, 5, 6).
+// Tags must be unique within the rank and in 1..natoms.
+int so3lr_compute_local(so3lr_handle *h, const so3lr_local_frame *in, so3lr_local_result *out, char *err,
+                        size_t errlen) {
+  if (!h || !in || !out || (in->nlocal > 0 && !out->f)) return fake_fail("so3lr_compute_local: NULL argument", err, errlen);
+  const char *fail_rank = std::getenv("FAKE_SO3LR_FAIL_RANK");  // a failure injected on one rank
+  if (fail_rank && std::atoi(fail_rank) == h->rank) return fake_fail("injected failure", err, errlen);
+  std::vector<char> seen(static_cast<std::size_t>(in->natoms), 0);
+  for (long long i = 0; i < in->nlocal; ++i) {
+    const long long t = in->tag[i];
+    if (t < 1 || t > in->natoms || seen[t - 1])
+      return fake_fail("SO3LR local frame: atom tags must be unique over the ranks and in 1..natoms", err, errlen);
+    seen[t - 1] = 1;
+    for (int d = 0; d < 3; ++d) out->f[3 * i + d] = -in->x[3 * i + d];
+    if (out->eatom) out->eatom[i] = 0.5 * in->z[i];
+    if (out->vatom)
+      for (int c = 0; c < 6; ++c) out->vatom[6 * i + c] = in->x[3 * i + c % 3] + 0.001 * t;
+  }
+  out->energy = double(in->natoms) + 0.5;
+  for (int c = 0; c < 6; ++c) out->virial[c] = c + 1.0;
+  if (g_profile_on) ++g_profile_calls;
+  return 0;
+}
 // several ranks: no communication in the stand-in, every rank evaluates the
 // whole system it is given (as every rank of the real library returns it)
 int so3lr_nccl_unique_id(char *out, char *, size_t) {

@@ -160,6 +160,71 @@ def test_multi_gpu_bit_identical(world, gpu_model):
         assert np.array_equal(va, ref_va)
 
 
+def _local_worker(rank, world, uid, nmol, seed, steps, result_q):
+    """Rank `rank` passes only its share of the atoms (a random split, not the
+    library's bricks) to so3lr_compute_local, for `steps` positions."""
+    try:
+        from so3lr_b200 import So3lrB200
+        from so3lr_b200.systems import water_box
+        m = So3lrB200(MODEL, rank)
+        m.comm_init(world, rank, uid)
+        w = water_box(nmol, seed=seed)
+        n = len(w.z)
+        mine = np.nonzero(np.random.default_rng(seed).integers(0, world, n) == rank)[0]
+        out = []
+        for k in range(steps):
+            pos = w.pos + 0.01 * k * np.sin(np.arange(3 * n).reshape(n, 3))
+            r = m.compute_local(n, mine + 1, pos[mine], w.z[mine], cell=w.cell, boxlo=w.boxlo, vatom=True)
+            out.append((r["energy"], r["virial"], r["forces"], r["eatom"], r["vatom"]))
+        result_q.put((rank, mine, out, None))
+        m.close()
+    except Exception as exc:  # report to the parent instead of hanging it
+        result_q.put((rank, None, None, repr(exc)))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_multi_gpu_local_frames_bit_identical(world, gpu_model):
+    """Every rank passes only its own atoms (as a LAMMPS rank does) through
+    so3lr_compute_local: each gets its atoms' forces, energies and per-atom
+    virials, bit-identical to the single-GPU evaluation of the whole system,
+    on a first call and on two later positions."""
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from so3lr_b200 import So3lrB200
+    from so3lr_b200.systems import water_box
+    nmol, seed, steps = 1000, 29, 3
+    w = water_box(nmol, seed=seed)
+    n = len(w.z)
+    refs = []
+    for k in range(steps):
+        pos = w.pos + 0.01 * k * np.sin(np.arange(3 * n).reshape(n, 3))
+        r = gpu_model.compute(pos, w.z, cell=w.cell, boxlo=w.boxlo)
+        refs.append((r, gpu_model.virial_atom(n)))
+    uid = So3lrB200.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_local_worker, args=(r, world, uid, nmol, seed, steps, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+    seen = np.zeros(n, dtype=int)
+    for rank, mine, out, err in res:
+        assert err is None, err
+        seen[mine] += 1
+        for k, (e, vir, f, ea, va) in enumerate(out):
+            ref, ref_va = refs[k]
+            assert e == ref["energy"], (rank, k)
+            assert np.array_equal(vir, ref["virial"]), (rank, k)
+            assert np.array_equal(f, ref["forces"][mine]), (rank, k)
+            assert np.array_equal(ea, ref["eatom"][mine]), (rank, k)
+            assert np.array_equal(va, ref_va[mine]), (rank, k)
+    assert (seen == 1).all()
+
+
 @pytest.mark.gpu
 def test_multi_gpu_bit_identical_with_optional_operators(tmp_path):
     """A model with RMSNorm, query/key normalisation (also on the halo rows each

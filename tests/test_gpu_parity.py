@@ -372,3 +372,40 @@ def test_gpu_edge_cases_without_short_range_pairs(case, gpu_model, oracle_model)
     assert abs(g["energy"] - o["energy"]) / len(s.z) <= 1e-9
     assert np.abs(g["forces"] - o["forces"]).max() <= 1e-9
     assert np.abs(g["e_lr"] - o["lr_energy"]).max() <= 1e-10
+
+
+def test_gpu_local_frame_matches_compute(gpu_model):
+    """so3lr_compute_local with the atoms in a shuffled tag order equals
+    so3lr_compute bit for bit (forces, per-atom energies and virials, energy,
+    virial): on the first call (prepared from the records), on a step that only
+    moves atoms (positions scattered by tag on the device), and after two atoms
+    swap atomic numbers (prepared again)."""
+    from so3lr_b200 import So3lrError
+    from so3lr_b200.systems import water_box
+    w = water_box(216, seed=41)
+    n = len(w.z)
+    rng = np.random.default_rng(5)
+    order = rng.permutation(n)          # local atom i is atom order[i]
+    tags = order + 1
+    pos = w.pos.copy()
+    z = w.z.copy()
+    for step in range(3):
+        if step == 1:
+            pos = pos + rng.normal(scale=0.02, size=pos.shape)
+        if step == 2:
+            o, h = int(np.nonzero(z == 8)[0][0]), int(np.nonzero(z == 1)[0][5])
+            z[o], z[h] = z[h], z[o]
+        ref = gpu_model.compute(pos, z, cell=w.cell, boxlo=w.boxlo)
+        ref_va = gpu_model.virial_atom(n)
+        got = gpu_model.compute_local(n, tags, pos[order], z[order], cell=w.cell, boxlo=w.boxlo, vatom=True)
+        assert got["energy"] == ref["energy"], step
+        assert np.array_equal(got["virial"], ref["virial"]), step
+        assert np.array_equal(got["forces"], ref["forces"][order]), step
+        assert np.array_equal(got["eatom"], ref["eatom"][order]), step
+        assert np.array_equal(got["vatom"], ref_va[order]), step
+    bad = tags.copy()
+    bad[1] = bad[0]
+    with pytest.raises(So3lrError, match="unique"):
+        gpu_model.compute_local(n, bad, pos[order], z[order], cell=w.cell, boxlo=w.boxlo)
+    with pytest.raises(So3lrError, match="atoms in all"):
+        gpu_model.compute_local(n + 3, tags, pos[order], z[order], cell=w.cell, boxlo=w.boxlo)

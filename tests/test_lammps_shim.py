@@ -157,9 +157,10 @@ def _water_input(tmp_path, nmol=8, seed=5):
 
 def test_multirank_routing_with_the_cpu_stand_in(tmp_path, monkeypatch):
     """so3lr/b200 on three ranks (threads) with atoms dealt out of order: every
-    rank gets back exactly its own atoms' forces and per-atom energies (the
-    stand-in returns f = -x and eatom = z / 2 by tag), and only rank 0 reports
-    the global energy."""
+    rank passes only its own atoms (so3lr_compute_local) and gets back exactly
+    their forces and per-atom energies (the stand-in returns f = -x and
+    eatom = z / 2 per atom), and only rank 0 reports the global energy (the
+    stand-in's natoms + 0.5)."""
     exe = _build(tmp_path, fake=True)
     monkeypatch.delenv("FAKE_SO3LR_FAIL_RANK", raising=False)
     w, inp = _water_input(tmp_path)
@@ -171,7 +172,7 @@ def test_multirank_routing_with_the_cpu_stand_in(tmp_path, monkeypatch):
         seen += list(rows)
         assert np.array_equal(np.array(o["forces"]), -w.pos[rows])
         assert np.array_equal(np.array(o["eatom"]), 0.5 * w.z[rows])
-        assert o["energy"] == (0.5 * w.z.sum() if o["rank"] == 0 else 0.0)
+        assert o["energy"] == (len(w.z) + 0.5 if o["rank"] == 0 else 0.0)
     assert sorted(seen) == list(range(len(w.z)))
 
 
@@ -192,7 +193,7 @@ def test_duplicate_atom_tags_are_refused(tmp_path):
     _, inp = _water_input(tmp_path, nmol=2)
     res = subprocess.run([str(exe), "run-duplicate-tag", "fake", str(inp)], capture_output=True, text=True,
                          timeout=120)
-    assert res.returncode != 0 and "unique atom tags" in res.stderr, res.stdout + res.stderr
+    assert res.returncode != 0 and "atom tags must be unique" in res.stdout + res.stderr, res.stdout + res.stderr
 
 
 def test_model_failure_on_one_rank_stops_every_rank(tmp_path):
@@ -238,6 +239,33 @@ def test_turbo_routes_each_image_back_to_its_partition(tmp_path):
         assert o["repeat_equal"] and o["evaluations"] == 2
         assert f"SO3LR_TURBO_LIVE image={k} universe_rank={k} coordinator={int(k == 0)} images=4" in o["log"]
         assert f"SO3LR turbo image {k}: total charge {q[k]:g}" in o["log"]
+
+
+def test_turbo_gpu_groups_keep_each_image_in_its_group(tmp_path, monkeypatch):
+    """SO3LR_B200_TURBO_GPUS=2 over four partitions: two groups of two
+    consecutive partitions, each with its own coordinator (universe ranks 0 and
+    2) and its own pack. The stand-in encodes an image's index inside the pack
+    it was evaluated in, so each partition's results show that its image went
+    to its own group's pack, at index k mod 2, and came back to it."""
+    from so3lr_b200.systems import turbo_batch
+    monkeypatch.setenv("SO3LR_B200_TURBO_GPUS", "2")
+    exe = _build(tmp_path, fake=True)
+    pos, z, off, q, m = turbo_batch(4, seed=7)
+    inp = tmp_path / "images.txt"
+    _write_images(inp, pos, z, off, q, m)
+    out = _run_images(exe, "fake", inp, 4)
+    for k, o in enumerate(out):
+        j = k % 2  # index of the image in its group's pack
+        sl = slice(off[k], off[k + 1])
+        x = pos[sl]
+        f = np.array(o["forces"])
+        assert o["image"] == k
+        assert np.array_equal(f, (j + 1) * x)
+        assert o["energy"] == float((z[sl] + 1000 * j).sum())
+        assert np.array_equal(np.array(o["vatom"]), x[:, [0, 1, 2, 0, 1, 2]] + j)
+        assert o["repeat_equal"] and o["evaluations"] == 2
+        assert (f"SO3LR_TURBO_LIVE image={k} universe_rank={k} coordinator={int(j == 0)} images=2" in o["log"]
+                and f"gpu_group={k // 2} of 2" in o["log"]), o["log"]
 
 
 def test_turbo_refusal_on_one_partition_stops_all(tmp_path):
@@ -338,3 +366,35 @@ def test_turbo_pair_style_matches_c_abi(tmp_path, gpu_model):
     res = subprocess.run([str(exe), "turbo-refuse", str(MODEL), str(inp)], capture_output=True, text=True,
                          timeout=600)
     assert "TURBO REFUSE OK" in res.stdout, res.stdout + res.stderr
+
+
+@pytest.mark.gpu
+def test_turbo_pair_style_on_two_gpus_matches_c_abi(tmp_path, gpu_model, monkeypatch):
+    """so3lr/b200/turbo with SO3LR_B200_TURBO_GPUS=2 over six partitions: two
+    coordinators, each with its own GPU (devices 0 and 1) and its own pack of
+    three images, no communication between them; every image's forces, energy
+    and per-atom virials equal so3lr_compute_batch of its group's pack bit for
+    bit."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from so3lr_b200.systems import turbo_batch
+    monkeypatch.setenv("SO3LR_B200_TURBO_GPUS", "2")
+    exe = _build(tmp_path)
+    pos, z, off, q, m = turbo_batch(6, seed=13)
+    inp = tmp_path / "images.txt"
+    _write_images(inp, pos, z, off, q, m)
+    out = _run_images(exe, MODEL, inp, 6)
+    for g in range(2):
+        ks = list(range(3 * g, 3 * g + 3))
+        a, b = off[ks[0]], off[ks[-1] + 1]
+        sub_off = off[ks[0]:ks[-1] + 2] - a
+        ref = gpu_model.compute_batch(pos[a:b], z[a:b], sub_off, q[ks], m[ks])
+        ref_va = gpu_model.virial_atom(b - a)
+        for j, k in enumerate(ks):
+            o = out[k]
+            sl = slice(sub_off[j], sub_off[j + 1])
+            assert np.array_equal(np.array(o["forces"]), ref["forces"][sl]), k
+            assert o["energy"] == ref["image_energy"][j], k
+            assert np.array_equal(np.array(o["vatom"]), ref_va[sl]), k
+            assert f"gpu_group={g} of 2" in o["log"]
