@@ -183,6 +183,33 @@ def measure_fp64_peak(device: int) -> float:
     return best
 
 
+def measure_tf32_peak(device: int) -> float:
+    """Dense TF32 tensor-core throughput of cuBLAS (torch.matmul float32 with
+    TF32 allowed, 8192^3), TFLOP/s, best of 5."""
+    import torch
+    n = 8192
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        a = torch.randn(n, n, dtype=torch.float32, device=f"cuda:{device}")
+        b = torch.randn(n, n, dtype=torch.float32, device=f"cuda:{device}")
+        torch.matmul(a, b)
+        torch.cuda.synchronize()
+        best = 0.0
+        for _ in range(5):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            torch.matmul(a, b)
+            e.record()
+            torch.cuda.synchronize()
+            best = max(best, 2.0 * n ** 3 / (s.elapsed_time(e) * 1e-3) / 1e12)
+        del a, b
+        torch.cuda.empty_cache()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    return best
+
+
 def cpu_model() -> str:
     """The host CPU's model name (lscpu / /proc/cpuinfo), for the baseline record."""
     try:
@@ -317,12 +344,17 @@ def run_ours(args) -> None:
         return float(t.item())
 
     nmol, cfg = workload(args.config, world)
+    mixed = args.precision == "mixed"
+    if mixed:
+        cfg["workload"] += " (mixed float32: pair-filter GEMMs as three-pass TF32 with float32 accumulation)"
     w = water_box(nmol, seed=2026)
     n = len(w.z)
     v0 = maxwell_boltzmann(w.mass, 300.0, seed=11)
-    peak = measure_fp64_peak(local)
+    peak = measure_tf32_peak(local) / 3.0 if mixed else measure_fp64_peak(local)
 
     model = So3lrB200(ROOT / "models" / "so3lr.so3lr", local)
+    if mixed:
+        model.set_precision("mixed")
     if world > 1:
         uid = [So3lrB200.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
@@ -431,7 +463,7 @@ def run_ours(args) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": "weak",
             "vs_baseline": (value / A100_24K_ATOM_STEPS) if (world == 1 and args.config == 3) else None,
-            "dtype": "f64", "data": "synthetic",
+            "dtype": "tf32x3+f64" if mixed else "f64", "data": "synthetic",
             "config": cfg,
             "stats": {"atoms_owned_rank0": owned, "sr_edges_rank0": stats["sr_edges"],
                       "sr_pairs_rank0": stats["sr_pairs"], "ns_per_day": steps_per_s * 0.0432,
@@ -445,8 +477,11 @@ def run_ours(args) -> None:
                     "call": "so3lr_compute" if world == 1 else "so3lr_compute_local (each rank its brick's atoms)"},
             "roofline": {"bound": "tensor", "kernel": dom_name, "achieved": achieved, "peak": peak,
                          "unit": "TFLOP/s", "frac": achieved / peak if peak else None, "traffic": traffic,
-                         "peak_source": "FP64 cuBLAS DGEMM 8192^3 (torch.matmul float64) measured on this GPU "
-                                        "before the timed region; MEASURED_PEAKS.json has no FP64 entry",
+                         "peak_source": ("a third of the cuBLAS TF32 GEMM throughput (torch.matmul float32 "
+                                         "8192^3, TF32 allowed) measured on this GPU before the timed region: "
+                                         "three TF32 passes per product" if mixed else
+                                         "FP64 cuBLAS DGEMM 8192^3 (torch.matmul float64) measured on this GPU "
+                                         "before the timed region; MEASURED_PEAKS.json has no FP64 entry"),
                          "launches": dom["launches"], "ms_per_launch": dom["ms"] / max(1, dom["launches"]),
                          "other": {("filter_reverse" if dom is prof[0] else "filter_forward"):
                                    {"ms": (prof[1] if dom is prof[0] else prof[0])["ms"],
@@ -456,8 +491,8 @@ def run_ours(args) -> None:
                                    "filter_share_of_step": (prof[0]["ms"] + prof[1]["ms"]) / ms}},
             # edge and pair counts are this rank's (its own rows and their halo
             # pairs); the work of the other ranks' equal bricks is taken as the same
-            "step_roofline": step_roofline(n / world, stats["sr_edges"], stats["sr_pairs"], lr_pairs / world,
-                                           steps_per_s, peak, world),
+            "step_roofline": None if mixed else step_roofline(n / world, stats["sr_edges"], stats["sr_pairs"],
+                                                              lr_pairs / world, steps_per_s, peak, world),
             "cpu_baseline": cpu,
             "clocks": clock_info,
             "gpu_launches": launches,
@@ -656,6 +691,8 @@ def main():
     ap.add_argument("--config", type=int, choices=[1, 2, 3, 5], default=3,
                     help="3 (default): the headline 24,000-atom box; 5: the turbo cluster pack")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--precision", choices=["float64", "mixed"], default="float64",
+                    help="mixed: pair-filter GEMMs as three-pass TF32 (the mixed float32 run of config 2)")
     ap.add_argument("--no-identity", action="store_true",
                     help="skip the single-point evaluation of the 192,000-atom box (energy and force hash)")
     args = ap.parse_args()

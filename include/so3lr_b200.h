@@ -258,6 +258,23 @@ int so3lr_profile(so3lr_handle *h, int enable);
 int so3lr_profile_read(so3lr_handle *h, int kernel, double *total_ms, long long *launches, double *flops, char *err,
                        size_t errlen);
 
+/* Arithmetic of the pair-filter MLPs, the dominant tensor work of every
+ * evaluation. SO3LR_PRECISION_FLOAT64 (the default) is the reference's float64
+ * arithmetic (src/kokkos_integrated_block0.cpp:194-255 forward,
+ * src/kokkos_block2_attention_input_reverse.cpp:186-336 reverse).
+ * SO3LR_PRECISION_MIXED runs their GEMMs on the TF32 tensor cores in three
+ * passes (each operand split into two TF32 parts) with float32 accumulation and
+ * the hidden-layer SiLU in float32; everything else stays float64 (geometry,
+ * attention, node layers, heads, long range, the exact global sums). Stated
+ * tolerance against float64: force MAE <= 1e-4 eV/A (measured ~1e-7 on water).
+ * The reference has no reduced-precision runtime (float32 is only a storage type
+ * of its model file, src/native_model.cpp:266); this mode serves the mixed
+ * float32 run of the benchmark configurations. Takes effect from the next
+ * evaluation; returns nonzero for an unknown value. */
+#define SO3LR_PRECISION_FLOAT64 0
+#define SO3LR_PRECISION_MIXED 1
+int so3lr_set_precision(so3lr_handle *h, int precision, char *err, size_t errlen);
+
 /* Total number of CUDA kernels this library has launched in the process. */
 long long so3lr_launch_count(void);
 

@@ -364,6 +364,16 @@ int so3lr_profile_read(so3lr_handle *h, int kernel, double *total_ms, long long 
   }
 }
 
+int so3lr_set_precision(so3lr_handle *h, int precision, char *err, size_t errlen) {
+  if (!h) return report_msg("so3lr_set_precision: NULL handle", err, errlen);
+  if (precision != SO3LR_PRECISION_FLOAT64 && precision != SO3LR_PRECISION_MIXED)
+    return report_msg("so3lr_set_precision: precision must be SO3LR_PRECISION_FLOAT64 (0) or "
+                      "SO3LR_PRECISION_MIXED (1)",
+                      err, errlen);
+  h->eval->set_mixed_precision(precision == SO3LR_PRECISION_MIXED);
+  return 0;
+}
+
 long long so3lr_launch_count(void) { return so3lr_b200::launch_counter().load(); }
 
 int so3lr_long_range_noalloc(so3lr_handle *h, long long natoms, const double *x, const double *q,

@@ -169,8 +169,20 @@ struct FilterW {
   const double *v1_f;     // K=128, N=32:  B(o, h) = v1[o][h]   reverse through ev layer 1
   const double *w0_f;     // K=128, N=32:  B(j, r) = w0[j][r]   reverse through layer 0
 };
+// The filter matrices for the mixed-precision kernels (filter_mixed.cu): every
+// fragment-major operand of FilterW split into two TF32 parts, x = hi + lo up to
+// 2^-22 |x| (hi = x rounded to TF32, lo = the rest rounded to TF32), in float;
+// biases and the ev branch's first layer in float. Same fragment-major order as
+// FilterW, with floats in place of doubles.
+struct FilterW32 {
+  const float *b0, *bc1;           // [128]
+  const float *v0, *c0;            // [32][4], [32]
+  const float *w0t_h, *w0t_l, *w1t_h, *w1t_l, *v1t_h, *v1t_l;  // forward operands
+  const float *w1_h, *w1_l, *v1_h, *v1_l, *w0_h, *w0_l;        // reverse operands
+};
 struct BlockW {
   FilterW finv, fev;
+  FilterW32 finv32, fev32;
   const double *cg_att, *cg_int;   // [24]
   const double *qkv_fwd;           // [4 heads][160 out (proj,o)][32 in]   (B col layout)
   const double *qkv_rev;           // [4 heads][32 out i][160 in (proj,o)] (B col layout)

@@ -61,6 +61,16 @@ static std::vector<double> fragment_major(int K, int N, const std::function<doub
   return out;
 }
 
+// x rounded to TF32 (10 explicit mantissa bits), to nearest with ties away from
+// zero, as cvt.rna.tf32.f32 rounds on the device
+static float tf32_round(float x) {
+  std::uint32_t u;
+  std::memcpy(&u, &x, sizeof(u));
+  if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
+  std::memcpy(&x, &u, sizeof(u));
+  return x;
+}
+
 void Evaluator::upload_weights() {
   const Architecture &a = model_.arch();
   layers_ = a.layers;
@@ -78,11 +88,37 @@ void Evaluator::upload_weights() {
   };
   const std::size_t F = kF, R = kR, H = kEH;
   struct FOff { std::size_t w0, b0, w1, b1, v0, c0, v1, c1, bc1, w0t_f, w1t_f, v1t_f, w1_f, v1_f, w0_f; };
+  // float copies for the mixed-precision filter kernels (FilterW32)
+  std::vector<float> host32;
+  auto push32 = [&](const std::vector<double> &v) {
+    while (host32.size() % 16) host32.push_back(0.0f);  // 64-byte alignment
+    const std::size_t off = host32.size();
+    for (double x : v) host32.push_back(float(x));
+    return off;
+  };
+  // a fragment-major operand as its TF32 high and low parts
+  auto push_split = [&](const std::vector<double> &v) {
+    std::vector<double> hi(v.size()), lo(v.size());
+    for (std::size_t i = 0; i < v.size(); ++i) {
+      const float h = tf32_round(float(v[i]));
+      hi[i] = h;
+      lo[i] = tf32_round(float(v[i] - double(h)));
+    }
+    const std::size_t a = push32(hi);
+    const std::size_t b = push32(lo);
+    return std::make_pair(a, b);
+  };
+  struct FOff32 {
+    std::size_t b0, bc1, v0, c0;
+    std::pair<std::size_t, std::size_t> w0t, w1t, v1t, w1, v1, w0;
+  };
   struct BOff {
     FOff finv, fev;
     std::size_t cg_att, cg_int, qf, qr, ln1w, ln1b, ln2w, ln2b, m1w, m1b, m2w, m2b, iw, ib;
   };
   std::vector<BOff> boff(layers_);
+  std::vector<FOff32> foff32(2 * std::size_t(layers_));
+  std::size_t filt_count = 0;  // filters in upload order: block 0 inv, ev, block 1 inv, ...
   auto filt = [&](const std::string &prefix) {
     FOff o;
     const auto w0 = model_.f64(prefix + ".mlp_rbf.0.weight", {F, R});                  // [j][r]
@@ -108,6 +144,17 @@ void Evaluator::upload_weights() {
     o.w1_f = push(fragment_major(iF, iF, [&](int oo, int j) { return w1[std::size_t(oo) * F + j]; }));
     o.v1_f = push(fragment_major(iF, iH, [&](int oo, int h) { return v1[std::size_t(oo) * H + h]; }));
     o.w0_f = push(fragment_major(iF, iR, [&](int j, int r) { return w0[std::size_t(j) * R + r]; }));
+    FOff32 &o32 = foff32[filt_count++];
+    o32.b0 = push32(model_.f64(prefix + ".mlp_rbf.0.bias", {F}));
+    o32.bc1 = push32(bc1);
+    o32.v0 = push32(model_.f64(prefix + ".mlp_ev.0.weight", {H, 4}));
+    o32.c0 = push32(model_.f64(prefix + ".mlp_ev.0.bias", {H}));
+    o32.w0t = push_split(fragment_major(iR, iF, [&](int r, int j) { return w0[std::size_t(j) * R + r]; }));
+    o32.w1t = push_split(fragment_major(iF, iF, [&](int j, int oo) { return w1[std::size_t(oo) * F + j]; }));
+    o32.v1t = push_split(fragment_major(iH, iF, [&](int h, int oo) { return v1[std::size_t(oo) * H + h]; }));
+    o32.w1 = push_split(fragment_major(iF, iF, [&](int oo, int j) { return w1[std::size_t(oo) * F + j]; }));
+    o32.v1 = push_split(fragment_major(iF, iH, [&](int oo, int h) { return v1[std::size_t(oo) * H + h]; }));
+    o32.w0 = push_split(fragment_major(iF, iR, [&](int j, int r) { return w0[std::size_t(j) * R + r]; }));
     return o;
   };
   for (int b = 0; b < layers_; ++b) {
@@ -246,6 +293,15 @@ void Evaluator::upload_weights() {
   double *d = wbuf_.reserve(host.size());
   SO3_CUDA(cudaMemcpy(d, host.data(), host.size() * sizeof(double), cudaMemcpyHostToDevice));
   auto P = [&](std::size_t off) { return off == kNoParam ? nullptr : static_cast<const double *>(d + off); };
+  float *d32 = wbuf32_.reserve(host32.size());
+  SO3_CUDA(cudaMemcpy(d32, host32.data(), host32.size() * sizeof(float), cudaMemcpyHostToDevice));
+  auto P32 = [&](std::size_t off) { return static_cast<const float *>(d32 + off); };
+  auto fw32 = [&](const FOff32 &f) {
+    return FilterW32{P32(f.b0),         P32(f.bc1),         P32(f.v0),          P32(f.c0),
+                     P32(f.w0t.first),  P32(f.w0t.second),  P32(f.w1t.first),   P32(f.w1t.second),
+                     P32(f.v1t.first),  P32(f.v1t.second),  P32(f.w1.first),    P32(f.w1.second),
+                     P32(f.v1.first),   P32(f.v1.second),   P32(f.w0.first),    P32(f.w0.second)};
+  };
   blocks_.resize(layers_);
   for (int b = 0; b < layers_; ++b) {
     const BOff &o = boff[b];
@@ -256,6 +312,8 @@ void Evaluator::upload_weights() {
     };
     w.finv = fw(o.finv);
     w.fev = fw(o.fev);
+    w.finv32 = fw32(foff32[2 * std::size_t(b)]);
+    w.fev32 = fw32(foff32[2 * std::size_t(b) + 1]);
     w.cg_att = P(o.cg_att);
     w.cg_int = P(o.cg_int);
     w.qkv_fwd = P(o.qf);
@@ -843,9 +901,14 @@ void Evaluator::compute() {
   for (int b = 0; b < layers_; ++b) {
     const BlockW &w = blocks_[b];
     prof_begin(kProfFilterForward);
-    launch_filter_forward(P, geo_.get(), nb_.pair_a, nb_.pair_b, b == 0 ? nullptr : evb_[b]->get(), w.cg_att, w.finv,
-                          w.fev, rad_, f_inv_[b]->get(), f_ev_[b]->get(), sp_[b]->get(),
-                          b == 0 ? drbf_.get() : nullptr, s);
+    if (mixed_)
+      launch_filter_forward_mixed(P, geo_.get(), nb_.pair_a, nb_.pair_b, b == 0 ? nullptr : evb_[b]->get(), w.cg_att,
+                                  w.finv32, w.fev32, rad_, f_inv_[b]->get(), f_ev_[b]->get(),
+                                  reinterpret_cast<float *>(sp_[b]->get()), b == 0 ? drbf_.get() : nullptr, s);
+    else
+      launch_filter_forward(P, geo_.get(), nb_.pair_a, nb_.pair_b, b == 0 ? nullptr : evb_[b]->get(), w.cg_att,
+                            w.finv, w.fev, rad_, f_inv_[b]->get(), f_ev_[b]->get(), sp_[b]->get(),
+                            b == 0 ? drbf_.get() : nullptr, s);
     prof_end(kProfFilterForward, kFilterFlopsPerPair * double(P));
     {  // per-head projections qkv[row][h][5][32] = x[row][h*32:(h+1)*32] W_h of every
        // row the attention reads: the owned rows and (decomposed) their halo
@@ -1019,9 +1082,16 @@ void Evaluator::compute() {
                              g_a_.get(), g_A_.get(), norm_, b > 0 ? g_qkv_.get() : nullptr, pair_sc_.get(),
                              g_filt_inv_.get(), g_filt_ev_.get(), s);
     prof_begin(kProfFilterReverse);
-    launch_filter_reverse(P, geo_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr, w.cg_att, w.finv,
-                          w.fev, rad_, g_filt_inv_.get(), g_filt_ev_.get(), sp_[b]->get(), drbf_.get(), g_A_.get(),
-                          pair_sc_.get(), b > 0, b < layers_ - 1, g_r_.get(), g_y_.get(), gl0_.get(), s);
+    if (mixed_)
+      launch_filter_reverse_mixed(P, geo_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr, w.cg_att,
+                                  w.finv, w.fev, w.finv32, w.fev32, g_filt_inv_.get(), g_filt_ev_.get(),
+                                  reinterpret_cast<const float *>(sp_[b]->get()), drbf_.get(), g_A_.get(),
+                                  pair_sc_.get(), b > 0, b < layers_ - 1, g_r_.get(), g_y_.get(), gl0_.get(), s);
+    else
+      launch_filter_reverse(P, geo_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr, w.cg_att,
+                            w.finv, w.fev, rad_, g_filt_inv_.get(), g_filt_ev_.get(), sp_[b]->get(), drbf_.get(),
+                            g_A_.get(), pair_sc_.get(), b > 0, b < layers_ - 1, g_r_.get(), g_y_.get(),
+                            gl0_.get(), s);
     prof_end(kProfFilterReverse, kFilterFlopsPerPair * double(P));
     if (b > 0) {
       if (qk_norm_)  // gradient w.r.t. the projections before their normalisation

@@ -147,6 +147,11 @@ class Evaluator {
     kProfKinds = 8
   };
   void set_profiling(bool on) { profiling_ = on; }
+  // Arithmetic of the pair-filter MLPs: float64 (default) or mixed (three-pass
+  // TF32 tensor-core GEMMs with float32 accumulation, filter_mixed.cu); every
+  // other step stays float64. Takes effect from the next evaluation.
+  void set_mixed_precision(bool on) { mixed_ = on; }
+  bool mixed_precision() const { return mixed_; }
   void read_profile(int kernel, double *ms, long long *launches, double *flops);
 
   // velocity-Verlet MD on the device (LAMMPS metal units); masses in g/mol
@@ -168,6 +173,7 @@ class Evaluator {
 
   // weights
   DeviceArray<double> wbuf_;
+  DeviceArray<float> wbuf32_;  // TF32-split filter operands (mixed precision)
   std::vector<BlockW> blocks_;
   HeadsW heads_{};
   RadialW rad_{};
@@ -255,6 +261,7 @@ class Evaluator {
     double flops = 0;
   };
   bool profiling_ = false;
+  bool mixed_ = false;
   KernelProfile prof_[kProfKinds];
   void prof_begin(int k);
   void prof_end(int k, double flops);

@@ -22,56 +22,12 @@
 // ones use 16x16 warp blocks.
 #include <cooperative_groups.h>
 
+#include "filter_common.cuh"
 #include "kernels.cuh"
 #include "sh.cuh"
 
 namespace so3lr_b200 {
 namespace {
-
-constexpr int TP = 64;     // pairs per tile
-// Row strides of the shared-memory tiles. A quarter-warp's 16-byte fragment
-// access covers 64 bytes of two rows; a stride of 8 (mod 16) doubles puts the
-// second row in the other half of the 32 banks.
-constexpr int LDU = 136;   // 128-wide tiles
-constexpr int LDR = 40;    // 32-wide tiles
-
-// silu'(hidden pre-activation) of the rbf branch, written by the forward and
-// read by the reverse in accumulator order:
-// [tile][filter][block][mi][ni][half][lane][2] with 32 x 32 blocks (block =
-// 4 (row / 32) + col / 32; 512 contiguous bytes per block and (mi, ni, half)).
-// A 64x16 warp slab's m16n8 block (mi, ni) is one such 512-byte run.
-__device__ __forceinline__ size_t sp_offset(int tile, int filt, int warp) {
-  return (((size_t)tile * 2 + filt) * 8 + warp) * (16 * 64);
-}
-
-__device__ inline void compute_rbf(const double *rr, double *rbf, const RadialW &rad) {
-  const int pl = threadIdx.x >> 2;
-  const int k0 = (threadIdx.x & 3) * 8;
-  const double r = rr[pl];
-  double x = exp(-rad.gamma * r);
-  if (x < 1.0e-6) x = 1.0e-6;
-  if (x > 1.0 - 1.0e-6) x = 1.0 - 1.0e-6;
-  const double lx = log(x), l1x = log(1.0 - x);
-#pragma unroll
-  for (int k = k0; k < k0 + 8; ++k) rbf[pl * LDR + k] = exp_tang(rad.b[k] + rad.k[k] * lx + rad.kr[k] * l1x);
-}
-
-__device__ inline void compute_l0(int P, int p0, const int *pa, const int *pb, const double *ev, const double *cg,
-                                  double *l0) {
-  const int pl = threadIdx.x >> 2, d = threadIdx.x & 3;
-  const int p = p0 + pl;
-  double v = 0.0;
-  if (ev != nullptr && p < P) {
-    const int a = pa[p], b = pb[p];
-    const int m0 = d == 0 ? 0 : (d == 1 ? 3 : (d == 2 ? 8 : 15));
-    const int m1 = d == 0 ? 3 : (d == 1 ? 8 : (d == 2 ? 15 : 24));
-    for (int m = m0; m < m1; ++m) {
-      const double diff = ev[(size_t)b * kEV + m] - ev[(size_t)a * kEV + m];
-      v += diff * diff * cg[m];
-    }
-  }
-  l0[pl * 4 + d] = v;
-}
 
 // b[j] = {B(8 ks + 2t, n), B(8 ks + 2t + 1, n)}, n = 32 slab + 8 (ni0 + j) + g, for
 // j < NB, from a fragment-major operand with `nslab` column slabs (8
@@ -270,26 +226,6 @@ void launch_filter_forward(int P, const double *geo, const int *pair_a, const in
 // All per-tile inputs are streamed into shared memory with cp.async at kernel
 // start so the tensor-core work never waits on a gather.
 // ---------------------------------------------------------------------------
-namespace {
-
-// copy a TP x width block of a row-major global array (row stride = width) to
-// shared memory with row stride lds; rows beyond P are zero-filled
-template <int WIDTH>
-__device__ inline void stage_rows(double *dst, int lds, const double *src, int p0, int P) {
-  constexpr int chunks = WIDTH / 2;  // 16-byte chunks per row
-  for (int idx = threadIdx.x; idx < TP * chunks; idx += blockDim.x) {
-    const int row = idx / chunks, c = idx % chunks;
-    double *d = dst + row * lds + 2 * c;
-    if (p0 + row < P) {
-      cp_async16(d, src + (size_t)(p0 + row) * WIDTH + 2 * c);
-    } else {
-      d[0] = 0.0;
-      d[1] = 0.0;
-    }
-  }
-}
-
-}  // namespace
 
 // One cluster of two CTAs per tile of TP pairs: CTA rank 0 pushes the gradient
 // of the invariant filter through its MLP, rank 1 that of the ev filter. Each

@@ -111,6 +111,19 @@ void launch_filter_reverse(int P, const double *geo, const int *pair_a, const in
                            const double *gA, const double *pair_sc, bool need_l0, bool accumulate, double *g_r,
                            double *g_y, double *gl0, cudaStream_t s);
 void launch_pair_tail(int P, const double *geo, const double *g_r, const double *g_y, double *gv, cudaStream_t s);
+// mixed precision (filter_mixed.cu): the same outputs with the filter GEMMs in
+// three TF32 passes (float32 accuracy); sp holds float32 silu' values
+// (filter_sp_doubles(P) floats)
+void launch_filter_forward_mixed(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
+                                 const double *cg_att, const FilterW32 &finv, const FilterW32 &fev,
+                                 const RadialW &rad, double *f_inv, double *f_ev, float *sp, double *drbf,
+                                 cudaStream_t s);
+void launch_filter_reverse_mixed(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
+                                 const double *cg_att, const FilterW &finv, const FilterW &fev,
+                                 const FilterW32 &finv32, const FilterW32 &fev32, const double *g_filt_inv,
+                                 const double *g_filt_ev, const float *sp, const double *drbf, const double *gA,
+                                 const double *pair_sc, bool need_l0, bool accumulate, double *g_r, double *g_y,
+                                 double *gl0, cudaStream_t s);
 
 // ---- attention (receiver CSR gathers) ----------------------------------------
 void launch_attention_forward(int n, const NeighborState &nb, const double *geo, const double *sh,

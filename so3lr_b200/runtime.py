@@ -26,7 +26,7 @@ EXPORTED = (
     "so3lr_create", "so3lr_describe", "so3lr_validate_charge_spin", "so3lr_element_from_token",
     "so3lr_inspect_model", "so3lr_compute", "so3lr_compute_local", "so3lr_compute_device", "so3lr_compute_batch",
     "so3lr_md_init", "so3lr_md_run", "so3lr_md_thermostat", "so3lr_md_thermostat_energy", "so3lr_md_state", "so3lr_profile", "so3lr_profile_read",
-    "so3lr_launch_count", "so3lr_long_range_noalloc", "so3lr_virial_atom", "so3lr_stream", "so3lr_last_stats",
+    "so3lr_launch_count", "so3lr_set_precision", "so3lr_long_range_noalloc", "so3lr_virial_atom", "so3lr_stream", "so3lr_last_stats",
     "so3lr_destroy",
     "so3lr_nccl_unique_id", "so3lr_comm_init", "so3lr_owned_atoms", "so3lr_partition",
 )
@@ -109,6 +109,7 @@ def load_library(path: os.PathLike | str | None = None) -> C.CDLL:
     lib.so3lr_md_state.argtypes = [C.c_void_p, _dp, _dp, _dp, _dp, C.c_char_p, C.c_size_t]
     lib.so3lr_profile.argtypes = [C.c_void_p, C.c_int]
     lib.so3lr_profile_read.argtypes = [C.c_void_p, C.c_int, _dp, _lp, _dp, C.c_char_p, C.c_size_t]
+    lib.so3lr_set_precision.argtypes = [C.c_void_p, C.c_int, C.c_char_p, C.c_size_t]
     lib.so3lr_launch_count.argtypes = []
     lib.so3lr_launch_count.restype = C.c_longlong
     lib.so3lr_long_range_noalloc.argtypes = [C.c_void_p, C.c_longlong] + [C.c_void_p] * 11 + [C.c_void_p, C.c_char_p,
@@ -243,6 +244,16 @@ class So3lrB200:
         _check(self._lib.so3lr_profile_read(self._h, int(kernel), C.byref(ms), C.byref(n), C.byref(fl), err, 1024),
                err)
         return {"ms": ms.value, "launches": n.value, "flops": fl.value}
+
+    PRECISIONS = {"float64": 0, "mixed": 1}
+
+    def set_precision(self, precision: str) -> None:
+        """'float64' (default) or 'mixed': the pair-filter MLPs as three-pass
+        TF32 tensor-core GEMMs with float32 accumulation, the rest float64."""
+        if precision not in self.PRECISIONS:
+            raise ValueError(f"precision must be one of {sorted(self.PRECISIONS)}")
+        err = C.create_string_buffer(1024)
+        _check(self._lib.so3lr_set_precision(self._h, self.PRECISIONS[precision], err, 1024), err)
 
     def launch_count(self) -> int:
         return int(self._lib.so3lr_launch_count())

@@ -409,3 +409,39 @@ def test_gpu_local_frame_matches_compute(gpu_model):
         gpu_model.compute_local(n, bad, pos[order], z[order], cell=w.cell, boxlo=w.boxlo)
     with pytest.raises(So3lrError, match="atoms in all"):
         gpu_model.compute_local(n + 3, tags, pos[order], z[order], cell=w.cell, boxlo=w.boxlo)
+
+
+@pytest.mark.parametrize("nmol", [64, 1000])
+def test_gpu_mixed_precision_within_stated_tolerance(nmol, gpu_model):
+    """SO3LR_PRECISION_MIXED (pair-filter GEMMs as three-pass TF32 on the
+    tensor cores, float32 accumulation) against float64 on configs 1 and 2:
+    force MAE <= 1e-4 eV/A (the stated tolerance), max force error <= 1e-3 eV/A,
+    energy <= 1e-4 eV/atom, virial <= 1e-3 eV per component per 100 atoms; and
+    switching back gives the float64 bits again."""
+    from so3lr_b200.systems import water_box
+    w = water_box(nmol, seed=2026)
+    n = len(w.z)
+    ref = gpu_model.compute(w.pos, w.z, cell=w.cell, boxlo=w.boxlo)
+    try:
+        gpu_model.set_precision("mixed")
+        mix = gpu_model.compute(w.pos, w.z, cell=w.cell, boxlo=w.boxlo)
+    finally:
+        gpu_model.set_precision("float64")
+    df = np.abs(mix["forces"] - ref["forces"])
+    assert df.mean() <= 1e-4, df.mean()
+    assert df.max() <= 1e-3, df.max()
+    assert abs(mix["energy"] - ref["energy"]) / n <= 1e-4
+    assert np.abs(mix["virial"] - ref["virial"]).max() <= 1e-3 * n / 100
+    assert df.mean() > 0.0  # the mixed kernels ran
+    again = gpu_model.compute(w.pos, w.z, cell=w.cell, boxlo=w.boxlo)
+    assert np.array_equal(again["forces"], ref["forces"]) and again["energy"] == ref["energy"]
+
+
+def test_gpu_mixed_precision_refuses_unknown_mode(gpu_model):
+    from so3lr_b200 import So3lrError
+    with pytest.raises(ValueError):
+        gpu_model.set_precision("bf16")
+    err = __import__("ctypes").create_string_buffer(256)
+    assert gpu_model._lib.so3lr_set_precision(gpu_model._h, 7, err, 256) != 0
+    assert b"precision must be" in err.value
+    assert So3lrError is not None
