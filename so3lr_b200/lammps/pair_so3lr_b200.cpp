@@ -20,6 +20,7 @@
 #include "force.h"
 #include "memory.h"
 #include "so3lr_b200.h"
+#include "so3lr_b200_precision.h"
 #include "utils.h"
 
 using namespace LAMMPS_NS;
@@ -76,6 +77,9 @@ void PairSO3LRB200::settings(int narg, char **arg) {
     const int device = dev ? std::atoi(dev) : comm->me;
     if (so3lr_create(model_path_.c_str(), device, &handle_, err, sizeof(err)) != 0)
       problem = std::string("Cannot initialize SO3LR model on the GPU: ") + err;
+    // $SO3LR_B200_PRECISION=mixed: pair-filter GEMMs as three-pass TF32
+    else if (so3lr_b200_precision_from_env(handle_, err, sizeof(err)) != 0)
+      problem = std::string("SO3LR precision: ") + err;
   }
   // a failure on some ranks only (a missing GPU, a file one node cannot read)
   // must not leave the others waiting in the next collective

@@ -31,6 +31,7 @@
 #include "force.h"
 #include "memory.h"
 #include "so3lr_b200.h"
+#include "so3lr_b200_precision.h"
 #include "universe.h"
 #include "utils.h"
 
@@ -105,6 +106,9 @@ void PairSO3LRB200Turbo::settings(int narg, char **arg) {
       if (so3lr_create(model_path_.c_str(), (dev ? std::atoi(dev) : 0) + group_, &handle_, err, sizeof(err)) != 0) {
         ok = 0;
         std::snprintf(msg, sizeof(msg), " on the GPU: %s", err);
+      } else if (so3lr_b200_precision_from_env(handle_, err, sizeof(err)) != 0) {
+        ok = 0;
+        std::snprintf(msg, sizeof(msg), ": %s", err);
       }
     }
   }

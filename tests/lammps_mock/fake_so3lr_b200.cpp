@@ -157,6 +157,12 @@ int so3lr_compute_local(so3lr_handle *h, const so3lr_local_frame *in, so3lr_loca
   if (g_profile_on) ++g_profile_calls;
   return 0;
 }
+int so3lr_set_precision(so3lr_handle *h, int precision, char *err, size_t errlen) {
+  if (!h || (precision != SO3LR_PRECISION_FLOAT64 && precision != SO3LR_PRECISION_MIXED))
+    return fake_fail("so3lr_set_precision: precision must be SO3LR_PRECISION_FLOAT64 (0) or SO3LR_PRECISION_MIXED (1)",
+                     err, errlen);
+  return 0;
+}
 // several ranks: no communication in the stand-in, every rank evaluates the
 // whole system it is given (as every rank of the real library returns it)
 int so3lr_nccl_unique_id(char *out, char *, size_t) {

@@ -196,6 +196,20 @@ def test_duplicate_atom_tags_are_refused(tmp_path):
     assert res.returncode != 0 and "atom tags must be unique" in res.stdout + res.stderr, res.stdout + res.stderr
 
 
+def test_precision_environment_variable(tmp_path, monkeypatch):
+    """SO3LR_B200_PRECISION=mixed switches the style's handle to the mixed
+    precision mode; any value other than float64 or mixed is refused when the
+    pair style is set up."""
+    exe = _build(tmp_path, fake=True)
+    _, inp = _water_input(tmp_path, nmol=2)
+    monkeypatch.setenv("SO3LR_B200_PRECISION", "bf16")
+    res = subprocess.run([str(exe), "run", "fake", str(inp)], capture_output=True, text=True, timeout=120)
+    assert res.returncode != 0 and "must be 'float64' or 'mixed'" in res.stdout + res.stderr, res.stdout + res.stderr
+    monkeypatch.setenv("SO3LR_B200_PRECISION", "mixed")
+    res = subprocess.run([str(exe), "run", "fake", str(inp)], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0, res.stdout + res.stderr
+
+
 def test_model_failure_on_one_rank_stops_every_rank(tmp_path):
     """so3lr/b200 on two ranks (threads) where only one cannot load the model:
     that rank reports the loader's message, the other learns of it in the same
