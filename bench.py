@@ -210,6 +210,18 @@ def measure_tf32_peak(device: int) -> float:
     return best
 
 
+def library_record() -> dict:
+    """Which build of libso3lr_b200.so this run loaded: SHA-256 (first 16 hex
+    digits) and modification time of the in-tree library, and whether it is
+    newer than every source file (built from the sources in this tree)."""
+    import hashlib
+    from so3lr_b200.build import LIB, headers, sources
+    data = LIB.read_bytes()
+    newest = max(p.stat().st_mtime for p in list(sources()) + list(headers()))
+    return {"path": "so3lr_b200/libso3lr_b200.so", "sha256_16": hashlib.sha256(data).hexdigest()[:16],
+            "mtime": LIB.stat().st_mtime, "newer_than_sources": LIB.stat().st_mtime >= newest}
+
+
 def cpu_model() -> str:
     """The host CPU's model name (lscpu / /proc/cpuinfo), for the baseline record."""
     try:
@@ -465,6 +477,7 @@ def run_ours(args) -> None:
             "vs_baseline": (value / A100_24K_ATOM_STEPS) if (world == 1 and args.config == 3) else None,
             "dtype": "tf32x3+f64" if mixed else "f64", "data": "synthetic",
             "config": cfg,
+            "library": library_record(),
             "stats": {"atoms_owned_rank0": owned, "sr_edges_rank0": stats["sr_edges"],
                       "sr_pairs_rank0": stats["sr_pairs"], "ns_per_day": steps_per_s * 0.0432,
                       "exchange_ms_per_step": exchange},
