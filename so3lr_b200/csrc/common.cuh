@@ -179,6 +179,11 @@ struct FilterW32 {
   const float *v0, *c0;            // [32][4], [32]
   const float *w0t_h, *w0t_l, *w1t_h, *w1t_l, *v1t_h, *v1t_l;  // forward operands
   const float *w1_h, *w1_l, *v1_h, *v1_l, *w0_h, *w0_l;        // reverse operands
+  // forward operands for the tcgen05 kernel (filter_tc.cu): six [128 x 32]
+  // K-chunks -- W0, W1 columns 0-31, 32-63, 64-95, 96-127, V1 -- each as a TF32
+  // hi tile then a lo tile of 16 KB in the 128-byte-swizzled K-major layout of
+  // the tensor core's shared-memory operands (32 KB per chunk, 192 KB in all)
+  const float *tc_fwd;
 };
 struct BlockW {
   FilterW finv, fev;

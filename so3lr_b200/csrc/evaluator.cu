@@ -3,6 +3,7 @@
 #include "nccl_dyn.hpp"
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <numeric>
@@ -19,7 +20,14 @@ Evaluator::Evaluator(const std::string &model_path, int device) : model_(Model::
   SO3_CUDA(cudaGetDeviceProperties(&prop, device));
   if (prop.major < 10)
     throw Error(std::string("SO3LR: this library is built for sm_100a (B200); device is ") + prop.name);
+  num_sms_ = prop.multiProcessorCount;
+  // the mixed-precision filter forward runs on the tcgen05 tensor cores unless
+  // SO3LR_B200_MIXED_FORWARD=mma selects the mma.sync kernel (for comparisons)
+  const char *fwd = std::getenv("SO3LR_B200_MIXED_FORWARD");
+  mixed_tc_ = !(fwd && std::string(fwd) == "mma");
   SO3_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  tc_err_ = tc_err_arr_.reserve(1);
+  SO3_CUDA(cudaMemset(tc_err_, 0, sizeof(int)));
   SO3_CUDA(cudaMallocHost(&host_small_, 16 * sizeof(int)));
   SO3_CUDA(cudaMallocHost(&host_totals_, 16 * sizeof(double)));
   upload_weights();
@@ -111,6 +119,32 @@ void Evaluator::upload_weights() {
   struct FOff32 {
     std::size_t b0, bc1, v0, c0;
     std::pair<std::size_t, std::size_t> w0t, w1t, v1t, w1, v1, w0;
+    std::size_t tc_fwd;
+  };
+  // [128 x 32] K-chunk c of a row-major [128 x K] matrix as TF32 hi and lo tiles
+  // in the 128-byte-swizzled K-major layout (row n, column k at byte
+  // 1024 (n / 8) + 128 (n % 8) + 16 ((k / 4) xor (n % 8)) + 4 (k % 4))
+  auto push_tc_chunks = [&](const std::vector<std::pair<const std::vector<double> *, int>> &chunks) {
+    std::vector<double> all;
+    for (const auto &ch : chunks) {
+      const std::vector<double> &m = *ch.first;
+      const int K = int(m.size() / 128), c = ch.second;
+      std::vector<double> hi(128 * 32), lo(128 * 32);
+      for (int n = 0; n < 128; ++n)
+        for (int k = 0; k < 32; ++k) {
+          const double v = m[std::size_t(n) * K + 32 * c + k];
+          const float h = tf32_round(float(v));
+          const std::size_t off = (n / 8) * 256 + (n % 8) * 32 + (((k / 4) ^ (n % 8)) * 4) + (k % 4);
+          hi[off] = h;
+          lo[off] = tf32_round(float(v - double(h)));
+        }
+      all.insert(all.end(), hi.begin(), hi.end());
+      all.insert(all.end(), lo.begin(), lo.end());
+    }
+    while (host32.size() % 256) host32.push_back(0.0f);  // 1024-byte alignment
+    const std::size_t off = host32.size();
+    for (double x : all) host32.push_back(float(x));
+    return off;
   };
   struct BOff {
     FOff finv, fev;
@@ -155,6 +189,7 @@ void Evaluator::upload_weights() {
     o32.w1 = push_split(fragment_major(iF, iF, [&](int oo, int j) { return w1[std::size_t(oo) * F + j]; }));
     o32.v1 = push_split(fragment_major(iF, iH, [&](int oo, int h) { return v1[std::size_t(oo) * H + h]; }));
     o32.w0 = push_split(fragment_major(iF, iR, [&](int j, int r) { return w0[std::size_t(j) * R + r]; }));
+    o32.tc_fwd = push_tc_chunks({{&w0, 0}, {&w1, 0}, {&w1, 1}, {&w1, 2}, {&w1, 3}, {&v1, 0}});
     return o;
   };
   for (int b = 0; b < layers_; ++b) {
@@ -300,7 +335,8 @@ void Evaluator::upload_weights() {
     return FilterW32{P32(f.b0),         P32(f.bc1),         P32(f.v0),          P32(f.c0),
                      P32(f.w0t.first),  P32(f.w0t.second),  P32(f.w1t.first),   P32(f.w1t.second),
                      P32(f.v1t.first),  P32(f.v1t.second),  P32(f.w1.first),    P32(f.w1.second),
-                     P32(f.v1.first),   P32(f.v1.second),   P32(f.w0.first),    P32(f.w0.second)};
+                     P32(f.v1.first),   P32(f.v1.second),   P32(f.w0.first),    P32(f.w0.second),
+                     P32(f.tc_fwd)};
   };
   blocks_.resize(layers_);
   for (int b = 0; b < layers_; ++b) {
@@ -713,6 +749,14 @@ void Evaluator::alloc_atoms() {
   stage_.resize(std::size_t(n) * 6);
 }
 
+// flags the kernels of the last evaluation left (copied to host_small_[8..9])
+void Evaluator::check_device_flags() const {
+  if (host_small_[8] != 0) throw Error("SO3LR: short-range list has an edge without its reverse");
+  if (host_small_[9] != 0)
+    throw Error("SO3LR: the tensor-core filter kernel gave up waiting for its pipeline (stage " +
+                std::to_string(host_small_[9]) + "); its results are not valid");
+}
+
 void Evaluator::upload_positions(const double *host_x) {
   SO3_CUDA(cudaSetDevice(device_));
   if (identity_) {
@@ -888,6 +932,7 @@ void Evaluator::compute() {
   cudaStream_t s = stream_;
   const int *own_seg = seg_.get();
   const int *count_seg = identity_ ? image_start_.get() : seg_.get() + 2;
+  if (mixed_ && mixed_tc_) SO3_CUDA(cudaMemsetAsync(tc_err_, 0, sizeof(int), s));
   build_neighbors();
   const int P = int(stats_.pairs);
   launch_pair_geometry(P, nb_, z_.get(), zbl_, sr_cut_, geo_.get(), sh_.get(), gv_.get(), s);
@@ -901,7 +946,12 @@ void Evaluator::compute() {
   for (int b = 0; b < layers_; ++b) {
     const BlockW &w = blocks_[b];
     prof_begin(kProfFilterForward);
-    if (mixed_)
+    if (mixed_ && mixed_tc_)
+      launch_filter_forward_tc(P, geo_.get(), nb_.pair_a, nb_.pair_b, b == 0 ? nullptr : evb_[b]->get(), w.cg_att,
+                               w.finv32, w.fev32, rad_, f_inv_[b]->get(), f_ev_[b]->get(),
+                               reinterpret_cast<float *>(sp_[b]->get()), b == 0 ? drbf_.get() : nullptr, tc_err_,
+                               num_sms_, s);
+    else if (mixed_)
       launch_filter_forward_mixed(P, geo_.get(), nb_.pair_a, nb_.pair_b, b == 0 ? nullptr : evb_[b]->get(), w.cg_att,
                                   w.finv32, w.fev32, rad_, f_inv_[b]->get(), f_ev_[b]->get(),
                                   reinterpret_cast<float *>(sp_[b]->get()), b == 0 ? drbf_.get() : nullptr, s);
@@ -1180,8 +1230,9 @@ Evaluator::HostResult Evaluator::download(double *f, double *eatom, double *char
   if (image_energy) SO3_CUDA(cudaMemcpyAsync(image_energy, image_energy_.get(), sizeof(double) * nimg, cudaMemcpyDeviceToHost, s));
   SO3_CUDA(cudaMemcpyAsync(host_totals_, totals_.get(), sizeof(double) * 7, cudaMemcpyDeviceToHost, s));
   SO3_CUDA(cudaMemcpyAsync(host_small_ + 8, nb_.error_flag, sizeof(int), cudaMemcpyDeviceToHost, s));
+  SO3_CUDA(cudaMemcpyAsync(host_small_ + 9, tc_err_, sizeof(int), cudaMemcpyDeviceToHost, s));
   SO3_CUDA(cudaStreamSynchronize(s));
-  if (host_small_[8] != 0) throw Error("SO3LR: short-range list has an edge without its reverse");
+  check_device_flags();
   HostResult r;
   r.energy = host_totals_[0];
   for (int k = 0; k < 6; ++k) r.virial[k] = host_totals_[1 + k];

@@ -262,6 +262,11 @@ class Evaluator {
   };
   bool profiling_ = false;
   bool mixed_ = false;
+  bool mixed_tc_ = true;           // mixed forward on tcgen05 (filter_tc.cu), else mma.sync
+  int num_sms_ = 148;
+  DeviceArray<int> tc_err_arr_;    // error word of the tcgen05 kernel
+  int *tc_err_ = nullptr;
+  void check_device_flags() const;
   KernelProfile prof_[kProfKinds];
   void prof_begin(int k);
   void prof_end(int k, double flops);

@@ -1,0 +1,439 @@
+// Mixed-precision pair-filter forward on the fifth-generation tensor cores
+// (tcgen05, TF32 kind): the same outputs as k_filter_forward_mixed
+// (filter_mixed.cu) -- both filters of every pair in float64, float32 silu' of
+// the rbf hidden layer for the reverse, d rbf/dr -- with the GEMMs issued as
+// tcgen05.mma from shared-memory descriptors into a TMEM accumulator.
+//
+// Tile: 128 pairs (one TMEM lane per pair). Per tile and filter
+//   D1 = rbf W0^T                      (K = 32)   TMEM columns   0..127
+//   u  = silu(D1 + b0)                 (epilogue warps, split into TF32 hi/lo)
+//   D2 = u W1^T + w V1^T               (K = 128 + 32) columns 128..255
+//   f  = D2 + b1 + c1                  (float64 to global)
+// with w = silu(L0 V0^T + c0) computed by the epilogue warps. Every product is
+// three TF32 MMAs (A_lo B_hi, A_hi B_lo, A_hi B_hi; see filter_mixed.cu).
+//
+// Warp roles: warps 0-7 build the A operands (rbf, w, u) in shared memory and
+// read the accumulators back (warp w owns TMEM lanes 32 (w % 4) .. + 31, i.e.
+// its pairs, and column half w / 4 of every 32-column chunk); warp 8 (one
+// elected lane) streams the weight K-chunks into a three-slot ring with bulk
+// asynchronous copies (cp.async.bulk, this GPU's own global memory, no
+// multicast) and issues the MMAs. The hidden layer is handed to the MMA in
+// 32-column chunks through a two-slot ring, so the second GEMM starts while
+// the epilogue still works on later chunks. All hand-offs are mbarriers; every
+// wait gives up after about two seconds, records where in an error word and
+// the CTA stops (no spin without a bound).
+//
+// Weights come pre-split and pre-swizzled (FilterW32::tc_fwd). Shared-memory
+// operands use the 128-byte-swizzled K-major layout: a [128 x 32] float tile is
+// 16 KB, row n, column k at byte 1024 (n / 8) + 128 (n % 8) + 16 ((k / 4) xor
+// (n % 8)) + 4 (k % 4); the descriptor's stride byte offset is 1024 (one 8-row
+// group) and each K step of 8 advances its start address by 32 bytes.
+//
+// The silu' values are written in the layout the mixed reverse reads
+// (sp_offset, 64-pair tiles), so k_filter_reverse_mixed consumes them unchanged.
+#include "filter_common.cuh"
+#include "kernels.cuh"
+
+namespace so3lr_b200 {
+namespace {
+
+constexpr int kTcRows = 128;
+constexpr int kTcEpiWarps = 8;
+constexpr int kTcThreads = (kTcEpiWarps + 1) * 32;
+constexpr uint32_t kTile = 128 * 32 * 4;  // one [128 x 32] float tile, 16 KB
+constexpr int kBSlots = 3;
+constexpr uint32_t kOffA1 = 0;                             // rbf: hi, lo
+constexpr uint32_t kOffA3 = kOffA1 + 2 * kTile;            // ev hidden w: hi, lo
+constexpr uint32_t kOffA2 = kOffA3 + 2 * kTile;            // hidden u chunks: 2 slots x (hi, lo)
+constexpr uint32_t kOffB = kOffA2 + 4 * kTile;             // weight chunks: kBSlots x (hi, lo)
+constexpr uint32_t kOffBar = kOffB + kBSlots * 2 * kTile;  // mbarriers
+constexpr int kNumBars = 16;
+constexpr uint32_t kSmemTc = kOffBar + kNumBars * 8 + 16 + 1024;  // + TMEM address + alignment slack
+// mbarrier indices
+constexpr int kFullB = 0;      // 3: weight chunk landed (transaction bytes)
+constexpr int kEmptyB = 3;     // 3: MMAs reading the weight slot done
+constexpr int kFullA = 6;      // 2: hidden chunk written (8 epilogue warps)
+constexpr int kEmptyA = 8;     // 2: MMAs reading the hidden slot done
+constexpr int kOpnd = 10;      // rbf (first filter) and w written (8 warps)
+constexpr int kD1Full = 11;    // D1 complete
+constexpr int kD2Full = 12;    // D2 complete
+constexpr int kD1Free = 13;    // D1 read by every epilogue warp (8)
+constexpr int kD2Free = 14;    // D2 read by every epilogue warp (8)
+constexpr int kDrain = 15;     // all MMAs of the CTA complete (teardown)
+constexpr long long kWaitCycles = 4000000000LL;  // about 2 s at 1.9 GHz
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+// Wait for the completion of the phase with the given parity, at most
+// kWaitCycles; false (and the error word set to `where`) when it gives up or
+// when another thread of the CTA already gave up.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, int *err,
+                                          int where) {
+  uint32_t done = 0;
+  const long long t0 = clock64();
+  while (true) {
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *abort_flag = 1;
+      atomicCAS(err, 0, where);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major, 128-byte swizzle, 8-row groups 1024 bytes apart (sm100 descriptor)
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
+  return uint64_t((saddr >> 4) & 0x3fff) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
+         (uint64_t(2) << 61);
+}
+// kind::tf32, D float32, A and B TF32 K-major, M = 128, N = 128
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(128 >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+
+__device__ __forceinline__ void mma_tf32_tc(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate));
+}
+// D (+)= A B^T over one 32-wide K-chunk in three TF32 passes; A, B: hi tile then lo tile
+__device__ __forceinline__ void mma_chunk(uint32_t d_tmem, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi,
+                                          uint32_t b_lo, bool accumulate) {
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    const uint32_t o = 32u * ks;
+    mma_tf32_tc(d_tmem, smem_desc(a_lo + o), smem_desc(b_hi + o), (accumulate || ks > 0) ? 1u : 0u);
+    mma_tf32_tc(d_tmem, smem_desc(a_hi + o), smem_desc(b_lo + o), 1u);
+    mma_tf32_tc(d_tmem, smem_desc(a_hi + o), smem_desc(b_hi + o), 1u);
+  }
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+// 16 consecutive float32 columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float tf32_hi(float x) {
+  unsigned r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+// 16 values of row `row`, columns 16 hh .. + 15 of a [128 x 32] tile pair (hi, lo)
+__device__ __forceinline__ void store_row16(char *hi_tile, char *lo_tile, int row, int hh, const float (&v)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int chunk = (4 * hh + q) ^ (row & 7);
+    const uint32_t off = (row >> 3) * 1024 + (row & 7) * 128 + chunk * 16;
+    float h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      h[e] = tf32_hi(v[4 * q + e]);
+      l[e] = tf32_hi(v[4 * q + e] - h[e]);
+    }
+    *reinterpret_cast<float4 *>(hi_tile + off) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4 *>(lo_tile + off) = make_float4(l[0], l[1], l[2], l[3]);
+  }
+}
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+
+// position of silu'(pair row64 of 64-pair tile t64, column col) in the layout of
+// the mixed forward and reverse (sp_offset): warp = col / 16, m16 block mi = row / 16
+__device__ __forceinline__ size_t sp_index(int t64, int filt, int row, int col) {
+  const int mi = row >> 4, hf = (row >> 3) & 1, g = row & 7;
+  const int w = col >> 4, ni = (col >> 3) & 1, t = (col >> 1) & 3, e = col & 1;
+  return sp_offset(t64, filt, (mi >> 1) * 4 + (w >> 1)) + (((mi & 1) * 4 + (w & 1) * 2 + ni) * 2) * 64 + hf * 64 +
+         (4 * g + t) * 2 + e;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kTcThreads, 1) k_filter_forward_tc(
+    int P, int ntiles, const double *__restrict__ geo, const int *__restrict__ pa, const int *__restrict__ pb,
+    const double *__restrict__ ev, const double *__restrict__ cg, FilterW32 finv, FilterW32 fev, RadialW rad,
+    double *__restrict__ f_inv, double *__restrict__ f_ev, float *__restrict__ sp, double *__restrict__ drbf,
+    int *__restrict__ err) {
+  extern __shared__ unsigned char smem_raw[];
+  // 1024-byte alignment for the swizzled operand tiles
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  unsigned char *sm = smem_raw + (base - raw);
+  const uint32_t bars = base + kOffBar;
+  auto bar = [&](int i) { return bars + 8u * i; };
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kOffBar + kNumBars * 8);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + kOffBar + kNumBars * 8 + 4);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  if (tid == 0) {
+    for (int i = 0; i < 3; ++i) mbar_init(bar(kFullB + i), 1);
+    for (int i = 0; i < 3; ++i) mbar_init(bar(kEmptyB + i), 1);
+    for (int i = 0; i < 2; ++i) mbar_init(bar(kFullA + i), kTcEpiWarps);
+    for (int i = 0; i < 2; ++i) mbar_init(bar(kEmptyA + i), 1);
+    mbar_init(bar(kOpnd), kTcEpiWarps);
+    mbar_init(bar(kD1Full), 1);
+    mbar_init(bar(kD2Full), 1);
+    mbar_init(bar(kD1Free), kTcEpiWarps);
+    mbar_init(bar(kD2Free), kTcEpiWarps);
+    mbar_init(bar(kDrain), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kTcEpiWarps) {  // the MMA warp owns the TMEM allocation: D1 and D2, 128 columns each
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(tmem_slot)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+
+  if (warp == kTcEpiWarps) {
+    // ------------------------------------------------------------------ MMA warp
+    if (lane == 0) {
+      const int total = my_tiles * 12;  // 6 weight chunks (MMA groups) per tile and filter
+      int next_load = 0, landed = 0;     // loads issued; loads waited for (their MMAs issued)
+      bool ok = true;
+      for (int g = 0; g < total && ok; ++g) {
+        // keep up to kBSlots weight chunks in flight
+        while (ok && next_load < total && next_load <= g + kBSlots - 1) {
+          const int s = next_load % kBSlots, n = next_load / kBSlots;
+          ok = mbar_wait(bar(kEmptyB + s), (n & 1) ^ 1, abort_flag, err, 1);
+          if (!ok) break;
+          const int tf = next_load / 6, gi = next_load % 6;
+          const FilterW32 &W = (tf & 1) ? fev : finv;
+          mbar_expect_tx(bar(kFullB + s), 2 * kTile);
+          bulk_load(base + kOffB + s * 2 * kTile, W.tc_fwd + size_t(gi) * (2 * kTile / 4), 2 * kTile, bar(kFullB + s));
+          ++next_load;
+        }
+        if (!ok) break;
+        const int tf = g / 6, gi = g % 6;  // (tile, filter) index and group within it
+        const int s = g % kBSlots;
+        const uint32_t b_hi = base + kOffB + s * 2 * kTile, b_lo = b_hi + kTile;
+        if (gi == 0) {
+          ok = mbar_wait(bar(kOpnd), tf & 1, abort_flag, err, 2) &&
+               mbar_wait(bar(kD1Free), (tf & 1) ^ 1, abort_flag, err, 3);
+        } else if (gi <= 4) {
+          const int c = gi - 1, slot = c & 1, use = tf * 2 + (c >> 1);
+          ok = mbar_wait(bar(kFullA + slot), use & 1, abort_flag, err, 4);
+          if (ok && c == 0) ok = mbar_wait(bar(kD2Free), (tf & 1) ^ 1, abort_flag, err, 5);
+        }
+        if (ok) ok = mbar_wait(bar(kFullB + s), (g / kBSlots) & 1, abort_flag, err, 6);
+        if (!ok) break;
+        landed = g + 1;
+        tc_fence_after();
+        if (gi == 0) {
+          mma_chunk(tmem, base + kOffA1, base + kOffA1 + kTile, b_hi, b_lo, false);
+          tc_commit(bar(kEmptyB + s));
+          tc_commit(bar(kD1Full));
+        } else if (gi <= 4) {
+          const int c = gi - 1, slot = c & 1;
+          const uint32_t a_hi = base + kOffA2 + slot * 2 * kTile;
+          mma_chunk(tmem + 128, a_hi, a_hi + kTile, b_hi, b_lo, c > 0);
+          tc_commit(bar(kEmptyB + s));
+          tc_commit(bar(kEmptyA + slot));
+        } else {
+          mma_chunk(tmem + 128, base + kOffA3, base + kOffA3 + kTile, b_hi, b_lo, true);
+          tc_commit(bar(kEmptyB + s));
+          tc_commit(bar(kD2Full));
+        }
+      }
+      // teardown: every MMA this thread issued has completed and, after a wait
+      // that gave up, every weight copy still in flight has landed (bounded)
+      tc_commit(bar(kDrain));
+      mbar_wait(bar(kDrain), 0, abort_flag, err, 7);
+      for (int i = landed; i < next_load; ++i) {
+        const long long t0 = clock64();
+        uint32_t d = 0;
+        while (!d && clock64() - t0 < kWaitCycles)
+          asm volatile(
+              "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+              " selp.u32 %0, 1, 0, p;\n}\n"
+              : "=r"(d)
+              : "r"(bar(kFullB + i % kBSlots)), "r"(uint32_t((i / kBSlots) & 1))
+              : "memory");
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue warps
+    const int q = warp & 3, hh = warp >> 2;
+    const int row = 32 * q + lane;
+    const uint32_t lane_base = tmem + (uint32_t(32 * q) << 16);
+    double l0[4] = {0, 0, 0, 0};
+    bool ok = true;
+    for (int it = 0; it < my_tiles && ok; ++it) {
+      const int tile = int(blockIdx.x) + it * int(gridDim.x);
+      const int p = tile * kTcRows + row;
+      const bool valid = p < P;
+      for (int f = 0; f < 2 && ok; ++f) {
+        const int tf = it * 2 + f;
+        const FilterW32 &W = f ? fev : finv;
+        double *out = f ? f_ev : f_inv;
+        if (f == 0) {
+          // radial basis (float64, as the float64 path) into A1, d rbf/dr, and L0
+          const double r = valid ? geo[(size_t)p * kGeo] : 1.0;
+          const double raw_x = exp(-rad.gamma * r);
+          double x = raw_x;
+          if (x < 1.0e-6) x = 1.0e-6;
+          if (x > 1.0 - 1.0e-6) x = 1.0 - 1.0e-6;
+          const double lx = log(x), l1x = log(1.0 - x);
+          const bool live = raw_x > 1.0e-6 && raw_x < 1.0 - 1.0e-6;
+          const double ratio = live ? raw_x / (1.0 - raw_x) : 0.0;
+          float v[16];
+          double d[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int k = 16 * hh + i;
+            const double b = exp_tang(rad.b[k] + rad.k[k] * lx + rad.kr[k] * l1x);
+            v[i] = float(b);
+            d[i] = live ? b * (-rad.gamma * rad.k[k] + rad.gamma * rad.kr[k] * ratio) : 0.0;
+          }
+          store_row16(reinterpret_cast<char *>(sm + kOffA1), reinterpret_cast<char *>(sm + kOffA1 + kTile), row, hh,
+                      v);
+          if (drbf != nullptr && valid) {
+            double2 *dst = reinterpret_cast<double2 *>(drbf + (size_t)p * kR + 16 * hh);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[i] = make_double2(d[2 * i], d[2 * i + 1]);
+          }
+          l0[0] = l0[1] = l0[2] = l0[3] = 0.0;
+          if (ev != nullptr && valid) {
+            const int a = pa[p], b = pb[p];
+            for (int m = 0; m < kEV; ++m) {
+              const double diff = ev[(size_t)b * kEV + m] - ev[(size_t)a * kEV + m];
+              l0[degree_of_channel(m)] += diff * diff * cg[m];
+            }
+          }
+        }
+        {  // ev branch hidden layer w = silu(L0 V0^T + c0) into A3
+          float v[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int j = 16 * hh + i;
+            const float s = float(l0[0]) * W.v0[j * 4] + float(l0[1]) * W.v0[j * 4 + 1] +
+                            float(l0[2]) * W.v0[j * 4 + 2] + float(l0[3]) * W.v0[j * 4 + 3] + W.c0[j];
+            v[i] = s * sigmoid_fast(s);
+          }
+          store_row16(reinterpret_cast<char *>(sm + kOffA3), reinterpret_cast<char *>(sm + kOffA3 + kTile), row, hh,
+                      v);
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kOpnd));
+        // hidden layer: D1 + b0 -> silu, in 32-column chunks through the hidden ring
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(kD1Full), tf & 1, abort_flag, err, 8));
+        if (!ok) break;
+        tc_fence_after();
+        for (int c = 0; c < 4 && ok; ++c) {
+          const int slot = c & 1, use = tf * 2 + (c >> 1);
+          ok = __all_sync(0xffffffffu, mbar_wait(bar(kEmptyA + slot), (use & 1) ^ 1, abort_flag, err, 9));
+          if (!ok) break;
+          float v[16];
+          tmem_ld16(lane_base + 32 * c + 16 * hh, v);
+          const int col0 = 32 * c + 16 * hh;
+          float u[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float x = v[i] + W.b0[col0 + i];
+            const float s = sigmoid_fast(x);
+            u[i] = x * s;
+            v[i] = s * (1.0f + x * (1.0f - s));  // silu'
+          }
+          char *a_hi = reinterpret_cast<char *>(sm + kOffA2 + slot * 2 * kTile);
+          store_row16(a_hi, a_hi + kTile, row, hh, u);
+          {  // every row of the tile, as the mma.sync forward writes them (finite values past P)
+            const int t64 = p >> 6, r64 = p & 63;
+#pragma unroll
+            for (int i = 0; i < 16; i += 2)
+              *reinterpret_cast<float2 *>(sp + sp_index(t64, f, r64, col0 + i)) = make_float2(v[i], v[i + 1]);
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(kFullA + slot));
+        }
+        if (!ok) break;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kD1Free));
+        // output: D2 + b1 + c1 in float64
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(kD2Full), tf & 1, abort_flag, err, 10));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float v[16];
+          tmem_ld16(lane_base + 128 + 32 * c + 16 * hh, v);
+          const int col0 = 32 * c + 16 * hh;
+          if (valid) {
+            double2 *dst = reinterpret_cast<double2 *>(out + (size_t)p * kF + col0);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              dst[i] = make_double2(double(v[2 * i] + W.bc1[col0 + 2 * i]), double(v[2 * i + 1] + W.bc1[col0 + 2 * i + 1]));
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kD2Free));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kTcEpiWarps) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+  }
+}
+
+// Fills the float64 outputs of launch_filter_forward_mixed with the tcgen05
+// kernel; err (device int, zeroed by the caller) receives the code of a wait
+// that gave up (0: none).
+void launch_filter_forward_tc(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
+                              const double *cg_att, const FilterW32 &finv, const FilterW32 &fev, const RadialW &rad,
+                              double *f_inv, double *f_ev, float *sp, double *drbf, int *err, int num_sms,
+                              cudaStream_t s) {
+  if (P == 0) return;
+  const int ntiles = (P + kTcRows - 1) / kTcRows;
+  allow_dynamic_smem(reinterpret_cast<const void *>(k_filter_forward_tc), kSmemTc);
+  const int grid = std::min(ntiles, std::max(1, num_sms));
+  k_filter_forward_tc<<<grid, kTcThreads, kSmemTc, s>>>(P, ntiles, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad,
+                                                        f_inv, f_ev, sp, drbf, err);
+  SO3_LAUNCH("filter_forward_tc");
+}
+
+}  // namespace so3lr_b200

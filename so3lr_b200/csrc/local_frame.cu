@@ -206,8 +206,9 @@ Evaluator::HostResult Evaluator::compute_local(const SystemSpec &frame, int nloc
   pick(vatom, w_atom_.get(), 6, want_v);
   SO3_CUDA(cudaMemcpyAsync(host_totals_, totals_.get(), sizeof(double) * 7, cudaMemcpyDeviceToHost, s));
   SO3_CUDA(cudaMemcpyAsync(host_small_ + 8, nb_.error_flag, sizeof(int), cudaMemcpyDeviceToHost, s));
+  SO3_CUDA(cudaMemcpyAsync(host_small_ + 9, tc_err_, sizeof(int), cudaMemcpyDeviceToHost, s));
   SO3_CUDA(cudaStreamSynchronize(s));
-  if (host_small_[8] != 0) throw Error("SO3LR: short-range list has an edge without its reverse");
+  check_device_flags();
   HostResult res;
   res.energy = host_totals_[0];
   for (int k = 0; k < 6; ++k) res.virial[k] = host_totals_[1 + k];

@@ -445,3 +445,35 @@ def test_gpu_mixed_precision_refuses_unknown_mode(gpu_model):
     assert gpu_model._lib.so3lr_set_precision(gpu_model._h, 7, err, 256) != 0
     assert b"precision must be" in err.value
     assert So3lrError is not None
+
+
+def test_gpu_mixed_tensor_core_forward_matches_mma_forward(monkeypatch):
+    """The mixed mode's filter forward on the tcgen05 tensor cores (default)
+    and on warp-level mma.sync (SO3LR_B200_MIXED_FORWARD=mma) form the same
+    three-pass TF32 products, so they differ only by float32 summation order:
+    forces within 2e-5 eV/A, energies within 1e-6 eV/atom, on a periodic box
+    whose pair count is not a multiple of the 128-pair tile, and on a charged
+    open cluster."""
+    from conftest import MODEL
+    from so3lr_b200 import So3lrB200
+    from so3lr_b200.systems import water_box, water_cluster
+    monkeypatch.setenv("SO3LR_B200_MIXED_FORWARD", "mma")
+    mma = So3lrB200(MODEL, 0)
+    monkeypatch.delenv("SO3LR_B200_MIXED_FORWARD")
+    tc = So3lrB200(MODEL, 0)
+    try:
+        for h in (mma, tc):
+            h.set_precision("mixed")
+        w = water_box(1000, seed=31)
+        cases = [(w.pos, w.z, w.cell, w.boxlo, 0.0)]
+        pos, z, q = water_cluster(40, np.random.default_rng(9), "hydronium")
+        cases.append((pos, z, None, None, q))
+        for pos, z, cell, boxlo, q in cases:
+            a = tc.compute(pos, z, cell=cell, boxlo=boxlo, charge=q)
+            b = mma.compute(pos, z, cell=cell, boxlo=boxlo, charge=q)
+            assert np.abs(a["forces"] - b["forces"]).max() <= 2e-5
+            assert abs(a["energy"] - b["energy"]) / len(z) <= 1e-6
+            assert not np.array_equal(a["forces"], b["forces"]) or len(z) < 10  # two different kernels ran
+    finally:
+        mma.close()
+        tc.close()
