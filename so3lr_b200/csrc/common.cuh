@@ -184,6 +184,10 @@ struct FilterW32 {
   // hi tile then a lo tile of 16 KB in the 128-byte-swizzled K-major layout of
   // the tensor core's shared-memory operands (32 KB per chunk, 192 KB in all)
   const float *tc_fwd;
+  // reverse operands for the tcgen05 kernel: for K-chunk c = 0..3 a 40 KB group
+  // [W1^T chunk (128 rows) hi | lo][V1^T chunk (32 rows) hi | lo], then for
+  // c = 0..3 an 8 KB group [W0^T chunk (32 rows) hi | lo], same layout
+  const float *tc_rev;
 };
 struct BlockW {
   FilterW finv, fev;

@@ -21,8 +21,8 @@ Evaluator::Evaluator(const std::string &model_path, int device) : model_(Model::
   if (prop.major < 10)
     throw Error(std::string("SO3LR: this library is built for sm_100a (B200); device is ") + prop.name);
   num_sms_ = prop.multiProcessorCount;
-  // the mixed-precision filter forward runs on the tcgen05 tensor cores unless
-  // SO3LR_B200_MIXED_FORWARD=mma selects the mma.sync kernel (for comparisons)
+  // the mixed-precision filter kernels run on the tcgen05 tensor cores unless
+  // SO3LR_B200_MIXED_FORWARD=mma selects the mma.sync kernels (for comparisons)
   const char *fwd = std::getenv("SO3LR_B200_MIXED_FORWARD");
   mixed_tc_ = !(fwd && std::string(fwd) == "mma");
   SO3_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
@@ -119,18 +119,22 @@ void Evaluator::upload_weights() {
   struct FOff32 {
     std::size_t b0, bc1, v0, c0;
     std::pair<std::size_t, std::size_t> w0t, w1t, v1t, w1, v1, w0;
-    std::size_t tc_fwd;
+    std::size_t tc_fwd, tc_rev;
   };
   // [128 x 32] K-chunk c of a row-major [128 x K] matrix as TF32 hi and lo tiles
   // in the 128-byte-swizzled K-major layout (row n, column k at byte
   // 1024 (n / 8) + 128 (n % 8) + 16 ((k / 4) xor (n % 8)) + 4 (k % 4))
-  auto push_tc_chunks = [&](const std::vector<std::pair<const std::vector<double> *, int>> &chunks) {
+  struct TcChunk {
+    const std::vector<double> *m;  // row-major [rows x K]
+    int rows, c;                   // rows (128 or 32) and K-chunk index
+  };
+  auto push_tc_chunks = [&](const std::vector<TcChunk> &chunks) {
     std::vector<double> all;
     for (const auto &ch : chunks) {
-      const std::vector<double> &m = *ch.first;
-      const int K = int(m.size() / 128), c = ch.second;
-      std::vector<double> hi(128 * 32), lo(128 * 32);
-      for (int n = 0; n < 128; ++n)
+      const std::vector<double> &m = *ch.m;
+      const int rows = ch.rows, K = int(m.size() / std::size_t(rows)), c = ch.c;
+      std::vector<double> hi(std::size_t(rows) * 32), lo(std::size_t(rows) * 32);
+      for (int n = 0; n < rows; ++n)
         for (int k = 0; k < 32; ++k) {
           const double v = m[std::size_t(n) * K + 32 * c + k];
           const float h = tf32_round(float(v));
@@ -189,7 +193,19 @@ void Evaluator::upload_weights() {
     o32.w1 = push_split(fragment_major(iF, iF, [&](int oo, int j) { return w1[std::size_t(oo) * F + j]; }));
     o32.v1 = push_split(fragment_major(iF, iH, [&](int oo, int h) { return v1[std::size_t(oo) * H + h]; }));
     o32.w0 = push_split(fragment_major(iF, iR, [&](int j, int r) { return w0[std::size_t(j) * R + r]; }));
-    o32.tc_fwd = push_tc_chunks({{&w0, 0}, {&w1, 0}, {&w1, 1}, {&w1, 2}, {&w1, 3}, {&v1, 0}});
+    o32.tc_fwd = push_tc_chunks({{&w0, 128, 0}, {&w1, 128, 0}, {&w1, 128, 1}, {&w1, 128, 2}, {&w1, 128, 3},
+                                 {&v1, 128, 0}});
+    // reverse operands: W1^T [j][o], V1^T [h][o], W0^T [r][j]
+    std::vector<double> w1t(F * F), v1t(H * F), w0t(R * F);
+    for (std::size_t o = 0; o < F; ++o)
+      for (std::size_t j = 0; j < F; ++j) w1t[j * F + o] = w1[o * F + j];
+    for (std::size_t o = 0; o < F; ++o)
+      for (std::size_t h = 0; h < H; ++h) v1t[h * F + o] = v1[o * H + h];
+    for (std::size_t j = 0; j < F; ++j)
+      for (std::size_t r = 0; r < R; ++r) w0t[r * F + j] = w0[j * R + r];
+    o32.tc_rev = push_tc_chunks({{&w1t, 128, 0}, {&v1t, 32, 0}, {&w1t, 128, 1}, {&v1t, 32, 1},
+                                 {&w1t, 128, 2}, {&v1t, 32, 2}, {&w1t, 128, 3}, {&v1t, 32, 3},
+                                 {&w0t, 32, 0}, {&w0t, 32, 1}, {&w0t, 32, 2}, {&w0t, 32, 3}});
     return o;
   };
   for (int b = 0; b < layers_; ++b) {
@@ -336,7 +352,7 @@ void Evaluator::upload_weights() {
                      P32(f.w0t.first),  P32(f.w0t.second),  P32(f.w1t.first),   P32(f.w1t.second),
                      P32(f.v1t.first),  P32(f.v1t.second),  P32(f.w1.first),    P32(f.w1.second),
                      P32(f.v1.first),   P32(f.v1.second),   P32(f.w0.first),    P32(f.w0.second),
-                     P32(f.tc_fwd)};
+                     P32(f.tc_fwd),     P32(f.tc_rev)};
   };
   blocks_.resize(layers_);
   for (int b = 0; b < layers_; ++b) {
@@ -1132,7 +1148,13 @@ void Evaluator::compute() {
                              g_a_.get(), g_A_.get(), norm_, b > 0 ? g_qkv_.get() : nullptr, pair_sc_.get(),
                              g_filt_inv_.get(), g_filt_ev_.get(), s);
     prof_begin(kProfFilterReverse);
-    if (mixed_)
+    if (mixed_ && mixed_tc_)
+      launch_filter_reverse_tc(P, geo_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr, w.cg_att,
+                               w.finv, w.fev, w.finv32, w.fev32, g_filt_inv_.get(), g_filt_ev_.get(),
+                               reinterpret_cast<const float *>(sp_[b]->get()), drbf_.get(), g_A_.get(),
+                               pair_sc_.get(), b > 0, b < layers_ - 1, g_r_.get(), g_y_.get(), gl0_.get(), tc_err_,
+                               num_sms_, s);
+    else if (mixed_)
       launch_filter_reverse_mixed(P, geo_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr, w.cg_att,
                                   w.finv, w.fev, w.finv32, w.fev32, g_filt_inv_.get(), g_filt_ev_.get(),
                                   reinterpret_cast<const float *>(sp_[b]->get()), drbf_.get(), g_A_.get(),

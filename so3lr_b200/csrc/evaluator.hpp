@@ -262,7 +262,7 @@ class Evaluator {
   };
   bool profiling_ = false;
   bool mixed_ = false;
-  bool mixed_tc_ = true;           // mixed forward on tcgen05 (filter_tc.cu), else mma.sync
+  bool mixed_tc_ = true;           // mixed filters on tcgen05 (filter_tc.cu), else mma.sync
   int num_sms_ = 148;
   DeviceArray<int> tc_err_arr_;    // error word of the tcgen05 kernel
   int *tc_err_ = nullptr;

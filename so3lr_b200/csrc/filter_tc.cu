@@ -108,24 +108,29 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
   return uint64_t((saddr >> 4) & 0x3fff) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
          (uint64_t(2) << 61);
 }
-// kind::tf32, D float32, A and B TF32 K-major, M = 128, N = 128
-constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(128 >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+// kind::tf32, D float32, A and B TF32 K-major, M = 128, N = n
+constexpr uint32_t idesc_tf32(int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+}
+constexpr uint32_t kIdesc = idesc_tf32(128);
+constexpr uint32_t kIdesc32 = idesc_tf32(32);
 
-__device__ __forceinline__ void mma_tf32_tc(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+__device__ __forceinline__ void mma_tf32_tc(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                            uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate));
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
 }
 // D (+)= A B^T over one 32-wide K-chunk in three TF32 passes; A, B: hi tile then lo tile
 __device__ __forceinline__ void mma_chunk(uint32_t d_tmem, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi,
-                                          uint32_t b_lo, bool accumulate) {
+                                          uint32_t b_lo, bool accumulate, uint32_t idesc = kIdesc) {
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks) {
     const uint32_t o = 32u * ks;
-    mma_tf32_tc(d_tmem, smem_desc(a_lo + o), smem_desc(b_hi + o), (accumulate || ks > 0) ? 1u : 0u);
-    mma_tf32_tc(d_tmem, smem_desc(a_hi + o), smem_desc(b_lo + o), 1u);
-    mma_tf32_tc(d_tmem, smem_desc(a_hi + o), smem_desc(b_hi + o), 1u);
+    mma_tf32_tc(d_tmem, smem_desc(a_lo + o), smem_desc(b_hi + o), idesc, (accumulate || ks > 0) ? 1u : 0u);
+    mma_tf32_tc(d_tmem, smem_desc(a_hi + o), smem_desc(b_lo + o), idesc, 1u);
+    mma_tf32_tc(d_tmem, smem_desc(a_hi + o), smem_desc(b_hi + o), idesc, 1u);
   }
 }
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
@@ -147,6 +152,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 32 consecutive float32 columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  float a[16], b[16];
+  tmem_ld16(taddr, a);
+  tmem_ld16(taddr + 16, b);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    v[i] = a[i];
+    v[16 + i] = b[i];
+  }
 }
 
 __device__ __forceinline__ float tf32_hi(float x) {
@@ -434,6 +451,282 @@ void launch_filter_forward_tc(int P, const double *geo, const int *pair_a, const
   k_filter_forward_tc<<<grid, kTcThreads, kSmemTc, s>>>(P, ntiles, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad,
                                                         f_inv, f_ev, sp, drbf, err);
   SO3_LAUNCH("filter_forward_tc");
+}
+
+// ---------------------------------------------------------------------------
+// reverse on tcgen05: per tile of 128 pairs and per filter
+//   D_h = gF W1      (K = 128, N = 128)   TMEM columns   0..127
+//   D_w = gF V1      (K = 128, N = 32)                 128..159
+//   g_pre = D_h * silu'      (epilogue, split)
+//   D_r (+)= g_pre W0 (K = 128, N = 32)                160..191, summed over both filters
+// then, per pair, the radial gradient sum_k g_rbf[k] d rbf_k/dr + the cutoff
+// term, the harmonic gradient and the L0 gradient, as k_filter_reverse_mixed
+// finishes a pair (the L0 part g_pe = (gF V1) * silu'(L0 V0^T + c0) in float64).
+// Both filters are handled by one CTA, so the radial-basis gradient of the two
+// is summed in the TMEM accumulator instead of across a CTA pair.
+// Weight chunks (FilterW32::tc_rev): for k-chunk c = 0..3 a 40 KB group
+// [W1^T chunk hi | lo (16 KB each)][V1^T chunk hi | lo (4 KB each)], then for
+// c = 0..3 an 8 KB group [W0^T chunk hi | lo (4 KB each)].
+// ---------------------------------------------------------------------------
+namespace {
+constexpr uint32_t kTile32 = 32 * 32 * 4;            // one [32 x 32] float tile, 4 KB
+constexpr uint32_t kGrpE12 = 2 * kTile + 2 * kTile32;  // 40 KB
+constexpr uint32_t kGrpE3 = 2 * kTile32;              // 8 KB
+constexpr uint32_t kRevOffA = 0;                      // 2 slots x (hi, lo) of [128 x 32]
+constexpr uint32_t kRevOffB = kRevOffA + 4 * kTile;   // kBSlots x 40 KB
+constexpr uint32_t kRevOffBar = kRevOffB + kBSlots * kGrpE12;
+constexpr uint32_t kSmemTcRev = kRevOffBar + kNumBars * 8 + 16 + 1024;
+constexpr int kRFullB = 0, kREmptyB = 3, kRFullA = 6, kREmptyA = 8, kRDhwFull = 10, kRDhwFree = 11, kRDrFull = 12,
+              kRDrFree = 13, kRDrain = 14;
+}  // namespace
+
+__global__ void __launch_bounds__(kTcThreads, 1) k_filter_reverse_tc(
+    int P, int ntiles, const double *__restrict__ geo, const int *__restrict__ pa, const int *__restrict__ pb,
+    const double *__restrict__ ev, const double *__restrict__ cg, FilterW finv, FilterW fev, FilterW32 finv32,
+    FilterW32 fev32, const double *__restrict__ g_filt_inv, const double *__restrict__ g_filt_ev,
+    const float *__restrict__ sp, const double *__restrict__ drbf, const double *__restrict__ gA,
+    const double *__restrict__ pair_sc, int need_l0, int accumulate, double *__restrict__ g_r,
+    double *__restrict__ g_y, double *__restrict__ gl0, int *__restrict__ err) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  unsigned char *sm = smem_raw + (base - raw);
+  const uint32_t bars = base + kRevOffBar;
+  auto bar = [&](int i) { return bars + 8u * i; };
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kRevOffBar + kNumBars * 8);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + kRevOffBar + kNumBars * 8 + 4);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  if (tid == 0) {
+    for (int i = 0; i < 3; ++i) mbar_init(bar(kRFullB + i), 1);
+    for (int i = 0; i < 3; ++i) mbar_init(bar(kREmptyB + i), 1);
+    for (int i = 0; i < 2; ++i) mbar_init(bar(kRFullA + i), kTcEpiWarps);
+    for (int i = 0; i < 2; ++i) mbar_init(bar(kREmptyA + i), 1);
+    mbar_init(bar(kRDhwFull), 1);
+    mbar_init(bar(kRDhwFree), kTcEpiWarps);
+    mbar_init(bar(kRDrFull), 1);
+    mbar_init(bar(kRDrFree), kTcEpiWarps);
+    mbar_init(bar(kRDrain), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kTcEpiWarps) {  // D_h, D_w, D_r: 192 of 256 columns
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(tmem_slot)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+
+  if (warp == kTcEpiWarps) {
+    // ------------------------------------------------------------------ MMA warp
+    if (lane == 0) {
+      const int total = my_tiles * 16;  // per tile and filter: 4 (gF W1, gF V1) groups, 4 (g_pre W0) groups
+      int next_load = 0, landed = 0;
+      bool ok = true;
+      for (int g = 0; g < total && ok; ++g) {
+        while (ok && next_load < total && next_load <= g + kBSlots - 1) {
+          const int s = next_load % kBSlots, n = next_load / kBSlots;
+          ok = mbar_wait(bar(kREmptyB + s), (n & 1) ^ 1, abort_flag, err, 21);
+          if (!ok) break;
+          const int tf = next_load / 8, gi = next_load % 8;
+          const FilterW32 &W = (tf & 1) ? fev32 : finv32;
+          const uint32_t bytes = gi < 4 ? kGrpE12 : kGrpE3;
+          const size_t off = gi < 4 ? size_t(gi) * kGrpE12 : 4 * size_t(kGrpE12) + size_t(gi - 4) * kGrpE3;
+          mbar_expect_tx(bar(kRFullB + s), bytes);
+          bulk_load(base + kRevOffB + s * kGrpE12, reinterpret_cast<const char *>(W.tc_rev) + off, bytes,
+                    bar(kRFullB + s));
+          ++next_load;
+        }
+        if (!ok) break;
+        const int tf = g / 8, gi = g % 8, it = tf >> 1, f = tf & 1;
+        const int s = g % kBSlots;
+        const int use = tf * 8 + gi, slot = use & 1;  // A-ring use: gF chunks 0-3, then g_pre chunks 0-3
+        const uint32_t b0 = base + kRevOffB + s * kGrpE12;
+        ok = mbar_wait(bar(kRFullA + slot), (use >> 1) & 1, abort_flag, err, 22);
+        if (ok && gi == 0) ok = mbar_wait(bar(kRDhwFree), (tf & 1) ^ 1, abort_flag, err, 23);
+        if (ok && gi == 4 && f == 0) ok = mbar_wait(bar(kRDrFree), (it & 1) ^ 1, abort_flag, err, 24);
+        if (ok) ok = mbar_wait(bar(kRFullB + s), (g / kBSlots) & 1, abort_flag, err, 25);
+        if (!ok) break;
+        landed = g + 1;
+        tc_fence_after();
+        const uint32_t a_hi = base + kRevOffA + slot * 2 * kTile, a_lo = a_hi + kTile;
+        if (gi < 4) {
+          mma_chunk(tmem, a_hi, a_lo, b0, b0 + kTile, gi > 0);
+          mma_chunk(tmem + 128, a_hi, a_lo, b0 + 2 * kTile, b0 + 2 * kTile + kTile32, gi > 0, kIdesc32);
+          tc_commit(bar(kREmptyB + s));
+          tc_commit(bar(kREmptyA + slot));
+          if (gi == 3) tc_commit(bar(kRDhwFull));
+        } else {
+          mma_chunk(tmem + 160, a_hi, a_lo, b0, b0 + kTile32, !(f == 0 && gi == 4), kIdesc32);
+          tc_commit(bar(kREmptyB + s));
+          tc_commit(bar(kREmptyA + slot));
+          if (f == 1 && gi == 7) tc_commit(bar(kRDrFull));
+        }
+      }
+      tc_commit(bar(kRDrain));
+      mbar_wait(bar(kRDrain), 0, abort_flag, err, 27);
+      for (int i = landed; i < next_load; ++i) {
+        const long long t0 = clock64();
+        uint32_t d = 0;
+        while (!d && clock64() - t0 < kWaitCycles)
+          asm volatile(
+              "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+              " selp.u32 %0, 1, 0, p;\n}\n"
+              : "=r"(d)
+              : "r"(bar(kRFullB + i % kBSlots)), "r"(uint32_t((i / kBSlots) & 1))
+              : "memory");
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue warps
+    const int q = warp & 3, hh = warp >> 2;
+    const int row = 32 * q + lane;
+    const uint32_t lane_base = tmem + (uint32_t(32 * q) << 16);
+    bool ok = true;
+    for (int it = 0; it < my_tiles && ok; ++it) {
+      const int tile = int(blockIdx.x) + it * int(gridDim.x);
+      const int p = tile * kTcRows + row;
+      const bool valid = p < P;
+      const int t64 = p >> 6, r64 = p & 63;
+      double l0[4] = {0, 0, 0, 0}, gl[4] = {0, 0, 0, 0};
+      if (need_l0 && valid) {
+        const int a = pa[p], b = pb[p];
+        for (int m = 0; m < kEV; ++m) {
+          const double diff = ev[(size_t)b * kEV + m] - ev[(size_t)a * kEV + m];
+          l0[degree_of_channel(m)] += diff * diff * cg[m];
+        }
+      }
+      for (int f = 0; f < 2 && ok; ++f) {
+        const int tf = it * 2 + f;
+        const double *gsrc = f ? g_filt_ev : g_filt_inv;
+        // the filter gradient into the A ring, 32 columns at a time
+        for (int c = 0; c < 4 && ok; ++c) {
+          const int use = tf * 8 + c, slot = use & 1;
+          ok = __all_sync(0xffffffffu, mbar_wait(bar(kREmptyA + slot), ((use >> 1) & 1) ^ 1, abort_flag, err, 28));
+          if (!ok) break;
+          float v[16];
+          if (valid) {
+            const double2 *src = reinterpret_cast<const double2 *>(gsrc + (size_t)p * kF + 32 * c + 16 * hh);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const double2 x = __ldg(src + i);
+              v[2 * i] = float(x.x);
+              v[2 * i + 1] = float(x.y);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+          }
+          char *a_hi = reinterpret_cast<char *>(sm + kRevOffA + slot * 2 * kTile);
+          store_row16(a_hi, a_hi + kTile, row, hh, v);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(kRFullA + slot));
+        }
+        if (!ok) break;
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(kRDhwFull), tf & 1, abort_flag, err, 29));
+        if (!ok) break;
+        tc_fence_after();
+        if (need_l0) {  // L0 gradient of this filter (float64, as the float64 path)
+          float gw[32];
+          tmem_ld32(lane_base + 128, gw);
+          const double *v0 = f ? fev.v0 : finv.v0;
+          const double *c0 = f ? fev.c0 : finv.c0;
+#pragma unroll
+          for (int j = 0; j < kEH; ++j) {
+            const double pe = l0[0] * v0[j * 4] + l0[1] * v0[j * 4 + 1] + l0[2] * v0[j * 4 + 2] +
+                              l0[3] * v0[j * 4 + 3] + c0[j];
+            const double gpe = double(gw[j]) * silu_prime(pe);
+#pragma unroll
+            for (int d = 0; d < 4; ++d) gl[d] += gpe * v0[j * 4 + d];
+          }
+        }
+        // hidden pre-activation gradient g_pre = D_h * silu' into the A ring
+        for (int c = 0; c < 4 && ok; ++c) {
+          const int use = tf * 8 + 4 + c, slot = use & 1;
+          ok = __all_sync(0xffffffffu, mbar_wait(bar(kREmptyA + slot), ((use >> 1) & 1) ^ 1, abort_flag, err, 30));
+          if (!ok) break;
+          float v[16];
+          tmem_ld16(lane_base + 32 * c + 16 * hh, v);
+          const int col0 = 32 * c + 16 * hh;
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            const float2 sv = __ldg(reinterpret_cast<const float2 *>(sp + sp_index(t64, f, r64, col0 + i)));
+            v[i] *= sv.x;
+            v[i + 1] *= sv.y;
+          }
+          char *a_hi = reinterpret_cast<char *>(sm + kRevOffA + slot * 2 * kTile);
+          store_row16(a_hi, a_hi + kTile, row, hh, v);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(kRFullA + slot));
+        }
+        if (!ok) break;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kRDhwFree));
+      }
+      if (!ok) break;
+      // finish the pairs: radial, cutoff, harmonic and L0 gradients
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(kRDrFull), it & 1, abort_flag, err, 31));
+      if (!ok) break;
+      tc_fence_after();
+      float grb[32];
+      tmem_ld32(lane_base + 160, grb);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kRDrFree));
+      if (valid) {
+        const double *sc = pair_sc + (size_t)p * kPairScalars;
+        const double dphi = geo[(size_t)p * kGeo + 5], phi = geo[(size_t)p * kGeo + 4];
+        if (hh == 0) {
+          double gr = 0.0;
+          const double *dr = drbf + (size_t)p * kR;
+#pragma unroll
+          for (int k = 0; k < kR; ++k) gr += double(grb[k]) * dr[k];
+          gr += __dmul_rn(sc[0], dphi);  // cutoff gradient (its weight is orientation-independent)
+          g_r[p] = accumulate ? g_r[p] + gr : gr;
+          if (need_l0)
+            for (int d = 0; d < 4; ++d) gl0[(size_t)p * 4 + d] = gl[d];
+        }
+        const int a = pa[p], b = pb[p];
+        for (int m = 12 * hh; m < 12 * hh + 12; ++m) {
+          const int d = degree_of_channel(m);
+          const double y = __dmul_rn(phi, __dadd_rn(__dmul_rn(sc[1 + d], gA[(size_t)a * kEV + m]),
+                                                    parity_sign(d) * __dmul_rn(sc[5 + d], gA[(size_t)b * kEV + m])));
+          double *dst = g_y + (size_t)p * kEV + m;
+          *dst = accumulate ? *dst + y : y;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kTcEpiWarps) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+  }
+}
+
+void launch_filter_reverse_tc(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
+                              const double *cg_att, const FilterW &finv, const FilterW &fev, const FilterW32 &finv32,
+                              const FilterW32 &fev32, const double *g_filt_inv, const double *g_filt_ev,
+                              const float *sp, const double *drbf, const double *gA, const double *pair_sc,
+                              bool need_l0, bool accumulate, double *g_r, double *g_y, double *gl0, int *err,
+                              int num_sms, cudaStream_t s) {
+  if (P == 0) return;
+  const int ntiles = (P + kTcRows - 1) / kTcRows;
+  allow_dynamic_smem(reinterpret_cast<const void *>(k_filter_reverse_tc), kSmemTcRev);
+  const int grid = std::min(ntiles, std::max(1, num_sms));
+  k_filter_reverse_tc<<<grid, kTcThreads, kSmemTcRev, s>>>(P, ntiles, geo, pair_a, pair_b, ev, cg_att, finv, fev,
+                                                           finv32, fev32, g_filt_inv, g_filt_ev, sp, drbf, gA,
+                                                           pair_sc, need_l0 ? 1 : 0, accumulate ? 1 : 0, g_r, g_y,
+                                                           gl0, err);
+  SO3_LAUNCH("filter_reverse_tc");
 }
 
 }  // namespace so3lr_b200

@@ -447,10 +447,11 @@ def test_gpu_mixed_precision_refuses_unknown_mode(gpu_model):
     assert So3lrError is not None
 
 
-def test_gpu_mixed_tensor_core_forward_matches_mma_forward(monkeypatch):
-    """The mixed mode's filter forward on the tcgen05 tensor cores (default)
-    and on warp-level mma.sync (SO3LR_B200_MIXED_FORWARD=mma) form the same
-    three-pass TF32 products, so they differ only by float32 summation order:
+def test_gpu_mixed_tensor_core_kernels_match_mma_kernels(monkeypatch):
+    """The mixed mode's filter kernels (forward and reverse) on the tcgen05
+    tensor cores (default) and on warp-level mma.sync
+    (SO3LR_B200_MIXED_FORWARD=mma) form the same three-pass TF32 products, so
+    they differ only by float32 summation order:
     forces within 2e-5 eV/A, energies within 1e-6 eV/atom, on a periodic box
     whose pair count is not a multiple of the 128-pair tile, and on a charged
     open cluster."""
