@@ -200,38 +200,79 @@ __device__ __forceinline__ size_t sp_index(int t64, int filt, int row, int col) 
 
 }  // namespace
 
-__global__ void __launch_bounds__(kTcThreads, 1) k_filter_forward_tc(
+// Forward pipeline. Epilogue warps 0-15: warp w owns TMEM lanes 32 (w % 4)
+// .. + 31 (its 32 pairs) and columns 8 (w / 4) .. + 7 of every 32-column
+// chunk; warp 16 (one lane) loads weights and issues MMAs. The layer-2
+// accumulator D2 has two buffers (TMEM columns 128-255 and 256-383), so the
+// MMAs of the next (tile, filter) run while the epilogue writes the outputs of
+// the current one; the next operands (rbf, w) are built before that.
+namespace {
+constexpr int kFwdEpiWarps = 16;
+constexpr int kFwdThreads = (kFwdEpiWarps + 1) * 32;
+constexpr int kFwdBars = 18;
+constexpr uint32_t kSmemFwd = kOffBar + kFwdBars * 8 + 16 + 1024;
+constexpr int kFFullB = 0, kFEmptyB = 3, kFFullA = 6, kFEmptyA = 8, kFOpnd = 10, kFD1Full = 11, kFD2Full = 12,
+              kFD1Free = 14, kFD2Free = 15, kFDrain = 17;
+
+// 8 consecutive float32 columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+// 8 values of row `row`, columns 8 part .. + 7 of a [128 x 32] tile pair (hi, lo)
+__device__ __forceinline__ void store_row8(char *hi_tile, char *lo_tile, int row, int part, const float (&v)[8]) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int chunk = (2 * part + q) ^ (row & 7);
+    const uint32_t off = (row >> 3) * 1024 + (row & 7) * 128 + chunk * 16;
+    float h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      h[e] = tf32_hi(v[4 * q + e]);
+      l[e] = tf32_hi(v[4 * q + e] - h[e]);
+    }
+    *reinterpret_cast<float4 *>(hi_tile + off) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4 *>(lo_tile + off) = make_float4(l[0], l[1], l[2], l[3]);
+  }
+}
+}  // namespace
+
+__global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
     int P, int ntiles, const double *__restrict__ geo, const int *__restrict__ pa, const int *__restrict__ pb,
     const double *__restrict__ ev, const double *__restrict__ cg, FilterW32 finv, FilterW32 fev, RadialW rad,
     double *__restrict__ f_inv, double *__restrict__ f_ev, float *__restrict__ sp, double *__restrict__ drbf,
     int *__restrict__ err) {
   extern __shared__ unsigned char smem_raw[];
-  // 1024-byte alignment for the swizzled operand tiles
   const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t base = (raw + 1023u) & ~1023u;  // 1024-byte alignment for the swizzled tiles
   unsigned char *sm = smem_raw + (base - raw);
   const uint32_t bars = base + kOffBar;
   auto bar = [&](int i) { return bars + 8u * i; };
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kOffBar + kNumBars * 8);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + kOffBar + kNumBars * 8 + 4);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kOffBar + kFwdBars * 8);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + kOffBar + kFwdBars * 8 + 4);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
-    for (int i = 0; i < 3; ++i) mbar_init(bar(kFullB + i), 1);
-    for (int i = 0; i < 3; ++i) mbar_init(bar(kEmptyB + i), 1);
-    for (int i = 0; i < 2; ++i) mbar_init(bar(kFullA + i), kTcEpiWarps);
-    for (int i = 0; i < 2; ++i) mbar_init(bar(kEmptyA + i), 1);
-    mbar_init(bar(kOpnd), kTcEpiWarps);
-    mbar_init(bar(kD1Full), 1);
-    mbar_init(bar(kD2Full), 1);
-    mbar_init(bar(kD1Free), kTcEpiWarps);
-    mbar_init(bar(kD2Free), kTcEpiWarps);
-    mbar_init(bar(kDrain), 1);
+    for (int i = 0; i < 3; ++i) mbar_init(bar(kFFullB + i), 1);
+    for (int i = 0; i < 3; ++i) mbar_init(bar(kFEmptyB + i), 1);
+    for (int i = 0; i < 2; ++i) mbar_init(bar(kFFullA + i), kFwdEpiWarps);
+    for (int i = 0; i < 2; ++i) mbar_init(bar(kFEmptyA + i), 1);
+    mbar_init(bar(kFOpnd), kFwdEpiWarps);
+    mbar_init(bar(kFD1Full), 1);
+    for (int i = 0; i < 2; ++i) mbar_init(bar(kFD2Full + i), 1);
+    mbar_init(bar(kFD1Free), kFwdEpiWarps);
+    for (int i = 0; i < 2; ++i) mbar_init(bar(kFD2Free + i), kFwdEpiWarps);
+    mbar_init(bar(kFDrain), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == kTcEpiWarps) {  // the MMA warp owns the TMEM allocation: D1 and D2, 128 columns each
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(tmem_slot)));
+  if (warp == kFwdEpiWarps) {  // the MMA warp owns the TMEM: D1 (128 columns), two D2 buffers (128 each)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -239,61 +280,63 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_filter_forward_tc(
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+  const int total_tf = 2 * my_tiles;  // (tile, filter) steps of this CTA
 
-  if (warp == kTcEpiWarps) {
+  if (warp == kFwdEpiWarps) {
     // ------------------------------------------------------------------ MMA warp
     if (lane == 0) {
-      const int total = my_tiles * 12;  // 6 weight chunks (MMA groups) per tile and filter
-      int next_load = 0, landed = 0;     // loads issued; loads waited for (their MMAs issued)
+      const int total = total_tf * 6;  // 6 weight chunks (MMA groups) per (tile, filter)
+      int next_load = 0, landed = 0;
       bool ok = true;
       for (int g = 0; g < total && ok; ++g) {
-        // keep up to kBSlots weight chunks in flight
-        while (ok && next_load < total && next_load <= g + kBSlots - 1) {
+        while (ok && next_load < total && next_load <= g + kBSlots - 1) {  // up to kBSlots chunks in flight
           const int s = next_load % kBSlots, n = next_load / kBSlots;
-          ok = mbar_wait(bar(kEmptyB + s), (n & 1) ^ 1, abort_flag, err, 1);
+          ok = mbar_wait(bar(kFEmptyB + s), (n & 1) ^ 1, abort_flag, err, 1);
           if (!ok) break;
           const int tf = next_load / 6, gi = next_load % 6;
           const FilterW32 &W = (tf & 1) ? fev : finv;
-          mbar_expect_tx(bar(kFullB + s), 2 * kTile);
-          bulk_load(base + kOffB + s * 2 * kTile, W.tc_fwd + size_t(gi) * (2 * kTile / 4), 2 * kTile, bar(kFullB + s));
+          mbar_expect_tx(bar(kFFullB + s), 2 * kTile);
+          bulk_load(base + kOffB + s * 2 * kTile, W.tc_fwd + size_t(gi) * (2 * kTile / 4), 2 * kTile,
+                    bar(kFFullB + s));
           ++next_load;
         }
         if (!ok) break;
-        const int tf = g / 6, gi = g % 6;  // (tile, filter) index and group within it
+        const int tf = g / 6, gi = g % 6, d2b = tf & 1, d2use = tf >> 1;
         const int s = g % kBSlots;
         const uint32_t b_hi = base + kOffB + s * 2 * kTile, b_lo = b_hi + kTile;
+        const uint32_t d2 = tmem + 128 + 128 * d2b;
         if (gi == 0) {
-          ok = mbar_wait(bar(kOpnd), tf & 1, abort_flag, err, 2) &&
-               mbar_wait(bar(kD1Free), (tf & 1) ^ 1, abort_flag, err, 3);
+          ok = mbar_wait(bar(kFOpnd), tf & 1, abort_flag, err, 2) &&
+               mbar_wait(bar(kFD1Free), (tf & 1) ^ 1, abort_flag, err, 3);
         } else if (gi <= 4) {
           const int c = gi - 1, slot = c & 1, use = tf * 2 + (c >> 1);
-          ok = mbar_wait(bar(kFullA + slot), use & 1, abort_flag, err, 4);
-          if (ok && c == 0) ok = mbar_wait(bar(kD2Free), (tf & 1) ^ 1, abort_flag, err, 5);
+          ok = mbar_wait(bar(kFFullA + slot), use & 1, abort_flag, err, 4);
+          if (ok && c == 0) ok = mbar_wait(bar(kFD2Free + d2b), (d2use & 1) ^ 1, abort_flag, err, 5);
         }
-        if (ok) ok = mbar_wait(bar(kFullB + s), (g / kBSlots) & 1, abort_flag, err, 6);
+        if (ok) ok = mbar_wait(bar(kFFullB + s), (g / kBSlots) & 1, abort_flag, err, 6);
         if (!ok) break;
         landed = g + 1;
         tc_fence_after();
         if (gi == 0) {
           mma_chunk(tmem, base + kOffA1, base + kOffA1 + kTile, b_hi, b_lo, false);
-          tc_commit(bar(kEmptyB + s));
-          tc_commit(bar(kD1Full));
+          tc_commit(bar(kFEmptyB + s));
+          tc_commit(bar(kFD1Full));
         } else if (gi <= 4) {
           const int c = gi - 1, slot = c & 1;
           const uint32_t a_hi = base + kOffA2 + slot * 2 * kTile;
-          mma_chunk(tmem + 128, a_hi, a_hi + kTile, b_hi, b_lo, c > 0);
-          tc_commit(bar(kEmptyB + s));
-          tc_commit(bar(kEmptyA + slot));
+          mma_chunk(d2, a_hi, a_hi + kTile, b_hi, b_lo, c > 0);
+          tc_commit(bar(kFEmptyB + s));
+          tc_commit(bar(kFEmptyA + slot));
         } else {
-          mma_chunk(tmem + 128, base + kOffA3, base + kOffA3 + kTile, b_hi, b_lo, true);
-          tc_commit(bar(kEmptyB + s));
-          tc_commit(bar(kD2Full));
+          mma_chunk(d2, base + kOffA3, base + kOffA3 + kTile, b_hi, b_lo, true);
+          tc_commit(bar(kFEmptyB + s));
+          tc_commit(bar(kFD2Full + d2b));
         }
       }
-      // teardown: every MMA this thread issued has completed and, after a wait
-      // that gave up, every weight copy still in flight has landed (bounded)
-      tc_commit(bar(kDrain));
-      mbar_wait(bar(kDrain), 0, abort_flag, err, 7);
+      // teardown: every MMA issued has completed and, after a wait that gave
+      // up, every weight copy still in flight has landed (bounded)
+      tc_commit(bar(kFDrain));
+      mbar_wait(bar(kFDrain), 0, abort_flag, err, 7);
       for (int i = landed; i < next_load; ++i) {
         const long long t0 = clock64();
         uint32_t d = 0;
@@ -302,138 +345,143 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_filter_forward_tc(
               "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
               " selp.u32 %0, 1, 0, p;\n}\n"
               : "=r"(d)
-              : "r"(bar(kFullB + i % kBSlots)), "r"(uint32_t((i / kBSlots) & 1))
+              : "r"(bar(kFFullB + i % kBSlots)), "r"(uint32_t((i / kBSlots) & 1))
               : "memory");
       }
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue warps
-    const int q = warp & 3, hh = warp >> 2;
+    const int q = warp & 3, part = warp >> 2;
     const int row = 32 * q + lane;
     const uint32_t lane_base = tmem + (uint32_t(32 * q) << 16);
     double l0[4] = {0, 0, 0, 0};
-    bool ok = true;
-    for (int it = 0; it < my_tiles && ok; ++it) {
-      const int tile = int(blockIdx.x) + it * int(gridDim.x);
-      const int p = tile * kTcRows + row;
+    // operands of (tile, filter) step tf: rbf into A1 (first filter of a tile), w into A3
+    auto prepare = [&](int tf) {
+      const int f = tf & 1;
+      const int p = (int(blockIdx.x) + (tf >> 1) * int(gridDim.x)) * kTcRows + row;
       const bool valid = p < P;
-      for (int f = 0; f < 2 && ok; ++f) {
-        const int tf = it * 2 + f;
-        const FilterW32 &W = f ? fev : finv;
-        double *out = f ? f_ev : f_inv;
-        if (f == 0) {
-          // radial basis (float64, as the float64 path) into A1, d rbf/dr, and L0
-          const double r = valid ? geo[(size_t)p * kGeo] : 1.0;
-          const double raw_x = exp(-rad.gamma * r);
-          double x = raw_x;
-          if (x < 1.0e-6) x = 1.0e-6;
-          if (x > 1.0 - 1.0e-6) x = 1.0 - 1.0e-6;
-          const double lx = log(x), l1x = log(1.0 - x);
-          const bool live = raw_x > 1.0e-6 && raw_x < 1.0 - 1.0e-6;
-          const double ratio = live ? raw_x / (1.0 - raw_x) : 0.0;
-          float v[16];
-          double d[16];
+      if (f == 0) {
+        const double r = valid ? geo[(size_t)p * kGeo] : 1.0;
+        const double raw_x = exp(-rad.gamma * r);
+        double x = raw_x;
+        if (x < 1.0e-6) x = 1.0e-6;
+        if (x > 1.0 - 1.0e-6) x = 1.0 - 1.0e-6;
+        const double lx = log(x), l1x = log(1.0 - x);
+        const bool live = raw_x > 1.0e-6 && raw_x < 1.0 - 1.0e-6;
+        const double ratio = live ? raw_x / (1.0 - raw_x) : 0.0;
+        float v[8];
+        double d[8];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int k = 16 * hh + i;
-            const double b = exp_tang(rad.b[k] + rad.k[k] * lx + rad.kr[k] * l1x);
-            v[i] = float(b);
-            d[i] = live ? b * (-rad.gamma * rad.k[k] + rad.gamma * rad.kr[k] * ratio) : 0.0;
-          }
-          store_row16(reinterpret_cast<char *>(sm + kOffA1), reinterpret_cast<char *>(sm + kOffA1 + kTile), row, hh,
-                      v);
-          if (drbf != nullptr && valid) {
-            double2 *dst = reinterpret_cast<double2 *>(drbf + (size_t)p * kR + 16 * hh);
+        for (int i = 0; i < 8; ++i) {
+          const int k = 8 * part + i;
+          const double b = exp_tang(rad.b[k] + rad.k[k] * lx + rad.kr[k] * l1x);
+          v[i] = float(b);
+          d[i] = live ? b * (-rad.gamma * rad.k[k] + rad.gamma * rad.kr[k] * ratio) : 0.0;
+        }
+        store_row8(reinterpret_cast<char *>(sm + kOffA1), reinterpret_cast<char *>(sm + kOffA1 + kTile), row, part,
+                   v);
+        if (drbf != nullptr && valid) {
+          double2 *dst = reinterpret_cast<double2 *>(drbf + (size_t)p * kR + 8 * part);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) dst[i] = make_double2(d[2 * i], d[2 * i + 1]);
-          }
-          l0[0] = l0[1] = l0[2] = l0[3] = 0.0;
-          if (ev != nullptr && valid) {
-            const int a = pa[p], b = pb[p];
-            for (int m = 0; m < kEV; ++m) {
-              const double diff = ev[(size_t)b * kEV + m] - ev[(size_t)a * kEV + m];
-              l0[degree_of_channel(m)] += diff * diff * cg[m];
-            }
+          for (int i = 0; i < 4; ++i) dst[i] = make_double2(d[2 * i], d[2 * i + 1]);
+        }
+        l0[0] = l0[1] = l0[2] = l0[3] = 0.0;
+        if (ev != nullptr && valid) {
+          const int a = pa[p], b = pb[p];
+#pragma unroll
+          for (int m = 0; m < kEV; ++m) {
+            const double diff = ev[(size_t)b * kEV + m] - ev[(size_t)a * kEV + m];
+            l0[degree_of_channel(m)] += diff * diff * cg[m];
           }
         }
-        {  // ev branch hidden layer w = silu(L0 V0^T + c0) into A3
-          float v[16];
+      }
+      const FilterW32 &W = f ? fev : finv;
+      float v[8];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int j = 16 * hh + i;
-            const float s = float(l0[0]) * W.v0[j * 4] + float(l0[1]) * W.v0[j * 4 + 1] +
-                            float(l0[2]) * W.v0[j * 4 + 2] + float(l0[3]) * W.v0[j * 4 + 3] + W.c0[j];
-            v[i] = s * sigmoid_fast(s);
-          }
-          store_row16(reinterpret_cast<char *>(sm + kOffA3), reinterpret_cast<char *>(sm + kOffA3 + kTile), row, hh,
-                      v);
+      for (int i = 0; i < 8; ++i) {
+        const int j = 8 * part + i;
+        const float s = float(l0[0]) * W.v0[j * 4] + float(l0[1]) * W.v0[j * 4 + 1] + float(l0[2]) * W.v0[j * 4 + 2] +
+                        float(l0[3]) * W.v0[j * 4 + 3] + W.c0[j];
+        v[i] = s * sigmoid_fast(s);
+      }
+      store_row8(reinterpret_cast<char *>(sm + kOffA3), reinterpret_cast<char *>(sm + kOffA3 + kTile), row, part, v);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kFOpnd));
+    };
+
+    bool ok = true;
+    if (total_tf > 0) prepare(0);
+    for (int tf = 0; tf < total_tf && ok; ++tf) {
+      const int f = tf & 1, d2b = tf & 1, d2use = tf >> 1;
+      const int p = (int(blockIdx.x) + (tf >> 1) * int(gridDim.x)) * kTcRows + row;
+      const bool valid = p < P;
+      const FilterW32 &W = f ? fev : finv;
+      double *out = f ? f_ev : f_inv;
+      // hidden layer: D1 + b0 -> silu, in 32-column chunks through the hidden ring
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(kFD1Full), tf & 1, abort_flag, err, 8));
+      if (!ok) break;
+      tc_fence_after();
+      for (int c = 0; c < 4 && ok; ++c) {
+        const int slot = c & 1, use = tf * 2 + (c >> 1);
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(kFEmptyA + slot), (use & 1) ^ 1, abort_flag, err, 9));
+        if (!ok) break;
+        const int col0 = 32 * c + 8 * part;
+        float v[8], u[8];
+        tmem_ld8(lane_base + col0, v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float x = v[i] + W.b0[col0 + i];
+          const float sg = sigmoid_fast(x);
+          u[i] = x * sg;
+          v[i] = sg * (1.0f + x * (1.0f - sg));  // silu'
+        }
+        char *a_hi = reinterpret_cast<char *>(sm + kOffA2 + slot * 2 * kTile);
+        store_row8(a_hi, a_hi + kTile, row, part, u);
+        {  // every row of the tile, as the mma.sync forward writes them (finite values past P)
+          const int t64 = p >> 6, r64 = p & 63;
+#pragma unroll
+          for (int i = 0; i < 8; i += 2)
+            *reinterpret_cast<float2 *>(sp + sp_index(t64, f, r64, col0 + i)) = make_float2(v[i], v[i + 1]);
         }
         fence_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(kOpnd));
-        // hidden layer: D1 + b0 -> silu, in 32-column chunks through the hidden ring
-        ok = __all_sync(0xffffffffu, mbar_wait(bar(kD1Full), tf & 1, abort_flag, err, 8));
-        if (!ok) break;
-        tc_fence_after();
-        for (int c = 0; c < 4 && ok; ++c) {
-          const int slot = c & 1, use = tf * 2 + (c >> 1);
-          ok = __all_sync(0xffffffffu, mbar_wait(bar(kEmptyA + slot), (use & 1) ^ 1, abort_flag, err, 9));
-          if (!ok) break;
-          float v[16];
-          tmem_ld16(lane_base + 32 * c + 16 * hh, v);
-          const int col0 = 32 * c + 16 * hh;
-          float u[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float x = v[i] + W.b0[col0 + i];
-            const float s = sigmoid_fast(x);
-            u[i] = x * s;
-            v[i] = s * (1.0f + x * (1.0f - s));  // silu'
-          }
-          char *a_hi = reinterpret_cast<char *>(sm + kOffA2 + slot * 2 * kTile);
-          store_row16(a_hi, a_hi + kTile, row, hh, u);
-          {  // every row of the tile, as the mma.sync forward writes them (finite values past P)
-            const int t64 = p >> 6, r64 = p & 63;
-#pragma unroll
-            for (int i = 0; i < 16; i += 2)
-              *reinterpret_cast<float2 *>(sp + sp_index(t64, f, r64, col0 + i)) = make_float2(v[i], v[i + 1]);
-          }
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(kFullA + slot));
-        }
-        if (!ok) break;
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(kD1Free));
-        // output: D2 + b1 + c1 in float64
-        ok = __all_sync(0xffffffffu, mbar_wait(bar(kD2Full), tf & 1, abort_flag, err, 10));
-        if (!ok) break;
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float v[16];
-          tmem_ld16(lane_base + 128 + 32 * c + 16 * hh, v);
-          const int col0 = 32 * c + 16 * hh;
-          if (valid) {
-            double2 *dst = reinterpret_cast<double2 *>(out + (size_t)p * kF + col0);
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              dst[i] = make_double2(double(v[2 * i] + W.bc1[col0 + 2 * i]), double(v[2 * i + 1] + W.bc1[col0 + 2 * i + 1]));
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(kD2Free));
+        if (lane == 0) mbar_arrive(bar(kFFullA + slot));
       }
+      if (!ok) break;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kFD1Free));
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(kFD2Full + d2b), d2use & 1, abort_flag, err, 10));
+      if (!ok) break;
+      tc_fence_after();
+      // the next step's operands first (A1 and A3 are free: every MMA of this
+      // step has completed), so its MMAs overlap the output writes below
+      if (tf + 1 < total_tf) prepare(tf + 1);
+      // output: D2 + b1 + c1 in float64
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        const int col0 = 32 * c + 8 * part;
+        float v[8];
+        tmem_ld8(lane_base + 128 + 128 * d2b + col0, v);
+        if (valid) {
+          double2 *dst = reinterpret_cast<double2 *>(out + (size_t)p * kF + col0);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_double2(double(v[2 * i] + W.bc1[col0 + 2 * i]), double(v[2 * i + 1] + W.bc1[col0 + 2 * i + 1]));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kFD2Free + d2b));
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kTcEpiWarps) {
+  if (warp == kFwdEpiWarps) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
   }
 }
 
@@ -446,9 +494,9 @@ void launch_filter_forward_tc(int P, const double *geo, const int *pair_a, const
                               cudaStream_t s) {
   if (P == 0) return;
   const int ntiles = (P + kTcRows - 1) / kTcRows;
-  allow_dynamic_smem(reinterpret_cast<const void *>(k_filter_forward_tc), kSmemTc);
+  allow_dynamic_smem(reinterpret_cast<const void *>(k_filter_forward_tc), kSmemFwd);
   const int grid = std::min(ntiles, std::max(1, num_sms));
-  k_filter_forward_tc<<<grid, kTcThreads, kSmemTc, s>>>(P, ntiles, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad,
+  k_filter_forward_tc<<<grid, kFwdThreads, kSmemFwd, s>>>(P, ntiles, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad,
                                                         f_inv, f_ev, sp, drbf, err);
   SO3_LAUNCH("filter_forward_tc");
 }
@@ -472,15 +520,20 @@ namespace {
 constexpr uint32_t kTile32 = 32 * 32 * 4;            // one [32 x 32] float tile, 4 KB
 constexpr uint32_t kGrpE12 = 2 * kTile + 2 * kTile32;  // 40 KB
 constexpr uint32_t kGrpE3 = 2 * kTile32;              // 8 KB
+constexpr int kRevEpiWarps = 16;                      // 4 per TMEM lane quarter, 8 columns of each chunk
+constexpr int kRevThreads = (kRevEpiWarps + 1) * 32;
 constexpr uint32_t kRevOffA = 0;                      // 2 slots x (hi, lo) of [128 x 32]
 constexpr uint32_t kRevOffB = kRevOffA + 4 * kTile;   // kBSlots x 40 KB
-constexpr uint32_t kRevOffBar = kRevOffB + kBSlots * kGrpE12;
-constexpr uint32_t kSmemTcRev = kRevOffBar + kNumBars * 8 + 16 + 1024;
+constexpr uint32_t kRevRed = kRevOffB + kBSlots * kGrpE12;  // 2 x [4 parts][128 rows][5] doubles
+constexpr uint32_t kRevRedBytes = 4 * 128 * 5 * 8;
+constexpr uint32_t kRevOffBar = kRevRed + 2 * kRevRedBytes;
+constexpr int kRevBars = 19;
+constexpr uint32_t kSmemTcRev = kRevOffBar + kRevBars * 8 + 16 + 1024;
 constexpr int kRFullB = 0, kREmptyB = 3, kRFullA = 6, kREmptyA = 8, kRDhwFull = 10, kRDhwFree = 11, kRDrFull = 12,
-              kRDrFree = 13, kRDrain = 14;
+              kRDrFree = 13, kRDrain = 14, kRRed = 15;  // kRRed + q: the 4 warps of row quarter q
 }  // namespace
 
-__global__ void __launch_bounds__(kTcThreads, 1) k_filter_reverse_tc(
+__global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
     int P, int ntiles, const double *__restrict__ geo, const int *__restrict__ pa, const int *__restrict__ pb,
     const double *__restrict__ ev, const double *__restrict__ cg, FilterW finv, FilterW fev, FilterW32 finv32,
     FilterW32 fev32, const double *__restrict__ g_filt_inv, const double *__restrict__ g_filt_ev,
@@ -493,24 +546,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_filter_reverse_tc(
   unsigned char *sm = smem_raw + (base - raw);
   const uint32_t bars = base + kRevOffBar;
   auto bar = [&](int i) { return bars + 8u * i; };
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kRevOffBar + kNumBars * 8);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + kRevOffBar + kNumBars * 8 + 4);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + kRevOffBar + kRevBars * 8);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + kRevOffBar + kRevBars * 8 + 4);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
     for (int i = 0; i < 3; ++i) mbar_init(bar(kRFullB + i), 1);
     for (int i = 0; i < 3; ++i) mbar_init(bar(kREmptyB + i), 1);
-    for (int i = 0; i < 2; ++i) mbar_init(bar(kRFullA + i), kTcEpiWarps);
+    for (int i = 0; i < 2; ++i) mbar_init(bar(kRFullA + i), kRevEpiWarps);
     for (int i = 0; i < 2; ++i) mbar_init(bar(kREmptyA + i), 1);
     mbar_init(bar(kRDhwFull), 1);
-    mbar_init(bar(kRDhwFree), kTcEpiWarps);
+    mbar_init(bar(kRDhwFree), kRevEpiWarps);
     mbar_init(bar(kRDrFull), 1);
-    mbar_init(bar(kRDrFree), kTcEpiWarps);
+    mbar_init(bar(kRDrFree), kRevEpiWarps);
     mbar_init(bar(kRDrain), 1);
+    for (int i = 0; i < 4; ++i) mbar_init(bar(kRRed + i), 4);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == kTcEpiWarps) {  // D_h, D_w, D_r: 192 of 256 columns
+  if (warp == kRevEpiWarps) {  // D_h, D_w, D_r: 192 of 256 columns
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(tmem_slot)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
@@ -520,7 +574,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_filter_reverse_tc(
   const uint32_t tmem = *tmem_slot;
   const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
 
-  if (warp == kTcEpiWarps) {
+  if (warp == kRevEpiWarps) {
     // ------------------------------------------------------------------ MMA warp
     if (lane == 0) {
       const int total = my_tiles * 16;  // per tile and filter: 4 (gF W1, gF V1) groups, 4 (g_pre W0) groups
@@ -583,7 +637,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_filter_reverse_tc(
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue warps
-    const int q = warp & 3, hh = warp >> 2;
+    // warp w: TMEM lanes 32 (w % 4) .. + 31 (its 32 pairs), columns
+    // 8 (w / 4) .. + 7 of every 32-column chunk
+    const int q = warp & 3, part = warp >> 2;
     const int row = 32 * q + lane;
     const uint32_t lane_base = tmem + (uint32_t(32 * q) << 16);
     bool ok = true;
@@ -595,6 +651,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_filter_reverse_tc(
       double l0[4] = {0, 0, 0, 0}, gl[4] = {0, 0, 0, 0};
       if (need_l0 && valid) {
         const int a = pa[p], b = pb[p];
+#pragma unroll
         for (int m = 0; m < kEV; ++m) {
           const double diff = ev[(size_t)b * kEV + m] - ev[(size_t)a * kEV + m];
           l0[degree_of_channel(m)] += diff * diff * cg[m];
@@ -608,21 +665,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_filter_reverse_tc(
           const int use = tf * 8 + c, slot = use & 1;
           ok = __all_sync(0xffffffffu, mbar_wait(bar(kREmptyA + slot), ((use >> 1) & 1) ^ 1, abort_flag, err, 28));
           if (!ok) break;
-          float v[16];
+          float v[8];
           if (valid) {
-            const double2 *src = reinterpret_cast<const double2 *>(gsrc + (size_t)p * kF + 32 * c + 16 * hh);
+            const double2 *src = reinterpret_cast<const double2 *>(gsrc + (size_t)p * kF + 32 * c + 8 * part);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int i = 0; i < 4; ++i) {
               const double2 x = __ldg(src + i);
               v[2 * i] = float(x.x);
               v[2 * i + 1] = float(x.y);
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+            for (int i = 0; i < 8; ++i) v[i] = 0.0f;
           }
           char *a_hi = reinterpret_cast<char *>(sm + kRevOffA + slot * 2 * kTile);
-          store_row16(a_hi, a_hi + kTile, row, hh, v);
+          store_row8(a_hi, a_hi + kTile, row, part, v);
           fence_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(kRFullA + slot));
@@ -631,16 +688,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_filter_reverse_tc(
         ok = __all_sync(0xffffffffu, mbar_wait(bar(kRDhwFull), tf & 1, abort_flag, err, 29));
         if (!ok) break;
         tc_fence_after();
-        if (need_l0) {  // L0 gradient of this filter (float64, as the float64 path)
-          float gw[32];
-          tmem_ld32(lane_base + 128, gw);
+        if (need_l0) {  // this part's 8 units of the L0 gradient (float64, as the float64 path)
+          float gw[8];
+          tmem_ld8(lane_base + 128 + 8 * part, gw);
           const double *v0 = f ? fev.v0 : finv.v0;
           const double *c0 = f ? fev.c0 : finv.c0;
 #pragma unroll
-          for (int j = 0; j < kEH; ++j) {
+          for (int i = 0; i < 8; ++i) {
+            const int j = 8 * part + i;
             const double pe = l0[0] * v0[j * 4] + l0[1] * v0[j * 4 + 1] + l0[2] * v0[j * 4 + 2] +
                               l0[3] * v0[j * 4 + 3] + c0[j];
-            const double gpe = double(gw[j]) * silu_prime(pe);
+            const double gpe = double(gw[i]) * silu_prime(pe);
 #pragma unroll
             for (int d = 0; d < 4; ++d) gl[d] += gpe * v0[j * 4 + d];
           }
@@ -650,17 +708,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_filter_reverse_tc(
           const int use = tf * 8 + 4 + c, slot = use & 1;
           ok = __all_sync(0xffffffffu, mbar_wait(bar(kREmptyA + slot), ((use >> 1) & 1) ^ 1, abort_flag, err, 30));
           if (!ok) break;
-          float v[16];
-          tmem_ld16(lane_base + 32 * c + 16 * hh, v);
-          const int col0 = 32 * c + 16 * hh;
+          const int col0 = 32 * c + 8 * part;
+          float v[8];
+          tmem_ld8(lane_base + col0, v);
 #pragma unroll
-          for (int i = 0; i < 16; i += 2) {
+          for (int i = 0; i < 8; i += 2) {
             const float2 sv = __ldg(reinterpret_cast<const float2 *>(sp + sp_index(t64, f, r64, col0 + i)));
             v[i] *= sv.x;
             v[i + 1] *= sv.y;
           }
           char *a_hi = reinterpret_cast<char *>(sm + kRevOffA + slot * 2 * kTile);
-          store_row16(a_hi, a_hi + kTile, row, hh, v);
+          store_row8(a_hi, a_hi + kTile, row, part, v);
           fence_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(kRFullA + slot));
@@ -675,26 +733,46 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_filter_reverse_tc(
       ok = __all_sync(0xffffffffu, mbar_wait(bar(kRDrFull), it & 1, abort_flag, err, 31));
       if (!ok) break;
       tc_fence_after();
-      float grb[32];
-      tmem_ld32(lane_base + 160, grb);
+      float grb[8];
+      tmem_ld8(lane_base + 160 + 8 * part, grb);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kRDrFree));
+      // partial sums of the four parts of a row meet in shared memory (a
+      // buffer per tile parity; an mbarrier of the row quarter's 4 warps)
+      double *red = reinterpret_cast<double *>(sm + kRevRed + (it & 1) * kRevRedBytes);
+      {
+        double gr = 0.0;
+        if (valid) {
+          const double *dr = drbf + (size_t)p * kR + 8 * part;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) gr += double(grb[i]) * dr[i];
+        }
+        double *mine = red + (size_t(part) * 128 + row) * 5;
+        mine[0] = gr;
+        for (int d = 0; d < 4; ++d) mine[1 + d] = gl[d];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kRRed + q));
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(kRRed + q), it & 1, abort_flag, err, 32));
+      if (!ok) break;
       if (valid) {
         const double *sc = pair_sc + (size_t)p * kPairScalars;
         const double dphi = geo[(size_t)p * kGeo + 5], phi = geo[(size_t)p * kGeo + 4];
-        if (hh == 0) {
-          double gr = 0.0;
-          const double *dr = drbf + (size_t)p * kR;
-#pragma unroll
-          for (int k = 0; k < kR; ++k) gr += double(grb[k]) * dr[k];
+        if (part == 0) {
+          double gr = 0.0, gsum[4] = {0, 0, 0, 0};
+          for (int k = 0; k < 4; ++k) {  // the parts in a fixed order
+            const double *o = red + (size_t(k) * 128 + row) * 5;
+            gr += o[0];
+            for (int d = 0; d < 4; ++d) gsum[d] += o[1 + d];
+          }
           gr += __dmul_rn(sc[0], dphi);  // cutoff gradient (its weight is orientation-independent)
           g_r[p] = accumulate ? g_r[p] + gr : gr;
           if (need_l0)
-            for (int d = 0; d < 4; ++d) gl0[(size_t)p * 4 + d] = gl[d];
+            for (int d = 0; d < 4; ++d) gl0[(size_t)p * 4 + d] = gsum[d];
         }
         const int a = pa[p], b = pb[p];
-        for (int m = 12 * hh; m < 12 * hh + 12; ++m) {
+        for (int m = 6 * part; m < 6 * part + 6; ++m) {
           const int d = degree_of_channel(m);
           const double y = __dmul_rn(phi, __dadd_rn(__dmul_rn(sc[1 + d], gA[(size_t)a * kEV + m]),
                                                     parity_sign(d) * __dmul_rn(sc[5 + d], gA[(size_t)b * kEV + m])));
@@ -706,7 +784,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_filter_reverse_tc(
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kTcEpiWarps) {
+  if (warp == kRevEpiWarps) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
   }
@@ -722,7 +800,7 @@ void launch_filter_reverse_tc(int P, const double *geo, const int *pair_a, const
   const int ntiles = (P + kTcRows - 1) / kTcRows;
   allow_dynamic_smem(reinterpret_cast<const void *>(k_filter_reverse_tc), kSmemTcRev);
   const int grid = std::min(ntiles, std::max(1, num_sms));
-  k_filter_reverse_tc<<<grid, kTcThreads, kSmemTcRev, s>>>(P, ntiles, geo, pair_a, pair_b, ev, cg_att, finv, fev,
+  k_filter_reverse_tc<<<grid, kRevThreads, kSmemTcRev, s>>>(P, ntiles, geo, pair_a, pair_b, ev, cg_att, finv, fev,
                                                            finv32, fev32, g_filt_inv, g_filt_ev, sp, drbf, gA,
                                                            pair_sc, need_l0 ? 1 : 0, accumulate ? 1 : 0, g_r, g_y,
                                                            gl0, err);
