@@ -189,6 +189,18 @@ struct FilterW32 {
   // c = 0..3 an 8 KB group [W0^T chunk (32 rows) hi | lo], same layout
   const float *tc_rev;
 };
+// Per-block constants of the tcgen05 filter kernels, passed by value as kernel
+// parameters (the constant bank: one broadcast read per warp instead of a
+// global load on the epilogue's critical path). Index 0: invariant filter, 1: ev.
+struct TcFwdConsts {
+  float b0[2][128], bc1[2][128], v0[2][128], c0[2][32];
+  double rb[32], rk[32], rkr[32], gamma;  // radial basis
+  double cg[24];                          // L0 weights of the block's attention
+};
+struct TcRevConsts {
+  double v0[2][128], c0[2][32];
+  double cg[24];
+};
 struct BlockW {
   FilterW finv, fev;
   FilterW32 finv32, fev32;

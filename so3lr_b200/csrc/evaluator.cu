@@ -157,6 +157,10 @@ void Evaluator::upload_weights() {
   std::vector<BOff> boff(layers_);
   std::vector<FOff32> foff32(2 * std::size_t(layers_));
   std::size_t filt_count = 0;  // filters in upload order: block 0 inv, ev, block 1 inv, ...
+  struct FiltHost {
+    std::vector<double> b0, bc1, v0, c0;
+  };
+  std::vector<FiltHost> filt_host(2 * std::size_t(layers_));
   auto filt = [&](const std::string &prefix) {
     FOff o;
     const auto w0 = model_.f64(prefix + ".mlp_rbf.0.weight", {F, R});                  // [j][r]
@@ -182,6 +186,8 @@ void Evaluator::upload_weights() {
     o.w1_f = push(fragment_major(iF, iF, [&](int oo, int j) { return w1[std::size_t(oo) * F + j]; }));
     o.v1_f = push(fragment_major(iF, iH, [&](int oo, int h) { return v1[std::size_t(oo) * H + h]; }));
     o.w0_f = push(fragment_major(iF, iR, [&](int j, int r) { return w0[std::size_t(j) * R + r]; }));
+    filt_host[filt_count] = {model_.f64(prefix + ".mlp_rbf.0.bias", {F}), bc1, model_.f64(prefix + ".mlp_ev.0.weight", {H, 4}),
+                             model_.f64(prefix + ".mlp_ev.0.bias", {H})};
     FOff32 &o32 = foff32[filt_count++];
     o32.b0 = push32(model_.f64(prefix + ".mlp_rbf.0.bias", {F}));
     o32.bc1 = push32(bc1);
@@ -401,6 +407,39 @@ void Evaluator::upload_weights() {
   rad_.k = P(o_rk);
   rad_.kr = P(o_rkr);
   rad_.gamma = model_.f64("model.radial_embedding.radial_basis_fn.gamma", {})[0];
+  {  // kernel-parameter constants of the tcgen05 filter kernels, per block
+    const auto rb = model_.f64("model.radial_embedding.radial_basis_fn.b", {R});
+    const auto rk = model_.i64("model.radial_embedding.radial_basis_fn.k");
+    const auto rkr = model_.i64("model.radial_embedding.radial_basis_fn.k_rev");
+    tc_fwd_consts_.assign(layers_, TcFwdConsts{});
+    tc_rev_consts_.assign(layers_, TcRevConsts{});
+    for (int b = 0; b < layers_; ++b) {
+      TcFwdConsts &cf = tc_fwd_consts_[b];
+      TcRevConsts &cr = tc_rev_consts_[b];
+      for (int f = 0; f < 2; ++f) {
+        const FiltHost &fh = filt_host[2 * std::size_t(b) + f];
+        for (int j = 0; j < kF; ++j) {
+          cf.b0[f][j] = float(fh.b0[j]);
+          cf.bc1[f][j] = float(fh.bc1[j]);
+          cf.v0[f][j] = float(fh.v0[j]);
+          cr.v0[f][j] = fh.v0[j];
+        }
+        for (int j = 0; j < kEH; ++j) {
+          cf.c0[f][j] = float(fh.c0[j]);
+          cr.c0[f][j] = fh.c0[j];
+        }
+      }
+      for (int k = 0; k < kR; ++k) {
+        cf.rb[k] = rb[k];
+        cf.rk[k] = double(rk[k]);
+        cf.rkr[k] = double(rkr[k]);
+      }
+      cf.gamma = rad_.gamma;
+      const std::string att = "model.euclidean_transformers." + std::to_string(b) + ".euclidean_attention_block.";
+      const auto cg = model_.f64(att + "so3_conv_invariants.cg_rep", {kEV});
+      for (int m = 0; m < kEV; ++m) cf.cg[m] = cr.cg[m] = cg[m];
+    }
+  }
   alpha_ref_ = P(o_alpha);
   c6_ref_ = P(o_c6);
   zbl_.ke = z.ke; zbl_.cutoff = z.cutoff; zbl_.switch_off = z.switch_off; zbl_.p = z.p; zbl_.d = z.d;
@@ -963,8 +1002,8 @@ void Evaluator::compute() {
     const BlockW &w = blocks_[b];
     prof_begin(kProfFilterForward);
     if (mixed_ && mixed_tc_)
-      launch_filter_forward_tc(P, geo_.get(), nb_.pair_a, nb_.pair_b, b == 0 ? nullptr : evb_[b]->get(), w.cg_att,
-                               w.finv32, w.fev32, rad_, f_inv_[b]->get(), f_ev_[b]->get(),
+      launch_filter_forward_tc(P, geo_.get(), nb_.pair_a, nb_.pair_b, b == 0 ? nullptr : evb_[b]->get(),
+                               tc_fwd_consts_[b], w.finv32, w.fev32, f_inv_[b]->get(), f_ev_[b]->get(),
                                reinterpret_cast<float *>(sp_[b]->get()), b == 0 ? drbf_.get() : nullptr, tc_err_,
                                num_sms_, s);
     else if (mixed_)
@@ -1149,8 +1188,8 @@ void Evaluator::compute() {
                              g_filt_inv_.get(), g_filt_ev_.get(), s);
     prof_begin(kProfFilterReverse);
     if (mixed_ && mixed_tc_)
-      launch_filter_reverse_tc(P, geo_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr, w.cg_att,
-                               w.finv, w.fev, w.finv32, w.fev32, g_filt_inv_.get(), g_filt_ev_.get(),
+      launch_filter_reverse_tc(P, geo_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr,
+                               tc_rev_consts_[b], w.finv32, w.fev32, g_filt_inv_.get(), g_filt_ev_.get(),
                                reinterpret_cast<const float *>(sp_[b]->get()), drbf_.get(), g_A_.get(),
                                pair_sc_.get(), b > 0, b < layers_ - 1, g_r_.get(), g_y_.get(), gl0_.get(), tc_err_,
                                num_sms_, s);

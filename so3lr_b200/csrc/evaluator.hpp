@@ -174,6 +174,8 @@ class Evaluator {
   // weights
   DeviceArray<double> wbuf_;
   DeviceArray<float> wbuf32_;  // TF32-split filter operands (mixed precision)
+  std::vector<TcFwdConsts> tc_fwd_consts_;  // per block, kernel parameters of the tcgen05 filters
+  std::vector<TcRevConsts> tc_rev_consts_;
   std::vector<BlockW> blocks_;
   HeadsW heads_{};
   RadialW rad_{};

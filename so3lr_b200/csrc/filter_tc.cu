@@ -244,7 +244,7 @@ __device__ __forceinline__ void store_row8(char *hi_tile, char *lo_tile, int row
 
 __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
     int P, int ntiles, const double *__restrict__ geo, const int *__restrict__ pa, const int *__restrict__ pb,
-    const double *__restrict__ ev, const double *__restrict__ cg, FilterW32 finv, FilterW32 fev, RadialW rad,
+    const double *__restrict__ ev, const __grid_constant__ TcFwdConsts c, FilterW32 finv, FilterW32 fev,
     double *__restrict__ f_inv, double *__restrict__ f_ev, float *__restrict__ sp, double *__restrict__ drbf,
     int *__restrict__ err) {
   extern __shared__ unsigned char smem_raw[];
@@ -309,9 +309,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
           ok = mbar_wait(bar(kFOpnd), tf & 1, abort_flag, err, 2) &&
                mbar_wait(bar(kFD1Free), (tf & 1) ^ 1, abort_flag, err, 3);
         } else if (gi <= 4) {
-          const int c = gi - 1, slot = c & 1, use = tf * 2 + (c >> 1);
+          const int ch = gi - 1, slot = ch & 1, use = tf * 2 + (ch >> 1);
           ok = mbar_wait(bar(kFFullA + slot), use & 1, abort_flag, err, 4);
-          if (ok && c == 0) ok = mbar_wait(bar(kFD2Free + d2b), (d2use & 1) ^ 1, abort_flag, err, 5);
+          if (ok && ch == 0) ok = mbar_wait(bar(kFD2Free + d2b), (d2use & 1) ^ 1, abort_flag, err, 5);
         }
         if (ok) ok = mbar_wait(bar(kFFullB + s), (g / kBSlots) & 1, abort_flag, err, 6);
         if (!ok) break;
@@ -322,9 +322,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
           tc_commit(bar(kFEmptyB + s));
           tc_commit(bar(kFD1Full));
         } else if (gi <= 4) {
-          const int c = gi - 1, slot = c & 1;
+          const int ch = gi - 1, slot = ch & 1;
           const uint32_t a_hi = base + kOffA2 + slot * 2 * kTile;
-          mma_chunk(d2, a_hi, a_hi + kTile, b_hi, b_lo, c > 0);
+          mma_chunk(d2, a_hi, a_hi + kTile, b_hi, b_lo, ch > 0);
           tc_commit(bar(kFEmptyB + s));
           tc_commit(bar(kFEmptyA + slot));
         } else {
@@ -363,7 +363,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
       const bool valid = p < P;
       if (f == 0) {
         const double r = valid ? geo[(size_t)p * kGeo] : 1.0;
-        const double raw_x = exp(-rad.gamma * r);
+        const double raw_x = exp(-c.gamma * r);
         double x = raw_x;
         if (x < 1.0e-6) x = 1.0e-6;
         if (x > 1.0 - 1.0e-6) x = 1.0 - 1.0e-6;
@@ -375,9 +375,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int k = 8 * part + i;
-          const double b = exp_tang(rad.b[k] + rad.k[k] * lx + rad.kr[k] * l1x);
+          const double b = exp_tang(c.rb[k] + c.rk[k] * lx + c.rkr[k] * l1x);
           v[i] = float(b);
-          d[i] = live ? b * (-rad.gamma * rad.k[k] + rad.gamma * rad.kr[k] * ratio) : 0.0;
+          d[i] = live ? b * (-c.gamma * c.rk[k] + c.gamma * c.rkr[k] * ratio) : 0.0;
         }
         store_row8(reinterpret_cast<char *>(sm + kOffA1), reinterpret_cast<char *>(sm + kOffA1 + kTile), row, part,
                    v);
@@ -392,17 +392,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
 #pragma unroll
           for (int m = 0; m < kEV; ++m) {
             const double diff = ev[(size_t)b * kEV + m] - ev[(size_t)a * kEV + m];
-            l0[degree_of_channel(m)] += diff * diff * cg[m];
+            l0[degree_of_channel(m)] += diff * diff * c.cg[m];
           }
         }
       }
-      const FilterW32 &W = f ? fev : finv;
       float v[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int j = 8 * part + i;
-        const float s = float(l0[0]) * W.v0[j * 4] + float(l0[1]) * W.v0[j * 4 + 1] + float(l0[2]) * W.v0[j * 4 + 2] +
-                        float(l0[3]) * W.v0[j * 4 + 3] + W.c0[j];
+        const float s = float(l0[0]) * c.v0[f][j * 4] + float(l0[1]) * c.v0[f][j * 4 + 1] +
+                        float(l0[2]) * c.v0[f][j * 4 + 2] + float(l0[3]) * c.v0[f][j * 4 + 3] + c.c0[f][j];
         v[i] = s * sigmoid_fast(s);
       }
       store_row8(reinterpret_cast<char *>(sm + kOffA3), reinterpret_cast<char *>(sm + kOffA3 + kTile), row, part, v);
@@ -417,22 +416,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
       const int f = tf & 1, d2b = tf & 1, d2use = tf >> 1;
       const int p = (int(blockIdx.x) + (tf >> 1) * int(gridDim.x)) * kTcRows + row;
       const bool valid = p < P;
-      const FilterW32 &W = f ? fev : finv;
       double *out = f ? f_ev : f_inv;
       // hidden layer: D1 + b0 -> silu, in 32-column chunks through the hidden ring
       ok = __all_sync(0xffffffffu, mbar_wait(bar(kFD1Full), tf & 1, abort_flag, err, 8));
       if (!ok) break;
       tc_fence_after();
-      for (int c = 0; c < 4 && ok; ++c) {
-        const int slot = c & 1, use = tf * 2 + (c >> 1);
+      for (int ch = 0; ch < 4 && ok; ++ch) {
+        const int slot = ch & 1, use = tf * 2 + (ch >> 1);
         ok = __all_sync(0xffffffffu, mbar_wait(bar(kFEmptyA + slot), (use & 1) ^ 1, abort_flag, err, 9));
         if (!ok) break;
-        const int col0 = 32 * c + 8 * part;
+        const int col0 = 32 * ch + 8 * part;
         float v[8], u[8];
         tmem_ld8(lane_base + col0, v);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float x = v[i] + W.b0[col0 + i];
+          const float x = v[i] + c.b0[f][col0 + i];
           const float sg = sigmoid_fast(x);
           u[i] = x * sg;
           v[i] = sg * (1.0f + x * (1.0f - sg));  // silu'
@@ -461,15 +459,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
       if (tf + 1 < total_tf) prepare(tf + 1);
       // output: D2 + b1 + c1 in float64
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        const int col0 = 32 * c + 8 * part;
+      for (int ch = 0; ch < 4; ++ch) {
+        const int col0 = 32 * ch + 8 * part;
         float v[8];
         tmem_ld8(lane_base + 128 + 128 * d2b + col0, v);
         if (valid) {
           double2 *dst = reinterpret_cast<double2 *>(out + (size_t)p * kF + col0);
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            dst[i] = make_double2(double(v[2 * i] + W.bc1[col0 + 2 * i]), double(v[2 * i + 1] + W.bc1[col0 + 2 * i + 1]));
+            dst[i] = make_double2(double(v[2 * i] + c.bc1[f][col0 + 2 * i]), double(v[2 * i + 1] + c.bc1[f][col0 + 2 * i + 1]));
         }
       }
       tc_fence_before();
@@ -489,15 +487,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
 // kernel; err (device int, zeroed by the caller) receives the code of a wait
 // that gave up (0: none).
 void launch_filter_forward_tc(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
-                              const double *cg_att, const FilterW32 &finv, const FilterW32 &fev, const RadialW &rad,
-                              double *f_inv, double *f_ev, float *sp, double *drbf, int *err, int num_sms,
-                              cudaStream_t s) {
+                              const TcFwdConsts &consts, const FilterW32 &finv, const FilterW32 &fev, double *f_inv,
+                              double *f_ev, float *sp, double *drbf, int *err, int num_sms, cudaStream_t s) {
   if (P == 0) return;
   const int ntiles = (P + kTcRows - 1) / kTcRows;
   allow_dynamic_smem(reinterpret_cast<const void *>(k_filter_forward_tc), kSmemFwd);
   const int grid = std::min(ntiles, std::max(1, num_sms));
-  k_filter_forward_tc<<<grid, kFwdThreads, kSmemFwd, s>>>(P, ntiles, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad,
-                                                        f_inv, f_ev, sp, drbf, err);
+  k_filter_forward_tc<<<grid, kFwdThreads, kSmemFwd, s>>>(P, ntiles, geo, pair_a, pair_b, ev, consts, finv, fev,
+                                                          f_inv, f_ev, sp, drbf, err);
   SO3_LAUNCH("filter_forward_tc");
 }
 
@@ -535,7 +532,7 @@ constexpr int kRFullB = 0, kREmptyB = 3, kRFullA = 6, kREmptyA = 8, kRDhwFull = 
 
 __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
     int P, int ntiles, const double *__restrict__ geo, const int *__restrict__ pa, const int *__restrict__ pb,
-    const double *__restrict__ ev, const double *__restrict__ cg, FilterW finv, FilterW fev, FilterW32 finv32,
+    const double *__restrict__ ev, const __grid_constant__ TcRevConsts c, FilterW32 finv32,
     FilterW32 fev32, const double *__restrict__ g_filt_inv, const double *__restrict__ g_filt_ev,
     const float *__restrict__ sp, const double *__restrict__ drbf, const double *__restrict__ gA,
     const double *__restrict__ pair_sc, int need_l0, int accumulate, double *__restrict__ g_r,
@@ -654,20 +651,20 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
 #pragma unroll
         for (int m = 0; m < kEV; ++m) {
           const double diff = ev[(size_t)b * kEV + m] - ev[(size_t)a * kEV + m];
-          l0[degree_of_channel(m)] += diff * diff * cg[m];
+          l0[degree_of_channel(m)] += diff * diff * c.cg[m];
         }
       }
       for (int f = 0; f < 2 && ok; ++f) {
         const int tf = it * 2 + f;
         const double *gsrc = f ? g_filt_ev : g_filt_inv;
         // the filter gradient into the A ring, 32 columns at a time
-        for (int c = 0; c < 4 && ok; ++c) {
-          const int use = tf * 8 + c, slot = use & 1;
+        for (int ch = 0; ch < 4 && ok; ++ch) {
+          const int use = tf * 8 + ch, slot = use & 1;
           ok = __all_sync(0xffffffffu, mbar_wait(bar(kREmptyA + slot), ((use >> 1) & 1) ^ 1, abort_flag, err, 28));
           if (!ok) break;
           float v[8];
           if (valid) {
-            const double2 *src = reinterpret_cast<const double2 *>(gsrc + (size_t)p * kF + 32 * c + 8 * part);
+            const double2 *src = reinterpret_cast<const double2 *>(gsrc + (size_t)p * kF + 32 * ch + 8 * part);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const double2 x = __ldg(src + i);
@@ -691,8 +688,8 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
         if (need_l0) {  // this part's 8 units of the L0 gradient (float64, as the float64 path)
           float gw[8];
           tmem_ld8(lane_base + 128 + 8 * part, gw);
-          const double *v0 = f ? fev.v0 : finv.v0;
-          const double *c0 = f ? fev.c0 : finv.c0;
+          const double *v0 = c.v0[f];
+          const double *c0 = c.c0[f];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int j = 8 * part + i;
@@ -704,11 +701,11 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
           }
         }
         // hidden pre-activation gradient g_pre = D_h * silu' into the A ring
-        for (int c = 0; c < 4 && ok; ++c) {
-          const int use = tf * 8 + 4 + c, slot = use & 1;
+        for (int ch = 0; ch < 4 && ok; ++ch) {
+          const int use = tf * 8 + 4 + ch, slot = use & 1;
           ok = __all_sync(0xffffffffu, mbar_wait(bar(kREmptyA + slot), ((use >> 1) & 1) ^ 1, abort_flag, err, 30));
           if (!ok) break;
-          const int col0 = 32 * c + 8 * part;
+          const int col0 = 32 * ch + 8 * part;
           float v[8];
           tmem_ld8(lane_base + col0, v);
 #pragma unroll
@@ -791,8 +788,8 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
 }
 
 void launch_filter_reverse_tc(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
-                              const double *cg_att, const FilterW &finv, const FilterW &fev, const FilterW32 &finv32,
-                              const FilterW32 &fev32, const double *g_filt_inv, const double *g_filt_ev,
+                              const TcRevConsts &consts, const FilterW32 &finv32, const FilterW32 &fev32,
+                              const double *g_filt_inv, const double *g_filt_ev,
                               const float *sp, const double *drbf, const double *gA, const double *pair_sc,
                               bool need_l0, bool accumulate, double *g_r, double *g_y, double *gl0, int *err,
                               int num_sms, cudaStream_t s) {
@@ -800,7 +797,7 @@ void launch_filter_reverse_tc(int P, const double *geo, const int *pair_a, const
   const int ntiles = (P + kTcRows - 1) / kTcRows;
   allow_dynamic_smem(reinterpret_cast<const void *>(k_filter_reverse_tc), kSmemTcRev);
   const int grid = std::min(ntiles, std::max(1, num_sms));
-  k_filter_reverse_tc<<<grid, kRevThreads, kSmemTcRev, s>>>(P, ntiles, geo, pair_a, pair_b, ev, cg_att, finv, fev,
+  k_filter_reverse_tc<<<grid, kRevThreads, kSmemTcRev, s>>>(P, ntiles, geo, pair_a, pair_b, ev, consts,
                                                            finv32, fev32, g_filt_inv, g_filt_ev, sp, drbf, gA,
                                                            pair_sc, need_l0 ? 1 : 0, accumulate ? 1 : 0, g_r, g_y,
                                                            gl0, err);

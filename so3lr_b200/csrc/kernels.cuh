@@ -122,12 +122,11 @@ void launch_filter_forward_mixed(int P, const double *geo, const int *pair_a, co
 // CTA per SM (num_sms); err (device int, zeroed by the caller) receives the
 // code of a wait that gave up, 0 when none did
 void launch_filter_forward_tc(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
-                              const double *cg_att, const FilterW32 &finv, const FilterW32 &fev, const RadialW &rad,
-                              double *f_inv, double *f_ev, float *sp, double *drbf, int *err, int num_sms,
-                              cudaStream_t s);
+                              const TcFwdConsts &consts, const FilterW32 &finv, const FilterW32 &fev, double *f_inv,
+                              double *f_ev, float *sp, double *drbf, int *err, int num_sms, cudaStream_t s);
 void launch_filter_reverse_tc(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
-                              const double *cg_att, const FilterW &finv, const FilterW &fev, const FilterW32 &finv32,
-                              const FilterW32 &fev32, const double *g_filt_inv, const double *g_filt_ev,
+                              const TcRevConsts &consts, const FilterW32 &finv32, const FilterW32 &fev32,
+                              const double *g_filt_inv, const double *g_filt_ev,
                               const float *sp, const double *drbf, const double *gA, const double *pair_sc,
                               bool need_l0, bool accumulate, double *g_r, double *g_y, double *gl0, int *err,
                               int num_sms, cudaStream_t s);
