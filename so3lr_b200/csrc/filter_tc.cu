@@ -188,6 +188,7 @@ __device__ __forceinline__ void store_row16(char *hi_tile, char *lo_tile, int ro
   }
 }
 __device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ void prefetch_l2(const void *p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
 // position of silu'(pair row64 of 64-pair tile t64, column col) in the layout of
 // the mixed forward and reverse (sp_offset): warp = col / 16, m16 block mi = row / 16
@@ -417,6 +418,22 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
       const int p = (int(blockIdx.x) + (tf >> 1) * int(gridDim.x)) * kTcRows + row;
       const bool valid = p < P;
       double *out = f ? f_ev : f_inv;
+      {  // the next tile's per-pair inputs into L2 ahead of its preparation
+        const int pn = p + int(gridDim.x) * kTcRows;
+        if (pn < P && part == 0) {
+          if (f == 0) {
+            prefetch_l2(geo + (size_t)pn * kGeo);
+            prefetch_l2(pa + pn);
+            prefetch_l2(pb + pn);
+          } else if (ev != nullptr) {
+            const int a = pa[pn], b = pb[pn];
+            prefetch_l2(ev + (size_t)a * kEV);
+            prefetch_l2(ev + (size_t)a * kEV + 16);
+            prefetch_l2(ev + (size_t)b * kEV);
+            prefetch_l2(ev + (size_t)b * kEV + 16);
+          }
+        }
+      }
       // hidden layer: D1 + b0 -> silu, in 32-column chunks through the hidden ring
       ok = __all_sync(0xffffffffu, mbar_wait(bar(kFD1Full), tf & 1, abort_flag, err, 8));
       if (!ok) break;
@@ -640,11 +657,33 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
     const int row = 32 * q + lane;
     const uint32_t lane_base = tmem + (uint32_t(32 * q) << 16);
     bool ok = true;
+    // this thread's inputs of the tile holding pair pp into L2: its 8-column
+    // slices of both filter gradients and of silu' (one 64- or 32-byte run per
+    // chunk), its radial-basis derivatives, the pair scalars and geometry
+    auto prefetch_tile = [&](int pp) {
+      if (pp >= P) return;
+      for (int f = 0; f < 2; ++f) {
+        const double *gsrc = f ? g_filt_ev : g_filt_inv;
+        for (int ch = 0; ch < 4; ++ch) {
+          prefetch_l2(gsrc + (size_t)pp * kF + 32 * ch + 8 * part);
+          prefetch_l2(sp + sp_index(pp >> 6, f, pp & 63, 32 * ch + 8 * part));
+        }
+      }
+      prefetch_l2(drbf + (size_t)pp * kR + 8 * part);
+      if (part == 0) {
+        prefetch_l2(pair_sc + (size_t)pp * kPairScalars);
+        prefetch_l2(geo + (size_t)pp * kGeo);
+        prefetch_l2(pa + pp);
+        prefetch_l2(pb + pp);
+      }
+    };
+    if (my_tiles > 0) prefetch_tile(int(blockIdx.x) * kTcRows + row);
     for (int it = 0; it < my_tiles && ok; ++it) {
       const int tile = int(blockIdx.x) + it * int(gridDim.x);
       const int p = tile * kTcRows + row;
       const bool valid = p < P;
       const int t64 = p >> 6, r64 = p & 63;
+      if (it + 1 < my_tiles) prefetch_tile(p + int(gridDim.x) * kTcRows);
       double l0[4] = {0, 0, 0, 0}, gl[4] = {0, 0, 0, 0};
       if (need_l0 && valid) {
         const int a = pa[p], b = pb[p];
@@ -660,9 +699,7 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
         // the filter gradient into the A ring, 32 columns at a time
         for (int ch = 0; ch < 4 && ok; ++ch) {
           const int use = tf * 8 + ch, slot = use & 1;
-          ok = __all_sync(0xffffffffu, mbar_wait(bar(kREmptyA + slot), ((use >> 1) & 1) ^ 1, abort_flag, err, 28));
-          if (!ok) break;
-          float v[8];
+          float v[8];  // loaded before the wait for the ring slot
           if (valid) {
             const double2 *src = reinterpret_cast<const double2 *>(gsrc + (size_t)p * kF + 32 * ch + 8 * part);
 #pragma unroll
@@ -675,6 +712,8 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
 #pragma unroll
             for (int i = 0; i < 8; ++i) v[i] = 0.0f;
           }
+          ok = __all_sync(0xffffffffu, mbar_wait(bar(kREmptyA + slot), ((use >> 1) & 1) ^ 1, abort_flag, err, 28));
+          if (!ok) break;
           char *a_hi = reinterpret_cast<char *>(sm + kRevOffA + slot * 2 * kTile);
           store_row8(a_hi, a_hi + kTile, row, part, v);
           fence_async_smem();
@@ -703,16 +742,19 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
         // hidden pre-activation gradient g_pre = D_h * silu' into the A ring
         for (int ch = 0; ch < 4 && ok; ++ch) {
           const int use = tf * 8 + 4 + ch, slot = use & 1;
+          const int col0 = 32 * ch + 8 * part;
+          float2 sv[4];  // silu', loaded before the waits
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            sv[i] = __ldg(reinterpret_cast<const float2 *>(sp + sp_index(t64, f, r64, col0 + 2 * i)));
           ok = __all_sync(0xffffffffu, mbar_wait(bar(kREmptyA + slot), ((use >> 1) & 1) ^ 1, abort_flag, err, 30));
           if (!ok) break;
-          const int col0 = 32 * ch + 8 * part;
           float v[8];
           tmem_ld8(lane_base + col0, v);
 #pragma unroll
-          for (int i = 0; i < 8; i += 2) {
-            const float2 sv = __ldg(reinterpret_cast<const float2 *>(sp + sp_index(t64, f, r64, col0 + i)));
-            v[i] *= sv.x;
-            v[i + 1] *= sv.y;
+          for (int i = 0; i < 4; ++i) {
+            v[2 * i] *= sv[i].x;
+            v[2 * i + 1] *= sv[i].y;
           }
           char *a_hi = reinterpret_cast<char *>(sm + kRevOffA + slot * 2 * kTile);
           store_row8(a_hi, a_hi + kTile, row, part, v);
