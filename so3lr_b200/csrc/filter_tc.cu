@@ -29,8 +29,8 @@
 // (n % 8)) + 4 (k % 4); the descriptor's stride byte offset is 1024 (one 8-row
 // group) and each K step of 8 advances its start address by 32 bytes.
 //
-// The silu' values are written in the layout the mixed reverse reads
-// (sp_offset, 64-pair tiles), so k_filter_reverse_mixed consumes them unchanged.
+// The silu' values go to the buffer of the float64 path in a column-major
+// per-tile layout (sp_tc_index) that the tcgen05 reverse reads.
 #include "filter_common.cuh"
 #include "kernels.cuh"
 
@@ -190,13 +190,12 @@ __device__ __forceinline__ void store_row16(char *hi_tile, char *lo_tile, int ro
 __device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 __device__ __forceinline__ void prefetch_l2(const void *p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
-// position of silu'(pair row64 of 64-pair tile t64, column col) in the layout of
-// the mixed forward and reverse (sp_offset): warp = col / 16, m16 block mi = row / 16
-__device__ __forceinline__ size_t sp_index(int t64, int filt, int row, int col) {
-  const int mi = row >> 4, hf = (row >> 3) & 1, g = row & 7;
-  const int w = col >> 4, ni = (col >> 3) & 1, t = (col >> 1) & 3, e = col & 1;
-  return sp_offset(t64, filt, (mi >> 1) * 4 + (w >> 1)) + (((mi & 1) * 4 + (w & 1) * 2 + ni) * 2) * 64 + hf * 64 +
-         (4 * g + t) * 2 + e;
+// position of silu'(row `row` of 128-pair tile `tile`, column `col`) in the
+// tcgen05 kernels' layout: column-major per tile and filter, so a warp's 32
+// consecutive rows of one column are one 128-byte line (the mma.sync kernels
+// use their own layout, sp_offset; the two kernel pairs do not mix)
+__device__ __forceinline__ size_t sp_tc_index(int tile, int filt, int row, int col) {
+  return ((size_t(tile) * 2 + filt) * 128 + col) * 128 + row;
 }
 
 }  // namespace
@@ -210,10 +209,15 @@ __device__ __forceinline__ size_t sp_index(int t64, int filt, int row, int col) 
 namespace {
 constexpr int kFwdEpiWarps = 16;
 constexpr int kFwdThreads = (kFwdEpiWarps + 1) * 32;
-constexpr int kFwdBars = 18;
+constexpr int kFwdBars = 22;
 constexpr uint32_t kSmemFwd = kOffBar + kFwdBars * 8 + 16 + 1024;
 constexpr int kFFullB = 0, kFEmptyB = 3, kFFullA = 6, kFEmptyA = 8, kFOpnd = 10, kFD1Full = 11, kFD2Full = 12,
-              kFD1Free = 14, kFD2Free = 15, kFDrain = 17;
+              kFD1Free = 14, kFD2Free = 15, kFDrain = 17, kFQuarter = 18;  // kFQuarter + q: 4 warps of row quarter q
+// output staging in the hidden ring (free while the outputs are written): per
+// row quarter 32 rows x 32 doubles, row stride 34 doubles (conflict-free 16-byte writes)
+constexpr int kStageLd = 34;
+constexpr uint32_t kStageBytes = 32 * kStageLd * 8;
+static_assert(4 * kStageBytes <= 4 * kTile, "output staging must fit the hidden ring");
 
 // 8 consecutive float32 columns of this warp's 32 TMEM lanes
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
@@ -269,6 +273,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
     mbar_init(bar(kFD1Free), kFwdEpiWarps);
     for (int i = 0; i < 2; ++i) mbar_init(bar(kFD2Free + i), kFwdEpiWarps);
     mbar_init(bar(kFDrain), 1);
+    for (int i = 0; i < 4; ++i) mbar_init(bar(kFQuarter + i), 4);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -412,6 +417,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
     };
 
     bool ok = true;
+    int quarter_phase = 0;  // completed phases of this row quarter's staging barrier
     if (total_tf > 0) prepare(0);
     for (int tf = 0; tf < total_tf && ok; ++tf) {
       const int f = tf & 1, d2b = tf & 1, d2use = tf >> 1;
@@ -454,11 +460,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
         }
         char *a_hi = reinterpret_cast<char *>(sm + kOffA2 + slot * 2 * kTile);
         store_row8(a_hi, a_hi + kTile, row, part, u);
-        {  // every row of the tile, as the mma.sync forward writes them (finite values past P)
-          const int t64 = p >> 6, r64 = p & 63;
+        {  // every row of the tile (finite values past P); a warp writes one line per column
+          const int tile = p >> 7;
 #pragma unroll
-          for (int i = 0; i < 8; i += 2)
-            *reinterpret_cast<float2 *>(sp + sp_index(t64, f, r64, col0 + i)) = make_float2(v[i], v[i + 1]);
+          for (int i = 0; i < 8; ++i) sp[sp_tc_index(tile, f, row, col0 + i)] = v[i];
         }
         fence_async_smem();
         __syncwarp();
@@ -474,19 +479,36 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
       // the next step's operands first (A1 and A3 are free: every MMA of this
       // step has completed), so its MMAs overlap the output writes below
       if (tf + 1 < total_tf) prepare(tf + 1);
-      // output: D2 + b1 + c1 in float64
+      // output: D2 + b1 + c1 in float64, 32 columns at a time through the
+      // quarter's staging block, so that each store writes 256 contiguous bytes
+      // of one row (8 rows per warp)
+      double *stage = reinterpret_cast<double *>(sm + kOffA2 + q * kStageBytes);
+      const int tile_row0 = (p >> 7) * kTcRows + 32 * q;  // first pair of this quarter
 #pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch) {
+      for (int ch = 0; ch < 4 && ok; ++ch) {
         const int col0 = 32 * ch + 8 * part;
         float v[8];
         tmem_ld8(lane_base + 128 + 128 * d2b + col0, v);
-        if (valid) {
-          double2 *dst = reinterpret_cast<double2 *>(out + (size_t)p * kF + col0);
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            dst[i] = make_double2(double(v[2 * i] + c.bc1[f][col0 + 2 * i]), double(v[2 * i + 1] + c.bc1[f][col0 + 2 * i + 1]));
+        for (int i = 0; i < 4; ++i)
+          *reinterpret_cast<double2 *>(stage + lane * kStageLd + 8 * part + 2 * i) =
+              make_double2(double(v[2 * i] + c.bc1[f][col0 + 2 * i]), double(v[2 * i + 1] + c.bc1[f][col0 + 2 * i + 1]));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kFQuarter + q));
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(kFQuarter + q), quarter_phase & 1, abort_flag, err, 11));
+        ++quarter_phase;
+        if (!ok) break;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int r = 8 * part + k, pr = tile_row0 + r;
+          if (pr < P) out[(size_t)pr * kF + 32 * ch + lane] = stage[r * kStageLd + lane];
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kFQuarter + q));
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(kFQuarter + q), quarter_phase & 1, abort_flag, err, 12));
+        ++quarter_phase;
       }
+      if (!ok) break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kFD2Free + d2b));
@@ -666,7 +688,6 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
         const double *gsrc = f ? g_filt_ev : g_filt_inv;
         for (int ch = 0; ch < 4; ++ch) {
           prefetch_l2(gsrc + (size_t)pp * kF + 32 * ch + 8 * part);
-          prefetch_l2(sp + sp_index(pp >> 6, f, pp & 63, 32 * ch + 8 * part));
         }
       }
       prefetch_l2(drbf + (size_t)pp * kR + 8 * part);
@@ -682,7 +703,6 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
       const int tile = int(blockIdx.x) + it * int(gridDim.x);
       const int p = tile * kTcRows + row;
       const bool valid = p < P;
-      const int t64 = p >> 6, r64 = p & 63;
       if (it + 1 < my_tiles) prefetch_tile(p + int(gridDim.x) * kTcRows);
       double l0[4] = {0, 0, 0, 0}, gl[4] = {0, 0, 0, 0};
       if (need_l0 && valid) {
@@ -743,19 +763,15 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
         for (int ch = 0; ch < 4 && ok; ++ch) {
           const int use = tf * 8 + 4 + ch, slot = use & 1;
           const int col0 = 32 * ch + 8 * part;
-          float2 sv[4];  // silu', loaded before the waits
+          float sv[8];  // silu', loaded before the waits (one line per column and warp)
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            sv[i] = __ldg(reinterpret_cast<const float2 *>(sp + sp_index(t64, f, r64, col0 + 2 * i)));
+          for (int i = 0; i < 8; ++i) sv[i] = __ldg(sp + sp_tc_index(tile, f, row, col0 + i));
           ok = __all_sync(0xffffffffu, mbar_wait(bar(kREmptyA + slot), ((use >> 1) & 1) ^ 1, abort_flag, err, 30));
           if (!ok) break;
           float v[8];
           tmem_ld8(lane_base + col0, v);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            v[2 * i] *= sv[i].x;
-            v[2 * i + 1] *= sv[i].y;
-          }
+          for (int i = 0; i < 8; ++i) v[i] *= sv[i];
           char *a_hi = reinterpret_cast<char *>(sm + kRevOffA + slot * 2 * kTile);
           store_row8(a_hi, a_hi + kTile, row, part, v);
           fence_async_smem();
