@@ -213,11 +213,18 @@ constexpr int kFwdBars = 22;
 constexpr uint32_t kSmemFwd = kOffBar + kFwdBars * 8 + 16 + 1024;
 constexpr int kFFullB = 0, kFEmptyB = 3, kFFullA = 6, kFEmptyA = 8, kFOpnd = 10, kFD1Full = 11, kFD2Full = 12,
               kFD1Free = 14, kFD2Free = 15, kFDrain = 17, kFQuarter = 18;  // kFQuarter + q: 4 warps of row quarter q
-// output staging in the hidden ring (free while the outputs are written): per
-// row quarter 32 rows x 32 doubles, row stride 34 doubles (conflict-free 16-byte writes)
-constexpr int kStageLd = 34;
-constexpr uint32_t kStageBytes = 32 * kStageLd * 8;
-static_assert(4 * kStageBytes <= 4 * kTile, "output staging must fit the hidden ring");
+// Output staging in the hidden ring, which is free while the outputs are
+// written: row quarter q stages its 32 rows x 32 doubles in the bytes that hold
+// its own rows of ring slot 0 (rows 0-15 where its rows of the hi tile are,
+// rows 16-31 where those of the lo tile are: 4 KB each), so quarters that run
+// ahead into the next step never touch another quarter's staging. The 16-byte
+// chunks of a 256-byte staging row are swizzled with the row (conflict-free
+// 16-byte writes by rows and 8-byte reads along a row).
+__device__ __forceinline__ double *stage_at(unsigned char *sm, int q, int r, int col) {
+  const uint32_t off = kOffA2 + (r < 16 ? 0u : kTile) + 4096u * q + uint32_t(r & 15) * 256u +
+                       uint32_t(((col >> 1) ^ (r & 15)) * 16 + (col & 1) * 8);
+  return reinterpret_cast<double *>(sm + off);
+}
 
 // 8 consecutive float32 columns of this warp's 32 TMEM lanes
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
@@ -482,7 +489,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
       // output: D2 + b1 + c1 in float64, 32 columns at a time through the
       // quarter's staging block, so that each store writes 256 contiguous bytes
       // of one row (8 rows per warp)
-      double *stage = reinterpret_cast<double *>(sm + kOffA2 + q * kStageBytes);
       const int tile_row0 = (p >> 7) * kTcRows + 32 * q;  // first pair of this quarter
 #pragma unroll 1
       for (int ch = 0; ch < 4 && ok; ++ch) {
@@ -491,7 +497,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
         tmem_ld8(lane_base + 128 + 128 * d2b + col0, v);
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-          *reinterpret_cast<double2 *>(stage + lane * kStageLd + 8 * part + 2 * i) =
+          *reinterpret_cast<double2 *>(stage_at(sm, q, lane, 8 * part + 2 * i)) =
               make_double2(double(v[2 * i] + c.bc1[f][col0 + 2 * i]), double(v[2 * i + 1] + c.bc1[f][col0 + 2 * i + 1]));
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(kFQuarter + q));
@@ -501,7 +507,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const int r = 8 * part + k, pr = tile_row0 + r;
-          if (pr < P) out[(size_t)pr * kF + 32 * ch + lane] = stage[r * kStageLd + lane];
+          if (pr < P) out[(size_t)pr * kF + 32 * ch + lane] = *stage_at(sm, q, r, lane);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(kFQuarter + q));
