@@ -217,7 +217,7 @@ def library_record() -> dict:
     import hashlib
     from so3lr_b200.build import LIB, headers, sources
     data = LIB.read_bytes()
-    newest = max(p.stat().st_mtime for p in list(sources()) + list(headers()))
+    newest = max(p.stat().st_mtime for p in [src for src, _ in sources()] + list(headers()))
     return {"path": "so3lr_b200/libso3lr_b200.so", "sha256_16": hashlib.sha256(data).hexdigest()[:16],
             "mtime": LIB.stat().st_mtime, "newer_than_sources": LIB.stat().st_mtime >= newest}
 
@@ -364,7 +364,10 @@ def run_ours(args) -> None:
     v0 = maxwell_boltzmann(w.mass, 300.0, seed=11)
     peak = measure_tf32_peak(local) / 3.0 if mixed else measure_fp64_peak(local)
 
-    model = So3lrB200(ROOT / "models" / "so3lr.so3lr", local)
+    model = So3lrB200(args.model, local)
+    if pathlib.Path(args.model).resolve() != (ROOT / "models" / "so3lr.so3lr").resolve():
+        info = model.describe()
+        cfg["workload"] += f" with the model file {pathlib.Path(args.model).name} ({info['summary']})"
     if mixed:
         model.set_precision("mixed")
     if world > 1:
@@ -706,6 +709,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--precision", choices=["float64", "mixed"], default="float64",
                     help="mixed: pair-filter GEMMs as three-pass TF32 (the mixed float32 run of config 2)")
+    ap.add_argument("--model", default=str(ROOT / "models" / "so3lr.so3lr"),
+                    help="model file for configs 1-3 (default: the shipped SO3LR model)")
     ap.add_argument("--no-identity", action="store_true",
                     help="skip the single-point evaluation of the 192,000-atom box (energy and force hash)")
     args = ap.parse_args()

@@ -115,7 +115,10 @@ typedef struct {
  * Replaces NativeModel::load (src/native_model.cpp:325-405),
  * describe_architecture (src/so3lr_architecture.cpp:296) and
  * negotiate_capabilities (src/so3lr_capabilities.cpp:276), as called from
- * PairSO3LRNativeMPI::settings (pair_so3lr_native_mpi.cpp:1097-1137). */
+ * PairSO3LRNativeMPI::settings (pair_so3lr_native_mpi.cpp:1097-1137).
+ * Both released widths load: invariant_features = 128 (4 heads, degrees
+ * [1,2,3,4], 32 radial functions) and 256 (8 heads, degrees [1,1,2,2,3,3,4,4],
+ * 64 radial functions); the handle runs the kernels compiled for that width. */
 int so3lr_create(const char *model_path, int cuda_device, so3lr_handle **out, char *err, size_t errlen);
 
 /* Architecture record of a loaded model (src/so3lr_architecture.cpp:296-450). */
@@ -270,7 +273,9 @@ int so3lr_profile_read(so3lr_handle *h, int kernel, double *total_ms, long long 
  * The reference has no reduced-precision runtime (float32 is only a storage type
  * of its model file, src/native_model.cpp:266); this mode serves the mixed
  * float32 run of the benchmark configurations. Takes effect from the next
- * evaluation; returns nonzero for an unknown value. */
+ * evaluation; returns nonzero for an unknown value, and for
+ * SO3LR_PRECISION_MIXED on a model with invariant_features = 256 (the
+ * mixed-precision kernels exist for the F = 128 width only). */
 #define SO3LR_PRECISION_FLOAT64 0
 #define SO3LR_PRECISION_MIXED 1
 int so3lr_set_precision(so3lr_handle *h, int precision, char *err, size_t errlen);

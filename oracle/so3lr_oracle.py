@@ -146,6 +146,7 @@ class OracleModel:
     degree_repeats: list
     degree_offsets: list
     deg_of_channel: torch.Tensor
+    feature_to_sh: torch.Tensor   # equivariant channel -> one of the 24 distinct harmonics
     norm1: str = "layer"          # "layer" (affine LayerNorm) or "rms" (RMSNorm, no scale)
     norm2: str = "layer"          # "layer", "rms" or "identity"
     qk_norm: bool = False
@@ -161,6 +162,15 @@ class OracleModel:
         reps = [int(x) for x in f.t("model.euclidean_transformers.0.euclidean_attention_block.degree_repeats")]
         offs = list(np.cumsum([0] + reps[:-1]))
         deg = torch.tensor(sum(([d] * r for d, r in enumerate(reps)), []), dtype=torch.long)
+        # degree slots may repeat a degree ({1,1,2,2,...}); every slot of degree
+        # l carries the same 2l+1 harmonics, the distinct harmonics being laid out
+        # l = 1..4 ascending (so3lr_architecture.cpp:270-293)
+        to_sh = []
+        for r in reps:
+            l = (r - 1) // 2
+            to_sh += [l * l - 1 + k for k in range(r)]
+        if int(a["attention_heads"]) != len(reps):
+            raise ValueError("attention_heads must equal the number of degree slots")
         # block norms (so3lr_architecture.cpp:369-389): one module choice for
         # both positions, each position switchable
         kind = "rms" if a.get("use_rms_norm", False) else "layer"
@@ -177,6 +187,7 @@ class OracleModel:
             r_lr=float(a["long_range_cutoff_angstrom"]),
             gamma=float(np.asarray(f.t("model.radial_embedding.radial_basis_fn.gamma")).reshape(-1)[0]),
             degree_repeats=reps, degree_offsets=[int(o) for o in offs], deg_of_channel=deg,
+            feature_to_sh=torch.tensor(to_sh, dtype=torch.long),
             norm1=norm1, norm2=norm2, qk_norm=bool(a.get("qk_norm", False)), resid=resid, x0_scale=x0s,
             repulsion=str(a.get("repulsion_type", "zbl_learned")))
 
@@ -420,11 +431,11 @@ def evaluate(m: OracleModel, s: System, graphs=None, want_forces: bool = True, c
     # --- geometry -------------------------------------------------------------
     r = torch.sqrt((sr_vec * sr_vec).sum(dim=1))
     inv_r = torch.where(r > 1.0e-14, 1.0 / r, torch.zeros_like(r))
-    sh = spherical_harmonics(sr_vec * inv_r[:, None])
+    sh = spherical_harmonics(sr_vec * inv_r[:, None])[:, m.feature_to_sh]
     cut = physnet_cutoff(r, m.r_sr)
     rbf = bernstein(r, m)
     deg = m.deg_of_channel
-    heads = 4
+    heads = len(m.degree_repeats)   # attention heads == degree slots
     hw = F // heads
 
     def block(b, x, ev):

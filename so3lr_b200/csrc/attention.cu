@@ -9,31 +9,37 @@
 // both roles over its own row: as receiver of edge b->a and as sender of the
 // reverse edge a->b, which visits each outgoing edge exactly once.
 //
-// Lane layout: lane owns channels 4*lane .. 4*lane+3 of the 128 invariant
-// channels (head = lane / 8); lanes 0..23 own the 24 equivariant channels.
+// Lane layout: lane owns invariant channels kPL lane .. kPL lane + kPL - 1
+// (kPL = F / 32: 4 for F = 128, 8 for F = 256; head = lane / kLPH, kLPH = 32 /
+// heads lanes per head) and equivariant channels lane + 32 j (j < kEVL).
 // qkv rows are head-major: [head][q, k, v, q_ev, k_ev][32].
 #include "kernels.cuh"
 
-namespace so3lr_b200 {
+SO3LR_SHAPE_BEGIN
 namespace {
 
-__device__ inline double head_sum(double v) {  // sum over the 8 lanes of a head
-  v += __shfl_xor_sync(0xffffffffu, v, 1);
-  v += __shfl_xor_sync(0xffffffffu, v, 2);
-  v += __shfl_xor_sync(0xffffffffu, v, 4);
+constexpr int kPL = kF / 32;          // invariant channels per lane
+constexpr int kLPH = 32 / kHeads;     // lanes per head
+constexpr int kEVL = (kEV + 31) / 32; // equivariant channels per lane
+
+__device__ inline double head_sum(double v) {  // sum over the kLPH lanes of a head
+#pragma unroll
+  for (int off = 1; off < kLPH; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
   return v;
 }
 
-// four consecutive doubles (32-byte aligned, read-only during the kernel) with
-// one 256-bit load
-__device__ inline void load4(const double *p, double (&v)[4]) {
-  asm("ld.global.nc.v4.f64 {%0,%1,%2,%3}, [%4];"
-               : "=d"(v[0]), "=d"(v[1]), "=d"(v[2]), "=d"(v[3])
-               : "l"(p));
+// kPL consecutive doubles (32-byte aligned, read-only during the kernel) with
+// 256-bit loads
+__device__ inline void load4(const double *p, double (&v)[kPL]) {
+#pragma unroll
+  for (int q = 0; q < kPL; q += 4)
+    asm("ld.global.nc.v4.f64 {%0,%1,%2,%3}, [%4];"
+        : "=d"(v[q]), "=d"(v[q + 1]), "=d"(v[q + 2]), "=d"(v[q + 3])
+        : "l"(p + q));
 }
-__device__ inline void store4(double *p, const double (&v)[4]) {
-  *reinterpret_cast<double2 *>(p) = make_double2(v[0], v[1]);
-  *reinterpret_cast<double2 *>(p + 2) = make_double2(v[2], v[3]);
+__device__ inline void store4(double *p, const double (&v)[kPL]) {
+#pragma unroll
+  for (int q = 0; q < kPL; q += 2) *reinterpret_cast<double2 *>(p + q) = make_double2(v[q], v[q + 1]);
 }
 
 }  // namespace
@@ -51,16 +57,26 @@ __global__ void __launch_bounds__(256) k_attention_forward(int n, int row0, cons
   const int lane = threadIdx.x & 31;
   if (r >= n) return;
   const int a = row0 + r;
-  const int h = lane >> 3, o = (lane & 7) * 4;
+  const int h = lane / kLPH, o = (lane % kLPH) * kPL;
   const size_t head_off = size_t(h) * 160 + o;
-  double qa[4], qea[4];
+  double qa[kPL], qea[kPL];
   load4(qkv + (size_t)a * kQKV + head_off + 0 * 32, qa);
   load4(qkv + (size_t)a * kQKV + head_off + 3 * 32, qea);
-  double acc[4] = {0, 0, 0, 0};
-  double acc_ev = 0.0;
+  double acc[kPL];
+#pragma unroll
+  for (int j = 0; j < kPL; ++j) acc[j] = 0.0;
+  double acc_ev[kEVL];
+  int my_deg[kEVL], my_sh[kEVL];
+  double my_par[kEVL];
+#pragma unroll
+  for (int j = 0; j < kEVL; ++j) {
+    const int m = lane + 32 * j;
+    acc_ev[j] = 0.0;
+    my_deg[j] = m < kEV ? degree_of_channel(m) : 0;
+    my_sh[j] = m < kEV ? sh_of_channel(m) : 0;
+    my_par[j] = parity_sign(my_deg[j]);
+  }
   const double inv_norm = 1.0 / norm;  // one division per atom instead of two per edge
-  const int my_deg = lane < kEV ? degree_of_channel(lane) : 0;
-  const double my_par = parity_sign(my_deg);
   const int e0 = row_start[r], e1 = row_start[r + 1];
   int b_nx = 0, code_nx = 0;  // indices of the next edge, loaded one iteration ahead
   if (e0 < e1) {
@@ -75,34 +91,35 @@ __global__ void __launch_bounds__(256) k_attention_forward(int n, int row0, cons
       code_nx = edge_pair[e + 1];
       // pull the next edge's rows into L1 while this one is processed: the k, v
       // and k_ev lines of each head (lines 2-5 and 8-9 of the head's ten 128-byte
-      // lines), both filters (8 lines each) and the harmonics (two 96-byte halves)
+      // lines), both filters (kF / 16 lines each) and the harmonics (two 96-byte halves)
       const int p_nx = code_nx >= 0 ? code_nx : ~code_nx;
-      for (int c = lane; c < 42; c += 32) {
+      constexpr int kQl = 6 * kHeads, kFl = kF / 16;
+      for (int c = lane; c < kQl + 2 * kFl + 2; c += 32) {
         const char *addr;
-        if (c < 24) {
+        if (c < kQl) {
           const int j = c % 6;
           addr = reinterpret_cast<const char *>(qkv + (size_t)b_nx * kQKV) + 128 * ((c / 6) * 10 + (j < 4 ? 2 + j : 4 + j));
-        } else if (c < 32) {
-          addr = reinterpret_cast<const char *>(f_inv + (size_t)p_nx * kF) + 128 * (c - 24);
-        } else if (c < 40) {
-          addr = reinterpret_cast<const char *>(f_ev + (size_t)p_nx * kF) + 128 * (c - 32);
+        } else if (c < kQl + kFl) {
+          addr = reinterpret_cast<const char *>(f_inv + (size_t)p_nx * kF) + 128 * (c - kQl);
+        } else if (c < kQl + 2 * kFl) {
+          addr = reinterpret_cast<const char *>(f_ev + (size_t)p_nx * kF) + 128 * (c - kQl - kFl);
         } else {
-          addr = reinterpret_cast<const char *>(sh + (size_t)p_nx * kEV) + 96 * (c - 40);
+          addr = reinterpret_cast<const char *>(sh + (size_t)p_nx * kSH) + 96 * (c - kQl - 2 * kFl);
         }
         asm volatile("prefetch.global.L1 [%0];\n" ::"l"(addr));
       }
     }
     const int p = code >= 0 ? code : ~code;
     const double phi = geo[(size_t)p * kGeo + 4];
-    double kb[4], vb[4], keb[4], fi[4], fe[4];
+    double kb[kPL], vb[kPL], keb[kPL], fi[kPL], fe[kPL];
     load4(qkv + (size_t)b * kQKV + head_off + 1 * 32, kb);
     load4(qkv + (size_t)b * kQKV + head_off + 2 * 32, vb);
     load4(qkv + (size_t)b * kQKV + head_off + 4 * 32, keb);
-    load4(f_inv + (size_t)p * kF + lane * 4, fi);
-    load4(f_ev + (size_t)p * kF + lane * 4, fe);
+    load4(f_inv + (size_t)p * kF + lane * kPL, fi);
+    load4(f_ev + (size_t)p * kF + lane * kPL, fe);
     double ai = 0.0, ae = 0.0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < kPL; ++j) {
       ai += qa[j] * kb[j] * fi[j];
       ae += qea[j] * keb[j] * fe[j];
     }
@@ -110,16 +127,21 @@ __global__ void __launch_bounds__(256) k_attention_forward(int n, int row0, cons
     ae = head_sum(ae) * inv_norm;
     const double wi = phi * ai;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[j] += wi * vb[j];
-    const double ae_m = __shfl_sync(0xffffffffu, ae, my_deg * 8);
-    if (lane < kEV) {
-      double y = sh[(size_t)p * kEV + lane];
-      if (code < 0) y *= my_par;
-      acc_ev += phi * ae_m * y;
+    for (int j = 0; j < kPL; ++j) acc[j] += wi * vb[j];
+#pragma unroll
+    for (int j = 0; j < kEVL; ++j) {
+      const double ae_m = __shfl_sync(0xffffffffu, ae, my_deg[j] * kLPH);
+      if (lane + 32 * j < kEV) {
+        double y = sh[(size_t)p * kSH + my_sh[j]];
+        if (code < 0) y *= my_par[j];
+        acc_ev[j] += phi * ae_m * y;
+      }
     }
   }
-  store4(d_inv + (size_t)a * kF + lane * 4, acc);
-  if (lane < kEV) d_ev[(size_t)a * kEV + lane] = acc_ev;
+  store4(d_inv + (size_t)a * kF + lane * kPL, acc);
+#pragma unroll
+  for (int j = 0; j < kEVL; ++j)
+    if (lane + 32 * j < kEV) d_ev[(size_t)a * kEV + lane + 32 * j] = acc_ev[j];
 }
 
 void launch_attention_forward(int n, const NeighborState &nb, const double *geo, const double *sh,
@@ -144,29 +166,35 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
   const int lane = threadIdx.x & 31;
   if (r >= n) return;
   const int a = row0 + r;
-  const int h = lane >> 3, o = (lane & 7) * 4;
+  const int h = lane / kLPH, o = (lane % kLPH) * kPL;
   const size_t head_off = size_t(h) * 160 + o;
   const double *qa_row = qkv + (size_t)a * kQKV + head_off;
-  double qa[4], ka[4], va[4], qea[4], kea[4], ga[4];
+  double qa[kPL], ka[kPL], va[kPL], qea[kPL], kea[kPL], ga[kPL];
   load4(qa_row + 0 * 32, qa);
   load4(qa_row + 1 * 32, ka);
   load4(qa_row + 2 * 32, va);
   load4(qa_row + 3 * 32, qea);
   load4(qa_row + 4 * 32, kea);
-  load4(g_a + (size_t)a * kF + lane * 4, ga);
-  // Equivariant channels by degree group: the 8 lanes of head h hold the
-  // channels of degree slot h (3, 5, 7 and 9 channels; lane 24 holds the ninth
-  // channel of the last degree as well), so a 3-step reduction inside the group
-  // gives every lane the degree sum its head uses.
-  const int dbase = h == 0 ? 0 : (h == 1 ? 3 : (h == 2 ? 8 : 15));
-  const int dcount = h == 0 ? 3 : (h == 1 ? 5 : (h == 2 ? 7 : 8));
-  const int ch0 = (lane & 7) < dcount ? dbase + (lane & 7) : -1;
-  const int ch1 = lane == 24 ? 23 : -1;
+  load4(g_a + (size_t)a * kF + lane * kPL, ga);
+  // Equivariant channels by degree group: the kLPH lanes of head h hold the
+  // channels of degree slot h (2 l + 1 of them; lane j of the group holds
+  // channels j, j + kLPH, ...), so a reduction inside the group gives every
+  // lane the degree sum its head uses. F = 128: 8 lanes for 3, 5, 7 and 9
+  // channels (the group's first lane holds the ninth channel of l = 4 as well).
+  constexpr int kCPL = (9 + kLPH - 1) / kLPH;  // channels per lane
+  int ch[kCPL], shc[kCPL];
+  double gAa[kCPL];
+#pragma unroll
+  for (int k = 0; k < kCPL; ++k) {
+    const int j = lane % kLPH + kLPH * k;
+    ch[k] = j < slot_width(h) ? slot_offset(h) + j : -1;
+    shc[k] = ch[k] >= 0 ? sh_of_channel(ch[k]) : 0;
+    gAa[k] = ch[k] >= 0 ? g_A[(size_t)a * kEV + ch[k]] : 0.0;
+  }
   const double par = parity_sign(h);
-  const double gAa0 = ch0 >= 0 ? g_A[(size_t)a * kEV + ch0] : 0.0;
-  const double gAa1 = ch1 >= 0 ? g_A[(size_t)a * kEV + ch1] : 0.0;
-  double gq[4] = {0, 0, 0, 0}, gk[4] = {0, 0, 0, 0}, gv[4] = {0, 0, 0, 0}, gqe[4] = {0, 0, 0, 0},
-         gke[4] = {0, 0, 0, 0};
+  double gq[kPL], gk[kPL], gv[kPL], gqe[kPL], gke[kPL];
+#pragma unroll
+  for (int j = 0; j < kPL; ++j) gq[j] = gk[j] = gv[j] = gqe[j] = gke[j] = 0.0;
   const double inv_norm = 1.0 / norm;
   const int e0 = row_start[r], e1 = row_start[r + 1];
   int b_nx = 0, code_nx = 0;
@@ -178,50 +206,64 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
     const int p = code >= 0 ? code : ~code;
     if (e + 1 < e1) {
       // pull the next edge's rows into L1 while this one is processed: the qkv
-      // row (40 lines of 128 B), g_a, f_inv and f_ev (8 lines each), and the
-      // two 96-byte halves of g_A and of the harmonics
+      // row (5 kF / 16 lines of 128 B), g_a, f_inv and f_ev (kF / 16 lines
+      // each), the 96-byte pieces of g_A and the two of the harmonics
       const int p_nx = code_nx >= 0 ? code_nx : ~code_nx;
+      constexpr int kQl = 5 * kF / 16, kFl = kF / 16, kAp = kEV / 12;
       const char *qrow = reinterpret_cast<const char *>(qkv + (size_t)b_nx * kQKV);
-      const char *l1 = lane < 8 ? qrow + 128 * (32 + lane)
-                     : lane < 16 ? reinterpret_cast<const char *>(g_a + (size_t)b_nx * kF) + 128 * (lane - 8)
-                     : lane < 24 ? reinterpret_cast<const char *>(f_inv + (size_t)p_nx * kF) + 128 * (lane - 16)
-                                 : reinterpret_cast<const char *>(f_ev + (size_t)p_nx * kF) + 128 * (lane - 24);
-      asm volatile("prefetch.global.L1 [%0];\n" ::"l"(qrow + 128 * lane));
-      asm volatile("prefetch.global.L1 [%0];\n" ::"l"(l1));
-      if (lane < 4) {
-        const char *l2 = lane < 2 ? reinterpret_cast<const char *>(g_A + (size_t)b_nx * kEV) + 96 * lane
-                                  : reinterpret_cast<const char *>(sh + (size_t)p_nx * kEV) + 96 * (lane - 2);
-        asm volatile("prefetch.global.L1 [%0];\n" ::"l"(l2));
+#pragma unroll
+      for (int c = lane; c < kQl + 3 * kFl + kAp + 2; c += 32) {
+        const char *addr = c < kQl            ? qrow + 128 * c
+                           : c < kQl + kFl     ? reinterpret_cast<const char *>(g_a + (size_t)b_nx * kF) + 128 * (c - kQl)
+                           : c < kQl + 2 * kFl ? reinterpret_cast<const char *>(f_inv + (size_t)p_nx * kF) + 128 * (c - kQl - kFl)
+                           : c < kQl + 3 * kFl ? reinterpret_cast<const char *>(f_ev + (size_t)p_nx * kF) + 128 * (c - kQl - 2 * kFl)
+                           : c < kQl + 3 * kFl + kAp
+                               ? reinterpret_cast<const char *>(g_A + (size_t)b_nx * kEV) + 96 * (c - kQl - 3 * kFl)
+                               : reinterpret_cast<const char *>(sh + (size_t)p_nx * kSH) + 96 * (c - kQl - 3 * kFl - kAp);
+        asm volatile("prefetch.global.L1 [%0];\n" ::"l"(addr));
       }
     }
     const double phi = geo[(size_t)p * kGeo + 4];
     const double *b_row = qkv + (size_t)b * kQKV + head_off;
-    double qb[4], kb[4], vb[4], qeb[4], keb[4], gb[4], fi[4], fe[4];
+    double qb[kPL], kb[kPL], vb[kPL], qeb[kPL], keb[kPL], gb[kPL], fi[kPL], fe[kPL];
     load4(b_row + 0 * 32, qb);
     load4(b_row + 1 * 32, kb);
     load4(b_row + 2 * 32, vb);
     load4(b_row + 3 * 32, qeb);
     load4(b_row + 4 * 32, keb);
-    load4(g_a + (size_t)b * kF + lane * 4, gb);
-    load4(f_inv + (size_t)p * kF + lane * 4, fi);
-    load4(f_ev + (size_t)p * kF + lane * 4, fe);
+    load4(g_a + (size_t)b * kF + lane * kPL, gb);
+    load4(f_inv + (size_t)p * kF + lane * kPL, fi);
+    load4(f_ev + (size_t)p * kF + lane * kPL, fe);
     // harmonic-weighted adjoint sums per degree, for edge b->a ("in": y of the
     // edge into a) and a->b ("out": parity times that)
     double s_in, s_out;
     {
       const double pin = code < 0 ? par : 1.0;  // harmonics are stored for the primary orientation
-      const double y0 = ch0 >= 0 ? sh[(size_t)p * kEV + ch0] * pin : 0.0;
-      const double y1 = ch1 >= 0 ? sh[(size_t)p * kEV + ch1] * pin : 0.0;
-      const double gAb0 = ch0 >= 0 ? g_A[(size_t)b * kEV + ch0] : 0.0;
-      const double gAb1 = ch1 >= 0 ? g_A[(size_t)b * kEV + ch1] : 0.0;
-      s_in = gAa0 * y0 + gAa1 * y1;
-      s_out = (gAb0 * y0 + gAb1 * y1) * par;
+      double y[kCPL], gAb[kCPL];
+#pragma unroll
+      for (int k = 0; k < kCPL; ++k) {
+        y[k] = ch[k] >= 0 ? sh[(size_t)p * kSH + shc[k]] * pin : 0.0;
+        gAb[k] = ch[k] >= 0 ? g_A[(size_t)b * kEV + ch[k]] : 0.0;
+      }
+      if constexpr (kCPL == 2) {
+        s_in = gAa[0] * y[0] + gAa[1] * y[1];
+        s_out = (gAb[0] * y[0] + gAb[1] * y[1]) * par;
+      } else {
+        s_in = gAa[0] * y[0];
+        s_out = gAb[0] * y[0];
+#pragma unroll
+        for (int k = 1; k < kCPL; ++k) {
+          s_in += gAa[k] * y[k];
+          s_out += gAb[k] * y[k];
+        }
+        s_out *= par;
+      }
       s_in = head_sum(s_in);
       s_out = head_sum(s_out);
     }
     double ai_out = 0, si_in = 0, si_out = 0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < kPL; ++j) {
       ai_out += qb[j] * ka[j] * fi[j];
       si_in += ga[j] * vb[j];
       si_out += gb[j] * va[j];
@@ -232,7 +274,7 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
     const double c_q = phi * si_in * inv_norm, c_qe = phi * s_in * inv_norm;
     const double c_v = phi * ai_out, c_k = phi * si_out * inv_norm, c_ke = phi * s_out * inv_norm;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < kPL; ++j) {
       gq[j] += c_q * (kb[j] * fi[j]);
       gqe[j] += c_qe * (keb[j] * fe[j]);
       gv[j] += c_v * gb[j];
@@ -246,18 +288,18 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
         // explicitly rounded products and sum (no FMA contraction): the two
         // directions' terms swap when the pair is held from its other endpoint,
         // and a rounded sum is exactly commutative
-        double gi[4], ge[4];
+        double gi[kPL], ge[kPL];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < kPL; ++j) {
           gi[j] = __dadd_rn(__dmul_rn(c_q, __dmul_rn(qa[j], kb[j])), __dmul_rn(c_k, __dmul_rn(qb[j], ka[j])));
           ge[j] = __dadd_rn(__dmul_rn(c_qe, __dmul_rn(qea[j], keb[j])), __dmul_rn(c_ke, __dmul_rn(qeb[j], kea[j])));
         }
-        store4(g_filt_inv + (size_t)p * kF + lane * 4, gi);
-        store4(g_filt_ev + (size_t)p * kF + lane * 4, ge);
+        store4(g_filt_inv + (size_t)p * kF + lane * kPL, gi);
+        store4(g_filt_ev + (size_t)p * kF + lane * kPL, ge);
       }
       double ai_in = 0, ae_in = 0, ae_out = 0;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < kPL; ++j) {
         ai_in += qa[j] * kb[j] * fi[j];
         ae_in += qea[j] * keb[j] * fe[j];
         ae_out += qeb[j] * kea[j] * fe[j];
@@ -273,14 +315,14 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
       // which endpoint holds the pair.
       double t = __dadd_rn(__dadd_rn(__dmul_rn(ai_in, si_in), __dmul_rn(ai_out, si_out)),
                            __dadd_rn(__dmul_rn(ae_in, s_in), __dmul_rn(ae_out, s_out)));
-      t += __shfl_xor_sync(0xffffffffu, t, 8);
-      t += __shfl_xor_sync(0xffffffffu, t, 16);
+#pragma unroll
+      for (int off = kLPH; off < 32; off <<= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
       double *ps = pair_sc + (size_t)p * kPairScalars;
       if (lane == 0) ps[0] = t;
-      if (lane == 1) ps[9] = 0.0;
-      if ((lane & 7) == 0) {
+      if (lane == 1) ps[kPairScalars - 1] = 0.0;
+      if (lane % kLPH == 0) {
         ps[1 + h] = ae_in;
-        ps[5 + h] = ae_out;
+        ps[1 + kHeads + h] = ae_out;
       }
     }
   }
@@ -307,26 +349,31 @@ void launch_attention_reverse(int n, const NeighborState &nb, const double *geo,
   SO3_LAUNCH("attention_reverse");
 }
 
-// g_ev[a][m] = g_A[a][m] + sum over a's pairs of 2 (ev_a - ev_b)[m] cg[m] gl0[p][deg m]
+// g_ev[a][m] = g_A[a][m] + sum over a's pairs of 2 (ev_a - ev_b)[m] cg[m] gl0[p][slot of m]
 __global__ void k_ev_l0_reverse(int n, int row0, const int *__restrict__ row_start, const int *__restrict__ nbr,
                                 const int *__restrict__ edge_pair, const double *__restrict__ ev,
                                 const double *__restrict__ cg, const double *__restrict__ gl0,
                                 const double *__restrict__ g_A, double *__restrict__ g_ev) {
   const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (r >= n || lane >= kEV) return;
+  if (r >= n) return;
   const int a = row0 + r;
-  const int d = degree_of_channel(lane);
-  const double eva = ev[(size_t)a * kEV + lane];
-  const double c = 2.0 * cg[lane];
-  double acc = 0.0;
-  for (int e = row_start[r]; e < row_start[r + 1]; ++e) {
-    const int b = nbr[e];
-    const int code = edge_pair[e];
-    const int p = code >= 0 ? code : ~code;
-    acc += (eva - ev[(size_t)b * kEV + lane]) * c * gl0[(size_t)p * 4 + d];
+#pragma unroll
+  for (int j = 0; j < kEVL; ++j) {
+    const int m = lane + 32 * j;
+    if (m >= kEV) break;
+    const int d = degree_of_channel(m);
+    const double eva = ev[(size_t)a * kEV + m];
+    const double c = 2.0 * cg[m];
+    double acc = 0.0;
+    for (int e = row_start[r]; e < row_start[r + 1]; ++e) {
+      const int b = nbr[e];
+      const int code = edge_pair[e];
+      const int p = code >= 0 ? code : ~code;
+      acc += (eva - ev[(size_t)b * kEV + m]) * c * gl0[(size_t)p * kHeads + d];
+    }
+    g_ev[(size_t)a * kEV + m] = g_A[(size_t)a * kEV + m] + acc;
   }
-  g_ev[(size_t)a * kEV + lane] = g_A[(size_t)a * kEV + lane] + acc;
 }
 
 void launch_ev_l0_reverse(int n, const NeighborState &nb, const double *ev, const double *cg_att,
@@ -337,4 +384,4 @@ void launch_ev_l0_reverse(int n, const NeighborState &nb, const double *ev, cons
   SO3_LAUNCH("ev_l0_reverse");
 }
 
-}  // namespace so3lr_b200
+SO3LR_SHAPE_END

@@ -12,10 +12,10 @@
 
 #include "nccl_dyn.hpp"
 
-#include "evaluator.hpp"
+#include "api.hpp"
 
 using so3lr_b200::Error;
-using so3lr_b200::Evaluator;
+using Evaluator = so3lr_b200::EvaluatorApi;
 using so3lr_b200::SystemSpec;
 
 std::atomic<long long> &so3lr_b200::launch_counter() {
@@ -86,7 +86,7 @@ int so3lr_create(const char *model_path, int cuda_device, so3lr_handle **out, ch
   *out = nullptr;
   try {
     auto h = std::make_unique<so3lr_handle>();
-    h->eval = std::make_unique<Evaluator>(model_path ? model_path : "", cuda_device);
+    h->eval = so3lr_b200::make_evaluator(model_path ? model_path : "", cuda_device);
     *out = h.release();
     return 0;
   } catch (const std::exception &e) {
@@ -370,8 +370,12 @@ int so3lr_set_precision(so3lr_handle *h, int precision, char *err, size_t errlen
     return report_msg("so3lr_set_precision: precision must be SO3LR_PRECISION_FLOAT64 (0) or "
                       "SO3LR_PRECISION_MIXED (1)",
                       err, errlen);
-  h->eval->set_mixed_precision(precision == SO3LR_PRECISION_MIXED);
-  return 0;
+  try {
+    h->eval->set_mixed_precision(precision == SO3LR_PRECISION_MIXED);
+    return 0;
+  } catch (const std::exception &e) {
+    return report(e, err, errlen, h);
+  }
 }
 
 long long so3lr_launch_count(void) { return so3lr_b200::launch_counter().load(); }

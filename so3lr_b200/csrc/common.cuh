@@ -1,9 +1,17 @@
 // Shared device definitions for the SO3LR B200 kernels.
 //
-// Fixed model shape (the capability table in model_host.cpp refuses anything
-// else): F = 128 invariant features, 4 heads of 32 channels, equivariant
-// degrees l = 1..4 (24 channels), 32 Bernstein radial functions, 32-wide
-// hidden layer in the equivariant filter branch.
+// Model shapes. The kernels are compiled once per supported model width: the
+// translation units whose code depends on the width (attention, filters, node
+// layers, evaluator) are built with SO3LR_FEATURES = 128 and again with 256,
+// and each build's code lives in its own namespace (so3lr_b200::f128 /
+// so3lr_b200::f256, opened with SO3LR_SHAPE_BEGIN). Everything else is
+// width-independent and built once.
+//   F = 128: 4 heads of 32, degrees {1,2,3,4} (24 equivariant channels),
+//            32 Bernstein radial functions, 32-wide ev-filter hidden layer
+//            (the released SO3LR v1/s/m shape);
+//   F = 256: 8 heads of 32, degrees {1,1,2,2,3,3,4,4} (48 channels), 64 radial
+//            functions, 64-wide ev-filter hidden layer (the "l" shape).
+// The capability table in model_host.cpp refuses every other shape.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -13,28 +21,78 @@
 #include <stdexcept>
 #include <string>
 
+#ifndef SO3LR_FEATURES
+#define SO3LR_FEATURES 128
+#endif
+#if SO3LR_FEATURES == 128
+#define SO3LR_SHAPE_NS f128
+#elif SO3LR_FEATURES == 256
+#define SO3LR_SHAPE_NS f256
+#else
+#error "SO3LR_FEATURES must be 128 or 256"
+#endif
+#define SO3LR_SHAPE_BEGIN \
+  namespace so3lr_b200 {  \
+  inline namespace SO3LR_SHAPE_NS {
+#define SO3LR_SHAPE_END \
+  }                     \
+  }
+
 namespace so3lr_b200 {
 
-constexpr int kF = 128;       // invariant features
-constexpr int kHeads = 4;     // attention heads == equivariant degrees
+constexpr int kSH = 24;       // distinct real harmonics l = 1..4 (per pair)
 constexpr int kHW = 32;       // head width
-constexpr int kEV = 24;       // equivariant channels (l = 1..4)
-constexpr int kR = 32;        // radial basis functions
-constexpr int kEH = 32;       // hidden width of the ev filter branch (F / 4)
-constexpr int kQKV = 5 * kF;  // q, k, v, q_ev, k_ev per node, head-major [4][5][32]
-constexpr int kIntW = 136;    // 132-wide interaction layer padded to a multiple of 8
 constexpr int kHeadHidden = 128;
 constexpr int kHirsh = 64;
 constexpr int kHeadCat = 2 * kHeadHidden + kHirsh;  // fused first layers of the 3 heads
 constexpr int kHeadCatC6 = kHeadCat + kHirsh;        // ... and of the optional C6 ratio head
 constexpr int kMaxLayers = 8;
+
+}  // namespace so3lr_b200
+
+SO3LR_SHAPE_BEGIN
+constexpr int kF = SO3LR_FEATURES;   // invariant features
+constexpr int kHeads = kF / kHW;     // attention heads == equivariant degree slots
+constexpr int kR = kF / 4;           // radial basis functions
+constexpr int kEH = kF / 4;          // hidden width of the ev filter branch
+constexpr int kQKV = 5 * kF;         // q, k, v, q_ev, k_ev per node, head-major [heads][5][32]
+constexpr int kIntW = (kF + kHeads + 7) / 8 * 8;  // interaction layer (F + heads) padded to a multiple of 8
+// equivariant channels: degree slot s has 2 l_s + 1 channels, l_s = s + 1
+// (F = 128) or s / 2 + 1 (F = 256, every degree twice)
+constexpr int kDupDegrees = kHeads / 4;
+__host__ __device__ constexpr int slot_degree(int s) { return s / kDupDegrees + 1; }
+__host__ __device__ constexpr int slot_width(int s) { return 2 * slot_degree(s) + 1; }
+// first channel of slot s: every degree below l_s fills kDupDegrees slots
+// of 2 l + 1 channels (sum = l_s^2 - 1 per copy), then the earlier copies of l_s
+__host__ __device__ constexpr int slot_offset(int s) {
+  return kDupDegrees * (slot_degree(s) * slot_degree(s) - 1) + (s % kDupDegrees) * slot_width(s);
+}
+constexpr int kEV = slot_offset(kHeads);  // 24 or 48
 // per pair, per block: the cutoff-gradient weight and the ev attention
 // coefficients of both directions per head (+1 pad: rows of 16-byte chunks)
-constexpr int kPairScalars = 10;
+constexpr int kPairScalars = 2 * kHeads + 2;
 // Algorithmic FLOPs of the two filter MLPs of one pair, one direction of the
-// pass (forward, or the reverse input gradients): 2 filters x (R F + F F + 4 H + H F)
+// pass (forward, or the reverse input gradients): 2 filters x (R F + F F + H EH + EH F)
 // multiply-adds x 2. The reverse's first-layer recompute is not counted.
-constexpr double kFilterFlopsPerPair = 2.0 * (kR * kF + kF * kF + 4 * kEH + kEH * kF) * 2.0;
+constexpr double kFilterFlopsPerPair = 2.0 * (kR * kF + kF * kF + kHeads * kEH + kEH * kF) * 2.0;
+
+// degree slot of equivariant channel m
+__host__ __device__ inline int degree_of_channel(int m) {
+  int s = 0;
+#pragma unroll
+  for (int k = 1; k < kHeads; ++k) s += m >= slot_offset(k) ? 1 : 0;
+  return s;
+}
+// the distinct harmonic (0..23, l = 1..4 ascending) that channel m carries
+__host__ __device__ inline int sh_of_channel(int m) {
+  const int s = degree_of_channel(m), l = slot_degree(s);
+  return l * l - 1 + (m - slot_offset(s));
+}
+// (-1)^l of a degree slot: odd l flips sign under v -> -v
+__host__ __device__ inline double parity_sign(int slot) { return (slot_degree(slot) & 1) ? -1.0 : 1.0; }
+SO3LR_SHAPE_END
+
+namespace so3lr_b200 {
 
 inline void cuda_check(cudaError_t e, const char *what) {
   if (e != cudaSuccess) throw std::runtime_error(std::string("CUDA error in ") + what + ": " + cudaGetErrorString(e));
@@ -50,10 +108,6 @@ std::atomic<long long> &launch_counter();
 void allow_dynamic_smem(const void *func, std::size_t bytes);
 #define SO3_LAUNCH(what) (++::so3lr_b200::launch_counter(), ::so3lr_b200::cuda_check(cudaGetLastError(), what))
 
-// degree slot of equivariant channel m (0..23): 3 + 5 + 7 + 9
-__host__ __device__ inline int degree_of_channel(int m) { return m < 3 ? 0 : (m < 8 ? 1 : (m < 15 ? 2 : 3)); }
-// (-1)^l for the degree slot (l = slot + 1): odd l flips sign under v -> -v
-__host__ __device__ inline double parity_sign(int slot) { return (slot & 1) ? 1.0 : -1.0; }
 
 // FP64 tensor-core MMA: D(8x8) = A(8x4, row) * B(4x8, col) + C.
 // Fragment ownership (lane = threadIdx.x % 32, g = lane >> 2, t = lane & 3):

@@ -9,9 +9,9 @@
 #include <numeric>
 #include <sstream>
 
-namespace so3lr_b200 {
+SO3LR_SHAPE_BEGIN
 
-Evaluator::Evaluator(const std::string &model_path, int device) : model_(Model::load(model_path)), device_(device) {
+Evaluator::Evaluator(Model &&model, int device) : model_(std::move(model)), device_(device) {
   int count = 0;
   SO3_CUDA(cudaGetDeviceCount(&count));
   if (device < 0 || device >= count) throw Error("SO3LR: CUDA device " + std::to_string(device) + " not available");
@@ -170,7 +170,7 @@ void Evaluator::upload_weights() {
     o.b0 = push(model_.f64(prefix + ".mlp_rbf.0.bias", {F}));
     o.w1 = push(w1);
     o.b1 = push(model_.f64(prefix + ".mlp_rbf.mlp_rbf_layer_1.0.bias", {F}));
-    o.v0 = push(model_.f64(prefix + ".mlp_ev.0.weight", {H, 4}));
+    o.v0 = push(model_.f64(prefix + ".mlp_ev.0.weight", {H, std::size_t(kHeads)}));
     o.c0 = push(model_.f64(prefix + ".mlp_ev.0.bias", {H}));
     o.v1 = push(v1);
     const auto b1 = model_.f64(prefix + ".mlp_rbf.mlp_rbf_layer_1.0.bias", {F});
@@ -186,12 +186,13 @@ void Evaluator::upload_weights() {
     o.w1_f = push(fragment_major(iF, iF, [&](int oo, int j) { return w1[std::size_t(oo) * F + j]; }));
     o.v1_f = push(fragment_major(iF, iH, [&](int oo, int h) { return v1[std::size_t(oo) * H + h]; }));
     o.w0_f = push(fragment_major(iF, iR, [&](int j, int r) { return w0[std::size_t(j) * R + r]; }));
-    filt_host[filt_count] = {model_.f64(prefix + ".mlp_rbf.0.bias", {F}), bc1, model_.f64(prefix + ".mlp_ev.0.weight", {H, 4}),
+    filt_host[filt_count] = {model_.f64(prefix + ".mlp_rbf.0.bias", {F}), bc1, model_.f64(prefix + ".mlp_ev.0.weight", {H, std::size_t(kHeads)}),
                              model_.f64(prefix + ".mlp_ev.0.bias", {H})};
     FOff32 &o32 = foff32[filt_count++];
+    if (kF != 128) return o;  // the mixed-precision operands exist for F = 128 only
     o32.b0 = push32(model_.f64(prefix + ".mlp_rbf.0.bias", {F}));
     o32.bc1 = push32(bc1);
-    o32.v0 = push32(model_.f64(prefix + ".mlp_ev.0.weight", {H, 4}));
+    o32.v0 = push32(model_.f64(prefix + ".mlp_ev.0.weight", {H, std::size_t(kHeads)}));
     o32.c0 = push32(model_.f64(prefix + ".mlp_ev.0.bias", {H}));
     o32.w0t = push_split(fragment_major(iR, iF, [&](int r, int j) { return w0[std::size_t(j) * R + r]; }));
     o32.w1t = push_split(fragment_major(iF, iF, [&](int j, int oo) { return w1[std::size_t(oo) * F + j]; }));
@@ -226,9 +227,9 @@ void Evaluator::upload_weights() {
     o.cg_int = push(model_.f64(blk + ".interaction_block.so3_conv_invariants.cg_rep", {kEV}));
     static const char *names[5] = {"W_q_inv", "W_k_inv", "W_v_inv", "W_q_ev", "W_k_ev"};
     std::vector<std::vector<double>> w(5);
-    for (int p = 0; p < 5; ++p) w[p] = model_.f64(att + names[p], {4, 32, 32});  // [head][in][out]
-    std::vector<double> qf(4 * 160 * 32), qr(4 * 32 * 160);
-    for (int h = 0; h < 4; ++h)
+    for (int p = 0; p < 5; ++p) w[p] = model_.f64(att + names[p], {std::size_t(kHeads), 32, 32});  // [head][in][out]
+    std::vector<double> qf(kHeads * 160 * 32), qr(kHeads * 32 * 160);
+    for (int h = 0; h < kHeads; ++h)
       for (int p = 0; p < 5; ++p)
         for (int i = 0; i < 32; ++i)
           for (int oo = 0; oo < 32; ++oo) {
@@ -252,12 +253,13 @@ void Evaluator::upload_weights() {
     o.m1b = push(model_.f64(blk + ".mlp_1.1.bias", {F}));
     o.m2w = push(model_.f64(blk + ".mlp_1.3.weight", {F, F}));
     o.m2b = push(model_.f64(blk + ".mlp_1.3.bias", {F}));
-    const auto iw = model_.f64(blk + ".interaction_block.linear_layer.weight", {132, 132});
-    const auto ib = model_.f64(blk + ".interaction_block.linear_layer.bias", {132});
+    constexpr std::size_t kIw = kF + kHeads;  // interaction layer: F features and one L0 invariant per slot
+    const auto iw = model_.f64(blk + ".interaction_block.linear_layer.weight", {kIw, kIw});
+    const auto ib = model_.f64(blk + ".interaction_block.linear_layer.bias", {kIw});
     std::vector<double> iwp(kIntW * kIntW, 0.0), ibp(kIntW, 0.0);
-    for (int r = 0; r < 132; ++r) {
+    for (std::size_t r = 0; r < kIw; ++r) {
       ibp[r] = ib[r];
-      for (int c = 0; c < 132; ++c) iwp[r * kIntW + c] = iw[r * 132 + c];
+      for (std::size_t c = 0; c < kIw; ++c) iwp[r * kIntW + c] = iw[r * kIw + c];
     }
     o.iw = push(iwp);
     o.ib = push(ibp);
@@ -370,8 +372,10 @@ void Evaluator::upload_weights() {
     };
     w.finv = fw(o.finv);
     w.fev = fw(o.fev);
-    w.finv32 = fw32(foff32[2 * std::size_t(b)]);
-    w.fev32 = fw32(foff32[2 * std::size_t(b) + 1]);
+    if (kF == 128) {
+      w.finv32 = fw32(foff32[2 * std::size_t(b)]);
+      w.fev32 = fw32(foff32[2 * std::size_t(b) + 1]);
+    }
     w.cg_att = P(o.cg_att);
     w.cg_int = P(o.cg_int);
     w.qkv_fwd = P(o.qf);
@@ -407,7 +411,7 @@ void Evaluator::upload_weights() {
   rad_.k = P(o_rk);
   rad_.kr = P(o_rkr);
   rad_.gamma = model_.f64("model.radial_embedding.radial_basis_fn.gamma", {})[0];
-  {  // kernel-parameter constants of the tcgen05 filter kernels, per block
+  if (kF == 128) {  // kernel-parameter constants of the tcgen05 filter kernels, per block
     const auto rb = model_.f64("model.radial_embedding.radial_basis_fn.b", {R});
     const auto rk = model_.i64("model.radial_embedding.radial_basis_fn.k");
     const auto rkr = model_.i64("model.radial_embedding.radial_basis_fn.k_rev");
@@ -542,43 +546,6 @@ void Evaluator::exact_sums(const double *v, int stride, int ncol, int nseg, cons
 }
 
 // brick index of a position (the same arithmetic on every rank)
-static int brick_of(const double *x, const SystemSpec &s, const int dims[3]) {
-  int idx[3];
-  for (int d = 0; d < 3; ++d) {
-    double p = x[d] - s.lo[d];
-    p -= std::floor(p / s.len[d]) * s.len[d];
-    int c = int(p * dims[d] / s.len[d]);
-    idx[d] = c < 0 ? 0 : (c >= dims[d] ? dims[d] - 1 : c);
-  }
-  return (idx[2] * dims[1] + idx[1]) * dims[0] + idx[0];
-}
-
-void brick_dims(int nranks, int dims[3]) {
-  dims[0] = dims[1] = dims[2] = 1;
-  int rest = nranks;
-  for (int f = 2; rest > 1;) {
-    if (rest % f == 0) {
-      // give the factor to the dimension with the fewest bricks, z first
-      int k = 2;
-      if (dims[1] < dims[k]) k = 1;
-      if (dims[0] < dims[k]) k = 0;
-      dims[k] *= f;
-      rest /= f;
-    } else {
-      ++f;
-    }
-  }
-}
-
-std::vector<int> partition_atoms(const SystemSpec &s, const double *x, int nranks) {
-  std::vector<int> owner(std::size_t(s.n), 0);
-  if (nranks == 1) return owner;
-  int dims[3];
-  brick_dims(nranks, dims);
-  for (int i = 0; i < s.n; ++i) owner[std::size_t(i)] = brick_of(x + 3 * std::size_t(i), s, dims);
-  return owner;
-}
-
 // ---------------------------------------------------------------------------
 // system preparation
 // ---------------------------------------------------------------------------
@@ -751,10 +718,10 @@ void Evaluator::alloc_atoms() {
   ensure_vec(n1_, layers_, n * kF);
   ensure_vec(A_, layers_, n * kEV);
   ensure_vec(hp_, layers_, n * kF);
-  ensure_vec(gate_, layers_, n * 4);
+  ensure_vec(gate_, layers_, n * kHeads);
   ensure_vec(xhat2_, layers_, n * kF);
   ensure_vec(rstd2_, layers_, n);
-  if (qk_norm_) ensure_vec(qkr_, layers_, n * 16);
+  if (qk_norm_) ensure_vec(qkr_, layers_, n * 4 * kHeads);
   if (residual_scalars_) x0_.reserve(n * kF);
   d_inv_.reserve(n * kF);
   d_ev_.reserve(n * kEV);
@@ -946,15 +913,15 @@ void Evaluator::build_neighbors() {
   fill_pairs(nb_, E, stream_);
   // per-pair storage
   geo_.reserve(std::size_t(P) * kGeo, 1.25);
-  sh_.reserve(std::size_t(P) * kEV, 1.25);
+  sh_.reserve(std::size_t(P) * kSH, 1.25);
   gv_.reserve(std::size_t(P) * 3, 1.25);
-  gl0_.reserve(std::size_t(P) * 4, 1.25);
+  gl0_.reserve(std::size_t(P) * kHeads, 1.25);
   pair_sc_.reserve(std::size_t(P) * kPairScalars, 1.25);
   g_filt_inv_.reserve(std::size_t(P) * kF, 1.25);
   g_filt_ev_.reserve(std::size_t(P) * kF, 1.25);
   drbf_.reserve(std::size_t(P) * kR, 1.25);
   g_r_.reserve(std::size_t(P), 1.25);
-  g_y_.reserve(std::size_t(P) * kEV, 1.25);
+  g_y_.reserve(std::size_t(P) * kSH, 1.25);
   while (int(f_inv_.size()) < layers_) {
     f_inv_.emplace_back(new DeviceArray<double>());
     f_ev_.emplace_back(new DeviceArray<double>());
@@ -1001,6 +968,7 @@ void Evaluator::compute() {
   for (int b = 0; b < layers_; ++b) {
     const BlockW &w = blocks_[b];
     prof_begin(kProfFilterForward);
+#if SO3LR_FEATURES == 128
     if (mixed_ && mixed_tc_)
       launch_filter_forward_tc(P, geo_.get(), nb_.pair_a, nb_.pair_b, b == 0 ? nullptr : evb_[b]->get(),
                                tc_fwd_consts_[b], w.finv32, w.fev32, f_inv_[b]->get(), f_ev_[b]->get(),
@@ -1011,6 +979,7 @@ void Evaluator::compute() {
                                   w.finv32, w.fev32, rad_, f_inv_[b]->get(), f_ev_[b]->get(),
                                   reinterpret_cast<float *>(sp_[b]->get()), b == 0 ? drbf_.get() : nullptr, s);
     else
+#endif
       launch_filter_forward(P, geo_.get(), nb_.pair_a, nb_.pair_b, b == 0 ? nullptr : evb_[b]->get(), w.cg_att,
                             w.finv, w.fev, rad_, f_inv_[b]->get(), f_ev_[b]->get(), sp_[b]->get(),
                             b == 0 ? drbf_.get() : nullptr, s);
@@ -1022,7 +991,7 @@ void Evaluator::compute() {
       g.A = xb_[b]->get() + (identity_ ? 0 : r0 * kF); g.lda = kF; g.strideA = 32;
       g.W = w.qkv_fwd; g.ldw = 32; g.transB = true; g.strideW = 160 * 32;
       g.C = qkv_[b]->get() + (identity_ ? 0 : r0 * kQKV); g.ldc = kQKV; g.strideC = 160;
-      g.batch = 4;
+      g.batch = kHeads;
       launch_gemm(g, s);
       if (!identity_ && halo_recv_off_[nranks_] > 0) {
         g.M = int(halo_recv_off_[nranks_]);
@@ -1033,7 +1002,7 @@ void Evaluator::compute() {
       }
       if (qk_norm_) {
         launch_qk_norm(identity_ ? N : n, nullptr, qkv_[b]->get() + (identity_ ? 0 : r0 * kQKV),
-                       qkr_[b]->get() + (identity_ ? 0 : r0 * 16), s);
+                       qkr_[b]->get() + (identity_ ? 0 : r0 * 4 * kHeads), s);
         if (!identity_ && halo_recv_off_[nranks_] > 0)
           launch_qk_norm(int(halo_recv_off_[nranks_]), halo_recv_rows_.get(), qkv_[b]->get(), qkr_[b]->get(), s);
       }
@@ -1076,7 +1045,7 @@ void Evaluator::compute() {
     }
     launch_post_attn_final(n, cat_.get() + r0 * kIntW, t_.get() + r0 * kIntW, A_[b]->get() + r0 * kEV, norm2_,
                            w.ln2w, w.ln2b, xhat2_[b]->get() + r0 * kF, rstd2_[b]->get() + r0,
-                           gate_[b]->get() + r0 * 4, xb_[b + 1]->get() + r0 * kF, evb_[b + 1]->get() + r0 * kEV, s);
+                           gate_[b]->get() + r0 * kHeads, xb_[b + 1]->get() + r0 * kF, evb_[b + 1]->get() + r0 * kEV, s);
     if (b + 1 < layers_) {
       if (residual_scalars_)  // the next block's input, on this GPU's rows
         launch_residual_combine(n, xb_[b + 1]->get() + r0 * kF, x0_.get() + r0 * kF, resid_[b + 1], x0s_[b + 1],
@@ -1146,7 +1115,7 @@ void Evaluator::compute() {
     const BlockW &w = blocks_[b];
     launch_post_attn_rev_final(n, gx + r0 * kF, gev ? gev + r0 * kEV : nullptr, xhat2_[b]->get() + r0 * kF,
                                rstd2_[b]->get() + r0, norm2_, w.ln2w, A_[b]->get() + r0 * kEV,
-                               gate_[b]->get() + r0 * 4, g_t_.get() + r0 * kIntW, g_A_.get() + r0 * kEV, s);
+                               gate_[b]->get() + r0 * kHeads, g_t_.get() + r0 * kIntW, g_A_.get() + r0 * kEV, s);
     {  // g_cat = g_t W_int; g_post = g_cat[:, :128] + g_t[:, :128]
       GemmArgs g{};
       g.M = n; g.N = kIntW; g.K = kIntW;
@@ -1187,6 +1156,7 @@ void Evaluator::compute() {
                              g_a_.get(), g_A_.get(), norm_, b > 0 ? g_qkv_.get() : nullptr, pair_sc_.get(),
                              g_filt_inv_.get(), g_filt_ev_.get(), s);
     prof_begin(kProfFilterReverse);
+#if SO3LR_FEATURES == 128
     if (mixed_ && mixed_tc_)
       launch_filter_reverse_tc(P, geo_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr,
                                tc_rev_consts_[b], w.finv32, w.fev32, g_filt_inv_.get(), g_filt_ev_.get(),
@@ -1199,6 +1169,7 @@ void Evaluator::compute() {
                                   reinterpret_cast<const float *>(sp_[b]->get()), drbf_.get(), g_A_.get(),
                                   pair_sc_.get(), b > 0, b < layers_ - 1, g_r_.get(), g_y_.get(), gl0_.get(), s);
     else
+#endif
       launch_filter_reverse(P, geo_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr, w.cg_att,
                             w.finv, w.fev, rad_, g_filt_inv_.get(), g_filt_ev_.get(), sp_[b]->get(), drbf_.get(),
                             g_A_.get(), pair_sc_.get(), b > 0, b < layers_ - 1, g_r_.get(), g_y_.get(),
@@ -1206,7 +1177,7 @@ void Evaluator::compute() {
     prof_end(kProfFilterReverse, kFilterFlopsPerPair * double(P));
     if (b > 0) {
       if (qk_norm_)  // gradient w.r.t. the projections before their normalisation
-        launch_qk_norm_reverse(n, qkv_[b]->get() + r0 * kQKV, qkr_[b]->get() + r0 * 16, g_qkv_.get() + r0 * kQKV, s);
+        launch_qk_norm_reverse(n, qkv_[b]->get() + r0 * kQKV, qkr_[b]->get() + r0 * 4 * kHeads, g_qkv_.get() + r0 * kQKV, s);
       GemmArgs g{};  // g_x_in = g_a + per-head (g_qkv W^T)
       g.M = n; g.N = 32; g.K = 160;
       g.A = g_qkv_.get() + r0 * kQKV; g.lda = kQKV; g.strideA = 160;
@@ -1214,7 +1185,7 @@ void Evaluator::compute() {
       g.C = gx_next + r0 * kF; g.ldc = kF; g.strideC = 32;
       g.aux = g_a_.get() + r0 * kF; g.ldaux = kF; g.strideAux = 32;
       g.epi = Epi::AddResidual;
-      g.batch = 4;
+      g.batch = kHeads;
       launch_gemm(g, s);
       // block b's input is resid[b] y + x0[b] x0: the previous output y gets resid[b] of it
       if (residual_scalars_) launch_scale_rows(n, gx_next + r0 * kF, resid_[b], s);
@@ -1415,4 +1386,23 @@ void Evaluator::md_download(double *x, double *v) {
   fetch(v, v_.get());
 }
 
+void Evaluator::set_mixed_precision(bool on) {
+  if (on && kF != 128)
+    throw Error("SO3LR: mixed precision is implemented for F = 128 models only; this model has F = " +
+                std::to_string(kF));
+  mixed_ = on;
+}
+
+SO3LR_SHAPE_END
+
+namespace so3lr_b200 {
+#if SO3LR_FEATURES == 128
+std::unique_ptr<EvaluatorApi> create_evaluator_f128(Model &&model, int device) {
+  return std::make_unique<Evaluator>(std::move(model), device);
+}
+#else
+std::unique_ptr<EvaluatorApi> create_evaluator_f256(Model &&model, int device) {
+  return std::make_unique<Evaluator>(std::move(model), device);
+}
+#endif
 }  // namespace so3lr_b200

@@ -17,152 +17,48 @@
 
 #include "nccl_dyn.hpp"
 
+#include "api.hpp"
 #include "kernels.cuh"
 #include "model_host.hpp"
 
-namespace so3lr_b200 {
+SO3LR_SHAPE_BEGIN
 
-template <class T>
-class DeviceArray {
+class Evaluator final : public EvaluatorApi {
  public:
-  DeviceArray() = default;
-  DeviceArray(const DeviceArray &) = delete;
-  DeviceArray &operator=(const DeviceArray &) = delete;
-  ~DeviceArray() { release(); }
-  void release() {
-    if (ptr_) cudaFree(ptr_);
-    ptr_ = nullptr;
-    cap_ = 0;
-  }
-  // grow-only; contents are not preserved
-  T *reserve(std::size_t n, double slack = 1.0) {
-    if (n > cap_) {
-      release();
-      const std::size_t want = std::max<std::size_t>(1, std::size_t(double(n) * slack));
-      SO3_CUDA(cudaMalloc(&ptr_, want * sizeof(T)));
-      cap_ = want;
-    }
-    return ptr_;
-  }
-  T *get() const { return ptr_; }
-  std::size_t capacity() const { return cap_; }
-  std::size_t bytes() const { return cap_ * sizeof(T); }
-
- private:
-  T *ptr_ = nullptr;
-  std::size_t cap_ = 0;
-};
-
-// What the caller asks to be evaluated. Atoms of one image are contiguous.
-struct SystemSpec {
-  int n = 0;
-  bool periodic = false;
-  double lo[3] = {0, 0, 0};
-  double len[3] = {0, 0, 0};
-  std::vector<int> z;                 // atomic numbers, 1..99
-  std::vector<int> image_start;       // n_images + 1 (one image when not batched)
-  std::vector<double> image_charge;   // n_images
-  std::vector<double> image_mult;     // n_images
-};
-
-struct StepStats {
-  long long edges = 0, pairs = 0;
-};
-
-// owner rank of every atom: spatial bricks of the periodic box (host-only, the
-// same arithmetic on every rank)
-std::vector<int> partition_atoms(const SystemSpec &s, const double *x, int nranks);
-void brick_dims(int nranks, int dims[3]);
-
-class Evaluator {
- public:
-  Evaluator(const std::string &model_path, int device);
-  ~Evaluator();
-  const Model &model() const { return model_; }
-  cudaStream_t stream() const { return stream_; }
-  int device() const { return device_; }
-
-  // Validates Z, charges and multiplicities (so3lr_charge_spin.cpp:116-141),
-  // builds the charge/spin offset tables, uploads static per-atom data.
-  // host_x (N x 3, input order) is needed only to partition atoms over GPUs.
-  void prepare(const SystemSpec &spec, const double *host_x = nullptr);
-  // Join a group of nranks GPUs (one Evaluator per GPU, same model, same
-  // system); unique_id is an ncclUniqueId made by rank 0 and shared by the
-  // caller. Atoms are partitioned into spatial bricks of the periodic box.
-  void set_comm(int nranks, int rank, const void *unique_id);
-  int nranks() const { return nranks_; }
-  // true once compute() has run for the current system
-  bool has_result() const { return computed_; }
-  int owned_atoms() const { return n_own_; }
-  const SystemSpec &spec() const { return spec_; }
-
-  // Device positions buffer for the prepared system (N x 3). Callers may write
-  // it directly (device-resident MD) or through upload_positions().
-  double *positions() { return x_.get(); }
-  void upload_positions(const double *host_x);
-  // Run the whole evaluation on stream(); outputs stay on the device.
-  void compute();
-  // Copy results to host (after compute(); synchronises the stream).
-  struct HostResult {
-    double energy = 0;
-    std::array<double, 6> virial{};
-  };
+  Evaluator(Model &&model, int device);
+  ~Evaluator() override;
+  const Model &model() const override { return model_; }
+  cudaStream_t stream() const override { return stream_; }
+  int device() const override { return device_; }
+  void prepare(const SystemSpec &spec, const double *host_x = nullptr) override;
+  void set_comm(int nranks, int rank, const void *unique_id) override;
+  int nranks() const override { return nranks_; }
+  bool has_result() const override { return computed_; }
+  int owned_atoms() const override { return n_own_; }
+  const SystemSpec &spec() const override { return spec_; }
+  double *positions() override { return x_.get(); }
+  void upload_positions(const double *host_x) override;
+  void compute() override;
   HostResult download(double *f, double *eatom, double *charges, double *ratios, double *e_learned, double *e_zbl,
-                      double *e_lr, double *e_elec, double *e_disp, double *image_energy);
-  // per-atom virial (natoms x 6, xx yy zz xy xz yz) of the last compute(), input
-  // atom order; collective when decomposed (synchronises the stream)
-  void download_virial_atom(double *vatom);
-  // Rank-local frame (local_frame.cu): this rank passes its own nlocal atoms
-  // (global tags 1..frame.n, positions, atomic numbers; frame.z unused) and gets
-  // the forces (nlocal x 3), and optionally per-atom energies and virials, of
-  // those atoms back. Collective on a multi-GPU handle.
+                      double *e_lr, double *e_elec, double *e_disp, double *image_energy) override;
+  void download_virial_atom(double *vatom) override;
   HostResult compute_local(const SystemSpec &frame, int nlocal, const long long *tag, const double *x, const int *z,
-                           double *f, double *eatom, double *vatom);
-  const double *forces() const { return force_.get(); }
-  const double *energy_device() const { return totals_.get(); }  // [0] energy, [1..6] virial
-  StepStats stats() const { return stats_; }
-  // long-range constants and reference tables (device) of the loaded model
-  struct LongRangeTables {
-    LrDev params;
-    const double *alpha_ref, *c6_ref;
-    int table_size;
-    double cutoff;
-  };
-  LongRangeTables long_range_tables() const { return {lr_, alpha_ref_, c6_ref_, ref_table_, lr_cut_}; }
-  bool has_c6_head() const { return heads_.c6_w2 != nullptr; }
-  std::size_t device_bytes() const;
-
-  // Optional CUDA-event timing on stream() of the pair-filter kernels and of the
-  // multi-GPU exchange phases (ProfileKind). read_profile() synchronises,
-  // returns the summed device time, launch count and algorithmic FLOPs, and resets.
-  enum ProfileKind {
-    kProfFilterForward = 0,
-    kProfFilterReverse = 1,
-    kProfPositionGather = 2,   // all-gather of positions after the drift
-    kProfHaloLists = 3,        // halo-list rebuild: lists, count all-gather, host check
-    kProfFeatureHalo = 4,      // block-feature halo exchanges (forward)
-    kProfAdjointHalo = 5,      // block-adjoint halo exchanges (reverse)
-    kProfLrGather = 6,         // all-gathers of charges and ratios before the long range
-    kProfExactSums = 7,        // exact global sums (integer all-gathers)
-    kProfKinds = 8
-  };
-  void set_profiling(bool on) { profiling_ = on; }
-  // Arithmetic of the pair-filter MLPs: float64 (default) or mixed (three-pass
-  // TF32 tensor-core GEMMs with float32 accumulation, filter_mixed.cu); every
-  // other step stays float64. Takes effect from the next evaluation.
-  void set_mixed_precision(bool on) { mixed_ = on; }
-  bool mixed_precision() const { return mixed_; }
-  void read_profile(int kernel, double *ms, long long *launches, double *flops);
-
-  // velocity-Verlet MD on the device (LAMMPS metal units); masses in g/mol
-  void md_setup(const double *host_v, const double *host_mass);
-  // Nose-Hoover chain (thermostat.cu) for the following md_steps; t_damp_ps <= 0
-  // switches back to NVE
-  void md_thermostat(double t_target_k, double t_damp_ps, int chain);
-  // the chain's energy: sum_j Q_j v_j^2 / 2 + N_f kT eta_1 + kT sum_{j>1} eta_j (eV)
-  double md_thermostat_energy();
-  void md_steps(int nsteps, double dt_ps);
-  void md_download(double *x, double *v);
+                           double *f, double *eatom, double *vatom) override;
+  const double *forces() const override { return force_.get(); }
+  const double *energy_device() const override { return totals_.get(); }
+  StepStats stats() const override { return stats_; }
+  LongRangeTables long_range_tables() const override { return {lr_, alpha_ref_, c6_ref_, ref_table_, lr_cut_}; }
+  bool has_c6_head() const override { return heads_.c6_w2 != nullptr; }
+  std::size_t device_bytes() const override;
+  void set_profiling(bool on) override { profiling_ = on; }
+  void set_mixed_precision(bool on) override;
+  bool mixed_precision() const override { return mixed_; }
+  void read_profile(int kernel, double *ms, long long *launches, double *flops) override;
+  void md_setup(const double *host_v, const double *host_mass) override;
+  void md_thermostat(double t_target_k, double t_damp_ps, int chain) override;
+  double md_thermostat_energy() override;
+  void md_steps(int nsteps, double dt_ps) override;
+  void md_download(double *x, double *v) override;
 
  private:
   Model model_;
@@ -278,4 +174,4 @@ class Evaluator {
   void build_neighbors();
 };
 
-}  // namespace so3lr_b200
+SO3LR_SHAPE_END

@@ -14,19 +14,19 @@
 // linear in the incoming gradient, so the two directions' gradients are summed
 // first and pushed through the MLP once.
 //
-// Tile: 64 pairs per CTA, 8 warps, m16n8k8 DMMA on fragments read from shared
-// memory (pair activations, one 16-byte load per row) and L2-resident weights
-// prepared in fragment order (16-byte loads per lane and k-step). The 128-wide
-// GEMMs give each warp a 64x16 column slab of the 64x128 output, so every
-// weight column is fetched from L2 by one warp of the CTA only; the 32-wide
-// ones use 16x16 warp blocks.
+// Tile: TP pairs per CTA (64 for F = 128, 32 for F = 256), 8 warps, m16n8k8
+// DMMA on fragments read from shared memory (pair activations, one 16-byte load
+// per row) and L2-resident weights prepared in fragment order (16-byte loads per
+// lane and k-step). The F-wide GEMMs give each warp a TP x (F / 8) column slab
+// of the TP x F output, so every weight column is fetched from L2 by one warp of
+// the CTA only; the R- and EH-wide ones use 16x16 warp blocks.
 #include <cooperative_groups.h>
 
 #include "filter_common.cuh"
 #include "kernels.cuh"
 #include "sh.cuh"
 
-namespace so3lr_b200 {
+SO3LR_SHAPE_BEGIN
 namespace {
 
 // b[j] = {B(8 ks + 2t, n), B(8 ks + 2t + 1, n)}, n = 32 slab + 8 (ni0 + j) + g, for
@@ -44,30 +44,31 @@ __device__ __forceinline__ void load_bfrag(const double *__restrict__ Bf, int ks
   }
 }
 
-// warp tile 64 x 16 (all 64 rows, cols 16 wc..) as 4 x 2 m16n8 blocks: each
-// weight column is read by one warp of the CTA only
-// acc += A(64 x K, smem, row stride lda) * B(K x 128, fragment-major)
+// warp slab TP x (F / 8) (all rows, cols wc F / 8 ..) as kMT x kNB m16n8
+// blocks: each weight column is read by one warp of the CTA only
+// acc += A(TP x K, smem, row stride lda) * B(K x F, fragment-major)
 template <int K>
-__device__ inline void mma_64x16(double (&acc)[4][2][4], const double *A, int lda, const double *__restrict__ Bf,
-                                 int wc, int lane) {
+__device__ inline void mma_64x16(double (&acc)[kMT][kNB][4], const double *A, int lda,
+                                 const double *__restrict__ Bf, int wc, int lane) {
   const int g = lane >> 2, t = lane & 3;
+  constexpr int kCW = kF / 8;  // columns per warp
 #pragma unroll 2
   for (int ks = 0; ks < K / 8; ++ks) {
-    double b[2][2];
-    load_bfrag<2>(Bf, ks, 4, wc >> 1, (wc & 1) * 2, lane, b);
+    double b[kNB][2];
+    load_bfrag<kNB>(Bf, ks, kF / 32, (wc * kCW) / 32, ((wc * kCW) % 32) / 8, lane, b);
 #pragma unroll
-    for (int mi = 0; mi < 4; ++mi) {
+    for (int mi = 0; mi < kMT; ++mi) {
       double a[4];
       load_afrag(A, lda, mi * 16, ks, g, t, a);
 #pragma unroll
-      for (int ni = 0; ni < 2; ++ni) dmma16(acc[mi][ni], a, b[ni]);
+      for (int ni = 0; ni < kNB; ++ni) dmma16(acc[mi][ni], a, b[ni]);
     }
   }
 }
 
-// warp tile 16 x 16 (rows r0.., cols 16 wc..) of a 64 x 32 output, the two K
-// halves as independent accumulation chains:
-// acc += A(rows, K, smem lda) * B(K x 32, fragment-major)
+// warp tile 16 x 16 (rows r0.., cols 16 wc..) of a TP x kR output (kR == kEH),
+// the two K halves as independent accumulation chains:
+// acc += A(rows, K, smem lda) * B(K x kR, fragment-major)
 template <int K>
 __device__ inline void mma_16x16(double (&acc)[2][4], const double *A, int lda, int r0,
                                  const double *__restrict__ Bf, int wc, int lane) {
@@ -80,8 +81,13 @@ __device__ inline void mma_16x16(double (&acc)[2][4], const double *A, int lda, 
     double a0[4], a1[4], b0[2][2], b1[2][2];
     load_afrag(A, lda, r0, ks, g, t, a0);
     load_afrag(A, lda, r0, ks + K / 16, g, t, a1);
-    load_bfrag<2>(Bf, ks, 1, 0, 2 * wc, lane, b0);
-    load_bfrag<2>(Bf, ks + K / 16, 1, 0, 2 * wc, lane, b1);
+    if constexpr (kR == 32) {  // one 32-column slab
+      load_bfrag<2>(Bf, ks, 1, 0, 2 * wc, lane, b0);
+      load_bfrag<2>(Bf, ks + K / 16, 1, 0, 2 * wc, lane, b1);
+    } else {
+      load_bfrag<2>(Bf, ks, kR / 32, wc >> 1, (wc & 1) * 2, lane, b0);
+      load_bfrag<2>(Bf, ks + K / 16, kR / 32, wc >> 1, (wc & 1) * 2, lane, b1);
+    }
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       dmma16(acc[j], a0, b0[j]);
@@ -97,7 +103,7 @@ __device__ inline void mma_16x16(double (&acc)[2][4], const double *A, int lda, 
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// forward: f_inv[p][128], f_ev[p][128]
+// forward: f_inv[p][F], f_ev[p][F]
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256, 2) k_filter_forward(int P, const double *__restrict__ geo,
                                                         const int *__restrict__ pa, const int *__restrict__ pb,
@@ -109,8 +115,8 @@ __global__ void __launch_bounds__(256, 2) k_filter_forward(int P, const double *
   double *rbf = sm;               // TP x LDR
   double *u = rbf + TP * LDR;     // TP x LDU
   double *w = u + TP * LDU;       // TP x LDR
-  double *l0 = w + TP * LDR;      // TP x 4
-  double *rr = l0 + TP * 4;       // TP
+  double *l0 = w + TP * LDR;      // TP x kHeads
+  double *rr = l0 + TP * kHeads;  // TP
   const int p0 = blockIdx.x * TP;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   if (tid < TP) {
@@ -124,7 +130,7 @@ __global__ void __launch_bounds__(256, 2) k_filter_forward(int P, const double *
   if (drbf != nullptr) {
     // d rbf_k / dr for the reverse pass (Bernstein derivative,
     // block2_attention_input_reverse.cpp:322-333): zero where the basis is clamped
-    const int pl = tid >> 2, k0 = (tid & 3) * 8;
+    const int pl = (tid >> kTPPLog), k0 = ((tid & (kTPP - 1))) * 8;
     const int p = p0 + pl;
     if (p < P) {
       const double raw_x = exp(-rad.gamma * rr[pl]);
@@ -144,31 +150,43 @@ __global__ void __launch_bounds__(256, 2) k_filter_forward(int P, const double *
   for (int filt = 0; filt < 2; ++filt) {
     const FilterW &W = filt ? fev : finv;
     double *out = filt ? f_ev : f_inv;
-    {  // ev branch hidden layer: w = silu(L0 V0^T + c0), 64 x 32
-      const int pl = tid >> 2, j0 = (tid & 3) * 8;
-      const double l00 = l0[pl * 4], l01 = l0[pl * 4 + 1], l02 = l0[pl * 4 + 2], l03 = l0[pl * 4 + 3];
+    {  // ev branch hidden layer: w = silu(L0 V0^T + c0), TP x EH
+      const int pl = (tid >> kTPPLog), j0 = ((tid & (kTPP - 1))) * (kEH / kTPP);
+      if constexpr (kHeads == 4) {
+        const double l00 = l0[pl * 4], l01 = l0[pl * 4 + 1], l02 = l0[pl * 4 + 2], l03 = l0[pl * 4 + 3];
 #pragma unroll
-      for (int j = j0; j < j0 + 8; ++j) {
-        const double s = l00 * W.v0[j * 4] + l01 * W.v0[j * 4 + 1] + l02 * W.v0[j * 4 + 2] + l03 * W.v0[j * 4 + 3];
-        w[pl * LDR + j] = silu(s + W.c0[j]);
+        for (int j = j0; j < j0 + 8; ++j) {
+          const double s = l00 * W.v0[j * 4] + l01 * W.v0[j * 4 + 1] + l02 * W.v0[j * 4 + 2] + l03 * W.v0[j * 4 + 3];
+          w[pl * LDR + j] = silu(s + W.c0[j]);
+        }
+      } else {
+        double lv[kHeads];
+#pragma unroll
+        for (int d = 0; d < kHeads; ++d) lv[d] = l0[pl * kHeads + d];
+#pragma unroll
+        for (int j = j0; j < j0 + kEH / kTPP; ++j) {
+          double s = lv[0] * W.v0[j * kHeads];
+#pragma unroll
+          for (int d = 1; d < kHeads; ++d) s += lv[d] * W.v0[j * kHeads + d];
+          w[pl * LDR + j] = silu(s + W.c0[j]);
+        }
       }
     }
-    double acc[4][2][4];
+    double acc[kMT][kNB][4];
 #pragma unroll
-    for (int mi = 0; mi < 4; ++mi)
+    for (int mi = 0; mi < kMT; ++mi)
 #pragma unroll
-      for (int ni = 0; ni < 2; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.0;
+      for (int ni = 0; ni < kNB; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.0;
     mma_64x16<kR>(acc, rbf, LDR, W.w0t_f, warp, lane);
     // hidden layer u = silu(pre) to shared memory, and silu'(pre) for the
     // reverse pass in the accumulator order of the reverse's 32 x 32 warp tiling
 #pragma unroll
-    for (int mi = 0; mi < 4; ++mi)
+    for (int mi = 0; mi < kMT; ++mi)
 #pragma unroll
-      for (int ni = 0; ni < 2; ++ni) {
-        const int col = warp * 16 + ni * 8 + 2 * t;
+      for (int ni = 0; ni < kNB; ++ni) {
+        const int col = warp * (kF / 8) + ni * 8 + 2 * t;
         const double bb0 = W.b0[col], bb1 = W.b0[col + 1];
-        double *sp_blk = sp + sp_offset(blockIdx.x, filt, (mi >> 1) * 4 + (warp >> 1)) +
-                         (((mi & 1) * 4 + (warp & 1) * 2 + ni) * 2) * 64;
+        double *sp_blk = sp + sp_block(blockIdx.x, filt, warp, mi, ni);
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {  // rows g and g + 8 of the m16 block
           const int row = mi * 16 + hf * 8 + g;
@@ -184,15 +202,15 @@ __global__ void __launch_bounds__(256, 2) k_filter_forward(int P, const double *
     mma_64x16<kF>(acc, u, LDU, W.w1t_f, warp, lane);
     mma_64x16<kEH>(acc, w, LDR, W.v1t_f, warp, lane);
 #pragma unroll
-    for (int mi = 0; mi < 4; ++mi)
+    for (int mi = 0; mi < kMT; ++mi)
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         const int row = mi * 16 + hf * 8 + g;
         const int p = p0 + row;
         if (p >= P) continue;
 #pragma unroll
-        for (int ni = 0; ni < 2; ++ni) {
-          const int col = warp * 16 + ni * 8 + 2 * t;
+        for (int ni = 0; ni < kNB; ++ni) {
+          const int col = warp * (kF / 8) + ni * 8 + 2 * t;
           double2 v;
           v.x = acc[mi][ni][2 * hf] + W.bc1[col];
           v.y = acc[mi][ni][2 * hf + 1] + W.bc1[col + 1];
@@ -207,7 +225,7 @@ void launch_filter_forward(int P, const double *geo, const int *pair_a, const in
                            const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,
                            double *f_inv, double *f_ev, double *sp, double *drbf, cudaStream_t s) {
   if (P == 0) return;
-  const size_t smem = sizeof(double) * (TP * LDR * 2 + TP * LDU + TP * 4 + TP);
+  const size_t smem = sizeof(double) * (TP * LDR * 2 + TP * LDU + TP * kHeads + TP);
   allow_dynamic_smem(reinterpret_cast<const void *>(k_filter_forward), smem);
   k_filter_forward<<<(P + TP - 1) / TP, 256, smem, s>>>(P, geo, pair_a, pair_b, ev, cg_att, finv, fev, rad, f_inv,
                                                          f_ev, sp, drbf);
@@ -217,7 +235,7 @@ void launch_filter_forward(int P, const double *geo, const int *pair_a, const in
 // ---------------------------------------------------------------------------
 // reverse: filter input gradients for both directions of every pair, then the
 // radial, cutoff and spherical-harmonic gradients accumulated into gv[p] (3)
-// and, when ev is live, the L0 gradient gl0[p][4].
+// and, when ev is live, the L0 gradient gl0[p][kHeads].
 // g_filt_inv/g_filt_ev[p][128]: dL/d(filter) with both directions summed,
 // written by the attention reverse. pair_sc[p][10] = the cutoff-gradient weight
 // sum_h (alpha s) over both directions and both attentions, then the ev
@@ -229,8 +247,8 @@ void launch_filter_forward(int P, const double *geo, const int *pair_a, const in
 
 // One cluster of two CTAs per tile of TP pairs: CTA rank 0 pushes the gradient
 // of the invariant filter through its MLP, rank 1 that of the ev filter. Each
-// CTA holds one 64 x 128 gradient tile (109 KB of shared memory, <= 128
-// registers per thread), so two CTAs fit on an SM. The radial-basis and L0
+// CTA holds one TP x F gradient tile (64 x 128 or 32 x 256: 109 KB of shared
+// memory with the rest, <= 128 registers per thread), so two CTAs fit on an SM. The radial-basis and L0
 // gradients of rank 1 are read by rank 0 through distributed shared memory and
 // added to its own (rank 0 + rank 1, a fixed order), and rank 0 finishes the
 // pair: radial/cutoff derivative, spherical-harmonic VJP, Cartesian gradient.
@@ -246,8 +264,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
   extern __shared__ double sm[];
   double *gF = sm;                // TP x LDU: filter gradient, then the hidden pre-activation gradient
   double *gw = gF + TP * LDU;     // TP x LDR: ev-hidden gradient, then the radial-basis gradient
-  double *l0 = gw + TP * LDR;     // TP x 4
-  double *gl = l0 + TP * 4;       // TP x 4
+  double *l0 = gw + TP * LDR;     // TP x kHeads
+  double *gl = l0 + TP * kHeads;  // TP x kHeads
   const int tile = blockIdx.x >> 1;
   const int p0 = tile * TP;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
@@ -257,7 +275,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
   const double *w0_f = f ? fev.w0_f : finv.w0_f;
   const double *v0 = f ? fev.v0 : finv.v0;
   const double *c0 = f ? fev.c0 : finv.c0;
-  const double *sp_tile = sp + sp_offset(tile, f, warp);  // prefetched below; read in slab order
+  const double *sp_tile = sp + sp_offset(tile, f, warp);  // this warp's eighth of the tile's silu', prefetched below
 
   stage_rows<kF>(gF, LDU, f ? g_filt_ev : g_filt_inv, p0, P);
   cp_async_commit();
@@ -269,21 +287,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
   cp_async_wait<0>();
   __syncthreads();
 
-  // gradient of the hidden layer: (gF W1) * silu'(pre), warp slab 64 x 16
-  // (hidden units 16 warp ..); silu' is stored in the 32 x 32 warp-block order
-  // (sp_offset), whose (warp, mi, ni) block this slab's (mi, ni) maps to
-  double acc[4][2][4];
+  // gradient of the hidden layer: (gF W1) * silu'(pre), warp slab TP x F/8
+  // (hidden units F/8 warp ..); silu' is read in the order the forward wrote
+  // it (sp_block)
+  double acc[kMT][kNB][4];
 #pragma unroll
-  for (int mi = 0; mi < 4; ++mi)
+  for (int mi = 0; mi < kMT; ++mi)
 #pragma unroll
-    for (int ni = 0; ni < 2; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.0;
+    for (int ni = 0; ni < kNB; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.0;
   mma_64x16<kF>(acc, gF, LDU, w1_f, warp, lane);
 #pragma unroll
-  for (int mi = 0; mi < 4; ++mi)
+  for (int mi = 0; mi < kMT; ++mi)
 #pragma unroll
-    for (int ni = 0; ni < 2; ++ni) {
-      const double *sp_blk = sp + sp_offset(tile, f, (mi >> 1) * 4 + (warp >> 1)) +
-                             (((mi & 1) * 4 + (warp & 1) * 2 + ni) * 2) * 64;
+    for (int ni = 0; ni < kNB; ++ni) {
+      const double *sp_blk = sp + sp_block(tile, f, warp, mi, ni);
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         const double2 s = __ldg(reinterpret_cast<const double2 *>(sp_blk + hf * 64 + lane * 2));
@@ -291,8 +308,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
         acc[mi][ni][2 * hf + 1] *= s.y;
       }
     }
-  // ev branch: g_w = gF V1 (64 x 32), warp tile 16 x 16
-  const int wr = warp >> 1, wc = warp & 1;
+  // ev branch: g_w = gF V1 (TP x EH), warp tile 16 x 16
+  const int wr = (warp >> (kEH / 32)), wc = (warp & (kEH / 16 - 1));
   double gwa[2][4];
 #pragma unroll
   for (int j = 0; j < 2; ++j) gwa[j][0] = gwa[j][1] = gwa[j][2] = gwa[j][3] = 0.0;
@@ -307,16 +324,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
   __syncthreads();  // every warp is done reading gF
   // the hidden pre-activation gradient replaces gF in shared memory
 #pragma unroll
-  for (int mi = 0; mi < 4; ++mi)
+  for (int mi = 0; mi < kMT; ++mi)
 #pragma unroll
-    for (int ni = 0; ni < 2; ++ni)
+    for (int ni = 0; ni < kNB; ++ni)
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        const int row = mi * 16 + hf * 8 + g, col = warp * 16 + ni * 8 + 2 * t;
+        const int row = mi * 16 + hf * 8 + g, col = warp * (kF / 8) + ni * 8 + 2 * t;
         *reinterpret_cast<double2 *>(gF + row * LDU + col) = make_double2(acc[mi][ni][2 * hf], acc[mi][ni][2 * hf + 1]);
       }
   __syncthreads();
-  // radial-basis gradient g_rbf = g_pre W0 (64 x 32), warp tile 16 x 16
+  // radial-basis gradient g_rbf = g_pre W0 (TP x R), warp tile 16 x 16
   double grb[2][4];
 #pragma unroll
   for (int j = 0; j < 2; ++j) grb[j][0] = grb[j][1] = grb[j][2] = grb[j][3] = 0.0;
@@ -324,20 +341,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
   // L0 gradient: g_pe = g_w * silu'(L0 V0^T + c0), gl[d] = sum_j g_pe[j] V0[j][d]
   if (need_l0) {
     {
-      const int pl = tid >> 2, j0 = (tid & 3) * 8;
-      const double l00 = l0[pl * 4], l01 = l0[pl * 4 + 1], l02 = l0[pl * 4 + 2], l03 = l0[pl * 4 + 3];
+      const int pl = (tid >> kTPPLog), j0 = ((tid & (kTPP - 1))) * (kEH / kTPP);
+      if constexpr (kHeads == 4) {
+        const double l00 = l0[pl * 4], l01 = l0[pl * 4 + 1], l02 = l0[pl * 4 + 2], l03 = l0[pl * 4 + 3];
 #pragma unroll
-      for (int j = j0; j < j0 + 8; ++j) {
-        const double pe = l00 * v0[j * 4] + l01 * v0[j * 4 + 1] + l02 * v0[j * 4 + 2] + l03 * v0[j * 4 + 3] + c0[j];
-        gw[pl * LDR + j] *= silu_prime(pe);
+        for (int j = j0; j < j0 + 8; ++j) {
+          const double pe = l00 * v0[j * 4] + l01 * v0[j * 4 + 1] + l02 * v0[j * 4 + 2] + l03 * v0[j * 4 + 3] + c0[j];
+          gw[pl * LDR + j] *= silu_prime(pe);
+        }
+      } else {
+        double lv[kHeads];
+#pragma unroll
+        for (int d = 0; d < kHeads; ++d) lv[d] = l0[pl * kHeads + d];
+#pragma unroll
+        for (int j = j0; j < j0 + kEH / kTPP; ++j) {
+          double pe = lv[0] * v0[j * kHeads];
+#pragma unroll
+          for (int d = 1; d < kHeads; ++d) pe += lv[d] * v0[j * kHeads + d];
+          gw[pl * LDR + j] *= silu_prime(pe + c0[j]);
+        }
       }
     }
     __syncthreads();
-    const int pl = tid >> 2, d = tid & 3;
+    const int pl = (tid >> kTPPLog), d = (tid & (kTPP - 1));
     double s = 0.0;
 #pragma unroll 8
-    for (int j = 0; j < kEH; ++j) s += gw[pl * LDR + j] * v0[j * 4 + d];
-    gl[pl * 4 + d] = s;
+    for (int j = 0; j < kEH; ++j) s += gw[pl * LDR + j] * v0[j * kHeads + d];
+    gl[pl * kHeads + d] = s;
   }
   __syncthreads();  // gw is read
 #pragma unroll
@@ -349,9 +379,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
     }
   // rank 0 prefetches the per-pair inputs of the radial and harmonic gradients
   // into the free gF region
-  double *sc = gF;                        // TP x 32 pair scalars
+  double *sc = gF;                        // TP x kPairScalars pair scalars
   double *geos = sc + TP * kPairScalars;  // TP x 8 geometry
-  double *drs = geos + TP * kGeo;         // TP x 32 radial-basis derivatives
+  double *drs = geos + TP * kGeo;         // TP x kR radial-basis derivatives
   if (f == 0) {
     stage_rows<kPairScalars>(sc, kPairScalars, pair_sc, p0, P);
     stage_rows<kGeo>(geos, kGeo, geo, p0, P);
@@ -377,9 +407,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
   // term, and the harmonic gradient g_Y[m]; both are summed over the blocks
   // (written by the first block reversed, added by the others) and turned into
   // the Cartesian pair gradient once per evaluation (launch_pair_tail).
-  // Four threads per pair: thread q sums basis functions 8q..8q+7 and handles
-  // harmonic channels 6q..6q+5.
-  const int pl = tid >> 2, q = tid & 3;
+  // kTPP threads per pair: thread q sums basis functions 8q..8q+7 and handles
+  // the distinct harmonics kSH/kTPP q ..; a harmonic of degree l collects the
+  // channels of every slot of degree l (one slot for F = 128, two for F = 256),
+  // slot by slot.
+  const int pl = (tid >> kTPPLog), q = (tid & (kTPP - 1));
   const int p = p0 + pl;
   double gr = 0.0;
 #pragma unroll
@@ -389,19 +421,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
   if (q == 0) gr += __dmul_rn(s[0], dphi);  // cutoff gradient (its weight is orientation-independent)
   gr += __shfl_xor_sync(0xffffffffu, gr, 1);
   gr += __shfl_xor_sync(0xffffffffu, gr, 2);
+  if constexpr (kTPP == 8) gr += __shfl_xor_sync(0xffffffffu, gr, 4);
   if (p < P) {
     if (q == 0) g_r[p] = accumulate ? g_r[p] + gr : gr;
     const int a = pa[p], b = pb[p];
+    constexpr int kShPer = kSH / kTPP;
+    if constexpr (kDupDegrees == 1) {  // one slot per degree: channel m is harmonic m
 #pragma unroll
-    for (int j = 0; j < 6; ++j) {
-      const int m = 6 * q + j;
-      const int d = degree_of_channel(m);
-      const double y = __dmul_rn(phi, __dadd_rn(__dmul_rn(s[1 + d], gA[(size_t)a * kEV + m]),
-                                                parity_sign(d) * __dmul_rn(s[5 + d], gA[(size_t)b * kEV + m])));
-      double *dst = g_y + (size_t)p * kEV + m;
+      for (int j = 0; j < 6; ++j) {
+        const int m = 6 * q + j;
+        const int d = degree_of_channel(m);
+        const double y = __dmul_rn(phi, __dadd_rn(__dmul_rn(s[1 + d], gA[(size_t)a * kEV + m]),
+                                                  parity_sign(d) * __dmul_rn(s[5 + d], gA[(size_t)b * kEV + m])));
+        double *dst = g_y + (size_t)p * kSH + m;
+        *dst = accumulate ? *dst + y : y;
+      }
+    } else {
+#pragma unroll
+    for (int j = 0; j < kShPer; ++j) {
+      const int m = kShPer * q + j;  // distinct harmonic
+      const int l = m < 3 ? 1 : (m < 8 ? 2 : (m < 15 ? 3 : 4));
+      double v = 0.0;
+#pragma unroll
+      for (int k = 0; k < kDupDegrees; ++k) {
+        const int d = (l - 1) * kDupDegrees + k;  // slot
+        const int c = slot_offset(d) + (m - (l * l - 1));
+        const double t = __dadd_rn(__dmul_rn(s[1 + d], gA[(size_t)a * kEV + c]),
+                                   parity_sign(d) * __dmul_rn(s[1 + kHeads + d], gA[(size_t)b * kEV + c]));
+        v = k == 0 ? t : __dadd_rn(v, t);
+      }
+      const double y = __dmul_rn(phi, v);
+      double *dst = g_y + (size_t)p * kSH + m;
       *dst = accumulate ? *dst + y : y;
     }
-    if (need_l0) gl0[(size_t)p * 4 + q] = gl[pl * 4 + q];
+    }
+    if (need_l0) gl0[(size_t)p * kHeads + q] = gl[pl * kHeads + q];
   }
 }
 
@@ -411,7 +465,7 @@ void launch_filter_reverse(int P, const double *geo, const int *pair_a, const in
                            const double *gA, const double *pair_sc, bool need_l0, bool accumulate, double *g_r,
                            double *g_y, double *gl0, cudaStream_t s) {
   if (P == 0) return;
-  const size_t smem = sizeof(double) * (TP * LDU + TP * LDR + 8 * TP);
+  const size_t smem = sizeof(double) * (TP * LDU + TP * LDR + 2 * kHeads * TP);
   static_assert(TP * (kPairScalars + kGeo + kR) <= TP * LDU, "per-pair inputs must fit in the gradient tile");
   allow_dynamic_smem(reinterpret_cast<const void *>(k_filter_reverse), smem);
   const int tiles = (P + TP - 1) / TP;
@@ -432,10 +486,10 @@ __global__ void k_pair_tail(int P, const double *__restrict__ geo, const double 
   if (p >= P) return;
   const double *gp = geo + (size_t)p * kGeo;
   const double r = gp[0], ux = gp[1], uy = gp[2], uz = gp[3];
-  double y[kEV];
+  double y[kSH];
 #pragma unroll
-  for (int m = 0; m < kEV; m += 2) {
-    const double2 v = *reinterpret_cast<const double2 *>(g_y + (size_t)p * kEV + m);
+  for (int m = 0; m < kSH; m += 2) {
+    const double2 v = *reinterpret_cast<const double2 *>(g_y + (size_t)p * kSH + m);
     y[m] = v.x;
     y[m + 1] = v.y;
   }
@@ -455,4 +509,4 @@ void launch_pair_tail(int P, const double *geo, const double *g_r, const double 
   SO3_LAUNCH("pair_tail");
 }
 
-}  // namespace so3lr_b200
+SO3LR_SHAPE_END

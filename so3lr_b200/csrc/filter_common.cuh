@@ -6,15 +6,24 @@
 
 #include "kernels.cuh"
 
-namespace so3lr_b200 {
+SO3LR_SHAPE_BEGIN
 namespace {
 
-constexpr int TP = 64;     // pairs per tile
+constexpr int TP = kFilterTile;  // pairs per tile: 64 (F = 128), 32 (F = 256)
+// threads of a 256-thread CTA per pair of the tile; equal to the number of
+// degree slots, so thread d of a pair owns slot d of its L0 invariants
+constexpr int kTPP = 256 / TP;
+constexpr int kTPPLog = kTPP == 4 ? 2 : 3;
+static_assert(kTPP == kHeads, "a pair's threads must match its degree slots");
+static_assert(kEH == kR, "the ev-hidden and radial-basis tiles share one row stride");
 // Row strides of the shared-memory tiles. A quarter-warp's 16-byte fragment
 // access covers 64 bytes of two rows; a stride of 8 (mod 16) doubles puts the
 // second row in the other half of the 32 banks.
-constexpr int LDU = 136;   // 128-wide tiles
-constexpr int LDR = 40;    // 32-wide tiles
+constexpr int LDU = kF + 8;   // F-wide tiles
+constexpr int LDR = kR + 8;   // R-wide (and EH-wide) tiles
+// the float64 kernels' warp slabs: each of the 8 warps owns kF / 8 output
+// columns of an F-wide GEMM, as kMT x kNB m16n8 blocks
+constexpr int kMT = TP / 16, kNB = kF / 64;
 
 // silu'(hidden pre-activation) of the rbf branch, written by the forward and
 // read by the reverse in accumulator order:
@@ -24,10 +33,19 @@ constexpr int LDR = 40;    // 32-wide tiles
 __device__ __forceinline__ size_t sp_offset(int tile, int filt, int warp) {
   return (((size_t)tile * 2 + filt) * 8 + warp) * (16 * 64);
 }
+// start of the 2 x 64 doubles (rows g and g + 8, lane-major pairs) of block
+// (mi, ni) of warp `warp`'s slab: the F = 128 order above; for F = 256 simply
+// [tile][filter][warp][mi][ni]
+__device__ __forceinline__ size_t sp_block(int tile, int filt, int warp, int mi, int ni) {
+  if constexpr (kF == 128)
+    return sp_offset(tile, filt, (mi >> 1) * 4 + (warp >> 1)) + (((mi & 1) * 4 + (warp & 1) * 2 + ni) * 2) * 64;
+  else
+    return (((size_t)tile * 2 + filt) * 8 + warp) * (kMT * kNB * 128) + (size_t)(mi * kNB + ni) * 128;
+}
 
 __device__ inline void compute_rbf(const double *rr, double *rbf, const RadialW &rad) {
-  const int pl = threadIdx.x >> 2;
-  const int k0 = (threadIdx.x & 3) * 8;
+  const int pl = threadIdx.x / kTPP;
+  const int k0 = (threadIdx.x % kTPP) * 8;
   const double r = rr[pl];
   double x = exp(-rad.gamma * r);
   if (x < 1.0e-6) x = 1.0e-6;
@@ -39,19 +57,25 @@ __device__ inline void compute_rbf(const double *rr, double *rbf, const RadialW 
 
 __device__ inline void compute_l0(int P, int p0, const int *pa, const int *pb, const double *ev, const double *cg,
                                   double *l0) {
-  const int pl = threadIdx.x >> 2, d = threadIdx.x & 3;
+  const int pl = threadIdx.x / kTPP, d = threadIdx.x % kTPP;
   const int p = p0 + pl;
   double v = 0.0;
   if (ev != nullptr && p < P) {
     const int a = pa[p], b = pb[p];
-    const int m0 = d == 0 ? 0 : (d == 1 ? 3 : (d == 2 ? 8 : 15));
-    const int m1 = d == 0 ? 3 : (d == 1 ? 8 : (d == 2 ? 15 : 24));
+    int m0, m1;
+    if constexpr (kHeads == 4) {
+      m0 = d == 0 ? 0 : (d == 1 ? 3 : (d == 2 ? 8 : 15));
+      m1 = d == 0 ? 3 : (d == 1 ? 8 : (d == 2 ? 15 : 24));
+    } else {
+      m0 = slot_offset(d);
+      m1 = m0 + slot_width(d);
+    }
     for (int m = m0; m < m1; ++m) {
       const double diff = ev[(size_t)b * kEV + m] - ev[(size_t)a * kEV + m];
       v += diff * diff * cg[m];
     }
   }
-  l0[pl * 4 + d] = v;
+  l0[pl * kHeads + d] = v;
 }
 
 // copy a TP x width block of a row-major global array (row stride = width) to
@@ -72,4 +96,4 @@ __device__ inline void stage_rows(double *dst, int lds, const double *src, int p
 }
 
 }  // namespace
-}  // namespace so3lr_b200
+SO3LR_SHAPE_END

@@ -26,7 +26,7 @@
 #include "filter_common.cuh"
 #include "kernels.cuh"
 
-namespace so3lr_b200 {
+SO3LR_SHAPE_BEGIN
 namespace {
 
 __device__ __forceinline__ float tf32_hi(float x) {
@@ -455,4 +455,4 @@ void launch_filter_reverse_mixed(int P, const double *geo, const int *pair_a, co
   SO3_LAUNCH("filter_reverse_mixed");
 }
 
-}  // namespace so3lr_b200
+SO3LR_SHAPE_END

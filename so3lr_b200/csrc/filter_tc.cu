@@ -34,7 +34,7 @@
 #include "filter_common.cuh"
 #include "kernels.cuh"
 
-namespace so3lr_b200 {
+SO3LR_SHAPE_BEGIN
 namespace {
 
 constexpr int kTcRows = 128;
@@ -868,4 +868,4 @@ void launch_filter_reverse_tc(int P, const double *geo, const int *pair_a, const
   SO3_LAUNCH("filter_reverse_tc");
 }
 
-}  // namespace so3lr_b200
+SO3LR_SHAPE_END

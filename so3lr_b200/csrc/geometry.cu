@@ -45,9 +45,9 @@ __global__ void k_pair_geometry(int P, const int *__restrict__ pa, const int *__
   const double r = sqrt(vx * vx + vy * vy + vz * vz);
   const double inv = r > 1.0e-14 ? 1.0 / r : 0.0;
   const double ux = vx * inv, uy = vy * inv, uz = vz * inv;
-  double y[kEV];
+  double y[kSH];
   real_sh(ux, uy, uz, y);
-  for (int m = 0; m < kEV; ++m) sh[(size_t)p * kEV + m] = y[m];
+  for (int m = 0; m < kSH; ++m) sh[(size_t)p * kSH + m] = y[m];
   // PhysNet cutoff 1 - 10x^3 + 15x^4 - 6x^5 and its derivative
   double phi = 0.0, dphi = 0.0;
   if (r < rc) {

@@ -93,16 +93,23 @@ void long_range_noalloc(int n, const double *x, const double *q, const double *h
                         double *e_lr, double *e_elec, double *e_disp, double *dq, double *dh, double *f,
                         double *w_atom, cudaStream_t s);
 
+}  // namespace so3lr_b200
+
+SO3LR_SHAPE_BEGIN
 // ---- filters (pair tiles, FP64 tensor cores) --------------------------------
 // sp: silu' of the rbf-branch hidden layer for the reverse pass, filter_sp_doubles(P) doubles;
-// drbf (optional, P x 32): d rbf_k / dr of every pair (it depends on the geometry only)
+// drbf (optional, P x kR): d rbf_k / dr of every pair (it depends on the geometry only)
 void launch_filter_forward(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
                            const double *cg_att, const FilterW &finv, const FilterW &fev, const RadialW &rad,
                            double *f_inv, double *f_ev, double *sp, double *drbf, cudaStream_t s);
-inline std::size_t filter_sp_doubles(int P) { return std::size_t((P + 63) / 64) * 2 * 64 * 128; }
+// pairs per tile of the float64 filter kernels: 64 (F = 128), 32 (F = 256)
+constexpr int kFilterTile = kF == 128 ? 64 : 32;
+inline std::size_t filter_sp_doubles(int P) {
+  return std::size_t((P + kFilterTile - 1) / kFilterTile) * 2 * kFilterTile * kF;
+}
 // g_filt_inv / g_filt_ev: per-pair gradient w.r.t. the two filter outputs (written by
 // the attention reverse at each pair's primary edge)
-// g_r (P) and g_y (P x 24): per-pair radial and harmonic gradients, written
+// g_r (P) and g_y (P x kSH): per-pair radial and distinct-harmonic gradients, written
 // (accumulate = false) or added to (accumulate = true); launch_pair_tail turns
 // their block sums into the Cartesian pair gradient gv (P x 3, +=)
 void launch_filter_reverse(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
@@ -148,6 +155,10 @@ void launch_attention_reverse(int n, const NeighborState &nb, const double *geo,
 void launch_ev_l0_reverse(int n, const NeighborState &nb, const double *ev, const double *cg_att,
                           const double *gl0, const double *g_A, double *g_ev, cudaStream_t s);
 
+SO3LR_SHAPE_END
+
+namespace so3lr_b200 {
+
 // ---- node GEMM (FP64 tensor cores) ------------------------------------------
 enum class Epi { None, Bias, BiasSilu, BiasStorePre, AddResidual, SiluPrimeMul, BiasResidual, GateSiluResidual };
 // C[M x N] = A[M x K] * B, B(k, n) = transB ? W[n*ldw + k] : W[k*ldw + n].
@@ -180,6 +191,9 @@ struct GemmArgs {
   int batch = 1;
   long long strideA = 0, strideW = 0, strideC = 0, strideAux = 0, strideBias = 0;
 };
+}  // namespace so3lr_b200
+
+SO3LR_SHAPE_BEGIN
 void launch_gemm(const GemmArgs &g, cudaStream_t s);
 // aux added only to columns < aux_cols; aux2 row stride ldaux2
 void launch_gemm_ex(const GemmArgs &g, int aux_cols, int ldaux2, cudaStream_t s);
@@ -227,6 +241,10 @@ void launch_heads_finalize(int n, const int *z, const double *hcat, const HeadsW
 void launch_heads_seed(int n, const int *z, const double *hpre, const double *hk, const HeadsW &hw,
                        const double *dq, const double *dq_mean, const int *image_of_atom, const double *dh,
                        const double *hk6, const double *dc6, double *g_hcat, cudaStream_t s);
+
+SO3LR_SHAPE_END
+
+namespace so3lr_b200 {
 
 void launch_charge_correct(int n, const double *raw, const double *raw_sum, const double *qtot,
                            const int *image_of_atom, const int *image_start, double *q, double *dq_mean_out,

@@ -25,7 +25,7 @@
 
 #include "evaluator.hpp"
 
-namespace so3lr_b200 {
+SO3LR_SHAPE_BEGIN
 namespace {
 
 constexpr int kRec = 5;  // tag, x, y, z, Z (tags and Z are exact in a double)
@@ -215,4 +215,4 @@ Evaluator::HostResult Evaluator::compute_local(const SystemSpec &frame, int nloc
   return res;
 }
 
-}  // namespace so3lr_b200
+SO3LR_SHAPE_END

@@ -483,11 +483,12 @@ std::string Architecture::summary() const {
 }
 
 // Architecture record + capability negotiation. The kernels of this library are
-// written for the released SO3LR shape (F=128, 4 heads of 32, degrees 1..4,
-// 32 Bernstein functions, LayerNorm blocks with one residual MLP, learned ZBL,
-// energy/charge/Hirshfeld heads); everything else is refused here, before any
-// device memory exists (so3lr_capabilities.cpp:181-289 does the same against
-// the reference's own table).
+// compiled for the two released SO3LR widths (F=128: 4 heads of 32, degrees
+// 1..4, 32 Bernstein functions; F=256: 8 heads of 32, degrees 1..4 twice, 64
+// Bernstein functions), with the optional block operators below, learned ZBL or
+// NLH repulsion and energy/charge/Hirshfeld (and C6) heads; everything else is
+// refused here, before any device memory exists (so3lr_capabilities.cpp:181-289
+// does the same against the reference's own table).
 void Model::describe_and_negotiate() {
   const Json &a = manifest_.at("architecture");
   std::vector<std::string> problems;
@@ -522,23 +523,44 @@ void Model::describe_and_negotiate() {
   r.ev_degrees = int(a.at("euclidean_degree_channels").uint());
   r.rbf = int(a.at("radial_basis_features").uint());
   need(r.layers >= 1 && r.layers <= 8, "interaction_blocks must be 1..8");
-  need(r.features == 128, "invariant_features must be 128 (kernels are specialised for it)");
-  need(r.heads == 4 && r.head_width == 32, "attention must be 4 heads of width 32");
-  need(r.ev_degrees == 4, "euclidean_degree_channels must be 4 (degrees 1..4)");
-  need(r.rbf == 32, "radial_basis_features must be 32");
+  // the two compiled widths (so3lr_capabilities.cpp:58-59 lists the same two):
+  // F = 128 with 32 radial functions and degrees [1,2,3,4], F = 256 with 64
+  // radial functions and the duplicated degrees [1,1,2,2,3,3,4,4]
+  need(r.features == 128 || r.features == 256,
+       "invariant_features must be 128 or 256 (the widths the kernels are compiled for)");
+  const bool wide = r.features == 256;
+  const int want_heads = r.features / 32;
+  need(r.heads == want_heads && r.head_width == 32,
+       "attention must be " + std::to_string(want_heads) + " heads of width 32 for invariant_features = " +
+           std::to_string(r.features));
+  need(r.ev_degrees == r.heads, "euclidean_degree_channels must equal attention_heads");
+  need(r.rbf == r.features / 4, "radial_basis_features must be " + std::to_string(r.features / 4) +
+                                    " for invariant_features = " + std::to_string(r.features));
   const std::string block0 = "model.euclidean_transformers.0.euclidean_attention_block.degree_repeats";
   if (has_tensor(block0)) {
     for (auto v : i64(block0)) r.degree_repeats.push_back(int(v));
   }
-  need(r.degree_repeats == std::vector<int>({3, 5, 7, 9}), "degree_repeats must be [3,5,7,9]");
+  const std::vector<int> want_reps = wide ? std::vector<int>({3, 3, 5, 5, 7, 7, 9, 9}) : std::vector<int>({3, 5, 7, 9});
+  need(r.degree_repeats == want_reps, wide ? "degree_repeats must be [3,3,5,5,7,7,9,9] for invariant_features = 256"
+                                           : "degree_repeats must be [3,5,7,9] for invariant_features = 128");
+  // every block declares the same degree layout
+  for (int b = 1; b < r.layers; ++b)
+    for (const char *part : {".euclidean_attention_block.degree_repeats", ".interaction_block.degree_repeats"}) {
+      const std::string key = "model.euclidean_transformers." + std::to_string(b) + part;
+      if (has_tensor(key)) {
+        std::vector<int> reps;
+        for (auto v : i64(key)) reps.push_back(int(v));
+        need(reps == r.degree_repeats, key + " differs from block 0's degree layout");
+      }
+    }
   int off = 0;
   for (int rep : r.degree_repeats) {
     r.degree_offsets.push_back(off);
     off += rep;
   }
   r.ev_width = off;
-  r.sh_width = off;
-  r.max_degree = int(r.degree_repeats.size());
+  r.max_degree = r.degree_repeats.empty() ? 0 : (r.degree_repeats.back() - 1) / 2;
+  r.sh_width = r.max_degree * (r.max_degree + 2);  // distinct harmonics l = 1..Lmax
   r.interaction_width = r.features + r.ev_degrees;
   r.sr_cutoff = a.has("short_range_cutoff_angstrom") ? a.at("short_range_cutoff_angstrom").num() : 0.0;
   r.lr_cutoff = a.has("long_range_cutoff_angstrom") ? a.at("long_range_cutoff_angstrom").num() : 0.0;

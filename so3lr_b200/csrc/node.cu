@@ -12,7 +12,7 @@
 // GEMM epilogue.
 #include "kernels.cuh"
 
-namespace so3lr_b200 {
+SO3LR_SHAPE_BEGIN
 namespace {
 
 // 64 x 64 output tile per CTA, 4 warps of 32 x 32 (2 x 4 m16n8k8 blocks), K in
@@ -222,34 +222,53 @@ __device__ inline double warp_sum(double v) {
   return v;
 }
 
-// Block norm of one 128-wide row held as 4 values per lane: xh = normalised
+// Row kernels: one warp per atom, lane owns invariant channels kPL lane ..
+// kPL lane + kPL - 1 and equivariant channels lane + 32 j (j < kEVL).
+constexpr int kPL = kF / 32;
+constexpr int kEVL = (kEV + 31) / 32;
+
+// sum over the warp of the per-lane terms t[j] of the channels of degree slot k
+// (ch[j] = slot of the lane's j-th equivariant channel, -1 when it has none)
+__device__ inline double slot_sum(int k, const int (&ch)[kEVL], const double (&t)[kEVL]) {
+  double v = ch[0] == k ? t[0] : 0.0;
+#pragma unroll
+  for (int j = 1; j < kEVL; ++j) v += ch[j] == k ? t[j] : 0.0;
+  return warp_sum(v);
+}
+
+// Block norm of one kF-wide row held as kPL values per lane: xh = normalised
 // row, returns the inverse standard deviation (LayerNorm) or inverse RMS
 // (RMSNorm without scale, post_attention_block0.cpp:124-146); identity for
 // kNormNone. eps = 1e-6 (the only value the model contract admits).
-__device__ inline double row_norm(int norm, const double (&v)[4], double (&xh)[4]) {
+__device__ inline double row_norm(int norm, const double (&v)[kPL], double (&xh)[kPL]) {
   if (norm == kNormNone) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) xh[j] = v[j];
+    for (int j = 0; j < kPL; ++j) xh[j] = v[j];
     return 1.0;
   }
   double mean = 0.0;
-  if (norm == kNormLayer) mean = warp_sum(v[0] + v[1] + v[2] + v[3]) / double(kF);
+  if (norm == kNormLayer) {
+    double s = v[0];
+#pragma unroll
+    for (int j = 1; j < kPL; ++j) s += v[j];
+    mean = warp_sum(s) / double(kF);
+  }
   double var = 0.0;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < kPL; ++j) {
     const double d = v[j] - mean;
     var += d * d;
   }
   var = warp_sum(var) / double(kF);
   const double rs = 1.0 / sqrt(var + 1.0e-6);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) xh[j] = (v[j] - mean) * rs;
+  for (int j = 0; j < kPL; ++j) xh[j] = (v[j] - mean) * rs;
   return rs;
 }
 }  // namespace
 
 // a = x + d_inv; A = ev + d_ev; n1 = LN1(a); act = silu(n1);
-// cat[:, 128:132] = L0'(A) (interaction cg), cat[:, 132:136] = 0. One warp per atom.
+// cat[:, F:F+H] = L0'(A) (interaction cg), cat[:, F+H:kIntW] = 0. One warp per atom.
 __global__ void k_post_attn_pre(int n, const double *__restrict__ x, const double *__restrict__ d_inv,
                                 const double *__restrict__ ev, const double *__restrict__ d_ev, int norm,
                                 const double *__restrict__ lnw, const double *__restrict__ lnb,
@@ -259,35 +278,41 @@ __global__ void k_post_attn_pre(int n, const double *__restrict__ x, const doubl
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
-  double a[4], xh[4];
+  double a[kPL], xh[kPL];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int c = lane * 4 + j;
+  for (int j = 0; j < kPL; ++j) {
+    const int c = lane * kPL + j;
     a[j] = x[(size_t)i * kF + c] + d_inv[(size_t)i * kF + c];
   }
   const double rs = row_norm(norm, a, xh);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int c = lane * 4 + j;
+  for (int j = 0; j < kPL; ++j) {
+    const int c = lane * kPL + j;
     const double y = norm == kNormLayer ? xh[j] * lnw[c] + lnb[c] : xh[j];
     xhat1[(size_t)i * kF + c] = xh[j];
     n1_out[(size_t)i * kF + c] = y;
     act[(size_t)i * kF + c] = silu(y);
   }
   if (lane == 0) rstd1[i] = rs;
-  double Am = 0.0;
-  if (lane < kEV) {
-    Am = ev[(size_t)i * kEV + lane] + d_ev[(size_t)i * kEV + lane];
-    A_out[(size_t)i * kEV + lane] = Am;
-  }
-  const int d = lane < kEV ? degree_of_channel(lane) : -1;
-  const double term = lane < kEV ? Am * Am * cg_int[lane] : 0.0;
+  int d[kEVL];
+  double term[kEVL];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const double sk = warp_sum(d == k ? term : 0.0);
+  for (int j = 0; j < kEVL; ++j) {
+    const int m = lane + 32 * j;
+    d[j] = m < kEV ? degree_of_channel(m) : -1;
+    term[j] = 0.0;
+    if (m < kEV) {
+      const double Am = ev[(size_t)i * kEV + m] + d_ev[(size_t)i * kEV + m];
+      A_out[(size_t)i * kEV + m] = Am;
+      term[j] = Am * Am * cg_int[m];
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kHeads; ++k) {
+    const double sk = slot_sum(k, d, term);
     if (lane == 0) cat[(size_t)i * kIntW + kF + k] = sk;
   }
-  if (lane < 4) cat[(size_t)i * kIntW + kF + 4 + lane] = 0.0;
+  if (lane < kIntW - kF - kHeads) cat[(size_t)i * kIntW + kF + kHeads + lane] = 0.0;
 }
 
 void launch_post_attn_pre(int n, const double *x, const double *d_inv, const double *ev, const double *d_ev,
@@ -298,7 +323,7 @@ void launch_post_attn_pre(int n, const double *x, const double *d_inv, const dou
   SO3_LAUNCH("post_attn_pre");
 }
 
-// pre2 = post + t[:128]; x' = LN2(pre2); ev' = A (1 + t_gate). One warp per atom.
+// pre2 = post + t[:F]; x' = LN2(pre2); ev' = A (1 + t_gate). One warp per atom.
 __global__ void k_post_attn_final(int n, const double *__restrict__ cat, const double *__restrict__ t,
                                   const double *__restrict__ A, int norm, const double *__restrict__ lnw,
                                   const double *__restrict__ lnb, double *__restrict__ xhat2,
@@ -307,24 +332,28 @@ __global__ void k_post_attn_final(int n, const double *__restrict__ cat, const d
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
-  double v[4], xh[4];
+  double v[kPL], xh[kPL];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int c = lane * 4 + j;
+  for (int j = 0; j < kPL; ++j) {
+    const int c = lane * kPL + j;
     v[j] = cat[(size_t)i * kIntW + c] + t[(size_t)i * kIntW + c];
   }
   const double rs = row_norm(norm, v, xh);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int c = lane * 4 + j;
+  for (int j = 0; j < kPL; ++j) {
+    const int c = lane * kPL + j;
     xhat2[(size_t)i * kF + c] = xh[j];
     x_out[(size_t)i * kF + c] = norm == kNormLayer ? xh[j] * lnw[c] + lnb[c] : xh[j];
   }
   if (lane == 0) rstd2[i] = rs;
-  if (lane < 4) gate[(size_t)i * 4 + lane] = t[(size_t)i * kIntW + kF + lane];
-  if (lane < kEV) {
-    const int d = degree_of_channel(lane);
-    ev_out[(size_t)i * kEV + lane] = A[(size_t)i * kEV + lane] * (1.0 + t[(size_t)i * kIntW + kF + d]);
+  if (lane < kHeads) gate[(size_t)i * kHeads + lane] = t[(size_t)i * kIntW + kF + lane];
+#pragma unroll
+  for (int j = 0; j < kEVL; ++j) {
+    const int m = lane + 32 * j;
+    if (m < kEV) {
+      const int d = degree_of_channel(m);
+      ev_out[(size_t)i * kEV + m] = A[(size_t)i * kEV + m] * (1.0 + t[(size_t)i * kIntW + kF + d]);
+    }
   }
 }
 
@@ -339,27 +368,27 @@ void launch_post_attn_final(int n, const double *cat, const double *t, const dou
 // Block-norm backward. LayerNorm (affine): g_x = rstd (g_xh - mean(g_xh) -
 // xh mean(g_xh xh)), g_xh = g_y w. RMSNorm without scale: g_x = rrms (g_y -
 // xh mean(g_y xh)). Identity: g_x = g_y.
-__device__ inline void norm_backward(int norm, const double (&gy)[4], const double (&xh)[4], const double *w,
-                                     int lane, double rs, double (&gx)[4]) {
+__device__ inline void norm_backward(int norm, const double (&gy)[kPL], const double (&xh)[kPL], const double *w,
+                                     int lane, double rs, double (&gx)[kPL]) {
   if (norm == kNormNone) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) gx[j] = gy[j];
+    for (int j = 0; j < kPL; ++j) gx[j] = gy[j];
     return;
   }
-  double gxh[4], s1 = 0.0, s2 = 0.0;
+  double gxh[kPL], s1 = 0.0, s2 = 0.0;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    gxh[j] = norm == kNormLayer ? gy[j] * w[lane * 4 + j] : gy[j];
+  for (int j = 0; j < kPL; ++j) {
+    gxh[j] = norm == kNormLayer ? gy[j] * w[lane * kPL + j] : gy[j];
     s1 += gxh[j];
     s2 += gxh[j] * xh[j];
   }
   s1 = norm == kNormLayer ? warp_sum(s1) / double(kF) : 0.0;
   s2 = warp_sum(s2) / double(kF);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) gx[j] = rs * (gxh[j] - s1 - xh[j] * s2);
+  for (int j = 0; j < kPL; ++j) gx[j] = rs * (gxh[j] - s1 - xh[j] * s2);
 }
 
-// reverse of k_post_attn_final: g_t[:128] = LN2^T(g_x), g_t[128+d] = sum g_ev A, g_A = g_ev (1 + gate)
+// reverse of k_post_attn_final: g_t[:F] = LN2^T(g_x), g_t[F+d] = sum g_ev A, g_A = g_ev (1 + gate)
 __global__ void k_post_attn_rev_final(int n, const double *__restrict__ g_x, const double *__restrict__ g_ev,
                                       const double *__restrict__ xhat2, const double *__restrict__ rstd2, int norm,
                                       const double *__restrict__ lnw2, const double *__restrict__ A,
@@ -368,29 +397,40 @@ __global__ void k_post_attn_rev_final(int n, const double *__restrict__ g_x, con
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
-  double gy[4], xh[4], gx[4];
+  double gy[kPL], xh[kPL], gx[kPL];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    gy[j] = g_x[(size_t)i * kF + lane * 4 + j];
-    xh[j] = xhat2[(size_t)i * kF + lane * 4 + j];
+  for (int j = 0; j < kPL; ++j) {
+    gy[j] = g_x[(size_t)i * kF + lane * kPL + j];
+    xh[j] = xhat2[(size_t)i * kF + lane * kPL + j];
   }
   norm_backward(norm, gy, xh, lnw2, lane, rstd2[i], gx);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) g_t[(size_t)i * kIntW + lane * 4 + j] = gx[j];
-  double ge = 0.0, Am = 0.0;
-  int d = -1;
-  if (lane < kEV && g_ev != nullptr) {
-    ge = g_ev[(size_t)i * kEV + lane];
-    Am = A[(size_t)i * kEV + lane];
-    d = degree_of_channel(lane);
+  for (int j = 0; j < kPL; ++j) g_t[(size_t)i * kIntW + lane * kPL + j] = gx[j];
+  double ge[kEVL], gA[kEVL];
+  int d[kEVL];
+#pragma unroll
+  for (int j = 0; j < kEVL; ++j) {
+    const int m = lane + 32 * j;
+    ge[j] = 0.0;
+    gA[j] = 0.0;
+    d[j] = -1;
+    if (m < kEV && g_ev != nullptr) {
+      ge[j] = g_ev[(size_t)i * kEV + m];
+      gA[j] = ge[j] * A[(size_t)i * kEV + m];
+      d[j] = degree_of_channel(m);
+    }
   }
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const double sk = warp_sum(d == k ? ge * Am : 0.0);
+  for (int k = 0; k < kHeads; ++k) {
+    const double sk = slot_sum(k, d, gA);
     if (lane == 0) g_t[(size_t)i * kIntW + kF + k] = sk;
   }
-  if (lane < 4) g_t[(size_t)i * kIntW + kF + 4 + lane] = 0.0;
-  if (lane < kEV) g_A[(size_t)i * kEV + lane] = d >= 0 ? ge * (1.0 + gate[(size_t)i * 4 + d]) : 0.0;
+  if (lane < kIntW - kF - kHeads) g_t[(size_t)i * kIntW + kF + kHeads + lane] = 0.0;
+#pragma unroll
+  for (int j = 0; j < kEVL; ++j) {
+    const int m = lane + 32 * j;
+    if (m < kEV) g_A[(size_t)i * kEV + m] = d[j] >= 0 ? ge[j] * (1.0 + gate[(size_t)i * kHeads + d[j]]) : 0.0;
+  }
 }
 
 void launch_post_attn_rev_final(int n, const double *g_x, const double *g_ev, const double *xhat2,
@@ -410,19 +450,23 @@ __global__ void k_post_attn_rev_ln1(int n, const double *__restrict__ g_n1, cons
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
-  double gy[4], xh[4], gx[4];
+  double gy[kPL], xh[kPL], gx[kPL];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    gy[j] = g_n1[(size_t)i * kF + lane * 4 + j];
-    xh[j] = xhat1[(size_t)i * kF + lane * 4 + j];
+  for (int j = 0; j < kPL; ++j) {
+    gy[j] = g_n1[(size_t)i * kF + lane * kPL + j];
+    xh[j] = xhat1[(size_t)i * kF + lane * kPL + j];
   }
   norm_backward(norm, gy, xh, lnw1, lane, rstd1[i], gx);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) g_a[(size_t)i * kF + lane * 4 + j] = gx[j];
-  if (lane < kEV) {
-    const int d = degree_of_channel(lane);
-    const double Am = A[(size_t)i * kEV + lane];
-    g_A[(size_t)i * kEV + lane] += 2.0 * Am * cg_int[lane] * g_cat[(size_t)i * kIntW + kF + d];
+  for (int j = 0; j < kPL; ++j) g_a[(size_t)i * kF + lane * kPL + j] = gx[j];
+#pragma unroll
+  for (int j = 0; j < kEVL; ++j) {
+    const int m = lane + 32 * j;
+    if (m < kEV) {
+      const int d = degree_of_channel(m);
+      const double Am = A[(size_t)i * kEV + m];
+      g_A[(size_t)i * kEV + m] += 2.0 * Am * cg_int[m] * g_cat[(size_t)i * kIntW + kF + d];
+    }
   }
 }
 
@@ -469,23 +513,24 @@ void launch_scale_rows(int n, double *v, double a, cudaStream_t s) {
 // per (row, head, slot), lane = channel.
 // ---------------------------------------------------------------------------
 __device__ inline int qk_slot_offset(int slot) { return slot < 2 ? slot * 32 : (slot + 1) * 32; }  // q k | q_ev k_ev
+constexpr int kQkPerRow = 4 * kHeads;  // normalised vectors per row
 
 __global__ void k_qk_norm(int n, const int *__restrict__ rows, double *__restrict__ qkv, double *__restrict__ rinv) {
   const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (w >= (long long)n * 16) return;
-  const int slot = int(w & 3), head = int((w >> 2) & 3);
-  const long long m = w >> 4;
+  if (w >= (long long)n * kQkPerRow) return;
+  const int slot = int(w & 3), head = int((w >> 2) % kHeads);
+  const long long m = w / kQkPerRow;
   const long long row = rows ? rows[m] : m;
   double *v = qkv + row * kQKV + head * 160 + qk_slot_offset(slot);
   const double x = v[lane];
   const double r = 1.0 / sqrt(warp_sum(x * x) / 32.0 + 1.0e-6);
   v[lane] = x * r;
-  if (lane == 0) rinv[row * 16 + head * 4 + slot] = r;
+  if (lane == 0) rinv[row * kQkPerRow + head * 4 + slot] = r;
 }
 void launch_qk_norm(int n, const int *rows, double *qkv, double *rinv, cudaStream_t s) {
   if (n == 0) return;
-  const long long threads = (long long)n * 16 * 32;
+  const long long threads = (long long)n * kQkPerRow * 32;
   k_qk_norm<<<unsigned((threads + 255) / 256), 256, 0, s>>>(n, rows, qkv, rinv);
   SO3_LAUNCH("qk_norm");
 }
@@ -494,17 +539,17 @@ __global__ void k_qk_norm_reverse(int n, const double *__restrict__ qkv, const d
                                   double *__restrict__ g) {
   const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (w >= (long long)n * 16) return;
-  const int slot = int(w & 3), head = int((w >> 2) & 3);
-  const long long row = w >> 4;
+  if (w >= (long long)n * kQkPerRow) return;
+  const int slot = int(w & 3), head = int((w >> 2) % kHeads);
+  const long long row = w / kQkPerRow;
   const long long off = row * kQKV + head * 160 + qk_slot_offset(slot);
   const double y = qkv[off + lane], gy = g[off + lane];
   const double mean_gy = warp_sum(gy * y) / 32.0;
-  g[off + lane] = rinv[row * 16 + head * 4 + slot] * (gy - y * mean_gy);
+  g[off + lane] = rinv[row * kQkPerRow + head * 4 + slot] * (gy - y * mean_gy);
 }
 void launch_qk_norm_reverse(int n, const double *qkv, const double *rinv, double *g, cudaStream_t s) {
   if (n == 0) return;
-  const long long threads = (long long)n * 16 * 32;
+  const long long threads = (long long)n * kQkPerRow * 32;
   k_qk_norm_reverse<<<unsigned((threads + 255) / 256), 256, 0, s>>>(n, qkv, rinv, g);
   SO3_LAUNCH("qk_norm_reverse");
 }
@@ -645,4 +690,4 @@ void launch_heads_seed(int n, const int *z, const double *hpre, const double *hk
   SO3_LAUNCH("heads_seed");
 }
 
-}  // namespace so3lr_b200
+SO3LR_SHAPE_END

@@ -101,3 +101,128 @@ def make_variant(base_path, out_path, *, rms_norm: bool = False, second_norm: bo
         for key, vals in (("physical.nlh_a", amp), ("physical.nlh_b", rate)):
             tensors.append(({"name": key, "state_key": key, "dtype": "float64", "role": "physical_constant"}, vals))
     return write_model(out_path, man, tensors)
+
+
+# ---------------------------------------------------------------------------
+# "l"-size model: F = 256 invariant features in 8 heads of 32, 64 radial
+# functions, duplicated degrees {1,1,2,2,3,3,4,4} (48 equivariant channels).
+# The reference accepts these widths (src/so3lr_capabilities.cpp:58-59, 74),
+# but no checkpoint of that size is in this repository. The weights here are
+# the shipped model's, widened: feature c = 32 h + j of the wide model stands
+# for feature 32 (h // 2) + j of the shipped one (heads 2k and 2k+1 both come
+# from head k, so the ev slot of head h has degree h // 2 + 1), radial function
+# k for function k // 2 and ev-branch hidden unit j for unit j // 2. A weight
+# whose input axis was widened is halved (both copies of an input feed it),
+# and every weight is multiplied by 1 + 0.1 N(0, 1), so no two heads, slots or
+# features of the wide model are equal.
+# ---------------------------------------------------------------------------
+L_FEATURES, L_HEADS, L_RBF = 256, 8, 64
+L_REPEATS = [3, 3, 5, 5, 7, 7, 9, 9]
+
+
+def _widen_index(width_new: int, width_old: int, group: int) -> np.ndarray:
+    """old index of every new index when each `group`-wide block of the old axis
+    appears twice in a row"""
+    idx = np.arange(width_new)
+    return (idx // (2 * group)) * group + idx % group
+
+
+def make_l_variant(base_path, out_path, *, seed: int = 0) -> pathlib.Path:
+    import math
+
+    base = load_model(str(base_path))
+    man = copy.deepcopy(base.manifest)
+    arch = man["architecture"]
+    F0 = int(arch["invariant_features"])
+    H0 = int(arch["attention_heads"])
+    R0 = int(arch["radial_basis_features"])
+    assert (F0, H0, R0) == (128, 4, 32), "the base must be the shipped F=128 model"
+    arch["invariant_features"] = L_FEATURES
+    arch["attention_heads"] = L_HEADS
+    arch["euclidean_degree_channels"] = L_HEADS
+    arch["radial_basis_features"] = L_RBF
+    rng = np.random.default_rng(seed)
+    fmap = _widen_index(L_FEATURES, F0, 32)          # features by head blocks
+    smap = np.arange(L_HEADS) // 2                    # degree slot / head
+    imap = np.concatenate([fmap, F0 + smap])          # interaction layer: F features + H invariants
+    rmap = np.arange(L_RBF) // 2                      # radial functions
+    hmap = np.arange(2 * 32) // 2                     # ev-branch hidden units (F / 4)
+    deg_of_channel = np.concatenate([[s] * r for s, r in enumerate(L_REPEATS)])
+    degree_l = np.concatenate([[(r - 1) // 2] * r for r in L_REPEATS])
+
+    def noisy(a):
+        a = np.asarray(a, dtype=np.float64)
+        return a * (1.0 + 0.1 * rng.standard_normal(a.shape))
+
+    def widen(a, out_map=None, in_map=None):
+        """rows by out_map, columns by in_map (halved), then noise"""
+        a = np.asarray(a, dtype=np.float64)
+        if out_map is not None:
+            a = a[out_map]
+        if in_map is not None:
+            a = a[..., in_map] * 0.5
+        return noisy(a)
+
+    def block_tensor(key, a):
+        part = key.split(".", 3)[3]  # after model.euclidean_transformers.<b>.
+        if part.endswith("degree_repeats"):
+            return np.asarray(L_REPEATS, dtype=np.int64)
+        if part.endswith("so3_conv_invariants.cg_rep"):
+            return 1.0 / np.sqrt(2.0 * degree_l + 1.0)
+        if part.endswith("so3_conv_invariants.segment_ids"):
+            return deg_of_channel.astype(np.int64)
+        if part.endswith("so3_conv_invariants.segment_sum_matrix"):
+            return np.eye(L_HEADS)[deg_of_channel]
+        if part.split(".")[-1] in ("W_q_inv", "W_k_inv", "W_v_inv", "W_q_ev", "W_k_ev"):
+            return noisy(np.asarray(a)[smap])
+        if "mlp_rbf.0.weight" in part:
+            return widen(a, fmap, rmap)
+        if "mlp_rbf.0.bias" in part or "mlp_rbf_layer_1.0.bias" in part or "mlp_ev_layer_1.0.bias" in part:
+            return widen(a, fmap)
+        if "mlp_rbf_layer_1.0.weight" in part:
+            return widen(a, fmap, fmap)
+        if "mlp_ev.0.weight" in part:
+            return widen(a, hmap, smap)
+        if "mlp_ev.0.bias" in part:
+            return widen(a, hmap)
+        if "mlp_ev_layer_1.0.weight" in part:
+            return widen(a, fmap, hmap)
+        if part == "interaction_block.linear_layer.weight":
+            return widen(a, imap, imap)
+        if part == "interaction_block.linear_layer.bias":
+            return widen(a, imap)
+        if part.startswith("layer_norm_inv_") or part in ("mlp_1.1.bias", "mlp_1.3.bias"):
+            return widen(a, fmap)
+        if part in ("mlp_1.1.weight", "mlp_1.3.weight"):
+            return widen(a, fmap, fmap)
+        raise KeyError(f"no widening rule for block tensor {key}")
+
+    def tensor(key, a):
+        if key.startswith("model.euclidean_transformers."):
+            return block_tensor(key, a)
+        if key == "model.radial_embedding.radial_basis_fn.b":
+            n = L_RBF - 1
+            return np.array([math.lgamma(n + 1) - math.lgamma(k + 1) - math.lgamma(n - k + 1) for k in range(L_RBF)])
+        if key == "model.radial_embedding.radial_basis_fn.k":
+            return np.arange(L_RBF, dtype=np.int64)
+        if key == "model.radial_embedding.radial_basis_fn.k_rev":
+            return (L_RBF - 1 - np.arange(L_RBF)).astype(np.int64)
+        if key in ("model.inv_feature_embedding.embedding.weight", "model.charge_embedding.Wq.weight",
+                   "model.spin_embedding.Wq.weight"):
+            return widen(a, fmap)
+        if key in ("model.charge_embedding.Wk", "model.charge_embedding.Wv", "model.spin_embedding.Wk",
+                   "model.spin_embedding.Wv"):
+            return noisy(np.asarray(a)[:, fmap])
+        if key.endswith("embedding.mlp.1.weight") or key.endswith("embedding.mlp.3.weight"):
+            return widen(a, fmap, fmap)
+        if key in ("model.atomic_energy_output_block.layers.0.weight",
+                   "model.partial_charges_output_block.transform_inv_features.0.weight",
+                   "model.hirshfeld_output_block.transform_features.0.weight"):
+            return widen(a, None, fmap)
+        return a
+
+    tensors = []
+    for rec in man["tensors"]:
+        key = rec["state_key"]
+        tensors.append((rec, tensor(key, base.tensors[key])))
+    return write_model(out_path, man, tensors)

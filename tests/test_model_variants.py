@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 from conftest import MODEL
-from model_variants import make_variant
+from model_variants import make_l_variant, make_variant
 from so3lr_b200.model_file import write_model
 
 RESID = ([0.9, 1.1, 0.8], [0.1, -0.2, 0.3])
@@ -27,6 +27,8 @@ VARIANTS = {
     "a0_c6_one_key": dict(hirshfeld_keys=1, c6_keys=1, seed=4),
     "all": dict(rms_norm=True, qk_norm=True, residual_scalars=RESID, nlh_capacity=9, hirshfeld_keys=1, c6_keys=1,
                 seed=2, attention_norm_factor=20.0),
+    # F = 256, 8 heads, 64 radial functions, degrees [1,1,2,2,3,3,4,4]
+    "l_size": dict(l_size=True, seed=7),
 }
 
 
@@ -38,7 +40,11 @@ def variant_dir(tmp_path_factory):
 def _variant(variant_dir, name):
     path = variant_dir / f"{name}.so3lr"
     if not path.exists():
-        make_variant(MODEL, path, **VARIANTS[name])
+        kw = dict(VARIANTS[name])
+        if kw.pop("l_size", False):
+            make_l_variant(MODEL, path, **kw)
+        else:
+            make_variant(MODEL, path, **kw)
     return path
 
 
@@ -93,6 +99,46 @@ def test_native_loader_accepts_variant(name, variant_dir):
     rc, err, info = _inspect(_variant(variant_dir, name))
     assert rc == 0, err
     assert ("repulsion=nlh" in info.summary.decode()) == ("nlh_capacity" in VARIANTS[name])
+    if "l_size" in VARIANTS[name]:
+        assert (info.features, info.heads, info.rbf, info.ev_width, info.degrees) == (256, 8, 64, 48, 4)
+        assert "degrees=[1,1,2,2,3,3,4,4]" in info.summary.decode()
+
+
+def test_native_loader_refuses_other_widths(variant_dir):
+    """Shapes outside the two compiled widths are refused with the loader's
+    reason: F = 256 with the F = 128 degree list, and a 256-wide model that
+    declares 32 radial functions."""
+    from oracle.model_io import load_model
+    base = load_model(str(_variant(variant_dir, "l_size")))
+    cases = [("l_degrees", "model.euclidean_transformers.0.euclidean_attention_block.degree_repeats",
+              np.array([3, 5, 7, 9, 3, 5, 7, 9], dtype=np.int64), None, "degree_repeats must be [3,3,5,5,7,7,9,9]"),
+             ("l_rbf32", None, None, dict(radial_basis_features=32), "radial_basis_features must be 64")]
+    for tag, key, value, arch, needle in cases:
+        import copy as _copy
+        man = _copy.deepcopy(base.manifest)
+        if arch:
+            man["architecture"].update(arch)
+        tensors = [(r, value if r["state_key"] == key else base.tensors[r["state_key"]]) for r in man["tensors"]]
+        rc, err, _ = _inspect(write_model(variant_dir / f"bad_{tag}.so3lr", man, tensors))
+        assert rc != 0 and needle in err, (tag, err)
+
+
+def test_oracle_l_size_is_rotation_invariant(variant_dir):
+    """The duplicated-degree layout keeps the model equivariant: rotating a
+    molecule leaves the energy and charges unchanged and rotates the forces
+    (a slot fed harmonics of another degree would break this)."""
+    from oracle.so3lr_oracle import OracleModel, System, evaluate
+    from so3lr_b200.systems import turbo_batch
+    m = OracleModel.load(str(_variant(variant_dir, "l_size")))
+    pos, z, off, q, mult = turbo_batch(3, seed=13)
+    sl = slice(off[2], off[3])
+    p0 = pos[sl] - pos[sl].mean(axis=0)
+    rot, _ = np.linalg.qr(np.random.default_rng(3).standard_normal((3, 3)))
+    a = evaluate(m, System(pos=p0, z=z[sl], charge=q[2], multiplicity=mult[2]))
+    b = evaluate(m, System(pos=p0 @ rot.T, z=z[sl], charge=q[2], multiplicity=mult[2]))
+    assert abs(a["energy"] - b["energy"]) <= 1e-9 * abs(a["energy"])
+    assert np.abs(a["forces"] @ rot.T - b["forces"]).max() <= 1e-9 * (1 + np.abs(a["forces"]).max())
+    assert np.abs(a["partial_charges"] - b["partial_charges"]).max() <= 1e-12
 
 
 def _mutated(variant_dir, tag, mutate_manifest=None, drop=(), add=()):
@@ -185,5 +231,20 @@ def test_gpu_variant_matches_oracle(name, variant_dir):
             assert np.abs(r["virial"] - o["virial"]).max() <= 1e-8 * (1 + np.abs(o["virial"]).max()), case
             assert np.abs(r["charges"] - o["partial_charges"]).max() <= 1e-10, case
             assert np.abs(r["ratios"] - o["hirshfeld_ratios"]).max() <= 1e-10, case
+    finally:
+        g.close()
+
+
+@pytest.mark.gpu
+def test_gpu_l_size_refuses_mixed_precision(variant_dir):
+    """The mixed-precision filter kernels exist for F = 128 only: an F = 256
+    handle refuses SO3LR_PRECISION_MIXED with the reason and keeps float64."""
+    from so3lr_b200 import So3lrB200
+    from so3lr_b200.runtime import So3lrError
+    g = So3lrB200(_variant(variant_dir, "l_size"), 0)
+    try:
+        with pytest.raises(So3lrError, match="F = 128 models only"):
+            g.set_precision("mixed")
+        g.set_precision("float64")
     finally:
         g.close()
