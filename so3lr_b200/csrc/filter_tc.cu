@@ -689,13 +689,16 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
     // slices of both filter gradients and of silu' (one 64- or 32-byte run per
     // chunk), its radial-basis derivatives, the pair scalars and geometry
     auto prefetch_tile = [&](int pp) {
-      if (pp >= P) return;
-      for (int f = 0; f < 2; ++f) {
-        const double *gsrc = f ? g_filt_ev : g_filt_inv;
-        for (int ch = 0; ch < 4; ++ch) {
-          prefetch_l2(gsrc + (size_t)pp * kF + 32 * ch + 8 * part);
+      // the filter gradients of the 8 rows this warp loads (1 KB per row and
+      // filter; lane: row 8 warp + lane / 4, lines 2 (lane % 4), + 1)
+      const int pg = pp - row + 8 * warp + (lane >> 2);
+      if (pg < P)
+        for (int f = 0; f < 2; ++f) {
+          const char *g = reinterpret_cast<const char *>((f ? g_filt_ev : g_filt_inv) + (size_t)pg * kF);
+          prefetch_l2(g + 256 * (lane & 3));
+          prefetch_l2(g + 256 * (lane & 3) + 128);
         }
-      }
+      if (pp >= P) return;
       prefetch_l2(drbf + (size_t)pp * kR + 8 * part);
       if (part == 0) {
         prefetch_l2(pair_sc + (size_t)pp * kPairScalars);
@@ -722,26 +725,37 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
       for (int f = 0; f < 2 && ok; ++f) {
         const int tf = it * 2 + f;
         const double *gsrc = f ? g_filt_ev : g_filt_inv;
-        // the filter gradient into the A ring, 32 columns at a time
+        // the filter gradient into the A ring, 32 columns at a time. The
+        // loads need not follow the TMEM rows: warp w loads rows 8 w .. 8 w + 7
+        // of the chunk, two whole 256-byte row segments per instruction (16
+        // lanes per row, two columns per lane), and writes them to the
+        // swizzled A tile
         for (int ch = 0; ch < 4 && ok; ++ch) {
           const int use = tf * 8 + ch, slot = use & 1;
-          float v[8];  // loaded before the wait for the ring slot
-          if (valid) {
-            const double2 *src = reinterpret_cast<const double2 *>(gsrc + (size_t)p * kF + 32 * ch + 8 * part);
+          const int k = 2 * (lane & 15);  // column within the chunk
+          float2 v2[4];                   // loaded before the wait for the ring slot
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const double2 x = __ldg(src + i);
-              v[2 * i] = float(x.x);
-              v[2 * i + 1] = float(x.y);
+          for (int i = 0; i < 4; ++i) {
+            const int r = 8 * warp + 2 * i + (lane >> 4);
+            const int pr = tile * kTcRows + r;
+            v2[i] = make_float2(0.0f, 0.0f);
+            if (pr < P) {
+              const double2 x = __ldg(reinterpret_cast<const double2 *>(gsrc + (size_t)pr * kF + 32 * ch + k));
+              v2[i] = make_float2(float(x.x), float(x.y));
             }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = 0.0f;
           }
           ok = __all_sync(0xffffffffu, mbar_wait(bar(kREmptyA + slot), ((use >> 1) & 1) ^ 1, abort_flag, err, 28));
           if (!ok) break;
           char *a_hi = reinterpret_cast<char *>(sm + kRevOffA + slot * 2 * kTile);
-          store_row8(a_hi, a_hi + kTile, row, part, v);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = 8 * warp + 2 * i + (lane >> 4);
+            const uint32_t off = (r >> 3) * 1024 + (r & 7) * 128 + (((k >> 2) ^ (r & 7)) * 16) + (k & 3) * 4;
+            const float h0 = tf32_hi(v2[i].x), h1 = tf32_hi(v2[i].y);
+            *reinterpret_cast<float2 *>(a_hi + off) = make_float2(h0, h1);
+            *reinterpret_cast<float2 *>(a_hi + kTile + off) =
+                make_float2(tf32_hi(v2[i].x - h0), tf32_hi(v2[i].y - h1));
+          }
           fence_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(kRFullA + slot));
