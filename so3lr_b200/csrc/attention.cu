@@ -13,6 +13,12 @@
 // (kPL = F / 32: 4 for F = 128, 8 for F = 256; head = lane / kLPH, kLPH = 32 /
 // heads lanes per head) and equivariant channels lane + 32 j (j < kEVL).
 // qkv rows are head-major: [head][q, k, v, q_ev, k_ev][32].
+//
+// Both kernels are templates on the real type T of the per-pair filters, the
+// per-atom rows they gather (qkv, and g_a, g_A in the reverse) and their
+// arithmetic: double for the float64 path, float for the mixed-precision path
+// with the tcgen05 filters (the filters are stored in float32 there and the
+// rows are float32 copies; outputs that float64 code consumes stay double).
 #include "kernels.cuh"
 
 SO3LR_SHAPE_BEGIN
@@ -22,11 +28,17 @@ constexpr int kPL = kF / 32;          // invariant channels per lane
 constexpr int kLPH = 32 / kHeads;     // lanes per head
 constexpr int kEVL = (kEV + 31) / 32; // equivariant channels per lane
 
-__device__ inline double head_sum(double v) {  // sum over the kLPH lanes of a head
+template <typename T>
+__device__ inline T head_sum(T v) {  // sum over the kLPH lanes of a head
 #pragma unroll
   for (int off = 1; off < kLPH; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
   return v;
 }
+// explicitly rounded product and sum (no FMA contraction)
+__device__ inline double mul_rn(double a, double b) { return __dmul_rn(a, b); }
+__device__ inline float mul_rn(float a, float b) { return __fmul_rn(a, b); }
+__device__ inline double add_rn(double a, double b) { return __dadd_rn(a, b); }
+__device__ inline float add_rn(float a, float b) { return __fadd_rn(a, b); }
 
 // kPL consecutive doubles (32-byte aligned, read-only during the kernel) with
 // 256-bit loads
@@ -41,17 +53,34 @@ __device__ inline void store4(double *p, const double (&v)[kPL]) {
 #pragma unroll
   for (int q = 0; q < kPL; q += 2) *reinterpret_cast<double2 *>(p + q) = make_double2(v[q], v[q + 1]);
 }
+// the same for float32 rows (16-byte aligned): 128-bit loads and stores
+__device__ inline void load4(const float *p, float (&v)[kPL]) {
+#pragma unroll
+  for (int q = 0; q < kPL; q += 4)
+    asm("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];"
+        : "=f"(v[q]), "=f"(v[q + 1]), "=f"(v[q + 2]), "=f"(v[q + 3])
+        : "l"(p + q));
+}
+__device__ inline void store4(float *p, const float (&v)[kPL]) {
+#pragma unroll
+  for (int q = 0; q < kPL; q += 4) *reinterpret_cast<float4 *>(p + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+}
+__device__ inline void store4(double *p, const float (&v)[kPL]) {  // widened for float64 consumers
+#pragma unroll
+  for (int q = 0; q < kPL; q += 2) *reinterpret_cast<double2 *>(p + q) = make_double2(v[q], v[q + 1]);
+}
 
 }  // namespace
 
+template <typename T>
 __global__ void __launch_bounds__(256) k_attention_forward(int n, int row0, const int *__restrict__ row_start,
                                                            const int *__restrict__ nbr,
                                                            const int *__restrict__ edge_pair,
                                                            const double *__restrict__ geo,
                                                            const double *__restrict__ sh,
-                                                           const double *__restrict__ qkv,
-                                                           const double *__restrict__ f_inv,
-                                                           const double *__restrict__ f_ev, double norm,
+                                                           const T *__restrict__ qkv,
+                                                           const T *__restrict__ f_inv,
+                                                           const T *__restrict__ f_ev, double norm,
                                                            double *__restrict__ d_inv, double *__restrict__ d_ev) {
   const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -59,24 +88,24 @@ __global__ void __launch_bounds__(256) k_attention_forward(int n, int row0, cons
   const int a = row0 + r;
   const int h = lane / kLPH, o = (lane % kLPH) * kPL;
   const size_t head_off = size_t(h) * 160 + o;
-  double qa[kPL], qea[kPL];
+  T qa[kPL], qea[kPL];
   load4(qkv + (size_t)a * kQKV + head_off + 0 * 32, qa);
   load4(qkv + (size_t)a * kQKV + head_off + 3 * 32, qea);
-  double acc[kPL];
+  T acc[kPL];
 #pragma unroll
-  for (int j = 0; j < kPL; ++j) acc[j] = 0.0;
-  double acc_ev[kEVL];
+  for (int j = 0; j < kPL; ++j) acc[j] = T(0);
+  T acc_ev[kEVL];
   int my_deg[kEVL], my_sh[kEVL];
-  double my_par[kEVL];
+  T my_par[kEVL];
 #pragma unroll
   for (int j = 0; j < kEVL; ++j) {
     const int m = lane + 32 * j;
-    acc_ev[j] = 0.0;
+    acc_ev[j] = T(0);
     my_deg[j] = m < kEV ? degree_of_channel(m) : 0;
     my_sh[j] = m < kEV ? sh_of_channel(m) : 0;
-    my_par[j] = parity_sign(my_deg[j]);
+    my_par[j] = T(parity_sign(my_deg[j]));
   }
-  const double inv_norm = 1.0 / norm;  // one division per atom instead of two per edge
+  const T inv_norm = T(1.0 / norm);  // one division per atom instead of two per edge
   const int e0 = row_start[r], e1 = row_start[r + 1];
   int b_nx = 0, code_nx = 0;  // indices of the next edge, loaded one iteration ahead
   if (e0 < e1) {
@@ -90,15 +119,18 @@ __global__ void __launch_bounds__(256) k_attention_forward(int n, int row0, cons
       b_nx = nbr[e + 1];
       code_nx = edge_pair[e + 1];
       // pull the next edge's rows into L1 while this one is processed: the k, v
-      // and k_ev lines of each head (lines 2-5 and 8-9 of the head's ten 128-byte
-      // lines), both filters (kF / 16 lines each) and the harmonics (two 96-byte halves)
+      // and k_ev lines of each head (double: lines 2-5 and 8-9 of the head's ten
+      // 128-byte lines; float: lines 1, 2 and 4 of five), both filters and the
+      // harmonics (two 96-byte halves)
       const int p_nx = code_nx >= 0 ? code_nx : ~code_nx;
-      constexpr int kQl = 6 * kHeads, kFl = kF / 16;
+      constexpr int kLq = sizeof(T) == 8 ? 6 : 3;  // lines per head
+      constexpr int kQl = kLq * kHeads, kFl = kF * int(sizeof(T)) / 128;
       for (int c = lane; c < kQl + 2 * kFl + 2; c += 32) {
         const char *addr;
         if (c < kQl) {
-          const int j = c % 6;
-          addr = reinterpret_cast<const char *>(qkv + (size_t)b_nx * kQKV) + 128 * ((c / 6) * 10 + (j < 4 ? 2 + j : 4 + j));
+          const int j = c % kLq;
+          const int line = sizeof(T) == 8 ? (c / 6) * 10 + (j < 4 ? 2 + j : 4 + j) : (c / 3) * 5 + (j < 2 ? 1 + j : 4);
+          addr = reinterpret_cast<const char *>(qkv + (size_t)b_nx * kQKV) + 128 * line;
         } else if (c < kQl + kFl) {
           addr = reinterpret_cast<const char *>(f_inv + (size_t)p_nx * kF) + 128 * (c - kQl);
         } else if (c < kQl + 2 * kFl) {
@@ -110,14 +142,14 @@ __global__ void __launch_bounds__(256) k_attention_forward(int n, int row0, cons
       }
     }
     const int p = code >= 0 ? code : ~code;
-    const double phi = geo[(size_t)p * kGeo + 4];
-    double kb[kPL], vb[kPL], keb[kPL], fi[kPL], fe[kPL];
+    const T phi = T(geo[(size_t)p * kGeo + 4]);
+    T kb[kPL], vb[kPL], keb[kPL], fi[kPL], fe[kPL];
     load4(qkv + (size_t)b * kQKV + head_off + 1 * 32, kb);
     load4(qkv + (size_t)b * kQKV + head_off + 2 * 32, vb);
     load4(qkv + (size_t)b * kQKV + head_off + 4 * 32, keb);
     load4(f_inv + (size_t)p * kF + lane * kPL, fi);
     load4(f_ev + (size_t)p * kF + lane * kPL, fe);
-    double ai = 0.0, ae = 0.0;
+    T ai = T(0), ae = T(0);
 #pragma unroll
     for (int j = 0; j < kPL; ++j) {
       ai += qa[j] * kb[j] * fi[j];
@@ -125,14 +157,14 @@ __global__ void __launch_bounds__(256) k_attention_forward(int n, int row0, cons
     }
     ai = head_sum(ai) * inv_norm;
     ae = head_sum(ae) * inv_norm;
-    const double wi = phi * ai;
+    const T wi = phi * ai;
 #pragma unroll
     for (int j = 0; j < kPL; ++j) acc[j] += wi * vb[j];
 #pragma unroll
     for (int j = 0; j < kEVL; ++j) {
-      const double ae_m = __shfl_sync(0xffffffffu, ae, my_deg[j] * kLPH);
+      const T ae_m = __shfl_sync(0xffffffffu, ae, my_deg[j] * kLPH);
       if (lane + 32 * j < kEV) {
-        double y = sh[(size_t)p * kSH + my_sh[j]];
+        T y = T(sh[(size_t)p * kSH + my_sh[j]]);
         if (code < 0) y *= my_par[j];
         acc_ev[j] += phi * ae_m * y;
       }
@@ -141,35 +173,46 @@ __global__ void __launch_bounds__(256) k_attention_forward(int n, int row0, cons
   store4(d_inv + (size_t)a * kF + lane * kPL, acc);
 #pragma unroll
   for (int j = 0; j < kEVL; ++j)
-    if (lane + 32 * j < kEV) d_ev[(size_t)a * kEV + lane + 32 * j] = acc_ev[j];
+    if (lane + 32 * j < kEV) d_ev[(size_t)a * kEV + lane + 32 * j] = double(acc_ev[j]);
 }
 
 void launch_attention_forward(int n, const NeighborState &nb, const double *geo, const double *sh,
                               const double *qkv, const double *f_inv, const double *f_ev, double norm,
                               double *d_inv, double *d_ev, cudaStream_t s) {
   if (n == 0) return;
-  k_attention_forward<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.edge_pair, geo, sh,
-                                                           qkv, f_inv, f_ev, norm, d_inv, d_ev);
+  k_attention_forward<double><<<(n * 32 + 255) / 256, 256, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.edge_pair,
+                                                                   geo, sh, qkv, f_inv, f_ev, norm, d_inv, d_ev);
   SO3_LAUNCH("attention_forward");
 }
+#if SO3LR_FEATURES == 128
+void launch_attention_forward32(int n, const NeighborState &nb, const double *geo, const double *sh,
+                                const float *qkv, const float *f_inv, const float *f_ev, double norm,
+                                double *d_inv, double *d_ev, cudaStream_t s) {
+  if (n == 0) return;
+  k_attention_forward<float><<<(n * 32 + 255) / 256, 256, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.edge_pair,
+                                                                  geo, sh, qkv, f_inv, f_ev, norm, d_inv, d_ev);
+  SO3_LAUNCH("attention_forward32");
+}
+#endif
 
 // Reverse: given g_a = dL/d(d_inv) (= dL/da) and g_A = dL/d(d_ev) for every atom,
 // produce dL/d{q,k,v,q_ev,k_ev} per atom and, for the primary edge of every pair,
 // the scalars the filter reverse needs.
+template <typename T>
 __global__ void __launch_bounds__(32) k_attention_reverse(
     int n, int row0, const int *__restrict__ row_start, const int *__restrict__ nbr, const int *__restrict__ edge_pair,
-    const double *__restrict__ geo, const double *__restrict__ sh, const double *__restrict__ qkv,
-    const double *__restrict__ f_inv, const double *__restrict__ f_ev, const double *__restrict__ g_a,
-    const double *__restrict__ g_A, double norm, double *__restrict__ g_qkv, double *__restrict__ pair_sc,
-    double *__restrict__ g_filt_inv, double *__restrict__ g_filt_ev) {
+    const double *__restrict__ geo, const double *__restrict__ sh, const T *__restrict__ qkv,
+    const T *__restrict__ f_inv, const T *__restrict__ f_ev, const T *__restrict__ g_a,
+    const T *__restrict__ g_A, double norm, double *__restrict__ g_qkv, double *__restrict__ pair_sc,
+    T *__restrict__ g_filt_inv, T *__restrict__ g_filt_ev) {
   const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (r >= n) return;
   const int a = row0 + r;
   const int h = lane / kLPH, o = (lane % kLPH) * kPL;
   const size_t head_off = size_t(h) * 160 + o;
-  const double *qa_row = qkv + (size_t)a * kQKV + head_off;
-  double qa[kPL], ka[kPL], va[kPL], qea[kPL], kea[kPL], ga[kPL];
+  const T *qa_row = qkv + (size_t)a * kQKV + head_off;
+  T qa[kPL], ka[kPL], va[kPL], qea[kPL], kea[kPL], ga[kPL];
   load4(qa_row + 0 * 32, qa);
   load4(qa_row + 1 * 32, ka);
   load4(qa_row + 2 * 32, va);
@@ -183,19 +226,19 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
   // channels (the group's first lane holds the ninth channel of l = 4 as well).
   constexpr int kCPL = (9 + kLPH - 1) / kLPH;  // channels per lane
   int ch[kCPL], shc[kCPL];
-  double gAa[kCPL];
+  T gAa[kCPL];
 #pragma unroll
   for (int k = 0; k < kCPL; ++k) {
     const int j = lane % kLPH + kLPH * k;
     ch[k] = j < slot_width(h) ? slot_offset(h) + j : -1;
     shc[k] = ch[k] >= 0 ? sh_of_channel(ch[k]) : 0;
-    gAa[k] = ch[k] >= 0 ? g_A[(size_t)a * kEV + ch[k]] : 0.0;
+    gAa[k] = ch[k] >= 0 ? g_A[(size_t)a * kEV + ch[k]] : T(0);
   }
-  const double par = parity_sign(h);
-  double gq[kPL], gk[kPL], gv[kPL], gqe[kPL], gke[kPL];
+  const T par = T(parity_sign(h));
+  T gq[kPL], gk[kPL], gv[kPL], gqe[kPL], gke[kPL];
 #pragma unroll
-  for (int j = 0; j < kPL; ++j) gq[j] = gk[j] = gv[j] = gqe[j] = gke[j] = 0.0;
-  const double inv_norm = 1.0 / norm;
+  for (int j = 0; j < kPL; ++j) gq[j] = gk[j] = gv[j] = gqe[j] = gke[j] = T(0);
+  const T inv_norm = T(1.0 / norm);
   const int e0 = row_start[r], e1 = row_start[r + 1];
   int b_nx = 0, code_nx = 0;
   if (e0 < e1) { b_nx = nbr[e0]; code_nx = edge_pair[e0]; }
@@ -209,7 +252,8 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
       // row (5 kF / 16 lines of 128 B), g_a, f_inv and f_ev (kF / 16 lines
       // each), the 96-byte pieces of g_A and the two of the harmonics
       const int p_nx = code_nx >= 0 ? code_nx : ~code_nx;
-      constexpr int kQl = 5 * kF / 16, kFl = kF / 16, kAp = kEV / 12;
+      constexpr int kQl = 5 * kF * int(sizeof(T)) / 128, kFl = kF * int(sizeof(T)) / 128;
+      constexpr int kAp = kEV * int(sizeof(T)) / 96;
       const char *qrow = reinterpret_cast<const char *>(qkv + (size_t)b_nx * kQKV);
 #pragma unroll
       for (int c = lane; c < kQl + 3 * kFl + kAp + 2; c += 32) {
@@ -223,9 +267,9 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
         asm volatile("prefetch.global.L1 [%0];\n" ::"l"(addr));
       }
     }
-    const double phi = geo[(size_t)p * kGeo + 4];
-    const double *b_row = qkv + (size_t)b * kQKV + head_off;
-    double qb[kPL], kb[kPL], vb[kPL], qeb[kPL], keb[kPL], gb[kPL], fi[kPL], fe[kPL];
+    const T phi = T(geo[(size_t)p * kGeo + 4]);
+    const T *b_row = qkv + (size_t)b * kQKV + head_off;
+    T qb[kPL], kb[kPL], vb[kPL], qeb[kPL], keb[kPL], gb[kPL], fi[kPL], fe[kPL];
     load4(b_row + 0 * 32, qb);
     load4(b_row + 1 * 32, kb);
     load4(b_row + 2 * 32, vb);
@@ -236,14 +280,14 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
     load4(f_ev + (size_t)p * kF + lane * kPL, fe);
     // harmonic-weighted adjoint sums per degree, for edge b->a ("in": y of the
     // edge into a) and a->b ("out": parity times that)
-    double s_in, s_out;
+    T s_in, s_out;
     {
-      const double pin = code < 0 ? par : 1.0;  // harmonics are stored for the primary orientation
-      double y[kCPL], gAb[kCPL];
+      const T pin = code < 0 ? par : T(1);  // harmonics are stored for the primary orientation
+      T y[kCPL], gAb[kCPL];
 #pragma unroll
       for (int k = 0; k < kCPL; ++k) {
-        y[k] = ch[k] >= 0 ? sh[(size_t)p * kSH + shc[k]] * pin : 0.0;
-        gAb[k] = ch[k] >= 0 ? g_A[(size_t)b * kEV + ch[k]] : 0.0;
+        y[k] = ch[k] >= 0 ? T(sh[(size_t)p * kSH + shc[k]]) * pin : T(0);
+        gAb[k] = ch[k] >= 0 ? g_A[(size_t)b * kEV + ch[k]] : T(0);
       }
       if constexpr (kCPL == 2) {
         s_in = gAa[0] * y[0] + gAa[1] * y[1];
@@ -261,7 +305,7 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
       s_in = head_sum(s_in);
       s_out = head_sum(s_out);
     }
-    double ai_out = 0, si_in = 0, si_out = 0;
+    T ai_out = 0, si_in = 0, si_out = 0;
 #pragma unroll
     for (int j = 0; j < kPL; ++j) {
       ai_out += qb[j] * ka[j] * fi[j];
@@ -271,8 +315,8 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
     ai_out = head_sum(ai_out) * inv_norm;
     si_in = head_sum(si_in);
     si_out = head_sum(si_out);
-    const double c_q = phi * si_in * inv_norm, c_qe = phi * s_in * inv_norm;
-    const double c_v = phi * ai_out, c_k = phi * si_out * inv_norm, c_ke = phi * s_out * inv_norm;
+    const T c_q = phi * si_in * inv_norm, c_qe = phi * s_in * inv_norm;
+    const T c_v = phi * ai_out, c_k = phi * si_out * inv_norm, c_ke = phi * s_out * inv_norm;
 #pragma unroll
     for (int j = 0; j < kPL; ++j) {
       gq[j] += c_q * (kb[j] * fi[j]);
@@ -288,16 +332,16 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
         // explicitly rounded products and sum (no FMA contraction): the two
         // directions' terms swap when the pair is held from its other endpoint,
         // and a rounded sum is exactly commutative
-        double gi[kPL], ge[kPL];
+        T gi[kPL], ge[kPL];
 #pragma unroll
         for (int j = 0; j < kPL; ++j) {
-          gi[j] = __dadd_rn(__dmul_rn(c_q, __dmul_rn(qa[j], kb[j])), __dmul_rn(c_k, __dmul_rn(qb[j], ka[j])));
-          ge[j] = __dadd_rn(__dmul_rn(c_qe, __dmul_rn(qea[j], keb[j])), __dmul_rn(c_ke, __dmul_rn(qeb[j], kea[j])));
+          gi[j] = add_rn(mul_rn(c_q, mul_rn(qa[j], kb[j])), mul_rn(c_k, mul_rn(qb[j], ka[j])));
+          ge[j] = add_rn(mul_rn(c_qe, mul_rn(qea[j], keb[j])), mul_rn(c_ke, mul_rn(qeb[j], kea[j])));
         }
         store4(g_filt_inv + (size_t)p * kF + lane * kPL, gi);
         store4(g_filt_ev + (size_t)p * kF + lane * kPL, ge);
       }
-      double ai_in = 0, ae_in = 0, ae_out = 0;
+      T ai_in = 0, ae_in = 0, ae_out = 0;
 #pragma unroll
       for (int j = 0; j < kPL; ++j) {
         ai_in += qa[j] * kb[j] * fi[j];
@@ -313,16 +357,16 @@ __global__ void __launch_bounds__(32) k_attention_reverse(
       // directions' products are added with explicitly rounded (commutative)
       // sums and the heads in a symmetric tree, so the values do not depend on
       // which endpoint holds the pair.
-      double t = __dadd_rn(__dadd_rn(__dmul_rn(ai_in, si_in), __dmul_rn(ai_out, si_out)),
-                           __dadd_rn(__dmul_rn(ae_in, s_in), __dmul_rn(ae_out, s_out)));
+      T t = add_rn(add_rn(mul_rn(ai_in, si_in), mul_rn(ai_out, si_out)),
+                   add_rn(mul_rn(ae_in, s_in), mul_rn(ae_out, s_out)));
 #pragma unroll
       for (int off = kLPH; off < 32; off <<= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
       double *ps = pair_sc + (size_t)p * kPairScalars;
-      if (lane == 0) ps[0] = t;
+      if (lane == 0) ps[0] = double(t);
       if (lane == 1) ps[kPairScalars - 1] = 0.0;
       if (lane % kLPH == 0) {
-        ps[1 + h] = ae_in;
-        ps[1 + kHeads + h] = ae_out;
+        ps[1 + h] = double(ae_in);
+        ps[1 + kHeads + h] = double(ae_out);
       }
     }
   }
@@ -343,11 +387,41 @@ void launch_attention_reverse(int n, const NeighborState &nb, const double *geo,
   if (n == 0) return;
   // one warp per CTA: at ~190 registers per thread a CTA's registers are freed
   // as soon as its own atom is done, instead of waiting for the slowest of eight
-  k_attention_reverse<<<n, 32, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.edge_pair, geo, sh,
-                                                           qkv, f_inv, f_ev, g_a, g_A, norm, g_qkv, pair_sc,
-                                                           g_filt_inv, g_filt_ev);
+  k_attention_reverse<double><<<n, 32, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.edge_pair, geo, sh, qkv, f_inv,
+                                               f_ev, g_a, g_A, norm, g_qkv, pair_sc, g_filt_inv, g_filt_ev);
   SO3_LAUNCH("attention_reverse");
 }
+#if SO3LR_FEATURES == 128
+void launch_attention_reverse32(int n, const NeighborState &nb, const double *geo, const double *sh,
+                                const float *qkv, const float *f_inv, const float *f_ev, const float *g_a,
+                                const float *g_A, double norm, double *g_qkv, double *pair_sc, float *g_filt_inv,
+                                float *g_filt_ev, cudaStream_t s) {
+  if (n == 0) return;
+  k_attention_reverse<float><<<n, 32, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.edge_pair, geo, sh, qkv, f_inv,
+                                              f_ev, g_a, g_A, norm, g_qkv, pair_sc, g_filt_inv, g_filt_ev);
+  SO3_LAUNCH("attention_reverse32");
+}
+
+// float32 copies of rows [r0, r0 + n) and of the listed rows of a row-major
+// double array of the given width (the rows the attention kernels gather)
+__global__ void k_rows_to_float(int n, int r0, int nlist, const int *__restrict__ rows, int width,
+                                const double *__restrict__ src, float *__restrict__ dst) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long total = (long long)(n + nlist) * (width / 2);
+  if (i >= total) return;
+  const int k = int(i / (width / 2)), c = int(i % (width / 2)) * 2;
+  const long long row = k < n ? (long long)r0 + k : (long long)rows[k - n];
+  const double2 v = *reinterpret_cast<const double2 *>(src + row * width + c);
+  *reinterpret_cast<float2 *>(dst + row * width + c) = make_float2(float(v.x), float(v.y));
+}
+void launch_rows_to_float(int n, int r0, int nlist, const int *rows, int width, const double *src, float *dst,
+                          cudaStream_t s) {
+  const long long total = (long long)(n + nlist) * (width / 2);
+  if (total == 0) return;
+  k_rows_to_float<<<unsigned((total + 255) / 256), 256, 0, s>>>(n, r0, nlist, rows, width, src, dst);
+  SO3_LAUNCH("rows_to_float");
+}
+#endif
 
 // g_ev[a][m] = g_A[a][m] + sum over a's pairs of 2 (ev_a - ev_b)[m] cg[m] gl0[p][slot of m]
 __global__ void k_ev_l0_reverse(int n, int row0, const int *__restrict__ row_start, const int *__restrict__ nbr,

@@ -797,6 +797,8 @@ std::size_t Evaluator::device_bytes() const {
   for (auto &v : f_inv_) total += v->bytes();
   for (auto &v : f_ev_) total += v->bytes();
   for (auto &v : sp_) total += v->bytes();
+  for (auto &v : qkv32_) total += v->bytes();
+  total += ga32_.bytes() + gA32_.bytes();
   for (auto *vec : {&xb_, &evb_, &qkv_, &xhat1_, &rstd1_, &n1_, &A_, &hp_, &gate_, &xhat2_, &rstd2_})
     for (auto &v : *vec) total += v->bytes();
   total += nbr_.bytes() * 8;
@@ -955,6 +957,15 @@ void Evaluator::compute() {
   const int *own_seg = seg_.get();
   const int *count_seg = identity_ ? image_start_.get() : seg_.get() + 2;
   if (mixed_ && mixed_tc_) SO3_CUDA(cudaMemsetAsync(tc_err_, 0, sizeof(int), s));
+  // mixed precision with the tcgen05 filters: filters, filter gradients and the
+  // attention in float32 (the stated tolerance holds; the float64 path and the
+  // mma.sync mixed path keep the float64 attention)
+  const bool att32 = kF == 128 && mixed_ && mixed_tc_;
+  (void)att32;
+  if (att32 && qkv32_.size() != std::size_t(layers_)) {
+    qkv32_.clear();
+    for (int b = 0; b < layers_; ++b) qkv32_.push_back(std::make_unique<DeviceArray<float>>());
+  }
   build_neighbors();
   const int P = int(stats_.pairs);
   launch_pair_geometry(P, nb_, z_.get(), zbl_, sr_cut_, geo_.get(), sh_.get(), gv_.get(), s);
@@ -971,7 +982,8 @@ void Evaluator::compute() {
 #if SO3LR_FEATURES == 128
     if (mixed_ && mixed_tc_)
       launch_filter_forward_tc(P, geo_.get(), nb_.pair_a, nb_.pair_b, b == 0 ? nullptr : evb_[b]->get(),
-                               tc_fwd_consts_[b], w.finv32, w.fev32, f_inv_[b]->get(), f_ev_[b]->get(),
+                               tc_fwd_consts_[b], w.finv32, w.fev32, reinterpret_cast<float *>(f_inv_[b]->get()),
+                               reinterpret_cast<float *>(f_ev_[b]->get()),
                                reinterpret_cast<float *>(sp_[b]->get()), b == 0 ? drbf_.get() : nullptr, tc_err_,
                                num_sms_, s);
     else if (mixed_)
@@ -1007,8 +1019,18 @@ void Evaluator::compute() {
           launch_qk_norm(int(halo_recv_off_[nranks_]), halo_recv_rows_.get(), qkv_[b]->get(), qkr_[b]->get(), s);
       }
     }
-    launch_attention_forward(n, nb_, geo_.get(), sh_.get(), qkv_[b]->get(), f_inv_[b]->get(), f_ev_[b]->get(), norm_,
-                             d_inv_.get(), d_ev_.get(), s);
+#if SO3LR_FEATURES == 128
+    if (att32) {  // float32 attention: float32 copies of the rows the QKV GEMM computed
+      float *q32 = qkv32_[b]->reserve(std::size_t(N) * kQKV);
+      launch_rows_to_float(identity_ ? N : n, identity_ ? 0 : int(r0), identity_ ? 0 : int(halo_recv_off_[nranks_]),
+                           halo_recv_rows_.get(), kQKV, qkv_[b]->get(), q32, s);
+      launch_attention_forward32(n, nb_, geo_.get(), sh_.get(), q32, reinterpret_cast<const float *>(f_inv_[b]->get()),
+                                 reinterpret_cast<const float *>(f_ev_[b]->get()), norm_, d_inv_.get(), d_ev_.get(),
+                                 s);
+    } else
+#endif
+      launch_attention_forward(n, nb_, geo_.get(), sh_.get(), qkv_[b]->get(), f_inv_[b]->get(), f_ev_[b]->get(),
+                               norm_, d_inv_.get(), d_ev_.get(), s);
     launch_post_attn_pre(n, xb_[b]->get() + r0 * kF, d_inv_.get() + r0 * kF, evb_[b]->get() + r0 * kEV,
                          d_ev_.get() + r0 * kEV, norm1_, w.ln1w, w.ln1b, w.cg_int, xhat1_[b]->get() + r0 * kF,
                          rstd1_[b]->get() + r0, n1_[b]->get() + r0 * kF, act_.get() + r0 * kF,
@@ -1152,14 +1174,31 @@ void Evaluator::compute() {
                              g_a_.get() + r0 * kF, g_A_.get() + r0 * kEV, s);
     // the sender role of the attention reverse reads the neighbours' adjoints
     halo_exchange(g_a_.get(), kF, g_A_.get(), kEV, kProfAdjointHalo);
-    launch_attention_reverse(n, nb_, geo_.get(), sh_.get(), qkv_[b]->get(), f_inv_[b]->get(), f_ev_[b]->get(),
-                             g_a_.get(), g_A_.get(), norm_, b > 0 ? g_qkv_.get() : nullptr, pair_sc_.get(),
-                             g_filt_inv_.get(), g_filt_ev_.get(), s);
+#if SO3LR_FEATURES == 128
+    if (att32) {  // float32 copies of the adjoint rows the reverse gathers (owned and halo)
+      const int nh = identity_ ? 0 : int(halo_recv_off_[nranks_]);
+      float *ga32 = ga32_.reserve(std::size_t(N) * kF), *gA32 = gA32_.reserve(std::size_t(N) * kEV);
+      launch_rows_to_float(identity_ ? N : n, identity_ ? 0 : int(r0), nh, halo_recv_rows_.get(), kF, g_a_.get(), ga32,
+                           s);
+      launch_rows_to_float(identity_ ? N : n, identity_ ? 0 : int(r0), nh, halo_recv_rows_.get(), kEV, g_A_.get(),
+                           gA32, s);
+      launch_attention_reverse32(n, nb_, geo_.get(), sh_.get(), qkv32_[b]->get(),
+                                 reinterpret_cast<const float *>(f_inv_[b]->get()),
+                                 reinterpret_cast<const float *>(f_ev_[b]->get()), ga32, gA32, norm_,
+                                 b > 0 ? g_qkv_.get() : nullptr, pair_sc_.get(),
+                                 reinterpret_cast<float *>(g_filt_inv_.get()), reinterpret_cast<float *>(g_filt_ev_.get()),
+                                 s);
+    } else
+#endif
+      launch_attention_reverse(n, nb_, geo_.get(), sh_.get(), qkv_[b]->get(), f_inv_[b]->get(), f_ev_[b]->get(),
+                               g_a_.get(), g_A_.get(), norm_, b > 0 ? g_qkv_.get() : nullptr, pair_sc_.get(),
+                               g_filt_inv_.get(), g_filt_ev_.get(), s);
     prof_begin(kProfFilterReverse);
 #if SO3LR_FEATURES == 128
     if (mixed_ && mixed_tc_)
       launch_filter_reverse_tc(P, geo_.get(), nb_.pair_a, nb_.pair_b, b > 0 ? evb_[b]->get() : nullptr,
-                               tc_rev_consts_[b], w.finv32, w.fev32, g_filt_inv_.get(), g_filt_ev_.get(),
+                               tc_rev_consts_[b], w.finv32, w.fev32, reinterpret_cast<const float *>(g_filt_inv_.get()),
+                               reinterpret_cast<const float *>(g_filt_ev_.get()),
                                reinterpret_cast<const float *>(sp_[b]->get()), drbf_.get(), g_A_.get(),
                                pair_sc_.get(), b > 0, b < layers_ - 1, g_r_.get(), g_y_.get(), gl0_.get(), tc_err_,
                                num_sms_, s);

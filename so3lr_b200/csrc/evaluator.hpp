@@ -115,6 +115,10 @@ class Evaluator final : public EvaluatorApi {
   void nhc_half(double dt);
   std::vector<std::unique_ptr<DeviceArray<double>>> xb_, evb_, qkv_, xhat1_, rstd1_, n1_, A_, hp_, gate_, xhat2_, rstd2_;
   std::vector<std::unique_ptr<DeviceArray<double>>> qkr_;  // inverse RMS of q, k, q_ev, k_ev [row][head][4]
+  // float32 copies of the rows the attention gathers, mixed precision with
+  // the tcgen05 filters: qkv per block, and the block adjoints g_a, g_A
+  std::vector<std::unique_ptr<DeviceArray<float>>> qkv32_;
+  DeviceArray<float> ga32_, gA32_;
   DeviceArray<double> x0_;                                  // embedding, kept with residual scalars
   DeviceArray<double> d_inv_, d_ev_, act_, cat_, t_, hpre_, hcat_, hk_, e_nn_, raw_q_, q_, ratio_;
   DeviceArray<double> hk6_, ratio6_, dc6_;  // C6 ratio head (models that have one)

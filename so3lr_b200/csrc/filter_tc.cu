@@ -257,7 +257,7 @@ __device__ __forceinline__ void store_row8(char *hi_tile, char *lo_tile, int row
 __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
     int P, int ntiles, const double *__restrict__ geo, const int *__restrict__ pa, const int *__restrict__ pb,
     const double *__restrict__ ev, const __grid_constant__ TcFwdConsts c, FilterW32 finv, FilterW32 fev,
-    double *__restrict__ f_inv, double *__restrict__ f_ev, float *__restrict__ sp, double *__restrict__ drbf,
+    float *__restrict__ f_inv, float *__restrict__ f_ev, float *__restrict__ sp, double *__restrict__ drbf,
     int *__restrict__ err) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -430,7 +430,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
       const int f = tf & 1, d2b = tf & 1, d2use = tf >> 1;
       const int p = (int(blockIdx.x) + (tf >> 1) * int(gridDim.x)) * kTcRows + row;
       const bool valid = p < P;
-      double *out = f ? f_ev : f_inv;
+      float *out = f ? f_ev : f_inv;
       {  // the next tile's per-pair inputs into L2 ahead of its preparation
         const int pn = p + int(gridDim.x) * kTcRows;
         if (pn < P && part == 0) {
@@ -486,8 +486,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
       // the next step's operands first (A1 and A3 are free: every MMA of this
       // step has completed), so its MMAs overlap the output writes below
       if (tf + 1 < total_tf) prepare(tf + 1);
-      // output: D2 + b1 + c1 in float64, 32 columns at a time through the
-      // quarter's staging block, so that each store writes 256 contiguous bytes
+      // output: D2 + b1 + c1 in float32, 32 columns at a time through the
+      // quarter's staging block, so that each store writes 128 contiguous bytes
       // of one row (8 rows per warp)
       const int tile_row0 = (p >> 7) * kTcRows + 32 * q;  // first pair of this quarter
 #pragma unroll 1
@@ -507,7 +507,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const int r = 8 * part + k, pr = tile_row0 + r;
-          if (pr < P) out[(size_t)pr * kF + 32 * ch + lane] = *stage_at(sm, q, r, lane);
+          if (pr < P) out[(size_t)pr * kF + 32 * ch + lane] = float(*stage_at(sm, q, r, lane));
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(kFQuarter + q));
@@ -532,8 +532,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) k_filter_forward_tc(
 // kernel; err (device int, zeroed by the caller) receives the code of a wait
 // that gave up (0: none).
 void launch_filter_forward_tc(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
-                              const TcFwdConsts &consts, const FilterW32 &finv, const FilterW32 &fev, double *f_inv,
-                              double *f_ev, float *sp, double *drbf, int *err, int num_sms, cudaStream_t s) {
+                              const TcFwdConsts &consts, const FilterW32 &finv, const FilterW32 &fev, float *f_inv,
+                              float *f_ev, float *sp, double *drbf, int *err, int num_sms, cudaStream_t s) {
   if (P == 0) return;
   const int ntiles = (P + kTcRows - 1) / kTcRows;
   allow_dynamic_smem(reinterpret_cast<const void *>(k_filter_forward_tc), kSmemFwd);
@@ -578,7 +578,7 @@ constexpr int kRFullB = 0, kREmptyB = 3, kRFullA = 6, kREmptyA = 8, kRDhwFull = 
 __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
     int P, int ntiles, const double *__restrict__ geo, const int *__restrict__ pa, const int *__restrict__ pb,
     const double *__restrict__ ev, const __grid_constant__ TcRevConsts c, FilterW32 finv32,
-    FilterW32 fev32, const double *__restrict__ g_filt_inv, const double *__restrict__ g_filt_ev,
+    FilterW32 fev32, const float *__restrict__ g_filt_inv, const float *__restrict__ g_filt_ev,
     const float *__restrict__ sp, const double *__restrict__ drbf, const double *__restrict__ gA,
     const double *__restrict__ pair_sc, int need_l0, int accumulate, double *__restrict__ g_r,
     double *__restrict__ g_y, double *__restrict__ gl0, int *__restrict__ err) {
@@ -689,15 +689,12 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
     // slices of both filter gradients and of silu' (one 64- or 32-byte run per
     // chunk), its radial-basis derivatives, the pair scalars and geometry
     auto prefetch_tile = [&](int pp) {
-      // the filter gradients of the 8 rows this warp loads (1 KB per row and
-      // filter; lane: row 8 warp + lane / 4, lines 2 (lane % 4), + 1)
+      // the filter gradients of the 8 rows this warp loads (512 B per row and
+      // filter; lane: row 8 warp + lane / 4, line lane % 4)
       const int pg = pp - row + 8 * warp + (lane >> 2);
       if (pg < P)
-        for (int f = 0; f < 2; ++f) {
-          const char *g = reinterpret_cast<const char *>((f ? g_filt_ev : g_filt_inv) + (size_t)pg * kF);
-          prefetch_l2(g + 256 * (lane & 3));
-          prefetch_l2(g + 256 * (lane & 3) + 128);
-        }
+        for (int f = 0; f < 2; ++f)
+          prefetch_l2(reinterpret_cast<const char *>((f ? g_filt_ev : g_filt_inv) + (size_t)pg * kF) + 128 * (lane & 3));
       if (pp >= P) return;
       prefetch_l2(drbf + (size_t)pp * kR + 8 * part);
       if (part == 0) {
@@ -724,11 +721,11 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
       }
       for (int f = 0; f < 2 && ok; ++f) {
         const int tf = it * 2 + f;
-        const double *gsrc = f ? g_filt_ev : g_filt_inv;
-        // the filter gradient into the A ring, 32 columns at a time. The
-        // loads need not follow the TMEM rows: warp w loads rows 8 w .. 8 w + 7
-        // of the chunk, two whole 256-byte row segments per instruction (16
-        // lanes per row, two columns per lane), and writes them to the
+        const float *gsrc = f ? g_filt_ev : g_filt_inv;
+        // the filter gradient (float32) into the A ring, 32 columns at a time.
+        // The loads need not follow the TMEM rows: warp w loads rows 8 w ..
+        // 8 w + 7 of the chunk, two whole 128-byte row segments per instruction
+        // (16 lanes per row, two columns per lane), and writes them to the
         // swizzled A tile
         for (int ch = 0; ch < 4 && ok; ++ch) {
           const int use = tf * 8 + ch, slot = use & 1;
@@ -739,10 +736,7 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
             const int r = 8 * warp + 2 * i + (lane >> 4);
             const int pr = tile * kTcRows + r;
             v2[i] = make_float2(0.0f, 0.0f);
-            if (pr < P) {
-              const double2 x = __ldg(reinterpret_cast<const double2 *>(gsrc + (size_t)pr * kF + 32 * ch + k));
-              v2[i] = make_float2(float(x.x), float(x.y));
-            }
+            if (pr < P) v2[i] = __ldg(reinterpret_cast<const float2 *>(gsrc + (size_t)pr * kF + 32 * ch + k));
           }
           ok = __all_sync(0xffffffffu, mbar_wait(bar(kREmptyA + slot), ((use >> 1) & 1) ^ 1, abort_flag, err, 28));
           if (!ok) break;
@@ -867,7 +861,7 @@ __global__ void __launch_bounds__(kRevThreads, 1) k_filter_reverse_tc(
 
 void launch_filter_reverse_tc(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
                               const TcRevConsts &consts, const FilterW32 &finv32, const FilterW32 &fev32,
-                              const double *g_filt_inv, const double *g_filt_ev,
+                              const float *g_filt_inv, const float *g_filt_ev,
                               const float *sp, const double *drbf, const double *gA, const double *pair_sc,
                               bool need_l0, bool accumulate, double *g_r, double *g_y, double *gl0, int *err,
                               int num_sms, cudaStream_t s) {

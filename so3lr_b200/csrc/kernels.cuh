@@ -128,12 +128,14 @@ void launch_filter_forward_mixed(int P, const double *geo, const int *pair_a, co
 // the same forward on the tcgen05 tensor cores (filter_tc.cu): persistent, one
 // CTA per SM (num_sms); err (device int, zeroed by the caller) receives the
 // code of a wait that gave up, 0 when none did
+// (filters written in float32 for the float32 attention of this path)
 void launch_filter_forward_tc(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
-                              const TcFwdConsts &consts, const FilterW32 &finv, const FilterW32 &fev, double *f_inv,
-                              double *f_ev, float *sp, double *drbf, int *err, int num_sms, cudaStream_t s);
+                              const TcFwdConsts &consts, const FilterW32 &finv, const FilterW32 &fev, float *f_inv,
+                              float *f_ev, float *sp, double *drbf, int *err, int num_sms, cudaStream_t s);
+// (filter gradients read in float32)
 void launch_filter_reverse_tc(int P, const double *geo, const int *pair_a, const int *pair_b, const double *ev,
                               const TcRevConsts &consts, const FilterW32 &finv32, const FilterW32 &fev32,
-                              const double *g_filt_inv, const double *g_filt_ev,
+                              const float *g_filt_inv, const float *g_filt_ev,
                               const float *sp, const double *drbf, const double *gA, const double *pair_sc,
                               bool need_l0, bool accumulate, double *g_r, double *g_y, double *gl0, int *err,
                               int num_sms, cudaStream_t s);
@@ -154,6 +156,22 @@ void launch_attention_reverse(int n, const NeighborState &nb, const double *geo,
                               double *g_filt_ev, cudaStream_t s);
 void launch_ev_l0_reverse(int n, const NeighborState &nb, const double *ev, const double *cg_att,
                           const double *gl0, const double *g_A, double *g_ev, cudaStream_t s);
+#if SO3LR_FEATURES == 128
+// float32 attention of the mixed-precision path (tcgen05 filters): filters,
+// qkv rows and adjoint rows in float32, arithmetic in float32; d_inv, d_ev,
+// g_qkv and the pair scalars are written in double for the float64 code that
+// reads them, the filter gradients in float32
+void launch_attention_forward32(int n, const NeighborState &nb, const double *geo, const double *sh,
+                                const float *qkv, const float *f_inv, const float *f_ev, double norm,
+                                double *d_inv, double *d_ev, cudaStream_t s);
+void launch_attention_reverse32(int n, const NeighborState &nb, const double *geo, const double *sh,
+                                const float *qkv, const float *f_inv, const float *f_ev, const float *g_a,
+                                const float *g_A, double norm, double *g_qkv, double *pair_sc, float *g_filt_inv,
+                                float *g_filt_ev, cudaStream_t s);
+// dst rows [r0, r0 + n) and rows[0..nlist) = float(src rows); width even
+void launch_rows_to_float(int n, int r0, int nlist, const int *rows, int width, const double *src, float *dst,
+                          cudaStream_t s);
+#endif
 
 SO3LR_SHAPE_END
 

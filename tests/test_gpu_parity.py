@@ -450,11 +450,12 @@ def test_gpu_mixed_precision_refuses_unknown_mode(gpu_model):
 def test_gpu_mixed_tensor_core_kernels_match_mma_kernels(monkeypatch):
     """The mixed mode's filter kernels (forward and reverse) on the tcgen05
     tensor cores (default) and on warp-level mma.sync
-    (SO3LR_B200_MIXED_FORWARD=mma) form the same three-pass TF32 products, so
-    they differ only by float32 summation order:
-    forces within 2e-5 eV/A, energies within 1e-6 eV/atom, on a periodic box
-    whose pair count is not a multiple of the 128-pair tile, and on a charged
-    open cluster."""
+    (SO3LR_B200_MIXED_FORWARD=mma) form the same three-pass TF32 products; the
+    tcgen05 path also runs the attention in float32 (the mma.sync path keeps it
+    in float64), so they differ by float32 rounding there and by summation
+    order: forces within 2e-5 eV/A, energies within 1e-6 eV/atom, on a periodic
+    box whose pair count is not a multiple of the 128-pair tile, and on a
+    charged open cluster."""
     from conftest import MODEL
     from so3lr_b200 import So3lrB200
     from so3lr_b200.systems import water_box, water_cluster
