@@ -268,10 +268,11 @@ int so3lr_profile_read(so3lr_handle *h, int kernel, double *total_ms, long long 
  * SO3LR_PRECISION_MIXED runs their GEMMs on the TF32 tensor cores in three
  * passes (each operand split into two TF32 parts) with float32 accumulation and
  * the hidden-layer SiLU in float32, keeps the filters and their gradients in
- * float32 and runs the attention message passing in float32; everything else
- * stays float64 (geometry, node layers, heads, long range, the exact global
- * sums). Stated tolerance against float64: force MAE <= 1e-4 eV/A (measured
- * 8.7e-6, max 2.5e-5, on water boxes of 192 to 24,000 atoms).
+ * float32, runs the attention message passing in float32 and evaluates the
+ * long-range pair term in float32 (summed per atom in float64); everything
+ * else stays float64 (geometry, node layers, heads, the exact global sums).
+ * Stated tolerance against float64: force MAE <= 1e-4 eV/A (measured 8.8e-6,
+ * max 2.5e-5, on water boxes of 192 to 24,000 atoms).
  * The reference has no reduced-precision runtime (float32 is only a storage type
  * of its model file, src/native_model.cpp:266); this mode serves the mixed
  * float32 run of the benchmark configurations. Takes effect from the next

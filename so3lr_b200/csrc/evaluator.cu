@@ -1110,7 +1110,7 @@ void Evaluator::compute() {
                     alpha_ref_, c6_ref_, ref_table_, lr_,
                     reinterpret_cast<double4 *>(lr_pos4_.get()), reinterpret_cast<double4 *>(lr_par4_.get()),
                     e_lr_.get(), e_elec_.get(), e_disp_.get(), dq_.get(), dh_.get(), c6 ? dc6_.get() : nullptr,
-                    f_lr_.get(), w_lr_.get(), s);
+                    f_lr_.get(), w_lr_.get(), s, att32);  // float32 pair term with the float32 attention
   if (identity_) {
     exact_sums(dq_.get(), 1, 1, nimg, image_start_.get(), img_sums_.get());
   } else {

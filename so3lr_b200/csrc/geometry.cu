@@ -10,6 +10,8 @@
 //   virial: plugins/lammps/pair_so3lr_native_mpi.cpp:944-990
 // The reference accumulates atoms with float atomics; here every per-atom sum is
 // a gather over the atom's own CSR row or cell stencil in a fixed order.
+#include <type_traits>
+
 #include "cells.cuh"
 #include "sh.cuh"
 
@@ -266,6 +268,138 @@ __device__ inline LrPair lr_pair_tab(const LrDev &p, const LrConst &k, double r,
   return o;
 }
 
+
+// The same pair term in float32 arithmetic, for the mixed-precision mode: the
+// caller passes the float32 distance and per-atom values and adds the float32
+// results into float64 sums. Same formulas and switch as lr_pair_tab, with
+// CUDA's float32 erf/exp/log and IEEE float32 division.
+struct LrConst32 {
+  float ke_s, hartree_s, inv_sigma, inv_elec_width, inv_disp_width, inv_bohr, cutoff, elec_cuton, disp_cuton, shift,
+      fshift, fine_factor, disp_scale;
+};
+__device__ inline LrConst32 lr_const32(const LrDev &p) {
+  LrConst32 c;
+  c.ke_s = float(p.full_scale * p.ke);
+  c.hartree_s = float(p.full_scale * p.hartree);
+  c.inv_sigma = float(1.0 / p.sigma);
+  c.inv_elec_width = float(1.0 / (p.cutoff - p.elec_cuton));
+  c.inv_disp_width = float(1.0 / (p.cutoff - p.disp_cuton));
+  c.inv_bohr = float(1.0 / p.bohr);
+  c.cutoff = float(p.cutoff);
+  c.elec_cuton = float(p.elec_cuton);
+  c.disp_cuton = float(p.disp_cuton);
+  c.shift = float(p.shift);
+  c.fshift = float(p.fshift);
+  c.fine_factor = float(p.fine_factor);
+  c.disp_scale = float(p.disp_scale);
+  return c;
+}
+__device__ inline void smooth_switch32(float r, float cuton, float cutoff, float inv_width, float &v, float &dv) {
+  if (r >= cutoff) {
+    v = 0.0f;
+    dv = 0.0f;
+    return;
+  }
+  const float c = (r - cuton) * inv_width;
+  const float left = 1.0f - c, right = c;
+  const float sl = left > 1.0e-12f ? left : 1.0e-12f, sr = right > 1.0e-12f ? right : 1.0e-12f;
+  const float isl = 1.0f / sl, isr = 1.0f / sr;
+  const float sig_l = left > 0.0f ? expf(-isl) : 0.0f;
+  const float sig_r = right > 0.0f ? expf(-isr) : 0.0f;
+  const float iden = 1.0f / (sig_l + sig_r + 1.0e-12f);
+  v = sig_l * iden;
+  const float dl = left > 0.0f ? -sig_l * isl * isl : 0.0f;
+  const float dr = right > 0.0f ? sig_r * isr * isr : 0.0f;
+  dv = (dl - v * (dl + dr)) * iden * inv_width;
+}
+template <bool kSepC6>
+__device__ inline LrPair lr_pair_f32(const LrConst32 &k, float r, float qi, float qj, float hi, float hj, float ai0,
+                                     float aj0, float ci0, float cj0, float si, float sj) {
+  constexpr float inv_sqrt_pi = 0.56418958354775628695f;
+  constexpr float inv7 = 1.0f / 7.0f;
+  LrPair o{0, 0, 0, 0, 0, 0};
+  float esw, desw;
+  smooth_switch32(r, k.elec_cuton, k.cutoff, k.inv_elec_width, esw, desw);
+  const float inv_r = 1.0f / r;
+  const float ratio = r * k.inv_sigma;
+  const float erf_t = erff(ratio);
+  const float exp_t = expf(-(ratio * ratio));
+  const float pot = erf_t * inv_r;
+  const float dpot = (2.0f * r * exp_t * inv_sqrt_pi * k.inv_sigma - erf_t) * (inv_r * inv_r);
+  const float disp = r - k.cutoff;
+  const float shifted = pot - k.shift - k.fshift * disp;
+  const float kernel = esw * (pot - k.shift) + (1.0f - esw) * shifted;
+  const float rkernel = dpot - (1.0f - esw) * k.fshift + desw * k.fshift * disp;
+  o.e_elec = k.ke_s * qi * qj * kernel;
+  o.dq = k.ke_s * kernel * qj;
+  const float erad = k.ke_s * qi * qj * rkernel;
+  float drad = 0.0f;
+  if (ai0 >= 0.0f && aj0 >= 0.0f) {
+    const float ai = ai0 * hi, aj = aj0 * hj;
+    const float c6i = kSepC6 ? ci0 * si : ci0 * hi * hi, c6j = kSepC6 ? cj0 * sj : cj0 * hj * hj;
+    const float alpha = 0.5f * (ai + aj);
+    const float num = 2.0f * c6i * c6j * aj * ai;
+    const float den = ai * ai * c6j + aj * aj * c6i;
+    if (alpha > 0.0f && den > 1.0e-30f) {
+      const float iden = 1.0f / den;
+      const float c6 = num * iden;
+      float dc6_dhi, dc6_dsi = 0.0f;
+      if (!kSepC6) {
+        const float dc6i = 2.0f * ci0 * hi;
+        const float dn_dhi = 2.0f * (dc6i * c6j * aj * ai + c6i * c6j * aj * ai0);
+        const float dd_dhi = 2.0f * ai * ai0 * c6j + aj * aj * dc6i;
+        dc6_dhi = (dn_dhi * den - num * dd_dhi) * (iden * iden);
+      } else {
+        const float dn_dai = 2.0f * c6i * c6j * aj * ai0;
+        const float dd_dai = 2.0f * ai * ai0 * c6j;
+        dc6_dhi = (dn_dai * den - num * dd_dai) * (iden * iden);
+        const float dn_dsi = 2.0f * ci0 * c6j * aj * ai;
+        const float dd_dsi = aj * aj * ci0;
+        dc6_dsi = (dn_dsi * den - num * dd_dsi) * (iden * iden);
+      }
+      const float ialpha7 = inv7 / alpha;
+      const float a7 = expf(logf(alpha) * inv7);
+      const float rv = k.fine_factor * a7;
+      constexpr float b0 = -0.00433008f, b1 = 0.24428889f, b2 = 0.04125273f, b3 = -0.00078893f;
+      const float sig = b3 * rv * rv * rv + b2 * rv * rv + b1 * rv + b0;
+      const float isig = 1.0f / sig;
+      const float gam = 0.5f * isig * isig;
+      const float igam = 2.0f * sig * sig;
+      const float drv = rv * ialpha7;
+      const float dsig = (3.0f * b3 * rv * rv + 2.0f * b2 * rv + b1) * drv;
+      const float dgam = -2.0f * gam * dsig * isig;
+      const float c8 = 5.0f * c6 * igam;
+      const float c10 = 245.0f * c6 * (igam * igam) * 0.125f;
+      const float damp = k.disp_scale * 2.0f * 2.54f * a7;
+      const float ddamp = damp * ialpha7;
+      const float ra = r * k.inv_bohr;
+      const float r2 = ra * ra, r4 = r2 * r2, r6 = r4 * r2, r8 = r4 * r4, r10 = r8 * r2;
+      const float p2 = damp * damp, p4 = p2 * p2, p6 = p4 * p2, p8 = p4 * p4, p10 = p8 * p2;
+      const float id6 = 1.0f / (r6 + p6), id8 = 1.0f / (r8 + p8), id10 = 1.0f / (r10 + p10);
+      const float qdo = -c6 * id6 - c8 * id8 - c10 * id10;
+      const float rad_au =
+          (6.0f * c6 * r4 * id6 * id6 + 8.0f * c8 * r6 * id8 * id8 + 10.0f * c10 * r8 * id10 * id10) * ra;
+      const float dc8 = -c8 * dgam * igam;
+      const float dc10 = -2.0f * c10 * dgam * igam;
+      const float dd6 = 6.0f * p4 * damp * ddamp;
+      const float dd8 = 8.0f * p6 * damp * ddamp;
+      const float dd10 = 10.0f * p8 * damp * ddamp;
+      const float dpot_da = c6 * dd6 * id6 * id6 - dc8 * id8 + c8 * dd8 * id8 * id8 - dc10 * id10 +
+                            c10 * dd10 * id10 * id10;
+      const float dpot_dc6 = -id6 - 5.0f * igam * id8 - 245.0f * 0.125f * (igam * igam) * id10;
+      const float dpot_dhi = dpot_dc6 * dc6_dhi + dpot_da * 0.5f * ai0;
+      float dsw, ddsw;
+      smooth_switch32(r, k.disp_cuton, k.cutoff, k.inv_disp_width, dsw, ddsw);
+      o.e_disp = k.hartree_s * qdo * dsw;
+      drad = k.hartree_s * (rad_au * dsw * k.inv_bohr + qdo * ddsw);
+      o.dh = k.hartree_s * dsw * dpot_dhi;
+      if (kSepC6) o.dc = k.hartree_s * dsw * dpot_dc6 * dc6_dsi;
+    }
+  }
+  o.radial = erad + drad;
+  return o;
+}
+
 // one 256-bit read-only load of a 32-byte aligned double4
 __device__ inline double4 ld4(const double4 *p) {
   double4 v;
@@ -309,7 +443,7 @@ struct LrStencil {
   signed char rx[kLrMaxReach + 1][kLrMaxReach + 1];
 };
 constexpr int kLrQueue = 64;
-template <bool kSepC6>
+template <bool kSepC6, bool kF32>
 __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
     int n, int row0, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
     const int *__restrict__ cell_start, const int *__restrict__ cell_count, const int *__restrict__ image_of,
@@ -332,6 +466,8 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
   const double ai0 = (Zi - 1 >= 0 && Zi - 1 < table) ? aref[Zi - 1] : -1.0;
   const double ci0 = (Zi - 1 >= 0 && Zi - 1 < table) ? cref[Zi - 1] : 0.0;
   const LrConst kc = lr_const(p);
+  LrConst32 kc32{};
+  if (kF32) kc32 = lr_const32(p);
   double acc_ee = 0, acc_ed = 0, acc_dq = 0, acc_dh = 0, acc_dc = 0, fx = 0, fy = 0, fz = 0;
   double wxx = 0, wyy = 0, wzz = 0, wxy = 0, wxz = 0, wyz = 0;
   int count = 0;  // warp-uniform queue length
@@ -340,7 +476,12 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
     const double vx = qv[wl][slot][0], vy = qv[wl][slot][1], vz = qv[wl][slot][2];
     const double r = sqrt(vx * vx + vy * vy + vz * vz);
     const double4 pj = ld4(pos4 + k), hj = ld4(par4 + k);
-    const LrPair o = lr_pair_tab<kSepC6>(p, kc, r, qi, pj.w, hi, hj.x, ai0, hj.y, ci0, hj.z, si, hj.w);
+    LrPair o;
+    if constexpr (kF32)
+      o = lr_pair_f32<kSepC6>(kc32, float(r), float(qi), float(pj.w), float(hi), float(hj.x), float(ai0), float(hj.y),
+                              float(ci0), float(hj.z), float(si), float(hj.w));
+    else
+      o = lr_pair_tab<kSepC6>(p, kc, r, qi, pj.w, hi, hj.x, ai0, hj.y, ci0, hj.z, si, hj.w);
     acc_ee += o.e_elec;
     acc_ed += o.e_disp;
     acc_dq += o.dq;
@@ -492,7 +633,7 @@ void launch_long_range(int n, int n_cells_atoms, const NeighborState &nb, double
                        const double *q, const double *h, const double *c6r, const double *alpha_ref,
                        const double *c6_ref, int table_size, LrDev p, double4 *pos4, double4 *par4, double *e_lr,
                        double *e_elec, double *e_disp, double *dq, double *dh, double *dc6, double *f_lr,
-                       double *w_lr, cudaStream_t s) {
+                       double *w_lr, cudaStream_t s, bool f32) {
   if (n == 0) return;
   k_lr_gather<<<(n_cells_atoms + 255) / 256, 256, 0, s>>>(n_cells_atoms, nb.grid.periodic || nb.grid.open_cells,
                                                           nb.cell_atoms, nb.xw, q, h,
@@ -520,16 +661,23 @@ void launch_long_range(int n, int n_cells_atoms, const NeighborState &nb, double
   }
   const int threads = kLrWarps * 32;
   const int blocks = (n * 32 + threads - 1) / threads;
-  if (c6r != nullptr)
-    k_long_range<true><<<blocks, threads, 0, s>>>(n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count,
-                                                  nb.image_of, nb.image_start, reach, st, rc_lr * rc_lr, pos4, par4, z,
-                                                  q, h, c6r, alpha_ref, c6_ref, table_size, p, e_lr, e_elec, e_disp,
-                                                  dq, dh, dc6, f_lr, w_lr);
-  else
-    k_long_range<false><<<blocks, threads, 0, s>>>(n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count,
-                                                   nb.image_of, nb.image_start, reach, st, rc_lr * rc_lr, pos4, par4,
-                                                   z, q, h, nullptr, alpha_ref, c6_ref, table_size, p, e_lr, e_elec,
-                                                   e_disp, dq, dh, nullptr, f_lr, w_lr);
+  auto go = [&](auto sep, auto f) {
+    constexpr bool kSep = decltype(sep)::value, kF = decltype(f)::value;
+    k_long_range<kSep, kF><<<blocks, threads, 0, s>>>(n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start,
+                                                      nb.cell_count, nb.image_of, nb.image_start, reach, st,
+                                                      rc_lr * rc_lr, pos4, par4, z, q, h, kSep ? c6r : nullptr,
+                                                      alpha_ref, c6_ref, table_size, p, e_lr, e_elec, e_disp, dq, dh,
+                                                      kSep ? dc6 : nullptr, f_lr, w_lr);
+  };
+  using T = std::true_type;
+  using F = std::false_type;
+  if (c6r != nullptr) {
+    if (f32) go(T{}, T{});
+    else go(T{}, F{});
+  } else {
+    if (f32) go(F{}, T{});
+    else go(F{}, F{});
+  }
   SO3_LAUNCH("long_range");
 }
 

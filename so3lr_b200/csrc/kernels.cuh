@@ -76,6 +76,7 @@ struct LrDev {
 // n: owned rows (nb.row0 ..); n_cells_atoms: atoms in the cell list (all real
 // atoms; with open boundaries, every row). pos4 / par4: n_cells_atoms-element
 // scratch for the cell-ordered partner data.
+// f32: the pair term in float32 arithmetic, summed in float64 (mixed precision).
 // c6r: per-atom C6 ratios of a model with a C6 head (C6_i = C6_ref c6r_i,
 // alpha_i = alpha_ref h_i; dc6 = dE/dc6r), or nullptr (C6_i = C6_ref h_i^2, dc6
 // unused)
@@ -83,7 +84,7 @@ void launch_long_range(int n, int n_cells_atoms, const NeighborState &nb, double
                        const double *q, const double *h, const double *c6r, const double *alpha_ref,
                        const double *c6_ref, int table_size, LrDev p, double4 *pos4, double4 *par4, double *e_lr,
                        double *e_elec, double *e_disp, double *dq, double *dh, double *dc6, double *f_lr,
-                       double *w_lr, cudaStream_t s);
+                       double *w_lr, cudaStream_t s, bool f32 = false);
 
 // Allocation-free variant of the long-range step for open-boundary systems of
 // at most noalloc_max_atoms() atoms (scratch in file-scope device arrays, noalloc.cu).
