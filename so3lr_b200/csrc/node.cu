@@ -15,22 +15,28 @@
 SO3LR_SHAPE_BEGIN
 namespace {
 
-// 64 x 64 output tile per CTA, 4 warps of 32 x 32 (2 x 4 m16n8k8 blocks), K in
-// steps of 16 through a two-stage cp.async pipeline. A is staged as [m][k] and
+// 32 x 64 output tile per CTA, 4 warps of 32 x 16 (2 x 2 m16n8k8 blocks), K in
+// steps of 16 through a two-stage cp.async pipeline. (The node GEMMs have
+// M = atoms and N, K = 32..320: at 24,000 atoms 64-row tiles gave 1.27 waves of
+// CTAs on 148 SMs; 32-row tiles at about 70 registers run 6 CTAs per SM and
+// measured 0.23 ms per MD step faster.) A is staged as [m][k] and
 // B as [n][k] (transposed weights) or [k][n]; the shared-memory row strides keep
 // the fragment loads free of bank conflicts (24 = 8 mod 16 doubles for 16-byte
 // loads of two rows, 66 = 2 mod 16 for 8-byte loads of four k rows).
-constexpr int BM = 64, BN = 64, BK = 16;
+constexpr int BN = 64, BK = 16;
 constexpr int LDA_S = BK + 8, LDBT_S = BK + 8, LDBN_S = BN + 2;
 constexpr int kGemmThreads = 128;
-template <bool TRANSB>
+template <bool TRANSB, int BMT>
 constexpr int gemm_smem_doubles() {
-  return 2 * BM * LDA_S + 2 * (TRANSB ? BN * LDBT_S : BK * LDBN_S);
+  return 2 * BMT * LDA_S + 2 * (TRANSB ? BN * LDBT_S : BK * LDBN_S);
 }
 
-template <bool TRANSB, Epi EPI>
+template <bool TRANSB, Epi EPI, int BMT>
 __global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols, int ldaux2) {
   extern __shared__ double gsm[];
+  constexpr int BM = BMT;
+  constexpr int WN = BMT == 64 ? 2 : 4;  // warps along N (warp tiles of 32 rows)
+  constexpr int NI = BN / WN / 8;        // n8 blocks per warp
   constexpr int ASTAGE = BM * LDA_S;
   constexpr int BSTAGE = TRANSB ? BN * LDBT_S : BK * LDBN_S;
   double *As = gsm;
@@ -43,7 +49,7 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols,
   const double *bias = g.bias ? g.bias + z * g.strideBias : nullptr;
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
-  const int wm = warp >> 1, wn = warp & 1;
+  const int wm = warp / WN, wn = warp % WN;
   auto load_stage = [&](int stage, int k0) {
     double *as = As + stage * ASTAGE;
     for (int c = tid; c < BM * BK / 2; c += kGemmThreads) {
@@ -84,11 +90,11 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols,
       }
     }
   };
-  double acc[2][4][4];
+  double acc[2][NI][4];
 #pragma unroll
   for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
-    for (int ni = 0; ni < 4; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.0;
+    for (int ni = 0; ni < NI; ++ni) acc[mi][ni][0] = acc[mi][ni][1] = acc[mi][ni][2] = acc[mi][ni][3] = 0.0;
   const int nk = (g.K + BK - 1) / BK;
   load_stage(0, 0);
   cp_async_commit();
@@ -101,12 +107,12 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols,
     const double *bs = Bs + (kt & 1) * BSTAGE;
 #pragma unroll
     for (int ks = 0; ks < BK / 8; ++ks) {
-      double a[2][4], b[4][2];
+      double a[2][4], b[NI][2];
       load_afrag(as, LDA_S, wm * 32, ks, gq, tq, a[0]);
       load_afrag(as, LDA_S, wm * 32 + 16, ks, gq, tq, a[1]);
 #pragma unroll
-      for (int ni = 0; ni < 4; ++ni) {
-        const int nn = wn * 32 + ni * 8 + gq;
+      for (int ni = 0; ni < NI; ++ni) {
+        const int nn = wn * (BN / WN) + ni * 8 + gq;
         if (TRANSB) {
           const double2 v = *reinterpret_cast<const double2 *>(bs + nn * LDBT_S + 8 * ks + 2 * tq);
           b[ni][0] = v.x;
@@ -119,7 +125,7 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols,
 #pragma unroll
       for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
-        for (int ni = 0; ni < 4; ++ni) dmma16(acc[mi][ni], a[mi], b[ni]);
+        for (int ni = 0; ni < NI; ++ni) dmma16(acc[mi][ni], a[mi], b[ni]);
     }
     __syncthreads();  // the stage is refilled two iterations later
   }
@@ -131,10 +137,10 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols,
       if (lrow >= g.M) continue;
       const int row = g.rows ? g.rows[lrow] : lrow;
 #pragma unroll
-      for (int ni = 0; ni < 4; ++ni) {
+      for (int ni = 0; ni < NI; ++ni) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int col = n0 + wn * 32 + ni * 8 + 2 * tq + h;
+          const int col = n0 + wn * (BN / WN) + ni * 8 + 2 * tq + h;
           if (col >= g.N) continue;
           double v = acc[mi][ni][2 * hf + h];
           if (EPI == Epi::Bias) {
@@ -160,11 +166,12 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols,
     }
 }
 
+constexpr int kGemmBM = 32;  // rows per tile (the kernel also supports 64)
 template <bool T, Epi E>
 void launch_gemm_kernel(const GemmArgs &g, dim3 grid, cudaStream_t s, int aux_cols, int ldaux2) {
-  constexpr size_t smem = sizeof(double) * gemm_smem_doubles<T>();
-  allow_dynamic_smem(reinterpret_cast<const void *>(k_gemm<T, E>), smem);
-  k_gemm<T, E><<<grid, kGemmThreads, smem, s>>>(g, aux_cols, ldaux2);
+  constexpr size_t smem = sizeof(double) * gemm_smem_doubles<T, kGemmBM>();
+  allow_dynamic_smem(reinterpret_cast<const void *>(k_gemm<T, E, kGemmBM>), smem);
+  k_gemm<T, E, kGemmBM><<<grid, kGemmThreads, smem, s>>>(g, aux_cols, ldaux2);
 }
 
 template <bool T>
@@ -185,7 +192,7 @@ void dispatch_epi(const GemmArgs &g, dim3 grid, cudaStream_t s, int aux_cols, in
 
 void launch_gemm_ex(const GemmArgs &g, int aux_cols, int ldaux2, cudaStream_t s) {
   if (g.M == 0) return;
-  dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.batch);
+  dim3 grid((g.N + BN - 1) / BN, (g.M + kGemmBM - 1) / kGemmBM, g.batch);
   if (g.transB) dispatch_epi<true>(g, grid, s, aux_cols, ldaux2);
   else dispatch_epi<false>(g, grid, s, aux_cols, ldaux2);
   SO3_LAUNCH("gemm");
