@@ -377,29 +377,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
       const int row = wr * 16 + hf * 8 + g, col = wc * 16 + j * 8 + 2 * t;
       *reinterpret_cast<double2 *>(gw + row * LDR + col) = make_double2(grb[j][2 * hf], grb[j][2 * hf + 1]);
     }
-  // rank 0 prefetches the per-pair inputs of the radial and harmonic gradients
-  // into the free gF region
-  double *sc = gF;                        // TP x kPairScalars pair scalars
-  double *geos = sc + TP * kPairScalars;  // TP x 8 geometry
-  double *drs = geos + TP * kGeo;         // TP x kR radial-basis derivatives
-  if (f == 0) {
-    stage_rows<kPairScalars>(sc, kPairScalars, pair_sc, p0, P);
-    stage_rows<kGeo>(geos, kGeo, geo, p0, P);
-    stage_rows<kR>(drs, kR, drbf, p0, P);
-    cp_async_commit();
-  }
+  // Each rank finishes half of the tile's pairs: rank f takes rows
+  // [f TP/2, (f+1) TP/2). It prefetches those pairs' inputs of the radial and
+  // harmonic gradients into its free gF region, then adds the two ranks'
+  // radial-basis and L0 gradients of its rows (rank 0's + rank 1's, the same
+  // order on either rank), reading the other rank's through distributed
+  // shared memory.
+  constexpr int kHalf = TP / 2;
+  const int r0 = f * kHalf;
+  double *sc = gF;                           // kHalf x kPairScalars pair scalars
+  double *geos = sc + kHalf * kPairScalars;  // kHalf x 8 geometry
+  double *drs = geos + kHalf * kGeo;         // kHalf x kR radial-basis derivatives
+  stage_rows<kPairScalars>(sc, kPairScalars, pair_sc, p0 + r0, P, kHalf);
+  stage_rows<kGeo>(geos, kGeo, geo, p0 + r0, P, kHalf);
+  stage_rows<kR>(drs, kR, drbf, p0 + r0, P, kHalf);
+  cp_async_commit();
   cluster.sync();  // both CTAs' radial-basis and L0 gradients are in shared memory
-  if (f == 0) {
-    const double *rgw = cluster.map_shared_rank(gw, 1);
-    const double *rgl = cluster.map_shared_rank(gl, 1);
-    for (int idx = tid; idx < TP * kR; idx += blockDim.x) {
-      const int row = idx / kR, c = idx % kR;
-      gw[row * LDR + c] += rgw[row * LDR + c];
+  {
+    const double *rgw = cluster.map_shared_rank(gw, f ^ 1);
+    const double *rgl = cluster.map_shared_rank(gl, f ^ 1);
+    for (int idx = tid; idx < kHalf * kR; idx += blockDim.x) {
+      const int row = r0 + idx / kR, c = idx % kR;
+      const double mine = gw[row * LDR + c], other = rgw[row * LDR + c];
+      gw[row * LDR + c] = f == 0 ? mine + other : other + mine;
     }
-    gl[tid] += rgl[tid];
+    if (tid < kHalf * kHeads) {
+      const int i = r0 * kHeads + tid;
+      const double mine = gl[i], other = rgl[i];
+      gl[i] = f == 0 ? mine + other : other + mine;
+    }
   }
-  cluster.sync();  // rank 1 stays resident until rank 0 has read its shared memory
-  if (f != 0) return;
+  cluster.sync();  // neither CTA leaves while the other reads its shared memory
   cp_async_wait<0>();
   __syncthreads();
 
@@ -407,39 +415,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
   // term, and the harmonic gradient g_Y[m]; both are summed over the blocks
   // (written by the first block reversed, added by the others) and turned into
   // the Cartesian pair gradient once per evaluation (launch_pair_tail).
-  // kTPP threads per pair: thread q sums basis functions 8q..8q+7 and handles
-  // the distinct harmonics kSH/kTPP q ..; a harmonic of degree l collects the
+  // 8 threads per pair: thread q sums basis functions kR/8 q .. and handles the
+  // distinct harmonics 3q, 3q + 1, 3q + 2; a harmonic of degree l collects the
   // channels of every slot of degree l (one slot for F = 128, two for F = 256),
   // slot by slot.
-  const int pl = (tid >> kTPPLog), q = (tid & (kTPP - 1));
-  const int p = p0 + pl;
+  constexpr int kRq = kR / 8;
+  const int pl = tid >> 3, q = tid & 7;
+  if (pl >= kHalf) return;
+  const int p = p0 + r0 + pl;
   double gr = 0.0;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) gr += gw[pl * LDR + 8 * q + j] * drs[pl * kR + 8 * q + j];
+  for (int j = 0; j < kRq; ++j) gr += gw[(r0 + pl) * LDR + kRq * q + j] * drs[pl * kR + kRq * q + j];
   const double *s = sc + pl * kPairScalars;
   const double dphi = geos[pl * kGeo + 5], phi = geos[pl * kGeo + 4];
   if (q == 0) gr += __dmul_rn(s[0], dphi);  // cutoff gradient (its weight is orientation-independent)
   gr += __shfl_xor_sync(0xffffffffu, gr, 1);
   gr += __shfl_xor_sync(0xffffffffu, gr, 2);
-  if constexpr (kTPP == 8) gr += __shfl_xor_sync(0xffffffffu, gr, 4);
+  gr += __shfl_xor_sync(0xffffffffu, gr, 4);
   if (p < P) {
     if (q == 0) g_r[p] = accumulate ? g_r[p] + gr : gr;
     const int a = pa[p], b = pb[p];
-    constexpr int kShPer = kSH / kTPP;
-    if constexpr (kDupDegrees == 1) {  // one slot per degree: channel m is harmonic m
 #pragma unroll
-      for (int j = 0; j < 6; ++j) {
-        const int m = 6 * q + j;
-        const int d = degree_of_channel(m);
-        const double y = __dmul_rn(phi, __dadd_rn(__dmul_rn(s[1 + d], gA[(size_t)a * kEV + m]),
-                                                  parity_sign(d) * __dmul_rn(s[5 + d], gA[(size_t)b * kEV + m])));
-        double *dst = g_y + (size_t)p * kSH + m;
-        *dst = accumulate ? *dst + y : y;
-      }
-    } else {
-#pragma unroll
-    for (int j = 0; j < kShPer; ++j) {
-      const int m = kShPer * q + j;  // distinct harmonic
+    for (int j = 0; j < 3; ++j) {
+      const int m = 3 * q + j;  // distinct harmonic
       const int l = m < 3 ? 1 : (m < 8 ? 2 : (m < 15 ? 3 : 4));
       double v = 0.0;
 #pragma unroll
@@ -454,8 +452,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 2) k_filter_rev
       double *dst = g_y + (size_t)p * kSH + m;
       *dst = accumulate ? *dst + y : y;
     }
-    }
-    if (need_l0) gl0[(size_t)p * kHeads + q] = gl[pl * kHeads + q];
+    if (need_l0 && q < kHeads) gl0[(size_t)p * kHeads + q] = gl[(r0 + pl) * kHeads + q];
   }
 }
 

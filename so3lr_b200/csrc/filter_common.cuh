@@ -78,12 +78,12 @@ __device__ inline void compute_l0(int P, int p0, const int *pa, const int *pb, c
   l0[pl * kHeads + d] = v;
 }
 
-// copy a TP x width block of a row-major global array (row stride = width) to
-// shared memory with row stride lds; rows beyond P are zero-filled
+// copy an nrows x width block of a row-major global array (row stride = width)
+// to shared memory with row stride lds; rows beyond P are zero-filled
 template <int WIDTH>
-__device__ inline void stage_rows(double *dst, int lds, const double *src, int p0, int P) {
+__device__ inline void stage_rows(double *dst, int lds, const double *src, int p0, int P, int nrows = TP) {
   constexpr int chunks = WIDTH / 2;  // 16-byte chunks per row
-  for (int idx = threadIdx.x; idx < TP * chunks; idx += blockDim.x) {
+  for (int idx = threadIdx.x; idx < nrows * chunks; idx += blockDim.x) {
     const int row = idx / chunks, c = idx % chunks;
     double *d = dst + row * lds + 2 * c;
     if (p0 + row < P) {
