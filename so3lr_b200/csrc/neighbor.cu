@@ -142,56 +142,155 @@ __global__ void k_cell_sort(int ncells, const int *__restrict__ cell_start, cons
   }
 }
 
-__global__ void k_sr_count(int n, int row0, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
-                           const int *__restrict__ cell_start, const int *__restrict__ cell_count,
-                           const int *__restrict__ cell_atoms, const int *__restrict__ image_of,
-                           const int *__restrict__ image_start, double rc2, int reach, const int *__restrict__ tag,
-                           int *__restrict__ deg) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+// Short-range neighbour rows: the degree of every owned atom (kFill = false),
+// then its CSR row (kFill = true). One warp per owned atom, the lanes testing 32 consecutive candidates of a contiguous
+// run of cells at a time (a stencil row of cells with one periodic shift, or an
+// image's atom range). The separation d = x_i - (x_j + shift) is evaluated in
+// a canonical orientation: from the endpoint with the smaller global tag (for
+// an atom and its own periodic image, from the positive image), the other
+// endpoint negating the same rounded result. Both atoms of a pair therefore see
+// bit-identical |d|, so every inclusion test is symmetric and the neighbour
+// lists of different GPUs agree exactly. The fill compacts the
+// accepted candidates into shared memory (ballot + prefix) and writes each at
+// its rank in the canonical order (sender's global tag, image), which the
+// lanes compute by counting smaller keys; a row longer than kSrCap is written
+// unsorted and sorted by one lane (insertion sort in global memory).
+constexpr int kSrWarps = 8;
+constexpr int kSrCap = 256;
+template <bool kFill>
+__global__ void __launch_bounds__(kSrWarps * 32) k_sr_warp(
+    int n, int row0, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
+    const int *__restrict__ cell_start, const int *__restrict__ cell_count, const int *__restrict__ cell_atoms,
+    const int *__restrict__ image_of, const int *__restrict__ image_start, double rc2, int reach,
+    const int *__restrict__ tag, int *__restrict__ deg, const int *__restrict__ row_start, int *__restrict__ nbr,
+    int *__restrict__ img) {
+  __shared__ long long skey[kFill ? kSrWarps : 1][kFill ? kSrCap : 1];
+  __shared__ int sj[kFill ? kSrWarps : 1][kFill ? kSrCap : 1];
+  const int wl = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kSrWarps + wl;
   if (r >= n) return;
   const int i = row0 + r;
+  const double xi = xw[3 * i], yi = xw[3 * i + 1], zi = xw[3 * i + 2];
+  const int ti = tag ? tag[i] : i;
+  const int rb = kFill ? row_start[r] : 0;
   int count = 0;
-  for_each_candidate(i, xw, g, cell, cell_start, cell_count, cell_atoms, image_of, image_start, reach, tag,
-                     [&](int, int, double dx, double dy, double dz) {
-                       const double r2 = dx * dx + dy * dy + dz * dz;
-                       if (r2 > 0.0 && r2 < rc2) ++count;
-                     });
-  deg[r] = count;
-}
-
-__global__ void k_sr_fill(int n, int row0, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
-                          const int *__restrict__ cell_start, const int *__restrict__ cell_count,
-                          const int *__restrict__ cell_atoms, const int *__restrict__ image_of,
-                          const int *__restrict__ image_start, double rc2, int reach, const int *__restrict__ tag,
-                          const int *__restrict__ row_start, int *__restrict__ nbr, int *__restrict__ img) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= n) return;
-  const int i = row0 + r;
-  const int base = row_start[r];
-  int count = 0;
-  for_each_candidate(i, xw, g, cell, cell_start, cell_count, cell_atoms, image_of, image_start, reach, tag,
-                     [&](int j, int code, double dx, double dy, double dz) {
-                       const double r2 = dx * dx + dy * dy + dz * dz;
-                       if (r2 > 0.0 && r2 < rc2) {
-                         nbr[base + count] = j;
-                         img[base + count] = code;
-                         ++count;
-                       }
-                     });
-  // canonical order: (sender's global tag, image), independent of the local layout
+  // candidates cell_atoms[s..e) (or atoms s..e when not cell ordered) with the
+  // periodic shift (sx, sy, sz)
+  auto run = [&](int s, int e, bool cell_ordered, bool periodic, int sx, int sy, int sz) {
+    const int code = periodic ? pack_image(sx, sy, sz) : kZeroImage;
+    const double shx = sx * g.len[0], shy = sy * g.len[1], shz = sz * g.len[2];
+    const bool positive = sz > 0 || (sz == 0 && (sy > 0 || (sy == 0 && sx > 0)));
+    for (int base = s; base < e; base += 32) {
+      const int k = base + lane;
+      bool valid = false;
+      int j = 0, tj = 0;
+      if (k < e) {
+        j = cell_ordered ? cell_atoms[k] : k;
+        tj = tag ? tag[j] : j;
+        double dx, dy, dz;
+        if (!periodic) {
+          dx = xi - xw[3 * j];
+          dy = yi - xw[3 * j + 1];
+          dz = zi - xw[3 * j + 2];
+        } else if (ti < tj || (ti == tj && positive)) {
+          dx = xi - (xw[3 * j] + shx);
+          dy = yi - (xw[3 * j + 1] + shy);
+          dz = zi - (xw[3 * j + 2] + shz);
+        } else {  // the other endpoint's expression, negated
+          dx = -(xw[3 * j] - (xi - shx));
+          dy = -(xw[3 * j + 1] - (yi - shy));
+          dz = -(xw[3 * j + 2] - (zi - shz));
+        }
+        const double r2 = dx * dx + dy * dy + dz * dz;
+        valid = r2 > 0.0 && r2 < rc2;
+      }
+      const unsigned mask = __ballot_sync(0xffffffffu, valid);
+      if (kFill && valid) {
+        const int slot = count + __popc(mask & ((1u << lane) - 1u));
+        if (slot < kSrCap) {
+          skey[wl][slot] = (long long)tj * 4294967296LL + code;
+          sj[wl][slot] = j;
+        } else {
+          nbr[rb + slot] = j;
+          img[rb + slot] = code;
+        }
+      }
+      count += __popc(mask);
+    }
+  };
+  if (!g.periodic && !g.open_cells) {
+    const int im = image_of[i];
+    run(image_start[im], image_start[im + 1], false, false, 0, 0, 0);
+  } else if (g.open_cells) {  // one open system on a clamped, non-wrapping grid
+    const int nx = g.ncell[0], ny = g.ncell[1], nz = g.ncell[2];
+    const int c = cell[i];
+    const int cx = c % nx, cy = (c / nx) % ny, cz = c / (nx * ny);
+    for (int wz = max(0, cz - reach); wz <= min(nz - 1, cz + reach); ++wz)
+      for (int wy = max(0, cy - reach); wy <= min(ny - 1, cy + reach); ++wy) {
+        const int row = (wz * ny + wy) * nx;
+        const int lo = max(0, cx - reach), hi = min(nx - 1, cx + reach);
+        run(cell_start[row + lo], cell_start[row + hi] + cell_count[row + hi], true, false, 0, 0, 0);
+      }
+  } else {
+    const int nx = g.ncell[0], ny = g.ncell[1], nz = g.ncell[2];
+    const int c = cell[i];
+    const int cx = c % nx, cy = (c / nx) % ny, cz = c / (nx * ny);
+    for (int oz = -reach; oz <= reach; ++oz) {
+      int wz = cz + oz, sz = 0;
+      while (wz < 0) { wz += nz; --sz; }
+      while (wz >= nz) { wz -= nz; ++sz; }
+      for (int oy = -reach; oy <= reach; ++oy) {
+        int wy = cy + oy, sy = 0;
+        while (wy < 0) { wy += ny; --sy; }
+        while (wy >= ny) { wy -= ny; ++sy; }
+        const int row = (wz * ny + wy) * nx;
+        // x runs of constant periodic shift: cells [lo, hi] of one row are contiguous
+        const int sx_lo = (cx - reach >= 0) ? 0 : -((reach - cx + nx - 1) / nx);
+        const int sx_hi = (cx + reach) / nx;
+        for (int sx = sx_lo; sx <= sx_hi; ++sx) {
+          const int lo = max(0, cx - reach - sx * nx), hi = min(nx - 1, cx + reach - sx * nx);
+          if (lo > hi) continue;
+          run(cell_start[row + lo], cell_start[row + hi] + cell_count[row + hi], true, true, sx, sy, sz);
+        }
+      }
+    }
+  }
+  if (!kFill) {
+    if (lane == 0) deg[r] = count;
+    return;
+  }
+  __syncwarp();
+  if (count <= kSrCap) {
+    for (int e = lane; e < count; e += 32) {
+      const long long key = skey[wl][e];
+      int rank = 0;
+      for (int t = 0; t < count; ++t) rank += skey[wl][t] < key ? 1 : 0;
+      nbr[rb + rank] = sj[wl][e];
+      img[rb + rank] = int(key & 0xffffffffLL);
+    }
+    return;
+  }
+  // long row: the first kSrCap entries join the others in global memory, then
+  // one lane sorts the row in the canonical order
+  for (int e = lane; e < kSrCap; e += 32) {
+    nbr[rb + e] = sj[wl][e];
+    img[rb + e] = int(skey[wl][e] & 0xffffffffLL);
+  }
+  __syncwarp();
+  if (lane != 0) return;
   for (int a = 1; a < count; ++a) {
-    const int vj = nbr[base + a], vc = img[base + a];
+    const int vj = nbr[rb + a], vc = img[rb + a];
     const int vt = tag ? tag[vj] : vj;
     int b = a - 1;
     while (b >= 0) {
-      const int bt = tag ? tag[nbr[base + b]] : nbr[base + b];
-      if (!(bt > vt || (bt == vt && img[base + b] > vc))) break;
-      nbr[base + b + 1] = nbr[base + b];
-      img[base + b + 1] = img[base + b];
+      const int bt = tag ? tag[nbr[rb + b]] : nbr[rb + b];
+      if (!(bt > vt || (bt == vt && img[rb + b] > vc))) break;
+      nbr[rb + b + 1] = nbr[rb + b];
+      img[rb + b + 1] = img[rb + b];
       --b;
     }
-    nbr[base + b + 1] = vj;
-    img[base + b + 1] = vc;
+    nbr[rb + b + 1] = vj;
+    img[rb + b + 1] = vc;
   }
 }
 
@@ -296,20 +395,24 @@ int sr_reach(const CellGrid &g, double rc) {
 void count_sr(NeighborState &nb, double rc, cudaStream_t s) {
   const int reach = sr_reach(nb.grid, rc);
   const int n = nb.n_own;
-  k_sr_count<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count,
-                                              nb.cell_atoms, nb.image_of, nb.image_start, rc * rc, reach, nb.tag,
-                                              nb.deg);
-  SO3_LAUNCH("sr_count");
+  if (n > 0) {
+    k_sr_warp<false><<<(n + kSrWarps - 1) / kSrWarps, kSrWarps * 32, 0, s>>>(
+        n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count, nb.cell_atoms, nb.image_of,
+        nb.image_start, rc * rc, reach, nb.tag, nb.deg, nullptr, nullptr, nullptr);
+    SO3_LAUNCH("sr_count");
+  }
   exclusive_scan(nb.deg, nb.row_start, n, nb.row_start + n, nb.scan_scratch, s);
 }
 
 void fill_sr(NeighborState &nb, double rc, int E, cudaStream_t s) {
   const int reach = sr_reach(nb.grid, rc);
   const int n = nb.n_own;
-  k_sr_fill<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count,
-                                             nb.cell_atoms, nb.image_of, nb.image_start, rc * rc, reach, nb.tag,
-                                             nb.row_start, nb.nbr, nb.img);
-  SO3_LAUNCH("sr_fill");
+  if (n > 0) {
+    k_sr_warp<true><<<(n + kSrWarps - 1) / kSrWarps, kSrWarps * 32, 0, s>>>(
+        n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start, nb.cell_count, nb.cell_atoms, nb.image_of,
+        nb.image_start, rc * rc, reach, nb.tag, nullptr, nb.row_start, nb.nbr, nb.img);
+    SO3_LAUNCH("sr_fill");
+  }
   k_edge_primary<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.img, nb.tag, nb.primary,
                                                   nb.rev, nb.error_flag);
   SO3_LAUNCH("edge_primary");
