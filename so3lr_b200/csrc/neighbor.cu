@@ -302,11 +302,12 @@ __global__ void __launch_bounds__(kSrWarps * 32) k_sr_warp(
 __global__ void k_edge_primary(int n, int row0, const int *__restrict__ row_start, const int *__restrict__ nbr,
                                const int *__restrict__ img, const int *__restrict__ tag, int *__restrict__ primary,
                                int *__restrict__ rev, int *__restrict__ error_flag) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;  // one warp per owned atom, a lane per edge
+  const int lane = threadIdx.x & 31;
   if (r >= n) return;
   const int i = row0 + r;
   const int ti = tag ? tag[i] : i;
-  for (int e = row_start[r]; e < row_start[r + 1]; ++e) {
+  for (int e = row_start[r] + lane; e < row_start[r + 1]; e += 32) {
     const int j = nbr[e], code = img[e];
     const int tj = tag ? tag[j] : j;
     const bool canonical = ti < tj || (ti == tj && code > kZeroImage);
@@ -337,11 +338,12 @@ __global__ void k_pair_fill(int n, int row0, const int *__restrict__ row_start, 
                             const int *__restrict__ pair_scan, int *__restrict__ edge_pair, int *__restrict__ pair_a,
                             int *__restrict__ pair_b, int *__restrict__ pair_img, int *__restrict__ pair_edge,
                             int *__restrict__ pair_canon) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;  // one warp per owned atom, a lane per edge
+  const int lane = threadIdx.x & 31;
   if (r >= n) return;
   const int i = row0 + r;
   const int ti = tag ? tag[i] : i;
-  for (int e = row_start[r]; e < row_start[r + 1]; ++e) {
+  for (int e = row_start[r] + lane; e < row_start[r + 1]; e += 32) {
     if (!primary[e]) continue;
     const int p = pair_scan[e];
     const int j = nbr[e];
@@ -413,15 +415,15 @@ void fill_sr(NeighborState &nb, double rc, int E, cudaStream_t s) {
         nb.image_start, rc * rc, reach, nb.tag, nullptr, nb.row_start, nb.nbr, nb.img);
     SO3_LAUNCH("sr_fill");
   }
-  k_edge_primary<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.img, nb.tag, nb.primary,
-                                                  nb.rev, nb.error_flag);
+  k_edge_primary<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.img, nb.tag,
+                                                       nb.primary, nb.rev, nb.error_flag);
   SO3_LAUNCH("edge_primary");
   exclusive_scan(nb.primary, nb.pair_scan, E, nb.scan_total, nb.scan_scratch, s);
 }
 
 void fill_pairs(NeighborState &nb, int E, cudaStream_t s) {
   const int n = nb.n_own;
-  k_pair_fill<<<(n + 127) / 128, 128, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.img, nb.tag, nb.primary,
+  k_pair_fill<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, nb.row0, nb.row_start, nb.nbr, nb.img, nb.tag, nb.primary,
                                                nb.pair_scan, nb.edge_pair, nb.pair_a, nb.pair_b, nb.pair_img,
                                                nb.pair_edge, nb.pair_canon);
   SO3_LAUNCH("pair_fill");
