@@ -49,7 +49,9 @@ __global__ void k_pair_geometry(int P, const int *__restrict__ pa, const int *__
   const double ux = vx * inv, uy = vy * inv, uz = vz * inv;
   double y[kSH];
   real_sh(ux, uy, uz, y);
-  for (int m = 0; m < kSH; ++m) sh[(size_t)p * kSH + m] = y[m];
+#pragma unroll
+  for (int m = 0; m < kSH; m += 2)  // 16-byte stores (a pair's row is 192 bytes)
+    *reinterpret_cast<double2 *>(sh + (size_t)p * kSH + m) = make_double2(y[m], y[m + 1]);
   // PhysNet cutoff 1 - 10x^3 + 15x^4 - 6x^5 and its derivative
   double phi = 0.0, dphi = 0.0;
   if (r < rc) {
@@ -106,9 +108,11 @@ __global__ void k_pair_geometry(int P, const int *__restrict__ pa, const int *__
     e_dir = 0.5 * sw * xx * yy;
     de_pair = 2.0 * (0.5 * (dsw * xx * yy + sw * dxx * yy + sw * xx * dyy));
   }
-  double *gp = geo + (size_t)p * kGeo;
-  gp[0] = r; gp[1] = ux; gp[2] = uy; gp[3] = uz;
-  gp[4] = phi; gp[5] = dphi; gp[6] = e_dir; gp[7] = de_pair;
+  double2 *gp = reinterpret_cast<double2 *>(geo + (size_t)p * kGeo);
+  gp[0] = make_double2(r, ux);
+  gp[1] = make_double2(uy, uz);
+  gp[2] = make_double2(phi, dphi);
+  gp[3] = make_double2(e_dir, de_pair);
   gv[3 * p] = de_pair * ux;
   gv[3 * p + 1] = de_pair * uy;
   gv[3 * p + 2] = de_pair * uz;

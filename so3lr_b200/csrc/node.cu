@@ -576,15 +576,21 @@ __device__ inline double ratio_head(const double *__restrict__ hh, const double 
                                     const double *__restrict__ vshift, double sqrt_k, int zz, int lane,
                                     double *__restrict__ k_out) {
   double k0 = b2[2 * lane], k1 = b2[2 * lane + 1];
-  double s0 = 0.0, s1 = 0.0;
-  for (int j = 0; j < kHirsh; ++j) {
-    const double hv = hh[j];
-    const double2 w = *reinterpret_cast<const double2 *>(w2t + j * kHirsh + 2 * lane);  // coalesced
-    s0 += hv * w.x;
-    s1 += hv * w.y;
+  // four independent partial sums per output (the 64-term dot product as four
+  // interleaved chains), added in a fixed order
+  double s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0};
+#pragma unroll 4
+  for (int j = 0; j < kHirsh; j += 4) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const double hv = hh[j + u];
+      const double2 w = *reinterpret_cast<const double2 *>(w2t + (j + u) * kHirsh + 2 * lane);  // coalesced
+      s0[u] += hv * w.x;
+      s1[u] += hv * w.y;
+    }
   }
-  k0 += s0;
-  k1 += s1;
+  k0 += (s0[0] + s0[1]) + (s0[2] + s0[3]);
+  k1 += (s1[0] + s1[1]) + (s1[2] + s1[3]);
   k_out[2 * lane] = k0;
   k_out[2 * lane + 1] = k1;
   double qk = qemb[zz * kHirsh + 2 * lane] * k0 + qemb[zz * kHirsh + 2 * lane + 1] * k1;
@@ -651,9 +657,13 @@ __device__ inline void ratio_head_seed(const double *__restrict__ hk, const doub
 #pragma unroll
   for (int jj = 0; jj < 2; ++jj) {
     const int j = 2 * lane + jj;
-    double s = 0.0;
-    for (int k = 0; k < kHirsh; ++k) s += gk[k] * w2[k * kHirsh + j];
-    g[j] = s * silu_prime(pre[j]);
+    double s[4] = {0, 0, 0, 0};  // four interleaved chains, added in a fixed order
+#pragma unroll 4
+    for (int k = 0; k < kHirsh; k += 4) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) s[u] += gk[k + u] * w2[(k + u) * kHirsh + j];
+    }
+    g[j] = ((s[0] + s[1]) + (s[2] + s[3])) * silu_prime(pre[j]);
   }
 }
 
