@@ -79,6 +79,27 @@ def test_gpu_matches_oracle_periodic_water(nmol, seed, gpu_model, oracle_model):
     assert np.abs(g["e_lr"] - o["lr_energy"]).max() <= 1e-10
 
 
+@pytest.mark.parametrize("scale", [0.55, 0.5])
+def test_gpu_dense_rows_match_oracle(scale, gpu_model, oracle_model):
+    """A 27-molecule box compressed to 0.55 and 0.5 of its size (4.7-5.1 A,
+    below twice the short-range cutoff): 230-310 short-range neighbours per
+    atom, so the neighbour rows fill the builder's shared-memory buffer (256
+    entries) and overflow it (rows sorted in global memory instead). Float64
+    bar relative to the magnitudes of this unphysical, strongly repulsive
+    system: energy <= 1e-9 (1 + |E|/N) eV/atom, forces <= 1e-9 (1 + max|F|)."""
+    from oracle.so3lr_oracle import System, evaluate
+    from so3lr_b200.systems import water_box
+    w = water_box(27, seed=5)
+    s = System(pos=w.pos * scale, z=w.z, cell=w.cell * scale)
+    g = _gpu(gpu_model, s)
+    o = evaluate(oracle_model, s)
+    n = len(w.z)
+    assert abs(g["energy"] - o["energy"]) / n <= 1e-9 * (1 + abs(o["energy"]) / n)
+    fmax = np.abs(o["forces"]).max()
+    assert np.abs(g["forces"] - o["forces"]).max() <= 1e-9 * (1 + fmax)
+    assert np.abs(g["charges"] - o["partial_charges"]).max() <= 1e-10
+
+
 @pytest.mark.parametrize("q, m", [(-1, 1), (1, 2), (0, 3), (2, 1)])
 def test_gpu_charged_open_shell_periodic(q, m, gpu_model, oracle_model):
     """Charge/spin embedding and charge conservation in a periodic box."""
