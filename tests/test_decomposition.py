@@ -226,20 +226,26 @@ def test_multi_gpu_local_frames_bit_identical(world, gpu_model):
 
 
 @pytest.mark.gpu
-def test_multi_gpu_bit_identical_with_optional_operators(tmp_path):
-    """A model with RMSNorm, query/key normalisation (also on the halo rows each
-    GPU projects itself), residual scalars, NLH repulsion and a C6 ratio head
-    (its ratios all-gathered like the Hirshfeld ratios): 2 GPUs give the
-    single-GPU bits."""
+@pytest.mark.parametrize("kind", ["optional_operators", "l_size"])
+def test_multi_gpu_bit_identical_other_models(kind, tmp_path):
+    """2 GPUs give the single-GPU bits for (a) a model with RMSNorm,
+    query/key normalisation (also on the halo rows each GPU projects itself),
+    residual scalars, NLH repulsion and a C6 ratio head (its ratios
+    all-gathered like the Hirshfeld ratios), and (b) the F = 256 width with
+    duplicated degrees (the halo rows carry 256 features and 48 equivariant
+    channels)."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    from model_variants import make_variant
+    from model_variants import make_l_variant, make_variant
     from so3lr_b200 import So3lrB200
     from so3lr_b200.systems import water_box
-    path = make_variant(MODEL, tmp_path / "all.so3lr", rms_norm=True, qk_norm=True,
-                        residual_scalars=([0.9, 1.1, 0.8], [0.1, -0.2, 0.3]), nlh_capacity=9, hirshfeld_keys=1,
-                        c6_keys=1, seed=2, attention_norm_factor=20.0)
+    if kind == "l_size":
+        path = make_l_variant(MODEL, tmp_path / "l.so3lr", seed=7)
+    else:
+        path = make_variant(MODEL, tmp_path / "all.so3lr", rms_norm=True, qk_norm=True,
+                            residual_scalars=([0.9, 1.1, 0.8], [0.1, -0.2, 0.3]), nlh_capacity=9,
+                            hirshfeld_keys=1, c6_keys=1, seed=2, attention_norm_factor=20.0)
     nmol, seed = 1000, 19
     w = water_box(nmol, seed=seed)
     single = So3lrB200(path, 0)
