@@ -107,68 +107,89 @@ __global__ void __launch_bounds__(256) k_attention_forward(int n, int row0, cons
   }
   const T inv_norm = T(1.0 / norm);  // one division per atom instead of two per edge
   const int e0 = row_start[r], e1 = row_start[r + 1];
-  int b_nx = 0, code_nx = 0;  // indices of the next edge, loaded one iteration ahead
-  if (e0 < e1) {
-    b_nx = nbr[e0];
-    code_nx = edge_pair[e0];
-  }
-  for (int e = e0; e < e1; ++e) {
-    const int b = b_nx;
-    const int code = code_nx;
-    if (e + 1 < e1) {
-      b_nx = nbr[e + 1];
-      code_nx = edge_pair[e + 1];
-      // pull the next edge's rows into L1 while this one is processed: the k, v
-      // and k_ev lines of each head (double: lines 2-5 and 8-9 of the head's ten
-      // 128-byte lines; float: lines 1, 2 and 4 of five), both filters and the
-      // harmonics (two 96-byte halves)
-      const int p_nx = code_nx >= 0 ? code_nx : ~code_nx;
-      constexpr int kLq = sizeof(T) == 8 ? 6 : 3;  // lines per head
-      constexpr int kQl = kLq * kHeads, kFl = kF * int(sizeof(T)) / 128;
-      for (int c = lane; c < kQl + 2 * kFl + 2; c += 32) {
-        const char *addr;
-        if (c < kQl) {
-          const int j = c % kLq;
-          const int line = sizeof(T) == 8 ? (c / 6) * 10 + (j < 4 ? 2 + j : 4 + j) : (c / 3) * 5 + (j < 2 ? 1 + j : 4);
-          addr = reinterpret_cast<const char *>(qkv + (size_t)b_nx * kQKV) + 128 * line;
-        } else if (c < kQl + kFl) {
-          addr = reinterpret_cast<const char *>(f_inv + (size_t)p_nx * kF) + 128 * (c - kQl);
-        } else if (c < kQl + 2 * kFl) {
-          addr = reinterpret_cast<const char *>(f_ev + (size_t)p_nx * kF) + 128 * (c - kQl - kFl);
-        } else {
-          addr = reinterpret_cast<const char *>(sh + (size_t)p_nx * kSH) + 96 * (c - kQl - 2 * kFl);
-        }
-        asm volatile("prefetch.global.L1 [%0];\n" ::"l"(addr));
+  // pull an edge's rows into L1 ahead of its use: the k, v and k_ev lines of
+  // each head (double: lines 2-5 and 8-9 of the head's ten 128-byte lines;
+  // float: lines 1, 2 and 4 of five), both filters and the harmonics (two
+  // 96-byte halves)
+  auto prefetch_edge = [&](int e) {
+    const int bb = nbr[e], cc = edge_pair[e];
+    const int pp = cc >= 0 ? cc : ~cc;
+    constexpr int kLq = sizeof(T) == 8 ? 6 : 3;  // lines per head
+    constexpr int kQl = kLq * kHeads, kFl = kF * int(sizeof(T)) / 128;
+    for (int c = lane; c < kQl + 2 * kFl + 2; c += 32) {
+      const char *addr;
+      if (c < kQl) {
+        const int j = c % kLq;
+        const int line = sizeof(T) == 8 ? (c / 6) * 10 + (j < 4 ? 2 + j : 4 + j) : (c / 3) * 5 + (j < 2 ? 1 + j : 4);
+        addr = reinterpret_cast<const char *>(qkv + (size_t)bb * kQKV) + 128 * line;
+      } else if (c < kQl + kFl) {
+        addr = reinterpret_cast<const char *>(f_inv + (size_t)pp * kF) + 128 * (c - kQl);
+      } else if (c < kQl + 2 * kFl) {
+        addr = reinterpret_cast<const char *>(f_ev + (size_t)pp * kF) + 128 * (c - kQl - kFl);
+      } else {
+        addr = reinterpret_cast<const char *>(sh + (size_t)pp * kSH) + 96 * (c - kQl - 2 * kFl);
       }
+      asm volatile("prefetch.global.L1 [%0];\n" ::"l"(addr));
     }
+  };
+  // one edge's attention coefficients (alpha of both attentions, already
+  // divided by the norm) and the rows its messages need
+  struct EdgeTerms {
+    T phi, ai, ae, vb[kPL], y[kEVL];
+  };
+  auto edge_terms = [&](int e, EdgeTerms &t) {
+    const int bb = nbr[e], code = edge_pair[e];
     const int p = code >= 0 ? code : ~code;
-    const T phi = T(geo[(size_t)p * kGeo + 4]);
-    T kb[kPL], vb[kPL], keb[kPL], fi[kPL], fe[kPL];
-    load4(qkv + (size_t)b * kQKV + head_off + 1 * 32, kb);
-    load4(qkv + (size_t)b * kQKV + head_off + 2 * 32, vb);
-    load4(qkv + (size_t)b * kQKV + head_off + 4 * 32, keb);
+    t.phi = T(geo[(size_t)p * kGeo + 4]);
+    T kb[kPL], keb[kPL], fi[kPL], fe[kPL];
+    load4(qkv + (size_t)bb * kQKV + head_off + 1 * 32, kb);
+    load4(qkv + (size_t)bb * kQKV + head_off + 2 * 32, t.vb);
+    load4(qkv + (size_t)bb * kQKV + head_off + 4 * 32, keb);
     load4(f_inv + (size_t)p * kF + lane * kPL, fi);
     load4(f_ev + (size_t)p * kF + lane * kPL, fe);
+#pragma unroll
+    for (int j = 0; j < kEVL; ++j) {
+      T y = lane + 32 * j < kEV ? T(sh[(size_t)p * kSH + my_sh[j]]) : T(0);
+      if (code < 0) y *= my_par[j];
+      t.y[j] = y;
+    }
     T ai = T(0), ae = T(0);
 #pragma unroll
     for (int j = 0; j < kPL; ++j) {
       ai += qa[j] * kb[j] * fi[j];
       ae += qea[j] * keb[j] * fe[j];
     }
-    ai = head_sum(ai) * inv_norm;
-    ae = head_sum(ae) * inv_norm;
-    const T wi = phi * ai;
+    t.ai = ai;
+    t.ae = ae;
+  };
+  // the messages of one edge, added in edge order
+  auto accumulate = [&](const EdgeTerms &t, T ai, T ae) {
+    const T wi = t.phi * ai;
 #pragma unroll
-    for (int j = 0; j < kPL; ++j) acc[j] += wi * vb[j];
+    for (int j = 0; j < kPL; ++j) acc[j] += wi * t.vb[j];
 #pragma unroll
     for (int j = 0; j < kEVL; ++j) {
       const T ae_m = __shfl_sync(0xffffffffu, ae, my_deg[j] * kLPH);
-      if (lane + 32 * j < kEV) {
-        T y = T(sh[(size_t)p * kSH + my_sh[j]]);
-        if (code < 0) y *= my_par[j];
-        acc_ev[j] += phi * ae_m * y;
-      }
+      if (lane + 32 * j < kEV) acc_ev[j] += t.phi * ae_m * t.y[j];
     }
+  };
+  // two edges per iteration: their loads and head reductions interleave
+  int e = e0;
+  for (; e + 1 < e1; e += 2) {
+    if (e + 2 < e1) prefetch_edge(e + 2);
+    if (e + 3 < e1) prefetch_edge(e + 3);
+    EdgeTerms t0, t1;
+    edge_terms(e, t0);
+    edge_terms(e + 1, t1);
+    const T ai0 = head_sum(t0.ai) * inv_norm, ai1 = head_sum(t1.ai) * inv_norm;
+    const T ae0 = head_sum(t0.ae) * inv_norm, ae1 = head_sum(t1.ae) * inv_norm;
+    accumulate(t0, ai0, ae0);
+    accumulate(t1, ai1, ae1);
+  }
+  if (e < e1) {
+    EdgeTerms t0;
+    edge_terms(e, t0);
+    accumulate(t0, head_sum(t0.ai) * inv_norm, head_sum(t0.ae) * inv_norm);
   }
   store4(d_inv + (size_t)a * kF + lane * kPL, acc);
 #pragma unroll
