@@ -132,32 +132,40 @@ void launch_pair_geometry(int P, const NeighborState &nb, const int *z, ZblDev z
 // Smooth switch of physical_long_range.cpp: v = s_l / (s_l + s_r + 1e-12) with
 // s_l = exp(-1/left), s_r = exp(-1/right), c = (r - cuton) / width, left = 1 - c,
 // right = c (each clamped below at 1e-12 inside the exponent), and its derivative
-// dv/dr. The divisions of the textbook form are folded into two reciprocals.
-__device__ inline void smooth_switch(double r, double cuton, double cutoff, double inv_width, double &v,
-                                     double &dv) {
+// dv/dr, for both switches of a pair (electrostatic and dispersion: the same
+// cutoff, different cutons). The divisions of the textbook form are folded into
+// reciprocals shared by the two switches: 1/(sl sr) of both from one division,
+// 1/den of both from another.
+__device__ inline void smooth_switch2(double r, double cutoff, double cuton_e, double inv_we, double cuton_d,
+                                      double inv_wd, double &ve, double &dve, double &vd, double &dvd) {
   if (r >= cutoff) {
-    v = 0.0;
-    dv = 0.0;
+    ve = dve = vd = dvd = 0.0;
     return;
   }
-  const double c = (r - cuton) * inv_width;
-  const double left = 1.0 - c, right = c;
-  const double sl = left > 1.0e-12 ? left : 1.0e-12, sr = right > 1.0e-12 ? right : 1.0e-12;
-  const double inv_lr = 1.0 / (sl * sr);
-  const double isl = sr * inv_lr, isr = sl * inv_lr;  // 1/sl, 1/sr
-  const double sig_l = left > 0.0 ? exp_tang(-isl) : 0.0;
-  const double sig_r = right > 0.0 ? exp_tang(-isr) : 0.0;
-  const double den = sig_l + sig_r + 1.0e-12;
-  const double iden = 1.0 / den;
-  v = sig_l * iden;
-  const double dl = left > 0.0 ? -sig_l * isl * isl : 0.0;
-  const double dr = right > 0.0 ? sig_r * isr * isr : 0.0;
-  // (dl den - s_l (dl + dr)) / den^2 / width
-  dv = (dl - v * (dl + dr)) * iden * inv_width;
+  const double ce = (r - cuton_e) * inv_we, cd = (r - cuton_d) * inv_wd;
+  const double le = 1.0 - ce, re = ce, ld = 1.0 - cd, rd = cd;
+  const double sle = le > 1.0e-12 ? le : 1.0e-12, sre = re > 1.0e-12 ? re : 1.0e-12;
+  const double sld = ld > 1.0e-12 ? ld : 1.0e-12, srd = rd > 1.0e-12 ? rd : 1.0e-12;
+  const double pe = sle * sre, pd = sld * srd;  // each >= ~1e-12: the product stays normal
+  const double ip = 1.0 / (pe * pd);
+  const double inv_e = pd * ip, inv_d = pe * ip;
+  const double isle = sre * inv_e, isre = sle * inv_e, isld = srd * inv_d, isrd = sld * inv_d;
+  const double sig_le = le > 0.0 ? exp_tang(-isle) : 0.0, sig_re = re > 0.0 ? exp_tang(-isre) : 0.0;
+  const double sig_ld = ld > 0.0 ? exp_tang(-isld) : 0.0, sig_rd = rd > 0.0 ? exp_tang(-isrd) : 0.0;
+  const double dene = sig_le + sig_re + 1.0e-12, dend = sig_ld + sig_rd + 1.0e-12;
+  const double iq = 1.0 / (dene * dend);
+  const double idene = dend * iq, idend = dene * iq;
+  ve = sig_le * idene;
+  vd = sig_ld * idend;
+  const double dle = le > 0.0 ? -sig_le * isle * isle : 0.0, dre = re > 0.0 ? sig_re * isre * isre : 0.0;
+  const double dld = ld > 0.0 ? -sig_ld * isld * isld : 0.0, drd = rd > 0.0 ? sig_rd * isrd * isrd : 0.0;
+  dve = (dle - ve * (dle + dre)) * idene * inv_we;
+  dvd = (dld - vd * (dld + drd)) * idend * inv_wd;
 }
 
 struct LrPair {
-  double e_elec, e_disp, dq, dh, dc, radial;
+  double e_elec, e_disp, dq, dh, dc;
+  double radial;  // float64 pair term: dE/dr divided by r; float32 pair term: dE/dr
 };
 
 // per-launch constants of the pair term, computed once per thread
@@ -189,8 +197,8 @@ __device__ inline LrPair lr_pair_tab(const LrDev &p, const LrConst &k, double r,
   constexpr double inv_sqrt_pi = 0.56418958354775628695;
   constexpr double inv7 = 1.0 / 7.0;
   LrPair o{0, 0, 0, 0, 0, 0};
-  double esw, desw;
-  smooth_switch(r, p.elec_cuton, p.cutoff, k.inv_elec_width, esw, desw);
+  double esw, desw, dsw, ddsw;
+  smooth_switch2(r, p.cutoff, p.elec_cuton, k.inv_elec_width, p.disp_cuton, k.inv_disp_width, esw, desw, dsw, ddsw);
   const double inv_r = 1.0 / r;
   const double ratio = r * k.inv_sigma;
   const double erf_t = erf(ratio);
@@ -212,7 +220,8 @@ __device__ inline LrPair lr_pair_tab(const LrDev &p, const LrConst &k, double r,
     const double num = 2.0 * c6i * c6j * aj * ai;
     const double den = ai * ai * c6j + aj * aj * c6i;
     if (alpha > 0.0 && den > 1.0e-30) {
-      const double iden = 1.0 / den;
+      const double iad = 1.0 / (alpha * den);  // 1/(alpha den): both positive, product far inside the normal range
+      const double iden = alpha * iad;
       const double c6 = num * iden;
       double dc6_dhi, dc6_dsi = 0.0;
       if (!kSepC6) {  // h_i drives both alpha_i and C6_i
@@ -228,7 +237,7 @@ __device__ inline LrPair lr_pair_tab(const LrDev &p, const LrConst &k, double r,
         const double dd_dsi = aj * aj * ci0;
         dc6_dsi = (dn_dsi * den - num * dd_dsi) * (iden * iden);
       }
-      const double ialpha7 = inv7 / alpha;  // 1 / (7 alpha)
+      const double ialpha7 = inv7 * (den * iad);  // 1 / (7 alpha)
       const double a7 = exp_tang(log(alpha) * inv7);
       const double rv = p.fine_factor * a7;
       constexpr double b0 = -0.00433008, b1 = 0.24428889, b2 = 0.04125273, b3 = -0.00078893;
@@ -247,7 +256,10 @@ __device__ inline LrPair lr_pair_tab(const LrDev &p, const LrConst &k, double r,
       const double r2 = ra * ra, r4 = r2 * r2, r6 = r4 * r2, r8 = r4 * r4, r10 = r8 * r2;
       const double p2 = damp * damp, p4 = p2 * p2, p6 = p4 * p2, p8 = p4 * p4, p10 = p8 * p2;
       const double d6 = r6 + p6, d8 = r8 + p8, d10 = r10 + p10;
-      const double id6 = 1.0 / d6, id8 = 1.0 / d8, id10 = 1.0 / d10;
+      // one division for the three denominators r^n + damp^n (n = 6, 8, 10):
+      // their product is at least damp^24 and overflows only beyond r ~ 1e12 bohr
+      const double id = 1.0 / (d6 * d8 * d10);
+      const double id6 = d8 * d10 * id, id8 = d6 * d10 * id, id10 = d6 * d8 * id;
       const double qdo = -c6 * id6 - c8 * id8 - c10 * id10;
       const double rad_au =
           (6.0 * c6 * r4 * id6 * id6 + 8.0 * c8 * r6 * id8 * id8 + 10.0 * c10 * r8 * id10 * id10) * ra;
@@ -260,15 +272,13 @@ __device__ inline LrPair lr_pair_tab(const LrDev &p, const LrConst &k, double r,
                              c10 * dd10 * id10 * id10;
       const double dpot_dc6 = -id6 - 5.0 * igam * id8 - 245.0 * 0.125 * (igam * igam) * id10;
       const double dpot_dhi = dpot_dc6 * dc6_dhi + dpot_da * 0.5 * ai0;
-      double dsw, ddsw;
-      smooth_switch(r, p.disp_cuton, p.cutoff, k.inv_disp_width, dsw, ddsw);
       o.e_disp = p.full_scale * p.hartree * qdo * dsw;
       drad = p.full_scale * p.hartree * (rad_au * dsw * k.inv_bohr + qdo * ddsw);
       o.dh = p.full_scale * p.hartree * dsw * dpot_dhi;
       if (kSepC6) o.dc = p.full_scale * p.hartree * dsw * dpot_dc6 * dc6_dsi;
     }
   }
-  o.radial = erad + drad;
+  o.radial = (erad + drad) * inv_r;
   return o;
 }
 
@@ -434,11 +444,15 @@ __global__ void k_lr_gather(int n, int cell_ordered, const int *__restrict__ cel
   par4[k] = make_double4(h[j], known ? aref[zj] : -1.0, known ? cref[zj] : 0.0, c6r ? c6r[j] : 0.0);
 }
 
-// One warp per atom. Lanes test 32 consecutive candidates of a contiguous
-// stencil range at a time; the ones inside the cutoff are compacted (ballot +
-// prefix) into a per-warp queue in shared memory, and the pair math runs only
-// on full batches of 32 queued pairs. Every lane accumulates its queue slots in
-// a fixed order, so the result is deterministic.
+// One warp per atom. The candidate ranges of the atom's cell stencil (x runs of
+// cells, contiguous in the cell-ordered arrays) are listed lane-parallel, 32
+// stencil rows at a time, into a per-warp table in shared memory; the lanes then
+// walk the concatenation of those ranges 32 candidates at a time, across range
+// boundaries. Candidates inside the cutoff are compacted (ballot + prefix) into
+// a per-warp queue (candidate index and periodic shift), and the pair math runs
+// only on full batches of 32 queued pairs. The queue receives the pairs in the
+// stencil's serial order (rows by z then y, runs by x shift) and every lane
+// accumulates its queue slots in a fixed order, so the result is deterministic.
 constexpr int kLrWarps = 8;
 constexpr int kLrMaxReach = 8;
 // per (|oy|, |oz|) of the cell stencil: the x reach of the cells that can hold
@@ -447,18 +461,26 @@ struct LrStencil {
   signed char rx[kLrMaxReach + 1][kLrMaxReach + 1];
 };
 constexpr int kLrQueue = 64;
+constexpr int kLrSegs = 64;  // candidate ranges per table fill (two per lane)
+// periodic shift (sx, sy, sz), each in [-127, 127], packed into one int
+__host__ __device__ inline int lr_shift_code(int sx, int sy, int sz) {
+  return (sx + 128) | ((sy + 128) << 8) | ((sz + 128) << 16);
+}
 template <bool kSepC6, bool kF32>
-__global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
+__global__ void __launch_bounds__(kLrWarps * 32, 2) k_long_range(
     int n, int row0, const double *__restrict__ xw, CellGrid g, const int *__restrict__ cell,
     const int *__restrict__ cell_start, const int *__restrict__ cell_count, const int *__restrict__ image_of,
-    const int *__restrict__ image_start, int reach, LrStencil st, double rc2, const double4 *__restrict__ pos4,
-    const double4 *__restrict__ par4, const int *__restrict__ z, const double *__restrict__ q,
-    const double *__restrict__ h, const double *__restrict__ c6r, const double *__restrict__ aref,
-    const double *__restrict__ cref, int table, LrDev p, double *__restrict__ e_lr, double *__restrict__ e_elec,
-    double *__restrict__ e_disp, double *__restrict__ dq, double *__restrict__ dh, double *__restrict__ dc6,
-    double *__restrict__ f_lr, double *__restrict__ w_lr) {
-  __shared__ int qk[kLrWarps][kLrQueue];
-  __shared__ double qv[kLrWarps][kLrQueue][3];
+    const int *__restrict__ image_start, int reach, int rows_per_fill, LrStencil st, double rc2,
+    const double4 *__restrict__ pos4, const double4 *__restrict__ par4, const int *__restrict__ z,
+    const double *__restrict__ q, const double *__restrict__ h, const double *__restrict__ c6r,
+    const double *__restrict__ aref, const double *__restrict__ cref, int table, LrDev p,
+    double *__restrict__ e_lr, double *__restrict__ e_elec, double *__restrict__ e_disp, double *__restrict__ dq,
+    double *__restrict__ dh, double *__restrict__ dc6, double *__restrict__ f_lr, double *__restrict__ w_lr) {
+  __shared__ int qk[kLrWarps][kLrQueue];       // queued candidate (cell-ordered index)
+  __shared__ int qs[kLrWarps][kLrQueue];       // its shift code
+  __shared__ int sg_first[kLrWarps][kLrSegs];  // range table: first candidate,
+  __shared__ int sg_pre[kLrWarps][kLrSegs + 1];  // concatenated offset,
+  __shared__ int sg_code[kLrWarps][kLrSegs];   // shift code
   const int wl = threadIdx.x >> 5;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -475,11 +497,20 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
   double acc_ee = 0, acc_ed = 0, acc_dq = 0, acc_dh = 0, acc_dc = 0, fx = 0, fy = 0, fz = 0;
   double wxx = 0, wyy = 0, wzz = 0, wxy = 0, wxz = 0, wyz = 0;
   int count = 0;  // warp-uniform queue length
+  // displacement from atom i to candidate k under the shift with this code
+  // (the same expression in the scan and in the pair evaluation: same bits)
+  auto displacement = [&](const double4 &pk, int code, double &vx, double &vy, double &vz) {
+    const int sx = (code & 255) - 128, sy = ((code >> 8) & 255) - 128, sz = ((code >> 16) & 255) - 128;
+    vx = pk.x + (sx == 0 ? 0.0 : sx * g.len[0]) - xi;
+    vy = pk.y + (sy == 0 ? 0.0 : sy * g.len[1]) - yi;
+    vz = pk.z + (sz == 0 ? 0.0 : sz * g.len[2]) - zi;
+  };
   auto evaluate = [&](int slot) {
     const int k = qk[wl][slot];
-    const double vx = qv[wl][slot][0], vy = qv[wl][slot][1], vz = qv[wl][slot][2];
-    const double r = sqrt(vx * vx + vy * vy + vz * vz);
     const double4 pj = ld4(pos4 + k), hj = ld4(par4 + k);
+    double vx, vy, vz;
+    displacement(pj, qs[wl][slot], vx, vy, vz);
+    const double r = sqrt(vx * vx + vy * vy + vz * vz);
     LrPair o;
     if constexpr (kF32)
       o = lr_pair_f32<kSepC6>(kc32, float(r), float(qi), float(pj.w), float(hi), float(hj.x), float(ai0), float(hj.y),
@@ -491,7 +522,8 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
     acc_dq += o.dq;
     acc_dh += o.dh;
     if (kSepC6) acc_dc += o.dc;
-    const double s = o.radial / r;  // one division per pair; r is the queue's own distance
+    // dE/dr / r: divided by r inside the float64 pair term, here in the float32 one
+    const double s = kF32 ? o.radial / r : o.radial;
     fx += s * vx;
     fy += s * vy;
     fz += s * vz;
@@ -502,17 +534,24 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
     wxz -= 0.5 * s * vx * vz;
     wyz -= 0.5 * s * vy * vz;
   };
-  // test the candidates [s, e) of the cell-ordered arrays, shifted by (shx, shy, shz)
-  auto scan_range = [&](int s, int e, double shx, double shy, double shz) {
-    for (int base = s; base < e; base += 32) {
-      const int k = base + lane;
+  // test every candidate of the nseg ranges in the table, in order
+  auto scan_table = [&](int nseg) {
+    const int total = sg_pre[wl][nseg];
+    int sg = 0, sg_nx = 0;  // this lane's range cursors (candidate v and v + 32)
+    for (int base = 0; base < total; base += 32) {
+      const int v = base + lane;
       bool valid = false;
-      double vx = 0, vy = 0, vz = 0;
-      if (k < e) {
-        const double4 pk = ld4(pos4 + k);
-        vx = pk.x + shx - xi;
-        vy = pk.y + shy - yi;
-        vz = pk.z + shz - zi;
+      int k = 0, code = 0;
+      if (v < total) {
+        while (sg_pre[wl][sg + 1] <= v) ++sg;
+        k = sg_first[wl][sg] + (v - sg_pre[wl][sg]);
+        code = sg_code[wl][sg];
+        if (v + 32 < total) {  // pull the next batch's candidate into L1
+          while (sg_pre[wl][sg_nx + 1] <= v + 32) ++sg_nx;
+          asm volatile("prefetch.global.L1 [%0];" ::"l"(pos4 + sg_first[wl][sg_nx] + (v + 32 - sg_pre[wl][sg_nx])));
+        }
+        double vx, vy, vz;
+        displacement(ld4(pos4 + k), code, vx, vy, vz);
         const double r2 = vx * vx + vy * vy + vz * vz;
         valid = r2 > 1.0e-24 && r2 < rc2;
       }
@@ -520,9 +559,7 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
       if (valid) {
         const int slot = count + __popc(mask & ((1u << lane) - 1u));
         qk[wl][slot] = k;
-        qv[wl][slot][0] = vx;
-        qv[wl][slot][1] = vy;
-        qv[wl][slot][2] = vz;
+        qs[wl][slot] = code;
       }
       count += __popc(mask);
       __syncwarp();
@@ -530,77 +567,151 @@ __global__ void __launch_bounds__(kLrWarps * 32) k_long_range(
         evaluate(lane);
         __syncwarp();
         const int rest = count - 32;
-        int mk = 0;
-        double m0 = 0, m1 = 0, m2 = 0;
+        int mk = 0, mc = 0;
         if (lane < rest) {
           mk = qk[wl][32 + lane];
-          m0 = qv[wl][32 + lane][0];
-          m1 = qv[wl][32 + lane][1];
-          m2 = qv[wl][32 + lane][2];
+          mc = qs[wl][32 + lane];
         }
         __syncwarp();
         if (lane < rest) {
           qk[wl][lane] = mk;
-          qv[wl][lane][0] = m0;
-          qv[wl][lane][1] = m1;
-          qv[wl][lane][2] = m2;
+          qs[wl][lane] = mc;
         }
         count = rest;
         __syncwarp();
       }
     }
   };
+  // Every lane brings m ranges (of one stencil row; at most kLrSegs over the
+  // warp), the q-th from run(q, first, len, code): write them to the table in
+  // lane order and turn their lengths into concatenated offsets.
+  auto fill_table = [&](int m, auto run) {
+    __syncwarp();  // the previous table has been read
+    int off = m;  // prefix of the lanes' range counts
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, off, d);
+      if (lane >= d) off += t;
+    }
+    const int nseg = __shfl_sync(0xffffffffu, off, 31);
+    off -= m;
+    for (int qq = 0; qq < m; ++qq) {
+      int first, len, code;
+      run(qq, first, len, code);
+      sg_first[wl][off + qq] = first;
+      sg_pre[wl][off + qq + 1] = len;  // lengths for now
+      sg_code[wl][off + qq] = code;
+    }
+    __syncwarp();
+    // offsets: lane l sums ranges 2l and 2l + 1, then a warp scan
+    const int l0 = 2 * lane < nseg ? sg_pre[wl][2 * lane + 1] : 0;
+    const int l1 = 2 * lane + 1 < nseg ? sg_pre[wl][2 * lane + 2] : 0;
+    int incl = l0 + l1;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += t;
+    }
+    __syncwarp();
+    if (2 * lane < nseg) sg_pre[wl][2 * lane + 1] = incl - l1;
+    if (2 * lane + 1 < nseg) sg_pre[wl][2 * lane + 2] = incl;
+    if (lane == 0) sg_pre[wl][0] = 0;
+    __syncwarp();
+    return nseg;
+  };
   if (!g.periodic && !g.open_cells) {
     const int im = image_of[i];
-    scan_range(image_start[im], image_start[im + 1], 0.0, 0.0, 0.0);
-  } else if (g.open_cells) {
-    // one open system on a clamped grid: the same trimmed stencil, no wrap and
-    // no shift (an atom outside the grid is farther from every other cell than
-    // its boundary cell is, so the cell-distance bounds still hold)
-    const int nx = g.ncell[0], ny = g.ncell[1], nz = g.ncell[2];
-    const int c = cell[i];
-    const int cx = c % nx, cy = (c / nx) % ny, cz = c / (nx * ny);
-    for (int oz = -reach; oz <= reach; ++oz) {
-      const int wz = cz + oz;
-      if (wz < 0 || wz >= nz) continue;
-      for (int oy = -reach; oy <= reach; ++oy) {
-        const int wy = cy + oy;
-        const int rx = st.rx[abs(oy)][abs(oz)];
-        if (rx < 0 || wy < 0 || wy >= ny) continue;
-        const int row = (wz * ny + wy) * nx;
-        const int lo = max(0, cx - rx), hi = min(nx - 1, cx + rx);
-        scan_range(cell_start[row + lo], cell_start[row + hi] + cell_count[row + hi], 0.0, 0.0, 0.0);
-      }
-    }
+    const int nseg = fill_table(lane == 0 ? 1 : 0, [&](int, int &first, int &len, int &code) {
+      first = image_start[im];
+      len = image_start[im + 1] - first;
+      code = lr_shift_code(0, 0, 0);
+    });
+    scan_table(nseg);
   } else {
     const int nx = g.ncell[0], ny = g.ncell[1], nz = g.ncell[2];
     const int c = cell[i];
     const int cx = c % nx, cy = (c / nx) % ny, cz = c / (nx * ny);
-    // cells farther than the cutoff from the home cell (nearest points) cannot
-    // hold a neighbour: rows with such (oy, oz) are skipped and each row's x run
-    // is trimmed to the cells that can (st.rx, tabulated on the host); the
-    // candidates that remain are the same as before, in the same order
-    for (int oz = -reach; oz <= reach; ++oz) {
-      int wz = cz + oz, sz = 0;
-      while (wz < 0) { wz += nz; --sz; }
-      while (wz >= nz) { wz -= nz; ++sz; }
-      for (int oy = -reach; oy <= reach; ++oy) {
+    const int side = 2 * reach + 1;
+    // The atom's offset from its cell's lower corner; along each axis, the gap
+    // from the atom to the cells o rows away is at least axis_gap (exact for a
+    // cell holding its atoms; a clamped open-grid cell's atoms lie farther out),
+    // less a margin far above the rounding of positions and cell bounds. Rows
+    // and x cells beyond the cutoff by these gaps hold no pair: trimming them
+    // drops only candidates that fail the distance test, in the same order.
+    constexpr double kGapMargin = 1.0e-7;
+    const double clx = g.len[0] / nx, cly = g.len[1] / ny, clz = g.len[2] / nz;
+    const double ux = (xi - g.lo[0]) - cx * clx, uy = (yi - g.lo[1]) - cy * cly, uz = (zi - g.lo[2]) - cz * clz;
+    auto axis_gap = [](int o, double u, double cl) {
+      const double d = o > 0 ? o * cl - u : (o < 0 ? u + (-o - 1) * cl : 0.0);
+      return fmax(d - kGapMargin, 0.0);
+    };
+    for (int t0 = 0; t0 < side * side; t0 += rows_per_fill) {
+      // lane j: stencil row t0 + j, (oz, oy) in the serial order (z outer)
+      const int t = t0 + lane;
+      const int oz = t / side - reach, oy = t % side - reach;
+      int m = 0, row = 0, xa = 0, xb = -1, sx_lo = 0, sy = 0, sz = 0;
+      if (lane < rows_per_fill && t < side * side) {
+        // cells farther than the cutoff from the home cell (nearest points)
+        // cannot hold a neighbour: rows with such (oy, oz) are skipped and each
+        // row's x run is trimmed to the cells that can (st.rx, tabulated on the
+        // host), then to the cells within the cutoff of the atom itself
         const int rx = st.rx[abs(oy)][abs(oz)];
-        if (rx < 0) continue;
-        int wy = cy + oy, sy = 0;
-        while (wy < 0) { wy += ny; --sy; }
-        while (wy >= ny) { wy -= ny; ++sy; }
-        const int row = (wz * ny + wy) * nx;
-        const double shy = sy * g.len[1], shz = sz * g.len[2];
-        // x runs of constant periodic shift: cells [lo, hi] of one row are contiguous
-        const int sx_lo = (cx - rx >= 0) ? 0 : -((rx - cx + nx - 1) / nx);
-        const int sx_hi = (cx + rx) / nx;
-        for (int sx = sx_lo; sx <= sx_hi; ++sx) {
-          const int lo = max(0, cx - rx - sx * nx), hi = min(nx - 1, cx + rx - sx * nx);
-          if (lo > hi) continue;
-          scan_range(cell_start[row + lo], cell_start[row + hi] + cell_count[row + hi], sx * g.len[0], shy, shz);
+        const double gy = axis_gap(oy, uy, cly), gz = axis_gap(oz, uz, clz);
+        const double rem = rc2 - gy * gy - gz * gz;
+        if (rx >= 0 && rem > 0.0) {
+          // cells cx + xa .. cx + xb (unwrapped): o > 0 while o clx - ux <= w,
+          // o < 0 while ux + (-o - 1) clx <= w, and always the atom's own
+          // column (gap 0: on a clamped open grid the atom can lie beyond it)
+          const double w = sqrt(rem) + kGapMargin;
+          const double hi_d = fmin(fmax(floor((w + ux) / clx), 0.0), double(rx));
+          const double lo_d = fmin(fmax(floor((w - ux) / clx + 1.0), 0.0), double(rx));
+          xb = cx + int(hi_d);
+          xa = cx - int(lo_d);
+        }
+        if (xa > xb) {
+          // nothing of this row is within the cutoff
+        } else if (g.open_cells) {
+          // one open system on a clamped grid: no wrap and no shift (an atom
+          // outside the grid is farther from every other cell than its
+          // boundary cell is, so the bounds above still hold)
+          const int wz = cz + oz, wy = cy + oy;
+          if (wz >= 0 && wz < nz && wy >= 0 && wy < ny && max(0, xa) <= min(nx - 1, xb)) {
+            row = (wz * ny + wy) * nx;
+            m = 1;
+          }
+        } else {
+          // x runs of constant periodic shift are contiguous
+          int wz = cz + oz, wy = cy + oy;
+          while (wz < 0) { wz += nz; --sz; }
+          while (wz >= nz) { wz -= nz; ++sz; }
+          while (wy < 0) { wy += ny; --sy; }
+          while (wy >= ny) { wy -= ny; ++sy; }
+          row = (wz * ny + wy) * nx;
+          sx_lo = xa >= 0 ? 0 : -((nx - 1 - xa) / nx);
+          const int sx_hi = xb >= 0 ? xb / nx : -1;
+          for (int sx = sx_lo; sx <= sx_hi; ++sx)
+            if (max(0, xa - sx * nx) <= min(nx - 1, xb - sx * nx)) ++m;
         }
       }
+      const int nseg = fill_table(m, [&](int qq, int &first, int &len, int &code) {
+        int lo, hi, sx;
+        if (g.open_cells) {
+          lo = max(0, xa);
+          hi = min(nx - 1, xb);
+          sx = 0;
+        } else {  // the qq-th non-empty x run of the row
+          sx = sx_lo;
+          for (int seen = -1;; ++sx) {
+            lo = max(0, xa - sx * nx);
+            hi = min(nx - 1, xb - sx * nx);
+            if (lo <= hi && ++seen == qq) break;
+          }
+        }
+        first = cell_start[row + lo];
+        len = cell_start[row + hi] + cell_count[row + hi] - first;
+        code = lr_shift_code(sx, sy, sz);
+      });
+      scan_table(nseg);
     }
   }
   if (lane < count) evaluate(lane);
@@ -645,6 +756,7 @@ void launch_long_range(int n, int n_cells_atoms, const NeighborState &nb, double
   SO3_LAUNCH("lr_gather");
   const int reach = sr_reach(nb.grid, rc_lr);
   LrStencil st;
+  int rows_per_fill = 32;
   {
     const CellGrid &g = nb.grid;
     const double clx = g.len[0] / g.ncell[0], cly = g.len[1] / g.ncell[1], clz = g.len[2] / g.ncell[2];
@@ -662,14 +774,33 @@ void launch_long_range(int n, int n_cells_atoms, const NeighborState &nb, double
     if ((g.periodic || g.open_cells) && reach > kLrMaxReach)
       throw std::runtime_error("SO3LR long range: cell stencil reach above " +
                                                        std::to_string(kLrMaxReach));
+    if (g.periodic) {
+      // x runs of one stencil row: one per periodic shift of the row's cells
+      // (two when the run wraps once); the kernel's range table holds kLrSegs
+      int max_runs = 1;
+      const int nx = g.ncell[0];
+      for (int a = 0; a <= reach; ++a)
+        for (int b = 0; b <= reach; ++b) {
+          const int rx = st.rx[a][b];
+          if (rx < 0) continue;
+          for (int cx = 0; cx < nx; ++cx) {
+            const int sx_lo = (cx - rx >= 0) ? 0 : -((rx - cx + nx - 1) / nx), sx_hi = (cx + rx) / nx;
+            int runs = 0;
+            for (int sx = sx_lo; sx <= sx_hi; ++sx)
+              if (std::max(0, cx - rx - sx * nx) <= std::min(nx - 1, cx + rx - sx * nx)) ++runs;
+            max_runs = std::max(max_runs, runs);
+          }
+        }
+      rows_per_fill = std::min(32, kLrSegs / max_runs);
+    }
   }
   const int threads = kLrWarps * 32;
   const int blocks = (n * 32 + threads - 1) / threads;
   auto go = [&](auto sep, auto f) {
     constexpr bool kSep = decltype(sep)::value, kF = decltype(f)::value;
     k_long_range<kSep, kF><<<blocks, threads, 0, s>>>(n, nb.row0, nb.xw, nb.grid, nb.cell, nb.cell_start,
-                                                      nb.cell_count, nb.image_of, nb.image_start, reach, st,
-                                                      rc_lr * rc_lr, pos4, par4, z, q, h, kSep ? c6r : nullptr,
+                                                      nb.cell_count, nb.image_of, nb.image_start, reach,
+                                                      rows_per_fill, st, rc_lr * rc_lr, pos4, par4, z, q, h, kSep ? c6r : nullptr,
                                                       alpha_ref, c6_ref, table_size, p, e_lr, e_elec, e_disp, dq, dh,
                                                       kSep ? dc6 : nullptr, f_lr, w_lr);
   };

@@ -226,6 +226,12 @@ def test_gpu_open_droplet_on_cell_grid(gpu_model, oracle_model):
         other.close()
     assert abs(e_range - g["energy"]) <= 1e-11 * abs(g["energy"])
     assert np.abs(fd.cpu().numpy() - g["forces"]).max() <= 1e-11
+    # moved by several cell widths' worth of margin on the same handle: the grid
+    # stays, many atoms lie beyond it in their clamped boundary cells, and the
+    # long-range stencil still finds every pair
+    t = gpu_model.compute(pos + np.array([6.1, -4.7, 3.3]), z)
+    assert abs(t["energy"] - g["energy"]) / n <= 1e-11
+    assert np.abs(t["forces"] - g["forces"]).max() <= 1e-9
 
 
 def test_gpu_open_droplet_above_range_search_limit(gpu_model):
