@@ -10,31 +10,37 @@
 // The reference runs each dense layer as a cuBLAS DGEMM followed by separate
 // elementwise kernels; here the bias/activation/residual work is fused into the
 // GEMM epilogue.
+#include <type_traits>
+
 #include "kernels.cuh"
 
 SO3LR_SHAPE_BEGIN
 namespace {
 
-// 32 x 64 output tile per CTA, 4 warps of 32 x 16 (2 x 2 m16n8k8 blocks), K in
-// steps of 16 through a two-stage cp.async pipeline. (The node GEMMs have
+// 32 x 64 (or 64 x 32) output tile per CTA, 4 warps of 32 x 16 (2 x 2 m16n8k8
+// blocks), K in steps of 16 through a two-stage cp.async pipeline. (The node GEMMs have
 // M = atoms and N, K = 32..320: at 24,000 atoms 64-row tiles gave 1.27 waves of
 // CTAs on 148 SMs; 32-row tiles at about 70 registers run 6 CTAs per SM and
 // measured 0.23 ms per MD step faster.) A is staged as [m][k] and
 // B as [n][k] (transposed weights) or [k][n]; the shared-memory row strides keep
 // the fragment loads free of bank conflicts (24 = 8 mod 16 doubles for 16-byte
-// loads of two rows, 66 = 2 mod 16 for 8-byte loads of four k rows).
-constexpr int BN = 64, BK = 16;
-constexpr int LDA_S = BK + 8, LDBT_S = BK + 8, LDBN_S = BN + 2;
+// loads of two rows, 66 or 34 = 2 mod 16 for 8-byte loads of four k rows).
+constexpr int BK = 16;
+constexpr int LDA_S = BK + 8, LDBT_S = BK + 8;
 constexpr int kGemmThreads = 128;
-template <bool TRANSB, int BMT>
+template <bool TRANSB, int BMT, int BNT>
 constexpr int gemm_smem_doubles() {
-  return 2 * BMT * LDA_S + 2 * (TRANSB ? BN * LDBT_S : BK * LDBN_S);
+  return 2 * BMT * LDA_S + 2 * (TRANSB ? BNT * LDBT_S : BK * (BNT + 2));
 }
 
-template <bool TRANSB, Epi EPI, int BMT>
+// BMT x BNT output tile: 32 x 64, or 64 x 32 for N that 64-column tiles would
+// pad by more (N = 32, 160, 136: the per-head QKV projections and the
+// interaction layer); either way a warp computes 32 x 16.
+template <bool TRANSB, Epi EPI, int BMT, int BNT>
 __global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols, int ldaux2) {
   extern __shared__ double gsm[];
-  constexpr int BM = BMT;
+  constexpr int BM = BMT, BN = BNT;
+  constexpr int LDBN_S = BN + 2;
   constexpr int WN = BMT == 64 ? 2 : 4;  // warps along N (warp tiles of 32 rows)
   constexpr int NI = BN / WN / 8;        // n8 blocks per warp
   constexpr int ASTAGE = BM * LDA_S;
@@ -166,25 +172,32 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols,
     }
 }
 
-constexpr int kGemmBM = 32;  // rows per tile (the kernel also supports 64)
 template <bool T, Epi E>
-void launch_gemm_kernel(const GemmArgs &g, dim3 grid, cudaStream_t s, int aux_cols, int ldaux2) {
-  constexpr size_t smem = sizeof(double) * gemm_smem_doubles<T, kGemmBM>();
-  allow_dynamic_smem(reinterpret_cast<const void *>(k_gemm<T, E, kGemmBM>), smem);
-  k_gemm<T, E, kGemmBM><<<grid, kGemmThreads, smem, s>>>(g, aux_cols, ldaux2);
+void launch_gemm_kernel(const GemmArgs &g, cudaStream_t s, int aux_cols, int ldaux2) {
+  auto go = [&](auto bm, auto bn) {
+    constexpr int BMT = decltype(bm)::value, BNT = decltype(bn)::value;
+    constexpr size_t smem = sizeof(double) * gemm_smem_doubles<T, BMT, BNT>();
+    allow_dynamic_smem(reinterpret_cast<const void *>(k_gemm<T, E, BMT, BNT>), smem);
+    const dim3 grid((g.N + BNT - 1) / BNT, (g.M + BMT - 1) / BMT, g.batch);
+    k_gemm<T, E, BMT, BNT><<<grid, kGemmThreads, smem, s>>>(g, aux_cols, ldaux2);
+  };
+  // the tile shape that pads N least (64 columns on a tie)
+  const int pad64 = (g.N + 63) / 64 * 64 - g.N, pad32 = (g.N + 31) / 32 * 32 - g.N;
+  if (pad32 < pad64) go(std::integral_constant<int, 64>{}, std::integral_constant<int, 32>{});
+  else go(std::integral_constant<int, 32>{}, std::integral_constant<int, 64>{});
 }
 
 template <bool T>
-void dispatch_epi(const GemmArgs &g, dim3 grid, cudaStream_t s, int aux_cols, int ldaux2) {
+void dispatch_epi(const GemmArgs &g, cudaStream_t s, int aux_cols, int ldaux2) {
   switch (g.epi) {
-    case Epi::None: launch_gemm_kernel<T, Epi::None>(g, grid, s, aux_cols, ldaux2); break;
-    case Epi::Bias: launch_gemm_kernel<T, Epi::Bias>(g, grid, s, aux_cols, ldaux2); break;
-    case Epi::BiasSilu: launch_gemm_kernel<T, Epi::BiasSilu>(g, grid, s, aux_cols, ldaux2); break;
-    case Epi::BiasStorePre: launch_gemm_kernel<T, Epi::BiasStorePre>(g, grid, s, aux_cols, ldaux2); break;
-    case Epi::AddResidual: launch_gemm_kernel<T, Epi::AddResidual>(g, grid, s, aux_cols, ldaux2); break;
-    case Epi::BiasResidual: launch_gemm_kernel<T, Epi::BiasResidual>(g, grid, s, aux_cols, ldaux2); break;
-    case Epi::SiluPrimeMul: launch_gemm_kernel<T, Epi::SiluPrimeMul>(g, grid, s, aux_cols, ldaux2); break;
-    case Epi::GateSiluResidual: launch_gemm_kernel<T, Epi::GateSiluResidual>(g, grid, s, aux_cols, ldaux2); break;
+    case Epi::None: launch_gemm_kernel<T, Epi::None>(g, s, aux_cols, ldaux2); break;
+    case Epi::Bias: launch_gemm_kernel<T, Epi::Bias>(g, s, aux_cols, ldaux2); break;
+    case Epi::BiasSilu: launch_gemm_kernel<T, Epi::BiasSilu>(g, s, aux_cols, ldaux2); break;
+    case Epi::BiasStorePre: launch_gemm_kernel<T, Epi::BiasStorePre>(g, s, aux_cols, ldaux2); break;
+    case Epi::AddResidual: launch_gemm_kernel<T, Epi::AddResidual>(g, s, aux_cols, ldaux2); break;
+    case Epi::BiasResidual: launch_gemm_kernel<T, Epi::BiasResidual>(g, s, aux_cols, ldaux2); break;
+    case Epi::SiluPrimeMul: launch_gemm_kernel<T, Epi::SiluPrimeMul>(g, s, aux_cols, ldaux2); break;
+    case Epi::GateSiluResidual: launch_gemm_kernel<T, Epi::GateSiluResidual>(g, s, aux_cols, ldaux2); break;
   }
 }
 
@@ -192,9 +205,8 @@ void dispatch_epi(const GemmArgs &g, dim3 grid, cudaStream_t s, int aux_cols, in
 
 void launch_gemm_ex(const GemmArgs &g, int aux_cols, int ldaux2, cudaStream_t s) {
   if (g.M == 0) return;
-  dim3 grid((g.N + BN - 1) / BN, (g.M + kGemmBM - 1) / kGemmBM, g.batch);
-  if (g.transB) dispatch_epi<true>(g, grid, s, aux_cols, ldaux2);
-  else dispatch_epi<false>(g, grid, s, aux_cols, ldaux2);
+  if (g.transB) dispatch_epi<true>(g, s, aux_cols, ldaux2);
+  else dispatch_epi<false>(g, s, aux_cols, ldaux2);
   SO3_LAUNCH("gemm");
 }
 void launch_gemm(const GemmArgs &g, cudaStream_t s) { launch_gemm_ex(g, g.N, g.ldaux, s); }
