@@ -10,6 +10,7 @@
 // The reference runs each dense layer as a cuBLAS DGEMM followed by separate
 // elementwise kernels; here the bias/activation/residual work is fused into the
 // GEMM epilogue.
+#include <cstdint>
 #include <type_traits>
 
 #include "kernels.cuh"
@@ -37,7 +38,7 @@ constexpr int gemm_smem_doubles() {
 // pad by more (N = 32, 160, 136: the per-head QKV projections and the
 // interaction layer); either way a warp computes 32 x 16.
 template <bool TRANSB, Epi EPI, int BMT, int BNT>
-__global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols, int ldaux2) {
+__global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols, int ldaux2, bool vec) {
   extern __shared__ double gsm[];
   constexpr int BM = BMT, BN = BNT;
   constexpr int LDBN_S = BN + 2;
@@ -135,6 +136,29 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols,
     }
     __syncthreads();  // the stage is refilled two iterations later
   }
+  // epilogue: each lane holds two adjacent columns of a row; with vec (every
+  // array 16-byte aligned, every row stride even) they move as one 16-byte
+  // load or store
+  auto epilogue = [&](int row, int col, double v, const double *aux_p, const double *aux2_p) {
+    if (EPI == Epi::Bias) {
+      v += bias[col];
+    } else if (EPI == Epi::BiasSilu) {
+      v = silu(v + bias[col]);
+    } else if (EPI == Epi::BiasStorePre) {
+      const double pre = v + bias[col];
+      g.aux_out[(size_t)row * g.ldaux + col] = pre;
+      v = silu(pre);
+    } else if (EPI == Epi::AddResidual) {
+      if (col < aux_cols) v += *aux_p;
+    } else if (EPI == Epi::BiasResidual) {
+      v = v + bias[col] + *aux_p;
+    } else if (EPI == Epi::SiluPrimeMul) {
+      v *= silu_prime(*aux_p);
+    } else if (EPI == Epi::GateSiluResidual) {
+      v = *aux2_p + v * silu_prime(*aux_p);
+    }
+    return v;
+  };
 #pragma unroll
   for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
@@ -144,29 +168,37 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols,
       const int row = g.rows ? g.rows[lrow] : lrow;
 #pragma unroll
       for (int ni = 0; ni < NI; ++ni) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int col = n0 + wn * (BN / WN) + ni * 8 + 2 * tq + h;
-          if (col >= g.N) continue;
-          double v = acc[mi][ni][2 * hf + h];
-          if (EPI == Epi::Bias) {
-            v += bias[col];
-          } else if (EPI == Epi::BiasSilu) {
-            v = silu(v + bias[col]);
-          } else if (EPI == Epi::BiasStorePre) {
-            const double pre = v + bias[col];
-            g.aux_out[(size_t)row * g.ldaux + col] = pre;
-            v = silu(pre);
-          } else if (EPI == Epi::AddResidual) {
-            if (col < aux_cols) v += aux[(size_t)row * g.ldaux + col];
-          } else if (EPI == Epi::BiasResidual) {
-            v = v + bias[col] + aux[(size_t)row * g.ldaux + col];
-          } else if (EPI == Epi::SiluPrimeMul) {
-            v *= silu_prime(aux[(size_t)row * g.ldaux + col]);
-          } else if (EPI == Epi::GateSiluResidual) {
-            v = g.aux2[(size_t)row * ldaux2 + col] + v * silu_prime(aux[(size_t)row * g.ldaux + col]);
+        const int col = n0 + wn * (BN / WN) + ni * 8 + 2 * tq;
+        const double *aux_p = aux ? aux + (size_t)row * g.ldaux + col : nullptr;
+        const double *aux2_p = g.aux2 ? g.aux2 + (size_t)row * ldaux2 + col : nullptr;
+        if (vec && col + 1 < g.N) {
+          double2 a2 = make_double2(0.0, 0.0), b2 = make_double2(0.0, 0.0);
+          if (EPI == Epi::AddResidual) {
+            if (col + 1 < aux_cols) a2 = *reinterpret_cast<const double2 *>(aux_p);
+            else if (col < aux_cols) a2.x = aux_p[0];
+          } else if (EPI == Epi::BiasResidual || EPI == Epi::SiluPrimeMul || EPI == Epi::GateSiluResidual) {
+            a2 = *reinterpret_cast<const double2 *>(aux_p);
           }
-          C[(size_t)row * g.ldc + col] = v;
+          if (EPI == Epi::GateSiluResidual) b2 = *reinterpret_cast<const double2 *>(aux2_p);
+          double2 out;
+          if (EPI == Epi::BiasStorePre) {
+            const double2 bb = *reinterpret_cast<const double2 *>(bias + col);
+            const double2 pre = make_double2(acc[mi][ni][2 * hf] + bb.x, acc[mi][ni][2 * hf + 1] + bb.y);
+            *reinterpret_cast<double2 *>(g.aux_out + (size_t)row * g.ldaux + col) = pre;
+            out = make_double2(silu(pre.x), silu(pre.y));
+          } else {
+            out.x = epilogue(row, col, acc[mi][ni][2 * hf], &a2.x, &b2.x);
+            out.y = epilogue(row, col + 1, acc[mi][ni][2 * hf + 1], &a2.y, &b2.y);
+          }
+          *reinterpret_cast<double2 *>(C + (size_t)row * g.ldc + col) = out;
+        } else {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (col + h >= g.N) continue;
+            const double v = epilogue(row, col + h, acc[mi][ni][2 * hf + h], aux_p ? aux_p + h : nullptr,
+                                      aux2_p ? aux2_p + h : nullptr);
+            C[(size_t)row * g.ldc + col + h] = v;
+          }
         }
       }
     }
@@ -174,12 +206,16 @@ __global__ void __launch_bounds__(kGemmThreads) k_gemm(GemmArgs g, int aux_cols,
 
 template <bool T, Epi E>
 void launch_gemm_kernel(const GemmArgs &g, cudaStream_t s, int aux_cols, int ldaux2) {
+  auto al = [](const void *p) { return (reinterpret_cast<std::uintptr_t>(p) & 15) == 0; };
+  auto ev = [](long long x) { return (x & 1) == 0; };
+  const bool vec = al(g.C) && al(g.bias) && al(g.aux) && al(g.aux2) && al(g.aux_out) && ev(g.ldc) &&
+                   ev(g.ldaux) && ev(ldaux2) && ev(g.strideC) && ev(g.strideAux) && ev(g.strideBias);
   auto go = [&](auto bm, auto bn) {
     constexpr int BMT = decltype(bm)::value, BNT = decltype(bn)::value;
     constexpr size_t smem = sizeof(double) * gemm_smem_doubles<T, BMT, BNT>();
     allow_dynamic_smem(reinterpret_cast<const void *>(k_gemm<T, E, BMT, BNT>), smem);
     const dim3 grid((g.N + BNT - 1) / BNT, (g.M + BMT - 1) / BMT, g.batch);
-    k_gemm<T, E, BMT, BNT><<<grid, kGemmThreads, smem, s>>>(g, aux_cols, ldaux2);
+    k_gemm<T, E, BMT, BNT><<<grid, kGemmThreads, smem, s>>>(g, aux_cols, ldaux2, vec);
   };
   // the tile shape that pads N least (64 columns on a tie)
   const int pad64 = (g.N + 63) / 64 * 64 - g.N, pad32 = (g.N + 31) / 32 * 32 - g.N;
