@@ -11,6 +11,7 @@
 // elementwise kernels; here the bias/activation/residual work is fused into the
 // GEMM epilogue.
 #include <cstdint>
+#include <initializer_list>
 #include <type_traits>
 
 #include "kernels.cuh"
@@ -282,6 +283,36 @@ __device__ inline double warp_sum(double v) {
 constexpr int kPL = kF / 32;
 constexpr int kEVL = (kEV + 31) / 32;
 
+// A lane's kPL consecutive channels of a row (row strides kF and kIntW are
+// multiples of 4 doubles): 256-bit loads and 128-bit stores when the launch's
+// row arrays are 32-byte aligned (vec, checked on the host), else 8-byte ones.
+__device__ inline void ld_lane(bool vec, const double *p, double (&v)[kPL]) {
+  if (vec) {
+#pragma unroll
+    for (int q = 0; q < kPL; q += 4)
+      asm("ld.global.v4.f64 {%0,%1,%2,%3}, [%4];"
+          : "=d"(v[q]), "=d"(v[q + 1]), "=d"(v[q + 2]), "=d"(v[q + 3])
+          : "l"(p + q));
+  } else {
+#pragma unroll
+    for (int q = 0; q < kPL; ++q) v[q] = p[q];
+  }
+}
+__device__ inline void st_lane(bool vec, double *p, const double (&v)[kPL]) {
+  if (vec) {
+#pragma unroll
+    for (int q = 0; q < kPL; q += 2) *reinterpret_cast<double2 *>(p + q) = make_double2(v[q], v[q + 1]);
+  } else {
+#pragma unroll
+    for (int q = 0; q < kPL; ++q) p[q] = v[q];
+  }
+}
+inline bool aligned32(std::initializer_list<const void *> ptrs) {
+  for (const void *p : ptrs)
+    if ((reinterpret_cast<std::uintptr_t>(p) & 31) != 0) return false;
+  return true;
+}
+
 // sum over the warp of the per-lane terms t[j] of the channels of degree slot k
 // (ch[j] = slot of the lane's j-th equivariant channel, -1 when it has none)
 __device__ inline double slot_sum(int k, const int (&ch)[kEVL], const double (&t)[kEVL]) {
@@ -329,25 +360,27 @@ __global__ void k_post_attn_pre(int n, const double *__restrict__ x, const doubl
                                 const double *__restrict__ lnw, const double *__restrict__ lnb,
                                 const double *__restrict__ cg_int, double *__restrict__ xhat1,
                                 double *__restrict__ rstd1, double *__restrict__ n1_out, double *__restrict__ act,
-                                double *__restrict__ A_out, double *__restrict__ cat) {
+                                double *__restrict__ A_out, double *__restrict__ cat, bool vec) {
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
-  double a[kPL], xh[kPL];
+  const size_t o = (size_t)i * kF + lane * kPL;
+  double a[kPL], xh[kPL], dv[kPL];
+  ld_lane(vec, x + o, a);
+  ld_lane(vec, d_inv + o, dv);
 #pragma unroll
-  for (int j = 0; j < kPL; ++j) {
-    const int c = lane * kPL + j;
-    a[j] = x[(size_t)i * kF + c] + d_inv[(size_t)i * kF + c];
-  }
+  for (int j = 0; j < kPL; ++j) a[j] += dv[j];
   const double rs = row_norm(norm, a, xh);
+  double y[kPL], sy[kPL];
 #pragma unroll
   for (int j = 0; j < kPL; ++j) {
     const int c = lane * kPL + j;
-    const double y = norm == kNormLayer ? xh[j] * lnw[c] + lnb[c] : xh[j];
-    xhat1[(size_t)i * kF + c] = xh[j];
-    n1_out[(size_t)i * kF + c] = y;
-    act[(size_t)i * kF + c] = silu(y);
+    y[j] = norm == kNormLayer ? xh[j] * lnw[c] + lnb[c] : xh[j];
+    sy[j] = silu(y[j]);
   }
+  st_lane(vec, xhat1 + o, xh);
+  st_lane(vec, n1_out + o, y);
+  st_lane(vec, act + o, sy);
   if (lane == 0) rstd1[i] = rs;
   int d[kEVL];
   double term[kEVL];
@@ -373,8 +406,9 @@ __global__ void k_post_attn_pre(int n, const double *__restrict__ x, const doubl
 void launch_post_attn_pre(int n, const double *x, const double *d_inv, const double *ev, const double *d_ev,
                           int norm, const double *lnw, const double *lnb, const double *cg_int, double *xhat1,
                           double *rstd1, double *n1, double *act, double *A, double *cat, cudaStream_t s) {
+  const bool vec = aligned32({x, d_inv, xhat1, n1, act});
   k_post_attn_pre<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, x, d_inv, ev, d_ev, norm, lnw, lnb, cg_int, xhat1, rstd1,
-                                                       n1, act, A, cat);
+                                                       n1, act, A, cat, vec);
   SO3_LAUNCH("post_attn_pre");
 }
 
@@ -383,23 +417,25 @@ __global__ void k_post_attn_final(int n, const double *__restrict__ cat, const d
                                   const double *__restrict__ A, int norm, const double *__restrict__ lnw,
                                   const double *__restrict__ lnb, double *__restrict__ xhat2,
                                   double *__restrict__ rstd2, double *__restrict__ gate,
-                                  double *__restrict__ x_out, double *__restrict__ ev_out) {
+                                  double *__restrict__ x_out, double *__restrict__ ev_out, bool vec) {
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
-  double v[kPL], xh[kPL];
+  const size_t oi = (size_t)i * kIntW + lane * kPL, o = (size_t)i * kF + lane * kPL;
+  double v[kPL], tv[kPL], xh[kPL];
+  ld_lane(vec, cat + oi, v);
+  ld_lane(vec, t + oi, tv);
 #pragma unroll
-  for (int j = 0; j < kPL; ++j) {
-    const int c = lane * kPL + j;
-    v[j] = cat[(size_t)i * kIntW + c] + t[(size_t)i * kIntW + c];
-  }
+  for (int j = 0; j < kPL; ++j) v[j] += tv[j];
   const double rs = row_norm(norm, v, xh);
+  double y[kPL];
 #pragma unroll
   for (int j = 0; j < kPL; ++j) {
     const int c = lane * kPL + j;
-    xhat2[(size_t)i * kF + c] = xh[j];
-    x_out[(size_t)i * kF + c] = norm == kNormLayer ? xh[j] * lnw[c] + lnb[c] : xh[j];
+    y[j] = norm == kNormLayer ? xh[j] * lnw[c] + lnb[c] : xh[j];
   }
+  st_lane(vec, xhat2 + o, xh);
+  st_lane(vec, x_out + o, y);
   if (lane == 0) rstd2[i] = rs;
   if (lane < kHeads) gate[(size_t)i * kHeads + lane] = t[(size_t)i * kIntW + kF + lane];
 #pragma unroll
@@ -415,8 +451,9 @@ __global__ void k_post_attn_final(int n, const double *__restrict__ cat, const d
 void launch_post_attn_final(int n, const double *cat, const double *t, const double *A, int norm, const double *lnw,
                             const double *lnb, double *xhat2, double *rstd2, double *gate, double *x_out,
                             double *ev_out, cudaStream_t s) {
+  const bool vec = aligned32({cat, t, xhat2, x_out});
   k_post_attn_final<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, cat, t, A, norm, lnw, lnb, xhat2, rstd2, gate, x_out,
-                                                         ev_out);
+                                                         ev_out, vec);
   SO3_LAUNCH("post_attn_final");
 }
 
@@ -448,19 +485,15 @@ __global__ void k_post_attn_rev_final(int n, const double *__restrict__ g_x, con
                                       const double *__restrict__ xhat2, const double *__restrict__ rstd2, int norm,
                                       const double *__restrict__ lnw2, const double *__restrict__ A,
                                       const double *__restrict__ gate, double *__restrict__ g_t,
-                                      double *__restrict__ g_A) {
+                                      double *__restrict__ g_A, bool vec) {
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
   double gy[kPL], xh[kPL], gx[kPL];
-#pragma unroll
-  for (int j = 0; j < kPL; ++j) {
-    gy[j] = g_x[(size_t)i * kF + lane * kPL + j];
-    xh[j] = xhat2[(size_t)i * kF + lane * kPL + j];
-  }
+  ld_lane(vec, g_x + (size_t)i * kF + lane * kPL, gy);
+  ld_lane(vec, xhat2 + (size_t)i * kF + lane * kPL, xh);
   norm_backward(norm, gy, xh, lnw2, lane, rstd2[i], gx);
-#pragma unroll
-  for (int j = 0; j < kPL; ++j) g_t[(size_t)i * kIntW + lane * kPL + j] = gx[j];
+  st_lane(vec, g_t + (size_t)i * kIntW + lane * kPL, gx);
   double ge[kEVL], gA[kEVL];
   int d[kEVL];
 #pragma unroll
@@ -491,8 +524,9 @@ __global__ void k_post_attn_rev_final(int n, const double *__restrict__ g_x, con
 void launch_post_attn_rev_final(int n, const double *g_x, const double *g_ev, const double *xhat2,
                                 const double *rstd2, int norm, const double *lnw2, const double *A,
                                 const double *gate, double *g_t, double *g_A, cudaStream_t s) {
+  const bool vec = aligned32({g_x, xhat2, g_t});
   k_post_attn_rev_final<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, g_x, g_ev, xhat2, rstd2, norm, lnw2, A, gate, g_t,
-                                                             g_A);
+                                                             g_A, vec);
   SO3_LAUNCH("post_attn_rev_final");
 }
 
@@ -501,19 +535,15 @@ __global__ void k_post_attn_rev_ln1(int n, const double *__restrict__ g_n1, cons
                                     const double *__restrict__ rstd1, int norm, const double *__restrict__ lnw1,
                                     const double *__restrict__ A, const double *__restrict__ cg_int,
                                     const double *__restrict__ g_cat, double *__restrict__ g_a,
-                                    double *__restrict__ g_A) {
+                                    double *__restrict__ g_A, bool vec) {
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
   double gy[kPL], xh[kPL], gx[kPL];
-#pragma unroll
-  for (int j = 0; j < kPL; ++j) {
-    gy[j] = g_n1[(size_t)i * kF + lane * kPL + j];
-    xh[j] = xhat1[(size_t)i * kF + lane * kPL + j];
-  }
+  ld_lane(vec, g_n1 + (size_t)i * kF + lane * kPL, gy);
+  ld_lane(vec, xhat1 + (size_t)i * kF + lane * kPL, xh);
   norm_backward(norm, gy, xh, lnw1, lane, rstd1[i], gx);
-#pragma unroll
-  for (int j = 0; j < kPL; ++j) g_a[(size_t)i * kF + lane * kPL + j] = gx[j];
+  st_lane(vec, g_a + (size_t)i * kF + lane * kPL, gx);
 #pragma unroll
   for (int j = 0; j < kEVL; ++j) {
     const int m = lane + 32 * j;
@@ -528,8 +558,9 @@ __global__ void k_post_attn_rev_ln1(int n, const double *__restrict__ g_n1, cons
 void launch_post_attn_rev_ln1(int n, const double *g_n1, const double *xhat1, const double *rstd1, int norm,
                               const double *lnw1, const double *A, const double *cg_int, const double *g_cat,
                               double *g_a, double *g_A, cudaStream_t s) {
+  const bool vec = aligned32({g_n1, xhat1, g_a});
   k_post_attn_rev_ln1<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, g_n1, xhat1, rstd1, norm, lnw1, A, cg_int, g_cat, g_a,
-                                                           g_A);
+                                                           g_A, vec);
   SO3_LAUNCH("post_attn_rev_ln1");
 }
 
