@@ -124,12 +124,35 @@ __global__ void k_cell_fill(int n, const int *__restrict__ cell, const int *__re
 // Sort the atoms of every cell by global tag: the fill above is
 // scheduling-dependent, and the tag order does not depend on how rows are laid
 // out across GPUs.
-__global__ void k_cell_sort(int ncells, const int *__restrict__ cell_start, const int *__restrict__ cell_count,
-                            const int *__restrict__ tag, int *__restrict__ cell_atoms) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+// One warp per cell: the cell's atoms in ascending tag order (tags, or atom
+// indices without tags, are unique), each placed at the count of smaller keys;
+// a cell of more than kCsCap atoms is sorted by one lane in place.
+constexpr int kCsWarps = 4, kCsCap = 64;
+__global__ void __launch_bounds__(kCsWarps * 32) k_cell_sort(int ncells, const int *__restrict__ cell_start,
+                                                             const int *__restrict__ cell_count,
+                                                             const int *__restrict__ tag, int *__restrict__ cell_atoms) {
+  __shared__ int sk[kCsWarps][kCsCap], sv[kCsWarps][kCsCap];
+  const int wl = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x * kCsWarps + wl;
   if (c >= ncells) return;
   int *a = cell_atoms + cell_start[c];
   const int m = cell_count[c];
+  if (m <= kCsCap) {
+    for (int e = lane; e < m; e += 32) {
+      const int v = a[e];
+      sv[wl][e] = v;
+      sk[wl][e] = tag ? tag[v] : v;
+    }
+    __syncwarp();
+    for (int e = lane; e < m; e += 32) {
+      const int key = sk[wl][e];
+      int rank = 0;
+      for (int q = 0; q < m; ++q) rank += sk[wl][q] < key ? 1 : 0;
+      a[rank] = sv[wl][e];
+    }
+    return;
+  }
+  if (lane != 0) return;
   for (int i = 1; i < m; ++i) {
     const int v = a[i];
     const int vt = tag ? tag[v] : v;
@@ -380,7 +403,8 @@ void build_cells(NeighborState &nb, int n, const double *x, cudaStream_t s) {
   exclusive_scan(nb.cell_count, nb.cell_start, nc, nb.scan_total, nb.scan_scratch, s);
   k_cell_fill<<<(n + 255) / 256, 256, 0, s>>>(n, nb.cell, nb.cell_start, nb.cell_fill, nb.cell_atoms);
   SO3_LAUNCH("cell_fill");
-  k_cell_sort<<<(nc + 127) / 128, 128, 0, s>>>(nc, nb.cell_start, nb.cell_count, nb.tag, nb.cell_atoms);
+  k_cell_sort<<<(nc + kCsWarps - 1) / kCsWarps, kCsWarps * 32, 0, s>>>(nc, nb.cell_start, nb.cell_count, nb.tag,
+                                                                      nb.cell_atoms);
   SO3_LAUNCH("cell_sort");
 }
 

@@ -650,61 +650,93 @@ void launch_qk_norm_reverse(int n, const double *qkv, const double *rinv, double
 // One ratio head (Hirshfeld / a0 or C6; 64 hidden units, keys zero-padded to
 // 64) of one atom: keys k = h1 W2^T + b2 (lane owns keys 2 lane, 2 lane + 1),
 // ratio = |v_shift[Z] + q_emb[Z] . k / sqrt(K)| (output_heads.cpp:135-176).
-__device__ inline double ratio_head(const double *__restrict__ hh, const double *__restrict__ w2t,
-                                    const double *__restrict__ b2, const double *__restrict__ qemb,
-                                    const double *__restrict__ vshift, double sqrt_k, int zz, int lane,
-                                    double *__restrict__ k_out) {
-  double k0 = b2[2 * lane], k1 = b2[2 * lane + 1];
-  // four independent partial sums per output (the 64-term dot product as four
-  // interleaved chains), added in a fixed order
-  double s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0};
-#pragma unroll 4
+// The ratio heads (Hirshfeld, C6) of kHA atoms per warp: every weight row is
+// loaded once for all of them. Per atom and output the 64-term dot product runs
+// as four interleaved chains added in a fixed order.
+constexpr int kHA = 4;
+__device__ inline void ratio_head(const double *const (&hh)[kHA], const double *__restrict__ w2t,
+                                  const double *__restrict__ b2, const double *__restrict__ qemb,
+                                  const double *__restrict__ vshift, double sqrt_k, const int (&zz)[kHA], int na,
+                                  int lane, double *const (&k_out)[kHA], double (&res)[kHA]) {
+  double s0[kHA][4], s1[kHA][4];
+#pragma unroll
+  for (int a = 0; a < kHA; ++a)
+#pragma unroll
+    for (int u = 0; u < 4; ++u) s0[a][u] = s1[a][u] = 0.0;
+#pragma unroll 2
   for (int j = 0; j < kHirsh; j += 4) {
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const double hv = hh[j + u];
       const double2 w = *reinterpret_cast<const double2 *>(w2t + (j + u) * kHirsh + 2 * lane);  // coalesced
-      s0[u] += hv * w.x;
-      s1[u] += hv * w.y;
+#pragma unroll
+      for (int a = 0; a < kHA; ++a) {
+        const double hv = hh[a][j + u];
+        s0[a][u] += hv * w.x;
+        s1[a][u] += hv * w.y;
+      }
     }
   }
-  k0 += (s0[0] + s0[1]) + (s0[2] + s0[3]);
-  k1 += (s1[0] + s1[1]) + (s1[2] + s1[3]);
-  k_out[2 * lane] = k0;
-  k_out[2 * lane + 1] = k1;
-  double qk = qemb[zz * kHirsh + 2 * lane] * k0 + qemb[zz * kHirsh + 2 * lane + 1] * k1;
-  qk = warp_sum(qk);
-  return fabs(vshift[zz] + qk / sqrt_k);
+#pragma unroll
+  for (int a = 0; a < kHA; ++a) {
+    if (a >= na) break;
+    double k0 = b2[2 * lane], k1 = b2[2 * lane + 1];
+    k0 += (s0[a][0] + s0[a][1]) + (s0[a][2] + s0[a][3]);
+    k1 += (s1[a][0] + s1[a][1]) + (s1[a][2] + s1[a][3]);
+    k_out[a][2 * lane] = k0;
+    k_out[a][2 * lane + 1] = k1;
+    double qk = qemb[zz[a] * kHirsh + 2 * lane] * k0 + qemb[zz[a] * kHirsh + 2 * lane + 1] * k1;
+    qk = warp_sum(qk);
+    res[a] = fabs(vshift[zz[a]] + qk / sqrt_k);
+  }
 }
 
+// Output heads of kHA atoms per warp: energy and charge (128-wide dot products)
+// and the ratio heads.
 __global__ void k_heads_finalize(int n, const int *__restrict__ z, const double *__restrict__ hcat, HeadsW hw,
                                  double *__restrict__ hk_out, double *__restrict__ e_nn, double *__restrict__ raw_q,
                                  double *__restrict__ ratio, double *__restrict__ hk6_out,
                                  double *__restrict__ ratio6) {
-  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int i0 = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * kHA;
   const int lane = threadIdx.x & 31;
-  if (i >= n) return;
-  const double *h = hcat + (size_t)i * hw.ldh;
-  double se = 0.0, sq = 0.0;
+  if (i0 >= n) return;
+  const int na = min(kHA, n - i0);
+  const double *hh[kHA], *hh6[kHA];
+  double *ko[kHA], *ko6[kHA];
+  int zz[kHA];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    se += h[lane * 4 + j] * hw.e_w2[lane * 4 + j];
-    sq += h[kHeadHidden + lane * 4 + j] * hw.c_w2[lane * 4 + j];
+  for (int a = 0; a < kHA; ++a) {
+    const int i = i0 + (a < na ? a : 0);  // surplus slots repeat the first atom; their results are dropped
+    const double *h = hcat + (size_t)i * hw.ldh;
+    hh[a] = h + 2 * kHeadHidden;
+    hh6[a] = h + kHeadCat;
+    ko[a] = hk_out + (size_t)i * kHirsh;
+    ko6[a] = hk6_out + (size_t)i * kHirsh;
+    zz[a] = z[i];
   }
-  se = warp_sum(se);
-  sq = warp_sum(sq);
-  const int zz = z[i];
-  const double rh = ratio_head(h + 2 * kHeadHidden, hw.h_w2t, hw.h_b2, hw.h_qemb, hw.h_vshift, hw.h_sqrt_k, zz, lane,
-                               hk_out + (size_t)i * kHirsh);
-  double r6 = 0.0;
-  if (hw.c6_w2 != nullptr)
-    r6 = ratio_head(h + kHeadCat, hw.c6_w2t, hw.c6_b2, hw.c6_qemb, hw.c6_vshift, hw.c6_sqrt_k, zz, lane,
-                    hk6_out + (size_t)i * kHirsh);
-  if (lane == 0) {
-    e_nn[i] = (se + hw.e_b2) * hw.e_scale[zz - 1] + hw.e_shift[zz - 1];
-    raw_q[i] = sq + hw.c_b2 + hw.c_emb[zz];
-    ratio[i] = rh;
-    if (hw.c6_w2 != nullptr) ratio6[i] = r6;
+  for (int a = 0; a < na; ++a) {
+    const int i = i0 + a;
+    const double *h = hcat + (size_t)i * hw.ldh;
+    double se = 0.0, sq = 0.0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      se += h[lane * 4 + j] * hw.e_w2[lane * 4 + j];
+      sq += h[kHeadHidden + lane * 4 + j] * hw.c_w2[lane * 4 + j];
+    }
+    se = warp_sum(se);
+    sq = warp_sum(sq);
+    if (lane == 0) {
+      e_nn[i] = (se + hw.e_b2) * hw.e_scale[zz[a] - 1] + hw.e_shift[zz[a] - 1];
+      raw_q[i] = sq + hw.c_b2 + hw.c_emb[zz[a]];
+    }
+  }
+  double rh[kHA];
+  ratio_head(hh, hw.h_w2t, hw.h_b2, hw.h_qemb, hw.h_vshift, hw.h_sqrt_k, zz, na, lane, ko, rh);
+  if (lane == 0)
+    for (int a = 0; a < na; ++a) ratio[i0 + a] = rh[a];
+  if (hw.c6_w2 != nullptr) {
+    ratio_head(hh6, hw.c6_w2t, hw.c6_b2, hw.c6_qemb, hw.c6_vshift, hw.c6_sqrt_k, zz, na, lane, ko6, rh);
+    if (lane == 0)
+      for (int a = 0; a < na; ++a) ratio6[i0 + a] = rh[a];
   }
 }
 
@@ -712,7 +744,9 @@ void launch_heads_finalize(int n, const int *z, const double *hcat, const HeadsW
                            double *e_nn, double *raw_q, double *ratio, double *hk6_out, double *ratio6,
                            cudaStream_t s) {
   if (n == 0) return;
-  k_heads_finalize<<<(n * 32 + 255) / 256, 256, 0, s>>>(n, z, hcat, hw, hk_out, e_nn, raw_q, ratio, hk6_out, ratio6);
+  const int warps = (n + kHA - 1) / kHA;
+  k_heads_finalize<<<(warps * 32 + 255) / 256, 256, 0, s>>>(n, z, hcat, hw, hk_out, e_nn, raw_q, ratio, hk6_out,
+                                                            ratio6);
   SO3_LAUNCH("heads_finalize");
 }
 
