@@ -767,16 +767,22 @@ __device__ inline void ratio_head_seed(const double *__restrict__ hk, const doub
   gk[2 * lane] = seed * qe0;
   gk[2 * lane + 1] = seed * qe1;
   __syncwarp();
+  // both of the lane's outputs from one 16-byte load of each weight row; per
+  // output four interleaved chains, added in a fixed order
+  double s[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+#pragma unroll 4
+  for (int k = 0; k < kHirsh; k += 4) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const double2 w = *reinterpret_cast<const double2 *>(w2 + (k + u) * kHirsh + 2 * lane);
+      s[0][u] += gk[k + u] * w.x;
+      s[1][u] += gk[k + u] * w.y;
+    }
+  }
 #pragma unroll
   for (int jj = 0; jj < 2; ++jj) {
     const int j = 2 * lane + jj;
-    double s[4] = {0, 0, 0, 0};  // four interleaved chains, added in a fixed order
-#pragma unroll 4
-    for (int k = 0; k < kHirsh; k += 4) {
-#pragma unroll
-      for (int u = 0; u < 4; ++u) s[u] += gk[k + u] * w2[(k + u) * kHirsh + j];
-    }
-    g[j] = ((s[0] + s[1]) + (s[2] + s[3])) * silu_prime(pre[j]);
+    g[j] = ((s[jj][0] + s[jj][1]) + (s[jj][2] + s[jj][3])) * silu_prime(pre[j]);
   }
 }
 
