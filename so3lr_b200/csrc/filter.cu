@@ -124,8 +124,11 @@ __global__ void __launch_bounds__(256, 2) k_filter_forward(int P, const double *
     rr[tid] = p < P ? geo[(size_t)p * kGeo] : 1.0;
   }
   compute_l0(P, p0, pa, pb, ev, cg, l0);
-  __syncthreads();
-  compute_rbf(rr, rbf, rad);
+  {  // the radial basis reads its pair's distance itself: no barrier between
+     // the L0 loads and the basis functions
+    const int p = p0 + tid / kTPP;
+    compute_rbf(p < P ? geo[(size_t)p * kGeo] : 1.0, rbf, rad);
+  }
   __syncthreads();
   if (drbf != nullptr) {
     // d rbf_k / dr for the reverse pass (Bernstein derivative,

@@ -43,10 +43,10 @@ __device__ __forceinline__ size_t sp_block(int tile, int filt, int warp, int mi,
     return (((size_t)tile * 2 + filt) * 8 + warp) * (kMT * kNB * 128) + (size_t)(mi * kNB + ni) * 128;
 }
 
-__device__ inline void compute_rbf(const double *rr, double *rbf, const RadialW &rad) {
+// r: the distance of this thread's pair (pair threadIdx.x / kTPP of the tile)
+__device__ inline void compute_rbf(double r, double *rbf, const RadialW &rad) {
   const int pl = threadIdx.x / kTPP;
   const int k0 = (threadIdx.x % kTPP) * 8;
-  const double r = rr[pl];
   double x = exp(-rad.gamma * r);
   if (x < 1.0e-6) x = 1.0e-6;
   if (x > 1.0 - 1.0e-6) x = 1.0 - 1.0e-6;
@@ -70,9 +70,23 @@ __device__ inline void compute_l0(int P, int p0, const int *pa, const int *pb, c
       m0 = slot_offset(d);
       m1 = m0 + slot_width(d);
     }
-    for (int m = m0; m < m1; ++m) {
-      const double diff = ev[(size_t)b * kEV + m] - ev[(size_t)a * kEV + m];
-      v += diff * diff * cg[m];
+    // a degree slot has at most 9 channels: all loads first, then the sum in
+    // channel order
+    constexpr int kMaxW = 9;
+    double eb[kMaxW], ea[kMaxW];
+#pragma unroll
+    for (int q = 0; q < kMaxW; ++q) {
+      const int m = m0 + q;
+      eb[q] = m < m1 ? ev[(size_t)b * kEV + m] : 0.0;
+      ea[q] = m < m1 ? ev[(size_t)a * kEV + m] : 0.0;
+    }
+#pragma unroll
+    for (int q = 0; q < kMaxW; ++q) {
+      const int m = m0 + q;
+      if (m < m1) {
+        const double diff = eb[q] - ea[q];
+        v += diff * diff * cg[m];
+      }
     }
   }
   l0[pl * kHeads + d] = v;
