@@ -150,8 +150,10 @@ __device__ inline void smooth_switch2(double r, double cutoff, double cuton_e, d
   const double ip = 1.0 / (pe * pd);
   const double inv_e = pd * ip, inv_d = pe * ip;
   const double isle = sre * inv_e, isre = sle * inv_e, isld = srd * inv_d, isrd = sld * inv_d;
-  const double sig_le = le > 0.0 ? exp_tang(-isle) : 0.0, sig_re = re > 0.0 ? exp_tang(-isre) : 0.0;
-  const double sig_ld = ld > 0.0 ? exp_tang(-isld) : 0.0, sig_rd = rd > 0.0 ? exp_tang(-isrd) : 0.0;
+  // exp_tang clamps its argument: computed for every lane, then selected
+  const double xle = exp_tang(-isle), xre = exp_tang(-isre), xld = exp_tang(-isld), xrd = exp_tang(-isrd);
+  const double sig_le = le > 0.0 ? xle : 0.0, sig_re = re > 0.0 ? xre : 0.0;
+  const double sig_ld = ld > 0.0 ? xld : 0.0, sig_rd = rd > 0.0 ? xrd : 0.0;
   const double dene = sig_le + sig_re + 1.0e-12, dend = sig_ld + sig_rd + 1.0e-12;
   const double iq = 1.0 / (dene * dend);
   const double idene = dend * iq, idend = dene * iq;
@@ -213,13 +215,20 @@ __device__ inline LrPair lr_pair_tab(const LrDev &p, const LrConst &k, double r,
   o.dq = p.full_scale * p.ke * kernel * qj;
   const double erad = p.full_scale * p.ke * qi * qj * rkernel;
   double drad = 0.0;
-  if (ai0 >= 0.0 && aj0 >= 0.0) {
+  {
+    // computed without branches, so that the dispersion chain interleaves with
+    // the electrostatic one; a pair without dispersion (no reference data, or
+    // alpha or the C6 denominator not positive) runs on stand-in values and its
+    // results are dropped at the end
+    const bool has = ai0 >= 0.0 && aj0 >= 0.0;
     const double ai = ai0 * hi, aj = aj0 * hj;
     const double c6i = kSepC6 ? ci0 * si : ci0 * hi * hi, c6j = kSepC6 ? cj0 * sj : cj0 * hj * hj;
-    const double alpha = 0.5 * (ai + aj);
+    const double alpha_v = 0.5 * (ai + aj);
     const double num = 2.0 * c6i * c6j * aj * ai;
-    const double den = ai * ai * c6j + aj * aj * c6i;
-    if (alpha > 0.0 && den > 1.0e-30) {
+    const double den_v = ai * ai * c6j + aj * aj * c6i;
+    const bool ok = has && alpha_v > 0.0 && den_v > 1.0e-30;
+    const double alpha = ok ? alpha_v : 1.0, den = ok ? den_v : 1.0;
+    {
       const double iad = 1.0 / (alpha * den);  // 1/(alpha den): both positive, product far inside the normal range
       const double iden = alpha * iad;
       const double c6 = num * iden;
@@ -272,10 +281,10 @@ __device__ inline LrPair lr_pair_tab(const LrDev &p, const LrConst &k, double r,
                              c10 * dd10 * id10 * id10;
       const double dpot_dc6 = -id6 - 5.0 * igam * id8 - 245.0 * 0.125 * (igam * igam) * id10;
       const double dpot_dhi = dpot_dc6 * dc6_dhi + dpot_da * 0.5 * ai0;
-      o.e_disp = p.full_scale * p.hartree * qdo * dsw;
-      drad = p.full_scale * p.hartree * (rad_au * dsw * k.inv_bohr + qdo * ddsw);
-      o.dh = p.full_scale * p.hartree * dsw * dpot_dhi;
-      if (kSepC6) o.dc = p.full_scale * p.hartree * dsw * dpot_dc6 * dc6_dsi;
+      o.e_disp = ok ? p.full_scale * p.hartree * qdo * dsw : 0.0;
+      drad = ok ? p.full_scale * p.hartree * (rad_au * dsw * k.inv_bohr + qdo * ddsw) : 0.0;
+      o.dh = ok ? p.full_scale * p.hartree * dsw * dpot_dhi : 0.0;
+      if (kSepC6) o.dc = ok ? p.full_scale * p.hartree * dsw * dpot_dc6 * dc6_dsi : 0.0;
     }
   }
   o.radial = (erad + drad) * inv_r;
