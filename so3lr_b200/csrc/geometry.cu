@@ -327,8 +327,9 @@ __device__ inline void smooth_switch32(float r, float cuton, float cutoff, float
   const float left = 1.0f - c, right = c;
   const float sl = left > 1.0e-12f ? left : 1.0e-12f, sr = right > 1.0e-12f ? right : 1.0e-12f;
   const float isl = 1.0f / sl, isr = 1.0f / sr;
-  const float sig_l = left > 0.0f ? expf(-isl) : 0.0f;
-  const float sig_r = right > 0.0f ? expf(-isr) : 0.0f;
+  const float xl = expf(-isl), xr = expf(-isr);  // for every lane, then selected
+  const float sig_l = left > 0.0f ? xl : 0.0f;
+  const float sig_r = right > 0.0f ? xr : 0.0f;
   const float iden = 1.0f / (sig_l + sig_r + 1.0e-12f);
   v = sig_l * iden;
   const float dl = left > 0.0f ? -sig_l * isl * isl : 0.0f;
@@ -357,13 +358,18 @@ __device__ inline LrPair lr_pair_f32(const LrConst32 &k, float r, float qi, floa
   o.dq = k.ke_s * kernel * qj;
   const float erad = k.ke_s * qi * qj * rkernel;
   float drad = 0.0f;
-  if (ai0 >= 0.0f && aj0 >= 0.0f) {
+  {
+    // without branches, as in the float64 term: stand-in values where a pair
+    // has no dispersion, results dropped at the end
+    const bool has = ai0 >= 0.0f && aj0 >= 0.0f;
     const float ai = ai0 * hi, aj = aj0 * hj;
     const float c6i = kSepC6 ? ci0 * si : ci0 * hi * hi, c6j = kSepC6 ? cj0 * sj : cj0 * hj * hj;
-    const float alpha = 0.5f * (ai + aj);
+    const float alpha_v = 0.5f * (ai + aj);
     const float num = 2.0f * c6i * c6j * aj * ai;
-    const float den = ai * ai * c6j + aj * aj * c6i;
-    if (alpha > 0.0f && den > 1.0e-30f) {
+    const float den_v = ai * ai * c6j + aj * aj * c6i;
+    const bool ok = has && alpha_v > 0.0f && den_v > 1.0e-30f;
+    const float alpha = ok ? alpha_v : 1.0f, den = ok ? den_v : 1.0f;
+    {
       const float iden = 1.0f / den;
       const float c6 = num * iden;
       float dc6_dhi, dc6_dsi = 0.0f;
@@ -413,10 +419,10 @@ __device__ inline LrPair lr_pair_f32(const LrConst32 &k, float r, float qi, floa
       const float dpot_dhi = dpot_dc6 * dc6_dhi + dpot_da * 0.5f * ai0;
       float dsw, ddsw;
       smooth_switch32(r, k.disp_cuton, k.cutoff, k.inv_disp_width, dsw, ddsw);
-      o.e_disp = k.hartree_s * qdo * dsw;
-      drad = k.hartree_s * (rad_au * dsw * k.inv_bohr + qdo * ddsw);
-      o.dh = k.hartree_s * dsw * dpot_dhi;
-      if (kSepC6) o.dc = k.hartree_s * dsw * dpot_dc6 * dc6_dsi;
+      o.e_disp = ok ? k.hartree_s * qdo * dsw : 0.0f;
+      drad = ok ? k.hartree_s * (rad_au * dsw * k.inv_bohr + qdo * ddsw) : 0.0f;
+      o.dh = ok ? k.hartree_s * dsw * dpot_dhi : 0.0f;
+      if (kSepC6) o.dc = ok ? k.hartree_s * dsw * dpot_dc6 * dc6_dsi : 0.0f;
     }
   }
   o.radial = erad + drad;
